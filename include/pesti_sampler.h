@@ -1,0 +1,118 @@
+/*
+ * pesti_sampler.h -- C ABI of the B200 (sm_100a) token sampler.
+ *
+ * Drop-in boundary for the PESTI sampling step
+ *   temperature -> softmax -> top-k -> top-p -> inverse-CDF draw
+ * that the reference implements in Rust as
+ *   pub fn sample(logits: &[f32], config: &SamplingConfig, rng: &mut StdRng) -> u32
+ *                                       (llm-runner/src/transformer/sampling.rs:39)
+ *   pub fn argmax(logits: &[f32]) -> u32 (llm-runner/src/transformer/sampling.rs:115)
+ * called from LlamaModel::generate (llm-runner/src/transformer/model.rs:517-521) and
+ * CpuModel::run (llm-runner/src/model.rs:823-828).  The reference has no GPU
+ * sampler; this library takes the place of the stubbed GPU crate
+ * (cuda-oxide/src/main.rs:1-3) and is the sampling entry the kernel layer
+ * (llm-runner/src/kernel/mod.rs) lacks.
+ *
+ * Results are those of the reference algorithm, bit for bit, given the same
+ * per-row uniform draw u (the value `rng.random::<f32>()` returns at
+ * sampling.rs:98) and given exp correctly rounded (the reference calls the
+ * platform expf, which differs from the correctly rounded value by one ulp on
+ * about 6e-4 of its inputs).
+ *
+ * Conventions (mirroring the reference kernel layer):
+ *  - every call returns 0 on success or a negative PESTI_E_* code; the message
+ *    of the last failure on the calling thread is pesti_last_error();
+ *  - device pointers are plain addresses (RawHandle(u64) in
+ *    llm-runner/src/kernel/memory.rs:22); the caller owns every buffer;
+ *  - batch calls are stream-ordered and never synchronize the host;
+ *  - there is no CPU fallback: without a usable sm_100 device the calls fail.
+ */
+#ifndef PESTI_SAMPLER_H
+#define PESTI_SAMPLER_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PESTI_OK 0
+#define PESTI_E_INVALID_ARG (-1)
+#define PESTI_E_CUDA (-2)
+#define PESTI_E_NCCL (-3)
+#define PESTI_E_TIMEOUT (-4)
+#define PESTI_E_UNSUPPORTED (-5)
+#define PESTI_E_NO_DEVICE (-6)
+
+typedef enum { PESTI_F32 = 0, PESTI_BF16 = 1 } pesti_dtype;
+
+/* Per-row sampling parameters: SamplingConfig (sampling.rs:12-21) without the
+ * seed, which sample() never reads. */
+typedef struct {
+  float temperature; /* sampling.rs:14; > 0 scales the logits, otherwise none */
+  float top_p;       /* sampling.rs:16; used only when top_k == 0 (sampling.rs:66) */
+  uint32_t top_k;    /* sampling.rs:18; 0 = disabled */
+  uint32_t flags;    /* PESTI_FLAG_* */
+} pesti_sampling_params;
+
+/* Apply the caller branch of generate()/run(): temperature == 0.0 -> argmax
+ * (transformer/model.rs:517-521, model.rs:823-828).  Without it a zero
+ * temperature means "no scaling", as in sample() itself (sampling.rs:43). */
+#define PESTI_FLAG_GREEDY_IF_ZERO_T 1u
+/* argmax ties go to the lowest index.  Default: the last index, as
+ * Iterator::max_by returns (sampling.rs:115-122). */
+#define PESTI_FLAG_ARGMAX_FIRST 2u
+
+typedef struct pesti_sampler pesti_sampler;
+
+/* Creates a sampler bound to CUDA device `device`: its own stream, events and
+ * a workspace that grows on demand.  Replaces the context set-up of
+ * CudaRuntime::new (llm-runner/src/cuda_runtime.rs:92-176) for this path.
+ * A handle may be used from one thread at a time. */
+int pesti_sampler_create(int device, pesti_sampler** out);
+void pesti_sampler_destroy(pesti_sampler* s);
+
+/*
+ * Batched sample over row-major logits [B, ld] (first V columns of each row),
+ * dtype F32 or BF16, on device memory.  Replaces, per row, the call
+ *   generate():  if T == 0 { argmax(row) } else { sample(row, cfg, rng) }
+ * (model.rs:517-521) when params carry PESTI_FLAG_GREEDY_IF_ZERO_T, and
+ * sample(row, cfg, rng) (sampling.rs:39) otherwise.
+ *
+ *  params          host pointer: B entries if params_per_row, else 1 entry.
+ *                  When params_on_device != 0 it is a device pointer instead.
+ *  d_u             device [B] f32: the draw r of each row (sampling.rs:98).
+ *  d_out_tokens    device [B] u32.
+ *  d_kept_p/idx    optional device [B, kept_width]: the first kept_width
+ *                  entries of each row's kept list (the (probability, index)
+ *                  pairs left after top-k / top-p, sampling.rs:56-78), padded
+ *                  with 0 / 0xffffffff.  Either may be NULL.
+ *  d_kept_count    optional device [B] i64: length of each kept list (0 for
+ *                  greedy rows).
+ *  stream          cudaStream_t (NULL = the handle's own stream).
+ */
+int pesti_sample_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, int64_t B,
+                       int64_t V, int64_t ld, const pesti_sampling_params* params,
+                       int params_per_row, int params_on_device, const float* d_u,
+                       uint32_t* d_out_tokens, float* d_kept_p, uint32_t* d_kept_idx,
+                       int64_t kept_width, int64_t* d_kept_count, void* stream);
+
+/* Batched argmax (sampling.rs:115-122, last of equal maxima; NaN handled as
+ * Iterator::max_by does) over device logits.  flags: PESTI_FLAG_ARGMAX_FIRST. */
+int pesti_argmax_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, int64_t B,
+                       int64_t V, int64_t ld, uint32_t flags, uint32_t* d_out_tokens,
+                       void* stream);
+
+/* One row from HOST memory, synchronous: the drop-in for
+ * sample(&logits, &cfg, &mut rng) (sampling.rs:39) with r drawn by the caller;
+ * honours PESTI_FLAG_GREEDY_IF_ZERO_T like the batch call. */
+int pesti_sample_row_host(pesti_sampler* s, const float* h_logits, int64_t V,
+                          const pesti_sampling_params* params, float u, uint32_t* out_token);
+
+/* Message of the last failure on the calling thread ("" if none). */
+const char* pesti_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PESTI_SAMPLER_H */

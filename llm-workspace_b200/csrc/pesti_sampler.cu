@@ -1,0 +1,385 @@
+// Host side of the sampler library: the C ABI of include/pesti_sampler.h.
+// Launch geometry, workspace and error reporting live here; the arithmetic is
+// in pesti_kernels.cuh.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/pesti_sampler.h"
+#include "../../include/pesti_profile.h"
+#include "pesti_kernels.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(PESTI_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define PESTI_CUDA_TRY(expr, what)          \
+  do {                                      \
+    cudaError_t _e = (expr);                \
+    if (_e != cudaSuccess) return cuda_fail(_e, what); \
+  } while (0)
+
+}  // namespace
+
+struct pesti_sampler {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  pesti_sampling_params* d_params = nullptr;
+  size_t d_params_cap = 0;
+  pesti_sampling_params* h_params = nullptr;  // pinned staging
+  size_t h_params_cap = 0;
+  cudaEvent_t params_ev = nullptr;
+  bool params_ev_used = false;
+  // single-row host API buffers
+  float* d_row = nullptr;
+  size_t d_row_cap = 0;
+  float* d_u1 = nullptr;
+  uint32_t* d_tok1 = nullptr;
+  // instrumentation (pesti_profile.h)
+  static constexpr int kProfMax = 4096;
+  bool prof = false;
+  int prof_n = 0;
+  cudaEvent_t prof_ev[kProfMax][3] = {};
+};
+
+namespace {
+
+struct Geometry {
+  int P;
+  long long SL;
+};
+
+Geometry pick_geometry(const pesti_sampler* s, long long B, long long V, int ve) {
+  const long long target = 4LL * s->num_sms;
+  long long P = (target + B - 1) / std::max(1LL, B);
+  const long long pmax_v = std::max(1LL, V / (pesti::K1_WARPS * 1024LL));
+  P = std::max(1LL, std::min({P, pmax_v, (long long)(pesti::MAX_SUBS / pesti::K1_WARPS)}));
+  const long long unit = 32LL * ve;
+  long long SL = (V + P * pesti::K1_WARPS - 1) / (P * pesti::K1_WARPS);
+  SL = std::max(unit, (SL + unit - 1) / unit * unit);
+  P = std::max(1LL, (V + SL * pesti::K1_WARPS - 1) / (SL * pesti::K1_WARPS));
+  return Geometry{(int)P, SL};
+}
+
+int ensure_ws(pesti_sampler* s, size_t bytes) {
+  if (bytes <= s->ws_bytes) return PESTI_OK;
+  if (s->ws) {
+    cudaError_t e = cudaStreamSynchronize(s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    cudaDeviceSynchronize();
+    cudaFree(s->ws);
+    s->ws = nullptr;
+    s->ws_bytes = 0;
+  }
+  const size_t want = bytes + bytes / 8;
+  cudaError_t e = cudaMalloc(&s->ws, want);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(workspace)");
+  s->ws_bytes = want;
+  return PESTI_OK;
+}
+
+size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
+
+bool needs_sorted_buffers(const pesti_sampling_params* p, long long n) {
+  for (long long i = 0; i < n; ++i) {
+    const bool greedy = (p[i].flags & PESTI_FLAG_GREEDY_IF_ZERO_T) && p[i].temperature == 0.0f;
+    if (greedy) continue;
+    if (p[i].top_k == 0) return true;  // top-p or no filter
+    if (p[i].top_k > (uint32_t)pesti::TOPK_SMALL) return true;
+  }
+  return false;
+}
+
+int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long B, long long V,
+           long long ld, const pesti_sampling_params& uni, const pesti_sampling_params* d_per_row,
+           bool sorted_bufs, const float* d_u, uint32_t* d_out, float* d_kept_p,
+           uint32_t* d_kept_idx, long long kept_width, int64_t* d_kept_count, cudaStream_t st) {
+  const int esize = dtype == PESTI_BF16 ? 2 : 4;
+  const int ve = 16 / esize;
+  const Geometry g = pick_geometry(s, B, V > 0 ? V : 1, ve);
+  const long long nsub = (long long)g.P * pesti::K1_WARPS;
+  const size_t bv = (size_t)B * (size_t)std::max(1LL, V);
+  size_t off = 0;
+  const size_t o_meta = off; off = align_up(off + (size_t)B * nsub * sizeof(pesti::WarpMeta));
+  const size_t o_sraw = off; off = align_up(off + bv * 4);
+  const size_t o_sidx = off; off = align_up(off + bv * 4);
+  const size_t o_E = off; off = align_up(off + bv * 4);
+  const size_t o_I = off; off = align_up(off + bv * 4);
+  const size_t o_status = off; off = align_up(off + 16);
+  size_t o_sk0 = 0, o_sv0 = 0, o_sk1 = 0, o_sv1 = 0, o_q = 0;
+  if (sorted_bufs) {
+    o_sk0 = off; off = align_up(off + bv * 4);
+    o_sv0 = off; off = align_up(off + bv * 4);
+    o_sk1 = off; off = align_up(off + bv * 4);
+    o_sv1 = off; off = align_up(off + bv * 4);
+    o_q = off; off = align_up(off + bv * 4);
+  }
+  int rc = ensure_ws(s, off);
+  if (rc) return rc;
+  char* ws = (char*)s->ws;
+
+  pesti::SliceArgs sa;
+  sa.logits = d_logits;
+  sa.B = B;
+  sa.V = V;
+  sa.ld = ld;
+  sa.uni = uni;
+  sa.per_row = d_per_row;
+  sa.P = g.P;
+  sa.SL = g.SL;
+  sa.meta = (pesti::WarpMeta*)(ws + o_meta);
+  sa.surv_raw = (float*)(ws + o_sraw);
+  sa.surv_idx = (uint32_t*)(ws + o_sidx);
+
+  cudaEvent_t* pev = nullptr;
+  if (s->prof && s->prof_n < pesti_sampler::kProfMax) {
+    pev = s->prof_ev[s->prof_n++];
+    for (int q = 0; q < 3; ++q)
+      if (!pev[q]) PESTI_CUDA_TRY(cudaEventCreate(&pev[q]), "cudaEventCreate(profile)");
+    PESTI_CUDA_TRY(cudaEventRecord(pev[0], st), "cudaEventRecord(profile)");
+  }
+  const bool aligned = ((uintptr_t)d_logits % 16 == 0) && ((ld * esize) % 16 == 0);
+  const dim3 g1((unsigned)(g.P * B));
+  if (dtype == PESTI_BF16) {
+    if (aligned) pesti::slice_scan_kernel<uint16_t, 8, 4, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
+    else pesti::slice_scan_kernel<uint16_t, 8, 4, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
+  } else {
+    if (aligned) pesti::slice_scan_kernel<float, 4, 8, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
+    else pesti::slice_scan_kernel<float, 4, 8, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "slice_scan_kernel launch");
+  if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[1], st), "cudaEventRecord(profile)");
+
+  pesti::RowArgs ra;
+  ra.logits = d_logits;
+  ra.dtype = (int)dtype;
+  ra.B = B;
+  ra.V = V;
+  ra.ld = ld;
+  ra.uni = uni;
+  ra.per_row = d_per_row;
+  ra.P = g.P;
+  ra.SL = g.SL;
+  ra.meta = sa.meta;
+  ra.surv_raw = sa.surv_raw;
+  ra.surv_idx = sa.surv_idx;
+  ra.E = (float*)(ws + o_E);
+  ra.I = (uint32_t*)(ws + o_I);
+  ra.SK0 = sorted_bufs ? (uint32_t*)(ws + o_sk0) : nullptr;
+  ra.SV0 = sorted_bufs ? (uint32_t*)(ws + o_sv0) : nullptr;
+  ra.SK1 = sorted_bufs ? (uint32_t*)(ws + o_sk1) : nullptr;
+  ra.SV1 = sorted_bufs ? (uint32_t*)(ws + o_sv1) : nullptr;
+  ra.Q = sorted_bufs ? (float*)(ws + o_q) : nullptr;
+  ra.u = d_u;
+  ra.out = d_out;
+  ra.kept_p = d_kept_p;
+  ra.kept_idx = d_kept_idx;
+  ra.kept_width = (d_kept_p || d_kept_idx) ? kept_width : 0;
+  ra.kept_count = d_kept_count;
+  ra.status = (int*)(ws + o_status);
+  pesti::row_kernel<<<(unsigned)B, pesti::K2_NT, sizeof(pesti::RowShared), st>>>(ra);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "row_kernel launch");
+  if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[2], st), "cudaEventRecord(profile)");
+  return PESTI_OK;
+}
+
+int check_common(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, int64_t B, int64_t V,
+                 int64_t ld) {
+  if (!s) return fail(PESTI_E_INVALID_ARG, "null sampler handle");
+  if (dtype != PESTI_F32 && dtype != PESTI_BF16) return fail(PESTI_E_INVALID_ARG, "unsupported dtype");
+  if (B < 0 || V < 0) return fail(PESTI_E_INVALID_ARG, "negative B or V");
+  if (V > 0x7fffffffLL) return fail(PESTI_E_INVALID_ARG, "V exceeds 2^31-1");
+  if (B > 0x7fffffffLL) return fail(PESTI_E_INVALID_ARG, "B exceeds 2^31-1");
+  if (B > 0 && V > 0 && !d_logits) return fail(PESTI_E_INVALID_ARG, "null logits");
+  if (B > 0 && ld < V) return fail(PESTI_E_INVALID_ARG, "leading dimension smaller than V");
+  return PESTI_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* pesti_last_error(void) { return g_last_error.c_str(); }
+
+int pesti_sampler_create(int device, pesti_sampler** out) {
+  if (!out) return fail(PESTI_E_INVALID_ARG, "null output pointer");
+  *out = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0) return fail(PESTI_E_NO_DEVICE, "no CUDA device available");
+  if (device < 0 || device >= n) return fail(PESTI_E_INVALID_ARG, "device index out of range");
+  cudaDeviceProp prop;
+  PESTI_CUDA_TRY(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+  if (prop.major < 10) return fail(PESTI_E_UNSUPPORTED, "the sampler is built for sm_100a (B200)");
+  PESTI_CUDA_TRY(cudaSetDevice(device), "cudaSetDevice");
+  PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)sizeof(pesti::RowShared)),
+                 "cudaFuncSetAttribute(row_kernel)");
+  pesti_sampler* s = new pesti_sampler();
+  s->device = device;
+  s->num_sms = prop.multiProcessorCount;
+  e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) { delete s; return cuda_fail(e, "cudaStreamCreate"); }
+  e = cudaEventCreateWithFlags(&s->params_ev, cudaEventDisableTiming);
+  if (e != cudaSuccess) { cudaStreamDestroy(s->stream); delete s; return cuda_fail(e, "cudaEventCreate"); }
+  *out = s;
+  return PESTI_OK;
+}
+
+void pesti_sampler_destroy(pesti_sampler* s) {
+  if (!s) return;
+  cudaSetDevice(s->device);
+  if (s->stream) cudaStreamSynchronize(s->stream);
+  cudaDeviceSynchronize();
+  if (s->ws) cudaFree(s->ws);
+  if (s->d_params) cudaFree(s->d_params);
+  if (s->h_params) cudaFreeHost(s->h_params);
+  if (s->d_row) cudaFree(s->d_row);
+  if (s->d_u1) cudaFree(s->d_u1);
+  if (s->d_tok1) cudaFree(s->d_tok1);
+  if (s->params_ev) cudaEventDestroy(s->params_ev);
+  for (int i = 0; i < pesti_sampler::kProfMax; ++i)
+    for (int q = 0; q < 3; ++q)
+      if (s->prof_ev[i][q]) cudaEventDestroy(s->prof_ev[i][q]);
+  if (s->stream) cudaStreamDestroy(s->stream);
+  delete s;
+}
+
+int pesti_sample_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, int64_t B,
+                       int64_t V, int64_t ld, const pesti_sampling_params* params,
+                       int params_per_row, int params_on_device, const float* d_u,
+                       uint32_t* d_out_tokens, float* d_kept_p, uint32_t* d_kept_idx,
+                       int64_t kept_width, int64_t* d_kept_count, void* stream) {
+  int rc = check_common(s, d_logits, dtype, B, V, ld);
+  if (rc) return rc;
+  if (!params) return fail(PESTI_E_INVALID_ARG, "null params");
+  if (B > 0 && (!d_u || !d_out_tokens)) return fail(PESTI_E_INVALID_ARG, "null u or output tokens");
+  if ((d_kept_p || d_kept_idx) && kept_width <= 0) return fail(PESTI_E_INVALID_ARG, "kept_width must be > 0");
+  if (B == 0) return PESTI_OK;
+  PESTI_CUDA_TRY(cudaSetDevice(s->device), "cudaSetDevice");
+  cudaStream_t st = stream ? (cudaStream_t)stream : s->stream;
+  pesti_sampling_params uni{};
+  const pesti_sampling_params* d_per_row = nullptr;
+  bool sorted_bufs = true;
+  if (params_on_device) {
+    if (params_per_row) d_per_row = params;
+    else {
+      // single device entry: read it back once (rare API use)
+      PESTI_CUDA_TRY(cudaMemcpyAsync(&uni, params, sizeof(uni), cudaMemcpyDeviceToHost, st), "params copy");
+      PESTI_CUDA_TRY(cudaStreamSynchronize(st), "params sync");
+      sorted_bufs = needs_sorted_buffers(&uni, 1);
+    }
+  } else if (params_per_row) {
+    sorted_bufs = needs_sorted_buffers(params, B);
+    if ((size_t)B > s->h_params_cap) {
+      if (s->params_ev_used) cudaEventSynchronize(s->params_ev);
+      if (s->h_params) cudaFreeHost(s->h_params);
+      if (s->d_params) cudaFree(s->d_params);
+      s->h_params = nullptr;
+      s->d_params = nullptr;
+      PESTI_CUDA_TRY(cudaMallocHost(&s->h_params, (size_t)B * sizeof(pesti_sampling_params)), "cudaMallocHost(params)");
+      PESTI_CUDA_TRY(cudaMalloc(&s->d_params, (size_t)B * sizeof(pesti_sampling_params)), "cudaMalloc(params)");
+      s->h_params_cap = s->d_params_cap = (size_t)B;
+    } else if (s->params_ev_used) {
+      PESTI_CUDA_TRY(cudaEventSynchronize(s->params_ev), "cudaEventSynchronize(params)");
+    }
+    std::memcpy(s->h_params, params, (size_t)B * sizeof(pesti_sampling_params));
+    PESTI_CUDA_TRY(cudaMemcpyAsync(s->d_params, s->h_params, (size_t)B * sizeof(pesti_sampling_params),
+                                   cudaMemcpyHostToDevice, st), "params copy");
+    PESTI_CUDA_TRY(cudaEventRecord(s->params_ev, st), "cudaEventRecord(params)");
+    s->params_ev_used = true;
+    d_per_row = s->d_params;
+  } else {
+    uni = params[0];
+    sorted_bufs = needs_sorted_buffers(&uni, 1);
+  }
+  return launch(s, d_logits, dtype, B, V, ld, uni, d_per_row, sorted_bufs, d_u, d_out_tokens,
+                d_kept_p, d_kept_idx, kept_width, d_kept_count, st);
+}
+
+int pesti_argmax_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, int64_t B,
+                       int64_t V, int64_t ld, uint32_t flags, uint32_t* d_out_tokens, void* stream) {
+  int rc = check_common(s, d_logits, dtype, B, V, ld);
+  if (rc) return rc;
+  if (B > 0 && !d_out_tokens) return fail(PESTI_E_INVALID_ARG, "null output tokens");
+  if (B == 0) return PESTI_OK;
+  PESTI_CUDA_TRY(cudaSetDevice(s->device), "cudaSetDevice");
+  cudaStream_t st = stream ? (cudaStream_t)stream : s->stream;
+  pesti_sampling_params uni{};
+  uni.temperature = 0.0f;
+  uni.flags = PESTI_FLAG_GREEDY_IF_ZERO_T | (flags & PESTI_FLAG_ARGMAX_FIRST);
+  return launch(s, d_logits, dtype, B, V, ld, uni, nullptr, false, nullptr, d_out_tokens, nullptr,
+                nullptr, 0, nullptr, st);
+}
+
+int pesti_sample_row_host(pesti_sampler* s, const float* h_logits, int64_t V,
+                          const pesti_sampling_params* params, float u, uint32_t* out_token) {
+  if (!s || !params || !out_token) return fail(PESTI_E_INVALID_ARG, "null argument");
+  if (V < 0 || V > 0x7fffffffLL) return fail(PESTI_E_INVALID_ARG, "bad V");
+  if (V > 0 && !h_logits) return fail(PESTI_E_INVALID_ARG, "null logits");
+  PESTI_CUDA_TRY(cudaSetDevice(s->device), "cudaSetDevice");
+  const size_t need = (size_t)std::max<int64_t>(V, 4);
+  if (need > s->d_row_cap) {
+    if (s->d_row) cudaFree(s->d_row);
+    s->d_row = nullptr;
+    PESTI_CUDA_TRY(cudaMalloc(&s->d_row, need * sizeof(float)), "cudaMalloc(row)");
+    s->d_row_cap = need;
+  }
+  if (!s->d_u1) PESTI_CUDA_TRY(cudaMalloc(&s->d_u1, 16), "cudaMalloc(u)");
+  if (!s->d_tok1) PESTI_CUDA_TRY(cudaMalloc(&s->d_tok1, 16), "cudaMalloc(token)");
+  cudaStream_t st = s->stream;
+  if (V > 0)
+    PESTI_CUDA_TRY(cudaMemcpyAsync(s->d_row, h_logits, (size_t)V * sizeof(float), cudaMemcpyHostToDevice, st), "logits copy");
+  PESTI_CUDA_TRY(cudaMemcpyAsync(s->d_u1, &u, sizeof(float), cudaMemcpyHostToDevice, st), "u copy");
+  int rc = launch(s, s->d_row, PESTI_F32, 1, V, std::max<int64_t>(V, 1), *params, nullptr,
+                  needs_sorted_buffers(params, 1), s->d_u1, s->d_tok1, nullptr, nullptr, 0, nullptr, st);
+  if (rc) return rc;
+  uint32_t tok = 0;
+  PESTI_CUDA_TRY(cudaMemcpyAsync(&tok, s->d_tok1, sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "token copy");
+  PESTI_CUDA_TRY(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+  *out_token = tok;
+  return PESTI_OK;
+}
+
+int pesti_profile_enable(pesti_sampler* s, int enable) {
+  if (!s) return fail(PESTI_E_INVALID_ARG, "null sampler handle");
+  s->prof = enable != 0;
+  s->prof_n = 0;
+  return PESTI_OK;
+}
+
+int pesti_profile_read(pesti_sampler* s, double* scan_ms, double* row_ms, int* calls) {
+  if (!s || !scan_ms || !row_ms || !calls) return fail(PESTI_E_INVALID_ARG, "null argument");
+  double a = 0.0, b = 0.0;
+  for (int i = 0; i < s->prof_n; ++i) {
+    PESTI_CUDA_TRY(cudaEventSynchronize(s->prof_ev[i][2]), "cudaEventSynchronize(profile)");
+    float t1 = 0.f, t2 = 0.f;
+    PESTI_CUDA_TRY(cudaEventElapsedTime(&t1, s->prof_ev[i][0], s->prof_ev[i][1]), "cudaEventElapsedTime");
+    PESTI_CUDA_TRY(cudaEventElapsedTime(&t2, s->prof_ev[i][1], s->prof_ev[i][2]), "cudaEventElapsedTime");
+    a += t1;
+    b += t2;
+  }
+  *scan_ms = a;
+  *row_ms = b;
+  *calls = s->prof_n;
+  return PESTI_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,309 @@
+"""Host-side mirror of the reference sampler API over the sm_100a C ABI.
+
+The reference (Rust) exposes, in llm-runner/src/transformer/sampling.rs:
+    pub struct SamplingConfig { temperature: f32, top_p: f32, top_k: usize, seed: Option<u64> }  (:12-21)
+    impl Default for SamplingConfig -> T=0.7, top_p=0.9, top_k=0, seed=None                      (:23-32)
+    pub fn sample(logits: &[f32], config: &SamplingConfig, rng: &mut StdRng) -> u32              (:39)
+    pub fn argmax(logits: &[f32]) -> u32                                                          (:115)
+and its callers branch on `temperature == 0.0` (transformer/model.rs:517-521).
+
+This module keeps those names and meanings and adds the batched form the
+decode loop needs (`Sampler.sample_batch`, rows of a [B, V] device tensor).
+Every call runs the CUDA kernels of libpesti_sampler.so; there is no CPU
+path: without the library or a B200 the calls raise.
+
+`rng` stands for the reference's StdRng: any object with `next_f32()`
+returning the next uniform draw in [0, 1) (sampling.rs:98 draws exactly one
+per `sample` call and none for argmax).  `Pcg32` below is the generator the
+benchmarks and tests use.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from dataclasses import dataclass
+from typing import Optional, Sequence, Union
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libpesti_sampler.so")
+CSRC = os.path.join(_HERE, "csrc")
+INCLUDE = os.path.join(os.path.dirname(_HERE), "include")
+
+PESTI_OK = 0
+PESTI_E_INVALID_ARG = -1
+PESTI_E_CUDA = -2
+PESTI_E_NCCL = -3
+PESTI_E_TIMEOUT = -4
+PESTI_E_UNSUPPORTED = -5
+PESTI_E_NO_DEVICE = -6
+
+PESTI_F32 = 0
+PESTI_BF16 = 1
+
+FLAG_GREEDY_IF_ZERO_T = 1
+FLAG_ARGMAX_FIRST = 2
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-Xcompiler", "-fPIC", "-shared",
+]
+
+
+def build(verbose: bool = False) -> str:
+    """Compiles csrc/ into libpesti_sampler.so for sm_100a (in-tree)."""
+    src = os.path.join(CSRC, "pesti_sampler.cu")
+    cmd = ["nvcc", *NVCC_FLAGS, "-o", LIB_PATH, src]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+    subprocess.run(cmd, check=True)
+    return LIB_PATH
+
+
+class SamplerError(RuntimeError):
+    """A failed library call: `code` is the PESTI_E_* value."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"pesti error {code}: {msg}")
+        self.code = code
+
+
+class _Params(ctypes.Structure):
+    _fields_ = [("temperature", ctypes.c_float), ("top_p", ctypes.c_float),
+                ("top_k", ctypes.c_uint32), ("flags", ctypes.c_uint32)]
+
+
+_lib = None
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Loads the sampler library; raises if it is missing (no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise FileNotFoundError(
+            f"{path} is missing: build it with __graft_entry__.build() (there is no CPU fallback)")
+    lib = ctypes.CDLL(path)
+    vp, i64, c_int = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    lib.pesti_sampler_create.argtypes = [c_int, ctypes.POINTER(vp)]
+    lib.pesti_sampler_create.restype = c_int
+    lib.pesti_sampler_destroy.argtypes = [vp]
+    lib.pesti_sampler_destroy.restype = None
+    lib.pesti_sample_batch.argtypes = [vp, vp, c_int, i64, i64, i64, ctypes.POINTER(_Params), c_int,
+                                       c_int, vp, vp, vp, vp, i64, vp, vp]
+    lib.pesti_sample_batch.restype = c_int
+    lib.pesti_argmax_batch.argtypes = [vp, vp, c_int, i64, i64, i64, ctypes.c_uint32, vp, vp]
+    lib.pesti_argmax_batch.restype = c_int
+    lib.pesti_sample_row_host.argtypes = [vp, ctypes.POINTER(ctypes.c_float), i64,
+                                          ctypes.POINTER(_Params), ctypes.c_float,
+                                          ctypes.POINTER(ctypes.c_uint32)]
+    lib.pesti_sample_row_host.restype = c_int
+    lib.pesti_last_error.argtypes = []
+    lib.pesti_last_error.restype = ctypes.c_char_p
+    _lib = lib
+    return lib
+
+
+def _check(rc: int) -> None:
+    if rc != PESTI_OK:
+        raise SamplerError(rc, load_library().pesti_last_error().decode())
+
+
+@dataclass
+class SamplingConfig:
+    """sampling.rs:12-32 (defaults included)."""
+    temperature: float = 0.7
+    top_p: float = 0.9
+    top_k: int = 0
+    seed: Optional[int] = None
+
+    def to_params(self, greedy_if_zero_t: bool = False, argmax_first: bool = False) -> _Params:
+        flags = (FLAG_GREEDY_IF_ZERO_T if greedy_if_zero_t else 0) | (FLAG_ARGMAX_FIRST if argmax_first else 0)
+        return _Params(float(self.temperature), float(self.top_p), int(self.top_k), flags)
+
+
+class Pcg32:
+    """PCG32 (O'Neill 2014, XSH-RR 64->32) with the reference's f32 draw.
+
+    next_f32() = (next_u32() >> 8) * 2^-24: the [0,1) 24-bit grid that rand's
+    `random::<f32>()` produces (sampling.rs:98).
+    """
+
+    MULT = 6364136223846793005
+    MASK = (1 << 64) - 1
+
+    def __init__(self, seed: int, stream: int = 54):
+        self.state = 0
+        self.inc = ((stream << 1) | 1) & self.MASK
+        self.next_u32()
+        self.state = (self.state + seed) & self.MASK
+        self.next_u32()
+
+    def next_u32(self) -> int:
+        old = self.state
+        self.state = (old * self.MULT + self.inc) & self.MASK
+        xs = (((old >> 18) ^ old) >> 27) & 0xFFFFFFFF
+        rot = old >> 59
+        return ((xs >> rot) | (xs << ((-rot) & 31))) & 0xFFFFFFFF
+
+    def next_f32(self) -> float:
+        return float(self.next_u32() >> 8) * (1.0 / (1 << 24))
+
+    def draws(self, n: int):
+        import numpy as np
+        return np.array([self.next_f32() for _ in range(n)], dtype=np.float32)
+
+
+class Sampler:
+    """A device-bound sampler handle (pesti_sampler_create / _destroy)."""
+
+    def __init__(self, device: int = 0):
+        lib = load_library()
+        h = ctypes.c_void_p()
+        _check(lib.pesti_sampler_create(int(device), ctypes.byref(h)))
+        self._h = h
+        self._lib = lib
+        self.device = device
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._lib.pesti_sampler_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- batched API (device tensors) --------------------------------------
+    def sample_batch(self, logits, configs: Union[SamplingConfig, Sequence[SamplingConfig]], u,
+                     out=None, greedy_if_zero_t: bool = True, argmax_first: bool = False,
+                     kept_width: int = 0, stream=None):
+        """Samples one token per row of `logits` ([B, V] f32 or bf16 CUDA tensor).
+
+        configs: one SamplingConfig for all rows or one per row.  u: [B] f32
+        CUDA tensor of draws.  Returns the [B] int32 token tensor (u32 bits),
+        or (tokens, kept_p, kept_idx, kept_count) when kept_width > 0.
+        """
+        import torch
+        if logits.dim() != 2:
+            raise ValueError("logits must be [B, V]")
+        B, V = logits.shape
+        dtype = {torch.float32: PESTI_F32, torch.bfloat16: PESTI_BF16}.get(logits.dtype)
+        if dtype is None:
+            raise ValueError("logits must be float32 or bfloat16")
+        if logits.stride(1) != 1:
+            raise ValueError("logits rows must be contiguous")
+        if isinstance(configs, SamplingConfig):
+            arr = (_Params * 1)(configs.to_params(greedy_if_zero_t, argmax_first))
+            per_row = 0
+        else:
+            if len(configs) != B:
+                raise ValueError("need one config per row")
+            arr = (_Params * B)(*[c.to_params(greedy_if_zero_t, argmax_first) for c in configs])
+            per_row = 1
+        if out is None:
+            out = torch.empty(B, dtype=torch.int32, device=logits.device)
+        kp = ki = kc = None
+        if kept_width > 0:
+            kp = torch.empty(B, kept_width, dtype=torch.float32, device=logits.device)
+            ki = torch.empty(B, kept_width, dtype=torch.int32, device=logits.device)
+            kc = torch.empty(B, dtype=torch.int64, device=logits.device)
+        st = stream if stream is not None else torch.cuda.current_stream(logits.device).cuda_stream
+        _check(self._lib.pesti_sample_batch(
+            self._h, logits.data_ptr(), dtype, B, V, logits.stride(0), arr, per_row, 0,
+            u.data_ptr(), out.data_ptr(),
+            kp.data_ptr() if kp is not None else None, ki.data_ptr() if ki is not None else None,
+            kept_width, kc.data_ptr() if kc is not None else None, st))
+        if kept_width > 0:
+            return out, kp, ki, kc
+        return out
+
+    def sample_batch_device_params(self, logits, d_params, u, out, stream=None):
+        """Per-row parameters already on the device (a [B, 4] int32/f32 view of
+        pesti_sampling_params records)."""
+        import torch
+        B, V = logits.shape
+        dtype = PESTI_BF16 if logits.dtype == torch.bfloat16 else PESTI_F32
+        st = stream if stream is not None else torch.cuda.current_stream(logits.device).cuda_stream
+        _check(self._lib.pesti_sample_batch(
+            self._h, logits.data_ptr(), dtype, B, V, logits.stride(0),
+            ctypes.cast(ctypes.c_void_p(d_params.data_ptr()), ctypes.POINTER(_Params)), 1, 1,
+            u.data_ptr(), out.data_ptr(), None, None, 0, None, st))
+        return out
+
+    def argmax_batch(self, logits, first: bool = False, out=None, stream=None):
+        """sampling.rs:115-122 over each row (last of equal maxima unless first)."""
+        import torch
+        B, V = logits.shape
+        dtype = PESTI_BF16 if logits.dtype == torch.bfloat16 else PESTI_F32
+        if out is None:
+            out = torch.empty(B, dtype=torch.int32, device=logits.device)
+        st = stream if stream is not None else torch.cuda.current_stream(logits.device).cuda_stream
+        _check(self._lib.pesti_argmax_batch(self._h, logits.data_ptr(), dtype, B, V, logits.stride(0),
+                                            FLAG_ARGMAX_FIRST if first else 0, out.data_ptr(), st))
+        return out
+
+    # -- single row from host memory (the reference's own signature) -------
+    def sample(self, logits, config: SamplingConfig, rng, greedy_if_zero_t: bool = False) -> int:
+        """sample(&logits, &config, &mut rng) (sampling.rs:39): one draw from rng."""
+        import numpy as np
+        x = np.ascontiguousarray(np.asarray(logits, dtype=np.float32))
+        r = rng.next_f32()
+        tok = ctypes.c_uint32()
+        p = config.to_params(greedy_if_zero_t)
+        _check(self._lib.pesti_sample_row_host(
+            self._h, x.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), int(x.size), ctypes.byref(p),
+            ctypes.c_float(r), ctypes.byref(tok)))
+        return int(tok.value)
+
+    def sample_with_u(self, logits, config: SamplingConfig, u: float, greedy_if_zero_t: bool = False) -> int:
+        import numpy as np
+        x = np.ascontiguousarray(np.asarray(logits, dtype=np.float32))
+        tok = ctypes.c_uint32()
+        p = config.to_params(greedy_if_zero_t)
+        _check(self._lib.pesti_sample_row_host(
+            self._h, x.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), int(x.size), ctypes.byref(p),
+            ctypes.c_float(u), ctypes.byref(tok)))
+        return int(tok.value)
+
+    def argmax(self, logits) -> int:
+        """argmax(&logits) (sampling.rs:115): greedy, no draw."""
+        import numpy as np
+        x = np.ascontiguousarray(np.asarray(logits, dtype=np.float32))
+        tok = ctypes.c_uint32()
+        p = _Params(0.0, 0.0, 0, FLAG_GREEDY_IF_ZERO_T)
+        _check(self._lib.pesti_sample_row_host(
+            self._h, x.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), int(x.size), ctypes.byref(p),
+            ctypes.c_float(0.0), ctypes.byref(tok)))
+        return int(tok.value)
+
+
+_default: Optional[Sampler] = None
+
+
+def _default_sampler() -> Sampler:
+    global _default
+    if _default is None:
+        _default = Sampler(0)
+    return _default
+
+
+def sample(logits, config: SamplingConfig, rng) -> int:
+    """Module-level drop-in for sampling.rs:39 on CUDA device 0."""
+    return _default_sampler().sample(logits, config, rng)
+
+
+def argmax(logits) -> int:
+    """Module-level drop-in for sampling.rs:115 on CUDA device 0."""
+    return _default_sampler().argmax(logits)
+
+
+def generate_step(logits, config: SamplingConfig, rng) -> int:
+    """The branch of LlamaModel::generate (transformer/model.rs:517-521)."""
+    if config.temperature == 0.0:
+        return argmax(logits)
+    return sample(logits, config, rng)

@@ -1,0 +1,194 @@
+"""ctypes binding of the CPU oracle (liboracle.so) -- TEST INFRASTRUCTURE ONLY.
+
+Used by tests/, __graft_entry__.smoke() (as the checker) and bench.py's
+cpu_baseline / `--impl reference` leg (as the timed reference algorithm).  The
+product library never imports this module.
+
+Also holds `py_sample`, a second, independent restatement of
+llm-runner/src/transformer/sampling.rs:39-134 written with numpy float32
+scalars in plain Python loops.  It is slow and meant for small rows; the tests
+use it to cross-check the C++ oracle (both must agree bit for bit when exp is
+correctly rounded).
+
+Parity pin: the Rust reference cannot be built in this image (no cargo or
+rustc), and its own tests (sampling.rs:142-207) pin properties only, not token
+ids; tests/test_oracle.py restates those six tests against both restatements.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(_HERE, "_build", "liboracle.so")
+
+EXP_PLATFORM = 0
+EXP_CR = 1
+FLAG_GREEDY_IF_ZERO_T = 1
+FLAG_ARGMAX_FIRST = 2
+
+
+class OracleParams(ctypes.Structure):
+    _fields_ = [("temperature", ctypes.c_float), ("top_p", ctypes.c_float),
+                ("top_k", ctypes.c_uint32), ("flags", ctypes.c_uint32)]
+
+
+def build() -> str:
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return LIB
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB):
+            build()
+        L = ctypes.CDLL(LIB)
+        fp, i64, vp = ctypes.POINTER(ctypes.c_float), ctypes.c_int64, ctypes.c_void_p
+        L.oracle_argmax.argtypes = [fp, i64]
+        L.oracle_argmax.restype = ctypes.c_uint32
+        L.oracle_argmax_first.argtypes = [fp, i64]
+        L.oracle_argmax_first.restype = ctypes.c_uint32
+        L.oracle_sample.argtypes = [fp, i64, ctypes.c_float, ctypes.c_float, i64, ctypes.c_float,
+                                    ctypes.c_int, vp, vp, i64, vp, vp]
+        L.oracle_sample.restype = ctypes.c_uint32
+        L.oracle_sample_batch.argtypes = [fp, i64, i64, i64, ctypes.POINTER(OracleParams), ctypes.c_int,
+                                          fp, ctypes.c_int, vp, vp, vp, i64, vp, vp, ctypes.c_int]
+        L.oracle_sample_batch.restype = None
+        L.oracle_exp_cr.argtypes = [ctypes.c_float]
+        L.oracle_exp_cr.restype = ctypes.c_float
+        _lib = L
+    return _lib
+
+
+def _fp(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+
+
+def argmax(logits) -> int:
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    return int(lib().oracle_argmax(_fp(x), x.size))
+
+
+def argmax_first(logits) -> int:
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    return int(lib().oracle_argmax_first(_fp(x), x.size))
+
+
+def sample(logits, temperature, top_p, top_k, r, exp_mode=EXP_PLATFORM, kept_width=0):
+    """One row of sampling.rs:39.  Returns token, or (token, kept_p, kept_idx,
+    kept_count, boundary_dist) when kept_width > 0."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    kp = np.zeros(max(kept_width, 1), np.float32)
+    ki = np.zeros(max(kept_width, 1), np.uint32)
+    kc = np.zeros(1, np.int64)
+    bd = np.zeros(1, np.float32)
+    tok = lib().oracle_sample(_fp(x), x.size, float(temperature), float(top_p), int(top_k), float(r),
+                              exp_mode, kp.ctypes.data, ki.ctypes.data, kept_width,
+                              kc.ctypes.data, bd.ctypes.data)
+    if kept_width > 0:
+        return int(tok), kp[:kept_width], ki[:kept_width], int(kc[0]), float(bd[0])
+    return int(tok)
+
+
+def sample_batch(logits: np.ndarray, params, u: np.ndarray, exp_mode=EXP_PLATFORM, kept_width=0,
+                 nthreads=0, greedy_if_zero_t=True, argmax_first=False):
+    """Rows of a [B, V] f32 array.  params: list of (temperature, top_p, top_k)
+    per row (or one tuple).  Returns dict(tokens, kept_p, kept_idx, kept_count,
+    boundary_dist)."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    B, V = x.shape
+    flags = (FLAG_GREEDY_IF_ZERO_T if greedy_if_zero_t else 0) | (FLAG_ARGMAX_FIRST if argmax_first else 0)
+    if isinstance(params, tuple):
+        arr = (OracleParams * 1)(OracleParams(params[0], params[1], params[2], flags))
+        per_row = 0
+    else:
+        arr = (OracleParams * B)(*[OracleParams(t, p, k, flags) for (t, p, k) in params])
+        per_row = 1
+    uu = np.ascontiguousarray(u, dtype=np.float32)
+    out = np.zeros(B, np.uint32)
+    kw = max(kept_width, 0)
+    kp = np.zeros((B, max(kw, 1)), np.float32)
+    ki = np.zeros((B, max(kw, 1)), np.uint32)
+    kc = np.zeros(B, np.int64)
+    bd = np.zeros(B, np.float32)
+    lib().oracle_sample_batch(_fp(x), B, V, V, arr, per_row, _fp(uu), exp_mode, out.ctypes.data,
+                              kp.ctypes.data if kw else None, ki.ctypes.data if kw else None, kw,
+                              kc.ctypes.data, bd.ctypes.data, int(nthreads))
+    return dict(tokens=out, kept_p=kp[:, :kw], kept_idx=ki[:, :kw], kept_count=kc, boundary_dist=bd)
+
+
+# ---------------------------------------------------------------------------
+# Independent pure-Python restatement (numpy float32 scalars), small rows only.
+# ---------------------------------------------------------------------------
+def _exp_cr(x: np.float32) -> np.float32:
+    if np.isnan(x):
+        return np.float32(np.nan)
+    if x == -np.inf:
+        return np.float32(0.0)
+    return np.float32(math.exp(float(x)))
+
+
+def py_argmax(logits) -> int:
+    x = [np.float32(v) for v in logits]
+    if not x:
+        return 0
+    best = 0
+    for i in range(1, len(x)):
+        if not (x[best] > x[i]):
+            best = i
+    return best
+
+
+def py_sample(logits, temperature, top_p, top_k, r):
+    """sampling.rs:39-112 with exp correctly rounded; returns (token, kept list)."""
+    f32 = np.float32
+    lg = [f32(v) for v in logits]
+    T = f32(temperature)
+    scaled = [v / T for v in lg] if T > f32(0.0) else list(lg)
+    m = f32(-np.inf)
+    for v in scaled:
+        m = v if np.isnan(m) else (m if np.isnan(v) else max(m, v))
+    with np.errstate(invalid="ignore", over="ignore"):
+        exps = [_exp_cr(f32(v - m)) for v in scaled]
+        s = f32(-0.0)
+        for e in exps:
+            s = f32(s + e)
+        if s > f32(0.0):
+            probs = [f32(e / s) for e in exps]
+        else:
+            probs = [f32(1.0) / f32(len(lg))] * len(lg)
+    ip = [(p, i) for i, p in enumerate(probs)]
+    if top_k > 0:
+        ip = sorted(ip, key=lambda t: -float(t[0]))
+        ip = ip[:min(top_k, len(ip))]
+    if f32(top_p) > f32(0.0) and top_k == 0:
+        ip = sorted(ip, key=lambda t: -float(t[0]))
+        c = f32(0.0)
+        cut = len(ip)
+        for i, (p, _) in enumerate(ip):
+            c = f32(c + p)
+            if c >= f32(top_p):
+                cut = i + 1
+                break
+        ip = ip[:cut]
+    total = f32(-0.0)
+    for p, _ in ip:
+        total = f32(total + p)
+    if total <= f32(0.0):
+        return py_argmax(logits), ip
+    norm = [(f32(p / total), i) for p, i in ip]
+    c = f32(0.0)
+    rr = f32(r)
+    for p, i in norm:
+        c = f32(c + p)
+        if rr <= c:
+            return i, ip
+    return (norm[-1][1] if norm else 0), ip

@@ -1,0 +1,176 @@
+"""GPU parity: the CUDA sampler against the CPU oracle, through the C ABI.
+
+Bar (from the drop-in contract):
+  * with exp correctly rounded in the oracle, every output is bit-identical:
+    token, kept-list length, kept indices and kept probabilities (bits);
+  * against the oracle with the platform expf (what the Rust reference calls),
+    top-k index sets are identical, probabilities agree within 1e-5 relative,
+    and tokens differ on at most 1e-4 of the rows whose draw is not within
+    1e-6 of a cumulative-probability boundary.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+import synth
+
+pytestmark = pytest.mark.gpu
+
+KW = 64  # kept-list entries compared per row
+PROB_RTOL = 1e-5
+BAND = 1e-6
+
+
+def run_gpu(sampler, x_f32, params, u, bf16=False, ld=None, kept_width=KW):
+    import torch
+    import pesti_sampler as ps
+    B, V = x_f32.shape
+    if bf16:
+        bits = synth.f32_to_bf16_bits(x_f32)
+        host = torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16)
+    else:
+        host = torch.from_numpy(np.ascontiguousarray(x_f32))
+    if ld is not None and ld != V:
+        big = torch.zeros((B, ld), dtype=host.dtype)
+        big[:, :V] = host
+        dev = big.cuda()[:, :V]
+    else:
+        dev = host.cuda()
+    cfgs = [ps.SamplingConfig(temperature=t, top_p=p, top_k=k) for (t, p, k) in params]
+    ud = torch.from_numpy(np.ascontiguousarray(u, dtype=np.float32)).cuda()
+    tok, kp, ki, kc = sampler.sample_batch(dev, cfgs, ud, kept_width=kept_width)
+    torch.cuda.synchronize()
+    return (tok.cpu().numpy().view(np.uint32), kp.cpu().numpy(), ki.cpu().numpy().view(np.uint32),
+            kc.cpu().numpy())
+
+
+def check_exact(x, params, u, got, label):
+    want = O.sample_batch(x, params, u, O.EXP_CR, kept_width=KW)
+    tok, kp, ki, kc = got
+    bad = np.nonzero(tok != want["tokens"])[0]
+    assert bad.size == 0, f"{label}: token mismatch rows {bad[:10]} got {tok[bad[:5]]} want {want['tokens'][bad[:5]]}"
+    assert np.array_equal(kc, want["kept_count"]), f"{label}: kept counts differ"
+    assert np.array_equal(ki, want["kept_idx"]), f"{label}: kept indices differ"
+    assert np.array_equal(kp.view(np.uint32), want["kept_p"].view(np.uint32)), f"{label}: kept probabilities differ"
+
+
+def check_reference_tolerances(x, params, u, got, label):
+    ref = O.sample_batch(x, params, u, O.EXP_PLATFORM, kept_width=KW)
+    tok, kp, ki, kc = got
+    B = len(tok)
+    mism = tok != ref["tokens"]
+    near = ref["boundary_dist"] <= BAND
+    outside = int((mism & ~near).sum())
+    # top-k sets (top_k > 0 rows that are not greedy)
+    for b in range(B):
+        t, p, k = params[b]
+        if t != 0.0 and k > 0 and k <= KW:
+            assert set(ki[b, :k].tolist()) == set(ref["kept_idx"][b, :k].tolist()), f"{label}: top-k set row {b}"
+    valid = ref["kept_idx"] != 0xFFFFFFFF
+    rp, gp = ref["kept_p"][valid].astype(np.float64), kp[valid].astype(np.float64)
+    same_idx = ki[valid] == ref["kept_idx"][valid]
+    rel = np.abs(gp[same_idx] - rp[same_idx]) / np.maximum(np.abs(rp[same_idx]), 1e-38)
+    print(f"[{label}] rows={B} token mismatches={int(mism.sum())} (outside 1e-6 band: {outside}, "
+          f"rows near a boundary: {int(near.sum())}) max rel prob err={rel.max() if rel.size else 0:.3g}")
+    assert rel.size == 0 or rel.max() <= PROB_RTOL
+    assert outside <= max(1e-4 * B, 0), f"{label}: {outside} token mismatches outside the boundary band"
+
+
+@pytest.mark.parametrize("w,B", [(1, 64), (2, 16), (3, 8), (4, 200), (5, 8)])
+def test_workloads_reduced_batch(sampler, w, B):
+    spec = synth.WORKLOADS[w]
+    V = spec["V"]
+    x = synth.make_logits(w, B=B)
+    params = synth.params_for(w, B, V)
+    u = synth.make_u(w, B)
+    got = run_gpu(sampler, x, params, u, bf16=spec["dtype"] == "bf16")
+    check_exact(x, params, u, got, f"workload{w}")
+    check_reference_tolerances(x, params, u, got, f"workload{w}")
+
+
+@pytest.mark.parametrize("w", [2, 4])
+def test_workloads_full_size(sampler, w):
+    spec = synth.WORKLOADS[w]
+    B, V = spec["B"], spec["V"]
+    x = synth.make_logits(w)
+    params = synth.params_for(w, B, V)
+    u = synth.make_u(w)
+    got = run_gpu(sampler, x, params, u, bf16=spec["dtype"] == "bf16")
+    check_exact(x, params, u, got, f"workload{w}-full")
+    check_reference_tolerances(x, params, u, got, f"workload{w}-full")
+
+
+def _edge_cases():
+    rng = np.random.default_rng(5)
+    cases = []
+    cases.append(("tiny-V", np.array([[0.1, 0.9, 0.3, 0.7]], np.float32), [(1.0, 0.0, 2)]))
+    cases.append(("V1", np.array([[3.0]], np.float32), [(1.0, 0.9, 0)]))
+    cases.append(("all-neg-inf", np.full((1, 37), -np.inf, np.float32), [(1.0, 0.9, 0)]))
+    x = rng.standard_normal((3, 97)).astype(np.float32)
+    x[0, 5] = np.nan
+    x[1, 7] = np.inf
+    cases.append(("nan-inf", x, [(1.0, 0.0, 5), (0.8, 0.95, 0), (1.0, 0.0, 0)]))
+    x = rng.standard_normal((4, 1000)).astype(np.float32)
+    cases.append(("temperatures", x, [(-1.0, 0.9, 0), (float("nan"), 0.0, 3), (1e-30, 0.0, 0), (1e30, 0.5, 0)]))
+    x = (rng.standard_normal((6, 5000)) * 40).astype(np.float32)  # large dynamic range: pruning
+    cases.append(("wide", x, [(0.1, 0.9, 0), (0.1, 0.0, 50), (1.0, 0.0, 0), (3.0, 0.95, 0), (0.5, 0.0, 3000), (0.5, 0.0, 5000)]))
+    x = np.round(rng.standard_normal((6, 4096)) * 2).astype(np.float32)  # many equal logits
+    cases.append(("ties", x, [(1.0, 0.0, 10), (1.0, 0.9, 0), (0.7, 0.0, 0), (1.0, 0.0, 4096), (1.0, 0.0, 1), (1.0, 1.0, 0)]))
+    x = np.zeros((2, 3000), np.float32)
+    cases.append(("constant", x, [(1.0, 0.9, 0), (1.0, 0.0, 7)]))
+    x = (rng.standard_normal((3, 20001)) * 3).astype(np.float32)  # odd V, vector tails
+    cases.append(("odd-V", x, [(0.9, 0.0, 64), (1.0, 0.95, 0), (0.8, 0.0, 1500)]))
+    return cases
+
+
+@pytest.mark.parametrize("case", _edge_cases(), ids=lambda c: c[0])
+def test_edge_cases(sampler, case):
+    name, x, params = case
+    B = x.shape[0]
+    for u in (np.zeros(B, np.float32), np.full(B, 0.5, np.float32), np.full(B, np.float32(0.99999994))):
+        got = run_gpu(sampler, x, params, u)
+        check_exact(x, params, u, got, name)
+
+
+def test_unaligned_rows_and_bf16(sampler):
+    rng = np.random.default_rng(9)
+    x = (rng.standard_normal((5, 3001)) * 2).astype(np.float32)
+    params = [(0.8, 0.0, 40)] * 5
+    u = rng.random(5).astype(np.float32)
+    check_exact(x, params, u, run_gpu(sampler, x, params, u, ld=3003), "unaligned")
+    xb = synth.bf16_bits_to_f32(synth.f32_to_bf16_bits(x))
+    params = [(1.0, 0.95, 0), (0.7, 0.0, 50), (0.0, 0.0, 0), (1.0, 0.0, 0), (1.2, 0.5, 0)]
+    check_exact(xb, params, u, run_gpu(sampler, xb, params, u, bf16=True), "bf16")
+    check_exact(xb, params, u, run_gpu(sampler, xb, params, u, bf16=True, ld=3005), "bf16-unaligned")
+
+
+def test_reference_unit_tests_on_gpu(sampler):
+    import pesti_sampler as ps
+    assert sampler.argmax([0.1, 0.9, 0.3, 0.7]) == 1
+    cfg = ps.SamplingConfig(temperature=1.0, top_p=0.0, top_k=2)
+    seen = {sampler.sample_with_u([0.1, 0.9, 0.3, 0.7], cfg, float(r)) for r in np.linspace(0, 0.9999, 65)}
+    assert seen == {1, 3}
+    x = [i * 0.01 for i in range(100)]
+    rng = ps.Pcg32(42)
+    assert sampler.sample(x, ps.SamplingConfig(), rng) < 100
+    assert sampler.sample_with_u([], ps.SamplingConfig(), 0.5) == 0
+
+
+def test_argmax_batch_semantics(sampler):
+    import torch
+    x = np.array([[1.0, 3.0, 3.0, 2.0], [5.0, np.nan, 1.0, 2.0], [5.0, 1.0, np.nan, np.nan],
+                  [-np.inf, -np.inf, -np.inf, -np.inf]], np.float32)
+    d = torch.from_numpy(x).cuda()
+    last = sampler.argmax_batch(d).cpu().numpy()
+    first = sampler.argmax_batch(d, first=True).cpu().numpy()
+    assert list(last) == [O.argmax(r) for r in x]
+    assert list(first) == [O.argmax_first(r) for r in x]
+
+
+def test_host_row_api_matches_oracle(sampler):
+    import pesti_sampler as ps
+    x = synth.make_logits(1, B=20)
+    u = synth.make_u(1, 20)
+    for b in range(20):
+        t = sampler.sample_with_u(x[b], ps.SamplingConfig(0.8, 0.95, 40), float(u[b]))
+        assert t == O.sample(x[b], 0.8, 0.95, 40, float(u[b]), O.EXP_CR)

@@ -401,21 +401,23 @@ __device__ __noinline__ int block_radix_sort(uint32_t* k0, uint32_t* v0, uint32_
     }
     __syncthreads();
     if (sm.skip) continue;  // uniform across the block
-    // exclusive scan in (digit, warp) order: 16 counters per thread
-    uint32_t loc[16];
+    // exclusive scan in (digit, warp) order: CPT counters per thread
+    constexpr int CPT = NW * 256 / NT;
+    static_assert(CPT * NT == NW * 256, "counter split");
+    uint32_t loc[CPT];
     uint32_t s = 0;
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      const int i = tid * 16 + r;  // i = digit*16 + warp
-      loc[r] = sm.hist[i & 15][i >> 4];
+    for (int r = 0; r < CPT; ++r) {
+      const int i = tid * CPT + r;  // i = digit*NW + warp
+      loc[r] = sm.hist[i % NW][i / NW];
       s += loc[r];
     }
     uint32_t tot;
     uint32_t ex = block_excl_scan_add(s, sm.iscr, tot);
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      const int i = tid * 16 + r;
-      sm.hist[i & 15][i >> 4] = ex;
+    for (int r = 0; r < CPT; ++r) {
+      const int i = tid * CPT + r;
+      sm.hist[i % NW][i / NW] = ex;
       ex += loc[r];
     }
     __syncthreads();

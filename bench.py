@@ -9,7 +9,7 @@ each rank samples its own 64 rows, no collective on the data path).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 Keys beyond the base contract:
-  roofline      the slice scan (the HBM pass over the logits; the dominant
+  roofline      the slice-max pass (the HBM pass over the logits; the dominant
                 kernel), achieved = logit bytes per launch / its mean CUDA-event
                 duration, against the measured HBM copy bandwidth
   step_hbm_gbs  logit bytes / whole step time (both kernels)
@@ -264,18 +264,19 @@ def main():
     lib = ps.load_library()
     import ctypes
     lib.pesti_profile_enable.argtypes = [ctypes.c_void_p, ctypes.c_int]
-    lib.pesti_profile_read.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_double),
-                                       ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int)]
+    lib.pesti_profile_read.argtypes = [ctypes.c_void_p] + [ctypes.POINTER(ctypes.c_double)] * 3 + \
+        [ctypes.POINTER(ctypes.c_int)]
     lib.pesti_profile_enable(s._h, 1)
     prof_steps = min(args.steps, 1000)
     for i in range(prof_steps):
         step(i)
     torch.cuda.synchronize()
-    a, b_, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_int()
-    lib.pesti_profile_read(s._h, ctypes.byref(a), ctypes.byref(b_), ctypes.byref(n))
+    t_max, t_surv, t_row, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_double(), ctypes.c_int()
+    lib.pesti_profile_read(s._h, ctypes.byref(t_max), ctypes.byref(t_surv), ctypes.byref(t_row), ctypes.byref(n))
     lib.pesti_profile_enable(s._h, 0)
-    scan_ms = a.value / max(1, n.value)
-    row_ms = b_.value / max(1, n.value)
+    scan_ms = t_max.value / max(1, n.value)
+    surv_ms = t_surv.value / max(1, n.value)
+    row_ms = t_row.value / max(1, n.value)
     peak, peak_kind = measured_peaks()
     achieved = step_bytes / (scan_ms / 1e3) / 1e9
     traffic = None
@@ -351,14 +352,14 @@ def main():
                        "params": "T0.7 top_k50 top_p0.9 (top-p unused since top_k > 0, sampling.rs:66)",
                        "l2": f"rotating {nbuf} input buffers ({nbuf * step_bytes / 2**20:.0f} MiB > 126 MiB L2)",
                        "parallelism": f"rows split, {world} GPU(s), no collective"},
-            "roofline": {"bound": "hbm", "kernel": "slice_scan", "achieved": achieved, "peak": peak,
+            "roofline": {"bound": "hbm", "kernel": "slice_max", "achieved": achieved, "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": traffic, "scan_us": scan_ms * 1e3, "row_us": row_ms * 1e3,
-                         "bytes_per_launch": step_bytes},
+                         "traffic": traffic, "bytes_per_launch": step_bytes},
+            "kernel_us": {"slice_max": scan_ms * 1e3, "survivors": surv_ms * 1e3, "row": row_ms * 1e3},
             "step_hbm_gbs": step_bytes / (ms_per_step / 1e3) / 1e9,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": step_bytes + B * 4,
                     "d2h_bytes_per_step": B * 4},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": 3 * args.steps,
             "clocks": clk,
             "b1_latency_us": lat,
             "cpu_baseline": cpu,

@@ -392,7 +392,12 @@ __device__ __noinline__ int block_radix_sort(uint32_t* k0, uint32_t* v0, uint32_
     for (int i = tid; i < NW * 256; i += NT) (&sm.hist[0][0])[i] = 0u;
     if (tid == 0) sm.skip = 0;
     __syncthreads();
-    for (long long j = beg + lane; j < end; j += 32) atomicAdd(&sm.hist[w][(kin[j] >> shift) & 255u], 1u);
+    for (long long j0 = beg; j0 < end; j0 += 32) {
+      const long long j = j0 + lane;
+      const uint32_t d = j < end ? ((kin[j] >> shift) & 255u) : 256u + (uint32_t)lane;
+      const uint32_t peers = __match_any_sync(PESTI_FULL_MASK, d);  // one add per digit per warp
+      if (d < 256u && (peers & ((1u << lane) - 1u)) == 0u) sm.hist[w][d] += (uint32_t)__popc(peers);
+    }
     __syncthreads();
     if (tid < 256) {
       uint32_t t = 0;

@@ -54,7 +54,7 @@ struct pesti_sampler {
   static constexpr int kProfMax = 4096;
   bool prof = false;
   int prof_n = 0;
-  cudaEvent_t prof_ev[kProfMax][3] = {};
+  cudaEvent_t prof_ev[kProfMax][4] = {};
 };
 
 namespace {
@@ -69,7 +69,9 @@ Geometry pick_geometry(const pesti_sampler* s, long long B, long long V, int ve)
   long long P = (target + B - 1) / std::max(1LL, B);
   const long long pmax_v = std::max(1LL, V / (pesti::K1_WARPS * 1024LL));
   P = std::max(1LL, std::min({P, pmax_v, (long long)(pesti::MAX_SUBS / pesti::K1_WARPS)}));
-  const long long unit = 32LL * ve;
+  // whole 16-byte-vector chunks per sub-slice (32 lanes x 16 bytes x 8 or 4
+  // loads in flight = 1024 elements): only the row's last sub-slice has a tail
+  const long long unit = 1024;
   long long SL = (V + P * pesti::K1_WARPS - 1) / (P * pesti::K1_WARPS);
   SL = std::max(unit, (SL + unit - 1) / unit * unit);
   P = std::max(1LL, (V + SL * pesti::K1_WARPS - 1) / (SL * pesti::K1_WARPS));
@@ -113,21 +115,33 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
   const int ve = 16 / esize;
   const Geometry g = pick_geometry(s, B, V > 0 ? V : 1, ve);
   const long long nsub = (long long)g.P * pesti::K1_WARPS;
+  const long long nseg = (std::max(1LL, V) + 32LL * ve - 1) / (32LL * ve);
   const size_t bv = (size_t)B * (size_t)std::max(1LL, V);
   size_t off = 0;
-  const size_t o_meta = off; off = align_up(off + (size_t)B * nsub * sizeof(pesti::WarpMeta));
-  const size_t o_sraw = off; off = align_up(off + bv * 4);
-  const size_t o_sidx = off; off = align_up(off + bv * 4);
-  const size_t o_E = off; off = align_up(off + bv * 4);
-  const size_t o_I = off; off = align_up(off + bv * 4);
-  const size_t o_status = off; off = align_up(off + 16);
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes);
+    return o;
+  };
+  const size_t o_stats = take((size_t)B * nsub * sizeof(pesti::SubStat));
+  const size_t o_surv = take((size_t)B * nsub * sizeof(pesti::SubSurv));
+  const size_t o_segmax = take((size_t)B * nseg * 4);
+  const size_t o_se = take(bv * 4);
+  const size_t o_si = take(bv * 4);
+  const size_t o_cc = take((size_t)B * 4);
+  const size_t o_ce = take((size_t)B * pesti::CAND_CAP * 4);
+  const size_t o_ci = take((size_t)B * pesti::CAND_CAP * 4);
+  const size_t o_tau = take((size_t)B * 4);
+  const size_t o_E = take(bv * 4);
+  const size_t o_I = take(bv * 4);
+  const size_t o_status = take(16);
   size_t o_sk0 = 0, o_sv0 = 0, o_sk1 = 0, o_sv1 = 0, o_q = 0;
   if (sorted_bufs) {
-    o_sk0 = off; off = align_up(off + bv * 4);
-    o_sv0 = off; off = align_up(off + bv * 4);
-    o_sk1 = off; off = align_up(off + bv * 4);
-    o_sv1 = off; off = align_up(off + bv * 4);
-    o_q = off; off = align_up(off + bv * 4);
+    o_sk0 = take(bv * 4);
+    o_sv0 = take(bv * 4);
+    o_sk1 = take(bv * 4);
+    o_sv1 = take(bv * 4);
+    o_q = take(bv * 4);
   }
   int rc = ensure_ws(s, off);
   if (rc) return rc;
@@ -142,29 +156,46 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
   sa.per_row = d_per_row;
   sa.P = g.P;
   sa.SL = g.SL;
-  sa.meta = (pesti::WarpMeta*)(ws + o_meta);
-  sa.surv_raw = (float*)(ws + o_sraw);
-  sa.surv_idx = (uint32_t*)(ws + o_sidx);
+  sa.nseg = nseg;
+  sa.stats = (pesti::SubStat*)(ws + o_stats);
+  sa.surv = (pesti::SubSurv*)(ws + o_surv);
+  sa.seg_max = (float*)(ws + o_segmax);
+  sa.surv_e = (float*)(ws + o_se);
+  sa.surv_idx = (uint32_t*)(ws + o_si);
+  sa.cand_count = (int*)(ws + o_cc);
+  sa.cand_e = (float*)(ws + o_ce);
+  sa.cand_idx = (uint32_t*)(ws + o_ci);
+  sa.row_tau = (float*)(ws + o_tau);
 
   cudaEvent_t* pev = nullptr;
   if (s->prof && s->prof_n < pesti_sampler::kProfMax) {
     pev = s->prof_ev[s->prof_n++];
-    for (int q = 0; q < 3; ++q)
+    for (int q = 0; q < 4; ++q)
       if (!pev[q]) PESTI_CUDA_TRY(cudaEventCreate(&pev[q]), "cudaEventCreate(profile)");
     PESTI_CUDA_TRY(cudaEventRecord(pev[0], st), "cudaEventRecord(profile)");
   }
   const bool aligned = ((uintptr_t)d_logits % 16 == 0) && ((ld * esize) % 16 == 0);
   const dim3 g1((unsigned)(g.P * B));
   if (dtype == PESTI_BF16) {
-    if (aligned) pesti::slice_scan_kernel<uint16_t, 8, 4, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
-    else pesti::slice_scan_kernel<uint16_t, 8, 4, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
+    if (aligned) pesti::slice_stats_kernel<uint16_t, 8, 4, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
+    else pesti::slice_stats_kernel<uint16_t, 8, 4, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
   } else {
-    if (aligned) pesti::slice_scan_kernel<float, 4, 8, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
-    else pesti::slice_scan_kernel<float, 4, 8, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
+    if (aligned) pesti::slice_stats_kernel<float, 4, 8, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
+    else pesti::slice_stats_kernel<float, 4, 8, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
   }
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "slice_scan_kernel launch");
+  if (e != cudaSuccess) return cuda_fail(e, "slice_stats_kernel launch");
   if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[1], st), "cudaEventRecord(profile)");
+  if (dtype == PESTI_BF16) {
+    if (aligned) pesti::survivor_kernel<uint16_t, 8, 4, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
+    else pesti::survivor_kernel<uint16_t, 8, 4, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
+  } else {
+    if (aligned) pesti::survivor_kernel<float, 4, 8, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
+    else pesti::survivor_kernel<float, 4, 8, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "survivor_kernel launch");
+  if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[2], st), "cudaEventRecord(profile)");
 
   pesti::RowArgs ra;
   ra.logits = d_logits;
@@ -176,9 +207,14 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
   ra.per_row = d_per_row;
   ra.P = g.P;
   ra.SL = g.SL;
-  ra.meta = sa.meta;
-  ra.surv_raw = sa.surv_raw;
+  ra.stats = sa.stats;
+  ra.surv = sa.surv;
+  ra.surv_e = sa.surv_e;
   ra.surv_idx = sa.surv_idx;
+  ra.cand_count = sa.cand_count;
+  ra.cand_e = sa.cand_e;
+  ra.cand_idx = sa.cand_idx;
+  ra.row_tau = sa.row_tau;
   ra.E = (float*)(ws + o_E);
   ra.I = (uint32_t*)(ws + o_I);
   ra.SK0 = sorted_bufs ? (uint32_t*)(ws + o_sk0) : nullptr;
@@ -196,7 +232,7 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
   pesti::row_kernel<<<(unsigned)B, pesti::K2_NT, sizeof(pesti::RowShared), st>>>(ra);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "row_kernel launch");
-  if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[2], st), "cudaEventRecord(profile)");
+  if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[3], st), "cudaEventRecord(profile)");
   return PESTI_OK;
 }
 
@@ -256,7 +292,7 @@ void pesti_sampler_destroy(pesti_sampler* s) {
   if (s->d_tok1) cudaFree(s->d_tok1);
   if (s->params_ev) cudaEventDestroy(s->params_ev);
   for (int i = 0; i < pesti_sampler::kProfMax; ++i)
-    for (int q = 0; q < 3; ++q)
+    for (int q = 0; q < 4; ++q)
       if (s->prof_ev[i][q]) cudaEventDestroy(s->prof_ev[i][q]);
   if (s->stream) cudaStreamDestroy(s->stream);
   delete s;
@@ -365,19 +401,20 @@ int pesti_profile_enable(pesti_sampler* s, int enable) {
   return PESTI_OK;
 }
 
-int pesti_profile_read(pesti_sampler* s, double* scan_ms, double* row_ms, int* calls) {
-  if (!s || !scan_ms || !row_ms || !calls) return fail(PESTI_E_INVALID_ARG, "null argument");
-  double a = 0.0, b = 0.0;
+int pesti_profile_read(pesti_sampler* s, double* max_ms, double* surv_ms, double* row_ms, int* calls) {
+  if (!s || !max_ms || !surv_ms || !row_ms || !calls) return fail(PESTI_E_INVALID_ARG, "null argument");
+  double t[3] = {0.0, 0.0, 0.0};
   for (int i = 0; i < s->prof_n; ++i) {
-    PESTI_CUDA_TRY(cudaEventSynchronize(s->prof_ev[i][2]), "cudaEventSynchronize(profile)");
-    float t1 = 0.f, t2 = 0.f;
-    PESTI_CUDA_TRY(cudaEventElapsedTime(&t1, s->prof_ev[i][0], s->prof_ev[i][1]), "cudaEventElapsedTime");
-    PESTI_CUDA_TRY(cudaEventElapsedTime(&t2, s->prof_ev[i][1], s->prof_ev[i][2]), "cudaEventElapsedTime");
-    a += t1;
-    b += t2;
+    PESTI_CUDA_TRY(cudaEventSynchronize(s->prof_ev[i][3]), "cudaEventSynchronize(profile)");
+    for (int q = 0; q < 3; ++q) {
+      float ms = 0.f;
+      PESTI_CUDA_TRY(cudaEventElapsedTime(&ms, s->prof_ev[i][q], s->prof_ev[i][q + 1]), "cudaEventElapsedTime");
+      t[q] += ms;
+    }
   }
-  *scan_ms = a;
-  *row_ms = b;
+  *max_ms = t[0];
+  *surv_ms = t[1];
+  *row_ms = t[2];
   *calls = s->prof_n;
   return PESTI_OK;
 }

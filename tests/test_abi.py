@@ -8,12 +8,13 @@ import subprocess
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADER = os.path.join(ROOT, "include", "pesti_sampler.h")
+HEADERS = [os.path.join(ROOT, "include", h) for h in sorted(os.listdir(os.path.join(ROOT, "include")))
+           if h.endswith(".h")]
 LIB = os.path.join(ROOT, "llm-workspace_b200", "libpesti_sampler.so")
 
 
 def declared_functions():
-    text = open(HEADER).read()
+    text = "\n".join(open(h).read() for h in HEADERS)
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     return sorted(set(re.findall(r"\b(pesti_[a-z0-9_]+)\s*\(", text)))
 

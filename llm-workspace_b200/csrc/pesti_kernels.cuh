@@ -5,15 +5,18 @@
 //
 // Three kernels per batch:
 //   slice_stats_kernel  the one HBM pass: per sub-slice (one warp each) the max
-//                       and argmax of the raw logits, NaN/inf flags, an
-//                       approximate partial softmax sum and per-segment maxima;
-//   survivor_kernel     re-reads each sub-slice (from L2) knowing the row max:
-//                       drops the elements that provably do not change any
-//                       fold, computes exp exactly for the rest, summarises
-//                       each sub-slice's part of the softmax fold and lists
-//                       the top-k candidates;
-//   row_kernel          one block per row: resolves the softmax fold from the
-//                       summaries, then top-k / top-p / draw.
+//                       of the raw logits, NaN/inf flags, an approximate
+//                       partial softmax sum and per-segment maxima.  The last
+//                       block of each row to finish turns these into the row
+//                       prologue (row max and argmax, candidate threshold,
+//                       per-sub-slice prefix mass and prefix max).
+//   survivor_kernel     re-reads each sub-slice (from L2): drops the elements
+//                       that provably do not change any fold, classifies the
+//                       rest into the sub-slice's part of the softmax fold
+//                       (runs of plain integer increments and single elements
+//                       to add directly) and lists the top-k candidates;
+//   row_kernel          one block per row: walks the fold entries to the exact
+//                       softmax sum, then top-k / top-p / draw.
 #pragma once
 #include <stdint.h>
 #include <cuda_bf16.h>
@@ -32,7 +35,12 @@ constexpr int TOPK_SMALL = 1024;  // top-k values handled by the generic candida
 constexpr int CAND_MAX = 2048;    // candidate buffer of that path
 constexpr int FAST_K = 256;       // top-k values handled by the fast path
 constexpr int CAND_CAP = 2048;    // candidates listed per row by the survivor kernel
+constexpr int FAST_CAND = 1024;   // candidates the fast path sorts
 constexpr int TAU_BINS = 4096;    // 12-bit histogram used to place the candidate threshold
+constexpr int NE = 32;            // fold entries per sub-slice
+constexpr int MAX_MATCH = 64;     // segments holding the row max re-scanned for its indices
+constexpr int QCAP = 512;         // survivor queue per warp (power of two)
+constexpr int STAGE = 256;        // values staged per round trip by warp_fold
 constexpr uint32_t TR_SAT = 0x40000000u;  // saturation of fold increments (>= any binade)
 
 // An element more than ABSORB scaled units below an EARLIER element of the
@@ -47,21 +55,38 @@ enum : uint32_t { MF_NAN = 1u, MF_POSINF = 2u, MF_NEGINF = 4u };
 
 struct SubStat {      // slice_stats_kernel, one per sub-slice
   float max_raw;      // max of the raw logits, NaN ignored (the f32::max fold, sampling.rs:126)
-  float sum_rel;      // sum of 2^(y - y_max), y = raw*log2(e)/T_eff (float, approximate)
-  uint32_t last_max;  // last index holding max_raw (0xffffffff if none)
-  uint32_t first_max; // first index holding max_raw
+  float sum_rel;      // sum of 2^(y - y_max), y = raw*log2(e)/T_eff (approximate)
   int32_t last_nan;   // last NaN index or -1
   uint32_t flags;     // MF_*
-  uint32_t pad[2];
+};
+
+struct RowInfo {      // row prologue, written by the last slice_stats block of the row
+  float max_raw;      // row max of the raw logits (NaN ignored)
+  float m;            // max of the scaled logits: RN(max_raw/T) when T > 0 (division is monotone)
+  float tau;          // candidate threshold (raw units); +inf when no candidates are needed
+  uint32_t flags;     // MF_* over the row
+  long long last_max, first_max, last_nan;  // argmax indices: greedy rows only
+  int uniform;        // the softmax sum is NaN or not > 0: all probabilities are 1/V
+  int pad;
+};
+
+struct SubPre {       // per sub-slice, from the row prologue
+  double A;           // approximate softmax mass of the earlier sub-slices
+  float P;            // max raw logit of the earlier sub-slices
+  float pad;
+};
+
+struct FoldEnt {      // one entry of a sub-slice's part of the softmax fold
+  uint32_t lo;        // binade (bits of its lowest value) of a run; fold::SPECIAL: one element
+  uint32_t a0, a1;    // run: increments for an even / odd entry state; special: bits of the value
+  uint32_t count;     // survivors covered
 };
 
 struct SubSurv {      // survivor_kernel, one per sub-slice
-  int32_t count;      // survivors stored (exact exp, logit index) at the sub-slice's own start
-  uint32_t lo_bits;   // binade the softmax fold is in when it enters the sub-slice
-                      // (speculated); fold::SPECIAL: replay the survivors one by one
-  uint32_t k0, k1;    // total fold increment (ulps of that binade) for an even / odd entry state
+  int32_t count;      // survivors stored (raw logit, index) at the sub-slice's own start
+  int32_t nent;       // fold entries
+  int32_t replay;     // entries overflowed: replay all survivors one by one
   float pruned_max;   // largest raw logit dropped (-inf if none)
-  uint32_t pad[3];
 };
 
 struct SliceArgs {
@@ -73,14 +98,17 @@ struct SliceArgs {
   long long SL;     // elements per sub-slice (one warp each)
   long long nseg;   // 32*VE-element segments per row
   SubStat* stats;   // [B][P*K1_WARPS]
+  SubPre* pre;      // [B][P*K1_WARPS]
+  RowInfo* info;    // [B]
+  int* row_ctr;     // [B] blocks of the row finished (reset by the last one)
   SubSurv* surv;    // [B][P*K1_WARPS]
+  FoldEnt* ents;    // [B][P*K1_WARPS][NE]
   float* seg_max;   // [B][nseg]
-  float* surv_e;    // [B][V]: survivors of sub-slice s compacted at its own start
+  float* surv_raw;  // [B][V]: raw logits of the survivors of sub-slice s, compacted at its own start
   uint32_t* surv_idx;
   int* cand_count;  // [B]
   float* cand_e;    // [B][CAND_CAP]
   uint32_t* cand_idx;
-  float* row_tau;   // [B] candidate threshold (raw units)
 };
 
 struct RowArgs {
@@ -91,14 +119,14 @@ struct RowArgs {
   const pesti_sampling_params* per_row;
   int P;
   long long SL;
-  const SubStat* stats;
+  const RowInfo* info;
   const SubSurv* surv;
-  const float* surv_e;
+  const FoldEnt* ents;
+  const float* surv_raw;
   const uint32_t* surv_idx;
   const int* cand_count;
   const float* cand_e;
   const uint32_t* cand_idx;
-  const float* row_tau;
   float* E;       // [B][V] sequence built by the generic path
   uint32_t* I;
   uint32_t* SK0;  // [B][V] sort buffers (null when no row needs them)
@@ -112,7 +140,8 @@ struct RowArgs {
   uint32_t* kept_idx;
   long long kept_width;
   int64_t* kept_count;
-  int* status;    // bit 0: a row needed sort buffers that were not provided
+  int* status;       // bit 0: a row needed sort buffers that were not provided
+  int fast_enabled;  // the launch provides the fast path's shared memory
 };
 
 __device__ __forceinline__ pesti_sampling_params row_params(const pesti_sampling_params& uni,
@@ -161,6 +190,17 @@ __device__ __forceinline__ float fkey_inv(uint32_t k) {
   return bitsf((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
+// 2^x by the hardware approximation (ex2.approx.ftz.f32, relative error about
+// 2^-22); used only for the approximate sums that steer the speculation.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Out-of-line copy of the exact exp for the kernels whose code size matters.
+__device__ __noinline__ float pesti_expf_call(float x) { return pesti_expf(x); }
+
 // ---------------------------------------------------------------------------
 // Fold transducers: the effect of a run of elements on the fold state while
 // it stays in one binade, as a pair of bit-increments for an even / odd entry
@@ -208,15 +248,21 @@ __device__ __forceinline__ Tr tr_warp_incl_scan(Tr t) {
 // loads (U of them in flight per lane) when the row is 16-byte aligned, scalar
 // loads for the tail.  f(x, pos0, nv) receives a lane's VE consecutive values
 // (nv valid) at positions pos0..; a call covers one 32*VE-element segment per
-// warp, and within a warp the calls run in row order.
+// warp, and within a warp the calls run in row order.  g() runs after every
+// chunk of U segments (and after every tail segment).
 // ---------------------------------------------------------------------------
-template <typename TIn, int VE, int U, bool VEC, typename F>
-__device__ __forceinline__ void stream_subslice(const TIn* row, long long start, long long end, F&& f) {
+struct NoChunkHook {
+  __device__ __forceinline__ void operator()() const {}
+};
+
+template <typename TIn, int VE, int U, bool VEC, typename F, typename G = NoChunkHook>
+__device__ __forceinline__ void stream_subslice(const TIn* row, long long start, long long end, F&& f,
+                                                G&& g = G()) {
   const int lane = threadIdx.x & 31;
   const long long CH = 32LL * VE * U;
   long long pos = start;
   if (VEC) {
-    for (; pos + CH <= end; pos += CH) {
+    for (; pos + CH <= end; pos += CH, g()) {
       float4 raw[U];
 #pragma unroll
       for (int uu = 0; uu < U; ++uu) {
@@ -241,7 +287,7 @@ __device__ __forceinline__ void stream_subslice(const TIn* row, long long start,
       }
     }
   }
-  for (; pos < end; pos += 32LL * VE) {
+  for (; pos < end; pos += 32LL * VE, g()) {
     float x[VE];
     const long long p0 = pos + (long long)lane * VE;
     int nv = 0;
@@ -260,174 +306,103 @@ __device__ __forceinline__ void stream_subslice(const TIn* row, long long start,
 }
 
 // ---------------------------------------------------------------------------
-// Pass 1, the HBM pass.
+// Pass 1, the HBM pass, and the row prologue.
 // ---------------------------------------------------------------------------
-template <typename TIn, int VE, int U, bool VEC>
-__global__ void __launch_bounds__(K1_NT) slice_stats_kernel(SliceArgs a) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const long long b = blockIdx.x / a.P;
-  const int slice = (int)(blockIdx.x % a.P);
-  const long long sub = (long long)slice * K1_WARPS + w;
-  const long long start = sub * a.SL;
-  long long end = start + a.SL;
-  if (end > a.V) end = a.V;
-  if (slice == 0 && w == 0 && lane == 0) a.cand_count[b] = 0;
-  const TIn* row = (const TIn*)a.logits + b * a.ld;
-  const pesti_sampling_params prm = row_params(a.uni, a.per_row, b);
-  const float c2 = 1.4426950408889634f / (prm.temperature > 0.0f ? prm.temperature : 1.0f);
-  const float NEG_INF = -__int_as_float(0x7f800000);
-  float best_v = NEG_INF, fbest_v = NEG_INF;
-  long long best_i = -1, fbest_i = -1, last_nan = -1;
-  uint32_t flags = 0;
-  float run_m = NEG_INF, run_s = 0.0f;  // online partial sum, log2 units
-  float* segmax = a.seg_max + b * a.nseg;
-  stream_subslice<TIn, VE, U, VEC>(row, start, end, [&](const float* x, long long pos0, int nv) {
-    float lm = NEG_INF;
-#pragma unroll
-    for (int e = 0; e < VE; ++e) {
-      if (e >= nv) continue;
-      const float xv = x[e];
-      const long long pos = pos0 + e;
-      if (is_nan(xv)) {
-        last_nan = pos;
-        flags |= MF_NAN;
-        continue;
-      }
-      lm = fmaxf(lm, xv);
-      if (best_i < 0 || xv >= best_v) { best_v = xv; best_i = pos; }
-      if (fbest_i < 0 || xv > fbest_v) { fbest_v = xv; fbest_i = pos; }
-      if (xv == -NEG_INF) flags |= MF_POSINF;
-      if (xv == NEG_INF) flags |= MF_NEGINF;
-    }
-    // approximate partial softmax sum (guides the fold speculation only)
-    const float nm = fmaxf(run_m, lm * c2);
-    if (nm > NEG_INF) {
-      float acc = run_s * exp2f(run_m - nm);
-#pragma unroll
-      for (int e = 0; e < VE; ++e)
-        if (e < nv && !is_nan(x[e])) acc += exp2f(x[e] * c2 - nm);
-      run_s = acc;
-      run_m = nm;
-    }
-    const float sm = warp_reduce_fmax(lm);
-    if (lane == 0) segmax[(pos0 - (long long)lane * VE) / (32LL * VE)] = sm;
-  });
-  const float mx = warp_reduce_fmax(best_i >= 0 ? best_v : NEG_INF);
-  long long li = (best_i >= 0 && best_v == mx) ? best_i : -1;
-  long long fi = (fbest_i >= 0 && fbest_v == mx) ? fbest_i : (1LL << 62);
-  li = warp_reduce_max(li);
-  fi = warp_reduce_min(fi);
-  const long long ln = warp_reduce_max(last_nan);
-  uint32_t fl = flags;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) fl |= __shfl_xor_sync(PESTI_FULL_MASK, fl, o);
-  const float wm = warp_reduce_fmax(run_m);
-  float ws = (run_m > NEG_INF && wm > NEG_INF) ? run_s * exp2f(run_m - wm) : 0.0f;
-  ws = warp_reduce_add(ws);
-  if (lane == 0) {
-    SubStat m;
-    m.max_raw = mx;
-    m.sum_rel = ws;  // relative to 2^(mx*c2) (wm == mx*c2: the same float product)
-    m.last_max = li >= 0 ? (uint32_t)li : 0xffffffffu;
-    m.first_max = fi < (1LL << 62) ? (uint32_t)fi : 0xffffffffu;
-    m.last_nan = (int32_t)ln;
-    m.flags = fl;
-    m.pad[0] = m.pad[1] = 0;
-    a.stats[b * (long long)a.P * K1_WARPS + sub] = m;
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Pass 2: survivors, exact exp, fold summaries, top-k candidates.
-//
-// Which elements may be dropped (x_i = raw_i/T is the scaled logit):
-//  (a) prefix max: an EARLIER element j with x_j >= x_i + 17.34 gives
-//      e_i <= 0.989*2^-25*e_j; the running softmax sum s_{i-1} >= e_j and
-//      ulp(s)/2 > s*2^-25, so fl(s + e_i) returns s.  The same ratio makes i a
-//      no-op in the sorted folds (they start at p_max >= p_j) and in the
-//      index-order folds of p and q.  Tested on raw values as
-//      raw_i < P - (17.35*T*(1+2^-20) + 2^-21*|P|), P = prefix max; the slack
-//      covers the rounding of raw/T, of x - m (<= 2^-24*104 wherever exp is
-//      not 0) and of exp.  Used while P/T >= m - 60.
-//  (b) running sum: each step of a fold of non-negative terms has relative
-//      error <= 2^-24, so s_{i-1} >= (sum_{j<i} e_j)*(1 - V*2^-24).  With the
-//      approximate prefix sum A of the earlier sub-slices (pass 1),
-//      L = A*(1 - V*2^-24)*(1 - 2^-10) <= s_{i-1}, and e_i < 0.99*2^-25*L makes
-//      i a no-op in the index-order folds (also for p = e/S and q = p/total,
-//      whose running sums are bounded the same way).  It does NOT bound the
-//      sorted folds, so it is used only for top-k rows (whose kept list is
-//      explicit and checked) and unfiltered rows (index order only).
-// ---------------------------------------------------------------------------
-struct SurvShared {
+struct StatsShared {
+  uint32_t hist[TAU_BINS];
   float mraw[MAX_SUBS];
   float srel[MAX_SUBS];
-  double apre[MAX_SUBS];
-  float ppre[MAX_SUBS];
-  uint32_t hist[TAU_BINS];
   double dscr[34];
   float fscr[34];
-  int iscr[34];
+  long long lscr[34];
   uint32_t uscr[34];
+  int iscr[34];
+  int match[MAX_MATCH];
+  int nmatch;
   float tau;
-  int flags;
+  int last;
 };
 
-template <typename TIn, int VE, int U, bool VEC>
-__global__ void __launch_bounds__(K1_NT) survivor_kernel(SliceArgs a) {
-  __shared__ SurvShared sh;
+// Everything that needs every sub-slice of the row: run by the last block.
+template <typename TIn, int VE>
+__device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  const long long b = blockIdx.x / a.P;
-  const int slice = (int)(blockIdx.x % a.P);
   const int nsub = a.P * K1_WARPS;
-  const long long sub = (long long)slice * K1_WARPS + w;
   const long long V = a.V;
+  const float NEG_INF = -__int_as_float(0x7f800000), INF = __int_as_float(0x7f800000);
   const pesti_sampling_params prm = row_params(a.uni, a.per_row, b);
   const float T = prm.temperature;
   const bool scale = T > 0.0f;
   const float t_eff = scale ? T : 1.0f;
-  const float NEG_INF = -__int_as_float(0x7f800000), INF = __int_as_float(0x7f800000);
-  SubSurv* so = a.surv + b * nsub + sub;
-  // ---- row prologue (every block of the row computes the same values) ----
+  const SubStat* st = a.stats + b * nsub;
   float mx = NEG_INF;
+  long long ln = -1;
   int f = 0;
   for (int s = tid; s < MAX_SUBS; s += K1_NT) {
     const bool has = s < nsub && (long long)s * a.SL < V;
-    SubStat st;
-    if (has) st = a.stats[b * nsub + s];
-    sh.mraw[s] = has ? st.max_raw : NEG_INF;
-    sh.srel[s] = has ? st.sum_rel : 0.0f;
+    float mr = NEG_INF, sr = 0.0f;
     if (has) {
-      mx = fmaxf(mx, st.max_raw);
-      f |= (int)st.flags;
+      const SubStat x = st[s];
+      mr = x.max_raw;
+      sr = x.sum_rel;
+      mx = fmaxf(mx, mr);
+      ln = ln > x.last_nan ? ln : x.last_nan;
+      f |= (int)x.flags;
     }
+    sh.mraw[s] = mr;
+    sh.srel[s] = sr;
   }
   mx = -block_reduce_min(-mx, sh.fscr);
+  ln = block_reduce_max(ln, sh.lscr);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) f |= __shfl_xor_sync(PESTI_FULL_MASK, f, o);
   if (lane == 0) sh.iscr[w] = f;
   __syncthreads();
-  if (tid == 0) {
-    int g = 0;
-    for (int q = 0; q < K1_WARPS; ++q) g |= sh.iscr[q];
-    sh.flags = g;
-  }
-  __syncthreads();
-  const uint32_t fl = (uint32_t)sh.flags;
-  const float m = scale ? fdiv(mx, T) : mx;
-  const bool uniform = (fl & MF_NAN) || (scale && T == INF && (fl & (MF_POSINF | MF_NEGINF))) || !(fabsf(m) < INF);
-  if (is_greedy(prm) || uniform || V <= 0) {
-    if (lane == 0) {
-      so->count = 0;
-      so->lo_bits = fold::SPECIAL;
-      so->k0 = so->k1 = 0;
-      so->pruned_max = NEG_INF;
+  int fl = 0;
+  for (int q = 0; q < K1_WARPS; ++q) fl |= sh.iscr[q];
+  long long li = -1, fi = 1LL << 62;
+  if (is_greedy(prm)) {
+    // first and last index holding the row max: re-scan only the segments
+    // whose max it is (usually one)
+    if (tid == 0) sh.nmatch = 0;
+    __syncthreads();
+    const float* segm = a.seg_max + b * a.nseg;
+    for (long long j = tid; j < a.nseg; j += K1_NT) {
+      if (segm[j] == mx) {
+        const int slot = atomicAdd(&sh.nmatch, 1);
+        if (slot < MAX_MATCH) sh.match[slot] = (int)j;
+      }
     }
-    return;
+    __syncthreads();
+    const int nmatch = sh.nmatch;
+    const TIn* row = (const TIn*)a.logits + b * a.ld;
+    if (nmatch <= MAX_MATCH) {
+      for (int q = 0; q < nmatch; ++q) {
+        const long long p = (long long)sh.match[q] * (32LL * VE) + tid;
+        if (tid < 32 * VE && p < V && load_logit<TIn>(row, p) == mx) {
+          li = li > p ? li : p;
+          fi = fi < p ? fi : p;
+        }
+      }
+    } else {  // many segments share the max (e.g. a constant row): scan the row
+      for (long long p = tid; p < V; p += K1_NT) {
+        if (load_logit<TIn>(row, p) == mx) {
+          li = li > p ? li : p;
+          fi = fi < p ? fi : p;
+        }
+      }
+    }
+    li = block_reduce_max(li, sh.lscr);
+    fi = block_reduce_min(fi, sh.lscr);
   }
-  const float c2 = 1.4426950408889634f / t_eff;
-  const float ym = mx * c2;
-  // exclusive prefix sums (approximate softmax mass) and prefix maxima over sub-slices
-  {
+  const float m = scale ? fdiv(mx, T) : mx;  // sampling.rs:46 on the max element
+  const bool uniform = (fl & MF_NAN) || (scale && T == INF && (fl & (MF_POSINF | MF_NEGINF))) ||
+                       !(fabsf(m) < INF) || V <= 0;
+  const bool need_pre = !is_greedy(prm) && !uniform;
+  if (need_pre) {
+    // exclusive prefix of the approximate softmax mass and of the max, per sub-slice
+    const float c2 = 1.4426950408889634f / t_eff;
+    const float ym = mx * c2;
     constexpr int PER = MAX_SUBS / K1_NT;
     double loc[PER];
     float lmx[PER];
@@ -460,18 +435,23 @@ __global__ void __launch_bounds__(K1_NT) survivor_kernel(SliceArgs a) {
 #pragma unroll
     for (int r = 0; r < PER; ++r) {
       const int s = tid * PER + r;
-      sh.apre[s] = ex;
-      sh.ppre[s] = pmax;
+      if (s < nsub) {
+        SubPre p;
+        p.A = ex;
+        p.P = pmax;
+        p.pad = 0.0f;
+        a.pre[b * nsub + s] = p;
+      }
       ex += loc[r];
       pmax = fmaxf(pmax, lmx[r]);
     }
-    __syncthreads();
   }
   // candidate threshold: a lower bound of the k-th largest raw logit, from the
   // segment maxima (maxima of disjoint segments are distinct elements),
   // rounded down to the start of its 12-bit key bin
+  float tau = INF;
   const long long k = (long long)prm.top_k;
-  if (fast_topk(prm, V)) {
+  if (need_pre && fast_topk(prm, V)) {
     const long long keff = k < V ? k : V;
     for (int i = tid; i < TAU_BINS; i += K1_NT) sh.hist[i] = 0u;
     __syncthreads();
@@ -485,13 +465,14 @@ __global__ void __launch_bounds__(K1_NT) survivor_kernel(SliceArgs a) {
       if (ok && (peers & ((1u << lane) - 1u)) == 0u) atomicAdd(&sh.hist[d], (uint32_t)__popc(peers));
     }
     __syncthreads();
-    // top-down scan over the bins: thread t owns bins [TAU_BINS-16(t+1), TAU_BINS-16t)
-    constexpr int BPT = TAU_BINS / K1_NT;
+    constexpr int BPT = TAU_BINS / K1_NT;  // top-down: thread t owns bins [4096-16(t+1), 4096-16t)
     uint32_t loc = 0;
 #pragma unroll
     for (int q = 0; q < BPT; ++q) loc += sh.hist[TAU_BINS - 1 - BPT * tid - q];
     uint32_t tot;
     const uint32_t ex = block_excl_scan_add(loc, sh.uscr, tot);
+    if (tid == 0) sh.tau = NEG_INF;
+    __syncthreads();
     if ((long long)ex < keff && (long long)(ex + loc) >= keff) {
       uint32_t cum = ex;
       for (int q = 0; q < BPT; ++q) {
@@ -503,19 +484,181 @@ __global__ void __launch_bounds__(K1_NT) survivor_kernel(SliceArgs a) {
         }
       }
     }
-    if (tid == 0 && (long long)tot < keff) sh.tau = NEG_INF;
     __syncthreads();
-    if (tid == 0 && slice == 0) a.row_tau[b] = sh.tau;
-  } else {
-    if (tid == 0) {
-      sh.tau = INF;
-      if (slice == 0) a.row_tau[b] = INF;
-    }
-    __syncthreads();
+    tau = sh.tau;
   }
-  const float tau = sh.tau;
+  if (tid == 0) {
+    RowInfo ri;
+    ri.max_raw = mx;
+    ri.m = m;
+    ri.tau = tau;
+    ri.flags = (uint32_t)fl;
+    ri.last_max = li;
+    ri.first_max = fi < (1LL << 62) ? fi : -1;
+    ri.last_nan = ln;
+    ri.uniform = uniform ? 1 : 0;
+    ri.pad = 0;
+    a.info[b] = ri;
+  }
+}
 
-  // ---- this warp's sub-slice ----
+template <typename TIn, int VE, int U, bool VEC>
+__global__ void __launch_bounds__(K1_NT) slice_stats_kernel(SliceArgs a) {
+  __shared__ StatsShared sh;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const long long b = blockIdx.x / a.P;
+  const int slice = (int)(blockIdx.x % a.P);
+  const long long sub = (long long)slice * K1_WARPS + w;
+  const long long start = sub * a.SL;
+  long long end = start + a.SL;
+  if (end > a.V) end = a.V;
+  if (slice == 0 && w == 0 && lane == 0) a.cand_count[b] = 0;
+  const TIn* row = (const TIn*)a.logits + b * a.ld;
+  const pesti_sampling_params prm = row_params(a.uni, a.per_row, b);
+  const float c2 = 1.4426950408889634f / (prm.temperature > 0.0f ? prm.temperature : 1.0f);
+  const float NEG_INF = -__int_as_float(0x7f800000), INF = __int_as_float(0x7f800000);
+  int last_nan = -1;
+  uint32_t flags = 0;
+  uint32_t sub_key = fkey(NEG_INF);     // max over the sub-slice, as an ordered key
+  float run_m = NEG_INF, run_s = 0.0f;  // online partial sum, log2 units
+  float* segmax = a.seg_max + b * a.nseg;
+  stream_subslice<TIn, VE, U, VEC>(row, start, end, [&](const float* x, long long pos0, int nv) {
+    float lm = NEG_INF;
+    bool odd = false;
+#pragma unroll
+    for (int e = 0; e < VE; ++e) {
+      if (e < nv) {
+        lm = fmaxf(lm, x[e]);  // fmaxf skips NaN, as f32::max does
+        odd |= !(fabsf(x[e]) < INF);
+      }
+    }
+    if (odd) {  // NaN or +-inf: rare
+#pragma unroll
+      for (int e = 0; e < VE; ++e) {
+        if (e >= nv) continue;
+        if (is_nan(x[e])) {
+          last_nan = (int)(pos0 + e);
+          flags |= MF_NAN;
+        } else if (!(fabsf(x[e]) < INF)) {
+          flags |= x[e] > 0.0f ? MF_POSINF : MF_NEGINF;
+        }
+      }
+    }
+    // approximate partial softmax sum (steers the fold speculation only)
+    const float nm = fmaxf(run_m, lm * c2);
+    if (nm > NEG_INF) {
+      float acc = run_s * ex2_approx(run_m - nm);
+#pragma unroll
+      for (int e = 0; e < VE; ++e)
+        if (e < nv && !is_nan(x[e])) acc += ex2_approx(fmaf(x[e], c2, -nm));
+      run_s = acc;
+      run_m = nm;
+    }
+    const uint32_t sk = __reduce_max_sync(PESTI_FULL_MASK, fkey(lm));
+    sub_key = sk > sub_key ? sk : sub_key;
+    if (lane == 0) segmax[(pos0 - (long long)lane * VE) / (32LL * VE)] = fkey_inv(sk);
+  });
+  const float mx = fkey_inv(sub_key);
+  const int ln = (int)__reduce_max_sync(PESTI_FULL_MASK, (unsigned)(last_nan + 1)) - 1;
+  const uint32_t fl = __reduce_or_sync(PESTI_FULL_MASK, flags);
+  const float wm = warp_reduce_fmax(run_m);
+  float ws = (run_m > NEG_INF && wm > NEG_INF) ? run_s * ex2_approx(run_m - wm) : 0.0f;
+  ws = warp_reduce_add(ws);
+  if (lane == 0) {
+    SubStat m;
+    m.max_raw = mx;
+    m.sum_rel = ws;  // relative to 2^(mx*c2) (wm == mx*c2: the same float product)
+    m.last_nan = ln;
+    m.flags = fl;
+    a.stats[b * (long long)a.P * K1_WARPS + sub] = m;
+  }
+  // the last block of the row to finish computes the row prologue (no waiting:
+  // the other blocks simply exit)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int prev = atomicAdd(&a.row_ctr[b], 1);
+    sh.last = prev == a.P - 1;
+  }
+  __syncthreads();
+  if (!sh.last) return;
+  __threadfence();
+  row_prologue<TIn, VE>(a, b, sh);
+  if (threadIdx.x == 0) a.row_ctr[b] = 0;
+}
+
+// ---------------------------------------------------------------------------
+// Pass 2: survivors, fold entries, top-k candidates.
+//
+// Which elements may be dropped (x_i = raw_i/T is the scaled logit):
+//  (a) prefix max: an EARLIER element j with x_j >= x_i + 17.34 gives
+//      e_i <= 0.989*2^-25*e_j; the running softmax sum s_{i-1} >= e_j and
+//      ulp(s)/2 > s*2^-25, so fl(s + e_i) returns s.  The same ratio makes i a
+//      no-op in the sorted folds (they start at p_max >= p_j) and in the
+//      index-order folds of p and q.  Tested on raw values as
+//      raw_i < P - (17.35*T*(1+2^-20) + 2^-21*|P|), P = the max of the row
+//      before the element's segment; the slack covers the rounding of raw/T,
+//      of x - m (<= 2^-24*104 wherever exp is not 0) and of exp.  Used while
+//      P/T >= m - 60.
+//  (b) running sum: each step of a fold of non-negative terms has relative
+//      error <= 2^-24, so s_{i-1} >= (sum_{j<i} e_j)*(1 - V*2^-24).  With the
+//      approximate prefix mass A of the earlier sub-slices (pass 1, margin
+//      for its own error), L <= s_{i-1}, and e_i < 0.99*2^-25*L makes i a
+//      no-op in the index-order folds (also for p = e/S and q = p/total,
+//      whose running sums are bounded the same way).  It does NOT bound the
+//      sorted folds, so it is used only for top-k rows (whose kept list is
+//      explicit and checked) and unfiltered rows (index order only).
+//
+// Fold entries: the survivors of a sub-slice, in row order, are classified
+// against an approximate running sum (A plus the sum of the earlier
+// survivors).  An element that is large next to the state (>= half its
+// binade's bottom) or may carry the state across a binade edge (within a
+// relative 2^-10 of it) is SPECIAL: the row kernel adds it with a real f32
+// add.  Maximal runs of the others in one binade become one entry holding the
+// run's integer increments for an even and an odd entry state.  An increment
+// is e/w rounded to an integer; it is taken from an approximation of e with
+// relative error < 2^-20 (pesti_expf_approx) whenever e/w is farther than that
+// from a rounding boundary, and from the exact exp otherwise.  The row kernel
+// checks every run against the exact state (right binade at entry, still
+// inside it at exit) and replays the run element by element when the check
+// fails, so the classification never decides a result.
+// ---------------------------------------------------------------------------
+struct SurvShared {
+  float q_raw[K1_WARPS][QCAP];
+  uint32_t q_idx[K1_WARPS][QCAP];
+  FoldEnt ent[K1_WARPS][NE];
+};
+
+template <typename TIn, int VE, int U, bool VEC>
+__global__ void __launch_bounds__(K1_NT) survivor_kernel(SliceArgs a) {
+  __shared__ SurvShared sh;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const long long b = blockIdx.x / a.P;
+  const int slice = (int)(blockIdx.x % a.P);
+  const int nsub = a.P * K1_WARPS;
+  const long long sub = (long long)slice * K1_WARPS + w;
+  const long long V = a.V;
+  const pesti_sampling_params prm = row_params(a.uni, a.per_row, b);
+  const RowInfo ri = a.info[b];
+  const float T = prm.temperature;
+  const bool scale = T > 0.0f;
+  const float t_eff = scale ? T : 1.0f;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  SubSurv* so = a.surv + b * nsub + sub;
+  if (is_greedy(prm) || ri.uniform) {
+    if (lane == 0) {
+      SubSurv z;
+      z.count = 0;
+      z.nent = 0;
+      z.replay = 0;
+      z.pruned_max = NEG_INF;
+      *so = z;
+    }
+    return;
+  }
+  const float m = ri.m;
+  const float tau = ri.tau;
+  const SubPre pr = a.pre[b * nsub + sub];
   const long long start = sub * a.SL;
   long long end = start + a.SL;
   if (end > V) end = V;
@@ -525,127 +668,212 @@ __global__ void __launch_bounds__(K1_NT) survivor_kernel(SliceArgs a) {
   const float pf = (m - PRUNE_FLOOR) * t_eff;
   const float p_floor = pf + 0x1p-20f * fabsf(pf);
   const float invT = 1.0f / t_eff;
-  float run_max = sh.ppre[sub];
-  const double A = sh.apre[sub];
-  // A is built from float products raw*c2 whose rounding grows with |y|:
+  const float ym = ri.max_raw * (1.4426950408889634f / t_eff);
+  // A was built from float products raw*c2 whose rounding grows with |y|:
   // widen the margin with the magnitude of the scaled logits
   const double mag = 0x1p-20 * ((double)fabsf(ym) + 64.0);
-  const double L = A * (1.0 - (double)V * 0x1p-24) * (1.0 - 0x1p-10) * exp2(-mag);
+  const double L = pr.A * (1.0 - (double)V * 0x1p-24) * (1.0 - 0x1p-10) * exp2(-mag);
   const bool use_L = sum_pruning_ok(prm) && L >= 0x1p-60;
   const float thrL = use_L ? m + (float)log(L) - 17.36f : NEG_INF;
-  // fold speculation: the softmax fold enters this sub-slice near A and
-  // leaves near A + own (a guess: the row kernel verifies it against the exact state)
-  const double own = sh.mraw[sub] > NEG_INF ? (double)exp2f(sh.mraw[sub] * c2 - ym) * (double)sh.srel[sub] : 0.0;
-  uint32_t lo = fold::SPECIAL;
-  if (A >= 0x1p-100) {
-    const uint32_t l = fbits(__double2float_rz(A)) & 0x7f800000u;
-    const double lov = (double)bitsf(l);
-    if (A >= lov * (1.0 + fold::MU) && A + own * (1.0 + 0x1p-8) <= 2.0 * lov * (1.0 - fold::MU)) lo = l;
-  }
-  const float lo_half = lo == fold::SPECIAL ? 0.0f : bitsf(lo - 0x00800000u);
-  Tr acc{0u, 0u};
-  bool complex_sub = lo == fold::SPECIAL;
-  long long total = 0;
+  float run_max = pr.P;
   float pruned_max = NEG_INF;
   int* ccount = a.cand_count + b;
+  float* qr = sh.q_raw[w];
+  uint32_t* qi = sh.q_idx[w];
+  FoldEnt* ent = sh.ent[w];
+  // queue and fold state (warp-uniform)
+  int qh = 0, qn = 0;
+  long long scount = 0;
+  double s_approx = pr.A;
+  int nent = 0;
+  bool replay = false;
+  uint32_t run_lo = 0u;
+  Tr run_acc{0u, 0u};
+  uint32_t run_cnt = 0u;
 
-  stream_subslice<TIn, VE, U, VEC>(row, start, end, [&](const float* x, long long pos0, int nv) {
-    float pre[VE];
-    float lm = NEG_INF;
-#pragma unroll
-    for (int e = 0; e < VE; ++e) {
-      pre[e] = lm;
-      if (e < nv) lm = fmaxf(lm, x[e]);
+  auto push_ent = [&](uint32_t lo, uint32_t a0, uint32_t a1, uint32_t cnt) {
+    if (nent < NE) {
+      if (lane == 0) ent[nent] = FoldEnt{lo, a0, a1, cnt};
+      ++nent;
+    } else {
+      replay = true;
     }
-    float inc = lm;
+  };
+  auto flush_run = [&]() {
+    if (run_cnt > 0u) push_ent(run_lo, run_acc.a0, run_acc.a1, run_cnt);
+    run_cnt = 0u;
+  };
+
+  // classification of nv (<= 32) queued survivors, one per lane
+  auto process_batch = [&](int nv) {
+    const bool valid = lane < nv;
+    const int slot = (qh + lane) & (QCAP - 1);
+    const float raw = valid ? qr[slot] : 0.0f;
+    const uint32_t idx = valid ? qi[slot] : 0u;
+    float d = 0.0f;
+    if (valid) {
+      const float xs = scale ? fdiv(raw, T) : raw;  // sampling.rs:46
+      d = fsub(xs, m);                              // sampling.rs:127 (argument of exp)
+      a.surv_raw[out_base + scount + lane] = raw;   // exact exp is recomputed where needed
+      a.surv_idx[out_base + scount + lane] = idx;
+    }
+    scount += nv;
+    qh = (qh + nv) & (QCAP - 1);
+    qn -= nv;
+    // exp within a relative 2^-20 (exact below where it matters)
+    const float ea = valid ? pesti_expf_approx(d) : 0.0f;
+    // approximate running state before each element
+    float inc = ea;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const float y = __shfl_up_sync(PESTI_FULL_MASK, inc, o);
-      if (lane >= o) inc = fmaxf(inc, y);
+      if (lane >= o) inc += y;
     }
-    float exc = __shfl_up_sync(PESTI_FULL_MASK, inc, 1);
-    if (lane == 0) exc = NEG_INF;
-    const float seg_max = __shfl_sync(PESTI_FULL_MASK, inc, 31);
-    const float p0 = fmaxf(run_max, exc);
-    bool sv[VE], cd[VE];
-    float ev[VE];
+    const double av = s_approx + (double)(inc - ea);
+    const double bv = av + (double)ea;
+    s_approx += (double)__shfl_sync(PESTI_FULL_MASK, inc, 31);
+    if (replay) return;
+    uint32_t lo;
+    bool special;
+    const float eu = ea * (1.0f + 0x1p-19f);  // upper bound of the exact value
+    if (av < 0x1p-126) {
+      lo = 0u;
+      special = eu >= 0x1p-127f || bv > 0x1p-126 * (1.0 - fold::MU);
+    } else {
+      lo = fbits(__double2float_rz(av)) & 0x7f800000u;
+      const double lov = (double)bitsf(lo);
+      special = eu >= bitsf(lo - 0x00800000u) || av < lov * (1.0 + fold::MU) || bv > 2.0 * lov * (1.0 - fold::MU);
+    }
+    // increment in ulps of the binade: ea/w rounded, exact unless ea/w is within
+    // the error bound of a rounding boundary (then from the exact exp)
+    Tr t{0u, 0u};
+    bool need_exact = valid && special;
+    if (valid && !special) {
+      const uint32_t E = lo >> 23;  // w = 2^(E-150) (E = 0: the subnormal grid 2^-149)
+      const int sh2 = 150 - (int)(E == 0u ? 1u : E);
+      if (ea == 0.0f) {
+        need_exact = E < 40u;  // exact e < 4.5e-38: rounds to 0 on any grid >= 2^-110
+      } else {
+        const float tt = __uint_as_float(fbits(ea) + ((uint32_t)sh2 << 23));  // ea/w, exact scaling
+        const float kr = rintf(tt);
+        const float slack = 0.5f - fabsf(tt - kr);
+        if (slack <= tt * 0x1p-19f + 0x1p-22f) need_exact = true;
+        else t.a0 = t.a1 = (uint32_t)kr;
+      }
+    }
+    float ex = 0.0f;
+    if (need_exact) {
+      ex = pesti_expf_call(d);  // sampling.rs:127, exact
+      if (!special) {
+        t.a0 = fbits(fadd(bitsf(lo), ex)) - lo;
+        t.a1 = fbits(fadd(bitsf(lo + 1u), ex)) - (lo + 1u);
+      }
+    }
+    const uint32_t breaks = __ballot_sync(PESTI_FULL_MASK, valid && (special || lo != run_lo || run_cnt == 0u));
+    if (breaks == 0u) {
+      // the whole batch continues the current run
+      const Tr r = tr_warp_reduce(t);
+      const Tr r0{__shfl_sync(PESTI_FULL_MASK, r.a0, 0), __shfl_sync(PESTI_FULL_MASK, r.a1, 0)};
+      run_acc = tr_compose(run_acc, r0);
+      run_cnt += (uint32_t)nv;
+      return;
+    }
+    for (int l = 0; l < nv; ++l) {  // element by element (warp-uniform)
+      const bool sp = __shfl_sync(PESTI_FULL_MASK, special, l);
+      const uint32_t lol = __shfl_sync(PESTI_FULL_MASK, lo, l);
+      const uint32_t k0 = __shfl_sync(PESTI_FULL_MASK, t.a0, l);
+      const uint32_t k1 = __shfl_sync(PESTI_FULL_MASK, t.a1, l);
+      const uint32_t eb = __shfl_sync(PESTI_FULL_MASK, fbits(ex), l);
+      if (sp) {
+        flush_run();
+        push_ent(fold::SPECIAL, eb, 0u, 1u);
+      } else if (run_cnt == 0u || lol != run_lo) {
+        flush_run();
+        run_lo = lol;
+        run_acc = Tr{k0, k1};
+        run_cnt = 1u;
+      } else {
+        run_acc = tr_compose(run_acc, Tr{k0, k1});
+        ++run_cnt;
+      }
+    }
+  };
+
+  stream_subslice<TIn, VE, U, VEC>(row, start, end, [&](const float* x, long long pos0, int nv) {
+    // max of the row before this segment (exact): a lower bound of every
+    // element's own prefix max
+    const float P = run_max;
+    const float thrP = P >= p_floor ? fsub(P, fadd(c1, 0x1p-21f * fabsf(P))) : NEG_INF;
+    bool sv[VE];
     int cnt = 0, ccnt = 0;
-    Tr lt{0u, 0u};
-    bool big = false;
+    float lm = NEG_INF;
 #pragma unroll
     for (int e = 0; e < VE; ++e) {
       const float xv = x[e];
       const bool valid = e < nv && !is_nan(xv);
-      const float P = fmaxf(p0, pre[e]);
-      const bool pruneP = P >= p_floor && xv < fsub(P, fadd(c1, 0x1p-21f * fabsf(P)));
+      if (e < nv) lm = fmaxf(lm, xv);
       const float xa = xv * invT;
       const bool pruneL = xa < thrL - 0x1p-19f * (fabsf(xa) + fabsf(thrL));
-      sv[e] = valid && !(pruneP || pruneL);
-      cd[e] = valid && xv >= tau;
-      ev[e] = 0.0f;
-      if (sv[e] || cd[e]) {
-        const float xs = scale ? fdiv(xv, T) : xv;  // sampling.rs:46
-        ev[e] = pesti_expf(fsub(xs, m));            // sampling.rs:127
-      }
+      sv[e] = valid && !(xv < thrP || pruneL);
       if (valid && !sv[e]) pruned_max = fmaxf(pruned_max, xv);
-      if (sv[e]) {
-        ++cnt;
-        if (!complex_sub) {
-          if (ev[e] >= lo_half) big = true;
-          const uint32_t k0 = fbits(fadd(bitsf(lo), ev[e])) - lo;
-          const uint32_t k1 = fbits(fadd(bitsf(lo + 1u), ev[e])) - (lo + 1u);
-          lt = tr_compose(lt, Tr{k0, k1});
-        }
-      }
-      ccnt += cd[e] ? 1 : 0;
+      cnt += sv[e] ? 1 : 0;
+      ccnt += (valid && xv >= tau) ? 1 : 0;
     }
-    run_max = fmaxf(run_max, seg_max);
-    // survivors, compacted in row order
+    run_max = fmaxf(run_max, fkey_inv(__reduce_max_sync(PESTI_FULL_MASK, fkey(lm))));
+    // survivors join the queue in row order
     const int cinc = warp_incl_scan_add(cnt);
     const int wsum = __shfl_sync(PESTI_FULL_MASK, cinc, 31);
-    long long o = out_base + total + (cinc - cnt);
+    int o = qh + qn + (cinc - cnt);
 #pragma unroll
     for (int e = 0; e < VE; ++e) {
       if (sv[e]) {
-        a.surv_e[o] = ev[e];
-        a.surv_idx[o] = (uint32_t)(pos0 + e);
+        qr[o & (QCAP - 1)] = x[e];
+        qi[o & (QCAP - 1)] = (uint32_t)(pos0 + e);
         ++o;
       }
     }
-    total += wsum;
-    // fold summary of this segment, composed in row order
-    if (__any_sync(PESTI_FULL_MASK, big)) complex_sub = true;
-    if (!complex_sub && wsum > 0) {
-      const Tr seg = tr_warp_reduce(lt);
-      if (lane == 0) acc = tr_compose(acc, seg);
-    }
-    // top-k candidates (one atomic per warp per segment)
-    const int ctot = warp_reduce_add(ccnt);
-    if (ctot > 0) {
+    qn += wsum;
+    // top-k candidates: few per row, exact exp computed right here
+    const uint32_t cm = __ballot_sync(PESTI_FULL_MASK, ccnt > 0);
+    if (cm) {
+      const int ctot = warp_reduce_add(ccnt);
       int basec = 0;
       if (lane == 0) basec = atomicAdd(ccount, ctot);
       basec = __shfl_sync(PESTI_FULL_MASK, basec, 0);
       int cex = warp_incl_scan_add(ccnt) - ccnt;
-#pragma unroll
       for (int e = 0; e < VE; ++e) {
-        if (cd[e]) {
+        const float xv = x[e];
+        if (e < nv && !is_nan(xv) && xv >= tau) {
           const int slot = basec + cex;
           if (slot < CAND_CAP) {
-            a.cand_e[b * CAND_CAP + slot] = ev[e];
+            const float xs = scale ? fdiv(xv, T) : xv;
+            a.cand_e[b * CAND_CAP + slot] = pesti_expf_call(fsub(xs, m));
             a.cand_idx[b * CAND_CAP + slot] = (uint32_t)(pos0 + e);
           }
           ++cex;
         }
       }
     }
+  }, [&]() {
+    __syncwarp();
+    while (qn >= 32) {
+      process_batch(32);
+      __syncwarp();
+    }
   });
+  if (qn > 0) process_batch(qn);
+  flush_run();
+  __syncwarp();
   const float pm = warp_reduce_fmax(pruned_max);
+  FoldEnt* gent = a.ents + (b * nsub + sub) * NE;
+  for (int i = lane; i < (nent < NE ? nent : NE); i += 32) gent[i] = ent[i];
   if (lane == 0) {
-    so->count = (int32_t)total;
-    so->lo_bits = complex_sub ? fold::SPECIAL : lo;
-    so->k0 = acc.a0;
-    so->k1 = acc.a1;
-    so->pruned_max = pm;
+    SubSurv z;
+    z.count = (int32_t)scount;
+    z.nent = nent < NE ? nent : NE;
+    z.replay = replay ? 1 : 0;
+    z.pruned_max = pm;
+    *so = z;
   }
 }
 
@@ -677,12 +905,22 @@ struct RowShared {
   float fscr[34];
   int iscr[34];
   long long n;
-  uint32_t flags;
-  uint32_t s_bits;
   uint32_t e_star;
   int need_dense;
   int fallback;
+  int fast_ok;
 };
+
+// Fast-path arrays, placed after RowShared in dynamic shared memory.
+struct FastSmem {
+  unsigned long long key[FAST_CAND];
+  float q[FAST_CAND];
+  float stage[STAGE];
+  // followed by SubSurv[nsub] and FoldEnt[nsub*NE]
+};
+__host__ __device__ inline size_t fast_smem_bytes(int nsub) {
+  return sizeof(FastSmem) + (size_t)nsub * (sizeof(SubSurv) + NE * sizeof(FoldEnt));
+}
 
 // Rust's Iterator::max_by over the raw logits with partial_cmp (sampling.rs:115-122)
 // when the row holds NaN: the scan adopts every NaN and then the element right
@@ -780,44 +1018,76 @@ __device__ void bitonic_desc(unsigned long long* key, int m) {
   }
 }
 
-// Fold of n values from global memory by one warp, starting from state s
-// (bits), 32 elements per step: a transducer scan over the lanes gives every
-// lane's state under the current binade; the first element that would leave
-// the binade (or is large next to s) is added directly, and the step resumes
-// after it.  Returns the final state.  All 32 lanes must call it.
-__device__ uint32_t warp_fold(const float* v, long long n, uint32_t s) {
+// The same, by one warp.
+__device__ void warp_bitonic_desc(unsigned long long* key, int m) {
   const int lane = threadIdx.x & 31;
-  long long j = 0;
-  while (j < n) {
-    const long long idx = j + lane;
-    const bool valid = idx < n;
-    const float x = valid ? v[idx] : 0.0f;
-    const uint32_t lo = fold::binade_lo_bits(s);
-    const uint32_t hi = fold::binade_hi_bits(lo);
-    const bool big = valid && (lo == 0u ? x >= 0x1p-127f : fbits(x) >= lo - 0x00800000u);
-    Tr t{0u, 0u};
-    if (valid && !big) {
-      t.a0 = fbits(fadd(bitsf(lo), x)) - lo;
-      t.a1 = fbits(fadd(bitsf(lo + 1u), x)) - (lo + 1u);
-    }
-    const Tr incl = tr_warp_incl_scan(t);
-    const unsigned long long sum = (unsigned long long)s + ((s & 1u) ? incl.a1 : incl.a0);
-    const uint32_t after = sum > 0xffffffffull ? 0xffffffffu : (uint32_t)sum;
-    const bool bad = valid && (big || after >= hi);
-    const uint32_t badm = __ballot_sync(PESTI_FULL_MASK, bad);
-    const int nvalid = (int)(n - j < 32 ? n - j : 32);
-    if (badm == 0u) {
-      s = __shfl_sync(PESTI_FULL_MASK, after, nvalid - 1);
-      j += nvalid;
-    } else {
-      const int f0 = __ffs(badm) - 1;
-      const uint32_t prev = __shfl_sync(PESTI_FULL_MASK, after, f0 > 0 ? f0 - 1 : 0);
-      const uint32_t before = f0 > 0 ? prev : s;  // lanes < f0 are exact
-      const float xf = __shfl_sync(PESTI_FULL_MASK, x, f0);
-      s = fbits(fadd(bitsf(before), xf));
-      j += f0 + 1;
+  for (int kk = 2; kk <= m; kk <<= 1) {
+    for (int j = kk >> 1; j > 0; j >>= 1) {
+      for (int i = lane; i < m; i += 32) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const unsigned long long x = key[i], y = key[ixj];
+          const bool desc = (i & kk) == 0;
+          if (desc ? (x < y) : (x > y)) {
+            key[i] = y;
+            key[ixj] = x;
+          }
+        }
+      }
+      __syncwarp();
     }
   }
+}
+
+// Fold of the exps of n survivors (their raw logits in global memory) by one
+// warp, starting from state s (bits).  The exact exps are staged STAGE at a
+// time in shared memory; each step takes 32 of them with a transducer scan
+// over the lanes, adds the first one that would leave the binade (or is large
+// next to s) directly, and resumes after it.  All 32 lanes must call it.
+__device__ uint32_t warp_fold(const float* raw, long long n, uint32_t s, float* stage, bool scale, float T,
+                              float m) {
+  const int lane = threadIdx.x & 31;
+  for (long long base = 0; base < n; base += STAGE) {
+    const int len = (int)(n - base < STAGE ? n - base : STAGE);
+    __syncwarp();
+    for (int i = lane; i < len; i += 32) {
+      const float xr = raw[base + i];
+      stage[i] = pesti_expf_call(fsub(scale ? fdiv(xr, T) : xr, m));  // sampling.rs:46,127
+    }
+    __syncwarp();
+    int j = 0;
+    while (j < len) {
+      const int idx = j + lane;
+      const bool valid = idx < len;
+      const float x = valid ? stage[idx] : 0.0f;
+      const uint32_t lo = fold::binade_lo_bits(s);
+      const uint32_t hi = fold::binade_hi_bits(lo);
+      const bool big = valid && (lo == 0u ? x >= 0x1p-127f : fbits(x) >= lo - 0x00800000u);
+      Tr t{0u, 0u};
+      if (valid && !big) {
+        t.a0 = fbits(fadd(bitsf(lo), x)) - lo;
+        t.a1 = fbits(fadd(bitsf(lo + 1u), x)) - (lo + 1u);
+      }
+      const Tr incl = tr_warp_incl_scan(t);
+      const unsigned long long sum = (unsigned long long)s + ((s & 1u) ? incl.a1 : incl.a0);
+      const uint32_t after = sum > 0xffffffffull ? 0xffffffffu : (uint32_t)sum;
+      const bool bad = valid && (big || after >= hi);
+      const uint32_t badm = __ballot_sync(PESTI_FULL_MASK, bad);
+      const int nvalid = len - j < 32 ? len - j : 32;
+      if (badm == 0u) {
+        s = __shfl_sync(PESTI_FULL_MASK, after, nvalid - 1);
+        j += nvalid;
+      } else {
+        const int f0 = __ffs(badm) - 1;
+        const uint32_t prev = __shfl_sync(PESTI_FULL_MASK, after, f0 > 0 ? f0 - 1 : 0);
+        const uint32_t before = f0 > 0 ? prev : s;  // lanes < f0 are exact
+        const float xf = __shfl_sync(PESTI_FULL_MASK, x, f0);
+        s = fbits(fadd(bitsf(before), xf));
+        j += f0 + 1;
+      }
+    }
+  }
+  __syncwarp();
   return s;
 }
 
@@ -828,6 +1098,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
   const long long b = blockIdx.x;
   const long long V = a.V;
   const pesti_sampling_params prm = row_params(a.uni, a.per_row, b);
+  const RowInfo ri = a.info[b];
   const float T = prm.temperature;
   const int nsub = a.P * K1_WARPS;
   const void* row = a.dtype == PESTI_BF16 ? (const void*)((const uint16_t*)a.logits + b * a.ld)
@@ -836,44 +1107,8 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
   uint32_t* I = a.I + b * V;
   const float r = a.u ? a.u[b] : 0.0f;
   const float INF = __int_as_float(0x7f800000);
-  const SubStat* stats = a.stats + b * nsub;
   const SubSurv* survs = a.surv + b * nsub;
-
-  // ---- row summary from the sub-slice statistics ----
-  float mx = -INF;
-  long long li = -1, fi = 1LL << 62, ln = -1;
-  int f = 0;
-  for (int s = tid; s < nsub; s += K2_NT) {
-    if ((long long)s * a.SL >= V) continue;
-    const SubStat st = stats[s];
-    mx = fmaxf(mx, st.max_raw);
-    ln = ln > st.last_nan ? ln : st.last_nan;
-    f |= (int)st.flags;
-  }
-  mx = -block_reduce_min(-mx, sh.fscr);
-  for (int s = tid; s < nsub; s += K2_NT) {
-    if ((long long)s * a.SL >= V) continue;
-    const SubStat st = stats[s];
-    if (st.max_raw == mx) {
-      if (st.last_max != 0xffffffffu) li = li > (long long)st.last_max ? li : (long long)st.last_max;
-      if (st.first_max != 0xffffffffu) fi = fi < (long long)st.first_max ? fi : (long long)st.first_max;
-    }
-  }
-  li = block_reduce_max(li, sh.lscr);
-  fi = block_reduce_min(fi, sh.lscr);
-  ln = block_reduce_max(ln, sh.lscr);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) f |= __shfl_xor_sync(PESTI_FULL_MASK, f, o);
-  if (lane == 0) sh.iscr[wid] = f;
-  __syncthreads();
-  if (tid == 0) {
-    int g = 0;
-    for (int q = 0; q < K2_NT / 32; ++q) g |= sh.iscr[q];
-    sh.flags = (uint32_t)g;
-  }
-  __syncthreads();
-  const uint32_t fl = sh.flags;
-  const long long last_max = li, first_max = fi < (1LL << 62) ? fi : -1, last_nan = ln;
+  const uint32_t fl = ri.flags;
 
   if (V <= 0) {  // empty slice: sample() and argmax() return 0
     if (tid == 0) {
@@ -886,9 +1121,9 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
 
   if (is_greedy(prm)) {  // generate(): temperature == 0 -> argmax (model.rs:517-521)
     uint32_t tok;
-    if (prm.flags & PESTI_FLAG_ARGMAX_FIRST) tok = first_max >= 0 ? (uint32_t)first_max : 0u;
-    else if (fl & MF_NAN) tok = nan_argmax(row, a.dtype, V, last_nan, sh);
-    else tok = last_max >= 0 ? (uint32_t)last_max : 0u;
+    if (prm.flags & PESTI_FLAG_ARGMAX_FIRST) tok = ri.first_max >= 0 ? (uint32_t)ri.first_max : 0u;
+    else if (fl & MF_NAN) tok = nan_argmax(row, a.dtype, V, ri.last_nan, sh);
+    else tok = ri.last_max >= 0 ? (uint32_t)ri.last_max : 0u;
     if (tid == 0) {
       a.out[b] = tok;
       if (a.kept_count) a.kept_count[b] = 0;
@@ -897,15 +1132,13 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
     return;
   }
 
-  // sampling.rs:43-50 temperature; the max of x/T is RN(max(raw)/T) (monotone)
   const bool scale = T > 0.0f;
-  const float m = scale ? fdiv(mx, T) : mx;
-  const bool nanx = (fl & MF_NAN) || (scale && T == INF && (fl & (MF_POSINF | MF_NEGINF)));
+  const float m = ri.m;
   const long long k = (long long)prm.top_k;
   const bool topp = prm.top_p > 0.0f && k == 0;
   const uint32_t r_tau = fold::tau_bits_of(r);
 
-  if (nanx || !(fabsf(m) < INF)) {
+  if (ri.uniform) {
     // softmax sum is NaN or not > 0: every probability is 1/V (sampling.rs:129-133).
     // All entries are equal, so both stable sorts keep index order.
     if (tid == 0) {
@@ -947,90 +1180,109 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
     return;
   }
 
+  // ---------------- fast path: explicit top-k of at most FAST_K (one warp) ----------------
+  if (a.fast_enabled && fast_topk(prm, V)) {
+    if (wid == 0) {
+      FastSmem& fs = *reinterpret_cast<FastSmem*>(row_smem + sizeof(RowShared));
+      SubSurv* ss = reinterpret_cast<SubSurv*>(row_smem + sizeof(RowShared) + sizeof(FastSmem));
+      FoldEnt* se = reinterpret_cast<FoldEnt*>(ss + nsub);
+      const FoldEnt* gent = a.ents + b * nsub * NE;
+      const long long keff = k < V ? k : V;
+      // stage the fold entries (independent loads)
+      for (int q = lane; q < nsub; q += 32) ss[q] = survs[q];
+      __syncwarp();
+      for (int q = lane; q < nsub; q += 32) {
+        const int ne = ss[q].replay ? 0 : ss[q].nent;
+        for (int i = 0; i < ne; ++i) se[q * NE + i] = gent[q * NE + i];
+      }
+      const int C = a.cand_count[b];
+      __syncwarp();
+      // softmax denominator (sampling.rs:128): walk the entries with the exact state
+      uint32_t s = 0u;
+      for (int q = 0; q < nsub; ++q) {
+        const long long st = (long long)q * a.SL;
+        if (st >= V) break;
+        const SubSurv sv = ss[q];
+        if (sv.count <= 0) continue;
+        const float* vals = a.surv_raw + b * V + st;
+        if (sv.replay) {
+          s = warp_fold(vals, sv.count, s, fs.stage, scale, T, m);
+          continue;
+        }
+        long long pos = 0;
+        for (int i = 0; i < sv.nent; ++i) {
+          const FoldEnt en = se[q * NE + i];
+          if (en.lo == fold::SPECIAL) {
+            s = fbits(fadd(bitsf(s), bitsf(en.a0)));
+          } else {
+            bool applied = false;
+            if (fold::binade_lo_bits(s) == en.lo) {
+              const unsigned long long ns = (unsigned long long)s + ((s & 1u) ? en.a1 : en.a0);
+              if (ns < (unsigned long long)fold::binade_hi_bits(en.lo)) {
+                s = (uint32_t)ns;
+                applied = true;
+              }
+            }
+            if (!applied) s = warp_fold(vals + pos, en.count, s, fs.stage, scale, T, m);
+          }
+          pos += en.count;
+        }
+      }
+      const float S = bitsf(s);
+      bool ok = C >= keff && C <= FAST_CAND;
+      if (ok) {
+        int mm2 = 1;
+        while (mm2 < C) mm2 <<= 1;
+        for (int j = lane; j < mm2; j += 32) {
+          unsigned long long key = 0ull;
+          if (j < C) {
+            const float p = fdiv(a.cand_e[b * CAND_CAP + j], S);  // sampling.rs:130
+            key = ((unsigned long long)fbits(p) << 32) | (unsigned long long)(~a.cand_idx[b * CAND_CAP + j]);
+          }
+          fs.key[j] = key;
+        }
+        __syncwarp();
+        warp_bitonic_desc(fs.key, mm2);  // (p desc, index asc): the stable sort of sampling.rs:60
+        // every element outside the candidates (raw < tau) must rank below the keff-th
+        const float pk = bitsf((uint32_t)(fs.key[keff - 1] >> 32));
+        const float tau = ri.tau;
+        const float e_tau = tau > -INF ? pesti_expf(fsub(scale ? fdiv(tau, T) : tau, m)) : 0.0f;
+        ok = fdiv(e_tau, S) < pk;
+      }
+      if (ok) {
+        // total over the kept list (sampling.rs:81), normalisation (:94), draw (:99-111)
+        uint32_t tb = 0u;
+        if (lane == 0)
+          for (long long j = 0; j < keff; ++j) tb = fbits(fadd(bitsf(tb), bitsf((uint32_t)(fs.key[j] >> 32))));
+        const float total = bitsf(__shfl_sync(PESTI_FULL_MASK, tb, 0));
+        for (long long j = lane; j < keff; j += 32) fs.q[j] = fdiv(bitsf((uint32_t)(fs.key[j] >> 32)), total);
+        __syncwarp();
+        if (lane == 0) {
+          const fold::Result dr = fold::thread_fold(fs.q, keff, 0u, r_tau, true);
+          const long long at = dr.hit >= 0 ? dr.hit : keff - 1;
+          a.out[b] = ~(uint32_t)(fs.key[at] & 0xffffffffull);
+          if (a.kept_count) a.kept_count[b] = keff;
+        }
+        for (long long j = lane; j < a.kept_width; j += 32) {
+          const bool in = j < keff;
+          const unsigned long long kv = in ? fs.key[j] : 0ull;
+          if (a.kept_p) a.kept_p[b * a.kept_width + j] = in ? bitsf((uint32_t)(kv >> 32)) : 0.0f;
+          if (a.kept_idx) a.kept_idx[b * a.kept_width + j] = in ? ~(uint32_t)(kv & 0xffffffffull) : 0xffffffffu;
+        }
+      }
+      if (lane == 0) sh.fast_ok = ok ? 1 : 0;
+    }
+    __syncthreads();
+    if (sh.fast_ok) return;
+    // otherwise: the generic path below
+  }
+
   // largest dropped logit -> an upper bound of the exp of every dropped element
   float pm = -INF;
   for (int s = tid; s < nsub; s += K2_NT)
     if ((long long)s * a.SL < V) pm = fmaxf(pm, survs[s].pruned_max);
   pm = -block_reduce_min(-pm, sh.fscr);
   const float e_pruned = pm > -INF ? pesti_expf(fsub(scale ? fdiv(pm, T) : pm, m)) : 0.0f;
-
-  // ---------------- fast path: explicit top-k of at most FAST_K ----------------
-  if (fast_topk(prm, V)) {
-    const long long keff = k < V ? k : V;
-    // softmax denominator (sampling.rs:128): resolve the index-order fold from
-    // the sub-slice summaries; replay a sub-slice element by element whenever
-    // its summary does not apply to the exact state.
-    if (wid == 0) {
-      uint32_t s = 0u;
-      for (int q = 0; q < nsub; ++q) {
-        const long long st = (long long)q * a.SL;
-        if (st >= V) break;
-        const SubSurv sv = survs[q];
-        if (sv.count <= 0) continue;
-        bool applied = false;
-        if (sv.lo_bits != fold::SPECIAL && fold::binade_lo_bits(s) == sv.lo_bits) {
-          const uint32_t inc = (s & 1u) ? sv.k1 : sv.k0;
-          const unsigned long long ns = (unsigned long long)s + inc;
-          if (ns < (unsigned long long)fold::binade_hi_bits(sv.lo_bits)) {
-            s = (uint32_t)ns;
-            applied = true;
-          }
-        }
-        if (!applied) s = warp_fold(a.surv_e + b * V + st, sv.count, s);
-      }
-      if (lane == 0) sh.s_bits = s;
-    }
-    __syncthreads();
-    const float S = bitsf(sh.s_bits);
-    const int C = a.cand_count[b];
-    const float tau = a.row_tau[b];
-    bool ok = C >= keff && C <= CAND_CAP && C <= CAND_MAX;
-    if (ok) {
-      int mm2 = 1;
-      while (mm2 < C) mm2 <<= 1;
-      for (int j = tid; j < mm2; j += K2_NT) {
-        unsigned long long key = 0ull;
-        if (j < C) {
-          const float p = fdiv(a.cand_e[b * CAND_CAP + j], S);  // sampling.rs:130
-          key = ((unsigned long long)fbits(p) << 32) | (unsigned long long)(~a.cand_idx[b * CAND_CAP + j]);
-        }
-        sh.u.c.key[j] = key;
-      }
-      __syncthreads();
-      bitonic_desc(sh.u.c.key, mm2);  // (p desc, index asc): the stable sort of sampling.rs:60
-      // every element outside the candidates (raw < tau) must rank below the keff-th
-      const float pk = bitsf((uint32_t)(sh.u.c.key[keff - 1] >> 32));
-      const float e_tau = tau > -INF ? pesti_expf(fsub(scale ? fdiv(tau, T) : tau, m)) : 0.0f;
-      ok = fdiv(e_tau, S) < pk;
-    }
-    if (ok) {
-      if (tid == 0) {
-        uint32_t s = 0u;  // total over the kept list (sampling.rs:81)
-        for (long long j = 0; j < keff; ++j) s = fbits(fadd(bitsf(s), bitsf((uint32_t)(sh.u.c.key[j] >> 32))));
-        sh.e_star = s;
-      }
-      __syncthreads();
-      const float total = bitsf(sh.e_star);
-      for (long long j = tid; j < keff; j += K2_NT)
-        sh.u.c.q[j] = fdiv(bitsf((uint32_t)(sh.u.c.key[j] >> 32)), total);  // sampling.rs:94
-      __syncthreads();
-      if (tid == 0) {
-        const fold::Result dr = fold::thread_fold(sh.u.c.q, keff, 0u, r_tau, true);  // sampling.rs:99-105
-        const long long at = dr.hit >= 0 ? dr.hit : keff - 1;                     // sampling.rs:108-111
-        a.out[b] = ~(uint32_t)(sh.u.c.key[at] & 0xffffffffull);
-        if (a.kept_count) a.kept_count[b] = keff;
-      }
-      for (long long j = tid; j < a.kept_width; j += K2_NT) {
-        const bool in = j < keff;
-        const unsigned long long kv = in ? sh.u.c.key[j] : 0ull;
-        if (a.kept_p) a.kept_p[b * a.kept_width + j] = in ? bitsf((uint32_t)(kv >> 32)) : 0.0f;
-        if (a.kept_idx) a.kept_idx[b * a.kept_width + j] = in ? ~(uint32_t)(kv & 0xffffffffull) : 0xffffffffu;
-      }
-      return;
-    }
-    __syncthreads();
-    // otherwise: the generic path below
-  }
 
   // ---------------- generic path ----------------
   bool dense_all = false;
@@ -1057,17 +1309,17 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
     for (int s = 0; s < nsub; ++s) {
       const SubInfo si = sh.sub[s];
       for (long long jj = tid; jj < si.cnt; jj += K2_NT) {
-        float e;
+        float raw;
         uint32_t idx;
         if (si.dense) {
           idx = (uint32_t)(si.start + jj);
-          const float raw = load_logit_dyn(row, a.dtype, si.start + jj);
-          const float x = scale ? fdiv(raw, T) : raw;  // sampling.rs:46
-          e = pesti_expf(fsub(x, m));                  // sampling.rs:127
+          raw = load_logit_dyn(row, a.dtype, si.start + jj);
         } else {
-          e = a.surv_e[b * V + si.start + jj];
+          raw = a.surv_raw[b * V + si.start + jj];
           idx = a.surv_idx[b * V + si.start + jj];
         }
+        const float x = scale ? fdiv(raw, T) : raw;  // sampling.rs:46
+        const float e = pesti_expf(fsub(x, m));      // sampling.rs:127
         E[si.base + jj] = e;
         I[si.base + jj] = idx;
         above += (dense_all || e > e_pruned) ? 1 : 0;

@@ -33,7 +33,10 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 }  // namespace
 
+constexpr size_t kRowSmemLimit = 220 * 1024;
+
 struct pesti_sampler {
+  size_t row_smem_attr = 0;  // dynamic shared memory the row kernel is currently allowed
   int device = 0;
   int num_sms = 148;
   cudaStream_t stream = nullptr;
@@ -91,6 +94,9 @@ int ensure_ws(pesti_sampler* s, size_t bytes) {
   const size_t want = bytes + bytes / 8;
   cudaError_t e = cudaMalloc(&s->ws, want);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(workspace)");
+  // the per-row completion counters must start at zero (the kernels reset them)
+  e = cudaMemset(s->ws, 0, want);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(workspace)");
   s->ws_bytes = want;
   return PESTI_OK;
 }
@@ -123,15 +129,18 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
     off = align_up(off + bytes);
     return o;
   };
+  const size_t o_ctr = take((size_t)B * 4);  // zeroed with the workspace, kept zero by the kernels
   const size_t o_stats = take((size_t)B * nsub * sizeof(pesti::SubStat));
+  const size_t o_pre = take((size_t)B * nsub * sizeof(pesti::SubPre));
+  const size_t o_info = take((size_t)B * sizeof(pesti::RowInfo));
   const size_t o_surv = take((size_t)B * nsub * sizeof(pesti::SubSurv));
+  const size_t o_ents = take((size_t)B * nsub * pesti::NE * sizeof(pesti::FoldEnt));
   const size_t o_segmax = take((size_t)B * nseg * 4);
   const size_t o_se = take(bv * 4);
   const size_t o_si = take(bv * 4);
   const size_t o_cc = take((size_t)B * 4);
   const size_t o_ce = take((size_t)B * pesti::CAND_CAP * 4);
   const size_t o_ci = take((size_t)B * pesti::CAND_CAP * 4);
-  const size_t o_tau = take((size_t)B * 4);
   const size_t o_E = take(bv * 4);
   const size_t o_I = take(bv * 4);
   const size_t o_status = take(16);
@@ -158,14 +167,17 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
   sa.SL = g.SL;
   sa.nseg = nseg;
   sa.stats = (pesti::SubStat*)(ws + o_stats);
+  sa.pre = (pesti::SubPre*)(ws + o_pre);
+  sa.info = (pesti::RowInfo*)(ws + o_info);
+  sa.row_ctr = (int*)(ws + o_ctr);
   sa.surv = (pesti::SubSurv*)(ws + o_surv);
+  sa.ents = (pesti::FoldEnt*)(ws + o_ents);
   sa.seg_max = (float*)(ws + o_segmax);
-  sa.surv_e = (float*)(ws + o_se);
+  sa.surv_raw = (float*)(ws + o_se);
   sa.surv_idx = (uint32_t*)(ws + o_si);
   sa.cand_count = (int*)(ws + o_cc);
   sa.cand_e = (float*)(ws + o_ce);
   sa.cand_idx = (uint32_t*)(ws + o_ci);
-  sa.row_tau = (float*)(ws + o_tau);
 
   cudaEvent_t* pev = nullptr;
   if (s->prof && s->prof_n < pesti_sampler::kProfMax) {
@@ -186,12 +198,13 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "slice_stats_kernel launch");
   if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[1], st), "cudaEventRecord(profile)");
+  // the survivor pass reads from L2: fewer loads in flight, smaller code
   if (dtype == PESTI_BF16) {
-    if (aligned) pesti::survivor_kernel<uint16_t, 8, 4, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
-    else pesti::survivor_kernel<uint16_t, 8, 4, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
+    if (aligned) pesti::survivor_kernel<uint16_t, 8, 1, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
+    else pesti::survivor_kernel<uint16_t, 8, 1, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
   } else {
-    if (aligned) pesti::survivor_kernel<float, 4, 8, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
-    else pesti::survivor_kernel<float, 4, 8, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
+    if (aligned) pesti::survivor_kernel<float, 4, 2, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
+    else pesti::survivor_kernel<float, 4, 2, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "survivor_kernel launch");
@@ -207,14 +220,14 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
   ra.per_row = d_per_row;
   ra.P = g.P;
   ra.SL = g.SL;
-  ra.stats = sa.stats;
+  ra.info = sa.info;
   ra.surv = sa.surv;
-  ra.surv_e = sa.surv_e;
+  ra.ents = sa.ents;
+  ra.surv_raw = sa.surv_raw;
   ra.surv_idx = sa.surv_idx;
   ra.cand_count = sa.cand_count;
   ra.cand_e = sa.cand_e;
   ra.cand_idx = sa.cand_idx;
-  ra.row_tau = sa.row_tau;
   ra.E = (float*)(ws + o_E);
   ra.I = (uint32_t*)(ws + o_I);
   ra.SK0 = sorted_bufs ? (uint32_t*)(ws + o_sk0) : nullptr;
@@ -229,7 +242,17 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
   ra.kept_width = (d_kept_p || d_kept_idx) ? kept_width : 0;
   ra.kept_count = d_kept_count;
   ra.status = (int*)(ws + o_status);
-  pesti::row_kernel<<<(unsigned)B, pesti::K2_NT, sizeof(pesti::RowShared), st>>>(ra);
+  // the fast path stages every fold entry of the row in shared memory; with
+  // very many sub-slices it does not fit and all rows take the generic path
+  const size_t fast_bytes = pesti::fast_smem_bytes((int)nsub);
+  ra.fast_enabled = sizeof(pesti::RowShared) + fast_bytes <= kRowSmemLimit ? 1 : 0;
+  const size_t smem2 = sizeof(pesti::RowShared) + (ra.fast_enabled ? fast_bytes : 0);
+  if (smem2 > s->row_smem_attr) {
+    PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2),
+                   "cudaFuncSetAttribute(row_kernel)");
+    s->row_smem_attr = smem2;
+  }
+  pesti::row_kernel<<<(unsigned)B, pesti::K2_NT, smem2, st>>>(ra);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "row_kernel launch");
   if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[3], st), "cudaEventRecord(profile)");
@@ -265,9 +288,6 @@ int pesti_sampler_create(int device, pesti_sampler** out) {
   PESTI_CUDA_TRY(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
   if (prop.major < 10) return fail(PESTI_E_UNSUPPORTED, "the sampler is built for sm_100a (B200)");
   PESTI_CUDA_TRY(cudaSetDevice(device), "cudaSetDevice");
-  PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)sizeof(pesti::RowShared)),
-                 "cudaFuncSetAttribute(row_kernel)");
   pesti_sampler* s = new pesti_sampler();
   s->device = device;
   s->num_sms = prop.multiProcessorCount;

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -36,7 +37,6 @@ int cuda_fail(cudaError_t e, const char* what) {
 constexpr size_t kRowSmemLimit = 220 * 1024;
 
 struct pesti_sampler {
-  size_t row_smem_attr = 0;  // dynamic shared memory the row kernel is currently allowed
   int device = 0;
   int num_sms = 148;
   cudaStream_t stream = nullptr;
@@ -67,8 +67,8 @@ struct Geometry {
   long long SL;
 };
 
-Geometry pick_geometry(const pesti_sampler* s, long long B, long long V, int ve) {
-  const long long target = 4LL * s->num_sms;
+Geometry pick_geometry(int num_sms, long long B, long long V, int ve) {
+  const long long target = 4LL * num_sms;
   long long P = (target + B - 1) / std::max(1LL, B);
   const long long pmax_v = std::max(1LL, V / (pesti::K1_WARPS * 1024LL));
   P = std::max(1LL, std::min({P, pmax_v, (long long)(pesti::MAX_SUBS / pesti::K1_WARPS)}));
@@ -113,15 +113,43 @@ bool needs_sorted_buffers(const pesti_sampling_params* p, long long n) {
   return false;
 }
 
-int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long B, long long V,
-           long long ld, const pesti_sampling_params& uni, const pesti_sampling_params* d_per_row,
-           bool sorted_bufs, const float* d_u, uint32_t* d_out, float* d_kept_p,
-           uint32_t* d_kept_idx, long long kept_width, int64_t* d_kept_count, cudaStream_t st) {
+// The row kernel's dynamic shared memory limit is a property of the function
+// on each device, shared by every caller in the process: it is raised once,
+// to the largest size any launch asks for, so that no caller lowers it under
+// another.
+constexpr int kMaxDevices = 64;
+std::atomic<bool> g_row_limit_set[kMaxDevices];
+
+int ensure_row_smem_limit(int device) {
+  const bool cached = device >= 0 && device < kMaxDevices;
+  if (cached && g_row_limit_set[device].load(std::memory_order_acquire)) return PESTI_OK;
+  PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)kRowSmemLimit),
+                 "cudaFuncSetAttribute(row_kernel)");
+  if (cached) g_row_limit_set[device].store(true, std::memory_order_release);
+  return PESTI_OK;
+}
+
+// Launch geometry and workspace layout of one batch call: byte offsets into
+// one workspace, each region 256-byte aligned.
+struct Plan {
+  Geometry g;
+  long long nsub, nseg;
+  bool sorted_bufs;
+  size_t o_ctr, o_stats, o_pre, o_info, o_surv, o_ents, o_segmax, o_se, o_si, o_cc, o_ce, o_ci;
+  size_t o_E, o_I, o_status;
+  size_t o_sk0 = 0, o_sv0 = 0, o_sk1 = 0, o_sv1 = 0, o_q = 0;
+  size_t bytes;  // workspace the call needs
+};
+
+Plan make_plan(int num_sms, pesti_dtype dtype, long long B, long long V, bool sorted_bufs) {
   const int esize = dtype == PESTI_BF16 ? 2 : 4;
   const int ve = 16 / esize;
-  const Geometry g = pick_geometry(s, B, V > 0 ? V : 1, ve);
-  const long long nsub = (long long)g.P * pesti::K1_WARPS;
-  const long long nseg = (std::max(1LL, V) + 32LL * ve - 1) / (32LL * ve);
+  Plan p;
+  p.g = pick_geometry(num_sms, B, V > 0 ? V : 1, ve);
+  p.nsub = (long long)p.g.P * pesti::K1_WARPS;
+  p.nseg = (std::max(1LL, V) + 32LL * ve - 1) / (32LL * ve);
+  p.sorted_bufs = sorted_bufs;
   const size_t bv = (size_t)B * (size_t)std::max(1LL, V);
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -129,32 +157,41 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
     off = align_up(off + bytes);
     return o;
   };
-  const size_t o_ctr = take((size_t)B * 4);  // zeroed with the workspace, kept zero by the kernels
-  const size_t o_stats = take((size_t)B * nsub * sizeof(pesti::SubStat));
-  const size_t o_pre = take((size_t)B * nsub * sizeof(pesti::SubPre));
-  const size_t o_info = take((size_t)B * sizeof(pesti::RowInfo));
-  const size_t o_surv = take((size_t)B * nsub * sizeof(pesti::SubSurv));
-  const size_t o_ents = take((size_t)B * nsub * pesti::NE * sizeof(pesti::FoldEnt));
-  const size_t o_segmax = take((size_t)B * nseg * 4);
-  const size_t o_se = take(bv * 4);
-  const size_t o_si = take(bv * 4);
-  const size_t o_cc = take((size_t)B * 4);
-  const size_t o_ce = take((size_t)B * pesti::CAND_CAP * 4);
-  const size_t o_ci = take((size_t)B * pesti::CAND_CAP * 4);
-  const size_t o_E = take(bv * 4);
-  const size_t o_I = take(bv * 4);
-  const size_t o_status = take(16);
-  size_t o_sk0 = 0, o_sv0 = 0, o_sk1 = 0, o_sv1 = 0, o_q = 0;
+  p.o_ctr = take((size_t)B * 4);  // must be zero at the start of a call; the kernels leave it zero
+  p.o_stats = take((size_t)B * p.nsub * sizeof(pesti::SubStat));
+  p.o_pre = take((size_t)B * p.nsub * sizeof(pesti::SubPre));
+  p.o_info = take((size_t)B * sizeof(pesti::RowInfo));
+  p.o_surv = take((size_t)B * p.nsub * sizeof(pesti::SubSurv));
+  p.o_ents = take((size_t)B * p.nsub * pesti::NE * sizeof(pesti::FoldEnt));
+  p.o_segmax = take((size_t)B * p.nseg * 4);
+  p.o_se = take(bv * 4);
+  p.o_si = take(bv * 4);
+  p.o_cc = take((size_t)B * 4);
+  p.o_ce = take((size_t)B * pesti::CAND_CAP * 4);
+  p.o_ci = take((size_t)B * pesti::CAND_CAP * 4);
+  p.o_E = take(bv * 4);
+  p.o_I = take(bv * 4);
+  p.o_status = take(16);
   if (sorted_bufs) {
-    o_sk0 = take(bv * 4);
-    o_sv0 = take(bv * 4);
-    o_sk1 = take(bv * 4);
-    o_sv1 = take(bv * 4);
-    o_q = take(bv * 4);
+    p.o_sk0 = take(bv * 4);
+    p.o_sv0 = take(bv * 4);
+    p.o_sk1 = take(bv * 4);
+    p.o_sv1 = take(bv * 4);
+    p.o_q = take(bv * 4);
   }
-  int rc = ensure_ws(s, off);
-  if (rc) return rc;
-  char* ws = (char*)s->ws;
+  p.bytes = off;
+  return p;
+}
+
+// Enqueues the three passes of one batch call on `st` over workspace `ws`
+// (laid out by `p`).  pev: four events bracketing the passes, or null.
+int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* d_logits,
+             pesti_dtype dtype, long long B, long long V, long long ld,
+             const pesti_sampling_params& uni, const pesti_sampling_params* d_per_row,
+             const float* d_u, uint32_t* d_out, float* d_kept_p, uint32_t* d_kept_idx,
+             long long kept_width, int64_t* d_kept_count, cudaStream_t st) {
+  const int esize = dtype == PESTI_BF16 ? 2 : 4;
+  const bool sorted_bufs = p.sorted_bufs;
 
   pesti::SliceArgs sa;
   sa.logits = d_logits;
@@ -163,31 +200,25 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
   sa.ld = ld;
   sa.uni = uni;
   sa.per_row = d_per_row;
-  sa.P = g.P;
-  sa.SL = g.SL;
-  sa.nseg = nseg;
-  sa.stats = (pesti::SubStat*)(ws + o_stats);
-  sa.pre = (pesti::SubPre*)(ws + o_pre);
-  sa.info = (pesti::RowInfo*)(ws + o_info);
-  sa.row_ctr = (int*)(ws + o_ctr);
-  sa.surv = (pesti::SubSurv*)(ws + o_surv);
-  sa.ents = (pesti::FoldEnt*)(ws + o_ents);
-  sa.seg_max = (float*)(ws + o_segmax);
-  sa.surv_raw = (float*)(ws + o_se);
-  sa.surv_idx = (uint32_t*)(ws + o_si);
-  sa.cand_count = (int*)(ws + o_cc);
-  sa.cand_e = (float*)(ws + o_ce);
-  sa.cand_idx = (uint32_t*)(ws + o_ci);
+  sa.P = p.g.P;
+  sa.SL = p.g.SL;
+  sa.nseg = p.nseg;
+  sa.stats = (pesti::SubStat*)(ws + p.o_stats);
+  sa.pre = (pesti::SubPre*)(ws + p.o_pre);
+  sa.info = (pesti::RowInfo*)(ws + p.o_info);
+  sa.row_ctr = (int*)(ws + p.o_ctr);
+  sa.surv = (pesti::SubSurv*)(ws + p.o_surv);
+  sa.ents = (pesti::FoldEnt*)(ws + p.o_ents);
+  sa.seg_max = (float*)(ws + p.o_segmax);
+  sa.surv_raw = (float*)(ws + p.o_se);
+  sa.surv_idx = (uint32_t*)(ws + p.o_si);
+  sa.cand_count = (int*)(ws + p.o_cc);
+  sa.cand_e = (float*)(ws + p.o_ce);
+  sa.cand_idx = (uint32_t*)(ws + p.o_ci);
 
-  cudaEvent_t* pev = nullptr;
-  if (s->prof && s->prof_n < pesti_sampler::kProfMax) {
-    pev = s->prof_ev[s->prof_n++];
-    for (int q = 0; q < 4; ++q)
-      if (!pev[q]) PESTI_CUDA_TRY(cudaEventCreate(&pev[q]), "cudaEventCreate(profile)");
-    PESTI_CUDA_TRY(cudaEventRecord(pev[0], st), "cudaEventRecord(profile)");
-  }
+  if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[0], st), "cudaEventRecord(profile)");
   const bool aligned = ((uintptr_t)d_logits % 16 == 0) && ((ld * esize) % 16 == 0);
-  const dim3 g1((unsigned)(g.P * B));
+  const dim3 g1((unsigned)(p.g.P * B));
   if (dtype == PESTI_BF16) {
     if (aligned) pesti::slice_stats_kernel<uint16_t, 8, 4, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
     else pesti::slice_stats_kernel<uint16_t, 8, 4, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
@@ -218,8 +249,8 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
   ra.ld = ld;
   ra.uni = uni;
   ra.per_row = d_per_row;
-  ra.P = g.P;
-  ra.SL = g.SL;
+  ra.P = p.g.P;
+  ra.SL = p.g.SL;
   ra.info = sa.info;
   ra.surv = sa.surv;
   ra.ents = sa.ents;
@@ -228,35 +259,51 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
   ra.cand_count = sa.cand_count;
   ra.cand_e = sa.cand_e;
   ra.cand_idx = sa.cand_idx;
-  ra.E = (float*)(ws + o_E);
-  ra.I = (uint32_t*)(ws + o_I);
-  ra.SK0 = sorted_bufs ? (uint32_t*)(ws + o_sk0) : nullptr;
-  ra.SV0 = sorted_bufs ? (uint32_t*)(ws + o_sv0) : nullptr;
-  ra.SK1 = sorted_bufs ? (uint32_t*)(ws + o_sk1) : nullptr;
-  ra.SV1 = sorted_bufs ? (uint32_t*)(ws + o_sv1) : nullptr;
-  ra.Q = sorted_bufs ? (float*)(ws + o_q) : nullptr;
+  ra.E = (float*)(ws + p.o_E);
+  ra.I = (uint32_t*)(ws + p.o_I);
+  ra.SK0 = sorted_bufs ? (uint32_t*)(ws + p.o_sk0) : nullptr;
+  ra.SV0 = sorted_bufs ? (uint32_t*)(ws + p.o_sv0) : nullptr;
+  ra.SK1 = sorted_bufs ? (uint32_t*)(ws + p.o_sk1) : nullptr;
+  ra.SV1 = sorted_bufs ? (uint32_t*)(ws + p.o_sv1) : nullptr;
+  ra.Q = sorted_bufs ? (float*)(ws + p.o_q) : nullptr;
   ra.u = d_u;
   ra.out = d_out;
   ra.kept_p = d_kept_p;
   ra.kept_idx = d_kept_idx;
   ra.kept_width = (d_kept_p || d_kept_idx) ? kept_width : 0;
   ra.kept_count = d_kept_count;
-  ra.status = (int*)(ws + o_status);
+  ra.status = (int*)(ws + p.o_status);
   // the fast path stages every fold entry of the row in shared memory; with
   // very many sub-slices it does not fit and all rows take the generic path
-  const size_t fast_bytes = pesti::fast_smem_bytes((int)nsub);
+  const size_t fast_bytes = pesti::fast_smem_bytes((int)p.nsub);
   ra.fast_enabled = sizeof(pesti::RowShared) + fast_bytes <= kRowSmemLimit ? 1 : 0;
   const size_t smem2 = sizeof(pesti::RowShared) + (ra.fast_enabled ? fast_bytes : 0);
-  if (smem2 > s->row_smem_attr) {
-    PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2),
-                   "cudaFuncSetAttribute(row_kernel)");
-    s->row_smem_attr = smem2;
+  if (smem2 > 48 * 1024) {
+    int rc = ensure_row_smem_limit(device);
+    if (rc) return rc;
   }
   pesti::row_kernel<<<(unsigned)B, pesti::K2_NT, smem2, st>>>(ra);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "row_kernel launch");
   if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[3], st), "cudaEventRecord(profile)");
   return PESTI_OK;
+}
+
+int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long B, long long V,
+           long long ld, const pesti_sampling_params& uni, const pesti_sampling_params* d_per_row,
+           bool sorted_bufs, const float* d_u, uint32_t* d_out, float* d_kept_p,
+           uint32_t* d_kept_idx, long long kept_width, int64_t* d_kept_count, cudaStream_t st) {
+  const Plan p = make_plan(s->num_sms, dtype, B, V, sorted_bufs);
+  int rc = ensure_ws(s, p.bytes);
+  if (rc) return rc;
+  cudaEvent_t* pev = nullptr;
+  if (s->prof && s->prof_n < pesti_sampler::kProfMax) {
+    pev = s->prof_ev[s->prof_n++];
+    for (int q = 0; q < 4; ++q)
+      if (!pev[q]) PESTI_CUDA_TRY(cudaEventCreate(&pev[q]), "cudaEventCreate(profile)");
+  }
+  return run_plan(p, (char*)s->ws, s->device, pev, d_logits, dtype, B, V, ld, uni, d_per_row, d_u,
+                  d_out, d_kept_p, d_kept_idx, kept_width, d_kept_count, st);
 }
 
 int check_common(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, int64_t B, int64_t V,

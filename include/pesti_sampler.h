@@ -109,6 +109,43 @@ int pesti_argmax_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype
 int pesti_sample_row_host(pesti_sampler* s, const float* h_logits, int64_t V,
                           const pesti_sampling_params* params, float u, uint32_t* out_token);
 
+/*
+ * No counterpart in the reference.
+ *
+ * pesti_sample_batch without a handle and without any device allocation, for
+ * callers that cannot allocate device memory while they sample: a decode loop
+ * that has handed the rest of HBM to its KV-cache page pool, where a
+ * cudaMalloc would fail, or one that must not stall its other streams, which
+ * cudaMalloc and cudaFree do (pesti_sample_batch grows its workspace with them
+ * whenever it meets a larger batch).
+ *
+ * Arguments and results are those of pesti_sample_batch.  It runs on the
+ * calling thread's current device; stream NULL is the legacy default stream.
+ * Its only device memory besides the caller's buffers is one static array of
+ * PESTI_NOALLOC_SCRATCH_BYTES on each device, shared by every call:
+ *  - a call that needs more scratch than the array holds fails with
+ *    PESTI_E_INVALID_ARG and launches nothing.  A call needs about 16 bytes
+ *    per logit (B*V) when every row is greedy or uses top_k <= 1024, 36 bytes
+ *    per logit otherwise (top-p, no filter, larger top_k, or params on the
+ *    device), plus host per-row params and at most about 0.3 MB per row:
+ *    8 rows of V = 128256 with top-p need about 37 MB;
+ *  - calls whose GPU work overlaps (on streams with no order between them)
+ *    race on the array: order them on one stream;
+ *  - host per-row params are copied into the array, so the caller may reuse
+ *    them once the call returns; a single params entry on the device is read
+ *    back with a stream synchronization, as in pesti_sample_batch.
+ * The first call on a device does the set-up: it looks the array up with
+ * cudaGetSymbolAddress, which loads it onto that device.  Make that first call
+ * before any stream capture.  No call allocates: none calls cudaMalloc,
+ * cudaFree or an allocating library routine.
+ */
+#define PESTI_NOALLOC_SCRATCH_BYTES (64ull << 20)
+int pesti_sample_batch_noalloc(const void* d_logits, pesti_dtype dtype, int64_t B, int64_t V,
+                               int64_t ld, const pesti_sampling_params* params,
+                               int params_per_row, int params_on_device, const float* d_u,
+                               uint32_t* d_out_tokens, float* d_kept_p, uint32_t* d_kept_idx,
+                               int64_t kept_width, int64_t* d_kept_count, void* stream);
+
 /* Message of the last failure on the calling thread ("" if none). */
 const char* pesti_last_error(void);
 

@@ -12,6 +12,7 @@
 #include "../../include/pesti_sampler.h"
 #include "../../include/pesti_profile.h"
 #include "pesti_kernels.cuh"
+#include "pesti_noalloc.h"
 
 namespace {
 
@@ -306,9 +307,7 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
                   d_out, d_kept_p, d_kept_idx, kept_width, d_kept_count, st);
 }
 
-int check_common(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, int64_t B, int64_t V,
-                 int64_t ld) {
-  if (!s) return fail(PESTI_E_INVALID_ARG, "null sampler handle");
+int check_shapes(const void* d_logits, pesti_dtype dtype, int64_t B, int64_t V, int64_t ld) {
   if (dtype != PESTI_F32 && dtype != PESTI_BF16) return fail(PESTI_E_INVALID_ARG, "unsupported dtype");
   if (B < 0 || V < 0) return fail(PESTI_E_INVALID_ARG, "negative B or V");
   if (V > 0x7fffffffLL) return fail(PESTI_E_INVALID_ARG, "V exceeds 2^31-1");
@@ -316,6 +315,12 @@ int check_common(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, int6
   if (B > 0 && V > 0 && !d_logits) return fail(PESTI_E_INVALID_ARG, "null logits");
   if (B > 0 && ld < V) return fail(PESTI_E_INVALID_ARG, "leading dimension smaller than V");
   return PESTI_OK;
+}
+
+int check_common(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, int64_t B, int64_t V,
+                 int64_t ld) {
+  if (!s) return fail(PESTI_E_INVALID_ARG, "null sampler handle");
+  return check_shapes(d_logits, dtype, B, V, ld);
 }
 
 }  // namespace
@@ -459,6 +464,66 @@ int pesti_sample_row_host(pesti_sampler* s, const float* h_logits, int64_t V,
   PESTI_CUDA_TRY(cudaStreamSynchronize(st), "cudaStreamSynchronize");
   *out_token = tok;
   return PESTI_OK;
+}
+
+int pesti_sample_batch_noalloc(const void* d_logits, pesti_dtype dtype, int64_t B, int64_t V,
+                               int64_t ld, const pesti_sampling_params* params,
+                               int params_per_row, int params_on_device, const float* d_u,
+                               uint32_t* d_out_tokens, float* d_kept_p, uint32_t* d_kept_idx,
+                               int64_t kept_width, int64_t* d_kept_count, void* stream) {
+  int rc = check_shapes(d_logits, dtype, B, V, ld);
+  if (rc) return rc;
+  if (!params) return fail(PESTI_E_INVALID_ARG, "null params");
+  if (B > 0 && (!d_u || !d_out_tokens)) return fail(PESTI_E_INVALID_ARG, "null u or output tokens");
+  if ((d_kept_p || d_kept_idx) && kept_width <= 0) return fail(PESTI_E_INVALID_ARG, "kept_width must be > 0");
+  if (B == 0) return PESTI_OK;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+    return fail(PESTI_E_NO_DEVICE, "no CUDA device available");
+  int device = 0;
+  PESTI_CUDA_TRY(cudaGetDevice(&device), "cudaGetDevice");
+  pesti_noalloc_device dev{};
+  PESTI_CUDA_TRY(pesti_noalloc_setup(device, &dev), "no-allocation scratch set-up");
+  if (dev.cc_major < 10) return fail(PESTI_E_UNSUPPORTED, "the sampler is built for sm_100a (B200)");
+  cudaStream_t st = (cudaStream_t)stream;
+
+  pesti_sampling_params uni{};
+  const pesti_sampling_params* d_per_row = nullptr;
+  bool sorted_bufs = true;
+  size_t params_bytes = 0;  // host per-row params go to the front of the scratch
+  if (params_on_device) {
+    if (params_per_row) d_per_row = params;
+    else {
+      PESTI_CUDA_TRY(cudaMemcpyAsync(&uni, params, sizeof(uni), cudaMemcpyDeviceToHost, st), "params copy");
+      PESTI_CUDA_TRY(cudaStreamSynchronize(st), "params sync");
+      sorted_bufs = needs_sorted_buffers(&uni, 1);
+    }
+  } else if (params_per_row) {
+    sorted_bufs = needs_sorted_buffers(params, B);
+    params_bytes = align_up((size_t)B * sizeof(pesti_sampling_params));
+  } else {
+    uni = params[0];
+    sorted_bufs = needs_sorted_buffers(&uni, 1);
+  }
+  const Plan p = make_plan(dev.num_sms, dtype, B, V, sorted_bufs);
+  const size_t need = params_bytes + p.bytes;
+  if (need > (size_t)PESTI_NOALLOC_SCRATCH_BYTES)
+    return fail(PESTI_E_INVALID_ARG,
+                "batch too large for pesti_sample_batch_noalloc: it needs " + std::to_string(need) +
+                    " bytes of scratch, the static array holds " +
+                    std::to_string((size_t)PESTI_NOALLOC_SCRATCH_BYTES) +
+                    " (PESTI_NOALLOC_SCRATCH_BYTES); split the batch or use pesti_sample_batch");
+  if (params_bytes) {
+    PESTI_CUDA_TRY(cudaMemcpyAsync(dev.scratch, params, (size_t)B * sizeof(pesti_sampling_params),
+                                   cudaMemcpyHostToDevice, st), "params copy");
+    d_per_row = (const pesti_sampling_params*)dev.scratch;
+  }
+  char* ws = dev.scratch + params_bytes;
+  // the per-row completion counters must start at zero, and the array holds
+  // whatever the previous call (or an aborted one) left there
+  PESTI_CUDA_TRY(cudaMemsetAsync(ws + p.o_ctr, 0, (size_t)B * sizeof(int), st), "cudaMemsetAsync(counters)");
+  return run_plan(p, ws, device, nullptr, d_logits, dtype, B, V, ld, uni, d_per_row, d_u, d_out_tokens,
+                  d_kept_p, d_kept_idx, kept_width, d_kept_count, st);
 }
 
 int pesti_profile_enable(pesti_sampler* s, int enable) {

@@ -53,8 +53,8 @@ NVCC_FLAGS = [
 
 def build(verbose: bool = False) -> str:
     """Compiles csrc/ into libpesti_sampler.so for sm_100a (in-tree)."""
-    src = os.path.join(CSRC, "pesti_sampler.cu")
-    cmd = ["nvcc", *NVCC_FLAGS, "-o", LIB_PATH, src]
+    srcs = [os.path.join(CSRC, "pesti_sampler.cu"), os.path.join(CSRC, "pesti_noalloc.cu")]
+    cmd = ["nvcc", *NVCC_FLAGS, "-o", LIB_PATH, *srcs]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)
@@ -100,6 +100,9 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
                                           ctypes.POINTER(_Params), ctypes.c_float,
                                           ctypes.POINTER(ctypes.c_uint32)]
     lib.pesti_sample_row_host.restype = c_int
+    lib.pesti_sample_batch_noalloc.argtypes = [vp, c_int, i64, i64, i64, ctypes.POINTER(_Params), c_int,
+                                               c_int, vp, vp, vp, vp, i64, vp, vp]
+    lib.pesti_sample_batch_noalloc.restype = c_int
     lib.pesti_last_error.argtypes = []
     lib.pesti_last_error.restype = ctypes.c_char_p
     _lib = lib
@@ -280,6 +283,48 @@ class Sampler:
             self._h, x.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), int(x.size), ctypes.byref(p),
             ctypes.c_float(0.0), ctypes.byref(tok)))
         return int(tok.value)
+
+
+NOALLOC_SCRATCH_BYTES = 64 << 20  # PESTI_NOALLOC_SCRATCH_BYTES
+
+
+def sample_batch_noalloc(logits, configs: Union[SamplingConfig, Sequence[SamplingConfig]], u, out,
+                         greedy_if_zero_t: bool = True, argmax_first: bool = False, kept=None,
+                         stream=None):
+    """Sampler.sample_batch through pesti_sample_batch_noalloc: no handle and no
+    device allocation inside the call, for callers that cannot allocate while
+    they sample (every output buffer is the caller's).
+
+    out: [B] int32 CUDA tensor for the tokens.  kept: None or a tuple
+    (kept_p [B, W] f32, kept_idx [B, W] int32, kept_count [B] int64).  Runs on
+    the current CUDA device in a static scratch array of NOALLOC_SCRATCH_BYTES
+    shared by every call: larger batches raise SamplerError, and calls on
+    unordered streams race.  The first call on a device sets the array up.
+    """
+    import torch
+    lib = load_library()
+    B, V = logits.shape
+    dtype = {torch.float32: PESTI_F32, torch.bfloat16: PESTI_BF16}.get(logits.dtype)
+    if dtype is None:
+        raise ValueError("logits must be float32 or bfloat16")
+    if logits.stride(1) != 1:
+        raise ValueError("logits rows must be contiguous")
+    if isinstance(configs, SamplingConfig):
+        arr = (_Params * 1)(configs.to_params(greedy_if_zero_t, argmax_first))
+        per_row = 0
+    else:
+        if len(configs) != B:
+            raise ValueError("need one config per row")
+        arr = (_Params * B)(*[c.to_params(greedy_if_zero_t, argmax_first) for c in configs])
+        per_row = 1
+    kp, ki, kc = kept if kept is not None else (None, None, None)
+    width = kp.shape[1] if kp is not None else 0
+    st = stream if stream is not None else torch.cuda.current_stream(logits.device).cuda_stream
+    _check(lib.pesti_sample_batch_noalloc(
+        logits.data_ptr(), dtype, B, V, logits.stride(0), arr, per_row, 0, u.data_ptr(), out.data_ptr(),
+        kp.data_ptr() if kp is not None else None, ki.data_ptr() if ki is not None else None, width,
+        kc.data_ptr() if kc is not None else None, st))
+    return out
 
 
 _default: Optional[Sampler] = None

@@ -168,6 +168,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernels-only", action="store_true",
+                    help="only the warm-up and timed steps (for profiler captures); prints ms_per_step")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -219,7 +221,7 @@ def main():
 
     # correctness guard on the benchmark's own input (exact vs the oracle)
     check_rows = None
-    if rank == 0:
+    if rank == 0 and not args.kernels_only:
         import oracle as O
         step(0)
         torch.cuda.synchronize()
@@ -229,6 +231,18 @@ def main():
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
+    if args.kernels_only:
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for i in range(args.steps):
+            step(i)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+        if rank == 0:
+            print(json.dumps({"kernels_only": True, "workload": spec["name"], "steps": args.steps,
+                              "ms_per_step": t_start.elapsed_time(t_end) / args.steps}))
+        return 0
     clocks = ClockSampler(local)
     barrier()
     torch.cuda.synchronize()

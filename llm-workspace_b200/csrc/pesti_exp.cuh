@@ -117,11 +117,11 @@ PESTI_HD float pesti_expf(float x) {
 // then the degree-7 Taylor polynomial of exp(r) on |r| <= ln2/2 in Horner form
 // with fma, scaled by 2^k.  Every step is a single IEEE float operation, so the
 // host build computes the same bits; tests/test_exp_exhaustive.py measures the
-// relative error against the correctly rounded exp over every float in
-// [-86, 0] (7.9e-8 at most) and checks it against PESTI_EXPF_APPROX_RELERR.
-// Returns 0 for x <= -86 (exp(x) < 4.5e-38); the caller treats those elements
-// exactly.
-#define PESTI_EXPF_APPROX_RELERR 0x1p-20f
+// relative error against the correctly rounded f32 exp (the value the folds
+// add) over every float in [-86, 0] and checks it against
+// PESTI_EXPF_APPROX_RELERR.  Returns 0 for x <= -86 (exp(x) < 4.5e-38); the
+// caller treats those elements exactly.
+#define PESTI_EXPF_APPROX_RELERR 0x1p-22f
 
 #if defined(__CUDA_ARCH__)
 #define PXF_FMA(a, b, c) __fmaf_rn((a), (b), (c))

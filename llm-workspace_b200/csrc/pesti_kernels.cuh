@@ -37,7 +37,7 @@ constexpr int FAST_K = 256;       // top-k values handled by the fast path
 constexpr int CAND_CAP = 2048;    // candidates listed per row by the survivor kernel
 constexpr int FAST_CAND = 1024;   // candidates the fast path sorts
 constexpr int TAU_BINS = 4096;    // 12-bit histogram used to place the candidate threshold
-constexpr int NE = 32;            // fold entries per sub-slice
+constexpr int NE = 96;            // fold entries per sub-slice
 constexpr int MAX_MATCH = 64;     // segments holding the row max re-scanned for its indices
 constexpr int QCAP = 512;         // survivor queue per warp (power of two)
 constexpr int STAGE = 256;        // values staged per round trip by warp_fold
@@ -623,14 +623,40 @@ __global__ void __launch_bounds__(K1_NT) slice_stats_kernel(SliceArgs a) {
 // inside it at exit) and replays the run element by element when the check
 // fails, so the classification never decides a result.
 // ---------------------------------------------------------------------------
+constexpr int GR = 8;            // survivors per lane in one classification group (consecutive)
+constexpr int GROUP = 32 * GR;   // survivors per group
+constexpr uint32_t KEY_NONE = 0xfffffffeu;  // no open run
+static_assert(QCAP >= 2 * GROUP, "a chunk may add 256 survivors to a queue holding up to GROUP-1");
+
+// The open run of a sub-slice's fold while its survivors are classified: the
+// composed increments, how many survivors it covers, and its binade
+// (KEY_NONE when there is no open run).
+struct Seg {
+  uint32_t a0, a1, cnt, key;
+};
+// Segmented composition: `b` follows `a`; a flagged `b` starts a new run.
+__device__ __forceinline__ Seg seg_join(Seg a, Seg b, bool b_starts) {
+  if (b_starts) return b;
+  const Tr t = tr_compose(Tr{a.a0, a.a1}, Tr{b.a0, b.a1});
+  return Seg{t.a0, t.a1, a.cnt + b.cnt, a.key};
+}
+__device__ __forceinline__ Seg seg_shfl_up(Seg s, int off) {
+  return Seg{__shfl_up_sync(PESTI_FULL_MASK, s.a0, off), __shfl_up_sync(PESTI_FULL_MASK, s.a1, off),
+             __shfl_up_sync(PESTI_FULL_MASK, s.cnt, off), __shfl_up_sync(PESTI_FULL_MASK, s.key, off)};
+}
+__device__ __forceinline__ Seg seg_shfl(Seg s, int src) {
+  return Seg{__shfl_sync(PESTI_FULL_MASK, s.a0, src), __shfl_sync(PESTI_FULL_MASK, s.a1, src),
+             __shfl_sync(PESTI_FULL_MASK, s.cnt, src), __shfl_sync(PESTI_FULL_MASK, s.key, src)};
+}
+
 struct SurvShared {
   float q_raw[K1_WARPS][QCAP];
-  uint32_t q_idx[K1_WARPS][QCAP];
   FoldEnt ent[K1_WARPS][NE];
+  float ea[K1_WARPS][GROUP];  // approximate exps of the group being classified
 };
 
 template <typename TIn, int VE, int U, bool VEC>
-__global__ void __launch_bounds__(K1_NT) survivor_kernel(SliceArgs a) {
+__global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
   __shared__ SurvShared sh;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const long long b = blockIdx.x / a.P;
@@ -675,80 +701,51 @@ __global__ void __launch_bounds__(K1_NT) survivor_kernel(SliceArgs a) {
   const double L = pr.A * (1.0 - (double)V * 0x1p-24) * (1.0 - 0x1p-10) * exp2(-mag);
   const bool use_L = sum_pruning_ok(prm) && L >= 0x1p-60;
   const float thrL = use_L ? m + (float)log(L) - 17.36f : NEG_INF;
+  // e_exact lies within a relative 2*RELERR of the approximation (margin for
+  // the float arithmetic of the bounds below)
+  constexpr float DE = 2.0f * PESTI_EXPF_APPROX_RELERR;
   float run_max = pr.P;
   float pruned_max = NEG_INF;
   int* ccount = a.cand_count + b;
   float* qr = sh.q_raw[w];
-  uint32_t* qi = sh.q_idx[w];
   FoldEnt* ent = sh.ent[w];
   // queue and fold state (warp-uniform)
   int qh = 0, qn = 0;
-  long long scount = 0;
+  long long sins = 0;   // survivors stored so far
   double s_approx = pr.A;
   int nent = 0;
   bool replay = false;
-  uint32_t run_lo = 0u;
-  Tr run_acc{0u, 0u};
-  uint32_t run_cnt = 0u;
+  Seg run{0u, 0u, 0u, KEY_NONE};
 
-  auto push_ent = [&](uint32_t lo, uint32_t a0, uint32_t a1, uint32_t cnt) {
-    if (nent < NE) {
-      if (lane == 0) ent[nent] = FoldEnt{lo, a0, a1, cnt};
-      ++nent;
-    } else {
-      replay = true;
-    }
-  };
-  auto flush_run = [&]() {
-    if (run_cnt > 0u) push_ent(run_lo, run_acc.a0, run_acc.a1, run_cnt);
-    run_cnt = 0u;
-  };
-
-  // classification of nv (<= 32) queued survivors, one per lane
-  auto process_batch = [&](int nv) {
-    const bool valid = lane < nv;
-    const int slot = (qh + lane) & (QCAP - 1);
-    const float raw = valid ? qr[slot] : 0.0f;
-    const uint32_t idx = valid ? qi[slot] : 0u;
-    float d = 0.0f;
-    if (valid) {
-      const float xs = scale ? fdiv(raw, T) : raw;  // sampling.rs:46
-      d = fsub(xs, m);                              // sampling.rs:127 (argument of exp)
-      a.surv_raw[out_base + scount + lane] = raw;   // exact exp is recomputed where needed
-      a.surv_idx[out_base + scount + lane] = idx;
-    }
-    scount += nv;
-    qh = (qh + nv) & (QCAP - 1);
-    qn -= nv;
-    // exp within a relative 2^-20 (exact below where it matters)
-    const float ea = valid ? pesti_expf_approx(d) : 0.0f;
-    // approximate running state before each element
-    float inc = ea;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float y = __shfl_up_sync(PESTI_FULL_MASK, inc, o);
-      if (lane >= o) inc += y;
-    }
-    const double av = s_approx + (double)(inc - ea);
-    const double bv = av + (double)ea;
-    s_approx += (double)__shfl_sync(PESTI_FULL_MASK, inc, 31);
-    if (replay) return;
-    uint32_t lo;
+  // Classification of the n (<= GROUP) survivors at the queue head.  Lane l
+  // takes survivors [l*GR, l*GR + GR) of the group, so one warp scan gives every
+  // element its approximate running state and a segmented scan over the lanes
+  // joins the runs that cross lane boundaries.  The per-element loops are kept
+  // rolled (the approximate exps wait in shared memory between the passes):
+  // this kernel runs out of instruction cache long before it runs out of issue
+  // slots, so straight-line code is the expensive kind here.
+  float* eas = sh.ea[w];
+  // Guard band around binade edges for the classification.  The approximate
+  // state tracks the fold within about 1.2e-4 (its bias is the mass that the
+  // fold absorbs); a run predicted in the wrong binade fails its check in the
+  // row kernel and is replayed there, so the band trades entries for replays
+  // and never decides a result.
+  constexpr float BAND = 0x1p-12f;
+  // element i of the group: its run key (binade or SPECIAL) and increments
+  auto classify = [&](int i, float ea, float av, float bv, uint32_t& key, uint32_t& k0, uint32_t& k1) {
+    uint32_t lo = 0u;
     bool special;
-    const float eu = ea * (1.0f + 0x1p-19f);  // upper bound of the exact value
-    if (av < 0x1p-126) {
-      lo = 0u;
-      special = eu >= 0x1p-127f || bv > 0x1p-126 * (1.0 - fold::MU);
+    const float eu = ea * (1.0f + DE);  // upper bound of the exact value
+    if (av < 0x1p-126f) {
+      special = eu >= 0x1p-127f || bv > 0x1p-126f * (1.0f - BAND);
     } else {
-      lo = fbits(__double2float_rz(av)) & 0x7f800000u;
-      const double lov = (double)bitsf(lo);
-      special = eu >= bitsf(lo - 0x00800000u) || av < lov * (1.0 + fold::MU) || bv > 2.0 * lov * (1.0 - fold::MU);
+      lo = fbits(av) & 0x7f800000u;
+      const float lov = bitsf(lo);
+      special = eu >= bitsf(lo - 0x00800000u) || av < lov * (1.0f + BAND) || bv > 2.0f * lov * (1.0f - BAND);
     }
-    // increment in ulps of the binade: ea/w rounded, exact unless ea/w is within
-    // the error bound of a rounding boundary (then from the exact exp)
-    Tr t{0u, 0u};
-    bool need_exact = valid && special;
-    if (valid && !special) {
+    bool need_exact = special;
+    k0 = k1 = 0u;
+    if (!special) {
       const uint32_t E = lo >> 23;  // w = 2^(E-150) (E = 0: the subnormal grid 2^-149)
       const int sh2 = 150 - (int)(E == 0u ? 1u : E);
       if (ea == 0.0f) {
@@ -757,120 +754,293 @@ __global__ void __launch_bounds__(K1_NT) survivor_kernel(SliceArgs a) {
         const float tt = __uint_as_float(fbits(ea) + ((uint32_t)sh2 << 23));  // ea/w, exact scaling
         const float kr = rintf(tt);
         const float slack = 0.5f - fabsf(tt - kr);
-        if (slack <= tt * 0x1p-19f + 0x1p-22f) need_exact = true;
-        else t.a0 = t.a1 = (uint32_t)kr;
+        if (slack <= tt * DE + 0x1p-24f) need_exact = true;
+        else k0 = k1 = (uint32_t)kr;
       }
     }
-    float ex = 0.0f;
     if (need_exact) {
-      ex = pesti_expf_call(d);  // sampling.rs:127, exact
-      if (!special) {
-        t.a0 = fbits(fadd(bitsf(lo), ex)) - lo;
-        t.a1 = fbits(fadd(bitsf(lo + 1u), ex)) - (lo + 1u);
+      const float raw = qr[(qh + i) & (QCAP - 1)];
+      const float ex = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127, exact
+      if (special) {
+        k0 = fbits(ex);
+      } else {
+        k0 = fbits(fadd(bitsf(lo), ex)) - lo;
+        k1 = fbits(fadd(bitsf(lo + 1u), ex)) - (lo + 1u);
       }
     }
-    const uint32_t breaks = __ballot_sync(PESTI_FULL_MASK, valid && (special || lo != run_lo || run_cnt == 0u));
-    if (breaks == 0u) {
-      // the whole batch continues the current run
-      const Tr r = tr_warp_reduce(t);
-      const Tr r0{__shfl_sync(PESTI_FULL_MASK, r.a0, 0), __shfl_sync(PESTI_FULL_MASK, r.a1, 0)};
-      run_acc = tr_compose(run_acc, r0);
-      run_cnt += (uint32_t)nv;
+    key = special ? fold::SPECIAL : lo;
+  };
+  auto process_group = [&](int n) {
+    if (replay) {  // the row kernel replays this sub-slice from its stored survivors
+      qh = (qh + n) & (QCAP - 1);
+      qn -= n;
       return;
     }
-    for (int l = 0; l < nv; ++l) {  // element by element (warp-uniform)
-      const bool sp = __shfl_sync(PESTI_FULL_MASK, special, l);
-      const uint32_t lol = __shfl_sync(PESTI_FULL_MASK, lo, l);
-      const uint32_t k0 = __shfl_sync(PESTI_FULL_MASK, t.a0, l);
-      const uint32_t k1 = __shfl_sync(PESTI_FULL_MASK, t.a1, l);
-      const uint32_t eb = __shfl_sync(PESTI_FULL_MASK, fbits(ex), l);
-      if (sp) {
-        flush_run();
-        push_ent(fold::SPECIAL, eb, 0u, 1u);
-      } else if (run_cnt == 0u || lol != run_lo) {
-        flush_run();
-        run_lo = lol;
-        run_acc = Tr{k0, k1};
-        run_cnt = 1u;
-      } else {
-        run_acc = tr_compose(run_acc, Tr{k0, k1});
-        ++run_cnt;
+    const int i0 = lane * GR;
+    const int nl = n - i0 < 0 ? 0 : (n - i0 > GR ? GR : n - i0);  // valid elements of the lane
+    // pass A: approximate exps (sampling.rs:46,127 up to a relative 2^-22)
+    float ltot = 0.0f;
+#pragma unroll 1
+    for (int j = 0; j < nl; ++j) {
+      const float raw = qr[(qh + i0 + j) & (QCAP - 1)];
+      const float e = pesti_expf_approx(fsub(scale ? fdiv(raw, T) : raw, m));
+      eas[j * 32 + lane] = e;
+      ltot += e;
+    }
+    const float lincl = warp_incl_scan_add(ltot);
+    const float gtot = __shfl_sync(PESTI_FULL_MASK, lincl, 31);
+    // approximate states as floats relative to the carried double (the guard
+    // band is 2^-10; float rounding is 2^-24)
+    const float sb = (float)s_approx;
+    const float lbase = lincl - ltot;
+    // the key of the lane's last element decides whether the next lane's first
+    // element continues its run
+    uint32_t last_key = KEY_NONE;
+    if (nl > 0) {
+      const float el = eas[(nl - 1) * 32 + lane];
+      const float avl = sb + (lbase + (ltot - el));
+      uint32_t k0, k1;
+      classify(i0 + nl - 1, el, avl, sb + (lbase + ltot), last_key, k0, k1);
+    }
+    uint32_t prev_key = __shfl_up_sync(PESTI_FULL_MASK, last_key, 1);
+    if (lane == 0) prev_key = run.cnt > 0u ? run.key : KEY_NONE;
+    // pass B: lane summary; `lead` continues the run open before the lane,
+    // `trail` is the run open after it (hh: the lane starts at least one run)
+    bool hh = false;
+    Seg lead{0u, 0u, 0u, KEY_NONE}, trail{0u, 0u, 0u, KEY_NONE};
+    int n_int = 0;  // entries closed inside the lane after its first run start
+    {
+      uint32_t cur = prev_key;
+      float runf = lbase;
+#pragma unroll 1
+      for (int j = 0; j < nl; ++j) {
+        const float ea = eas[j * 32 + lane];
+        const float av = sb + runf;
+        runf += ea;
+        uint32_t k, k0, k1;
+        classify(i0 + j, ea, av, sb + runf, k, k0, k1);
+        const bool head = k == fold::SPECIAL || cur == fold::SPECIAL || cur == KEY_NONE || k != cur;
+        if (head) {
+          if (hh && trail.cnt > 0u) ++n_int;
+          hh = true;
+          if (k == fold::SPECIAL) {
+            ++n_int;
+            trail = Seg{0u, 0u, 0u, KEY_NONE};
+          } else {
+            trail = Seg{k0, k1, 1u, k};
+          }
+        } else if (!hh) {
+          const Tr t = tr_compose(Tr{lead.a0, lead.a1}, Tr{k0, k1});
+          lead = Seg{t.a0, t.a1, lead.cnt + 1u, KEY_NONE};
+        } else {
+          const Tr t = tr_compose(Tr{trail.a0, trail.a1}, Tr{k0, k1});
+          trail = Seg{t.a0, t.a1, trail.cnt + 1u, trail.key};
+        }
+        cur = k;
       }
+    }
+    s_approx += (double)gtot;
+    // segmented inclusive scan over the lanes
+    Seg inc = hh ? trail : lead;
+    bool fl = hh;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const Seg o = seg_shfl_up(inc, off);
+      const bool of = __shfl_up_sync(PESTI_FULL_MASK, fl, off);
+      if (lane >= off) {
+        inc = seg_join(o, inc, fl);
+        fl = fl || of;
+      }
+    }
+    // the run open before the lane (the group's carried run joined in)
+    Seg xin = seg_shfl_up(inc, 1);
+    const bool xfl = __shfl_up_sync(PESTI_FULL_MASK, fl, 1);
+    xin = lane == 0 ? run : seg_join(run, xin, xfl);
+    const Seg last = seg_shfl(inc, 31);
+    const bool lastfl = __shfl_sync(PESTI_FULL_MASK, fl, 31);
+    // entries, in row order: the run closed by the lane's first start, then
+    // the ones closed inside the lane
+    const Seg first = seg_join(xin, lead, false);
+    const int ne = n_int + ((hh && first.cnt > 0u) ? 1 : 0);
+    const int neincl = warp_incl_scan_add(ne);
+    const int netot = __shfl_sync(PESTI_FULL_MASK, neincl, 31);
+    if (nent + netot > NE) {
+      replay = true;
+    } else if (netot > 0) {
+      int slot = nent + neincl - ne;
+      if (hh) {  // pass C: the same walk, writing the entries
+        uint32_t cur = prev_key;
+        bool started = false;
+        Seg tr{0u, 0u, 0u, KEY_NONE};
+        float runf = lbase;
+#pragma unroll 1
+        for (int j = 0; j < nl; ++j) {
+          const float ea = eas[j * 32 + lane];
+          const float av = sb + runf;
+          runf += ea;
+          uint32_t k, k0, k1;
+          classify(i0 + j, ea, av, sb + runf, k, k0, k1);
+          const bool head = k == fold::SPECIAL || cur == fold::SPECIAL || cur == KEY_NONE || k != cur;
+          if (head) {
+            if (!started) {
+              if (first.cnt > 0u) ent[slot++] = FoldEnt{first.key, first.a0, first.a1, first.cnt};
+              started = true;
+            } else if (tr.cnt > 0u) {
+              ent[slot++] = FoldEnt{tr.key, tr.a0, tr.a1, tr.cnt};
+            }
+            if (k == fold::SPECIAL) {
+              ent[slot++] = FoldEnt{fold::SPECIAL, k0, 0u, 1u};
+              tr = Seg{0u, 0u, 0u, KEY_NONE};
+            } else {
+              tr = Seg{k0, k1, 1u, k};
+            }
+          } else if (started) {
+            const Tr t = tr_compose(Tr{tr.a0, tr.a1}, Tr{k0, k1});
+            tr = Seg{t.a0, t.a1, tr.cnt + 1u, tr.key};
+          }
+          cur = k;
+        }
+      }
+      nent += netot;
+    }
+    qh = (qh + n) & (QCAP - 1);
+    qn -= n;
+    if (!replay) {
+      run = seg_join(run, last, lastfl);
+      if (run.cnt == 0u) run = Seg{0u, 0u, 0u, KEY_NONE};
     }
   };
 
-  stream_subslice<TIn, VE, U, VEC>(row, start, end, [&](const float* x, long long pos0, int nv) {
-    // max of the row before this segment (exact): a lower bound of every
-    // element's own prefix max
-    const float P = run_max;
-    const float thrP = P >= p_floor ? fsub(P, fadd(c1, 0x1p-21f * fabsf(P))) : NEG_INF;
-    bool sv[VE];
-    int cnt = 0, ccnt = 0;
-    float lm = NEG_INF;
+  // One loop over the sub-slice's 32*VE*U-element chunks, then one more pass
+  // that drains the queue; the element code and process_group each appear
+  // once (the kernel is sensitive to its code size).
+  const long long CH = 32LL * VE * U;
+  for (long long pos = start;; pos += CH) {
+    const bool more = pos < end;
+    if (more) {
+      float xs_[U][VE];
+      int nvs[U];
+      if (VEC && pos + CH <= end) {
 #pragma unroll
-    for (int e = 0; e < VE; ++e) {
-      const float xv = x[e];
-      const bool valid = e < nv && !is_nan(xv);
-      if (e < nv) lm = fmaxf(lm, xv);
-      const float xa = xv * invT;
-      const bool pruneL = xa < thrL - 0x1p-19f * (fabsf(xa) + fabsf(thrL));
-      sv[e] = valid && !(xv < thrP || pruneL);
-      if (valid && !sv[e]) pruned_max = fmaxf(pruned_max, xv);
-      cnt += sv[e] ? 1 : 0;
-      ccnt += (valid && xv >= tau) ? 1 : 0;
-    }
-    run_max = fmaxf(run_max, fkey_inv(__reduce_max_sync(PESTI_FULL_MASK, fkey(lm))));
-    // survivors join the queue in row order
-    const int cinc = warp_incl_scan_add(cnt);
-    const int wsum = __shfl_sync(PESTI_FULL_MASK, cinc, 31);
-    int o = qh + qn + (cinc - cnt);
+        for (int uu = 0; uu < U; ++uu) {
+          const float4 r4 = __ldg(reinterpret_cast<const float4*>(row + pos + (long long)uu * 32 * VE + (long long)lane * VE));
+          if (sizeof(TIn) == 4) {
+            xs_[uu][0] = r4.x; xs_[uu][1] = r4.y; xs_[uu][2] = r4.z; xs_[uu][3] = r4.w;
+          } else {
+            const uint32_t wds[4] = {__float_as_uint(r4.x), __float_as_uint(r4.y), __float_as_uint(r4.z),
+                                     __float_as_uint(r4.w)};
 #pragma unroll
-    for (int e = 0; e < VE; ++e) {
-      if (sv[e]) {
-        qr[o & (QCAP - 1)] = x[e];
-        qi[o & (QCAP - 1)] = (uint32_t)(pos0 + e);
-        ++o;
-      }
-    }
-    qn += wsum;
-    // top-k candidates: few per row, exact exp computed right here
-    const uint32_t cm = __ballot_sync(PESTI_FULL_MASK, ccnt > 0);
-    if (cm) {
-      const int ctot = warp_reduce_add(ccnt);
-      int basec = 0;
-      if (lane == 0) basec = atomicAdd(ccount, ctot);
-      basec = __shfl_sync(PESTI_FULL_MASK, basec, 0);
-      int cex = warp_incl_scan_add(ccnt) - ccnt;
-      for (int e = 0; e < VE; ++e) {
-        const float xv = x[e];
-        if (e < nv && !is_nan(xv) && xv >= tau) {
-          const int slot = basec + cex;
-          if (slot < CAND_CAP) {
-            const float xs = scale ? fdiv(xv, T) : xv;
-            a.cand_e[b * CAND_CAP + slot] = pesti_expf_call(fsub(xs, m));
-            a.cand_idx[b * CAND_CAP + slot] = (uint32_t)(pos0 + e);
+            for (int q = 0; q < 4; ++q) {
+              xs_[uu][2 * q] = __uint_as_float(wds[q] << 16);
+              xs_[uu][2 * q + 1] = __uint_as_float(wds[q] & 0xffff0000u);
+            }
           }
-          ++cex;
+          nvs[uu] = VE;
+        }
+      } else {
+#pragma unroll
+        for (int uu = 0; uu < U; ++uu) {
+          const long long p0 = pos + (long long)uu * 32 * VE + (long long)lane * VE;
+          int nv = 0;
+#pragma unroll
+          for (int e = 0; e < VE; ++e) {
+            const long long j = p0 + e;
+            xs_[uu][e] = j < end ? load_logit<TIn>(row, j) : 0.0f;
+            nv = j < end ? e + 1 : nv;
+          }
+          nvs[uu] = nv;
+        }
+      }
+#pragma unroll
+      for (int uu = 0; uu < U; ++uu) {
+        const float(&x)[VE] = xs_[uu];
+        const int nv = nvs[uu];
+        const long long pos0 = pos + (long long)uu * 32 * VE + (long long)lane * VE;
+        // max of the row before this segment (exact): a lower bound of every
+        // element's own prefix max
+        const float P = run_max;
+        const float thrP = P >= p_floor ? fsub(P, fadd(c1, 0x1p-21f * fabsf(P))) : NEG_INF;
+        bool sv[VE];
+        int cnt = 0, ccnt = 0;
+        float lm = NEG_INF;
+#pragma unroll
+        for (int e = 0; e < VE; ++e) {
+          const float xv = x[e];
+          const bool valid = e < nv && !is_nan(xv);
+          if (e < nv) lm = fmaxf(lm, xv);
+          const float xa = xv * invT;
+          const bool pruneL = xa < thrL - 0x1p-19f * (fabsf(xa) + fabsf(thrL));
+          sv[e] = valid && !(xv < thrP || pruneL);
+          if (valid && !sv[e]) pruned_max = fmaxf(pruned_max, xv);
+          cnt += sv[e] ? 1 : 0;
+          ccnt += (valid && xv >= tau) ? 1 : 0;
+        }
+        run_max = fmaxf(run_max, fkey_inv(__reduce_max_sync(PESTI_FULL_MASK, fkey(lm))));
+        // survivors join the queue and the stored sequence in row order
+        const int cinc = warp_incl_scan_add(cnt);
+        const int wsum = __shfl_sync(PESTI_FULL_MASK, cinc, 31);
+        int o = qh + qn + (cinc - cnt);
+        long long g = out_base + sins + (cinc - cnt);
+#pragma unroll
+        for (int e = 0; e < VE; ++e) {
+          if (sv[e]) {
+            qr[o & (QCAP - 1)] = x[e];
+            a.surv_raw[g] = x[e];  // exact exp is recomputed from these where needed
+            a.surv_idx[g] = (uint32_t)(pos0 + e);
+            ++o;
+            ++g;
+          }
+        }
+        qn += wsum;
+        sins += wsum;
+        // top-k candidates: few per row, exact exp computed right here
+        if (__any_sync(PESTI_FULL_MASK, ccnt > 0)) {
+          const int cex0 = warp_incl_scan_add(ccnt);
+          const int ctot = __shfl_sync(PESTI_FULL_MASK, cex0, 31);
+          int basec = 0;
+          if (lane == 0) basec = atomicAdd(ccount, ctot);
+          basec = __shfl_sync(PESTI_FULL_MASK, basec, 0);
+          int slot = basec + cex0 - ccnt;
+#pragma unroll
+          for (int e = 0; e < VE; ++e) {
+            const float xv = x[e];
+            if (e < nv && !is_nan(xv) && xv >= tau) {
+              if (slot < CAND_CAP) {
+                const float xsc = scale ? fdiv(xv, T) : xv;
+                a.cand_e[b * CAND_CAP + slot] = pesti_expf_call(fsub(xsc, m));
+                a.cand_idx[b * CAND_CAP + slot] = (uint32_t)(pos0 + e);
+              }
+              ++slot;
+            }
+          }
         }
       }
     }
-  }, [&]() {
     __syncwarp();
-    while (qn >= 32) {
-      process_batch(32);
+    const int need = more ? GROUP : 1;
+    while (qn >= need) {
+      process_group(qn < GROUP ? qn : GROUP);
       __syncwarp();
     }
-  });
-  if (qn > 0) process_batch(qn);
-  flush_run();
+    if (!more) break;
+  }
+  if (!replay && run.cnt > 0u) {
+    if (nent < NE) {
+      if (lane == 0) ent[nent] = FoldEnt{run.key, run.a0, run.a1, run.cnt};
+      ++nent;
+    } else {
+      replay = true;
+    }
+  }
   __syncwarp();
   const float pm = warp_reduce_fmax(pruned_max);
   FoldEnt* gent = a.ents + (b * nsub + sub) * NE;
-  for (int i = lane; i < (nent < NE ? nent : NE); i += 32) gent[i] = ent[i];
+  const int nout = replay ? 0 : nent;
+  for (int i = lane; i < nout; i += 32) gent[i] = ent[i];
   if (lane == 0) {
     SubSurv z;
-    z.count = (int32_t)scount;
-    z.nent = nent < NE ? nent : NE;
+    z.count = (int32_t)sins;
+    z.nent = nout;
     z.replay = replay ? 1 : 0;
     z.pruned_max = pm;
     *so = z;
@@ -912,14 +1082,21 @@ struct RowShared {
 };
 
 // Fast-path arrays, placed after RowShared in dynamic shared memory.
+constexpr int FAST_ENTS = 1024;  // fold entries of a row the fast path stages
+constexpr uint32_t ENT_REPLAY = 0xfffffffdu;  // staged entry: replay the whole sub-slice
 struct FastSmem {
   unsigned long long key[FAST_CAND];
   float q[FAST_CAND];
   float stage[STAGE];
-  // followed by SubSurv[nsub] and FoldEnt[nsub*NE]
+  FoldEnt ent[FAST_ENTS];      // the row's entries, sub-slice after sub-slice
+  uint32_t epos[FAST_ENTS];    // first survivor of each entry within its sub-slice
+  uint16_t esub[FAST_ENTS];    // sub-slice of each entry
+  int total;                   // entries of the row (> FAST_ENTS: not staged)
+  float p_tau;                 // exp of the candidate threshold (scaled, minus m)
+  // followed by SubSurv[nsub] and int eoff[nsub] (first entry of each sub-slice)
 };
 __host__ __device__ inline size_t fast_smem_bytes(int nsub) {
-  return sizeof(FastSmem) + (size_t)nsub * (sizeof(SubSurv) + NE * sizeof(FoldEnt));
+  return sizeof(FastSmem) + (size_t)nsub * (sizeof(SubSurv) + sizeof(int));
 }
 
 // Rust's Iterator::max_by over the raw logits with partial_cmp (sampling.rs:115-122)
@@ -1037,6 +1214,54 @@ __device__ void warp_bitonic_desc(unsigned long long* key, int m) {
       __syncwarp();
     }
   }
+}
+
+// Bitonic sort, descending, of 32*R keys held R per lane (element r*32 + lane),
+// by one warp in registers.
+template <int R>
+__device__ __forceinline__ void warp_sort_desc_regs(unsigned long long (&v)[R]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= 32 * R; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= 32) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int rp = r ^ (j >> 5);
+          if (rp > r) {
+            const bool desc = ((r * 32 + lane) & k) == 0;
+            const unsigned long long x = v[r], y = v[rp];
+            if (desc ? (x < y) : (x > y)) {
+              v[r] = y;
+              v[rp] = x;
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const unsigned long long y = __shfl_xor_sync(PESTI_FULL_MASK, v[r], j);
+          const bool desc = ((r * 32 + lane) & k) == 0;
+          const bool keep_max = desc == ((lane & j) == 0);
+          v[r] = keep_max ? (v[r] > y ? v[r] : y) : (v[r] < y ? v[r] : y);
+        }
+      }
+    }
+  }
+}
+
+template <int R>
+__device__ void warp_sort_keys(unsigned long long* key, int n) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long v[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) v[r] = r * 32 + lane < n ? key[r * 32 + lane] : 0ull;
+  warp_sort_desc_regs<R>(v);
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+    if (r * 32 + lane < n) key[r * 32 + lane] = v[r];
+  __syncwarp();
 }
 
 // Fold of the exps of n survivors (their raw logits in global memory) by one
@@ -1182,72 +1407,134 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
 
   // ---------------- fast path: explicit top-k of at most FAST_K (one warp) ----------------
   if (a.fast_enabled && fast_topk(prm, V)) {
-    if (wid == 0) {
-      FastSmem& fs = *reinterpret_cast<FastSmem*>(row_smem + sizeof(RowShared));
-      SubSurv* ss = reinterpret_cast<SubSurv*>(row_smem + sizeof(RowShared) + sizeof(FastSmem));
-      FoldEnt* se = reinterpret_cast<FoldEnt*>(ss + nsub);
+    FastSmem& fs = *reinterpret_cast<FastSmem*>(row_smem + sizeof(RowShared));
+    SubSurv* ss = reinterpret_cast<SubSurv*>(row_smem + sizeof(RowShared) + sizeof(FastSmem));
+    int* eoff = reinterpret_cast<int*>(ss + nsub);
+    // stage the row's fold entries, compacted, with the whole block; a
+    // sub-slice whose entries overflowed stages one marker to replay it
+    const long long keff = k < V ? k : V;
+    {
       const FoldEnt* gent = a.ents + b * nsub * NE;
-      const long long keff = k < V ? k : V;
-      // stage the fold entries (independent loads)
-      for (int q = lane; q < nsub; q += 32) ss[q] = survs[q];
-      __syncwarp();
-      for (int q = lane; q < nsub; q += 32) {
-        const int ne = ss[q].replay ? 0 : ss[q].nent;
-        for (int i = 0; i < ne; ++i) se[q * NE + i] = gent[q * NE + i];
+      int ne = 0;
+      if (tid < nsub) {
+        const SubSurv sv = survs[tid];
+        ss[tid] = sv;
+        ne = sv.count <= 0 ? 0 : (sv.replay ? 1 : sv.nent);
       }
-      const int C = a.cand_count[b];
-      __syncwarp();
-      // softmax denominator (sampling.rs:128): walk the entries with the exact state
-      uint32_t s = 0u;
-      for (int q = 0; q < nsub; ++q) {
-        const long long st = (long long)q * a.SL;
-        if (st >= V) break;
-        const SubSurv sv = ss[q];
-        if (sv.count <= 0) continue;
-        const float* vals = a.surv_raw + b * V + st;
-        if (sv.replay) {
-          s = warp_fold(vals, sv.count, s, fs.stage, scale, T, m);
-          continue;
-        }
-        long long pos = 0;
-        for (int i = 0; i < sv.nent; ++i) {
-          const FoldEnt en = se[q * NE + i];
-          if (en.lo == fold::SPECIAL) {
-            s = fbits(fadd(bitsf(s), bitsf(en.a0)));
-          } else {
-            bool applied = false;
-            if (fold::binade_lo_bits(s) == en.lo) {
-              const unsigned long long ns = (unsigned long long)s + ((s & 1u) ? en.a1 : en.a0);
-              if (ns < (unsigned long long)fold::binade_hi_bits(en.lo)) {
-                s = (uint32_t)ns;
-                applied = true;
-              }
+      int tot;
+      const int ex = block_excl_scan_add(ne, sh.iscr, tot);
+      if (tid < nsub) eoff[tid] = ex;
+      if (tid == 0) fs.total = tot;
+      __syncthreads();
+      if (tot <= FAST_ENTS) {
+        for (int q = wid; q < nsub; q += K2_NT / 32) {
+          const SubSurv sv = ss[q];
+          if (sv.count <= 0) continue;
+          const int e0 = eoff[q];
+          if (sv.replay) {
+            if (lane == 0) {
+              fs.ent[e0] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)sv.count};
+              fs.epos[e0] = 0u;
+              fs.esub[e0] = (uint16_t)q;
             }
-            if (!applied) s = warp_fold(vals + pos, en.count, s, fs.stage, scale, T, m);
+            continue;
           }
-          pos += en.count;
+          uint32_t base = 0u;
+          for (int i0 = 0; i0 < sv.nent; i0 += 32) {
+            const int i = i0 + lane;
+            FoldEnt en{0u, 0u, 0u, 0u};
+            if (i < sv.nent) en = gent[q * NE + i];
+            const uint32_t inc = warp_incl_scan_add(en.count);
+            if (i < sv.nent) {
+              fs.ent[e0 + i] = en;
+              fs.epos[e0 + i] = base + inc - en.count;
+              fs.esub[e0 + i] = (uint16_t)q;
+            }
+            base += __shfl_sync(PESTI_FULL_MASK, inc, 31);
+          }
         }
       }
-      const float S = bitsf(s);
-      bool ok = C >= keff && C <= FAST_CAND;
-      if (ok) {
+      __syncthreads();
+    }
+    const int C = a.cand_count[b];
+    const bool cand_ok = C >= keff && C <= FAST_CAND;
+    if (wid == 1 && fs.total <= FAST_ENTS && cand_ok) {
+      // candidates by (e desc, index asc) while warp 0 folds; the order by p
+      // = e/S differs only inside groups of equal p (fixed up below)
+      for (int j = lane; j < C; j += 32)
+        fs.key[j] = ((unsigned long long)fbits(a.cand_e[b * CAND_CAP + j]) << 32) |
+                    (unsigned long long)(~a.cand_idx[b * CAND_CAP + j]);
+      __syncwarp();
+      if (C <= 32) warp_sort_keys<1>(fs.key, C);
+      else if (C <= 64) warp_sort_keys<2>(fs.key, C);
+      else if (C <= 128) warp_sort_keys<4>(fs.key, C);
+      else {
         int mm2 = 1;
         while (mm2 < C) mm2 <<= 1;
-        for (int j = lane; j < mm2; j += 32) {
-          unsigned long long key = 0ull;
-          if (j < C) {
-            const float p = fdiv(a.cand_e[b * CAND_CAP + j], S);  // sampling.rs:130
-            key = ((unsigned long long)fbits(p) << 32) | (unsigned long long)(~a.cand_idx[b * CAND_CAP + j]);
+        for (int j = C + lane; j < mm2; j += 32) fs.key[j] = 0ull;
+        __syncwarp();
+        warp_bitonic_desc(fs.key, mm2);
+      }
+      const float tau = ri.tau;
+      const float e_tau = tau > -INF ? pesti_expf(fsub(scale ? fdiv(tau, T) : tau, m)) : 0.0f;
+      if (lane == 0) fs.p_tau = e_tau;
+    }
+    uint32_t s = 0u;
+    if (wid == 0 && fs.total <= FAST_ENTS) {
+      // softmax denominator (sampling.rs:128): walk the entries with the exact
+      // state; a run the state does not fit (or a replay marker) is folded
+      // from its survivors
+      const int total = fs.total;
+      int i = 0;
+      while (i < total) {
+        for (; i < total; ++i) {
+          const FoldEnt en = fs.ent[i];
+          if (en.lo == fold::SPECIAL) {
+            s = fbits(fadd(bitsf(s), bitsf(en.a0)));
+            continue;
           }
-          fs.key[j] = key;
+          if (fold::binade_lo_bits(s) != en.lo) break;  // also every replay marker
+          const unsigned long long ns = (unsigned long long)s + ((s & 1u) ? en.a1 : en.a0);
+          if (ns >= (unsigned long long)fold::binade_hi_bits(en.lo)) break;
+          s = (uint32_t)ns;
+        }
+        if (i >= total) break;
+        const float* vals = a.surv_raw + b * V + (long long)fs.esub[i] * a.SL + fs.epos[i];
+        s = warp_fold(vals, fs.ent[i].count, s, fs.stage, scale, T, m);
+        ++i;
+      }
+    }
+    __syncthreads();
+    if (wid == 0 && fs.total <= FAST_ENTS) {
+      const float S = bitsf(s);
+      bool ok = cand_ok;
+      if (ok) {
+        // p = e/S (sampling.rs:130); the list stays sorted by p except inside
+        // groups of equal p, which the stable sort (sampling.rs:60) orders by index
+        for (int j = lane; j < C; j += 32) {
+          const unsigned long long kv = fs.key[j];
+          fs.key[j] = ((unsigned long long)fbits(fdiv(bitsf((uint32_t)(kv >> 32)), S)) << 32) | (kv & 0xffffffffull);
         }
         __syncwarp();
-        warp_bitonic_desc(fs.key, mm2);  // (p desc, index asc): the stable sort of sampling.rs:60
+        bool viol = false;
+        for (int j = lane; j + 1 < C; j += 32) viol |= fs.key[j] < fs.key[j + 1];
+        if (__any_sync(PESTI_FULL_MASK, viol)) {
+          if (lane == 0) {  // insertion sort: only equal-p groups are out of order
+            for (int j = 1; j < C; ++j) {
+              const unsigned long long kv = fs.key[j];
+              int t = j - 1;
+              while (t >= 0 && fs.key[t] < kv) {
+                fs.key[t + 1] = fs.key[t];
+                --t;
+              }
+              fs.key[t + 1] = kv;
+            }
+          }
+          __syncwarp();
+        }
         // every element outside the candidates (raw < tau) must rank below the keff-th
         const float pk = bitsf((uint32_t)(fs.key[keff - 1] >> 32));
-        const float tau = ri.tau;
-        const float e_tau = tau > -INF ? pesti_expf(fsub(scale ? fdiv(tau, T) : tau, m)) : 0.0f;
-        ok = fdiv(e_tau, S) < pk;
+        ok = fdiv(fs.p_tau, S) < pk;
       }
       if (ok) {
         // total over the kept list (sampling.rs:81), normalisation (:94), draw (:99-111)
@@ -1271,6 +1558,8 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
         }
       }
       if (lane == 0) sh.fast_ok = ok ? 1 : 0;
+    } else if (tid == 0 && fs.total > FAST_ENTS) {
+      sh.fast_ok = 0;
     }
     __syncthreads();
     if (sh.fast_ok) return;

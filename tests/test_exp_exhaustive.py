@@ -44,5 +44,4 @@ def test_approximate_exp_error_bound():
         out = subprocess.run([exe, "-104"], check=True, capture_output=True, text=True).stdout
     n, worst, over = out.split()
     assert int(n) == 1120927745
-    assert int(over) == 0, out
-    assert float(worst) < 2.0 ** -22  # measured 7.9e-8; the kernels assume 2^-20
+    assert int(over) == 0, out  # within PESTI_EXPF_APPROX_RELERR (2^-22) of the f32 exp everywhere

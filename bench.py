@@ -40,6 +40,10 @@ UNIT = "rows/s"
 L2_BYTES = 126 * 1024 * 1024
 
 
+# slice_stats_kernel, survivor_kernel, classify_kernel, row_kernel
+KERNELS_PER_STEP = 4
+
+
 def measured_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -373,7 +377,7 @@ def main():
             "step_hbm_gbs": step_bytes / (ms_per_step / 1e3) / 1e9,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": step_bytes + B * 4,
                     "d2h_bytes_per_step": B * 4},
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": KERNELS_PER_STEP * args.steps,
             "clocks": clk,
             "b1_latency_us": lat,
             "cpu_baseline": cpu,

@@ -37,9 +37,11 @@ constexpr int FAST_K = 256;       // top-k values handled by the fast path
 constexpr int CAND_CAP = 2048;    // candidates listed per row by the survivor kernel
 constexpr int FAST_CAND = 1024;   // candidates the fast path sorts
 constexpr int TAU_BINS = 4096;    // 12-bit histogram used to place the candidate threshold
-constexpr int NE = 96;            // fold entries per sub-slice
 constexpr int MAX_MATCH = 64;     // segments holding the row max re-scanned for its indices
 constexpr int QCAP = 512;         // survivor queue per warp (power of two)
+constexpr int GR = 8;             // survivors per lane in one classification task
+constexpr int GROUP = 32 * GR;    // survivors per classification task
+constexpr int POOL_CAP = 4096;    // fold entries per row (all its classification tasks)
 constexpr int STAGE = 256;        // values staged per round trip by warp_fold
 constexpr uint32_t TR_SAT = 0x40000000u;  // saturation of fold increments (>= any binade)
 
@@ -83,14 +85,27 @@ struct FoldEnt {      // one entry of a sub-slice's part of the softmax fold
 };
 
 struct SubSurv {      // survivor_kernel, one per sub-slice
-  int32_t count;      // survivors stored (raw logit, index) at the sub-slice's own start
-  int32_t nent;       // fold entries
-  int32_t replay;     // entries overflowed: replay all survivors one by one
+  int32_t count;      // survivors stored at the sub-slice's own start
+  int32_t ngroups;    // classification tasks of the sub-slice (fast-path rows)
+  int32_t pad;
   float pruned_max;   // largest raw logit dropped (-inf if none)
+};
+
+struct ClassTask {    // one group of GROUP survivors of a sub-slice
+  int32_t b;          // row
+  int32_t qj;         // sub-slice * jmax + group
+};
+
+struct GroupEnt {     // classify_kernel, one per task: its fold entries in the row's pool
+  int32_t off;        // first entry
+  int32_t nent;       // entries (0 with replay)
+  int32_t replay;     // the pool was full: the row kernel replays the sub-slice
+  int32_t pad;
 };
 
 struct SliceArgs {
   const void* logits;
+  int dtype;        // pesti_dtype of the logits
   long long B, V, ld;
   pesti_sampling_params uni;
   const pesti_sampling_params* per_row;
@@ -102,13 +117,22 @@ struct SliceArgs {
   RowInfo* info;    // [B]
   int* row_ctr;     // [B] blocks of the row finished (reset by the last one)
   SubSurv* surv;    // [B][P*K1_WARPS]
-  FoldEnt* ents;    // [B][P*K1_WARPS][NE]
   float* seg_max;   // [B][nseg]
   float* surv_raw;  // [B][V]: raw logits of the survivors of sub-slice s, compacted at its own start
+  float* surv_ea;   // the same array for fast-path rows: approximate exps of the survivors
   uint32_t* surv_idx;
+  int jmax;         // classification groups per sub-slice (ceil(SL / GROUP))
+  float* gsum;      // [B][P*K1_WARPS][jmax] approximate mass of each group
+  ClassTask* tasks; // [B*P*K1_WARPS*jmax]
+  int* task_count;  // tasks queued
+  int* task_next;   // tasks taken
+  GroupEnt* gsurv;  // [B][P*K1_WARPS][jmax]
+  FoldEnt* pool;    // [B][POOL_CAP] fold entries
+  int* pool_ctr;    // [B]
   int* cand_count;  // [B]
-  float* cand_e;    // [B][CAND_CAP]
+  float* cand_raw;  // [B][CAND_CAP] raw logits of the top-k candidates
   uint32_t* cand_idx;
+  int fast_enabled; // rows of the fast path keep no survivors (see survivor_kernel)
 };
 
 struct RowArgs {
@@ -121,11 +145,13 @@ struct RowArgs {
   long long SL;
   const RowInfo* info;
   const SubSurv* surv;
-  const FoldEnt* ents;
+  int jmax;
+  const GroupEnt* gsurv;
+  const FoldEnt* pool;
   const float* surv_raw;
   const uint32_t* surv_idx;
   const int* cand_count;
-  const float* cand_e;
+  const float* cand_raw;
   const uint32_t* cand_idx;
   float* E;       // [B][V] sequence built by the generic path
   uint32_t* I;
@@ -512,7 +538,14 @@ __global__ void __launch_bounds__(K1_NT) slice_stats_kernel(SliceArgs a) {
   const long long start = sub * a.SL;
   long long end = start + a.SL;
   if (end > a.V) end = a.V;
-  if (slice == 0 && w == 0 && lane == 0) a.cand_count[b] = 0;
+  if (slice == 0 && w == 0 && lane == 0) {
+    a.cand_count[b] = 0;
+    a.pool_ctr[b] = 0;
+    if (b == 0) {
+      *a.task_count = 0;
+      *a.task_next = 0;
+    }
+  }
   const TIn* row = (const TIn*)a.logits + b * a.ld;
   const pesti_sampling_params prm = row_params(a.uni, a.per_row, b);
   const float c2 = 1.4426950408889634f / (prm.temperature > 0.0f ? prm.temperature : 1.0f);
@@ -623,12 +656,10 @@ __global__ void __launch_bounds__(K1_NT) slice_stats_kernel(SliceArgs a) {
 // inside it at exit) and replays the run element by element when the check
 // fails, so the classification never decides a result.
 // ---------------------------------------------------------------------------
-constexpr int GR = 8;            // survivors per lane in one classification group (consecutive)
-constexpr int GROUP = 32 * GR;   // survivors per group
 constexpr uint32_t KEY_NONE = 0xfffffffeu;  // no open run
-static_assert(QCAP >= 2 * GROUP, "a chunk may add 256 survivors to a queue holding up to GROUP-1");
+static_assert(QCAP >= 32 + 256, "a chunk may add 256 survivors to a queue holding up to 31");
 
-// The open run of a sub-slice's fold while its survivors are classified: the
+// The open run of a group's fold while its survivors are classified: the
 // composed increments, how many survivors it covers, and its binade
 // (KEY_NONE when there is no open run).
 struct Seg {
@@ -651,8 +682,7 @@ __device__ __forceinline__ Seg seg_shfl(Seg s, int src) {
 
 struct SurvShared {
   float q_raw[K1_WARPS][QCAP];
-  FoldEnt ent[K1_WARPS][NE];
-  float ea[K1_WARPS][GROUP];  // approximate exps of the group being classified
+  uint32_t q_idx[K1_WARPS][QCAP];
 };
 
 template <typename TIn, int VE, int U, bool VEC>
@@ -672,14 +702,7 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
   const float NEG_INF = -__int_as_float(0x7f800000);
   SubSurv* so = a.surv + b * nsub + sub;
   if (is_greedy(prm) || ri.uniform) {
-    if (lane == 0) {
-      SubSurv z;
-      z.count = 0;
-      z.nent = 0;
-      z.replay = 0;
-      z.pruned_max = NEG_INF;
-      *so = z;
-    }
+    if (lane == 0) *so = SubSurv{0, 0, 0, NEG_INF};
     return;
   }
   const float m = ri.m;
@@ -701,219 +724,53 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
   const double L = pr.A * (1.0 - (double)V * 0x1p-24) * (1.0 - 0x1p-10) * exp2(-mag);
   const bool use_L = sum_pruning_ok(prm) && L >= 0x1p-60;
   const float thrL = use_L ? m + (float)log(L) - 17.36f : NEG_INF;
-  // e_exact lies within a relative 2*RELERR of the approximation (margin for
-  // the float arithmetic of the bounds below)
-  constexpr float DE = 2.0f * PESTI_EXPF_APPROX_RELERR;
   float run_max = pr.P;
   float pruned_max = NEG_INF;
   int* ccount = a.cand_count + b;
   float* qr = sh.q_raw[w];
-  FoldEnt* ent = sh.ent[w];
-  // queue and fold state (warp-uniform)
+  uint32_t* qi = sh.q_idx[w];
+  // Rows of the fast path store, per survivor, its approximate exp and index,
+  // and queue one classification task per GROUP survivors (with the group's
+  // approximate mass, so that any warp can classify any group).  Other rows
+  // (top-p, no filter, large top-k) store the raw logit and index for the
+  // generic path.
+  const bool fast = a.fast_enabled && fast_topk(prm, V);
+  float* gsum = a.gsum + (b * nsub + sub) * a.jmax;
   int qh = 0, qn = 0;
-  long long sins = 0;   // survivors stored so far
-  double s_approx = pr.A;
-  int nent = 0;
-  bool replay = false;
-  Seg run{0u, 0u, 0u, KEY_NONE};
+  long long sins = 0;  // survivors stored so far
+  double gacc = 0.0;   // approximate mass of the group being filled
+  int ngroups = 0;
 
-  // Classification of the n (<= GROUP) survivors at the queue head.  Lane l
-  // takes survivors [l*GR, l*GR + GR) of the group, so one warp scan gives every
-  // element its approximate running state and a segmented scan over the lanes
-  // joins the runs that cross lane boundaries.  The per-element loops are kept
-  // rolled (the approximate exps wait in shared memory between the passes):
-  // this kernel runs out of instruction cache long before it runs out of issue
-  // slots, so straight-line code is the expensive kind here.
-  float* eas = sh.ea[w];
-  // Guard band around binade edges for the classification.  The approximate
-  // state tracks the fold within about 1.2e-4 (its bias is the mass that the
-  // fold absorbs); a run predicted in the wrong binade fails its check in the
-  // row kernel and is replayed there, so the band trades entries for replays
-  // and never decides a result.
-  constexpr float BAND = 0x1p-12f;
-  // element i of the group: its run key (binade or SPECIAL) and increments
-  auto classify = [&](int i, float ea, float av, float bv, uint32_t& key, uint32_t& k0, uint32_t& k1) {
-    uint32_t lo = 0u;
-    bool special;
-    const float eu = ea * (1.0f + DE);  // upper bound of the exact value
-    if (av < 0x1p-126f) {
-      special = eu >= 0x1p-127f || bv > 0x1p-126f * (1.0f - BAND);
-    } else {
-      lo = fbits(av) & 0x7f800000u;
-      const float lov = bitsf(lo);
-      special = eu >= bitsf(lo - 0x00800000u) || av < lov * (1.0f + BAND) || bv > 2.0f * lov * (1.0f - BAND);
-    }
-    bool need_exact = special;
-    k0 = k1 = 0u;
-    if (!special) {
-      const uint32_t E = lo >> 23;  // w = 2^(E-150) (E = 0: the subnormal grid 2^-149)
-      const int sh2 = 150 - (int)(E == 0u ? 1u : E);
-      if (ea == 0.0f) {
-        need_exact = E < 40u;  // exact e < 4.5e-38: rounds to 0 on any grid >= 2^-110
-      } else {
-        const float tt = __uint_as_float(fbits(ea) + ((uint32_t)sh2 << 23));  // ea/w, exact scaling
-        const float kr = rintf(tt);
-        const float slack = 0.5f - fabsf(tt - kr);
-        if (slack <= tt * DE + 0x1p-24f) need_exact = true;
-        else k0 = k1 = (uint32_t)kr;
+  // the n (<= 32) survivors at the queue head, one per lane
+  auto drain = [&](int n) {
+    const bool valid = lane < n;
+    const int slot = (qh + lane) & (QCAP - 1);
+    const long long g = out_base + sins + lane;
+    if (fast) {
+      float e = 0.0f;
+      if (valid) {
+        const float raw = qr[slot];
+        e = pesti_expf_approx(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127 within 2^-22
+        a.surv_ea[g] = e;
+        a.surv_idx[g] = qi[slot];
       }
-    }
-    if (need_exact) {
-      const float raw = qr[(qh + i) & (QCAP - 1)];
-      const float ex = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127, exact
-      if (special) {
-        k0 = fbits(ex);
-      } else {
-        k0 = fbits(fadd(bitsf(lo), ex)) - lo;
-        k1 = fbits(fadd(bitsf(lo + 1u), ex)) - (lo + 1u);
+      gacc += (double)warp_reduce_add(e);
+      if (((sins + n) & (GROUP - 1)) == 0) {  // a full group (a partial last one closes below)
+        if (lane == 0) gsum[ngroups] = (float)gacc;
+        ++ngroups;
+        gacc = 0.0;
       }
+    } else if (valid) {
+      a.surv_raw[g] = qr[slot];
+      a.surv_idx[g] = qi[slot];
     }
-    key = special ? fold::SPECIAL : lo;
-  };
-  auto process_group = [&](int n) {
-    if (replay) {  // the row kernel replays this sub-slice from its stored survivors
-      qh = (qh + n) & (QCAP - 1);
-      qn -= n;
-      return;
-    }
-    const int i0 = lane * GR;
-    const int nl = n - i0 < 0 ? 0 : (n - i0 > GR ? GR : n - i0);  // valid elements of the lane
-    // pass A: approximate exps (sampling.rs:46,127 up to a relative 2^-22)
-    float ltot = 0.0f;
-#pragma unroll 1
-    for (int j = 0; j < nl; ++j) {
-      const float raw = qr[(qh + i0 + j) & (QCAP - 1)];
-      const float e = pesti_expf_approx(fsub(scale ? fdiv(raw, T) : raw, m));
-      eas[j * 32 + lane] = e;
-      ltot += e;
-    }
-    const float lincl = warp_incl_scan_add(ltot);
-    const float gtot = __shfl_sync(PESTI_FULL_MASK, lincl, 31);
-    // approximate states as floats relative to the carried double (the guard
-    // band is 2^-10; float rounding is 2^-24)
-    const float sb = (float)s_approx;
-    const float lbase = lincl - ltot;
-    // the key of the lane's last element decides whether the next lane's first
-    // element continues its run
-    uint32_t last_key = KEY_NONE;
-    if (nl > 0) {
-      const float el = eas[(nl - 1) * 32 + lane];
-      const float avl = sb + (lbase + (ltot - el));
-      uint32_t k0, k1;
-      classify(i0 + nl - 1, el, avl, sb + (lbase + ltot), last_key, k0, k1);
-    }
-    uint32_t prev_key = __shfl_up_sync(PESTI_FULL_MASK, last_key, 1);
-    if (lane == 0) prev_key = run.cnt > 0u ? run.key : KEY_NONE;
-    // pass B: lane summary; `lead` continues the run open before the lane,
-    // `trail` is the run open after it (hh: the lane starts at least one run)
-    bool hh = false;
-    Seg lead{0u, 0u, 0u, KEY_NONE}, trail{0u, 0u, 0u, KEY_NONE};
-    int n_int = 0;  // entries closed inside the lane after its first run start
-    {
-      uint32_t cur = prev_key;
-      float runf = lbase;
-#pragma unroll 1
-      for (int j = 0; j < nl; ++j) {
-        const float ea = eas[j * 32 + lane];
-        const float av = sb + runf;
-        runf += ea;
-        uint32_t k, k0, k1;
-        classify(i0 + j, ea, av, sb + runf, k, k0, k1);
-        const bool head = k == fold::SPECIAL || cur == fold::SPECIAL || cur == KEY_NONE || k != cur;
-        if (head) {
-          if (hh && trail.cnt > 0u) ++n_int;
-          hh = true;
-          if (k == fold::SPECIAL) {
-            ++n_int;
-            trail = Seg{0u, 0u, 0u, KEY_NONE};
-          } else {
-            trail = Seg{k0, k1, 1u, k};
-          }
-        } else if (!hh) {
-          const Tr t = tr_compose(Tr{lead.a0, lead.a1}, Tr{k0, k1});
-          lead = Seg{t.a0, t.a1, lead.cnt + 1u, KEY_NONE};
-        } else {
-          const Tr t = tr_compose(Tr{trail.a0, trail.a1}, Tr{k0, k1});
-          trail = Seg{t.a0, t.a1, trail.cnt + 1u, trail.key};
-        }
-        cur = k;
-      }
-    }
-    s_approx += (double)gtot;
-    // segmented inclusive scan over the lanes
-    Seg inc = hh ? trail : lead;
-    bool fl = hh;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const Seg o = seg_shfl_up(inc, off);
-      const bool of = __shfl_up_sync(PESTI_FULL_MASK, fl, off);
-      if (lane >= off) {
-        inc = seg_join(o, inc, fl);
-        fl = fl || of;
-      }
-    }
-    // the run open before the lane (the group's carried run joined in)
-    Seg xin = seg_shfl_up(inc, 1);
-    const bool xfl = __shfl_up_sync(PESTI_FULL_MASK, fl, 1);
-    xin = lane == 0 ? run : seg_join(run, xin, xfl);
-    const Seg last = seg_shfl(inc, 31);
-    const bool lastfl = __shfl_sync(PESTI_FULL_MASK, fl, 31);
-    // entries, in row order: the run closed by the lane's first start, then
-    // the ones closed inside the lane
-    const Seg first = seg_join(xin, lead, false);
-    const int ne = n_int + ((hh && first.cnt > 0u) ? 1 : 0);
-    const int neincl = warp_incl_scan_add(ne);
-    const int netot = __shfl_sync(PESTI_FULL_MASK, neincl, 31);
-    if (nent + netot > NE) {
-      replay = true;
-    } else if (netot > 0) {
-      int slot = nent + neincl - ne;
-      if (hh) {  // pass C: the same walk, writing the entries
-        uint32_t cur = prev_key;
-        bool started = false;
-        Seg tr{0u, 0u, 0u, KEY_NONE};
-        float runf = lbase;
-#pragma unroll 1
-        for (int j = 0; j < nl; ++j) {
-          const float ea = eas[j * 32 + lane];
-          const float av = sb + runf;
-          runf += ea;
-          uint32_t k, k0, k1;
-          classify(i0 + j, ea, av, sb + runf, k, k0, k1);
-          const bool head = k == fold::SPECIAL || cur == fold::SPECIAL || cur == KEY_NONE || k != cur;
-          if (head) {
-            if (!started) {
-              if (first.cnt > 0u) ent[slot++] = FoldEnt{first.key, first.a0, first.a1, first.cnt};
-              started = true;
-            } else if (tr.cnt > 0u) {
-              ent[slot++] = FoldEnt{tr.key, tr.a0, tr.a1, tr.cnt};
-            }
-            if (k == fold::SPECIAL) {
-              ent[slot++] = FoldEnt{fold::SPECIAL, k0, 0u, 1u};
-              tr = Seg{0u, 0u, 0u, KEY_NONE};
-            } else {
-              tr = Seg{k0, k1, 1u, k};
-            }
-          } else if (started) {
-            const Tr t = tr_compose(Tr{tr.a0, tr.a1}, Tr{k0, k1});
-            tr = Seg{t.a0, t.a1, tr.cnt + 1u, tr.key};
-          }
-          cur = k;
-        }
-      }
-      nent += netot;
-    }
+    sins += n;
     qh = (qh + n) & (QCAP - 1);
     qn -= n;
-    if (!replay) {
-      run = seg_join(run, last, lastfl);
-      if (run.cnt == 0u) run = Seg{0u, 0u, 0u, KEY_NONE};
-    }
   };
 
   // One loop over the sub-slice's 32*VE*U-element chunks, then one more pass
-  // that drains the queue; the element code and process_group each appear
-  // once (the kernel is sensitive to its code size).
+  // that drains the queue.
   const long long CH = 32LL * VE * U;
   for (long long pos = start;; pos += CH) {
     const bool more = pos < end;
@@ -976,24 +833,20 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
           ccnt += (valid && xv >= tau) ? 1 : 0;
         }
         run_max = fmaxf(run_max, fkey_inv(__reduce_max_sync(PESTI_FULL_MASK, fkey(lm))));
-        // survivors join the queue and the stored sequence in row order
+        // survivors join the queue in row order
         const int cinc = warp_incl_scan_add(cnt);
         const int wsum = __shfl_sync(PESTI_FULL_MASK, cinc, 31);
         int o = qh + qn + (cinc - cnt);
-        long long g = out_base + sins + (cinc - cnt);
 #pragma unroll
         for (int e = 0; e < VE; ++e) {
           if (sv[e]) {
             qr[o & (QCAP - 1)] = x[e];
-            a.surv_raw[g] = x[e];  // exact exp is recomputed from these where needed
-            a.surv_idx[g] = (uint32_t)(pos0 + e);
+            qi[o & (QCAP - 1)] = (uint32_t)(pos0 + e);
             ++o;
-            ++g;
           }
         }
         qn += wsum;
-        sins += wsum;
-        // top-k candidates: few per row, exact exp computed right here
+        // top-k candidates: few per row (their exact exps are taken by the row kernel)
         if (__any_sync(PESTI_FULL_MASK, ccnt > 0)) {
           const int cex0 = warp_incl_scan_add(ccnt);
           const int ctot = __shfl_sync(PESTI_FULL_MASK, cex0, 31);
@@ -1006,8 +859,7 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
             const float xv = x[e];
             if (e < nv && !is_nan(xv) && xv >= tau) {
               if (slot < CAND_CAP) {
-                const float xsc = scale ? fdiv(xv, T) : xv;
-                a.cand_e[b * CAND_CAP + slot] = pesti_expf_call(fsub(xsc, m));
+                a.cand_raw[b * CAND_CAP + slot] = xv;
                 a.cand_idx[b * CAND_CAP + slot] = (uint32_t)(pos0 + e);
               }
               ++slot;
@@ -1017,33 +869,257 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
       }
     }
     __syncwarp();
-    const int need = more ? GROUP : 1;
+    const int need = more ? 32 : 1;
     while (qn >= need) {
-      process_group(qn < GROUP ? qn : GROUP);
+      drain(qn < 32 ? qn : 32);
       __syncwarp();
     }
     if (!more) break;
   }
-  if (!replay && run.cnt > 0u) {
-    if (nent < NE) {
-      if (lane == 0) ent[nent] = FoldEnt{run.key, run.a0, run.a1, run.cnt};
-      ++nent;
-    } else {
-      replay = true;
-    }
+  if (fast && sins > (long long)ngroups * GROUP) {  // the partial last group
+    if (lane == 0) gsum[ngroups] = (float)gacc;
+    ++ngroups;
   }
-  __syncwarp();
   const float pm = warp_reduce_fmax(pruned_max);
-  FoldEnt* gent = a.ents + (b * nsub + sub) * NE;
-  const int nout = replay ? 0 : nent;
-  for (int i = lane; i < nout; i += 32) gent[i] = ent[i];
-  if (lane == 0) {
-    SubSurv z;
-    z.count = (int32_t)sins;
-    z.nent = nout;
-    z.replay = replay ? 1 : 0;
-    z.pruned_max = pm;
-    *so = z;
+  if (fast && ngroups > 0 && lane == 0) {
+    const int t0 = atomicAdd(a.task_count, ngroups);
+    for (int j = 0; j < ngroups; ++j) a.tasks[t0 + j] = ClassTask{(int)b, (int)(sub * a.jmax + j)};
+  }
+  if (lane == 0) *so = SubSurv{(int32_t)sins, ngroups, 0, pm};
+}
+
+// ---------------------------------------------------------------------------
+// Classification of survivor groups into fold entries (rows of the fast path).
+//
+// Each task is GROUP consecutive survivors of one sub-slice.  Its approximate
+// starting state is the sub-slice's prefix mass A plus the masses of the
+// sub-slice's earlier groups, so the tasks are independent and a persistent
+// grid of warps takes them from a counter; the heavy start of every row (where
+// the running sum is still small and most elements survive) is spread over
+// many warps.  Lane l takes survivors [l*g, l*g + g), g = ceil(n/32): one warp
+// scan gives every element its approximate running state and a segmented scan
+// over the lanes joins the runs that cross lane boundaries.  The per-element
+// loops are kept rolled (the values wait in shared memory between the
+// passes): this code runs out of instruction cache long before it runs out of
+// issue slots.
+// ---------------------------------------------------------------------------
+struct ClassShared {
+  float ea[K1_WARPS][GROUP];
+  uint32_t ck[K1_WARPS][GROUP];
+  uint32_t c0[K1_WARPS][GROUP];
+  uint32_t c1[K1_WARPS][GROUP];
+};
+
+__global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
+  __shared__ ClassShared sh;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int nsub = a.P * K1_WARPS;
+  const long long V = a.V;
+  const int ntasks = *a.task_count;
+  float* eas = sh.ea[w];
+  uint32_t* cks = sh.ck[w];
+  uint32_t* c0s = sh.c0[w];
+  uint32_t* c1s = sh.c1[w];
+  // e_exact lies within a relative 2*RELERR of the approximation (margin for
+  // the float arithmetic of the bounds below)
+  constexpr float DE = 2.0f * PESTI_EXPF_APPROX_RELERR;
+  // Guard band around binade edges.  The approximate state tracks the fold
+  // within about 1.2e-4 (its bias is the mass that the fold absorbs); a run
+  // predicted in the wrong binade fails its check in the row kernel and is
+  // replayed there, so the band trades entries for replays and never decides
+  // a result.
+  constexpr float BAND = 0x1p-12f;
+  for (;;) {
+    int t = 0;
+    if (lane == 0) t = atomicAdd(a.task_next, 1);
+    t = __shfl_sync(PESTI_FULL_MASK, t, 0);
+    if (t >= ntasks) break;
+    const ClassTask tk = a.tasks[t];
+    const long long b = tk.b;
+    const long long sub = tk.qj / a.jmax;
+    const int j = tk.qj - (int)sub * a.jmax;
+    const pesti_sampling_params prm = row_params(a.uni, a.per_row, b);
+    const RowInfo ri = a.info[b];
+    const float T = prm.temperature;
+    const bool scale = T > 0.0f;
+    const float m = ri.m;
+    const SubSurv ssv = a.surv[b * nsub + sub];
+    const long long gbase = b * V + sub * a.SL + (long long)j * GROUP;  // first survivor of the group
+    const int n = ssv.count - j * GROUP < GROUP ? ssv.count - j * GROUP : GROUP;
+    const float* gsum = a.gsum + (b * nsub + sub) * a.jmax;
+    double s_approx = a.pre[b * nsub + sub].A;
+    for (int jj = 0; jj < j; ++jj) s_approx += (double)gsum[jj];
+    const void* row = a.dtype == PESTI_BF16 ? (const void*)((const uint16_t*)a.logits + b * a.ld)
+                                            : (const void*)((const float*)a.logits + b * a.ld);
+
+    // element i of the group: its run key (binade or SPECIAL) and increments
+    auto classify = [&](int i, float ea, float av, float bv, uint32_t& key, uint32_t& k0, uint32_t& k1) {
+      uint32_t lo = 0u;
+      bool special;
+      const float eu = ea * (1.0f + DE);  // upper bound of the exact value
+      if (av < 0x1p-126f) {
+        special = eu >= 0x1p-127f || bv > 0x1p-126f * (1.0f - BAND);
+      } else {
+        lo = fbits(av) & 0x7f800000u;
+        const float lov = bitsf(lo);
+        special = eu >= bitsf(lo - 0x00800000u) || av < lov * (1.0f + BAND) || bv > 2.0f * lov * (1.0f - BAND);
+      }
+      bool need_exact = special;
+      k0 = k1 = 0u;
+      if (!special) {
+        const uint32_t E = lo >> 23;  // w = 2^(E-150) (E = 0: the subnormal grid 2^-149)
+        const int sh2 = 150 - (int)(E == 0u ? 1u : E);
+        if (ea == 0.0f) {
+          need_exact = E < 40u;  // exact e < 4.5e-38: rounds to 0 on any grid >= 2^-110
+        } else {
+          const float tt = __uint_as_float(fbits(ea) + ((uint32_t)sh2 << 23));  // ea/w, exact scaling
+          const float kr = rintf(tt);
+          const float slack = 0.5f - fabsf(tt - kr);
+          if (slack <= tt * DE + 0x1p-24f) need_exact = true;
+          else k0 = k1 = (uint32_t)kr;
+        }
+      }
+      if (need_exact) {
+        const float raw = load_logit_dyn(row, a.dtype, (long long)a.surv_idx[gbase + i]);
+        const float ex = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127, exact
+        if (special) {
+          k0 = fbits(ex);
+        } else {
+          k0 = fbits(fadd(bitsf(lo), ex)) - lo;
+          k1 = fbits(fadd(bitsf(lo + 1u), ex)) - (lo + 1u);
+        }
+      }
+      key = special ? fold::SPECIAL : lo;
+    };
+
+    const int g = (n + 31) >> 5;  // elements per lane: the group's fill decides the loop length
+    const int i0 = lane * g;
+    const int nl = n - i0 < 0 ? 0 : (n - i0 > g ? g : n - i0);  // valid elements of the lane
+    __syncwarp();
+    float ltot = 0.0f;
+#pragma unroll 1
+    for (int jj = 0; jj < nl; ++jj) {
+      const float e = a.surv_ea[gbase + i0 + jj];
+      eas[jj * 32 + lane] = e;
+      ltot += e;
+    }
+    const float lincl = warp_incl_scan_add(ltot);
+    // approximate states as floats relative to the carried double (the guard
+    // band is 2^-12; float rounding is 2^-24)
+    const float sb = (float)s_approx;
+    const float lbase = lincl - ltot;
+    // the key of the lane's last element decides whether the next lane's first
+    // element continues its run
+    uint32_t last_key = KEY_NONE;
+    if (nl > 0) {
+      const float el = eas[(nl - 1) * 32 + lane];
+      uint32_t k0, k1;
+      classify(i0 + nl - 1, el, sb + (lbase + (ltot - el)), sb + (lbase + ltot), last_key, k0, k1);
+    }
+    uint32_t prev_key = __shfl_up_sync(PESTI_FULL_MASK, last_key, 1);
+    if (lane == 0) prev_key = KEY_NONE;
+    // pass B: lane summary; `lead` continues the run open before the lane,
+    // `trail` is the run open after it (hh: the lane starts at least one run)
+    bool hh = false;
+    Seg lead{0u, 0u, 0u, KEY_NONE}, trail{0u, 0u, 0u, KEY_NONE};
+    int n_int = 0;  // entries closed inside the lane after its first run start
+    {
+      uint32_t cur = prev_key;
+      float runf = lbase;
+#pragma unroll 1
+      for (int jj = 0; jj < nl; ++jj) {
+        const float ea = eas[jj * 32 + lane];
+        const float av = sb + runf;
+        runf += ea;
+        uint32_t k, k0, k1;
+        classify(i0 + jj, ea, av, sb + runf, k, k0, k1);
+        cks[jj * 32 + lane] = k;
+        c0s[jj * 32 + lane] = k0;
+        c1s[jj * 32 + lane] = k1;
+        const bool head = k == fold::SPECIAL || cur == fold::SPECIAL || cur == KEY_NONE || k != cur;
+        if (head) {
+          if (hh && trail.cnt > 0u) ++n_int;
+          hh = true;
+          if (k == fold::SPECIAL) {
+            ++n_int;
+            trail = Seg{0u, 0u, 0u, KEY_NONE};
+          } else {
+            trail = Seg{k0, k1, 1u, k};
+          }
+        } else if (!hh) {
+          const Tr tt = tr_compose(Tr{lead.a0, lead.a1}, Tr{k0, k1});
+          lead = Seg{tt.a0, tt.a1, lead.cnt + 1u, KEY_NONE};
+        } else {
+          const Tr tt = tr_compose(Tr{trail.a0, trail.a1}, Tr{k0, k1});
+          trail = Seg{tt.a0, tt.a1, trail.cnt + 1u, trail.key};
+        }
+        cur = k;
+      }
+    }
+    // segmented inclusive scan over the lanes
+    Seg inc = hh ? trail : lead;
+    bool fl = hh;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const Seg o = seg_shfl_up(inc, off);
+      const bool of = __shfl_up_sync(PESTI_FULL_MASK, fl, off);
+      if (lane >= off) {
+        inc = seg_join(o, inc, fl);
+        fl = fl || of;
+      }
+    }
+    // the run open before the lane
+    const Seg none{0u, 0u, 0u, KEY_NONE};
+    Seg xin = seg_shfl_up(inc, 1);
+    const bool xfl = __shfl_up_sync(PESTI_FULL_MASK, fl, 1);
+    xin = lane == 0 ? none : seg_join(none, xin, xfl);
+    const Seg last = seg_shfl(inc, 31);
+    // entries, in row order: the run closed by the lane's first start, then
+    // the ones closed inside the lane; the run still open at the group's end
+    // closes it
+    const Seg first = seg_join(xin, lead, false);
+    const int ne = n_int + ((hh && first.cnt > 0u) ? 1 : 0);
+    const int neincl = warp_incl_scan_add(ne);
+    const int nclosed = __shfl_sync(PESTI_FULL_MASK, neincl, 31);
+    const int netot = nclosed + (last.cnt > 0u ? 1 : 0);
+    int off0 = 0;
+    if (lane == 0) off0 = atomicAdd(a.pool_ctr + b, netot);
+    off0 = __shfl_sync(PESTI_FULL_MASK, off0, 0);
+    const bool replay = off0 + netot > POOL_CAP;
+    if (!replay) {
+      FoldEnt* ent = a.pool + b * POOL_CAP + off0;
+      int slot = neincl - ne;
+      if (hh) {  // pass C: the same walk, writing the entries
+        uint32_t cur = prev_key;
+        bool started = false;
+        Seg tr{0u, 0u, 0u, KEY_NONE};
+#pragma unroll 1
+        for (int jj = 0; jj < nl; ++jj) {
+          const uint32_t k = cks[jj * 32 + lane], k0 = c0s[jj * 32 + lane], k1 = c1s[jj * 32 + lane];
+          const bool head = k == fold::SPECIAL || cur == fold::SPECIAL || cur == KEY_NONE || k != cur;
+          if (head) {
+            if (!started) {
+              if (first.cnt > 0u) ent[slot++] = FoldEnt{first.key, first.a0, first.a1, first.cnt};
+              started = true;
+            } else if (tr.cnt > 0u) {
+              ent[slot++] = FoldEnt{tr.key, tr.a0, tr.a1, tr.cnt};
+            }
+            if (k == fold::SPECIAL) {
+              ent[slot++] = FoldEnt{fold::SPECIAL, k0, 0u, 1u};
+              tr = Seg{0u, 0u, 0u, KEY_NONE};
+            } else {
+              tr = Seg{k0, k1, 1u, k};
+            }
+          } else if (started) {
+            const Tr tt = tr_compose(Tr{tr.a0, tr.a1}, Tr{k0, k1});
+            tr = Seg{tt.a0, tt.a1, tr.cnt + 1u, tr.key};
+          }
+          cur = k;
+        }
+      }
+      if (lane == 0 && last.cnt > 0u) ent[nclosed] = FoldEnt{last.key, last.a0, last.a1, last.cnt};
+    }
+    if (lane == 0) a.gsurv[(b * nsub + sub) * a.jmax + j] = GroupEnt{off0, replay ? 0 : netot, replay ? 1 : 0, 0};
   }
 }
 
@@ -1089,7 +1165,6 @@ struct FastSmem {
   float q[FAST_CAND];
   float stage[STAGE];
   FoldEnt ent[FAST_ENTS];      // the row's entries, sub-slice after sub-slice
-  uint32_t epos[FAST_ENTS];    // first survivor of each entry within its sub-slice
   uint16_t esub[FAST_ENTS];    // sub-slice of each entry
   int total;                   // entries of the row (> FAST_ENTS: not staged)
   float p_tau;                 // exp of the candidate threshold (scaled, minus m)
@@ -1264,19 +1339,19 @@ __device__ void warp_sort_keys(unsigned long long* key, int n) {
   __syncwarp();
 }
 
-// Fold of the exps of n survivors (their raw logits in global memory) by one
+// Fold of the exps of n raw logits (f32 or bf16, in global memory) by one
 // warp, starting from state s (bits).  The exact exps are staged STAGE at a
 // time in shared memory; each step takes 32 of them with a transducer scan
 // over the lanes, adds the first one that would leave the binade (or is large
 // next to s) directly, and resumes after it.  All 32 lanes must call it.
-__device__ uint32_t warp_fold(const float* raw, long long n, uint32_t s, float* stage, bool scale, float T,
-                              float m) {
+__device__ uint32_t warp_fold(const void* raw, int dtype, long long n, uint32_t s, float* stage, bool scale,
+                              float T, float m) {
   const int lane = threadIdx.x & 31;
   for (long long base = 0; base < n; base += STAGE) {
     const int len = (int)(n - base < STAGE ? n - base : STAGE);
     __syncwarp();
     for (int i = lane; i < len; i += 32) {
-      const float xr = raw[base + i];
+      const float xr = load_logit_dyn(raw, dtype, base + i);
       stage[i] = pesti_expf_call(fsub(scale ? fdiv(xr, T) : xr, m));  // sampling.rs:46,127
     }
     __syncwarp();
@@ -1414,12 +1489,22 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
     // sub-slice whose entries overflowed stages one marker to replay it
     const long long keff = k < V ? k : V;
     {
-      const FoldEnt* gent = a.ents + b * nsub * NE;
+      const GroupEnt* gs = a.gsurv + b * nsub * a.jmax;
+      const FoldEnt* pool = a.pool + b * POOL_CAP;
       int ne = 0;
       if (tid < nsub) {
         const SubSurv sv = survs[tid];
         ss[tid] = sv;
-        ne = sv.count <= 0 ? 0 : (sv.replay ? 1 : sv.nent);
+        if (sv.count > 0) {
+          bool rep = false;
+          for (int j = 0; j < sv.ngroups; ++j) {
+            const GroupEnt ge = gs[tid * a.jmax + j];
+            ne += ge.nent;
+            rep |= ge.replay != 0;
+          }
+          if (rep) ne = 1;
+          ss[tid].pad = rep ? 1 : 0;
+        }
       }
       int tot;
       const int ex = block_excl_scan_add(ne, sh.iscr, tot);
@@ -1430,27 +1515,21 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
         for (int q = wid; q < nsub; q += K2_NT / 32) {
           const SubSurv sv = ss[q];
           if (sv.count <= 0) continue;
-          const int e0 = eoff[q];
-          if (sv.replay) {
+          int e0 = eoff[q];
+          if (sv.pad) {  // a group of the sub-slice overflowed the pool: replay it whole
             if (lane == 0) {
               fs.ent[e0] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)sv.count};
-              fs.epos[e0] = 0u;
               fs.esub[e0] = (uint16_t)q;
             }
             continue;
           }
-          uint32_t base = 0u;
-          for (int i0 = 0; i0 < sv.nent; i0 += 32) {
-            const int i = i0 + lane;
-            FoldEnt en{0u, 0u, 0u, 0u};
-            if (i < sv.nent) en = gent[q * NE + i];
-            const uint32_t inc = warp_incl_scan_add(en.count);
-            if (i < sv.nent) {
-              fs.ent[e0 + i] = en;
-              fs.epos[e0 + i] = base + inc - en.count;
+          for (int j = 0; j < sv.ngroups; ++j) {
+            const GroupEnt ge = gs[q * a.jmax + j];
+            for (int i = lane; i < ge.nent; i += 32) {
+              fs.ent[e0 + i] = pool[ge.off + i];
               fs.esub[e0 + i] = (uint16_t)q;
             }
-            base += __shfl_sync(PESTI_FULL_MASK, inc, 31);
+            e0 += ge.nent;
           }
         }
       }
@@ -1461,9 +1540,11 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
     if (wid == 1 && fs.total <= FAST_ENTS && cand_ok) {
       // candidates by (e desc, index asc) while warp 0 folds; the order by p
       // = e/S differs only inside groups of equal p (fixed up below)
-      for (int j = lane; j < C; j += 32)
-        fs.key[j] = ((unsigned long long)fbits(a.cand_e[b * CAND_CAP + j]) << 32) |
-                    (unsigned long long)(~a.cand_idx[b * CAND_CAP + j]);
+      for (int j = lane; j < C; j += 32) {
+        const float xr = a.cand_raw[b * CAND_CAP + j];
+        const float e = pesti_expf(fsub(scale ? fdiv(xr, T) : xr, m));  // sampling.rs:46,127
+        fs.key[j] = ((unsigned long long)fbits(e) << 32) | (unsigned long long)(~a.cand_idx[b * CAND_CAP + j]);
+      }
       __syncwarp();
       if (C <= 32) warp_sort_keys<1>(fs.key, C);
       else if (C <= 64) warp_sort_keys<2>(fs.key, C);
@@ -1484,11 +1565,21 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
       // softmax denominator (sampling.rs:128): walk the entries with the exact
       // state; a run the state does not fit (or a replay marker) is folded
       // from its survivors
+      // On a failure the whole sub-slice is folded again from its raw logits,
+      // starting from the state it was entered with (dropped elements are
+      // exact no-ops, so folding all of them gives the same state).
       const int total = fs.total;
       int i = 0;
+      int cur_q = -1;
+      uint32_t s_q = 0u;  // state at the start of sub-slice cur_q
       while (i < total) {
         for (; i < total; ++i) {
           const FoldEnt en = fs.ent[i];
+          const int q = fs.esub[i];
+          if (q != cur_q) {
+            cur_q = q;
+            s_q = s;
+          }
           if (en.lo == fold::SPECIAL) {
             s = fbits(fadd(bitsf(s), bitsf(en.a0)));
             continue;
@@ -1499,9 +1590,12 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
           s = (uint32_t)ns;
         }
         if (i >= total) break;
-        const float* vals = a.surv_raw + b * V + (long long)fs.esub[i] * a.SL + fs.epos[i];
-        s = warp_fold(vals, fs.ent[i].count, s, fs.stage, scale, T, m);
-        ++i;
+        const long long st = (long long)cur_q * a.SL;
+        const long long len = V - st < a.SL ? V - st : a.SL;
+        const void* sub_row = a.dtype == PESTI_BF16 ? (const void*)((const uint16_t*)row + st)
+                                                    : (const void*)((const float*)row + st);
+        s = warp_fold(sub_row, a.dtype, len, s_q, fs.stage, scale, T, m);
+        i = cur_q + 1 < nsub ? eoff[cur_q + 1] : total;  // the next sub-slice's entries
       }
     }
     __syncthreads();
@@ -1574,7 +1668,8 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
   const float e_pruned = pm > -INF ? pesti_expf(fsub(scale ? fdiv(pm, T) : pm, m)) : 0.0f;
 
   // ---------------- generic path ----------------
-  bool dense_all = false;
+  // rows of the fast path have no survivor list: all their elements
+  bool dense_all = a.fast_enabled && fast_topk(prm, V);
   for (int attempt = 0; attempt < 2; ++attempt) {
     for (int s = tid; s < nsub; s += K2_NT) {
       const long long st = (long long)s * a.SL;

@@ -135,9 +135,11 @@ int ensure_row_smem_limit(int device) {
 // one workspace, each region 256-byte aligned.
 struct Plan {
   Geometry g;
-  long long nsub, nseg;
+  int num_sms;
+  long long nsub, nseg, jmax;
   bool sorted_bufs;
-  size_t o_ctr, o_stats, o_pre, o_info, o_surv, o_ents, o_segmax, o_se, o_si, o_cc, o_ce, o_ci;
+  size_t o_ctr, o_stats, o_pre, o_info, o_surv, o_segmax, o_se, o_si, o_cc, o_ce, o_ci;
+  size_t o_gsum, o_gsurv, o_tasks, o_tctr, o_pctr, o_pool;
   size_t o_E, o_I, o_status;
   size_t o_sk0 = 0, o_sv0 = 0, o_sk1 = 0, o_sv1 = 0, o_q = 0;
   size_t bytes;  // workspace the call needs
@@ -148,8 +150,11 @@ Plan make_plan(int num_sms, pesti_dtype dtype, long long B, long long V, bool so
   const int ve = 16 / esize;
   Plan p;
   p.g = pick_geometry(num_sms, B, V > 0 ? V : 1, ve);
+  p.num_sms = num_sms;
   p.nsub = (long long)p.g.P * pesti::K1_WARPS;
   p.nseg = (std::max(1LL, V) + 32LL * ve - 1) / (32LL * ve);
+  p.jmax = (p.g.SL + pesti::GROUP - 1) / pesti::GROUP;
+  const size_t ngrp = (size_t)B * p.nsub * p.jmax;
   p.sorted_bufs = sorted_bufs;
   const size_t bv = (size_t)B * (size_t)std::max(1LL, V);
   size_t off = 0;
@@ -163,7 +168,6 @@ Plan make_plan(int num_sms, pesti_dtype dtype, long long B, long long V, bool so
   p.o_pre = take((size_t)B * p.nsub * sizeof(pesti::SubPre));
   p.o_info = take((size_t)B * sizeof(pesti::RowInfo));
   p.o_surv = take((size_t)B * p.nsub * sizeof(pesti::SubSurv));
-  p.o_ents = take((size_t)B * p.nsub * pesti::NE * sizeof(pesti::FoldEnt));
   p.o_segmax = take((size_t)B * p.nseg * 4);
   p.o_se = take(bv * 4);
   p.o_si = take(bv * 4);
@@ -173,6 +177,12 @@ Plan make_plan(int num_sms, pesti_dtype dtype, long long B, long long V, bool so
   p.o_E = take(bv * 4);
   p.o_I = take(bv * 4);
   p.o_status = take(16);
+  p.o_gsum = take(ngrp * sizeof(float));
+  p.o_gsurv = take(ngrp * sizeof(pesti::GroupEnt));
+  p.o_tasks = take(ngrp * sizeof(pesti::ClassTask));
+  p.o_tctr = take(2 * sizeof(int));
+  p.o_pctr = take((size_t)B * sizeof(int));
+  p.o_pool = take((size_t)B * pesti::POOL_CAP * sizeof(pesti::FoldEnt));
   if (sorted_bufs) {
     p.o_sk0 = take(bv * 4);
     p.o_sv0 = take(bv * 4);
@@ -196,6 +206,7 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
 
   pesti::SliceArgs sa;
   sa.logits = d_logits;
+  sa.dtype = (int)dtype;
   sa.B = B;
   sa.V = V;
   sa.ld = ld;
@@ -209,13 +220,26 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
   sa.info = (pesti::RowInfo*)(ws + p.o_info);
   sa.row_ctr = (int*)(ws + p.o_ctr);
   sa.surv = (pesti::SubSurv*)(ws + p.o_surv);
-  sa.ents = (pesti::FoldEnt*)(ws + p.o_ents);
   sa.seg_max = (float*)(ws + p.o_segmax);
   sa.surv_raw = (float*)(ws + p.o_se);
+  sa.surv_ea = sa.surv_raw;  // fast-path rows store approximate exps there instead
   sa.surv_idx = (uint32_t*)(ws + p.o_si);
+  sa.jmax = (int)p.jmax;
+  sa.gsum = (float*)(ws + p.o_gsum);
+  sa.tasks = (pesti::ClassTask*)(ws + p.o_tasks);
+  sa.task_count = (int*)(ws + p.o_tctr);
+  sa.task_next = sa.task_count + 1;
+  sa.gsurv = (pesti::GroupEnt*)(ws + p.o_gsurv);
+  sa.pool = (pesti::FoldEnt*)(ws + p.o_pool);
+  sa.pool_ctr = (int*)(ws + p.o_pctr);
   sa.cand_count = (int*)(ws + p.o_cc);
-  sa.cand_e = (float*)(ws + p.o_ce);
+  sa.cand_raw = (float*)(ws + p.o_ce);
   sa.cand_idx = (uint32_t*)(ws + p.o_ci);
+
+  // the fast path stages the row's fold entries in shared memory; with very
+  // many sub-slices it does not fit and all rows take the generic path
+  const size_t fast_bytes = pesti::fast_smem_bytes((int)p.nsub);
+  sa.fast_enabled = sizeof(pesti::RowShared) + fast_bytes <= kRowSmemLimit ? 1 : 0;
 
   if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[0], st), "cudaEventRecord(profile)");
   const bool aligned = ((uintptr_t)d_logits % 16 == 0) && ((ld * esize) % 16 == 0);
@@ -240,6 +264,14 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "survivor_kernel launch");
+  // classification tasks: a persistent grid takes them from a counter
+  {
+    const long long most = (long long)B * p.nsub * p.jmax;
+    const long long blocks = std::min<long long>(4LL * p.num_sms, (most + pesti::K1_WARPS - 1) / pesti::K1_WARPS);
+    pesti::classify_kernel<<<(unsigned)std::max(1LL, blocks), pesti::K1_NT, 0, st>>>(sa);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "classify_kernel launch");
+  }
   if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[2], st), "cudaEventRecord(profile)");
 
   pesti::RowArgs ra;
@@ -254,11 +286,13 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
   ra.SL = p.g.SL;
   ra.info = sa.info;
   ra.surv = sa.surv;
-  ra.ents = sa.ents;
+  ra.jmax = sa.jmax;
+  ra.gsurv = sa.gsurv;
+  ra.pool = sa.pool;
   ra.surv_raw = sa.surv_raw;
   ra.surv_idx = sa.surv_idx;
   ra.cand_count = sa.cand_count;
-  ra.cand_e = sa.cand_e;
+  ra.cand_raw = sa.cand_raw;
   ra.cand_idx = sa.cand_idx;
   ra.E = (float*)(ws + p.o_E);
   ra.I = (uint32_t*)(ws + p.o_I);
@@ -274,10 +308,7 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
   ra.kept_width = (d_kept_p || d_kept_idx) ? kept_width : 0;
   ra.kept_count = d_kept_count;
   ra.status = (int*)(ws + p.o_status);
-  // the fast path stages every fold entry of the row in shared memory; with
-  // very many sub-slices it does not fit and all rows take the generic path
-  const size_t fast_bytes = pesti::fast_smem_bytes((int)p.nsub);
-  ra.fast_enabled = sizeof(pesti::RowShared) + fast_bytes <= kRowSmemLimit ? 1 : 0;
+  ra.fast_enabled = sa.fast_enabled;
   const size_t smem2 = sizeof(pesti::RowShared) + (ra.fast_enabled ? fast_bytes : 0);
   if (smem2 > 48 * 1024) {
     int rc = ensure_row_smem_limit(device);

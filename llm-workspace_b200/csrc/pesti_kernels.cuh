@@ -119,7 +119,6 @@ struct SliceArgs {
   SubSurv* surv;    // [B][P*K1_WARPS]
   float* seg_max;   // [B][nseg]
   float* surv_raw;  // [B][V]: raw logits of the survivors of sub-slice s, compacted at its own start
-  float* surv_ea;   // the same array for fast-path rows: approximate exps of the survivors
   uint32_t* surv_idx;
   int jmax;         // classification groups per sub-slice (ceil(SL / GROUP))
   float* gsum;      // [B][P*K1_WARPS][jmax] approximate mass of each group
@@ -223,6 +222,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+
+// Programmatic dependent launch: a kernel lets the next one in the stream be
+// scheduled early (launch_dependents) and the next one waits for the
+// previous grid's completion and memory (wait) before it touches its inputs.
+// Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch_next() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 // Out-of-line copy of the exact exp for the kernels whose code size matters.
 __device__ __noinline__ float pesti_expf_call(float x) { return pesti_expf(x); }
@@ -531,6 +537,7 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
 template <typename TIn, int VE, int U, bool VEC>
 __global__ void __launch_bounds__(K1_NT) slice_stats_kernel(SliceArgs a) {
   __shared__ StatsShared sh;
+  grid_dep_launch_next();
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const long long b = blockIdx.x / a.P;
   const int slice = (int)(blockIdx.x % a.P);
@@ -688,6 +695,8 @@ struct SurvShared {
 template <typename TIn, int VE, int U, bool VEC>
 __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
   __shared__ SurvShared sh;
+  grid_dep_launch_next();
+  grid_dep_wait();
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const long long b = blockIdx.x / a.P;
   const int slice = (int)(blockIdx.x % a.P);
@@ -723,17 +732,29 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
   const double mag = 0x1p-20 * ((double)fabsf(ym) + 64.0);
   const double L = pr.A * (1.0 - (double)V * 0x1p-24) * (1.0 - 0x1p-10) * exp2(-mag);
   const bool use_L = sum_pruning_ok(prm) && L >= 0x1p-60;
-  const float thrL = use_L ? m + (float)log(L) - 17.36f : NEG_INF;
+  // (b) in raw units: with t = m + ln(L) - 17.36 and eta = 2^-20 (|t| + |m| + 1),
+  // x < (t - eta) T implies fl(fl(x/T) - m) < t - m - eta/2 (the roundings of
+  // x/T and of the difference are below eta/8), so the exact exp is below
+  // e^-17.36 L (1 + 2^-24) < 0.99 * 2^-25 L.  Rounded toward -inf as a float.
+  float thrLr = NEG_INF;
+  if (use_L) {
+    const double tL = (double)m + log(L) - 17.36;
+    const double eta = 0x1p-20 * (fabs(tL) + fabs((double)m) + 1.0);
+    thrLr = __double2float_rd((tL - eta) * (double)t_eff);
+  }
+  // group masses for the classification tasks: exp(x/T - m) = 2^(x c2 - m log2 e)
+  const float c2 = 1.4426950408889634f / t_eff;
+  const float mc = m * 1.4426950408889634f;
   float run_max = pr.P;
   float pruned_max = NEG_INF;
   int* ccount = a.cand_count + b;
   float* qr = sh.q_raw[w];
   uint32_t* qi = sh.q_idx[w];
-  // Rows of the fast path store, per survivor, its approximate exp and index,
-  // and queue one classification task per GROUP survivors (with the group's
-  // approximate mass, so that any warp can classify any group).  Other rows
-  // (top-p, no filter, large top-k) store the raw logit and index for the
-  // generic path.
+  // Every survivor is stored (raw logit and index) at the sub-slice's start.
+  // Rows of the fast path also queue one classification task per GROUP
+  // survivors, with the group's approximate mass, so that any warp can
+  // classify any group; the largest dropped logit is kept for the other rows
+  // (top-p, no filter, large top-k), whose generic path bounds with it.
   const bool fast = a.fast_enabled && fast_topk(prm, V);
   float* gsum = a.gsum + (b * nsub + sub) * a.jmax;
   int qh = 0, qn = 0;
@@ -745,24 +766,21 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
   auto drain = [&](int n) {
     const bool valid = lane < n;
     const int slot = (qh + lane) & (QCAP - 1);
-    const long long g = out_base + sins + lane;
+    float e2 = 0.0f;
+    if (valid) {
+      const float raw = qr[slot];
+      const long long g = out_base + sins + lane;
+      a.surv_raw[g] = raw;
+      a.surv_idx[g] = qi[slot];
+      e2 = ex2_approx(fmaf(raw, c2, -mc));
+    }
     if (fast) {
-      float e = 0.0f;
-      if (valid) {
-        const float raw = qr[slot];
-        e = pesti_expf_approx(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127 within 2^-22
-        a.surv_ea[g] = e;
-        a.surv_idx[g] = qi[slot];
-      }
-      gacc += (double)warp_reduce_add(e);
+      gacc += (double)warp_reduce_add(e2);
       if (((sins + n) & (GROUP - 1)) == 0) {  // a full group (a partial last one closes below)
         if (lane == 0) gsum[ngroups] = (float)gacc;
         ++ngroups;
         gacc = 0.0;
       }
-    } else if (valid) {
-      a.surv_raw[g] = qr[slot];
-      a.surv_idx[g] = qi[slot];
     }
     sins += n;
     qh = (qh + n) & (QCAP - 1);
@@ -814,23 +832,23 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
         const int nv = nvs[uu];
         const long long pos0 = pos + (long long)uu * 32 * VE + (long long)lane * VE;
         // max of the row before this segment (exact): a lower bound of every
-        // element's own prefix max
+        // element's own prefix max; one threshold for both bounds (NaN fails it)
         const float P = run_max;
         const float thrP = P >= p_floor ? fsub(P, fadd(c1, 0x1p-21f * fabsf(P))) : NEG_INF;
+        const float thr = fmaxf(thrP, thrLr);
         bool sv[VE];
-        int cnt = 0, ccnt = 0;
+        int cnt = 0;
+        bool anyc = false;
         float lm = NEG_INF;
 #pragma unroll
         for (int e = 0; e < VE; ++e) {
           const float xv = x[e];
-          const bool valid = e < nv && !is_nan(xv);
-          if (e < nv) lm = fmaxf(lm, xv);
-          const float xa = xv * invT;
-          const bool pruneL = xa < thrL - 0x1p-19f * (fabsf(xa) + fabsf(thrL));
-          sv[e] = valid && !(xv < thrP || pruneL);
-          if (valid && !sv[e]) pruned_max = fmaxf(pruned_max, xv);
+          const bool in = e < nv;
+          sv[e] = in && xv >= thr;
+          if (in) lm = fmaxf(lm, xv);
+          if (!fast && in && !sv[e]) pruned_max = fmaxf(pruned_max, xv);  // fmaxf skips NaN
           cnt += sv[e] ? 1 : 0;
-          ccnt += (valid && xv >= tau) ? 1 : 0;
+          anyc |= in && xv >= tau;
         }
         run_max = fmaxf(run_max, fkey_inv(__reduce_max_sync(PESTI_FULL_MASK, fkey(lm))));
         // survivors join the queue in row order
@@ -847,7 +865,10 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
         }
         qn += wsum;
         // top-k candidates: few per row (their exact exps are taken by the row kernel)
-        if (__any_sync(PESTI_FULL_MASK, ccnt > 0)) {
+        if (__any_sync(PESTI_FULL_MASK, anyc)) {
+          int ccnt = 0;
+#pragma unroll
+          for (int e = 0; e < VE; ++e) ccnt += (e < nv && x[e] >= tau) ? 1 : 0;
           const int cex0 = warp_incl_scan_add(ccnt);
           const int ctot = __shfl_sync(PESTI_FULL_MASK, cex0, 31);
           int basec = 0;
@@ -857,7 +878,7 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
 #pragma unroll
           for (int e = 0; e < VE; ++e) {
             const float xv = x[e];
-            if (e < nv && !is_nan(xv) && xv >= tau) {
+            if (e < nv && xv >= tau) {
               if (slot < CAND_CAP) {
                 a.cand_raw[b * CAND_CAP + slot] = xv;
                 a.cand_idx[b * CAND_CAP + slot] = (uint32_t)(pos0 + e);
@@ -912,6 +933,8 @@ struct ClassShared {
 
 __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
   __shared__ ClassShared sh;
+  grid_dep_launch_next();
+  grid_dep_wait();
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int nsub = a.P * K1_WARPS;
   const long long V = a.V;
@@ -949,9 +972,6 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
     const float* gsum = a.gsum + (b * nsub + sub) * a.jmax;
     double s_approx = a.pre[b * nsub + sub].A;
     for (int jj = 0; jj < j; ++jj) s_approx += (double)gsum[jj];
-    const void* row = a.dtype == PESTI_BF16 ? (const void*)((const uint16_t*)a.logits + b * a.ld)
-                                            : (const void*)((const float*)a.logits + b * a.ld);
-
     // element i of the group: its run key (binade or SPECIAL) and increments
     auto classify = [&](int i, float ea, float av, float bv, uint32_t& key, uint32_t& k0, uint32_t& k1) {
       uint32_t lo = 0u;
@@ -980,7 +1000,7 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
         }
       }
       if (need_exact) {
-        const float raw = load_logit_dyn(row, a.dtype, (long long)a.surv_idx[gbase + i]);
+        const float raw = a.surv_raw[gbase + i];
         const float ex = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127, exact
         if (special) {
           k0 = fbits(ex);
@@ -996,10 +1016,12 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
     const int i0 = lane * g;
     const int nl = n - i0 < 0 ? 0 : (n - i0 > g ? g : n - i0);  // valid elements of the lane
     __syncwarp();
+    // pass A: approximate exps (sampling.rs:46,127 within 2^-22)
     float ltot = 0.0f;
 #pragma unroll 1
     for (int jj = 0; jj < nl; ++jj) {
-      const float e = a.surv_ea[gbase + i0 + jj];
+      const float raw = a.surv_raw[gbase + i0 + jj];
+      const float e = pesti_expf_approx(fsub(scale ? fdiv(raw, T) : raw, m));
       eas[jj * 32 + lane] = e;
       ltot += e;
     }
@@ -1392,6 +1414,7 @@ __device__ uint32_t warp_fold(const void* raw, int dtype, long long n, uint32_t 
 }
 
 __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
+  grid_dep_wait();
   extern __shared__ __align__(16) unsigned char row_smem[];
   RowShared& sh = *reinterpret_cast<RowShared*>(row_smem);
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -1489,50 +1512,59 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
     // sub-slice whose entries overflowed stages one marker to replay it
     const long long keff = k < V ? k : V;
     {
+      // one thread per (sub-slice, group) pair in row order; a sub-slice with
+      // an overflowed group stages a single replay marker
       const GroupEnt* gs = a.gsurv + b * nsub * a.jmax;
       const FoldEnt* pool = a.pool + b * POOL_CAP;
-      int ne = 0;
-      if (tid < nsub) {
-        const SubSurv sv = survs[tid];
-        ss[tid] = sv;
-        if (sv.count > 0) {
-          bool rep = false;
-          for (int j = 0; j < sv.ngroups; ++j) {
-            const GroupEnt ge = gs[tid * a.jmax + j];
-            ne += ge.nent;
-            rep |= ge.replay != 0;
-          }
-          if (rep) ne = 1;
-          ss[tid].pad = rep ? 1 : 0;
-        }
+      int* rep = eoff;  // per sub-slice: any group overflowed (reused as offsets below)
+      for (int q = tid; q < nsub; q += K2_NT) {
+        ss[q] = survs[q];
+        rep[q] = 0;
       }
-      int tot;
-      const int ex = block_excl_scan_add(ne, sh.iscr, tot);
-      if (tid < nsub) eoff[tid] = ex;
-      if (tid == 0) fs.total = tot;
       __syncthreads();
-      if (tot <= FAST_ENTS) {
-        for (int q = wid; q < nsub; q += K2_NT / 32) {
+      const int npair = nsub * a.jmax;
+      for (int t = tid; t < npair; t += K2_NT) {
+        const int q = t / a.jmax, j = t - q * a.jmax;
+        if (j < ss[q].ngroups && gs[t].replay) rep[q] = 1;
+      }
+      __syncthreads();
+      for (int q = tid; q < nsub; q += K2_NT) ss[q].pad = rep[q];
+      __syncthreads();
+      int base = 0;
+      for (int t0 = 0; t0 < npair; t0 += K2_NT) {
+        const int t = t0 + tid;
+        int ne = 0, off = 0, q = 0, j = 0;
+        if (t < npair) {
+          q = t / a.jmax;
+          j = t - q * a.jmax;
           const SubSurv sv = ss[q];
-          if (sv.count <= 0) continue;
-          int e0 = eoff[q];
-          if (sv.pad) {  // a group of the sub-slice overflowed the pool: replay it whole
-            if (lane == 0) {
-              fs.ent[e0] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)sv.count};
-              fs.esub[e0] = (uint16_t)q;
+          if (j < sv.ngroups) {
+            if (sv.pad) {
+              ne = j == 0 ? 1 : 0;
+            } else {
+              const GroupEnt ge = gs[t];
+              ne = ge.nent;
+              off = ge.off;
             }
-            continue;
-          }
-          for (int j = 0; j < sv.ngroups; ++j) {
-            const GroupEnt ge = gs[q * a.jmax + j];
-            for (int i = lane; i < ge.nent; i += 32) {
-              fs.ent[e0 + i] = pool[ge.off + i];
-              fs.esub[e0 + i] = (uint16_t)q;
-            }
-            e0 += ge.nent;
           }
         }
+        int tot;
+        const int ex = base + block_excl_scan_add(ne, sh.iscr, tot);
+        if (t < npair && j == 0) eoff[q] = ex;  // where the sub-slice's entries start
+        if (t < npair && ne > 0) {
+          if (ss[q].pad) {
+            fs.ent[ex] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)ss[q].count};
+            fs.esub[ex] = (uint16_t)q;
+          } else if (ex + ne <= FAST_ENTS) {
+            for (int i = 0; i < ne; ++i) {
+              fs.ent[ex + i] = pool[off + i];
+              fs.esub[ex + i] = (uint16_t)q;
+            }
+          }
+        }
+        base += tot;
       }
+      if (tid == 0) fs.total = base;
       __syncthreads();
     }
     const int C = a.cand_count[b];
@@ -1573,23 +1605,34 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
       int cur_q = -1;
       uint32_t s_q = 0u;  // state at the start of sub-slice cur_q
       while (i < total) {
-        for (; i < total; ++i) {
-          const FoldEnt en = fs.ent[i];
-          const int q = fs.esub[i];
-          if (q != cur_q) {
-            cur_q = q;
-            s_q = s;
+        int fi = -1;  // first entry the state does not fit
+        for (; i < total && fi < 0; i += 4) {
+          // four entries at a time: their loads do not depend on the state
+          FoldEnt en[4];
+          int qq[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int ii = i + u < total ? i + u : i;
+            en[u] = fs.ent[ii];
+            qq[u] = fs.esub[ii];
           }
-          if (en.lo == fold::SPECIAL) {
-            s = fbits(fadd(bitsf(s), bitsf(en.a0)));
-            continue;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (fi < 0 && i + u < total) {
+              s_q = qq[u] != cur_q ? s : s_q;
+              cur_q = qq[u];
+              const bool sp = en[u].lo == fold::SPECIAL;
+              const uint32_t s_sp = fbits(fadd(bitsf(s), bitsf(en[u].a0)));
+              const uint32_t ns = s + ((s & 1u) ? en[u].a1 : en[u].a0);  // < 2^31 + 2^30: no wrap
+              // also false for every replay marker (no binade has its bits)
+              const bool fits = fold::binade_lo_bits(s) == en[u].lo && ns < fold::binade_hi_bits(en[u].lo);
+              if (!sp && !fits) fi = i + u;
+              else s = sp ? s_sp : ns;
+            }
           }
-          if (fold::binade_lo_bits(s) != en.lo) break;  // also every replay marker
-          const unsigned long long ns = (unsigned long long)s + ((s & 1u) ? en.a1 : en.a0);
-          if (ns >= (unsigned long long)fold::binade_hi_bits(en.lo)) break;
-          s = (uint32_t)ns;
         }
-        if (i >= total) break;
+        if (fi < 0) break;
+        i = fi;
         const long long st = (long long)cur_q * a.SL;
         const long long len = V - st < a.SL ? V - st : a.SL;
         const void* sub_row = a.dtype == PESTI_BF16 ? (const void*)((const uint16_t*)row + st)

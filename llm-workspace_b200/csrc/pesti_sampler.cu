@@ -131,6 +131,25 @@ int ensure_row_smem_limit(int device) {
   return PESTI_OK;
 }
 
+// Launch of a kernel that may start while the previous kernel of the stream
+// is finishing (programmatic dependent launch): it waits on the device for
+// that kernel's results (griddepcontrol.wait) before reading them.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                             Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // Launch geometry and workspace layout of one batch call: byte offsets into
 // one workspace, each region 256-byte aligned.
 struct Plan {
@@ -222,7 +241,6 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
   sa.surv = (pesti::SubSurv*)(ws + p.o_surv);
   sa.seg_max = (float*)(ws + p.o_segmax);
   sa.surv_raw = (float*)(ws + p.o_se);
-  sa.surv_ea = sa.surv_raw;  // fast-path rows store approximate exps there instead
   sa.surv_idx = (uint32_t*)(ws + p.o_si);
   sa.jmax = (int)p.jmax;
   sa.gsum = (float*)(ws + p.o_gsum);
@@ -255,21 +273,22 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
   if (e != cudaSuccess) return cuda_fail(e, "slice_stats_kernel launch");
   if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[1], st), "cudaEventRecord(profile)");
   // the survivor pass reads from L2: fewer loads in flight, smaller code
+  const dim3 b1(pesti::K1_NT);
   if (dtype == PESTI_BF16) {
-    if (aligned) pesti::survivor_kernel<uint16_t, 8, 1, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
-    else pesti::survivor_kernel<uint16_t, 8, 1, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
+    if (aligned) e = launch_dependent(pesti::survivor_kernel<uint16_t, 8, 1, true>, g1, b1, 0, st, sa);
+    else e = launch_dependent(pesti::survivor_kernel<uint16_t, 8, 1, false>, g1, b1, 0, st, sa);
   } else {
-    if (aligned) pesti::survivor_kernel<float, 4, 2, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
-    else pesti::survivor_kernel<float, 4, 2, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
+    if (aligned) e = launch_dependent(pesti::survivor_kernel<float, 4, 2, true>, g1, b1, 0, st, sa);
+    else e = launch_dependent(pesti::survivor_kernel<float, 4, 2, false>, g1, b1, 0, st, sa);
   }
-  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "survivor_kernel launch");
   // classification tasks: a persistent grid takes them from a counter
   {
     const long long most = (long long)B * p.nsub * p.jmax;
     const long long blocks = std::min<long long>(4LL * p.num_sms, (most + pesti::K1_WARPS - 1) / pesti::K1_WARPS);
-    pesti::classify_kernel<<<(unsigned)std::max(1LL, blocks), pesti::K1_NT, 0, st>>>(sa);
-    e = cudaGetLastError();
+    e = launch_dependent(pesti::classify_kernel, dim3((unsigned)std::max(1LL, blocks)), b1, 0, st, sa);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "classify_kernel launch");
   }
   if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[2], st), "cudaEventRecord(profile)");
@@ -314,8 +333,8 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
     int rc = ensure_row_smem_limit(device);
     if (rc) return rc;
   }
-  pesti::row_kernel<<<(unsigned)B, pesti::K2_NT, smem2, st>>>(ra);
-  e = cudaGetLastError();
+  e = launch_dependent(pesti::row_kernel, dim3((unsigned)B), dim3(pesti::K2_NT), smem2, st, ra);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "row_kernel launch");
   if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[3], st), "cudaEventRecord(profile)");
   return PESTI_OK;

@@ -75,7 +75,7 @@ struct RowInfo {      // row prologue, written by the last slice_stats block of 
 struct SubPre {       // per sub-slice, from the row prologue
   double A;           // approximate softmax mass of the earlier sub-slices
   float P;            // max raw logit of the earlier sub-slices
-  float pad;
+  float thrL;         // raw logits below it are absorbed by the running sum (bound (b)), or -inf
 };
 
 struct FoldEnt {      // one entry of a sub-slice's part of the softmax fold
@@ -87,7 +87,8 @@ struct FoldEnt {      // one entry of a sub-slice's part of the softmax fold
 struct SubSurv {      // survivor_kernel, one per sub-slice
   int32_t count;      // survivors stored at the sub-slice's own start
   int32_t ngroups;    // classification tasks of the sub-slice (fast-path rows)
-  int32_t pad;
+  int32_t pad;        // survivor_kernel: the classification tasks list the candidates;
+                      // row_kernel: the sub-slice is replayed
   float pruned_max;   // largest raw logit dropped (-inf if none)
 };
 
@@ -121,7 +122,6 @@ struct SliceArgs {
   float* surv_raw;  // [B][V]: raw logits of the survivors of sub-slice s, compacted at its own start
   uint32_t* surv_idx;
   int jmax;         // classification groups per sub-slice (ceil(SL / GROUP))
-  float* gsum;      // [B][P*K1_WARPS][jmax] approximate mass of each group
   ClassTask* tasks; // [B*P*K1_WARPS*jmax]
   int* task_count;  // tasks queued
   int* task_next;   // tasks taken
@@ -465,13 +465,29 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
     if (lane == 0) exc = NEG_INF;
     float pmax = fmaxf(wpre, exc);
 #pragma unroll
+    // bound (b) of the survivor pass, in raw units: with
+    // L = A (1 - V 2^-24)(1 - 2^-10) 2^-(2^-20 (|y_max| + 64)) <= the running
+    // sum (A was built from float products raw*c2 whose rounding grows with
+    // |y|), t = m + ln(L) - 17.36 and eta = 2^-20 (|t| + |m| + 1),
+    // x < (t - eta) T implies fl(fl(x/T) - m) < t - m - eta/2 (the roundings
+    // of x/T and of the difference are below eta/8), so the exact exp is below
+    // e^-17.36 L (1 + 2^-24) < 0.99 * 2^-25 L.  Rounded toward -inf.
+    const bool sum_ok = sum_pruning_ok(prm);
+    const double lfac = (1.0 - (double)V * 0x1p-24) * (1.0 - 0x1p-10) * exp2(-0x1p-20 * ((double)fabsf(ym) + 64.0));
+#pragma unroll
     for (int r = 0; r < PER; ++r) {
       const int s = tid * PER + r;
       if (s < nsub) {
         SubPre p;
         p.A = ex;
         p.P = pmax;
-        p.pad = 0.0f;
+        p.thrL = -INF;
+        const double L = ex * lfac;
+        if (sum_ok && L >= 0x1p-60) {
+          const double tL = (double)m + log(L) - 17.36;
+          const double eta = 0x1p-20 * (fabs(tL) + fabs((double)m) + 1.0);
+          p.thrL = __double2float_rd((tL - eta) * (double)t_eff);
+        }
         a.pre[b * nsub + s] = p;
       }
       ex += loc[r];
@@ -687,14 +703,33 @@ __device__ __forceinline__ Seg seg_shfl(Seg s, int src) {
              __shfl_sync(PESTI_FULL_MASK, s.cnt, src), __shfl_sync(PESTI_FULL_MASK, s.key, src)};
 }
 
+constexpr int K1_STAGES = 4;  // 16-byte loads in flight per lane in the survivor pass
+
 struct SurvShared {
-  float q_raw[K1_WARPS][QCAP];
-  uint32_t q_idx[K1_WARPS][QCAP];
+  float4 stage[K1_WARPS][K1_STAGES][32];  // chunks on their way from L2 (cp.async)
 };
 
-template <typename TIn, int VE, int U, bool VEC>
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// One warp per sub-slice.  The sub-slice is read from L2 in 32*VE-element
+// chunks (one 16-byte load per lane) with K1_STAGES chunks in flight; every
+// element either provably leaves every fold unchanged (derivation above) or
+// survives, and survivors are stored (raw logit and index) in row order at the
+// sub-slice's start.  For rows of the fast path the sub-slice then becomes
+// ceil(count / GROUP) classification tasks; their candidates for the top-k are
+// taken from the survivors by the classification pass whenever tau lies above
+// every threshold the sub-slice can use (SubSurv::cand_here = 0), else here.
+template <typename TIn, int VE, bool VEC>
 __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
-  __shared__ SurvShared sh;
+  __shared__ __align__(16) SurvShared sh;
   grid_dep_launch_next();
   grid_dep_wait();
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -721,192 +756,133 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
   long long end = start + a.SL;
   if (end > V) end = V;
   const TIn* row = (const TIn*)a.logits + b * a.ld;
-  const long long out_base = b * V + start;
+  float* sraw = a.surv_raw + b * V + start;
+  uint32_t* sidx = a.surv_idx + b * V + start;
   const float c1 = ABSORB * t_eff * (1.0f + 0x1p-20f);
   const float pf = (m - PRUNE_FLOOR) * t_eff;
   const float p_floor = pf + 0x1p-20f * fabsf(pf);
-  const float invT = 1.0f / t_eff;
-  const float ym = ri.max_raw * (1.4426950408889634f / t_eff);
-  // A was built from float products raw*c2 whose rounding grows with |y|:
-  // widen the margin with the magnitude of the scaled logits
-  const double mag = 0x1p-20 * ((double)fabsf(ym) + 64.0);
-  const double L = pr.A * (1.0 - (double)V * 0x1p-24) * (1.0 - 0x1p-10) * exp2(-mag);
-  const bool use_L = sum_pruning_ok(prm) && L >= 0x1p-60;
-  // (b) in raw units: with t = m + ln(L) - 17.36 and eta = 2^-20 (|t| + |m| + 1),
-  // x < (t - eta) T implies fl(fl(x/T) - m) < t - m - eta/2 (the roundings of
-  // x/T and of the difference are below eta/8), so the exact exp is below
-  // e^-17.36 L (1 + 2^-24) < 0.99 * 2^-25 L.  Rounded toward -inf as a float.
-  float thrLr = NEG_INF;
-  if (use_L) {
-    const double tL = (double)m + log(L) - 17.36;
-    const double eta = 0x1p-20 * (fabs(tL) + fabs((double)m) + 1.0);
-    thrLr = __double2float_rd((tL - eta) * (double)t_eff);
-  }
-  // group masses for the classification tasks: exp(x/T - m) = 2^(x c2 - m log2 e)
-  const float c2 = 1.4426950408889634f / t_eff;
-  const float mc = m * 1.4426950408889634f;
+  const float thrLr = pr.thrL;  // bound (b), from the row prologue
+  auto bound_a = [&](float P) { return P >= p_floor ? fsub(P, fadd(c1, 0x1p-21f * fabsf(P))) : NEG_INF; };
+  // bound (a) uses the max of the row before each chunk: the maxima of the
+  // earlier sub-slices, then this sub-slice's segment maxima from the first pass
+  const float* segm = a.seg_max + b * a.nseg + start / (32LL * VE);
   float run_max = pr.P;
   float pruned_max = NEG_INF;
-  int* ccount = a.cand_count + b;
-  float* qr = sh.q_raw[w];
-  uint32_t* qi = sh.q_idx[w];
-  // Every survivor is stored (raw logit and index) at the sub-slice's start.
-  // Rows of the fast path also queue one classification task per GROUP
-  // survivors, with the group's approximate mass, so that any warp can
-  // classify any group; the largest dropped logit is kept for the other rows
-  // (top-p, no filter, large top-k), whose generic path bounds with it.
   const bool fast = a.fast_enabled && fast_topk(prm, V);
-  float* gsum = a.gsum + (b * nsub + sub) * a.jmax;
-  int qh = 0, qn = 0;
+  // the largest threshold any chunk can use is that of the row max: with tau
+  // above it every candidate (raw >= tau) survives
+  const bool cand_here = fast && !(tau >= fmaxf(bound_a(ri.max_raw), thrLr));
+  int* ccount = a.cand_count + b;
+  float4* stg = sh.stage[w][0];
   long long sins = 0;  // survivors stored so far
-  double gacc = 0.0;   // approximate mass of the group being filled
-  int ngroups = 0;
 
-  // the n (<= 32) survivors at the queue head, one per lane
-  auto drain = [&](int n) {
-    const bool valid = lane < n;
-    const int slot = (qh + lane) & (QCAP - 1);
-    float e2 = 0.0f;
-    if (valid) {
-      const float raw = qr[slot];
-      const long long g = out_base + sins + lane;
-      a.surv_raw[g] = raw;
-      a.surv_idx[g] = qi[slot];
-      e2 = ex2_approx(fmaf(raw, c2, -mc));
-    }
-    if (fast) {
-      gacc += (double)warp_reduce_add(e2);
-      if (((sins + n) & (GROUP - 1)) == 0) {  // a full group (a partial last one closes below)
-        if (lane == 0) gsum[ngroups] = (float)gacc;
-        ++ngroups;
-        gacc = 0.0;
-      }
-    }
-    sins += n;
-    qh = (qh + n) & (QCAP - 1);
-    qn -= n;
-  };
-
-  // One loop over the sub-slice's 32*VE*U-element chunks, then one more pass
-  // that drains the queue.
-  const long long CH = 32LL * VE * U;
-  for (long long pos = start;; pos += CH) {
-    const bool more = pos < end;
-    if (more) {
-      float xs_[U][VE];
-      int nvs[U];
-      if (VEC && pos + CH <= end) {
+  constexpr long long CHV = 32LL * VE;  // elements per chunk
+  const long long nchunk = (end - start + CHV - 1) / CHV;
+  const long long nfull = VEC ? (end - start) / CHV : 0;  // chunks read through the pipeline
+  if (VEC) {
 #pragma unroll
-        for (int uu = 0; uu < U; ++uu) {
-          const float4 r4 = __ldg(reinterpret_cast<const float4*>(row + pos + (long long)uu * 32 * VE + (long long)lane * VE));
-          if (sizeof(TIn) == 4) {
-            xs_[uu][0] = r4.x; xs_[uu][1] = r4.y; xs_[uu][2] = r4.z; xs_[uu][3] = r4.w;
-          } else {
-            const uint32_t wds[4] = {__float_as_uint(r4.x), __float_as_uint(r4.y), __float_as_uint(r4.z),
-                                     __float_as_uint(r4.w)};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              xs_[uu][2 * q] = __uint_as_float(wds[q] << 16);
-              xs_[uu][2 * q + 1] = __uint_as_float(wds[q] & 0xffff0000u);
-            }
-          }
-          nvs[uu] = VE;
-        }
+    for (int st = 0; st < K1_STAGES; ++st) {
+      if (st < nfull) cp_async16(&stg[st * 32 + lane], row + start + st * CHV + lane * VE);
+      cp_async_commit();
+    }
+  }
+  float segv = NEG_INF;  // segment maxima of chunks c0 + lane, 32 at a time
+  for (long long c = 0; c < nchunk; ++c) {
+    if ((c & 31) == 0) segv = c + lane < nchunk ? segm[c + lane] : NEG_INF;
+    const float segmx = __shfl_sync(PESTI_FULL_MASK, segv, (int)(c & 31));
+    float x[VE];
+    int nv = VE;
+    const bool piped = VEC && c < nfull;
+    if (piped) {
+      cp_async_wait<K1_STAGES - 1>();  // chunk c has arrived (each lane reads its own bytes)
+      const float4 r4 = stg[(c % K1_STAGES) * 32 + lane];
+      if (sizeof(TIn) == 4) {
+        x[0] = r4.x; x[1] = r4.y; x[2] = r4.z; x[3] = r4.w;
       } else {
+        const uint32_t wds[4] = {__float_as_uint(r4.x), __float_as_uint(r4.y), __float_as_uint(r4.z),
+                                 __float_as_uint(r4.w)};
 #pragma unroll
-        for (int uu = 0; uu < U; ++uu) {
-          const long long p0 = pos + (long long)uu * 32 * VE + (long long)lane * VE;
-          int nv = 0;
-#pragma unroll
-          for (int e = 0; e < VE; ++e) {
-            const long long j = p0 + e;
-            xs_[uu][e] = j < end ? load_logit<TIn>(row, j) : 0.0f;
-            nv = j < end ? e + 1 : nv;
-          }
-          nvs[uu] = nv;
+        for (int q = 0; q < 4; ++q) {
+          x[2 * q] = __uint_as_float(wds[q] << 16);
+          x[2 * q + 1] = __uint_as_float(wds[q] & 0xffff0000u);
         }
       }
+    } else {
+      const long long p0 = start + c * CHV + (long long)lane * VE;
+      nv = 0;
 #pragma unroll
-      for (int uu = 0; uu < U; ++uu) {
-        const float(&x)[VE] = xs_[uu];
-        const int nv = nvs[uu];
-        const long long pos0 = pos + (long long)uu * 32 * VE + (long long)lane * VE;
-        // max of the row before this segment (exact): a lower bound of every
-        // element's own prefix max; one threshold for both bounds (NaN fails it)
-        const float P = run_max;
-        const float thrP = P >= p_floor ? fsub(P, fadd(c1, 0x1p-21f * fabsf(P))) : NEG_INF;
-        const float thr = fmaxf(thrP, thrLr);
-        bool sv[VE];
-        int cnt = 0;
-        bool anyc = false;
-        float lm = NEG_INF;
+      for (int e = 0; e < VE; ++e) {
+        const long long j = p0 + e;
+        x[e] = j < end ? load_logit<TIn>(row, j) : 0.0f;
+        nv = j < end ? e + 1 : nv;
+      }
+    }
+    // one threshold for both bounds (NaN fails it): bound (a) with the max of
+    // the row before the chunk (exact), bound (b)
+    const float thr = fmaxf(bound_a(run_max), thrLr);
+    run_max = fmaxf(run_max, segmx);
+    bool sv[VE];
+    int cnt = 0;
+#pragma unroll
+    for (int e = 0; e < VE; ++e) {
+      sv[e] = e < nv && x[e] >= thr;
+      cnt += sv[e] ? 1 : 0;
+    }
+    // survivors are stored in row order
+    const int cinc = warp_incl_scan_add(cnt);
+    long long o = sins + (cinc - cnt);
+    const uint32_t p0 = (uint32_t)(start + c * CHV) + (uint32_t)(lane * VE);
+#pragma unroll
+    for (int e = 0; e < VE; ++e) {
+      if (sv[e]) {
+        sraw[o] = x[e];
+        sidx[o] = p0 + (uint32_t)e;
+        ++o;
+      }
+    }
+    sins += __shfl_sync(PESTI_FULL_MASK, cinc, 31);
+    if (!fast) {  // the largest dropped logit (fmaxf skips NaN)
+#pragma unroll
+      for (int e = 0; e < VE; ++e)
+        if (e < nv && !sv[e]) pruned_max = fmaxf(pruned_max, x[e]);
+    }
+    if (cand_here) {  // top-k candidates (their exact exps are taken by the row kernel)
+      int ccnt = 0;
+#pragma unroll
+      for (int e = 0; e < VE; ++e) ccnt += (e < nv && x[e] >= tau) ? 1 : 0;
+      if (__any_sync(PESTI_FULL_MASK, ccnt > 0)) {
+        const int cex0 = warp_incl_scan_add(ccnt);
+        const int ctot = __shfl_sync(PESTI_FULL_MASK, cex0, 31);
+        int basec = 0;
+        if (lane == 0) basec = atomicAdd(ccount, ctot);
+        basec = __shfl_sync(PESTI_FULL_MASK, basec, 0);
+        int slot = basec + cex0 - ccnt;
 #pragma unroll
         for (int e = 0; e < VE; ++e) {
-          const float xv = x[e];
-          const bool in = e < nv;
-          sv[e] = in && xv >= thr;
-          if (in) lm = fmaxf(lm, xv);
-          if (!fast && in && !sv[e]) pruned_max = fmaxf(pruned_max, xv);  // fmaxf skips NaN
-          cnt += sv[e] ? 1 : 0;
-          anyc |= in && xv >= tau;
-        }
-        run_max = fmaxf(run_max, fkey_inv(__reduce_max_sync(PESTI_FULL_MASK, fkey(lm))));
-        // survivors join the queue in row order
-        const int cinc = warp_incl_scan_add(cnt);
-        const int wsum = __shfl_sync(PESTI_FULL_MASK, cinc, 31);
-        int o = qh + qn + (cinc - cnt);
-#pragma unroll
-        for (int e = 0; e < VE; ++e) {
-          if (sv[e]) {
-            qr[o & (QCAP - 1)] = x[e];
-            qi[o & (QCAP - 1)] = (uint32_t)(pos0 + e);
-            ++o;
-          }
-        }
-        qn += wsum;
-        // top-k candidates: few per row (their exact exps are taken by the row kernel)
-        if (__any_sync(PESTI_FULL_MASK, anyc)) {
-          int ccnt = 0;
-#pragma unroll
-          for (int e = 0; e < VE; ++e) ccnt += (e < nv && x[e] >= tau) ? 1 : 0;
-          const int cex0 = warp_incl_scan_add(ccnt);
-          const int ctot = __shfl_sync(PESTI_FULL_MASK, cex0, 31);
-          int basec = 0;
-          if (lane == 0) basec = atomicAdd(ccount, ctot);
-          basec = __shfl_sync(PESTI_FULL_MASK, basec, 0);
-          int slot = basec + cex0 - ccnt;
-#pragma unroll
-          for (int e = 0; e < VE; ++e) {
-            const float xv = x[e];
-            if (e < nv && xv >= tau) {
-              if (slot < CAND_CAP) {
-                a.cand_raw[b * CAND_CAP + slot] = xv;
-                a.cand_idx[b * CAND_CAP + slot] = (uint32_t)(pos0 + e);
-              }
-              ++slot;
+          if (e < nv && x[e] >= tau) {
+            if (slot < CAND_CAP) {
+              a.cand_raw[b * CAND_CAP + slot] = x[e];
+              a.cand_idx[b * CAND_CAP + slot] = p0 + (uint32_t)e;
             }
+            ++slot;
           }
         }
       }
     }
-    __syncwarp();
-    const int need = more ? 32 : 1;
-    while (qn >= need) {
-      drain(qn < 32 ? qn : 32);
-      __syncwarp();
+    if (piped) {  // the stage just read (its values are used above) takes chunk c + K1_STAGES
+      const long long cn = c + K1_STAGES;
+      if (cn < nfull) cp_async16(&stg[(c % K1_STAGES) * 32 + lane], row + start + cn * CHV + lane * VE);
+      cp_async_commit();
     }
-    if (!more) break;
   }
-  if (fast && sins > (long long)ngroups * GROUP) {  // the partial last group
-    if (lane == 0) gsum[ngroups] = (float)gacc;
-    ++ngroups;
-  }
+  if (VEC) cp_async_wait<0>();
   const float pm = warp_reduce_fmax(pruned_max);
-  if (fast && ngroups > 0 && lane == 0) {
+  const int ngroups = fast ? (int)((sins + GROUP - 1) / GROUP) : 0;
+  if (ngroups > 0 && lane == 0) {
     const int t0 = atomicAdd(a.task_count, ngroups);
     for (int j = 0; j < ngroups; ++j) a.tasks[t0 + j] = ClassTask{(int)b, (int)(sub * a.jmax + j)};
   }
-  if (lane == 0) *so = SubSurv{(int32_t)sins, ngroups, 0, pm};
+  if (lane == 0) *so = SubSurv{(int32_t)sins, ngroups, cand_here ? 0 : 1, pm};
 }
 
 // ---------------------------------------------------------------------------
@@ -969,9 +945,37 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
     const SubSurv ssv = a.surv[b * nsub + sub];
     const long long gbase = b * V + sub * a.SL + (long long)j * GROUP;  // first survivor of the group
     const int n = ssv.count - j * GROUP < GROUP ? ssv.count - j * GROUP : GROUP;
-    const float* gsum = a.gsum + (b * nsub + sub) * a.jmax;
+    const float* sraw = a.surv_raw + b * V + sub * a.SL;
+    // approximate state at the group's start: the prefix mass of the earlier
+    // sub-slices plus that of the sub-slice's earlier survivors
+    // (exp(x/T - m) = 2^(x c2 - m log2 e); a relative 2^-12 is all it needs)
     double s_approx = a.pre[b * nsub + sub].A;
-    for (int jj = 0; jj < j; ++jj) s_approx += (double)gsum[jj];
+    if (j > 0) {
+      const float c2 = 1.4426950408889634f / (scale ? T : 1.0f);
+      const float mc = m * 1.4426950408889634f;
+      float acc = 0.0f;
+      for (int i = lane; i < j * GROUP; i += 32) acc += ex2_approx(fmaf(sraw[i], c2, -mc));
+      s_approx += (double)warp_reduce_add(acc);
+    }
+    if (ssv.pad) {  // the group's top-k candidates (all of them survived)
+      const float tau = ri.tau;
+      for (int i0 = 0; i0 < n; i0 += 32) {
+        const int i = i0 + lane;
+        const float raw = i < n ? sraw[(long long)j * GROUP + i] : 0.0f;
+        const bool cand = i < n && raw >= tau;
+        const uint32_t bal = __ballot_sync(PESTI_FULL_MASK, cand);
+        if (bal) {
+          int basec = 0;
+          if (lane == 0) basec = atomicAdd(a.cand_count + b, __popc(bal));
+          basec = __shfl_sync(PESTI_FULL_MASK, basec, 0);
+          const int slot = basec + __popc(bal & ((1u << lane) - 1u));
+          if (cand && slot < CAND_CAP) {
+            a.cand_raw[b * CAND_CAP + slot] = raw;
+            a.cand_idx[b * CAND_CAP + slot] = a.surv_idx[gbase + i];
+          }
+        }
+      }
+    }
     // element i of the group: its run key (binade or SPECIAL) and increments
     auto classify = [&](int i, float ea, float av, float bv, uint32_t& key, uint32_t& k0, uint32_t& k1) {
       uint32_t lo = 0u;

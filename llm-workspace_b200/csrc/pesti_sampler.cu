@@ -158,7 +158,7 @@ struct Plan {
   long long nsub, nseg, jmax;
   bool sorted_bufs;
   size_t o_ctr, o_stats, o_pre, o_info, o_surv, o_segmax, o_se, o_si, o_cc, o_ce, o_ci;
-  size_t o_gsum, o_gsurv, o_tasks, o_tctr, o_pctr, o_pool;
+  size_t o_gsurv, o_tasks, o_tctr, o_pctr, o_pool;
   size_t o_E, o_I, o_status;
   size_t o_sk0 = 0, o_sv0 = 0, o_sk1 = 0, o_sv1 = 0, o_q = 0;
   size_t bytes;  // workspace the call needs
@@ -196,7 +196,6 @@ Plan make_plan(int num_sms, pesti_dtype dtype, long long B, long long V, bool so
   p.o_E = take(bv * 4);
   p.o_I = take(bv * 4);
   p.o_status = take(16);
-  p.o_gsum = take(ngrp * sizeof(float));
   p.o_gsurv = take(ngrp * sizeof(pesti::GroupEnt));
   p.o_tasks = take(ngrp * sizeof(pesti::ClassTask));
   p.o_tctr = take(2 * sizeof(int));
@@ -243,7 +242,6 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
   sa.surv_raw = (float*)(ws + p.o_se);
   sa.surv_idx = (uint32_t*)(ws + p.o_si);
   sa.jmax = (int)p.jmax;
-  sa.gsum = (float*)(ws + p.o_gsum);
   sa.tasks = (pesti::ClassTask*)(ws + p.o_tasks);
   sa.task_count = (int*)(ws + p.o_tctr);
   sa.task_next = sa.task_count + 1;
@@ -275,11 +273,11 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
   // the survivor pass reads from L2: fewer loads in flight, smaller code
   const dim3 b1(pesti::K1_NT);
   if (dtype == PESTI_BF16) {
-    if (aligned) e = launch_dependent(pesti::survivor_kernel<uint16_t, 8, 1, true>, g1, b1, 0, st, sa);
-    else e = launch_dependent(pesti::survivor_kernel<uint16_t, 8, 1, false>, g1, b1, 0, st, sa);
+    if (aligned) e = launch_dependent(pesti::survivor_kernel<uint16_t, 8, true>, g1, b1, 0, st, sa);
+    else e = launch_dependent(pesti::survivor_kernel<uint16_t, 8, false>, g1, b1, 0, st, sa);
   } else {
-    if (aligned) e = launch_dependent(pesti::survivor_kernel<float, 4, 2, true>, g1, b1, 0, st, sa);
-    else e = launch_dependent(pesti::survivor_kernel<float, 4, 2, false>, g1, b1, 0, st, sa);
+    if (aligned) e = launch_dependent(pesti::survivor_kernel<float, 4, true>, g1, b1, 0, st, sa);
+    else e = launch_dependent(pesti::survivor_kernel<float, 4, false>, g1, b1, 0, st, sa);
   }
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "survivor_kernel launch");

@@ -69,7 +69,7 @@ struct RowInfo {      // row prologue, written by the last slice_stats block of 
   uint32_t flags;     // MF_* over the row
   long long last_max, first_max, last_nan;  // argmax indices: greedy rows only
   int uniform;        // the softmax sum is NaN or not > 0: all probabilities are 1/V
-  int pad;
+  float e_tau;        // exact exp(RN(tau/T) - m) when tau is finite, else 0
 };
 
 struct SubPre {       // per sub-slice, from the row prologue
@@ -81,7 +81,8 @@ struct SubPre {       // per sub-slice, from the row prologue
 struct FoldEnt {      // one entry of a sub-slice's part of the softmax fold
   uint32_t lo;        // binade (bits of its lowest value) of a run; fold::SPECIAL: one element
   uint32_t a0, a1;    // run: increments for an even / odd entry state; special: bits of the value
-  uint32_t count;     // survivors covered
+  uint32_t end;       // row index just past the entry's last element: the entry covers the
+                      // row from the previous entry's end (the elements between are no-ops)
 };
 
 struct SubSurv {      // survivor_kernel, one per sub-slice
@@ -129,7 +130,7 @@ struct SliceArgs {
   FoldEnt* pool;    // [B][POOL_CAP] fold entries
   int* pool_ctr;    // [B]
   int* cand_count;  // [B]
-  float* cand_raw;  // [B][CAND_CAP] raw logits of the top-k candidates
+  float* cand_e;    // [B][CAND_CAP] exact exps of the top-k candidates (sampling.rs:127)
   uint32_t* cand_idx;
   int fast_enabled; // rows of the fast path keep no survivors (see survivor_kernel)
 };
@@ -150,7 +151,7 @@ struct RowArgs {
   const float* surv_raw;
   const uint32_t* surv_idx;
   const int* cand_count;
-  const float* cand_raw;
+  const float* cand_e;
   const uint32_t* cand_idx;
   float* E;       // [B][V] sequence built by the generic path
   uint32_t* I;
@@ -464,7 +465,6 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
     float exc = __shfl_up_sync(PESTI_FULL_MASK, inc, 1);
     if (lane == 0) exc = NEG_INF;
     float pmax = fmaxf(wpre, exc);
-#pragma unroll
     // bound (b) of the survivor pass, in raw units: with
     // L = A (1 - V 2^-24)(1 - 2^-10) 2^-(2^-20 (|y_max| + 64)) <= the running
     // sum (A was built from float products raw*c2 whose rounding grows with
@@ -545,7 +545,7 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
     ri.first_max = fi < (1LL << 62) ? fi : -1;
     ri.last_nan = ln;
     ri.uniform = uniform ? 1 : 0;
-    ri.pad = 0;
+    ri.e_tau = tau > NEG_INF && tau < INF ? pesti_expf_call(fsub(scale ? fdiv(tau, T) : tau, m)) : 0.0f;
     a.info[b] = ri;
   }
 }
@@ -861,7 +861,7 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
         for (int e = 0; e < VE; ++e) {
           if (e < nv && x[e] >= tau) {
             if (slot < CAND_CAP) {
-              a.cand_raw[b * CAND_CAP + slot] = x[e];
+              a.cand_e[b * CAND_CAP + slot] = pesti_expf_call(fsub(scale ? fdiv(x[e], T) : x[e], m));
               a.cand_idx[b * CAND_CAP + slot] = p0 + (uint32_t)e;
             }
             ++slot;
@@ -970,7 +970,7 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
           basec = __shfl_sync(PESTI_FULL_MASK, basec, 0);
           const int slot = basec + __popc(bal & ((1u << lane) - 1u));
           if (cand && slot < CAND_CAP) {
-            a.cand_raw[b * CAND_CAP + slot] = raw;
+            a.cand_e[b * CAND_CAP + slot] = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127
             a.cand_idx[b * CAND_CAP + slot] = a.surv_idx[gbase + i];
           }
         }
@@ -1119,19 +1119,20 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
         uint32_t cur = prev_key;
         bool started = false;
         Seg tr{0u, 0u, 0u, KEY_NONE};
+        auto rend = [&](int i) { return a.surv_idx[gbase + i] + 1u; };  // past survivor i
 #pragma unroll 1
         for (int jj = 0; jj < nl; ++jj) {
           const uint32_t k = cks[jj * 32 + lane], k0 = c0s[jj * 32 + lane], k1 = c1s[jj * 32 + lane];
           const bool head = k == fold::SPECIAL || cur == fold::SPECIAL || cur == KEY_NONE || k != cur;
           if (head) {
             if (!started) {
-              if (first.cnt > 0u) ent[slot++] = FoldEnt{first.key, first.a0, first.a1, first.cnt};
+              if (first.cnt > 0u) ent[slot++] = FoldEnt{first.key, first.a0, first.a1, rend(i0 + jj - 1)};
               started = true;
             } else if (tr.cnt > 0u) {
-              ent[slot++] = FoldEnt{tr.key, tr.a0, tr.a1, tr.cnt};
+              ent[slot++] = FoldEnt{tr.key, tr.a0, tr.a1, rend(i0 + jj - 1)};
             }
             if (k == fold::SPECIAL) {
-              ent[slot++] = FoldEnt{fold::SPECIAL, k0, 0u, 1u};
+              ent[slot++] = FoldEnt{fold::SPECIAL, k0, 0u, rend(i0 + jj)};
               tr = Seg{0u, 0u, 0u, KEY_NONE};
             } else {
               tr = Seg{k0, k1, 1u, k};
@@ -1143,7 +1144,7 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
           cur = k;
         }
       }
-      if (lane == 0 && last.cnt > 0u) ent[nclosed] = FoldEnt{last.key, last.a0, last.a1, last.cnt};
+      if (lane == 0 && last.cnt > 0u) ent[nclosed] = FoldEnt{last.key, last.a0, last.a1, a.surv_idx[gbase + n - 1] + 1u};
     }
     if (lane == 0) a.gsurv[(b * nsub + sub) * a.jmax + j] = GroupEnt{off0, replay ? 0 : netot, replay ? 1 : 0, 0};
   }
@@ -1190,11 +1191,14 @@ struct FastSmem {
   unsigned long long key[FAST_CAND];
   float q[FAST_CAND];
   float stage[STAGE];
-  FoldEnt ent[FAST_ENTS];      // the row's entries, sub-slice after sub-slice
-  uint16_t esub[FAST_ENTS];    // sub-slice of each entry
+  FoldEnt ent[FAST_ENTS];      // the row's entries in row order
+  FoldEnt ment[FAST_ENTS];     // the same with consecutive runs of one binade merged
+  Seg wseg[K2_NT / 32];        // block-wide segmented scan: per-warp totals and prefixes
+  Seg wpre[K2_NT / 32];
+  int wfl[K2_NT / 32];
   int total;                   // entries of the row (> FAST_ENTS: not staged)
-  float p_tau;                 // exp of the candidate threshold (scaled, minus m)
-  // followed by SubSurv[nsub] and int eoff[nsub] (first entry of each sub-slice)
+  int nment;                   // merged entries
+  // followed by SubSurv[nsub] and int eoff[nsub] (scratch)
 };
 __host__ __device__ inline size_t fast_smem_bytes(int nsub) {
   return sizeof(FastSmem) + (size_t)nsub * (sizeof(SubSurv) + sizeof(int));
@@ -1512,15 +1516,14 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
     FastSmem& fs = *reinterpret_cast<FastSmem*>(row_smem + sizeof(RowShared));
     SubSurv* ss = reinterpret_cast<SubSurv*>(row_smem + sizeof(RowShared) + sizeof(FastSmem));
     int* eoff = reinterpret_cast<int*>(ss + nsub);
-    // stage the row's fold entries, compacted, with the whole block; a
-    // sub-slice whose entries overflowed stages one marker to replay it
+    // stage the row's fold entries, compacted, with the whole block: one
+    // thread per (sub-slice, group) pair in row order; a sub-slice with an
+    // overflowed group stages a single replay marker
     const long long keff = k < V ? k : V;
     {
-      // one thread per (sub-slice, group) pair in row order; a sub-slice with
-      // an overflowed group stages a single replay marker
       const GroupEnt* gs = a.gsurv + b * nsub * a.jmax;
       const FoldEnt* pool = a.pool + b * POOL_CAP;
-      int* rep = eoff;  // per sub-slice: any group overflowed (reused as offsets below)
+      int* rep = eoff;  // per sub-slice: a group overflowed
       for (int q = tid; q < nsub; q += K2_NT) {
         ss[q] = survs[q];
         rep[q] = 0;
@@ -1532,19 +1535,18 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
         if (j < ss[q].ngroups && gs[t].replay) rep[q] = 1;
       }
       __syncthreads();
-      for (int q = tid; q < nsub; q += K2_NT) ss[q].pad = rep[q];
-      __syncthreads();
       int base = 0;
       for (int t0 = 0; t0 < npair; t0 += K2_NT) {
         const int t = t0 + tid;
-        int ne = 0, off = 0, q = 0, j = 0;
+        int ne = 0, off = 0, q = 0;
+        bool mark = false;
         if (t < npair) {
           q = t / a.jmax;
-          j = t - q * a.jmax;
-          const SubSurv sv = ss[q];
-          if (j < sv.ngroups) {
-            if (sv.pad) {
+          const int j = t - q * a.jmax;
+          if (j < ss[q].ngroups) {
+            if (rep[q]) {
               ne = j == 0 ? 1 : 0;
+              mark = true;
             } else {
               const GroupEnt ge = gs[t];
               ne = ge.nent;
@@ -1554,16 +1556,13 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
         }
         int tot;
         const int ex = base + block_excl_scan_add(ne, sh.iscr, tot);
-        if (t < npair && j == 0) eoff[q] = ex;  // where the sub-slice's entries start
-        if (t < npair && ne > 0) {
-          if (ss[q].pad) {
-            fs.ent[ex] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)ss[q].count};
-            fs.esub[ex] = (uint16_t)q;
-          } else if (ex + ne <= FAST_ENTS) {
-            for (int i = 0; i < ne; ++i) {
-              fs.ent[ex + i] = pool[off + i];
-              fs.esub[ex + i] = (uint16_t)q;
-            }
+        if (ne > 0 && ex + ne <= FAST_ENTS) {
+          if (mark) {
+            const long long qend = ((long long)q + 1) * a.SL;
+            fs.ent[ex] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)(qend < V ? qend : V)};
+          } else {
+#pragma unroll 8
+            for (int i = 0; i < ne; ++i) fs.ent[ex + i] = pool[off + i];  // independent loads overlap
           }
         }
         base += tot;
@@ -1571,16 +1570,83 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
       if (tid == 0) fs.total = base;
       __syncthreads();
     }
+    // Merge consecutive runs of one binade (their increments compose; the
+    // merged run covers the row up to the last one's end), so that the walk
+    // below takes one step per binade change or special.  A block-wide
+    // segmented scan: each thread holds two entries.
+    if (fs.total <= FAST_ENTS) {
+      const int total = fs.total;
+      auto single = [](uint32_t key) { return key == fold::SPECIAL || key == ENT_REPLAY; };
+      const int e0 = 2 * tid, e1 = e0 + 1;
+      const FoldEnt none{KEY_NONE, 0u, 0u, 0u};
+      const FoldEnt x0 = e0 < total ? fs.ent[e0] : none;
+      const FoldEnt x1 = e1 < total ? fs.ent[e1] : none;
+      const uint32_t kp = e0 > 0 && e0 < total ? fs.ent[e0 - 1].lo : KEY_NONE;
+      const uint32_t kn = e1 + 1 < total ? fs.ent[e1 + 1].lo : KEY_NONE;
+      const bool h0 = e0 < total && (e0 == 0 || single(x0.lo) || single(kp) || x0.lo != kp);
+      const bool h1 = e1 < total && (single(x1.lo) || single(x0.lo) || x1.lo != x0.lo);
+      const bool h2 = e1 + 1 < total && (single(kn) || single(x1.lo) || kn != x1.lo);
+      const Seg v0{x0.a0, x0.a1, 0u, x0.lo}, v1{x1.a0, x1.a1, 0u, x1.lo};
+      const Seg agg = e1 < total ? seg_join(v0, v1, h1) : v0;
+      const bool aflag = h0 || h1;
+      Seg inc = agg;
+      bool fl = aflag;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const Seg o = seg_shfl_up(inc, off);
+        const bool of = __shfl_up_sync(PESTI_FULL_MASK, fl, off);
+        if (lane >= off) {
+          inc = seg_join(o, inc, fl);
+          fl = fl || of;
+        }
+      }
+      if (lane == 31) {
+        fs.wseg[wid] = inc;
+        fs.wfl[wid] = fl ? 1 : 0;
+      }
+      __syncthreads();
+      if (wid == 0) {  // exclusive segmented scan over the warps' totals
+        constexpr int NW = K2_NT / 32;
+        const Seg idn{0u, 0u, 0u, KEY_NONE};
+        Seg wi = lane < NW ? fs.wseg[lane] : idn;
+        bool wf = lane < NW ? fs.wfl[lane] != 0 : false;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const Seg o = seg_shfl_up(wi, off);
+          const bool of = __shfl_up_sync(PESTI_FULL_MASK, wf, off);
+          if (lane >= off) {
+            wi = seg_join(o, wi, wf);
+            wf = wf || of;
+          }
+        }
+        const Seg we = seg_shfl_up(wi, 1);
+        if (lane < NW) fs.wpre[lane] = lane == 0 ? idn : we;
+      }
+      __syncthreads();
+      Seg pre = fs.wpre[wid];
+      const Seg ex = seg_shfl_up(inc, 1);
+      const bool exf = __shfl_up_sync(PESTI_FULL_MASK, fl, 1);
+      if (lane > 0) pre = seg_join(pre, ex, exf);
+      const Seg i0v = seg_join(pre, v0, h0);
+      const Seg i1v = seg_join(i0v, v1, h1);
+      const bool end0 = e0 < total && (e1 >= total || h1);
+      const bool end1 = e1 < total && (e1 + 1 >= total || h2);
+      int tot;
+      const int slot = block_excl_scan_add((end0 ? 1 : 0) + (end1 ? 1 : 0), sh.iscr, tot);
+      int o = slot;
+      if (end0) fs.ment[o++] = FoldEnt{single(x0.lo) ? x0.lo : i0v.key, i0v.a0, i0v.a1, x0.end};
+      if (end1) fs.ment[o] = FoldEnt{single(x1.lo) ? x1.lo : i1v.key, i1v.a0, i1v.a1, x1.end};
+      if (tid == 0) fs.nment = tot;
+      __syncthreads();
+    }
     const int C = a.cand_count[b];
     const bool cand_ok = C >= keff && C <= FAST_CAND;
     if (wid == 1 && fs.total <= FAST_ENTS && cand_ok) {
       // candidates by (e desc, index asc) while warp 0 folds; the order by p
       // = e/S differs only inside groups of equal p (fixed up below)
-      for (int j = lane; j < C; j += 32) {
-        const float xr = a.cand_raw[b * CAND_CAP + j];
-        const float e = pesti_expf(fsub(scale ? fdiv(xr, T) : xr, m));  // sampling.rs:46,127
-        fs.key[j] = ((unsigned long long)fbits(e) << 32) | (unsigned long long)(~a.cand_idx[b * CAND_CAP + j]);
-      }
+      for (int j = lane; j < C; j += 32)
+        fs.key[j] = ((unsigned long long)fbits(a.cand_e[b * CAND_CAP + j]) << 32) |
+                    (unsigned long long)(~a.cand_idx[b * CAND_CAP + j]);
       __syncwarp();
       if (C <= 32) warp_sort_keys<1>(fs.key, C);
       else if (C <= 64) warp_sort_keys<2>(fs.key, C);
@@ -1592,39 +1658,25 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
         __syncwarp();
         warp_bitonic_desc(fs.key, mm2);
       }
-      const float tau = ri.tau;
-      const float e_tau = tau > -INF ? pesti_expf(fsub(scale ? fdiv(tau, T) : tau, m)) : 0.0f;
-      if (lane == 0) fs.p_tau = e_tau;
+
     }
     uint32_t s = 0u;
     if (wid == 0 && fs.total <= FAST_ENTS) {
-      // softmax denominator (sampling.rs:128): walk the entries with the exact
-      // state; a run the state does not fit (or a replay marker) is folded
-      // from its survivors
-      // On a failure the whole sub-slice is folded again from its raw logits,
-      // starting from the state it was entered with (dropped elements are
-      // exact no-ops, so folding all of them gives the same state).
-      const int total = fs.total;
+      // softmax denominator (sampling.rs:128): walk the merged entries with the
+      // exact state.  An entry the state does not fit (or a replay marker) is folded from
+      // the raw logits of the row range it covers, from the state before it
+      // (the dropped elements in the range are exact no-ops).
+      const int nm = fs.nment;
       int i = 0;
-      int cur_q = -1;
-      uint32_t s_q = 0u;  // state at the start of sub-slice cur_q
-      while (i < total) {
+      while (i < nm) {
         int fi = -1;  // first entry the state does not fit
-        for (; i < total && fi < 0; i += 4) {
-          // four entries at a time: their loads do not depend on the state
-          FoldEnt en[4];
-          int qq[4];
+        for (; i < nm && fi < 0; i += 4) {
+          FoldEnt en[4];  // four at a time: their loads do not depend on the state
+#pragma unroll
+          for (int u = 0; u < 4; ++u) en[u] = fs.ment[i + u < nm ? i + u : i];
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            const int ii = i + u < total ? i + u : i;
-            en[u] = fs.ent[ii];
-            qq[u] = fs.esub[ii];
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if (fi < 0 && i + u < total) {
-              s_q = qq[u] != cur_q ? s : s_q;
-              cur_q = qq[u];
+            if (fi < 0 && i + u < nm) {
               const bool sp = en[u].lo == fold::SPECIAL;
               const uint32_t s_sp = fbits(fadd(bitsf(s), bitsf(en[u].a0)));
               const uint32_t ns = s + ((s & 1u) ? en[u].a1 : en[u].a0);  // < 2^31 + 2^30: no wrap
@@ -1636,13 +1688,12 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
           }
         }
         if (fi < 0) break;
-        i = fi;
-        const long long st = (long long)cur_q * a.SL;
-        const long long len = V - st < a.SL ? V - st : a.SL;
-        const void* sub_row = a.dtype == PESTI_BF16 ? (const void*)((const uint16_t*)row + st)
-                                                    : (const void*)((const float*)row + st);
-        s = warp_fold(sub_row, a.dtype, len, s_q, fs.stage, scale, T, m);
-        i = cur_q + 1 < nsub ? eoff[cur_q + 1] : total;  // the next sub-slice's entries
+        const uint32_t from = fi > 0 ? fs.ment[fi - 1].end : 0u;
+        const uint32_t to = fs.ment[fi].end;
+        const void* src = a.dtype == PESTI_BF16 ? (const void*)((const uint16_t*)row + from)
+                                                : (const void*)((const float*)row + from);
+        s = warp_fold(src, a.dtype, (long long)to - from, s, fs.stage, scale, T, m);
+        i = fi + 1;
       }
     }
     __syncthreads();
@@ -1675,7 +1726,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
         }
         // every element outside the candidates (raw < tau) must rank below the keff-th
         const float pk = bitsf((uint32_t)(fs.key[keff - 1] >> 32));
-        ok = fdiv(fs.p_tau, S) < pk;
+        ok = fdiv(ri.e_tau, S) < pk;
       }
       if (ok) {
         // total over the kept list (sampling.rs:81), normalisation (:94), draw (:99-111)

@@ -249,7 +249,7 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
   sa.pool = (pesti::FoldEnt*)(ws + p.o_pool);
   sa.pool_ctr = (int*)(ws + p.o_pctr);
   sa.cand_count = (int*)(ws + p.o_cc);
-  sa.cand_raw = (float*)(ws + p.o_ce);
+  sa.cand_e = (float*)(ws + p.o_ce);
   sa.cand_idx = (uint32_t*)(ws + p.o_ci);
 
   // the fast path stages the row's fold entries in shared memory; with very
@@ -309,7 +309,7 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
   ra.surv_raw = sa.surv_raw;
   ra.surv_idx = sa.surv_idx;
   ra.cand_count = sa.cand_count;
-  ra.cand_raw = sa.cand_raw;
+  ra.cand_e = sa.cand_e;
   ra.cand_idx = sa.cand_idx;
   ra.E = (float*)(ws + p.o_E);
   ra.I = (uint32_t*)(ws + p.o_I);

@@ -901,6 +901,8 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
 // issue slots.
 // ---------------------------------------------------------------------------
 struct ClassShared {
+  float raw[K1_WARPS][GROUP];     // the task's survivors (raw logit, row index)
+  uint32_t idx[K1_WARPS][GROUP];
   float ea[K1_WARPS][GROUP];
   uint32_t ck[K1_WARPS][GROUP];
   uint32_t c0[K1_WARPS][GROUP];
@@ -915,6 +917,8 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
   const int nsub = a.P * K1_WARPS;
   const long long V = a.V;
   const int ntasks = *a.task_count;
+  float* graw = sh.raw[w];
+  uint32_t* gidx = sh.idx[w];
   float* eas = sh.ea[w];
   uint32_t* cks = sh.ck[w];
   uint32_t* c0s = sh.c0[w];
@@ -946,6 +950,12 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
     const long long gbase = b * V + sub * a.SL + (long long)j * GROUP;  // first survivor of the group
     const int n = ssv.count - j * GROUP < GROUP ? ssv.count - j * GROUP : GROUP;
     const float* sraw = a.surv_raw + b * V + sub * a.SL;
+    __syncwarp();  // the previous task is done with the shared arrays
+#pragma unroll 8
+    for (int i = lane; i < n; i += 32) {  // the group's survivors, in one coalesced pass
+      graw[i] = a.surv_raw[gbase + i];
+      gidx[i] = a.surv_idx[gbase + i];
+    }
     // approximate state at the group's start: the prefix mass of the earlier
     // sub-slices plus that of the sub-slice's earlier survivors
     // (exp(x/T - m) = 2^(x c2 - m log2 e); a relative 2^-12 is all it needs)
@@ -954,14 +964,16 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
       const float c2 = 1.4426950408889634f / (scale ? T : 1.0f);
       const float mc = m * 1.4426950408889634f;
       float acc = 0.0f;
+#pragma unroll 4
       for (int i = lane; i < j * GROUP; i += 32) acc += ex2_approx(fmaf(sraw[i], c2, -mc));
       s_approx += (double)warp_reduce_add(acc);
     }
+    __syncwarp();
     if (ssv.pad) {  // the group's top-k candidates (all of them survived)
       const float tau = ri.tau;
       for (int i0 = 0; i0 < n; i0 += 32) {
         const int i = i0 + lane;
-        const float raw = i < n ? sraw[(long long)j * GROUP + i] : 0.0f;
+        const float raw = i < n ? graw[i] : 0.0f;
         const bool cand = i < n && raw >= tau;
         const uint32_t bal = __ballot_sync(PESTI_FULL_MASK, cand);
         if (bal) {
@@ -971,7 +983,7 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
           const int slot = basec + __popc(bal & ((1u << lane) - 1u));
           if (cand && slot < CAND_CAP) {
             a.cand_e[b * CAND_CAP + slot] = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127
-            a.cand_idx[b * CAND_CAP + slot] = a.surv_idx[gbase + i];
+            a.cand_idx[b * CAND_CAP + slot] = gidx[i];
           }
         }
       }
@@ -1004,7 +1016,7 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
         }
       }
       if (need_exact) {
-        const float raw = a.surv_raw[gbase + i];
+        const float raw = graw[i];
         const float ex = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127, exact
         if (special) {
           k0 = fbits(ex);
@@ -1024,7 +1036,7 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
     float ltot = 0.0f;
 #pragma unroll 1
     for (int jj = 0; jj < nl; ++jj) {
-      const float raw = a.surv_raw[gbase + i0 + jj];
+      const float raw = graw[i0 + jj];
       const float e = pesti_expf_approx(fsub(scale ? fdiv(raw, T) : raw, m));
       eas[jj * 32 + lane] = e;
       ltot += e;
@@ -1119,7 +1131,7 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
         uint32_t cur = prev_key;
         bool started = false;
         Seg tr{0u, 0u, 0u, KEY_NONE};
-        auto rend = [&](int i) { return a.surv_idx[gbase + i] + 1u; };  // past survivor i
+        auto rend = [&](int i) { return gidx[i] + 1u; };  // past survivor i
 #pragma unroll 1
         for (int jj = 0; jj < nl; ++jj) {
           const uint32_t k = cks[jj * 32 + lane], k0 = c0s[jj * 32 + lane], k1 = c1s[jj * 32 + lane];
@@ -1144,7 +1156,7 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
           cur = k;
         }
       }
-      if (lane == 0 && last.cnt > 0u) ent[nclosed] = FoldEnt{last.key, last.a0, last.a1, a.surv_idx[gbase + n - 1] + 1u};
+      if (lane == 0 && last.cnt > 0u) ent[nclosed] = FoldEnt{last.key, last.a0, last.a1, gidx[n - 1] + 1u};
     }
     if (lane == 0) a.gsurv[(b * nsub + sub) * a.jmax + j] = GroupEnt{off0, replay ? 0 : netot, replay ? 1 : 0, 0};
   }
@@ -1186,6 +1198,7 @@ struct RowShared {
 
 // Fast-path arrays, placed after RowShared in dynamic shared memory.
 constexpr int FAST_ENTS = 1024;  // fold entries of a row the fast path stages
+constexpr int FAST_PAIRS = 2048; // (sub-slice, group) pairs of a row the fast path stages
 constexpr uint32_t ENT_REPLAY = 0xfffffffdu;  // staged entry: replay the whole sub-slice
 struct FastSmem {
   unsigned long long key[FAST_CAND];
@@ -1196,6 +1209,9 @@ struct FastSmem {
   Seg wseg[K2_NT / 32];        // block-wide segmented scan: per-warp totals and prefixes
   Seg wpre[K2_NT / 32];
   int wfl[K2_NT / 32];
+  uint16_t owner[FAST_ENTS];   // staging: the pair each entry comes from
+  int pstart[FAST_PAIRS];      // staging: each pair's first entry in the row and in the pool
+  int poff[FAST_PAIRS];
   int total;                   // entries of the row (> FAST_ENTS: not staged)
   int nment;                   // merged entries
   // followed by SubSurv[nsub] and int eoff[nsub] (scratch)
@@ -1535,18 +1551,19 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
         if (j < ss[q].ngroups && gs[t].replay) rep[q] = 1;
       }
       __syncthreads();
+      // each pair's place in the row (a block scan), then every entry copied
+      // by its own thread: the loads from the pool are all in flight at once
       int base = 0;
       for (int t0 = 0; t0 < npair; t0 += K2_NT) {
         const int t = t0 + tid;
-        int ne = 0, off = 0, q = 0;
-        bool mark = false;
+        int ne = 0, off = 0;
         if (t < npair) {
-          q = t / a.jmax;
+          const int q = t / a.jmax;
           const int j = t - q * a.jmax;
           if (j < ss[q].ngroups) {
             if (rep[q]) {
               ne = j == 0 ? 1 : 0;
-              mark = true;
+              off = -1 - q;  // replay marker of sub-slice q
             } else {
               const GroupEnt ge = gs[t];
               ne = ge.nent;
@@ -1556,16 +1573,27 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
         }
         int tot;
         const int ex = base + block_excl_scan_add(ne, sh.iscr, tot);
-        if (ne > 0 && ex + ne <= FAST_ENTS) {
-          if (mark) {
-            const long long qend = ((long long)q + 1) * a.SL;
-            fs.ent[ex] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)(qend < V ? qend : V)};
+        if (t < FAST_PAIRS) {
+          fs.pstart[t] = ex;
+          fs.poff[t] = off;
+        }
+        if (t < FAST_PAIRS && ex + ne <= FAST_ENTS)
+          for (int i = 0; i < ne; ++i) fs.owner[ex + i] = (uint16_t)t;
+        base += tot;
+      }
+      if (npair > FAST_PAIRS) base = FAST_ENTS + 1;  // too many pairs to stage: the generic path
+      __syncthreads();
+      if (base <= FAST_ENTS) {
+        for (int e = tid; e < base; e += K2_NT) {
+          const int t = fs.owner[e];
+          const int off = fs.poff[t];
+          if (off < 0) {
+            const long long qend = ((long long)(-1 - off) + 1) * a.SL;
+            fs.ent[e] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)(qend < V ? qend : V)};
           } else {
-#pragma unroll 8
-            for (int i = 0; i < ne; ++i) fs.ent[ex + i] = pool[off + i];  // independent loads overlap
+            fs.ent[e] = pool[off + (e - fs.pstart[t])];
           }
         }
-        base += tot;
       }
       if (tid == 0) fs.total = base;
       __syncthreads();

@@ -368,10 +368,24 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
   const bool scale = T > 0.0f;
   const float t_eff = scale ? T : 1.0f;
   const SubStat* st = a.stats + b * nsub;
+  // the segment maxima (for the candidate threshold) are fetched now, while
+  // the sub-slice statistics are combined
+  constexpr int SEG_REG = 4;
+  const float* segm = a.seg_max + b * a.nseg;
+  const bool seg_in_regs = a.nseg <= (long long)SEG_REG * K1_NT;
+  float segr[SEG_REG];
+#pragma unroll
+  for (int r = 0; r < SEG_REG; ++r) {
+    const long long j = (long long)r * K1_NT + tid;
+    segr[r] = seg_in_regs && j < a.nseg ? segm[j] : NEG_INF;
+  }
   float mx = NEG_INF;
-  long long ln = -1;
+  int ln = -1;
   int f = 0;
-  for (int s = tid; s < MAX_SUBS; s += K1_NT) {
+  constexpr int PERS = MAX_SUBS / K1_NT;
+#pragma unroll
+  for (int r = 0; r < PERS; ++r) {
+    const int s = r * K1_NT + tid;
     const bool has = s < nsub && (long long)s * a.SL < V;
     float mr = NEG_INF, sr = 0.0f;
     if (has) {
@@ -385,21 +399,33 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
     sh.mraw[s] = mr;
     sh.srel[s] = sr;
   }
-  mx = -block_reduce_min(-mx, sh.fscr);
-  ln = block_reduce_max(ln, sh.lscr);
+  // row max, last NaN and flags in one reduction
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) f |= __shfl_xor_sync(PESTI_FULL_MASK, f, o);
-  if (lane == 0) sh.iscr[w] = f;
+  for (int o = 16; o > 0; o >>= 1) {
+    mx = fmaxf(mx, __shfl_xor_sync(PESTI_FULL_MASK, mx, o));
+    const int lo2 = __shfl_xor_sync(PESTI_FULL_MASK, ln, o);
+    ln = ln > lo2 ? ln : lo2;
+    f |= __shfl_xor_sync(PESTI_FULL_MASK, f, o);
+  }
+  if (lane == 0) {
+    sh.fscr[w] = mx;
+    sh.iscr[w] = f;
+    sh.lscr[w] = ln;
+  }
   __syncthreads();
   int fl = 0;
-  for (int q = 0; q < K1_WARPS; ++q) fl |= sh.iscr[q];
+  for (int q = 0; q < K1_WARPS; ++q) {
+    mx = fmaxf(mx, sh.fscr[q]);
+    fl |= sh.iscr[q];
+    ln = ln > (int)sh.lscr[q] ? ln : (int)sh.lscr[q];
+  }
+  __syncthreads();
   long long li = -1, fi = 1LL << 62;
   if (is_greedy(prm)) {
     // first and last index holding the row max: re-scan only the segments
     // whose max it is (usually one)
     if (tid == 0) sh.nmatch = 0;
     __syncthreads();
-    const float* segm = a.seg_max + b * a.nseg;
     for (long long j = tid; j < a.nseg; j += K1_NT) {
       if (segm[j] == mx) {
         const int slot = atomicAdd(&sh.nmatch, 1);
@@ -503,14 +529,20 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
     const long long keff = k < V ? k : V;
     for (int i = tid; i < TAU_BINS; i += K1_NT) sh.hist[i] = 0u;
     __syncthreads();
-    const float* segm = a.seg_max + b * a.nseg;
-    for (long long j0 = 0; j0 < a.nseg; j0 += K1_NT) {
-      const long long j = j0 + tid;
-      const float v = j < a.nseg ? segm[j] : NEG_INF;
-      const bool ok = j < a.nseg && !is_nan(v) && v > NEG_INF;
+    auto add = [&](float v) {  // -inf (also padding) and NaN are not counted
+      const bool ok = !is_nan(v) && v > NEG_INF;
       const uint32_t d = ok ? (fkey(v) >> 20) : (uint32_t)(TAU_BINS + lane);
       const uint32_t peers = __match_any_sync(PESTI_FULL_MASK, d);
       if (ok && (peers & ((1u << lane) - 1u)) == 0u) atomicAdd(&sh.hist[d], (uint32_t)__popc(peers));
+    };
+    if (seg_in_regs) {
+#pragma unroll
+      for (int r = 0; r < SEG_REG; ++r) add(segr[r]);
+    } else {
+      for (long long j0 = 0; j0 < a.nseg; j0 += K1_NT) {
+        const long long j = j0 + tid;
+        add(j < a.nseg ? segm[j] : NEG_INF);
+      }
     }
     __syncthreads();
     constexpr int BPT = TAU_BINS / K1_NT;  // top-down: thread t owns bins [4096-16(t+1), 4096-16t)
@@ -932,11 +964,12 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
   // replayed there, so the band trades entries for replays and never decides
   // a result.
   constexpr float BAND = 0x1p-12f;
+  int t_next = 0;
+  if (lane == 0) t_next = atomicAdd(a.task_next, 1);
   for (;;) {
-    int t = 0;
-    if (lane == 0) t = atomicAdd(a.task_next, 1);
-    t = __shfl_sync(PESTI_FULL_MASK, t, 0);
+    const int t = __shfl_sync(PESTI_FULL_MASK, t_next, 0);
     if (t >= ntasks) break;
+    if (lane == 0) t_next = atomicAdd(a.task_next, 1);  // the next one, while this one runs
     const ClassTask tk = a.tasks[t];
     const long long b = tk.b;
     const long long sub = tk.qj / a.jmax;
@@ -965,6 +998,7 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
       const float mc = m * 1.4426950408889634f;
       float acc = 0.0f;
 #pragma unroll 4
+#pragma unroll 8
       for (int i = lane; i < j * GROUP; i += 32) acc += ex2_approx(fmaf(sraw[i], c2, -mc));
       s_approx += (double)warp_reduce_add(acc);
     }
@@ -1033,19 +1067,68 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
     const int nl = n - i0 < 0 ? 0 : (n - i0 > g ? g : n - i0);  // valid elements of the lane
     __syncwarp();
     // pass A: approximate exps (sampling.rs:46,127 within 2^-22)
-    float ltot = 0.0f;
+    float ltot = 0.0f, lmax = 0.0f;
 #pragma unroll 1
     for (int jj = 0; jj < nl; ++jj) {
       const float raw = graw[i0 + jj];
       const float e = pesti_expf_approx(fsub(scale ? fdiv(raw, T) : raw, m));
       eas[jj * 32 + lane] = e;
       ltot += e;
+      lmax = fmaxf(lmax, e);
     }
     const float lincl = warp_incl_scan_add(ltot);
     // approximate states as floats relative to the carried double (the guard
     // band is 2^-12; float rounding is 2^-24)
     const float sb = (float)s_approx;
     const float lbase = lincl - ltot;
+
+    // A clean group: the whole range of its approximate states lies inside one
+    // binade (within the guard band) and no element is large next to it, so
+    // every element is a plain increment rint(e/w) of one run.  When all of
+    // them are decided by the approximation with no tie, the group's fold is
+    // that run with the sum of the increments: one entry, no segmentation.
+    {
+      const float gtot = __shfl_sync(PESTI_FULL_MASK, lincl, 31);
+      const float gmax = warp_reduce_fmax(lmax);
+      bool clean = false;
+      uint32_t clo = 0u;
+      if (sb >= 0x1p-126f) {
+        clo = fbits(sb) & 0x7f800000u;
+        const float lov = bitsf(clo);
+        clean = sb >= lov * (1.0f + BAND) && sb + gtot <= 2.0f * lov * (1.0f - BAND) &&
+                gmax * (1.0f + DE) < bitsf(clo - 0x00800000u);
+      }
+      if (clean) {
+        const int sh2 = 150 - (int)(clo >> 23);  // w = 2^(E-150)
+        uint32_t ksum = 0u;
+        bool decided = true;
+#pragma unroll 1
+        for (int jj = 0; jj < nl; ++jj) {
+          const float ea = eas[jj * 32 + lane];
+          if (ea == 0.0f) {
+            decided = decided && (clo >> 23) >= 40u;  // exact e < 4.5e-38 rounds to 0 on this grid
+          } else {
+            const float tt = __uint_as_float(fbits(ea) + ((uint32_t)sh2 << 23));  // ea/w, exact scaling
+            const float kr = rintf(tt);
+            const float slack = 0.5f - fabsf(tt - kr);
+            decided = decided && slack > tt * DE + 0x1p-24f;
+            ksum += (uint32_t)kr;
+          }
+        }
+        if (__all_sync(PESTI_FULL_MASK, decided)) {
+          const uint32_t inc = tr_sat(warp_reduce_add(ksum));  // each < 2^22, at most 256 of them
+          int off0 = 0;
+          if (lane == 0) off0 = atomicAdd(a.pool_ctr + b, 1);
+          off0 = __shfl_sync(PESTI_FULL_MASK, off0, 0);
+          const bool full = off0 + 1 > POOL_CAP;
+          if (lane == 0) {
+            if (!full) a.pool[b * POOL_CAP + off0] = FoldEnt{clo, inc, inc, gidx[n - 1] + 1u};
+            a.gsurv[(b * nsub + sub) * a.jmax + j] = GroupEnt{off0, full ? 0 : 1, full ? 1 : 0, 0};
+          }
+          continue;
+        }
+      }
+    }
     // the key of the lane's last element decides whether the next lane's first
     // element continues its run
     uint32_t last_key = KEY_NONE;

@@ -298,7 +298,7 @@ def main():
     peak, peak_kind = measured_peaks()
     achieved = step_bytes / (scan_ms / 1e3) / 1e9
     traffic = None
-    tpath = os.path.join(ROOT, "profiles", "slice_scan_traffic.json")
+    tpath = os.path.join(ROOT, "profiles", "slice_stats_traffic.json")
     if os.path.exists(tpath):
         try:
             traffic = json.load(open(tpath)).get(f"workload{w}")
@@ -370,10 +370,10 @@ def main():
                        "params": "T0.7 top_k50 top_p0.9 (top-p unused since top_k > 0, sampling.rs:66)",
                        "l2": f"rotating {nbuf} input buffers ({nbuf * step_bytes / 2**20:.0f} MiB > 126 MiB L2)",
                        "parallelism": f"rows split, {world} GPU(s), no collective"},
-            "roofline": {"bound": "hbm", "kernel": "slice_max", "achieved": achieved, "peak": peak,
+            "roofline": {"bound": "hbm", "kernel": "slice_stats_kernel", "achieved": achieved, "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": traffic, "bytes_per_launch": step_bytes},
-            "kernel_us": {"slice_max": scan_ms * 1e3, "survivors": surv_ms * 1e3, "row": row_ms * 1e3},
+            "kernel_us": {"slice_stats": scan_ms * 1e3, "survivor+classify": surv_ms * 1e3, "row": row_ms * 1e3},
             "step_hbm_gbs": step_bytes / (ms_per_step / 1e3) / 1e9,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": step_bytes + B * 4,
                     "d2h_bytes_per_step": B * 4},

@@ -184,6 +184,7 @@ def main():
 
     import pesti_sampler as ps
     import synth
+    from rows import max_over_ranks, rank_rows
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -197,7 +198,7 @@ def main():
     w = args.workload
     spec = synth.WORKLOADS[w]
     B, V = spec["B"], spec["V"]
-    rows = range(rank * B, (rank + 1) * B)
+    rows = rank_rows(rank, world, B)
     x = synth.make_logits(w, rows=rows)
     params = synth.params_for(w, B, V)
     u = synth.make_u(w, B)
@@ -271,10 +272,7 @@ def main():
     torch.cuda.synchronize()
     clk = clocks.stop()
     barrier()
-    if world > 1:
-        t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
+    elapsed_ms = max_over_ranks(elapsed_ms, dev)
     ms_per_step = elapsed_ms / args.steps
     value = world * B * args.steps / (elapsed_ms / 1e3)
 
@@ -331,10 +329,7 @@ def main():
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(e2e_ms, dev)
     e2e_value = world * B * e2e_steps / (e2e_ms / 1e3)
 
     # B = 1 latency (workload 1 shape), device-resident logits, host wall clock

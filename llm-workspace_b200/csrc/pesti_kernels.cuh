@@ -737,8 +737,10 @@ __device__ __forceinline__ Seg seg_shfl(Seg s, int src) {
 
 constexpr int K1_STAGES = 4;  // 16-byte loads in flight per lane in the survivor pass
 
+constexpr int K1_LOADS = 2;  // 16-byte loads per lane per chunk of the survivor pass
+
 struct SurvShared {
-  float4 stage[K1_WARPS][K1_STAGES][32];  // chunks on their way from L2 (cp.async)
+  float4 stage[K1_WARPS][K1_STAGES][K1_LOADS][32];  // chunks on their way from L2 (cp.async)
 };
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -805,108 +807,149 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
   // above it every candidate (raw >= tau) survives
   const bool cand_here = fast && !(tau >= fmaxf(bound_a(ri.max_raw), thrLr));
   int* ccount = a.cand_count + b;
-  float4* stg = sh.stage[w][0];
+  float4* stg = &sh.stage[w][0][0][0];
   long long sins = 0;  // survivors stored so far
 
-  constexpr long long CHV = 32LL * VE;  // elements per chunk
-  const long long nchunk = (end - start + CHV - 1) / CHV;
-  const long long nfull = VEC ? (end - start) / CHV : 0;  // chunks read through the pipeline
+  // a chunk is K1_LOADS segments of 32*VE elements, one 16-byte load per lane
+  // each; segment q of chunk c starts at c*CHV + q*SEG, lane l holds its
+  // elements l*VE .. l*VE + VE-1
+  constexpr int SEG = 32 * VE;
+  constexpr int CHV = K1_LOADS * SEG;
+  const int len = (int)(end - start);
+  const int nchunk = (len + CHV - 1) / CHV;
+  const int nfull = VEC ? len / CHV : 0;  // chunks read through the pipeline
+  const TIn* rsub = row + start;
   if (VEC) {
 #pragma unroll
     for (int st = 0; st < K1_STAGES; ++st) {
-      if (st < nfull) cp_async16(&stg[st * 32 + lane], row + start + st * CHV + lane * VE);
+      if (st < nfull)
+#pragma unroll
+        for (int q = 0; q < K1_LOADS; ++q) cp_async16(&stg[(st * K1_LOADS + q) * 32 + lane], rsub + st * CHV + q * SEG + lane * VE);
       cp_async_commit();
     }
   }
-  float segv = NEG_INF;  // segment maxima of chunks c0 + lane, 32 at a time
-  for (long long c = 0; c < nchunk; ++c) {
-    if ((c & 31) == 0) segv = c + lane < nchunk ? segm[c + lane] : NEG_INF;
-    const float segmx = __shfl_sync(PESTI_FULL_MASK, segv, (int)(c & 31));
-    float x[VE];
-    int nv = VE;
+  float segv = NEG_INF;  // segment maxima of segments s0 + lane, 32 at a time
+  uint32_t sins32 = 0u;  // survivors stored so far (< SL)
+  for (int c = 0; c < nchunk; ++c) {
+    if (((c * K1_LOADS) & 31) == 0) {
+      const int s0 = c * K1_LOADS + lane;
+      segv = s0 < (len + SEG - 1) / SEG ? segm[s0] : NEG_INF;
+    }
+    float x[K1_LOADS][VE];
+    int nv[K1_LOADS];
     const bool piped = VEC && c < nfull;
     if (piped) {
       cp_async_wait<K1_STAGES - 1>();  // chunk c has arrived (each lane reads its own bytes)
-      const float4 r4 = stg[(c % K1_STAGES) * 32 + lane];
-      if (sizeof(TIn) == 4) {
-        x[0] = r4.x; x[1] = r4.y; x[2] = r4.z; x[3] = r4.w;
-      } else {
-        const uint32_t wds[4] = {__float_as_uint(r4.x), __float_as_uint(r4.y), __float_as_uint(r4.z),
-                                 __float_as_uint(r4.w)};
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          x[2 * q] = __uint_as_float(wds[q] << 16);
-          x[2 * q + 1] = __uint_as_float(wds[q] & 0xffff0000u);
+      for (int q = 0; q < K1_LOADS; ++q) {
+        const float4 r4 = stg[((c % K1_STAGES) * K1_LOADS + q) * 32 + lane];
+        if (sizeof(TIn) == 4) {
+          x[q][0] = r4.x; x[q][1] = r4.y; x[q][2] = r4.z; x[q][3] = r4.w;
+        } else {
+          const uint32_t wds[4] = {__float_as_uint(r4.x), __float_as_uint(r4.y), __float_as_uint(r4.z),
+                                   __float_as_uint(r4.w)};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            x[q][2 * h] = __uint_as_float(wds[h] << 16);
+            x[q][2 * h + 1] = __uint_as_float(wds[h] & 0xffff0000u);
+          }
         }
+        nv[q] = VE;
       }
     } else {
-      const long long p0 = start + c * CHV + (long long)lane * VE;
-      nv = 0;
 #pragma unroll
-      for (int e = 0; e < VE; ++e) {
-        const long long j = p0 + e;
-        x[e] = j < end ? load_logit<TIn>(row, j) : 0.0f;
-        nv = j < end ? e + 1 : nv;
-      }
-    }
-    // one threshold for both bounds (NaN fails it): bound (a) with the max of
-    // the row before the chunk (exact), bound (b)
-    const float thr = fmaxf(bound_a(run_max), thrLr);
-    run_max = fmaxf(run_max, segmx);
-    bool sv[VE];
-    int cnt = 0;
-#pragma unroll
-    for (int e = 0; e < VE; ++e) {
-      sv[e] = e < nv && x[e] >= thr;
-      cnt += sv[e] ? 1 : 0;
-    }
-    // survivors are stored in row order
-    const int cinc = warp_incl_scan_add(cnt);
-    long long o = sins + (cinc - cnt);
-    const uint32_t p0 = (uint32_t)(start + c * CHV) + (uint32_t)(lane * VE);
-#pragma unroll
-    for (int e = 0; e < VE; ++e) {
-      if (sv[e]) {
-        sraw[o] = x[e];
-        sidx[o] = p0 + (uint32_t)e;
-        ++o;
-      }
-    }
-    sins += __shfl_sync(PESTI_FULL_MASK, cinc, 31);
-    if (!fast) {  // the largest dropped logit (fmaxf skips NaN)
-#pragma unroll
-      for (int e = 0; e < VE; ++e)
-        if (e < nv && !sv[e]) pruned_max = fmaxf(pruned_max, x[e]);
-    }
-    if (cand_here) {  // top-k candidates (their exact exps are taken by the row kernel)
-      int ccnt = 0;
-#pragma unroll
-      for (int e = 0; e < VE; ++e) ccnt += (e < nv && x[e] >= tau) ? 1 : 0;
-      if (__any_sync(PESTI_FULL_MASK, ccnt > 0)) {
-        const int cex0 = warp_incl_scan_add(ccnt);
-        const int ctot = __shfl_sync(PESTI_FULL_MASK, cex0, 31);
-        int basec = 0;
-        if (lane == 0) basec = atomicAdd(ccount, ctot);
-        basec = __shfl_sync(PESTI_FULL_MASK, basec, 0);
-        int slot = basec + cex0 - ccnt;
+      for (int q = 0; q < K1_LOADS; ++q) {
+        const int p0 = c * CHV + q * SEG + lane * VE;
+        nv[q] = 0;
 #pragma unroll
         for (int e = 0; e < VE; ++e) {
-          if (e < nv && x[e] >= tau) {
-            if (slot < CAND_CAP) {
-              a.cand_e[b * CAND_CAP + slot] = pesti_expf_call(fsub(scale ? fdiv(x[e], T) : x[e], m));
-              a.cand_idx[b * CAND_CAP + slot] = p0 + (uint32_t)e;
+          x[q][e] = p0 + e < len ? load_logit<TIn>(rsub, p0 + e) : 0.0f;
+          nv[q] = p0 + e < len ? e + 1 : nv[q];
+        }
+      }
+    }
+    // per segment one threshold for both bounds (NaN fails it): bound (a)
+    // with the max of the row before the segment (exact), bound (b)
+    bool sv[K1_LOADS][VE];
+    uint32_t packed = 0u;
+    float thr_lo = __int_as_float(0x7f800000);
+#pragma unroll
+    for (int q = 0; q < K1_LOADS; ++q) {
+      const float thr = fmaxf(bound_a(run_max), thrLr);
+      thr_lo = fminf(thr_lo, thr);
+      run_max = fmaxf(run_max, __shfl_sync(PESTI_FULL_MASK, segv, (c * K1_LOADS + q) & 31));
+      uint32_t n = 0u;
+#pragma unroll
+      for (int e = 0; e < VE; ++e) {
+        sv[q][e] = e < nv[q] && x[q][e] >= thr;
+        n += sv[q][e] ? 1u : 0u;
+      }
+      packed |= n << (16 * q);
+    }
+    static_assert(K1_LOADS == 2, "segment counts are packed in 16-bit halves");
+    // survivors are stored in row order (segment by segment, lane by lane)
+    const uint32_t incl = warp_incl_scan_add(packed);
+    const uint32_t tot = __shfl_sync(PESTI_FULL_MASK, incl, 31);
+    const uint32_t excl = incl - packed;
+#pragma unroll
+    for (int q = 0; q < K1_LOADS; ++q) {
+      uint32_t o = sins32 + ((excl >> (16 * q)) & 0xffffu) + (q == 1 ? (tot & 0xffffu) : 0u);
+      const uint32_t p0 = (uint32_t)(start + c * CHV + q * SEG + lane * VE);
+#pragma unroll
+      for (int e = 0; e < VE; ++e) {
+        if (sv[q][e]) {
+          sraw[o] = x[q][e];
+          sidx[o] = p0 + (uint32_t)e;
+          ++o;
+        }
+      }
+    }
+    sins32 += (tot & 0xffffu) + (tot >> 16);
+    if (!fast) {  // the largest dropped logit (fmaxf skips NaN)
+#pragma unroll
+      for (int q = 0; q < K1_LOADS; ++q)
+#pragma unroll
+        for (int e = 0; e < VE; ++e)
+          if (e < nv[q] && !sv[q][e]) pruned_max = fmaxf(pruned_max, x[q][e]);
+    }
+    if (cand_here) {  // top-k candidates (their exact exps are taken by the row kernel)
+#pragma unroll
+      for (int q = 0; q < K1_LOADS; ++q) {
+        int ccnt = 0;
+#pragma unroll
+        for (int e = 0; e < VE; ++e) ccnt += (e < nv[q] && x[q][e] >= tau) ? 1 : 0;
+        if (__any_sync(PESTI_FULL_MASK, ccnt > 0)) {
+          const int cex0 = warp_incl_scan_add(ccnt);
+          const int ctot = __shfl_sync(PESTI_FULL_MASK, cex0, 31);
+          int basec = 0;
+          if (lane == 0) basec = atomicAdd(ccount, ctot);
+          basec = __shfl_sync(PESTI_FULL_MASK, basec, 0);
+          int slot = basec + cex0 - ccnt;
+          const uint32_t p0 = (uint32_t)(start + c * CHV + q * SEG + lane * VE);
+#pragma unroll
+          for (int e = 0; e < VE; ++e) {
+            if (e < nv[q] && x[q][e] >= tau) {
+              if (slot < CAND_CAP) {
+                a.cand_e[b * CAND_CAP + slot] = pesti_expf_call(fsub(scale ? fdiv(x[q][e], T) : x[q][e], m));
+                a.cand_idx[b * CAND_CAP + slot] = p0 + (uint32_t)e;
+              }
+              ++slot;
             }
-            ++slot;
           }
         }
       }
     }
+    (void)thr_lo;
     if (piped) {  // the stage just read (its values are used above) takes chunk c + K1_STAGES
-      const long long cn = c + K1_STAGES;
-      if (cn < nfull) cp_async16(&stg[(c % K1_STAGES) * 32 + lane], row + start + cn * CHV + lane * VE);
+      const int cn = c + K1_STAGES;
+      if (cn < nfull)
+#pragma unroll
+        for (int q = 0; q < K1_LOADS; ++q)
+          cp_async16(&stg[((c % K1_STAGES) * K1_LOADS + q) * 32 + lane], rsub + cn * CHV + q * SEG + lane * VE);
       cp_async_commit();
     }
   }
+  sins = sins32;
   if (VEC) cp_async_wait<0>();
   const float pm = warp_reduce_fmax(pruned_max);
   const int ngroups = fast ? (int)((sins + GROUP - 1) / GROUP) : 0;

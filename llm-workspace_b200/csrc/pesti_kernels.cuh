@@ -1007,13 +1007,18 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
   // replayed there, so the band trades entries for replays and never decides
   // a result.
   constexpr float BAND = 0x1p-12f;
-  int t_next = 0;
-  if (lane == 0) t_next = atomicAdd(a.task_next, 1);
+  // Each warp's first task is its own index (a burst of thousands of atomics
+  // on one counter would serialise the start); later ones come from the
+  // counter, claimed while the current task runs.  The list is taken from its
+  // end: the survivor pass queues the tasks of its slowest warps (the dense
+  // start of each row, whose tasks cost the most) last.
+  const int nwarps = (int)gridDim.x * K1_WARPS;
+  int t_next = (int)blockIdx.x * K1_WARPS + w;
   for (;;) {
     const int t = __shfl_sync(PESTI_FULL_MASK, t_next, 0);
     if (t >= ntasks) break;
-    if (lane == 0) t_next = atomicAdd(a.task_next, 1);  // the next one, while this one runs
-    const ClassTask tk = a.tasks[t];
+    if (lane == 0) t_next = nwarps + atomicAdd(a.task_next, 1);  // the next one, while this one runs
+    const ClassTask tk = a.tasks[ntasks - 1 - t];
     const long long b = tk.b;
     const long long sub = tk.qj / a.jmax;
     const int j = tk.qj - (int)sub * a.jmax;

@@ -98,11 +98,12 @@ struct ClassTask {    // one group of GROUP survivors of a sub-slice
   int32_t qj;         // sub-slice * jmax + group
 };
 
-struct GroupEnt {     // classify_kernel, one per task: its fold entries in the row's pool
-  int32_t off;        // first entry
+struct GroupEnt {     // classify_kernel, one per task: its fold entries
+  uint32_t ent[4];    // inl: the task's only entry (a FoldEnt), kept here instead of the pool
+  int32_t off;        // first entry in the row's pool
   int32_t nent;       // entries (0 with replay)
   int32_t replay;     // the pool was full: the row kernel replays the sub-slice
-  int32_t pad;
+  int32_t inl;
 };
 
 struct SliceArgs {
@@ -1012,13 +1013,21 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
   // counter, claimed while the current task runs.  The list is taken from its
   // end: the survivor pass queues the tasks of its slowest warps (the dense
   // start of each row, whose tasks cost the most) last.
+  // The next task's index and record are fetched while a task runs.
   const int nwarps = (int)gridDim.x * K1_WARPS;
-  int t_next = (int)blockIdx.x * K1_WARPS + w;
+  int t = (int)blockIdx.x * K1_WARPS + w;
+  ClassTask tk_next = t < ntasks ? a.tasks[ntasks - 1 - t] : ClassTask{0, 0};
+  int claim = 0;
+  if (lane == 0 && t < ntasks) claim = atomicAdd(a.task_next, 1);
   for (;;) {
-    const int t = __shfl_sync(PESTI_FULL_MASK, t_next, 0);
     if (t >= ntasks) break;
-    if (lane == 0) t_next = nwarps + atomicAdd(a.task_next, 1);  // the next one, while this one runs
-    const ClassTask tk = a.tasks[ntasks - 1 - t];
+    const ClassTask tk = tk_next;
+    const int tn = nwarps + __shfl_sync(PESTI_FULL_MASK, claim, 0);
+    if (tn < ntasks) {
+      tk_next = a.tasks[ntasks - 1 - tn];
+      if (lane == 0) claim = atomicAdd(a.task_next, 1);
+    }
+    t = tn;
     const long long b = tk.b;
     const long long sub = tk.qj / a.jmax;
     const int j = tk.qj - (int)sub * a.jmax;
@@ -1115,14 +1124,13 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
     const int nl = n - i0 < 0 ? 0 : (n - i0 > g ? g : n - i0);  // valid elements of the lane
     __syncwarp();
     // pass A: approximate exps (sampling.rs:46,127 within 2^-22)
-    float ltot = 0.0f, lmax = 0.0f;
+    float ltot = 0.0f;
 #pragma unroll 1
     for (int jj = 0; jj < nl; ++jj) {
       const float raw = graw[i0 + jj];
       const float e = pesti_expf_approx(fsub(scale ? fdiv(raw, T) : raw, m));
       eas[jj * 32 + lane] = e;
       ltot += e;
-      lmax = fmaxf(lmax, e);
     }
     const float lincl = warp_incl_scan_add(ltot);
     // approximate states as floats relative to the carried double (the guard
@@ -1131,20 +1139,20 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
     const float lbase = lincl - ltot;
 
     // A clean group: the whole range of its approximate states lies inside one
-    // binade (within the guard band) and no element is large next to it, so
-    // every element is a plain increment rint(e/w) of one run.  When all of
-    // them are decided by the approximation with no tie, the group's fold is
-    // that run with the sum of the increments: one entry, no segmentation.
+    // binade (within the guard band), so every element is a plain increment
+    // k = rint(e/w) of one run (e < lo there, so k is in the binade's units).
+    // k comes from the approximation where it decides it and from the exact
+    // exp otherwise; unless some element is a tie (its k depends on the
+    // parity of the state), the group's fold is that run with the sum of the
+    // increments: one entry, no segmentation.
     {
       const float gtot = __shfl_sync(PESTI_FULL_MASK, lincl, 31);
-      const float gmax = warp_reduce_fmax(lmax);
       bool clean = false;
       uint32_t clo = 0u;
       if (sb >= 0x1p-126f) {
         clo = fbits(sb) & 0x7f800000u;
         const float lov = bitsf(clo);
-        clean = sb >= lov * (1.0f + BAND) && sb + gtot <= 2.0f * lov * (1.0f - BAND) &&
-                gmax * (1.0f + DE) < bitsf(clo - 0x00800000u);
+        clean = sb >= lov * (1.0f + BAND) && sb + gtot <= 2.0f * lov * (1.0f - BAND);
       }
       if (clean) {
         const int sh2 = 150 - (int)(clo >> 23);  // w = 2^(E-150)
@@ -1153,26 +1161,29 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
 #pragma unroll 1
         for (int jj = 0; jj < nl; ++jj) {
           const float ea = eas[jj * 32 + lane];
+          bool exact = false;
           if (ea == 0.0f) {
-            decided = decided && (clo >> 23) >= 40u;  // exact e < 4.5e-38 rounds to 0 on this grid
+            exact = (clo >> 23) < 40u;  // else: exact e < 4.5e-38 rounds to 0 on this grid
           } else {
             const float tt = __uint_as_float(fbits(ea) + ((uint32_t)sh2 << 23));  // ea/w, exact scaling
             const float kr = rintf(tt);
             const float slack = 0.5f - fabsf(tt - kr);
-            decided = decided && slack > tt * DE + 0x1p-24f;
-            ksum += (uint32_t)kr;
+            if (slack > tt * DE + 0x1p-24f) ksum += (uint32_t)kr;
+            else exact = true;
+          }
+          if (exact) {
+            const float raw = graw[i0 + jj];
+            const float ex = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127, exact
+            const uint32_t k0 = fbits(fadd(bitsf(clo), ex)) - clo;
+            const uint32_t k1 = fbits(fadd(bitsf(clo + 1u), ex)) - (clo + 1u);
+            decided = decided && k0 == k1;
+            ksum += k0;
           }
         }
         if (__all_sync(PESTI_FULL_MASK, decided)) {
           const uint32_t inc = tr_sat(warp_reduce_add(ksum));  // each < 2^22, at most 256 of them
-          int off0 = 0;
-          if (lane == 0) off0 = atomicAdd(a.pool_ctr + b, 1);
-          off0 = __shfl_sync(PESTI_FULL_MASK, off0, 0);
-          const bool full = off0 + 1 > POOL_CAP;
-          if (lane == 0) {
-            if (!full) a.pool[b * POOL_CAP + off0] = FoldEnt{clo, inc, inc, gidx[n - 1] + 1u};
-            a.gsurv[(b * nsub + sub) * a.jmax + j] = GroupEnt{off0, full ? 0 : 1, full ? 1 : 0, 0};
-          }
+          if (lane == 0)
+            a.gsurv[(b * nsub + sub) * a.jmax + j] = GroupEnt{{clo, inc, inc, gidx[n - 1] + 1u}, 0, 1, 0, 1};
           continue;
         }
       }
@@ -1289,7 +1300,8 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
       }
       if (lane == 0 && last.cnt > 0u) ent[nclosed] = FoldEnt{last.key, last.a0, last.a1, gidx[n - 1] + 1u};
     }
-    if (lane == 0) a.gsurv[(b * nsub + sub) * a.jmax + j] = GroupEnt{off0, replay ? 0 : netot, replay ? 1 : 0, 0};
+    if (lane == 0)
+      a.gsurv[(b * nsub + sub) * a.jmax + j] = GroupEnt{{0u, 0u, 0u, 0u}, off0, replay ? 0 : netot, replay ? 1 : 0, 0};
   }
 }
 
@@ -1688,6 +1700,8 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
       for (int t0 = 0; t0 < npair; t0 += K2_NT) {
         const int t = t0 + tid;
         int ne = 0, off = 0;
+        bool inl = false;
+        FoldEnt ient{0u, 0u, 0u, 0u};
         if (t < npair) {
           const int q = t / a.jmax;
           const int j = t - q * a.jmax;
@@ -1699,6 +1713,8 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
               const GroupEnt ge = gs[t];
               ne = ge.nent;
               off = ge.off;
+              inl = ge.inl != 0;
+              ient = FoldEnt{ge.ent[0], ge.ent[1], ge.ent[2], ge.ent[3]};
             }
           }
         }
@@ -1708,8 +1724,14 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
           fs.pstart[t] = ex;
           fs.poff[t] = off;
         }
-        if (t < FAST_PAIRS && ex + ne <= FAST_ENTS)
-          for (int i = 0; i < ne; ++i) fs.owner[ex + i] = (uint16_t)t;
+        if (t < FAST_PAIRS && ex + ne <= FAST_ENTS) {
+          if (inl) {  // a one-entry task keeps its entry in its record
+            fs.ent[ex] = ient;
+            fs.owner[ex] = 0xffffu;
+          } else {
+            for (int i = 0; i < ne; ++i) fs.owner[ex + i] = (uint16_t)t;
+          }
+        }
         base += tot;
       }
       if (npair > FAST_PAIRS) base = FAST_ENTS + 1;  // too many pairs to stage: the generic path
@@ -1717,6 +1739,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
       if (base <= FAST_ENTS) {
         for (int e = tid; e < base; e += K2_NT) {
           const int t = fs.owner[e];
+          if (t == 0xffff) continue;  // staged already
           const int off = fs.poff[t];
           if (off < 0) {
             const long long qend = ((long long)(-1 - off) + 1) * a.SL;

@@ -146,6 +146,42 @@ int pesti_sample_batch_noalloc(const void* d_logits, pesti_dtype dtype, int64_t 
                                uint32_t* d_out_tokens, float* d_kept_p, uint32_t* d_kept_idx,
                                int64_t kept_width, int64_t* d_kept_count, void* stream);
 
+/*
+ * No counterpart in the reference (it has no multi-GPU path).
+ *
+ * Vocabulary-sharded sampling: each of the communicator's ranks holds one
+ * contiguous column range of every row, all ranges V_shard wide and in rank
+ * order (rank r holds columns [r*V_shard, (r+1)*V_shard) of rows that are
+ * world*V_shard long).  Every rank calls pesti_sample_batch_sharded with the
+ * same B, V_shard, params and u (the draws of all B rows), its own shard as
+ * d_logits [B, ld], and receives the tokens and kept lists of ALL B rows.
+ * Results are those of pesti_sample_batch on the whole rows, bit for bit.
+ *
+ * Top-k rows (1 <= top_k <= 256) and greedy rows are sampled without moving
+ * logits: three NCCL all-gathers of per-row summaries (a few hundred bytes
+ * per row and shard).  Other rows (top-p, no filter, larger top_k, NaN, and
+ * the rare row the sharded algorithm cannot settle) take a gathered path:
+ * their shards are all-gathered into whole rows on every rank and sampled
+ * there.  The call synchronizes the stream once, to learn which rows those
+ * are.
+ *
+ * A communicator is made once per rank: one rank calls pesti_comm_id, the
+ * caller broadcasts its PESTI_COMM_ID_BYTES bytes to the others, and every
+ * rank calls pesti_comm_create with them (ncclGetUniqueId /
+ * ncclCommInitRank; NCCL is loaded from libnccl.so.2 on first use).  The
+ * sampler and the communicator must be on the same device.
+ */
+typedef struct pesti_comm pesti_comm;
+#define PESTI_COMM_ID_BYTES 128
+int pesti_comm_id(void* id);
+int pesti_comm_create(int world_size, int rank, const void* id, int device, pesti_comm** out);
+void pesti_comm_destroy(pesti_comm* c);
+int pesti_sample_batch_sharded(pesti_sampler* s, pesti_comm* c, const void* d_logits, pesti_dtype dtype,
+                               int64_t B, int64_t V_shard, int64_t ld, const pesti_sampling_params* params,
+                               int params_per_row, int params_on_device, const float* d_u,
+                               uint32_t* d_out_tokens, float* d_kept_p, uint32_t* d_kept_idx,
+                               int64_t kept_width, int64_t* d_kept_count, void* stream);
+
 /* Message of the last failure on the calling thread ("" if none). */
 const char* pesti_last_error(void);
 

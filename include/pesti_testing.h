@@ -1,0 +1,28 @@
+/*
+ * pesti_testing.h -- test entry points of the sampler library (no
+ * counterpart in the reference).
+ */
+#ifndef PESTI_TESTING_H
+#define PESTI_TESTING_H
+#include "pesti_sampler.h"
+#ifdef __cplusplus
+extern "C" {
+#endif
+/*
+ * The sharded call of pesti_sample_batch_sharded, with `shards` equally wide
+ * vocabulary shards of the whole matrix d_logits [B, ld] (V a multiple of
+ * `shards`) run one after another in this process on the handle's device,
+ * the exchanges being plain device memory instead of NCCL: the sharded
+ * algorithm on one GPU, for tests.  Results are those of pesti_sample_batch.
+ */
+int pesti_sample_batch_sharded_emulated(pesti_sampler* s, int shards, const void* d_logits, pesti_dtype dtype,
+                                        int64_t B, int64_t V, int64_t ld, const pesti_sampling_params* params,
+                                        int params_per_row, int params_on_device, const float* d_u,
+                                        uint32_t* d_out_tokens, float* d_kept_p, uint32_t* d_kept_idx,
+                                        int64_t kept_width, int64_t* d_kept_count, void* stream);
+/* Rows of the handle's last sharded call that took the gathered path. */
+int64_t pesti_last_gathered_rows(pesti_sampler* s);
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -70,7 +70,23 @@ struct RowInfo {      // row prologue, written by the last slice_stats block of 
   long long last_max, first_max, last_nan;  // argmax indices: greedy rows only
   int uniform;        // the softmax sum is NaN or not > 0: all probabilities are 1/V
   float e_tau;        // exact exp(RN(tau/T) - m) when tau is finite, else 0
+  float s_start;      // vocabulary shard: approximate softmax fold state at the shard's first
+                      // column (the mass of the earlier shards); 0 for whole rows
 };
+
+// One vocabulary shard of a row, summarised before the shards are combined
+// (first phase of the sharded path).  Every rank holds one contiguous,
+// equally wide column range; the summaries of all ranks are all-gathered.
+struct ShardSum {
+  float max_raw;          // max of the shard's raw logits (NaN ignored)
+  uint32_t flags;         // MF_* over the shard
+  float tau;              // lower bound of the shard's k-th largest raw logit (-inf: none;
+                          // +inf: not a top-k row)
+  int32_t last_nan;       // shard column of its last NaN, -1
+  double mass;            // approximate softmax mass of the shard relative to 2^(max_raw*c2)
+  long long last_max, first_max;  // shard columns holding its max (greedy rows), -1
+};
+static_assert(sizeof(ShardSum) == 40, "ShardSum is exchanged as raw bytes");
 
 struct SubPre {       // per sub-slice, from the row prologue
   double A;           // approximate softmax mass of the earlier sub-slices
@@ -134,6 +150,12 @@ struct SliceArgs {
   float* cand_e;    // [B][CAND_CAP] exact exps of the top-k candidates (sampling.rs:127)
   uint32_t* cand_idx;
   int fast_enabled; // rows of the fast path keep no survivors (see survivor_kernel)
+  long long V_total;      // length of the whole row (V unless the call is one vocabulary shard)
+  float band;             // relative guard band of the fold classification around binade edges
+  // vocabulary shards (all null / 0 for whole rows)
+  ShardSum* shard_out;        // first phase: the row's shard summary instead of its prologue
+  const ShardSum* shard_all;  // second phase: [G][B] summaries of every shard
+  int shard_G, shard_rank;
 };
 
 struct RowArgs {
@@ -169,7 +191,34 @@ struct RowArgs {
   int64_t* kept_count;
   int* status;       // bit 0: a row needed sort buffers that were not provided
   int fast_enabled;  // the launch provides the fast path's shared memory
+  long long V_total;   // length of the whole row (V unless the call is one vocabulary shard)
+  // vocabulary shard (shard = 1): instead of sampling, each row's fold from
+  // the shard's approximate start state and its top candidates go to an
+  // exchange record, and its merged fold entries are kept for the table walks
+  int shard;
+  long long col0;          // the shard's first column in the whole row
+  unsigned char* rec;      // [B] records of rec_stride bytes: ShardRec + ksh ShardCand
+  long long rec_stride;
+  int ksh;
+  FoldEnt* ment_g;         // [B][FAST_ENTS] merged fold entries
+  int* nment_g;            // [B] their count (-1: the row is not sampled from shards)
 };
+
+// Exchange record of one row of one vocabulary shard (second phase).
+enum : uint32_t { SH_OK = 0u, SH_SKIP = 1u, SH_FAIL = 2u };
+struct ShardRec {
+  double delta;     // exact fold of the shard's softmax terms from s_start, minus s_start
+  float s_start;    // the approximate state the fold started from
+  uint32_t status;  // SH_OK; SH_SKIP: not a sharded row; SH_FAIL: the row needs the gathered path
+  float bound;      // every element of the shard not listed has an exp <= bound
+  int32_t n;        // candidates listed (at most ksh), by (exp desc, column asc)
+  uint32_t pad[2];
+};
+struct ShardCand {
+  uint32_t e_bits;  // exact exp (sampling.rs:127)
+  uint32_t col;     // column in the whole row
+};
+static_assert(sizeof(ShardRec) == 32 && sizeof(ShardCand) == 8, "records are exchanged as raw bytes");
 
 __device__ __forceinline__ pesti_sampling_params row_params(const pesti_sampling_params& uni,
                                                             const pesti_sampling_params* per_row,
@@ -357,12 +406,74 @@ struct StatsShared {
   int last;
 };
 
+// Candidate threshold: a lower bound of the k-th largest raw logit among the
+// call's columns, from the segment maxima (maxima of disjoint segments are
+// distinct elements), rounded down to the start of its 12-bit key bin; -inf
+// when there are fewer than k segments.  Every thread of the block calls it.
+template <int SEG_REG>
+__device__ float kth_lower_bound(const SliceArgs& a, const float* segm, const float (&segr)[SEG_REG],
+                                 bool seg_in_regs, long long keff, StatsShared& sh) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  for (int i = tid; i < TAU_BINS; i += K1_NT) sh.hist[i] = 0u;
+  __syncthreads();
+  auto add = [&](float v) {  // -inf (also padding) and NaN are not counted
+    const bool ok = !is_nan(v) && v > NEG_INF;
+    const uint32_t d = ok ? (fkey(v) >> 20) : (uint32_t)(TAU_BINS + lane);
+    const uint32_t peers = __match_any_sync(PESTI_FULL_MASK, d);
+    if (ok && (peers & ((1u << lane) - 1u)) == 0u) atomicAdd(&sh.hist[d], (uint32_t)__popc(peers));
+  };
+  if (seg_in_regs) {
+#pragma unroll
+    for (int r = 0; r < SEG_REG; ++r) add(segr[r]);
+  } else {
+    for (long long j0 = 0; j0 < a.nseg; j0 += K1_NT) {
+      const long long j = j0 + tid;
+      add(j < a.nseg ? segm[j] : NEG_INF);
+    }
+  }
+  __syncthreads();
+  constexpr int BPT = TAU_BINS / K1_NT;  // top-down: thread t owns bins [4096-16(t+1), 4096-16t)
+  uint32_t loc = 0;
+#pragma unroll
+  for (int q = 0; q < BPT; ++q) loc += sh.hist[TAU_BINS - 1 - BPT * tid - q];
+  uint32_t tot;
+  const uint32_t ex = block_excl_scan_add(loc, sh.uscr, tot);
+  if (tid == 0) sh.tau = NEG_INF;
+  __syncthreads();
+  if ((long long)ex < keff && (long long)(ex + loc) >= keff) {
+    uint32_t cum = ex;
+    for (int q = 0; q < BPT; ++q) {
+      const int bin = TAU_BINS - 1 - BPT * tid - q;
+      cum += sh.hist[bin];
+      if ((long long)cum >= keff) {
+        sh.tau = fkey_inv((uint32_t)bin << 20);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  return sh.tau;
+}
+
 // Everything that needs every sub-slice of the row: run by the last block.
+// Three forms:
+//  - whole rows: the row prologue (RowInfo and the per-sub-slice SubPre);
+//  - first phase of a vocabulary shard (a.shard_out): the shard's summary
+//    (its max, flags, approximate mass, candidate threshold and, for greedy
+//    rows, the columns of its max) instead;
+//  - second phase (a.shard_all): the row prologue of this shard with the row
+//    max, flags, candidate threshold and argmax taken over every shard's
+//    summary, and the prefix mass and prefix max of every sub-slice starting
+//    from those of the earlier shards.
 template <typename TIn, int VE>
 __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int nsub = a.P * K1_WARPS;
-  const long long V = a.V;
+  const long long V = a.V;         // columns of this call (one shard's, when sharded)
+  const long long VT = a.V_total;  // length of the whole row
+  const bool summary = a.shard_out != nullptr;
+  const bool sharded = a.shard_all != nullptr;
   const float NEG_INF = -__int_as_float(0x7f800000), INF = __int_as_float(0x7f800000);
   const pesti_sampling_params prm = row_params(a.uni, a.per_row, b);
   const float T = prm.temperature;
@@ -378,7 +489,7 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
 #pragma unroll
   for (int r = 0; r < SEG_REG; ++r) {
     const long long j = (long long)r * K1_NT + tid;
-    segr[r] = seg_in_regs && j < a.nseg ? segm[j] : NEG_INF;
+    segr[r] = !sharded && seg_in_regs && j < a.nseg ? segm[j] : NEG_INF;
   }
   float mx = NEG_INF;
   int ln = -1;
@@ -422,7 +533,38 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
   }
   __syncthreads();
   long long li = -1, fi = 1LL << 62;
-  if (is_greedy(prm)) {
+  long long lnl = ln;   // last NaN (row index)
+  double ex0 = 0.0;     // approximate mass of the earlier shards
+  float pmax0 = NEG_INF;  // their max
+  float tau_all = INF;    // the candidate threshold over every shard
+  if (sharded) {
+    // combine the shards' summaries (each thread reads all of them)
+    const float c2 = 1.4426950408889634f / t_eff;
+    float gmx = NEG_INF, tmax = NEG_INF;
+    uint32_t gfl = 0u;
+    lnl = -1;
+    for (int r = 0; r < a.shard_G; ++r) {
+      const ShardSum q = a.shard_all[(long long)r * a.B + b];
+      gmx = fmaxf(gmx, q.max_raw);
+      gfl |= q.flags;
+      tmax = fmaxf(tmax, q.tau);
+      if (q.last_nan >= 0) lnl = (long long)r * V + q.last_nan;
+    }
+    for (int r = 0; r < a.shard_G; ++r) {
+      const ShardSum q = a.shard_all[(long long)r * a.B + b];
+      if (q.max_raw == gmx) {  // greedy rows: the columns of the row max
+        if (q.first_max >= 0 && fi == (1LL << 62)) fi = (long long)r * V + q.first_max;
+        if (q.last_max >= 0) li = (long long)r * V + q.last_max;
+      }
+      if (r < a.shard_rank) {
+        pmax0 = fmaxf(pmax0, q.max_raw);
+        if (q.max_raw > NEG_INF) ex0 += exp2((double)(q.max_raw * c2) - (double)(gmx * c2)) * q.mass;
+      }
+    }
+    mx = gmx;
+    fl = (int)gfl;
+    tau_all = tmax;
+  } else if (is_greedy(prm)) {
     // first and last index holding the row max: re-scan only the segments
     // whose max it is (usually one)
     if (tid == 0) sh.nmatch = 0;
@@ -455,9 +597,38 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
     li = block_reduce_max(li, sh.lscr);
     fi = block_reduce_min(fi, sh.lscr);
   }
+  const long long k = (long long)prm.top_k;
+  const long long keff = k < VT ? k : VT;
+  if (summary) {
+    // the shard's approximate mass relative to its own max, and its candidate threshold
+    const float c2 = 1.4426950408889634f / t_eff;
+    const float ym = mx * c2;
+    constexpr int PER = MAX_SUBS / K1_NT;
+    double lsum = 0.0;
+#pragma unroll
+    for (int r = 0; r < PER; ++r) {
+      const float mm = sh.mraw[tid * PER + r];
+      lsum += mm > NEG_INF ? (double)exp2f(mm * c2 - ym) * (double)sh.srel[tid * PER + r] : 0.0;
+    }
+    const double mass = block_reduce_add(lsum, sh.dscr);
+    float tau = INF;
+    if (!is_greedy(prm) && fast_topk(prm, VT)) tau = kth_lower_bound<SEG_REG>(a, segm, segr, seg_in_regs, keff, sh);
+    if (tid == 0) {
+      ShardSum q;
+      q.max_raw = mx;
+      q.flags = (uint32_t)fl;
+      q.tau = tau;
+      q.last_nan = ln;
+      q.mass = mass;
+      q.last_max = li;
+      q.first_max = fi < (1LL << 62) ? fi : -1;
+      a.shard_out[b] = q;
+    }
+    return;
+  }
   const float m = scale ? fdiv(mx, T) : mx;  // sampling.rs:46 on the max element
   const bool uniform = (fl & MF_NAN) || (scale && T == INF && (fl & (MF_POSINF | MF_NEGINF))) ||
-                       !(fabsf(m) < INF) || V <= 0;
+                       !(fabsf(m) < INF) || VT <= 0;
   const bool need_pre = !is_greedy(prm) && !uniform;
   if (need_pre) {
     // exclusive prefix of the approximate softmax mass and of the max, per sub-slice
@@ -478,7 +649,7 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
       run = fmaxf(run, mm);
     }
     double dt;
-    double ex = block_excl_scan_add(lsum, sh.dscr, dt);
+    double ex = ex0 + block_excl_scan_add(lsum, sh.dscr, dt);
     float inc = run;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -487,7 +658,7 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
     }
     if (lane == 31) sh.fscr[w] = inc;
     __syncthreads();
-    float wpre = NEG_INF;
+    float wpre = pmax0;
     for (int q = 0; q < w; ++q) wpre = fmaxf(wpre, sh.fscr[q]);
     float exc = __shfl_up_sync(PESTI_FULL_MASK, inc, 1);
     if (lane == 0) exc = NEG_INF;
@@ -500,7 +671,7 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
     // of x/T and of the difference are below eta/8), so the exact exp is below
     // e^-17.36 L (1 + 2^-24) < 0.99 * 2^-25 L.  Rounded toward -inf.
     const bool sum_ok = sum_pruning_ok(prm);
-    const double lfac = (1.0 - (double)V * 0x1p-24) * (1.0 - 0x1p-10) * exp2(-0x1p-20 * ((double)fabsf(ym) + 64.0));
+    const double lfac = (1.0 - (double)VT * 0x1p-24) * (1.0 - 0x1p-10) * exp2(-0x1p-20 * ((double)fabsf(ym) + 64.0));
 #pragma unroll
     for (int r = 0; r < PER; ++r) {
       const int s = tid * PER + r;
@@ -521,53 +692,9 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
       pmax = fmaxf(pmax, lmx[r]);
     }
   }
-  // candidate threshold: a lower bound of the k-th largest raw logit, from the
-  // segment maxima (maxima of disjoint segments are distinct elements),
-  // rounded down to the start of its 12-bit key bin
   float tau = INF;
-  const long long k = (long long)prm.top_k;
-  if (need_pre && fast_topk(prm, V)) {
-    const long long keff = k < V ? k : V;
-    for (int i = tid; i < TAU_BINS; i += K1_NT) sh.hist[i] = 0u;
-    __syncthreads();
-    auto add = [&](float v) {  // -inf (also padding) and NaN are not counted
-      const bool ok = !is_nan(v) && v > NEG_INF;
-      const uint32_t d = ok ? (fkey(v) >> 20) : (uint32_t)(TAU_BINS + lane);
-      const uint32_t peers = __match_any_sync(PESTI_FULL_MASK, d);
-      if (ok && (peers & ((1u << lane) - 1u)) == 0u) atomicAdd(&sh.hist[d], (uint32_t)__popc(peers));
-    };
-    if (seg_in_regs) {
-#pragma unroll
-      for (int r = 0; r < SEG_REG; ++r) add(segr[r]);
-    } else {
-      for (long long j0 = 0; j0 < a.nseg; j0 += K1_NT) {
-        const long long j = j0 + tid;
-        add(j < a.nseg ? segm[j] : NEG_INF);
-      }
-    }
-    __syncthreads();
-    constexpr int BPT = TAU_BINS / K1_NT;  // top-down: thread t owns bins [4096-16(t+1), 4096-16t)
-    uint32_t loc = 0;
-#pragma unroll
-    for (int q = 0; q < BPT; ++q) loc += sh.hist[TAU_BINS - 1 - BPT * tid - q];
-    uint32_t tot;
-    const uint32_t ex = block_excl_scan_add(loc, sh.uscr, tot);
-    if (tid == 0) sh.tau = NEG_INF;
-    __syncthreads();
-    if ((long long)ex < keff && (long long)(ex + loc) >= keff) {
-      uint32_t cum = ex;
-      for (int q = 0; q < BPT; ++q) {
-        const int bin = TAU_BINS - 1 - BPT * tid - q;
-        cum += sh.hist[bin];
-        if ((long long)cum >= keff) {
-          sh.tau = fkey_inv((uint32_t)bin << 20);
-          break;
-        }
-      }
-    }
-    __syncthreads();
-    tau = sh.tau;
-  }
+  if (need_pre && fast_topk(prm, VT))
+    tau = sharded ? tau_all : kth_lower_bound<SEG_REG>(a, segm, segr, seg_in_regs, keff, sh);
   if (tid == 0) {
     RowInfo ri;
     ri.max_raw = mx;
@@ -576,9 +703,10 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
     ri.flags = (uint32_t)fl;
     ri.last_max = li;
     ri.first_max = fi < (1LL << 62) ? fi : -1;
-    ri.last_nan = ln;
+    ri.last_nan = lnl;
     ri.uniform = uniform ? 1 : 0;
     ri.e_tau = tau > NEG_INF && tau < INF ? pesti_expf_call(fsub(scale ? fdiv(tau, T) : tau, m)) : 0.0f;
+    ri.s_start = (float)ex0;
     a.info[b] = ri;
   }
 }
@@ -674,6 +802,15 @@ __global__ void __launch_bounds__(K1_NT) slice_stats_kernel(SliceArgs a) {
   __threadfence();
   row_prologue<TIn, VE>(a, b, sh);
   if (threadIdx.x == 0) a.row_ctr[b] = 0;
+}
+
+// Second phase of a vocabulary shard: the row prologue of the shard once the
+// summaries of every shard are in a.shard_all (one block per row).
+template <typename TIn, int VE>
+__global__ void __launch_bounds__(K1_NT) shard_prologue_kernel(SliceArgs a) {
+  __shared__ StatsShared sh;
+  grid_dep_launch_next();
+  row_prologue<TIn, VE>(a, (long long)blockIdx.x, sh);
 }
 
 // ---------------------------------------------------------------------------
@@ -803,7 +940,7 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
   const float* segm = a.seg_max + b * a.nseg + start / (32LL * VE);
   float run_max = pr.P;
   float pruned_max = NEG_INF;
-  const bool fast = a.fast_enabled && fast_topk(prm, V);
+  const bool fast = a.fast_enabled && fast_topk(prm, a.V_total);
   // the largest threshold any chunk can use is that of the row max: with tau
   // above it every candidate (raw >= tau) survives
   const bool cand_here = fast && !(tau >= fmaxf(bound_a(ri.max_raw), thrLr));
@@ -1002,12 +1139,13 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
   // e_exact lies within a relative 2*RELERR of the approximation (margin for
   // the float arithmetic of the bounds below)
   constexpr float DE = 2.0f * PESTI_EXPF_APPROX_RELERR;
-  // Guard band around binade edges.  The approximate state tracks the fold
-  // within about 1.2e-4 (its bias is the mass that the fold absorbs); a run
+  // Guard band around binade edges (2^-12 for whole rows).  The approximate
+  // state tracks the fold within about 1.2e-4 on a row of 128k (its bias is
+  // the mass that the fold absorbs, and it grows along the row); a run
   // predicted in the wrong binade fails its check in the row kernel and is
   // replayed there, so the band trades entries for replays and never decides
   // a result.
-  constexpr float BAND = 0x1p-12f;
+  const float BAND = a.band;
   // Each warp's first task is its own index (a burst of thousands of atomics
   // on one counter would serialise the start); later ones come from the
   // counter, claimed while the current task runs.  The list is taken from its
@@ -1600,6 +1738,21 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
   const SubSurv* survs = a.surv + b * nsub;
   const uint32_t fl = ri.flags;
 
+  const long long VT = a.V_total;
+  if (a.shard) {
+    // of a vocabulary shard, only rows of the fast top-k path are sampled
+    // through exchange records; the others are marked for the gathered path
+    const bool ok = V > 0 && !is_greedy(prm) && !ri.uniform && a.fast_enabled && fast_topk(prm, VT);
+    if (!ok) {
+      if (tid == 0) {
+        ShardRec* rc = reinterpret_cast<ShardRec*>(a.rec + b * a.rec_stride);
+        *rc = ShardRec{0.0, 0.0f, SH_SKIP, 0.0f, 0, {0u, 0u}};
+        a.nment_g[b] = -1;
+      }
+      return;
+    }
+  }
+
   if (V <= 0) {  // empty slice: sample() and argmax() return 0
     if (tid == 0) {
       a.out[b] = 0u;
@@ -1671,14 +1824,14 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
   }
 
   // ---------------- fast path: explicit top-k of at most FAST_K (one warp) ----------------
-  if (a.fast_enabled && fast_topk(prm, V)) {
+  if (a.fast_enabled && fast_topk(prm, VT)) {
     FastSmem& fs = *reinterpret_cast<FastSmem*>(row_smem + sizeof(RowShared));
     SubSurv* ss = reinterpret_cast<SubSurv*>(row_smem + sizeof(RowShared) + sizeof(FastSmem));
     int* eoff = reinterpret_cast<int*>(ss + nsub);
     // stage the row's fold entries, compacted, with the whole block: one
     // thread per (sub-slice, group) pair in row order; a sub-slice with an
     // overflowed group stages a single replay marker
-    const long long keff = k < V ? k : V;
+    const long long keff = k < VT ? k : VT;
     {
       const GroupEnt* gs = a.gsurv + b * nsub * a.jmax;
       const FoldEnt* pool = a.pool + b * POOL_CAP;
@@ -1822,7 +1975,9 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
       __syncthreads();
     }
     const int C = a.cand_count[b];
-    const bool cand_ok = C >= keff && C <= FAST_CAND;
+    // a shard lists any number of candidates up to FAST_CAND (the row's k-th
+    // largest may lie in another shard)
+    const bool cand_ok = (a.shard || C >= keff) && C <= FAST_CAND;
     if (wid == 1 && fs.total <= FAST_ENTS && cand_ok) {
       // candidates by (e desc, index asc) while warp 0 folds; the order by p
       // = e/S differs only inside groups of equal p (fixed up below)
@@ -1842,7 +1997,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
       }
 
     }
-    uint32_t s = 0u;
+    uint32_t s = a.shard ? fbits(ri.s_start) : 0u;
     if (wid == 0 && fs.total <= FAST_ENTS) {
       // softmax denominator (sampling.rs:128): walk the merged entries with the
       // exact state.  An entry the state does not fit (or a replay marker) is folded from
@@ -1879,6 +2034,36 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
       }
     }
     __syncthreads();
+    if (a.shard) {
+      // exchange record: the exact fold from the approximate start, the top
+      // ksh candidates with their columns in the whole row, and a bound on
+      // every element not listed (the next candidate's exp, or exp(tau) above
+      // every non-candidate)
+      if (wid == 0) {
+        ShardRec* rc = reinterpret_cast<ShardRec*>(a.rec + b * a.rec_stride);
+        ShardCand* cd = reinterpret_cast<ShardCand*>(rc + 1);
+        const bool ok = fs.total <= FAST_ENTS && cand_ok;
+        const int nl = ok ? (C < a.ksh ? C : a.ksh) : 0;
+        for (int j = lane; j < nl; j += 32) {
+          const unsigned long long kv = fs.key[j];
+          cd[j] = ShardCand{(uint32_t)(kv >> 32), ~(uint32_t)(kv & 0xffffffffull) + (uint32_t)a.col0};
+        }
+        if (ok)
+          for (int i = lane; i < fs.nment; i += 32) a.ment_g[b * FAST_ENTS + i] = fs.ment[i];
+        if (lane == 0) {
+          ShardRec r;
+          r.delta = ok ? (double)bitsf(s) - (double)ri.s_start : 0.0;
+          r.s_start = ri.s_start;
+          r.status = ok ? SH_OK : SH_FAIL;
+          r.bound = ok && C > a.ksh ? bitsf((uint32_t)(fs.key[a.ksh] >> 32)) : ri.e_tau;
+          r.n = nl;
+          r.pad[0] = r.pad[1] = 0u;
+          *rc = r;
+          a.nment_g[b] = ok ? fs.nment : -1;
+        }
+      }
+      return;
+    }
     if (wid == 0 && fs.total <= FAST_ENTS) {
       const float S = bitsf(s);
       bool ok = cand_ok;

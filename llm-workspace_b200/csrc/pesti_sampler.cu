@@ -3,16 +3,23 @@
 // in pesti_kernels.cuh.
 #include <cuda_runtime.h>
 
+#include <dlfcn.h>
+#include <nccl.h>
+
 #include <algorithm>
 #include <atomic>
+#include <climits>
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "../../include/pesti_sampler.h"
 #include "../../include/pesti_profile.h"
+#include "../../include/pesti_testing.h"
 #include "pesti_kernels.cuh"
 #include "pesti_noalloc.h"
+#include "pesti_shard.cuh"
 
 namespace {
 
@@ -43,6 +50,10 @@ struct pesti_sampler {
   cudaStream_t stream = nullptr;
   void* ws = nullptr;
   size_t ws_bytes = 0;
+  // rows whose completion counters (at the start of the workspace) are known
+  // to be zero: the kernels leave the counters of their own call zero, and
+  // the rest of the workspace may hold anything
+  long long ctr_zero_rows = 0;
   pesti_sampling_params* d_params = nullptr;
   size_t d_params_cap = 0;
   pesti_sampling_params* h_params = nullptr;  // pinned staging
@@ -59,6 +70,8 @@ struct pesti_sampler {
   bool prof = false;
   int prof_n = 0;
   cudaEvent_t prof_ev[kProfMax][4] = {};
+  // rows of the last sharded call that took the gathered path
+  long long last_gathered_rows = 0;
 };
 
 namespace {
@@ -99,6 +112,15 @@ int ensure_ws(pesti_sampler* s, size_t bytes) {
   e = cudaMemset(s->ws, 0, want);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(workspace)");
   s->ws_bytes = want;
+  s->ctr_zero_rows = LLONG_MAX;
+  return PESTI_OK;
+}
+
+// The completion counters of B rows at the start of the workspace are zero
+// on the stream before the first kernel of the call.
+int zero_counters(pesti_sampler* s, long long B, cudaStream_t st) {
+  if (B > s->ctr_zero_rows)
+    PESTI_CUDA_TRY(cudaMemsetAsync(s->ws, 0, (size_t)B * sizeof(int), st), "cudaMemsetAsync(counters)");
   return PESTI_OK;
 }
 
@@ -212,17 +234,11 @@ Plan make_plan(int num_sms, pesti_dtype dtype, long long B, long long V, bool so
   return p;
 }
 
-// Enqueues the three passes of one batch call on `st` over workspace `ws`
-// (laid out by `p`).  pev: four events bracketing the passes, or null.
-int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* d_logits,
-             pesti_dtype dtype, long long B, long long V, long long ld,
-             const pesti_sampling_params& uni, const pesti_sampling_params* d_per_row,
-             const float* d_u, uint32_t* d_out, float* d_kept_p, uint32_t* d_kept_idx,
-             long long kept_width, int64_t* d_kept_count, cudaStream_t st) {
-  const int esize = dtype == PESTI_BF16 ? 2 : 4;
-  const bool sorted_bufs = p.sorted_bufs;
-
-  pesti::SliceArgs sa;
+// Arguments of the slice kernels over workspace `ws` laid out by `p`.
+pesti::SliceArgs make_slice_args(const Plan& p, char* ws, const void* d_logits, pesti_dtype dtype, long long B,
+                                 long long V, long long ld, const pesti_sampling_params& uni,
+                                 const pesti_sampling_params* d_per_row) {
+  pesti::SliceArgs sa{};
   sa.logits = d_logits;
   sa.dtype = (int)dtype;
   sa.B = B;
@@ -251,16 +267,26 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
   sa.cand_count = (int*)(ws + p.o_cc);
   sa.cand_e = (float*)(ws + p.o_ce);
   sa.cand_idx = (uint32_t*)(ws + p.o_ci);
-
+  sa.V_total = V;
+  sa.band = 0x1p-12f;
   // the fast path stages the row's fold entries in shared memory; with very
   // many sub-slices it does not fit and all rows take the generic path
   const size_t fast_bytes = pesti::fast_smem_bytes((int)p.nsub);
   sa.fast_enabled = sizeof(pesti::RowShared) + fast_bytes <= kRowSmemLimit ? 1 : 0;
+  return sa;
+}
 
-  if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[0], st), "cudaEventRecord(profile)");
-  const bool aligned = ((uintptr_t)d_logits % 16 == 0) && ((ld * esize) % 16 == 0);
-  const dim3 g1((unsigned)(p.g.P * B));
-  if (dtype == PESTI_BF16) {
+bool rows_aligned(const void* d_logits, pesti_dtype dtype, long long ld) {
+  const int esize = dtype == PESTI_BF16 ? 2 : 4;
+  return ((uintptr_t)d_logits % 16 == 0) && ((ld * esize) % 16 == 0);
+}
+
+// The HBM pass (slice_stats_kernel): row prologues, or shard summaries when
+// sa.shard_out is set.
+int launch_slice_stats(const Plan& p, const pesti::SliceArgs& sa, cudaStream_t st) {
+  const bool aligned = rows_aligned(sa.logits, (pesti_dtype)sa.dtype, sa.ld);
+  const dim3 g1((unsigned)(p.g.P * sa.B));
+  if (sa.dtype == PESTI_BF16) {
     if (aligned) pesti::slice_stats_kernel<uint16_t, 8, 4, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
     else pesti::slice_stats_kernel<uint16_t, 8, 4, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
   } else {
@@ -269,10 +295,17 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "slice_stats_kernel launch");
-  if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[1], st), "cudaEventRecord(profile)");
+  return PESTI_OK;
+}
+
+// The survivor and classification passes.
+int launch_survivors(const Plan& p, const pesti::SliceArgs& sa, cudaStream_t st) {
+  const bool aligned = rows_aligned(sa.logits, (pesti_dtype)sa.dtype, sa.ld);
+  const dim3 g1((unsigned)(p.g.P * sa.B));
   // the survivor pass reads from L2: fewer loads in flight, smaller code
   const dim3 b1(pesti::K1_NT);
-  if (dtype == PESTI_BF16) {
+  cudaError_t e;
+  if (sa.dtype == PESTI_BF16) {
     if (aligned) e = launch_dependent(pesti::survivor_kernel<uint16_t, 8, true>, g1, b1, 0, st, sa);
     else e = launch_dependent(pesti::survivor_kernel<uint16_t, 8, false>, g1, b1, 0, st, sa);
   } else {
@@ -282,16 +315,24 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "survivor_kernel launch");
   // classification tasks: a persistent grid takes them from a counter
-  {
-    const long long most = (long long)B * p.nsub * p.jmax;
-    const long long blocks = std::min<long long>(4LL * p.num_sms, (most + pesti::K1_WARPS - 1) / pesti::K1_WARPS);
-    e = launch_dependent(pesti::classify_kernel, dim3((unsigned)std::max(1LL, blocks)), b1, 0, st, sa);
-    if (e == cudaSuccess) e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "classify_kernel launch");
-  }
-  if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[2], st), "cudaEventRecord(profile)");
+  const long long most = (long long)sa.B * p.nsub * p.jmax;
+  const long long blocks = std::min<long long>(4LL * p.num_sms, (most + pesti::K1_WARPS - 1) / pesti::K1_WARPS);
+  e = launch_dependent(pesti::classify_kernel, dim3((unsigned)std::max(1LL, blocks)), b1, 0, st, sa);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "classify_kernel launch");
+  return PESTI_OK;
+}
 
-  pesti::RowArgs ra;
+// Arguments of the row kernel for the slice arguments `sa`.
+pesti::RowArgs make_row_args(const Plan& p, char* ws, const pesti::SliceArgs& sa, const float* d_u, uint32_t* d_out,
+                             float* d_kept_p, uint32_t* d_kept_idx, long long kept_width, int64_t* d_kept_count) {
+  const bool sorted_bufs = p.sorted_bufs;
+  const void* d_logits = sa.logits;
+  const pesti_dtype dtype = (pesti_dtype)sa.dtype;
+  const long long B = sa.B, V = sa.V, ld = sa.ld;
+  const pesti_sampling_params uni = sa.uni;
+  const pesti_sampling_params* d_per_row = sa.per_row;
+  pesti::RowArgs ra{};
   ra.logits = d_logits;
   ra.dtype = (int)dtype;
   ra.B = B;
@@ -326,14 +367,40 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
   ra.kept_count = d_kept_count;
   ra.status = (int*)(ws + p.o_status);
   ra.fast_enabled = sa.fast_enabled;
-  const size_t smem2 = sizeof(pesti::RowShared) + (ra.fast_enabled ? fast_bytes : 0);
+  ra.V_total = sa.V_total;
+  return ra;
+}
+
+int launch_row(const Plan& p, int device, const pesti::RowArgs& ra, cudaStream_t st) {
+  const size_t smem2 = sizeof(pesti::RowShared) + (ra.fast_enabled ? pesti::fast_smem_bytes((int)p.nsub) : 0);
   if (smem2 > 48 * 1024) {
     int rc = ensure_row_smem_limit(device);
     if (rc) return rc;
   }
-  e = launch_dependent(pesti::row_kernel, dim3((unsigned)B), dim3(pesti::K2_NT), smem2, st, ra);
+  cudaError_t e = launch_dependent(pesti::row_kernel, dim3((unsigned)ra.B), dim3(pesti::K2_NT), smem2, st, ra);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "row_kernel launch");
+  return PESTI_OK;
+}
+
+// Enqueues the four passes of one batch call on `st` over workspace `ws`
+// (laid out by `p`).  pev: four events bracketing the passes, or null.
+int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* d_logits,
+             pesti_dtype dtype, long long B, long long V, long long ld,
+             const pesti_sampling_params& uni, const pesti_sampling_params* d_per_row,
+             const float* d_u, uint32_t* d_out, float* d_kept_p, uint32_t* d_kept_idx,
+             long long kept_width, int64_t* d_kept_count, cudaStream_t st) {
+  const pesti::SliceArgs sa = make_slice_args(p, ws, d_logits, dtype, B, V, ld, uni, d_per_row);
+  if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[0], st), "cudaEventRecord(profile)");
+  int rc = launch_slice_stats(p, sa, st);
+  if (rc) return rc;
+  if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[1], st), "cudaEventRecord(profile)");
+  rc = launch_survivors(p, sa, st);
+  if (rc) return rc;
+  if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[2], st), "cudaEventRecord(profile)");
+  const pesti::RowArgs ra = make_row_args(p, ws, sa, d_u, d_out, d_kept_p, d_kept_idx, kept_width, d_kept_count);
+  rc = launch_row(p, device, ra, st);
+  if (rc) return rc;
   if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[3], st), "cudaEventRecord(profile)");
   return PESTI_OK;
 }
@@ -345,14 +412,461 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
   const Plan p = make_plan(s->num_sms, dtype, B, V, sorted_bufs);
   int rc = ensure_ws(s, p.bytes);
   if (rc) return rc;
+  rc = zero_counters(s, B, st);
+  if (rc) return rc;
   cudaEvent_t* pev = nullptr;
   if (s->prof && s->prof_n < pesti_sampler::kProfMax) {
     pev = s->prof_ev[s->prof_n++];
     for (int q = 0; q < 4; ++q)
       if (!pev[q]) PESTI_CUDA_TRY(cudaEventCreate(&pev[q]), "cudaEventCreate(profile)");
   }
-  return run_plan(p, (char*)s->ws, s->device, pev, d_logits, dtype, B, V, ld, uni, d_per_row, d_u,
-                  d_out, d_kept_p, d_kept_idx, kept_width, d_kept_count, st);
+  rc = run_plan(p, (char*)s->ws, s->device, pev, d_logits, dtype, B, V, ld, uni, d_per_row, d_u,
+                d_out, d_kept_p, d_kept_idx, kept_width, d_kept_count, st);
+  s->ctr_zero_rows = rc ? 0 : B;
+  return rc;
+}
+
+// Per-row parameters as the kernels read them: one uniform entry, or a
+// device array (the caller's, or the host entries copied to the handle's).
+int stage_params(pesti_sampler* s, const pesti_sampling_params* params, int params_per_row, int params_on_device,
+                 long long B, cudaStream_t st, pesti_sampling_params& uni,
+                 const pesti_sampling_params*& d_per_row, bool& sorted_bufs) {
+  uni = pesti_sampling_params{};
+  d_per_row = nullptr;
+  sorted_bufs = true;
+  if (params_on_device) {
+    if (params_per_row) d_per_row = params;
+    else {
+      // single device entry: read it back once (rare API use)
+      PESTI_CUDA_TRY(cudaMemcpyAsync(&uni, params, sizeof(uni), cudaMemcpyDeviceToHost, st), "params copy");
+      PESTI_CUDA_TRY(cudaStreamSynchronize(st), "params sync");
+      sorted_bufs = needs_sorted_buffers(&uni, 1);
+    }
+  } else if (params_per_row) {
+    sorted_bufs = needs_sorted_buffers(params, B);
+    if ((size_t)B > s->h_params_cap) {
+      if (s->params_ev_used) cudaEventSynchronize(s->params_ev);
+      if (s->h_params) cudaFreeHost(s->h_params);
+      if (s->d_params) cudaFree(s->d_params);
+      s->h_params = nullptr;
+      s->d_params = nullptr;
+      PESTI_CUDA_TRY(cudaMallocHost(&s->h_params, (size_t)B * sizeof(pesti_sampling_params)), "cudaMallocHost(params)");
+      PESTI_CUDA_TRY(cudaMalloc(&s->d_params, (size_t)B * sizeof(pesti_sampling_params)), "cudaMalloc(params)");
+      s->h_params_cap = s->d_params_cap = (size_t)B;
+    } else if (s->params_ev_used) {
+      PESTI_CUDA_TRY(cudaEventSynchronize(s->params_ev), "cudaEventSynchronize(params)");
+    }
+    std::memcpy(s->h_params, params, (size_t)B * sizeof(pesti_sampling_params));
+    PESTI_CUDA_TRY(cudaMemcpyAsync(s->d_params, s->h_params, (size_t)B * sizeof(pesti_sampling_params),
+                                   cudaMemcpyHostToDevice, st), "params copy");
+    PESTI_CUDA_TRY(cudaEventRecord(s->params_ev, st), "cudaEventRecord(params)");
+    s->params_ev_used = true;
+    d_per_row = s->d_params;
+  } else {
+    uni = params[0];
+    sorted_bufs = needs_sorted_buffers(&uni, 1);
+  }
+  return PESTI_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Vocabulary shards: every rank holds one contiguous, equally wide column
+// range of each row (pesti_shard.cuh describes the algorithm).
+// ---------------------------------------------------------------------------
+
+// NCCL is loaded when the first communicator is made, so that the library
+// itself has no link-time dependency on it (libnccl.so.2: the copy the
+// process already holds, if any, else the system's).
+struct NcclApi {
+  bool loaded = false;
+  std::string err;
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+const NcclApi& nccl_api() {
+  static const NcclApi api = [] {
+    NcclApi a;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      const char* why = dlerror();
+      a.err = std::string("cannot load libnccl.so.2: ") + (why ? why : "unknown");
+      return a;
+    }
+    a.get_unique_id = (decltype(a.get_unique_id))dlsym(h, "ncclGetUniqueId");
+    a.comm_init_rank = (decltype(a.comm_init_rank))dlsym(h, "ncclCommInitRank");
+    a.comm_destroy = (decltype(a.comm_destroy))dlsym(h, "ncclCommDestroy");
+    a.all_gather = (decltype(a.all_gather))dlsym(h, "ncclAllGather");
+    a.error_string = (decltype(a.error_string))dlsym(h, "ncclGetErrorString");
+    a.loaded = a.get_unique_id && a.comm_init_rank && a.comm_destroy && a.all_gather && a.error_string;
+    if (!a.loaded) a.err = "libnccl.so.2 lacks an entry point";
+    return a;
+  }();
+  return api;
+}
+
+int nccl_fail(ncclResult_t r, const char* what) {
+  const NcclApi& n = nccl_api();
+  return fail(PESTI_E_NCCL, std::string(what) + ": " + (n.error_string ? n.error_string(r) : "error"));
+}
+
+}  // namespace
+
+struct pesti_comm {
+  int world = 1;
+  int rank = 0;
+  int device = 0;
+  ncclComm_t comm = nullptr;
+};
+
+namespace {
+
+// Relative guard band of the fold classification for shards: the
+// approximate start of a shard (the true mass of the earlier shards) runs
+// ahead of the fold by the mass the fold absorbs, up to about 6e-4 of it on
+// rows of 256k; the band keeps the fold entries valid at the exact start.
+constexpr float kShardBand = 0x1p-10f;
+
+// Workspace of one sharded call: one set of single-shard passes per shard the
+// process holds (one with NCCL, all of them when emulated), then the
+// exchange buffers.  Each shard's region starts with its completion counters.
+struct ShardPlan {
+  Plan local;            // one shard's passes over [B, Vs]
+  int G = 1, nlocal = 1;
+  long long B = 0, Vs = 0, VT = 0;
+  int ksh = 0;
+  long long rec_stride = 0;
+  size_t local_stride = 0;
+  size_t o_ment = 0, o_nment = 0;  // within a shard's region
+  size_t o_sum_recv = 0, o_sum_send = 0, o_rec_recv = 0, o_rec_send = 0, o_tab_recv = 0, o_tab_send = 0;
+  size_t o_nflag = 0, o_flags = 0;
+  size_t bytes = 0;
+};
+
+ShardPlan make_shard_plan(int num_sms, pesti_dtype dtype, long long B, long long Vs, int G, int nlocal, int ksh) {
+  ShardPlan sp;
+  sp.local = make_plan(num_sms, dtype, B, Vs, false);
+  sp.G = G;
+  sp.nlocal = nlocal;
+  sp.B = B;
+  sp.Vs = Vs;
+  sp.VT = Vs * G;
+  sp.ksh = ksh;
+  sp.rec_stride = (long long)((sizeof(pesti::ShardRec) + (size_t)ksh * sizeof(pesti::ShardCand) + 15) / 16 * 16);
+  sp.o_ment = align_up(sp.local.bytes);
+  sp.o_nment = sp.o_ment + align_up((size_t)B * pesti::FAST_ENTS * sizeof(pesti::FoldEnt));
+  sp.local_stride = sp.o_nment + align_up((size_t)B * sizeof(int));
+  size_t off = sp.local_stride * (size_t)nlocal;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes);
+    return o;
+  };
+  const size_t nsum = (size_t)B * sizeof(pesti::ShardSum);
+  const size_t nrec = (size_t)B * (size_t)sp.rec_stride;
+  const size_t ntab = (size_t)B * sizeof(pesti::ShardTab);
+  sp.o_sum_recv = take(nsum * G);
+  sp.o_sum_send = take(nsum);
+  sp.o_rec_recv = take(nrec * G);
+  sp.o_rec_send = take(nrec);
+  sp.o_tab_recv = take(ntab * G);
+  sp.o_tab_send = take(ntab);
+  sp.o_nflag = take(16);
+  sp.o_flags = take((size_t)B * sizeof(int));
+  sp.bytes = off;
+  return sp;
+}
+
+struct ShardCall {
+  pesti_dtype dtype;
+  long long B, Vs, ld;
+  pesti_sampling_params uni;
+  const pesti_sampling_params* d_per_row;
+  const float* d_u;
+  uint32_t* d_out;
+  float* d_kept_p;
+  uint32_t* d_kept_idx;
+  long long kept_width;
+  int64_t* d_kept_count;
+  cudaStream_t st;
+};
+
+// First phase of shard r held in region li: its summary (max, flags, mass,
+// candidate threshold, argmax columns) to `sum_out`.
+int shard_phase1(const ShardPlan& sp, char* ws, int li, const ShardCall& c, const void* lg,
+                 pesti::ShardSum* sum_out) {
+  char* lws = ws + (size_t)li * sp.local_stride;
+  PESTI_CUDA_TRY(cudaMemsetAsync(lws + sp.local.o_ctr, 0, (size_t)c.B * sizeof(int), c.st), "cudaMemsetAsync(counters)");
+  pesti::SliceArgs sa = make_slice_args(sp.local, lws, lg, c.dtype, c.B, c.Vs, c.ld, c.uni, c.d_per_row);
+  sa.V_total = sp.VT;
+  sa.band = kShardBand;
+  sa.shard_out = sum_out;
+  return launch_slice_stats(sp.local, sa, c.st);
+}
+
+// Second phase of shard r (region li), once every summary is in `sums`:
+// the shard's prologue, survivor and classification passes, and its
+// exchange record (fold increment and candidates) to `rec_out`.
+int shard_phase2(const ShardPlan& sp, char* ws, int li, int r, int device, const ShardCall& c, const void* lg,
+                 const pesti::ShardSum* sums, unsigned char* rec_out) {
+  char* lws = ws + (size_t)li * sp.local_stride;
+  pesti::SliceArgs sa = make_slice_args(sp.local, lws, lg, c.dtype, c.B, c.Vs, c.ld, c.uni, c.d_per_row);
+  sa.V_total = sp.VT;
+  sa.band = kShardBand;
+  sa.shard_all = sums;
+  sa.shard_G = sp.G;
+  sa.shard_rank = r;
+  if (c.dtype == PESTI_BF16) pesti::shard_prologue_kernel<uint16_t, 8><<<(unsigned)c.B, pesti::K1_NT, 0, c.st>>>(sa);
+  else pesti::shard_prologue_kernel<float, 4><<<(unsigned)c.B, pesti::K1_NT, 0, c.st>>>(sa);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "shard_prologue_kernel launch");
+  int rc = launch_survivors(sp.local, sa, c.st);
+  if (rc) return rc;
+  pesti::RowArgs ra = make_row_args(sp.local, lws, sa, c.d_u, c.d_out, nullptr, nullptr, 0, nullptr);
+  ra.shard = 1;
+  ra.col0 = (long long)r * c.Vs;
+  ra.rec = rec_out;
+  ra.rec_stride = sp.rec_stride;
+  ra.ksh = sp.ksh;
+  ra.ment_g = (pesti::FoldEnt*)(lws + sp.o_ment);
+  ra.nment_g = (int*)(lws + sp.o_nment);
+  return launch_row(sp.local, device, ra, c.st);
+}
+
+// Third phase of shard r (region li), once every record is in `recs`: its
+// table of exact folds around the chained estimate of its start, to `tab_out`.
+int shard_phase3(const ShardPlan& sp, char* ws, int li, int r, const ShardCall& c, const void* lg,
+                 const unsigned char* recs, pesti::ShardTab* tab_out) {
+  char* lws = ws + (size_t)li * sp.local_stride;
+  pesti::TabArgs ta{};
+  ta.logits = lg;
+  ta.dtype = (int)c.dtype;
+  ta.B = c.B;
+  ta.ld = c.ld;
+  ta.uni = c.uni;
+  ta.per_row = c.d_per_row;
+  ta.info = (const pesti::RowInfo*)(lws + sp.local.o_info);
+  ta.recs = recs;
+  ta.rec_stride = sp.rec_stride;
+  ta.rank = r;
+  ta.ment_g = (const pesti::FoldEnt*)(lws + sp.o_ment);
+  ta.nment_g = (const int*)(lws + sp.o_nment);
+  ta.tab_out = tab_out;
+  pesti::shard_table_kernel<<<(unsigned)c.B, 32, 0, c.st>>>(ta);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "shard_table_kernel launch");
+  return PESTI_OK;
+}
+
+// Every row on every rank: chain, merge, draw; rows it cannot settle are listed.
+int shard_finish(const ShardPlan& sp, char* ws, const ShardCall& c) {
+  int* nflag = (int*)(ws + sp.o_nflag);
+  PESTI_CUDA_TRY(cudaMemsetAsync(nflag, 0, sizeof(int), c.st), "cudaMemsetAsync(flags)");
+  pesti::FinishArgs fa{};
+  fa.B = c.B;
+  fa.V_total = sp.VT;
+  fa.G = sp.G;
+  fa.uni = c.uni;
+  fa.per_row = c.d_per_row;
+  fa.info = (const pesti::RowInfo*)(ws + sp.local.o_info);  // region 0
+  fa.recs = (const unsigned char*)(ws + sp.o_rec_recv);
+  fa.rec_stride = sp.rec_stride;
+  fa.ksh = sp.ksh;
+  fa.tabs = (const pesti::ShardTab*)(ws + sp.o_tab_recv);
+  fa.u = c.d_u;
+  fa.out = c.d_out;
+  fa.kept_p = c.d_kept_p;
+  fa.kept_idx = c.d_kept_idx;
+  fa.kept_width = (c.d_kept_p || c.d_kept_idx) ? c.kept_width : 0;
+  fa.kept_count = c.d_kept_count;
+  fa.nflag = nflag;
+  fa.flag_rows = (int*)(ws + sp.o_flags);
+  pesti::shard_finish_kernel<<<(unsigned)c.B, pesti::K2_NT, 0, c.st>>>(fa);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "shard_finish_kernel launch");
+  return PESTI_OK;
+}
+
+// The rows listed by the finish (a host copy, sorted: every rank sees the
+// same list).  Synchronizes the stream.
+int read_flagged(const ShardPlan& sp, char* ws, cudaStream_t st, std::vector<int>& rows) {
+  int n = 0;
+  PESTI_CUDA_TRY(cudaMemcpyAsync(&n, ws + sp.o_nflag, sizeof(int), cudaMemcpyDeviceToHost, st), "flag count copy");
+  PESTI_CUDA_TRY(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+  rows.assign((size_t)n, 0);
+  if (n > 0) {
+    PESTI_CUDA_TRY(cudaMemcpy(rows.data(), ws + sp.o_flags, (size_t)n * sizeof(int), cudaMemcpyDeviceToHost),
+                   "flag list copy");
+    std::sort(rows.begin(), rows.end());
+  }
+  return PESTI_OK;
+}
+
+// Gathered path for the listed rows: whole rows are assembled (from the
+// shards by an NCCL all-gather, or from the whole matrix when emulated) and
+// sampled by the single-device passes; the results go to their rows.
+int shard_gathered(pesti_sampler* s, pesti_comm* comm, const ShardPlan& sp, const ShardCall& c,
+                   const void* local_logits, const void* whole_logits, const std::vector<int>& rows) {
+  const long long nf = (long long)rows.size();
+  if (nf == 0) return PESTI_OK;
+  const int esize = c.dtype == PESTI_BF16 ? 2 : 4;
+  const long long VT = sp.VT;
+  const long long W = (c.d_kept_p || c.d_kept_idx) ? c.kept_width : 0;
+  const Plan pf = make_plan(s->num_sms, c.dtype, nf, VT, true);
+  size_t off = align_up(pf.bytes);
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes);
+    return o;
+  };
+  const size_t o_rows = take((size_t)nf * sizeof(int));
+  const size_t o_full = take((size_t)nf * VT * esize);
+  const size_t o_u = take((size_t)nf * sizeof(float));
+  const size_t o_prm = take((size_t)nf * sizeof(pesti_sampling_params));
+  const size_t o_tok = take((size_t)nf * sizeof(uint32_t));
+  const size_t o_kp = take((size_t)nf * std::max<long long>(W, 1) * sizeof(float));
+  const size_t o_ki = take((size_t)nf * std::max<long long>(W, 1) * sizeof(uint32_t));
+  const size_t o_kc = take((size_t)nf * sizeof(int64_t));
+  const size_t o_send = take(comm ? (size_t)nf * c.Vs * esize : 0);
+  const size_t o_recv = take(comm ? (size_t)nf * VT * esize : 0);
+  // the sharded passes are done with the workspace (the stream was synchronized)
+  int rc = ensure_ws(s, off);
+  if (rc) return rc;
+  char* ws = (char*)s->ws;
+  // the gathered plan's counters: zero on the first sp.B rows after the sharded passes
+  if (nf > sp.B) PESTI_CUDA_TRY(cudaMemsetAsync(ws, 0, (size_t)nf * sizeof(int), c.st), "cudaMemsetAsync(counters)");
+  int* d_rows = (int*)(ws + o_rows);
+  PESTI_CUDA_TRY(cudaMemcpyAsync(d_rows, rows.data(), (size_t)nf * sizeof(int), cudaMemcpyHostToDevice, c.st),
+                 "row list copy");
+  unsigned char* full = (unsigned char*)(ws + o_full);
+  const long long row_bytes = VT * esize;
+  if (comm) {
+    const long long sh_bytes = c.Vs * esize;
+    unsigned char* send = (unsigned char*)(ws + o_send);
+    unsigned char* recv = (unsigned char*)(ws + o_recv);
+    pesti::gather_rows_kernel<<<dim3(16, (unsigned)nf), 256, 0, c.st>>>(
+        (const unsigned char*)local_logits, c.ld * esize, d_rows, (int)nf, sh_bytes, send, sh_bytes);
+    PESTI_CUDA_TRY(cudaGetLastError(), "gather_rows_kernel launch");
+    const ncclResult_t nr = nccl_api().all_gather(send, recv, (size_t)(nf * sh_bytes), ncclUint8, comm->comm, c.st);
+    if (nr != ncclSuccess) return nccl_fail(nr, "ncclAllGather(rows)");
+    for (int g = 0; g < sp.G; ++g)
+      PESTI_CUDA_TRY(cudaMemcpy2DAsync(full + (size_t)g * sh_bytes, (size_t)row_bytes, recv + (size_t)g * nf * sh_bytes,
+                                       (size_t)sh_bytes, (size_t)sh_bytes, (size_t)nf, cudaMemcpyDeviceToDevice, c.st),
+                     "row assembly copy");
+  } else {
+    pesti::gather_rows_kernel<<<dim3(16, (unsigned)nf), 256, 0, c.st>>>(
+        (const unsigned char*)whole_logits, c.ld * esize, d_rows, (int)nf, row_bytes, full, row_bytes);
+    PESTI_CUDA_TRY(cudaGetLastError(), "gather_rows_kernel launch");
+  }
+  float* u_f = (float*)(ws + o_u);
+  pesti_sampling_params* prm_f = (pesti_sampling_params*)(ws + o_prm);
+  pesti::gather_row_values_kernel<<<(unsigned)((nf + 255) / 256), 256, 0, c.st>>>(d_rows, (int)nf, c.d_u, u_f,
+                                                                                    c.d_per_row, prm_f);
+  PESTI_CUDA_TRY(cudaGetLastError(), "gather_row_values_kernel launch");
+  uint32_t* tok = (uint32_t*)(ws + o_tok);
+  float* kp = (float*)(ws + o_kp);
+  uint32_t* ki = (uint32_t*)(ws + o_ki);
+  int64_t* kc = (int64_t*)(ws + o_kc);
+  rc = run_plan(pf, ws, s->device, nullptr, full, c.dtype, nf, VT, VT, c.uni, c.d_per_row ? prm_f : nullptr, u_f,
+                tok, W ? kp : nullptr, W ? ki : nullptr, W, kc, c.st);
+  s->ctr_zero_rows = rc ? 0 : nf;
+  if (rc) return rc;
+  pesti::scatter_results_kernel<<<(unsigned)nf, 256, 0, c.st>>>(d_rows, (int)nf, tok, kp, ki, kc, W, c.d_out,
+                                                                 c.d_kept_p, c.d_kept_idx, c.d_kept_count);
+  PESTI_CUDA_TRY(cudaGetLastError(), "scatter_results_kernel launch");
+  return PESTI_OK;
+}
+
+// Candidates each shard lists per row: the largest top-k of the call's
+// top-k rows plus 8 (so that the bound on the unlisted ones lies well below
+// the k-th), at most FIN_KEYS over all shards.
+int shard_list_size(const pesti_sampling_params* params, int per_row, int on_device, long long B, long long VT, int G) {
+  long long kmax = pesti::FAST_K;
+  if (!on_device) {
+    kmax = 1;
+    const long long n = per_row ? B : 1;
+    for (long long i = 0; i < n; ++i) {
+      const long long k = std::min<long long>(params[i].top_k, VT);
+      if (k >= 1 && k <= pesti::FAST_K) kmax = std::max(kmax, k);
+    }
+  }
+  return (int)std::min<long long>(kmax + 8, pesti::FIN_KEYS / std::max(1, G));
+}
+
+// The sharded call.  comm == nullptr emulates `G` shards of the whole matrix
+// `d_logits` in one process; otherwise d_logits is this rank's shard.
+int sample_sharded(pesti_sampler* s, pesti_comm* comm, int G, const void* d_logits, pesti_dtype dtype,
+                   long long B, long long Vs, long long ld, const pesti_sampling_params* params, int params_per_row,
+                   int params_on_device, const float* d_u, uint32_t* d_out, float* d_kept_p, uint32_t* d_kept_idx,
+                   long long kept_width, int64_t* d_kept_count, void* stream) {
+  PESTI_CUDA_TRY(cudaSetDevice(s->device), "cudaSetDevice");
+  cudaStream_t st = stream ? (cudaStream_t)stream : s->stream;
+  ShardCall c{};
+  c.dtype = dtype;
+  c.B = B;
+  c.Vs = Vs;
+  c.ld = ld;
+  c.d_u = d_u;
+  c.d_out = d_out;
+  c.d_kept_p = d_kept_p;
+  c.d_kept_idx = d_kept_idx;
+  c.kept_width = kept_width;
+  c.d_kept_count = d_kept_count;
+  c.st = st;
+  bool sorted_bufs = false;
+  int rc = stage_params(s, params, params_per_row, params_on_device, B, st, c.uni, c.d_per_row, sorted_bufs);
+  if (rc) return rc;
+  const int esize = dtype == PESTI_BF16 ? 2 : 4;
+  const int nlocal = comm ? 1 : G;
+  const int ksh = shard_list_size(params, params_per_row, params_on_device, B, Vs * G, G);
+  const ShardPlan sp = make_shard_plan(s->num_sms, dtype, B, Vs, G, nlocal, ksh);
+  rc = ensure_ws(s, sp.bytes);
+  if (rc) return rc;
+  char* ws = (char*)s->ws;
+  auto lg = [&](int g) {  // shard g's columns
+    return comm ? d_logits : (const void*)((const char*)d_logits + (size_t)g * Vs * esize);
+  };
+  pesti::ShardSum* sum_recv = (pesti::ShardSum*)(ws + sp.o_sum_recv);
+  unsigned char* rec_recv = (unsigned char*)(ws + sp.o_rec_recv);
+  pesti::ShardTab* tab_recv = (pesti::ShardTab*)(ws + sp.o_tab_recv);
+  s->ctr_zero_rows = 0;
+  if (comm) {
+    const NcclApi& n = nccl_api();
+    pesti::ShardSum* sum_send = (pesti::ShardSum*)(ws + sp.o_sum_send);
+    unsigned char* rec_send = (unsigned char*)(ws + sp.o_rec_send);
+    pesti::ShardTab* tab_send = (pesti::ShardTab*)(ws + sp.o_tab_send);
+    rc = shard_phase1(sp, ws, 0, c, d_logits, sum_send);
+    if (rc) return rc;
+    ncclResult_t nr = n.all_gather(sum_send, sum_recv, (size_t)B * sizeof(pesti::ShardSum), ncclUint8, comm->comm, st);
+    if (nr != ncclSuccess) return nccl_fail(nr, "ncclAllGather(summaries)");
+    rc = shard_phase2(sp, ws, 0, comm->rank, s->device, c, d_logits, sum_recv, rec_send);
+    if (rc) return rc;
+    nr = n.all_gather(rec_send, rec_recv, (size_t)(B * sp.rec_stride), ncclUint8, comm->comm, st);
+    if (nr != ncclSuccess) return nccl_fail(nr, "ncclAllGather(records)");
+    rc = shard_phase3(sp, ws, 0, comm->rank, c, d_logits, rec_recv, tab_send);
+    if (rc) return rc;
+    nr = n.all_gather(tab_send, tab_recv, (size_t)B * sizeof(pesti::ShardTab), ncclUint8, comm->comm, st);
+    if (nr != ncclSuccess) return nccl_fail(nr, "ncclAllGather(tables)");
+  } else {
+    for (int g = 0; g < G; ++g)
+      if ((rc = shard_phase1(sp, ws, g, c, lg(g), sum_recv + (size_t)g * B))) return rc;
+    for (int g = 0; g < G; ++g)
+      if ((rc = shard_phase2(sp, ws, g, g, s->device, c, lg(g), sum_recv, rec_recv + (size_t)g * B * sp.rec_stride)))
+        return rc;
+    for (int g = 0; g < G; ++g)
+      if ((rc = shard_phase3(sp, ws, g, g, c, lg(g), rec_recv, tab_recv + (size_t)g * B))) return rc;
+  }
+  rc = shard_finish(sp, ws, c);
+  if (rc) return rc;
+  s->ctr_zero_rows = B;
+  std::vector<int> rows;
+  rc = read_flagged(sp, ws, st, rows);
+  if (rc) return rc;
+  s->last_gathered_rows = (long long)rows.size();
+  return shard_gathered(s, comm, sp, c, d_logits, d_logits, rows);
 }
 
 int check_shapes(const void* d_logits, pesti_dtype dtype, int64_t B, int64_t V, int64_t ld) {
@@ -434,38 +948,8 @@ int pesti_sample_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype
   pesti_sampling_params uni{};
   const pesti_sampling_params* d_per_row = nullptr;
   bool sorted_bufs = true;
-  if (params_on_device) {
-    if (params_per_row) d_per_row = params;
-    else {
-      // single device entry: read it back once (rare API use)
-      PESTI_CUDA_TRY(cudaMemcpyAsync(&uni, params, sizeof(uni), cudaMemcpyDeviceToHost, st), "params copy");
-      PESTI_CUDA_TRY(cudaStreamSynchronize(st), "params sync");
-      sorted_bufs = needs_sorted_buffers(&uni, 1);
-    }
-  } else if (params_per_row) {
-    sorted_bufs = needs_sorted_buffers(params, B);
-    if ((size_t)B > s->h_params_cap) {
-      if (s->params_ev_used) cudaEventSynchronize(s->params_ev);
-      if (s->h_params) cudaFreeHost(s->h_params);
-      if (s->d_params) cudaFree(s->d_params);
-      s->h_params = nullptr;
-      s->d_params = nullptr;
-      PESTI_CUDA_TRY(cudaMallocHost(&s->h_params, (size_t)B * sizeof(pesti_sampling_params)), "cudaMallocHost(params)");
-      PESTI_CUDA_TRY(cudaMalloc(&s->d_params, (size_t)B * sizeof(pesti_sampling_params)), "cudaMalloc(params)");
-      s->h_params_cap = s->d_params_cap = (size_t)B;
-    } else if (s->params_ev_used) {
-      PESTI_CUDA_TRY(cudaEventSynchronize(s->params_ev), "cudaEventSynchronize(params)");
-    }
-    std::memcpy(s->h_params, params, (size_t)B * sizeof(pesti_sampling_params));
-    PESTI_CUDA_TRY(cudaMemcpyAsync(s->d_params, s->h_params, (size_t)B * sizeof(pesti_sampling_params),
-                                   cudaMemcpyHostToDevice, st), "params copy");
-    PESTI_CUDA_TRY(cudaEventRecord(s->params_ev, st), "cudaEventRecord(params)");
-    s->params_ev_used = true;
-    d_per_row = s->d_params;
-  } else {
-    uni = params[0];
-    sorted_bufs = needs_sorted_buffers(&uni, 1);
-  }
+  rc = stage_params(s, params, params_per_row, params_on_device, B, st, uni, d_per_row, sorted_bufs);
+  if (rc) return rc;
   return launch(s, d_logits, dtype, B, V, ld, uni, d_per_row, sorted_bufs, d_u, d_out_tokens,
                 d_kept_p, d_kept_idx, kept_width, d_kept_count, st);
 }
@@ -573,6 +1057,90 @@ int pesti_sample_batch_noalloc(const void* d_logits, pesti_dtype dtype, int64_t 
   return run_plan(p, ws, device, nullptr, d_logits, dtype, B, V, ld, uni, d_per_row, d_u, d_out_tokens,
                   d_kept_p, d_kept_idx, kept_width, d_kept_count, st);
 }
+
+int pesti_comm_id(void* id) {
+  if (!id) return fail(PESTI_E_INVALID_ARG, "null id buffer");
+  const NcclApi& n = nccl_api();
+  if (!n.loaded) return fail(PESTI_E_NCCL, n.err);
+  ncclUniqueId u;
+  const ncclResult_t r = n.get_unique_id(&u);
+  if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
+  static_assert(sizeof(ncclUniqueId) == PESTI_COMM_ID_BYTES, "NCCL unique id size");
+  std::memcpy(id, &u, sizeof(u));
+  return PESTI_OK;
+}
+
+int pesti_comm_create(int world_size, int rank, const void* id, int device, pesti_comm** out) {
+  if (!out || !id) return fail(PESTI_E_INVALID_ARG, "null argument");
+  *out = nullptr;
+  if (world_size < 1 || world_size > pesti::FIN_MAXG || rank < 0 || rank >= world_size)
+    return fail(PESTI_E_INVALID_ARG, "bad world size or rank (1..64 ranks)");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(PESTI_E_NO_DEVICE, "no CUDA device available");
+  if (device < 0 || device >= ndev) return fail(PESTI_E_INVALID_ARG, "device index out of range");
+  const NcclApi& n = nccl_api();
+  if (!n.loaded) return fail(PESTI_E_NCCL, n.err);
+  PESTI_CUDA_TRY(cudaSetDevice(device), "cudaSetDevice");
+  ncclUniqueId u;
+  std::memcpy(&u, id, sizeof(u));
+  ncclComm_t comm = nullptr;
+  const ncclResult_t r = n.comm_init_rank(&comm, world_size, u, rank);
+  if (r != ncclSuccess) return nccl_fail(r, "ncclCommInitRank");
+  pesti_comm* c = new pesti_comm();
+  c->world = world_size;
+  c->rank = rank;
+  c->device = device;
+  c->comm = comm;
+  *out = c;
+  return PESTI_OK;
+}
+
+void pesti_comm_destroy(pesti_comm* c) {
+  if (!c) return;
+  if (c->comm) {
+    cudaSetDevice(c->device);
+    nccl_api().comm_destroy(c->comm);
+  }
+  delete c;
+}
+
+int pesti_sample_batch_sharded(pesti_sampler* s, pesti_comm* c, const void* d_logits, pesti_dtype dtype,
+                               int64_t B, int64_t V_shard, int64_t ld, const pesti_sampling_params* params,
+                               int params_per_row, int params_on_device, const float* d_u,
+                               uint32_t* d_out_tokens, float* d_kept_p, uint32_t* d_kept_idx,
+                               int64_t kept_width, int64_t* d_kept_count, void* stream) {
+  int rc = check_common(s, d_logits, dtype, B, V_shard, ld);
+  if (rc) return rc;
+  if (!c) return fail(PESTI_E_INVALID_ARG, "null communicator");
+  if (c->device != s->device) return fail(PESTI_E_INVALID_ARG, "sampler and communicator on different devices");
+  if (!params) return fail(PESTI_E_INVALID_ARG, "null params");
+  if (V_shard < 1) return fail(PESTI_E_INVALID_ARG, "every shard needs at least one column");
+  if ((long long)V_shard * c->world > 0x7fffffffLL) return fail(PESTI_E_INVALID_ARG, "whole rows exceed 2^31-1");
+  if (B > 0 && (!d_u || !d_out_tokens)) return fail(PESTI_E_INVALID_ARG, "null u or output tokens");
+  if ((d_kept_p || d_kept_idx) && kept_width <= 0) return fail(PESTI_E_INVALID_ARG, "kept_width must be > 0");
+  if (B == 0) return PESTI_OK;
+  return sample_sharded(s, c, c->world, d_logits, dtype, B, V_shard, ld, params, params_per_row, params_on_device,
+                        d_u, d_out_tokens, d_kept_p, d_kept_idx, kept_width, d_kept_count, stream);
+}
+
+int pesti_sample_batch_sharded_emulated(pesti_sampler* s, int shards, const void* d_logits, pesti_dtype dtype,
+                                        int64_t B, int64_t V, int64_t ld, const pesti_sampling_params* params,
+                                        int params_per_row, int params_on_device, const float* d_u,
+                                        uint32_t* d_out_tokens, float* d_kept_p, uint32_t* d_kept_idx,
+                                        int64_t kept_width, int64_t* d_kept_count, void* stream) {
+  int rc = check_common(s, d_logits, dtype, B, V, ld);
+  if (rc) return rc;
+  if (shards < 1 || shards > pesti::FIN_MAXG) return fail(PESTI_E_INVALID_ARG, "shards must be 1..64");
+  if (V < shards || V % shards != 0) return fail(PESTI_E_INVALID_ARG, "V must be a multiple of the shard count");
+  if (!params) return fail(PESTI_E_INVALID_ARG, "null params");
+  if (B > 0 && (!d_u || !d_out_tokens)) return fail(PESTI_E_INVALID_ARG, "null u or output tokens");
+  if ((d_kept_p || d_kept_idx) && kept_width <= 0) return fail(PESTI_E_INVALID_ARG, "kept_width must be > 0");
+  if (B == 0) return PESTI_OK;
+  return sample_sharded(s, nullptr, shards, d_logits, dtype, B, V / shards, ld, params, params_per_row,
+                        params_on_device, d_u, d_out_tokens, d_kept_p, d_kept_idx, kept_width, d_kept_count, stream);
+}
+
+int64_t pesti_last_gathered_rows(pesti_sampler* s) { return s ? s->last_gathered_rows : -1; }
 
 int pesti_profile_enable(pesti_sampler* s, int enable) {
   if (!s) return fail(PESTI_E_INVALID_ARG, "null sampler handle");

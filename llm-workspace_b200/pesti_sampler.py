@@ -54,7 +54,7 @@ NVCC_FLAGS = [
 def build(verbose: bool = False) -> str:
     """Compiles csrc/ into libpesti_sampler.so for sm_100a (in-tree)."""
     srcs = [os.path.join(CSRC, "pesti_sampler.cu"), os.path.join(CSRC, "pesti_noalloc.cu")]
-    cmd = ["nvcc", *NVCC_FLAGS, "-o", LIB_PATH, *srcs]
+    cmd = ["nvcc", *NVCC_FLAGS, "-o", LIB_PATH, *srcs, "-ldl"]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)
@@ -105,6 +105,20 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.pesti_sample_batch_noalloc.restype = c_int
     lib.pesti_last_error.argtypes = []
     lib.pesti_last_error.restype = ctypes.c_char_p
+    lib.pesti_comm_id.argtypes = [vp]
+    lib.pesti_comm_id.restype = c_int
+    lib.pesti_comm_create.argtypes = [c_int, c_int, vp, c_int, ctypes.POINTER(vp)]
+    lib.pesti_comm_create.restype = c_int
+    lib.pesti_comm_destroy.argtypes = [vp]
+    lib.pesti_comm_destroy.restype = None
+    lib.pesti_sample_batch_sharded.argtypes = [vp, vp, vp, c_int, i64, i64, i64, ctypes.POINTER(_Params), c_int,
+                                               c_int, vp, vp, vp, vp, i64, vp, vp]
+    lib.pesti_sample_batch_sharded.restype = c_int
+    lib.pesti_sample_batch_sharded_emulated.argtypes = [vp, c_int, vp, c_int, i64, i64, i64, ctypes.POINTER(_Params),
+                                                        c_int, c_int, vp, vp, vp, vp, i64, vp, vp]
+    lib.pesti_sample_batch_sharded_emulated.restype = c_int
+    lib.pesti_last_gathered_rows.argtypes = [vp]
+    lib.pesti_last_gathered_rows.restype = i64
     _lib = lib
     return lib
 
@@ -191,39 +205,49 @@ class Sampler:
         CUDA tensor of draws.  Returns the [B] int32 token tensor (u32 bits),
         or (tokens, kept_p, kept_idx, kept_count) when kept_width > 0.
         """
-        import torch
-        if logits.dim() != 2:
-            raise ValueError("logits must be [B, V]")
-        B, V = logits.shape
-        dtype = {torch.float32: PESTI_F32, torch.bfloat16: PESTI_BF16}.get(logits.dtype)
-        if dtype is None:
-            raise ValueError("logits must be float32 or bfloat16")
-        if logits.stride(1) != 1:
-            raise ValueError("logits rows must be contiguous")
-        if isinstance(configs, SamplingConfig):
-            arr = (_Params * 1)(configs.to_params(greedy_if_zero_t, argmax_first))
-            per_row = 0
-        else:
-            if len(configs) != B:
-                raise ValueError("need one config per row")
-            arr = (_Params * B)(*[c.to_params(greedy_if_zero_t, argmax_first) for c in configs])
-            per_row = 1
-        if out is None:
-            out = torch.empty(B, dtype=torch.int32, device=logits.device)
-        kp = ki = kc = None
-        if kept_width > 0:
-            kp = torch.empty(B, kept_width, dtype=torch.float32, device=logits.device)
-            ki = torch.empty(B, kept_width, dtype=torch.int32, device=logits.device)
-            kc = torch.empty(B, dtype=torch.int64, device=logits.device)
-        st = stream if stream is not None else torch.cuda.current_stream(logits.device).cuda_stream
+        B, V, dtype, arr, per_row, out, kp, ki, kc, st = _batch_args(
+            logits, configs, out, greedy_if_zero_t, argmax_first, kept_width, stream)
         _check(self._lib.pesti_sample_batch(
             self._h, logits.data_ptr(), dtype, B, V, logits.stride(0), arr, per_row, 0,
-            u.data_ptr(), out.data_ptr(),
-            kp.data_ptr() if kp is not None else None, ki.data_ptr() if ki is not None else None,
-            kept_width, kc.data_ptr() if kc is not None else None, st))
+            u.data_ptr(), out.data_ptr(), _ptr(kp), _ptr(ki), kept_width, _ptr(kc), st))
         if kept_width > 0:
             return out, kp, ki, kc
         return out
+
+    def sample_batch_sharded(self, comm: "Comm", logits_shard, configs, u, out=None,
+                             greedy_if_zero_t: bool = True, argmax_first: bool = False,
+                             kept_width: int = 0, stream=None):
+        """pesti_sample_batch_sharded: `logits_shard` is this rank's column range
+        [B, V_shard] of rows that are comm.world * V_shard long (rank r holds
+        columns [r*V_shard, (r+1)*V_shard)).  Every rank passes the same
+        configs and u ([B], all rows) and receives the results of all B rows.
+        """
+        B, Vs, dtype, arr, per_row, out, kp, ki, kc, st = _batch_args(
+            logits_shard, configs, out, greedy_if_zero_t, argmax_first, kept_width, stream)
+        _check(self._lib.pesti_sample_batch_sharded(
+            self._h, comm._h, logits_shard.data_ptr(), dtype, B, Vs, logits_shard.stride(0), arr, per_row, 0,
+            u.data_ptr(), out.data_ptr(), _ptr(kp), _ptr(ki), kept_width, _ptr(kc), st))
+        if kept_width > 0:
+            return out, kp, ki, kc
+        return out
+
+    def sample_batch_sharded_emulated(self, logits, configs, u, shards: int, out=None,
+                                      greedy_if_zero_t: bool = True, argmax_first: bool = False,
+                                      kept_width: int = 0, stream=None):
+        """The sharded algorithm over `shards` equal column ranges of the whole
+        matrix `logits`, all on this device (pesti_testing.h)."""
+        B, V, dtype, arr, per_row, out, kp, ki, kc, st = _batch_args(
+            logits, configs, out, greedy_if_zero_t, argmax_first, kept_width, stream)
+        _check(self._lib.pesti_sample_batch_sharded_emulated(
+            self._h, int(shards), logits.data_ptr(), dtype, B, V, logits.stride(0), arr, per_row, 0,
+            u.data_ptr(), out.data_ptr(), _ptr(kp), _ptr(ki), kept_width, _ptr(kc), st))
+        if kept_width > 0:
+            return out, kp, ki, kc
+        return out
+
+    def last_gathered_rows(self) -> int:
+        """Rows of the last sharded call that took the gathered path."""
+        return int(self._lib.pesti_last_gathered_rows(self._h))
 
     def sample_batch_device_params(self, logits, d_params, u, out, stream=None):
         """Per-row parameters already on the device (a [B, 4] int32/f32 view of
@@ -283,6 +307,80 @@ class Sampler:
             self._h, x.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), int(x.size), ctypes.byref(p),
             ctypes.c_float(0.0), ctypes.byref(tok)))
         return int(tok.value)
+
+
+def _ptr(t):
+    return t.data_ptr() if t is not None else None
+
+
+def _batch_args(logits, configs, out, greedy_if_zero_t, argmax_first, kept_width, stream):
+    """Shape, dtype, parameter array and output tensors of a batch call."""
+    import torch
+    if logits.dim() != 2:
+        raise ValueError("logits must be [B, V]")
+    B, V = logits.shape
+    dtype = {torch.float32: PESTI_F32, torch.bfloat16: PESTI_BF16}.get(logits.dtype)
+    if dtype is None:
+        raise ValueError("logits must be float32 or bfloat16")
+    if logits.stride(1) != 1:
+        raise ValueError("logits rows must be contiguous")
+    if isinstance(configs, SamplingConfig):
+        arr = (_Params * 1)(configs.to_params(greedy_if_zero_t, argmax_first))
+        per_row = 0
+    else:
+        if len(configs) != B:
+            raise ValueError("need one config per row")
+        arr = (_Params * B)(*[c.to_params(greedy_if_zero_t, argmax_first) for c in configs])
+        per_row = 1
+    if out is None:
+        out = torch.empty(B, dtype=torch.int32, device=logits.device)
+    kp = ki = kc = None
+    if kept_width > 0:
+        kp = torch.empty(B, kept_width, dtype=torch.float32, device=logits.device)
+        ki = torch.empty(B, kept_width, dtype=torch.int32, device=logits.device)
+        kc = torch.empty(B, dtype=torch.int64, device=logits.device)
+    st = stream if stream is not None else torch.cuda.current_stream(logits.device).cuda_stream
+    return B, V, dtype, arr, per_row, out, kp, ki, kc, st
+
+
+COMM_ID_BYTES = 128  # PESTI_COMM_ID_BYTES
+
+
+class Comm:
+    """A pesti_comm (an NCCL communicator over this process group's ranks) for
+    Sampler.sample_batch_sharded.  Rank 0 makes the id (pesti_comm_id); it is
+    broadcast over the default torch.distributed group, then every rank
+    calls pesti_comm_create.  Collective: every rank constructs it."""
+
+    def __init__(self, device: int):
+        import torch
+        import torch.distributed as dist
+        lib = load_library()
+        rank, world = dist.get_rank(), dist.get_world_size()
+        buf = (ctypes.c_uint8 * COMM_ID_BYTES)()
+        if rank == 0:
+            _check(lib.pesti_comm_id(buf))
+        t = torch.tensor(list(bytes(buf)), dtype=torch.uint8)
+        if dist.get_backend() == "nccl":
+            t = t.to(f"cuda:{device}")
+        dist.broadcast(t, 0)
+        buf = (ctypes.c_uint8 * COMM_ID_BYTES).from_buffer_copy(bytes(t.cpu().tolist()))
+        h = ctypes.c_void_p()
+        _check(lib.pesti_comm_create(world, rank, buf, int(device), ctypes.byref(h)))
+        self._h = h
+        self._lib = lib
+        self.rank, self.world, self.device = rank, world, device
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._lib.pesti_comm_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 NOALLOC_SCRATCH_BYTES = 64 << 20  # PESTI_NOALLOC_SCRATCH_BYTES

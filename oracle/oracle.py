@@ -64,6 +64,10 @@ def lib() -> ctypes.CDLL:
         L.oracle_sample_batch.restype = None
         L.oracle_exp_cr.argtypes = [ctypes.c_float]
         L.oracle_exp_cr.restype = ctypes.c_float
+        L.oracle_softmax_terms.argtypes = [fp, i64, ctypes.c_float, ctypes.c_float, ctypes.c_int, fp]
+        L.oracle_softmax_terms.restype = None
+        L.oracle_fold.argtypes = [fp, i64, ctypes.c_float]
+        L.oracle_fold.restype = ctypes.c_float
         _lib = L
     return _lib
 
@@ -96,6 +100,21 @@ def sample(logits, temperature, top_p, top_k, r, exp_mode=EXP_PLATFORM, kept_wid
     if kept_width > 0:
         return int(tok), kp[:kept_width], ki[:kept_width], int(kc[0]), float(bd[0])
     return int(tok)
+
+
+def softmax_terms(logits, temperature, m, exp_mode=EXP_CR) -> np.ndarray:
+    """exp(scaled_i - m) of each logit (sampling.rs:43-50, :127), m being the
+    max of the scaled whole row (the caller's, when `logits` is a shard)."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    out = np.empty_like(x)
+    lib().oracle_softmax_terms(_fp(x), x.size, float(temperature), float(m), exp_mode, _fp(out))
+    return out
+
+
+def fold(v, s0=0.0) -> np.float32:
+    """The sequential f32 fold s = s0; s = s + v[i] (sampling.rs:128 from any start)."""
+    x = np.ascontiguousarray(v, dtype=np.float32)
+    return np.float32(lib().oracle_fold(_fp(x), x.size, float(np.float32(s0))))
 
 
 def sample_batch(logits: np.ndarray, params, u: np.ndarray, exp_mode=EXP_PLATFORM, kept_width=0,

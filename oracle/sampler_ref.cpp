@@ -213,6 +213,22 @@ void oracle_sample_batch(const float* logits, int64_t B, int64_t V, int64_t ld,
   for (auto& t : ts) t.join();
 }
 
+// sampling.rs:43-50 (scaling) and :127 (exp of the difference to the max)
+void oracle_softmax_terms(const float* logits, int64_t n, float temperature, float m, int exp_mode,
+                          float* out) {
+  for (int64_t i = 0; i < n; ++i) {
+    const float x = temperature > 0.0f ? logits[i] / temperature : logits[i];
+    out[i] = exp_mode_apply(x - m, exp_mode);
+  }
+}
+
+// sampling.rs:128 (exps.iter().sum()) from an arbitrary start
+float oracle_fold(const float* v, int64_t n, float s0) {
+  float s = s0;
+  for (int64_t i = 0; i < n; ++i) s = s + v[i];
+  return s;
+}
+
 void oracle_bf16_to_f32(const uint16_t* in, float* out, int64_t n) {
   for (int64_t i = 0; i < n; ++i) {
     uint32_t bits = static_cast<uint32_t>(in[i]) << 16;

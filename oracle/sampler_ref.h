@@ -84,6 +84,17 @@ void oracle_bf16_to_f32(const uint16_t* in, float* out, int64_t n);
 /* The exp used by mode 1, exposed for the exhaustive exp check. */
 float oracle_exp_cr(float x);
 
+/*
+ * Pieces of sampling.rs:43-50 and :125-128 for checking a vocabulary-sharded
+ * evaluation: the softmax terms e_i = exp(scaled_i - m) of n logits
+ * (scaled_i = logits_i / temperature when temperature > 0, else logits_i),
+ * with m the max of the scaled WHOLE row given by the caller, and the
+ * sequential f32 fold s = s0; s = s + v[i] of n terms from any start s0.
+ */
+void oracle_softmax_terms(const float* logits, int64_t n, float temperature, float m, int exp_mode,
+                          float* out);
+float oracle_fold(const float* v, int64_t n, float s0);
+
 #ifdef __cplusplus
 }
 #endif

@@ -6,7 +6,13 @@ per-row draws from PCG32 seed 1.  A step samples one token for every row of
 one batch already resident in HBM; per GPU the batch is fixed (weak scaling:
 each rank samples its own 64 rows, no collective on the data path).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload 1..5]
+
+--workload 5 under torchrun (N > 1) runs the vocabulary-sharded path instead:
+the [1024, 256000] f32 batch is split into N contiguous column ranges, one
+per rank (strong scaling: the total work is fixed), and every rank receives
+all 1024 tokens (pesti_sample_batch_sharded; three NCCL all-gathers of
+per-row records, no logits moved).
 
 Keys beyond the base contract:
   roofline      the slice-max pass (the HBM pass over the logits; the dominant
@@ -164,6 +170,156 @@ def run_reference(args):
     return 0
 
 
+def run_vocab_sharded(args, rank, world, local, dev):
+    """Workload 5 over `world` ranks, each holding one column range of every row."""
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    import pesti_sampler as ps
+    import synth
+    from rows import max_over_ranks
+    w = 5
+    spec = synth.WORKLOADS[w]
+    B, V = spec["B"], spec["V"]
+    if V % world:
+        raise SystemExit(f"V={V} is not a multiple of {world} ranks")
+    Vs = V // world
+    cols = range(rank * Vs, (rank + 1) * Vs)
+    x = synth.make_logits(w, cols=cols)
+    u = synth.make_u(w, B)
+    T, P, K = synth.params_for(w, 1, V)[0]
+    cfg = ps.SamplingConfig(T, P, K)
+    host = torch.from_numpy(x)
+    step_bytes = B * Vs * 4  # this rank's logits
+    nbuf = max(2, math.ceil(2 * L2_BYTES / step_bytes))
+    bufs = [host.to(dev) for _ in range(nbuf)]
+    ud = torch.from_numpy(u).to(dev)
+    out = torch.empty(B, dtype=torch.int32, device=dev)
+    s = ps.Sampler(local)
+    comm = ps.Comm(local)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        s.sample_batch_sharded(comm, bufs[i % nbuf], cfg, ud, out=out)
+
+    # correctness guard: every rank's tokens against the whole rows sampled on rank 0's GPU
+    step(0)
+    torch.cuda.synchronize()
+    gathered_first = s.last_gathered_rows()
+    gathered_why = s.last_gathered_reasons()
+    mine = out.cpu().numpy().view(np.uint32).copy()
+    check = None
+    if rank == 0:
+        whole = torch.from_numpy(synth.make_logits(w)).to(dev)
+        ref = s.sample_batch(whole, cfg, ud)
+        torch.cuda.synchronize()
+        check = ref.cpu().numpy().view(np.uint32)
+        del whole
+        torch.cuda.empty_cache()
+    all_tok = [None] * world
+    dist.all_gather_object(all_tok, mine)
+    exact = int(sum(int((t == check).sum()) for t in all_tok)) if rank == 0 else None
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        step(i)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    clk = clocks.stop()
+    dist.barrier()
+    elapsed_ms = max_over_ranks(elapsed_ms, dev)
+    ms_per_step = elapsed_ms / args.steps
+    value = B * args.steps / (elapsed_ms / 1e3)
+
+    # the HBM pass over the shard, timed alone (profiled steps)
+    lib = ps.load_library()
+    lib.pesti_profile_enable.argtypes = [ctypes.c_void_p, ctypes.c_int]
+    lib.pesti_profile_read.argtypes = [ctypes.c_void_p] + [ctypes.POINTER(ctypes.c_double)] * 3 + \
+        [ctypes.POINTER(ctypes.c_int)]
+    lib.pesti_profile_enable(s._h, 1)
+    prof_steps = min(args.steps, 50)
+    for i in range(prof_steps):
+        step(i)
+    torch.cuda.synchronize()
+    t_max, t_mid, t_fin, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_double(), ctypes.c_int()
+    lib.pesti_profile_read(s._h, ctypes.byref(t_max), ctypes.byref(t_mid), ctypes.byref(t_fin), ctypes.byref(n))
+    lib.pesti_profile_enable(s._h, 0)
+    scan_ms = max_over_ranks(t_max.value / max(1, n.value), dev)
+    mid_ms = max_over_ranks(t_mid.value / max(1, n.value), dev)
+    fin_ms = max_over_ranks(t_fin.value / max(1, n.value), dev)
+    peak, peak_kind = measured_peaks()
+    achieved = step_bytes / (scan_ms / 1e3) / 1e9
+
+    # end to end: each rank's shard from pinned host memory, all tokens back
+    pinned = host.pin_memory()
+    u_pinned = torch.from_numpy(u).pin_memory()
+    dbuf = torch.empty_like(bufs[0])
+    ubuf = torch.empty_like(ud)
+    tok_host = torch.empty(B, dtype=torch.int32).pin_memory()
+    e2e_steps = max(5, min(args.steps, 50))
+
+    def e2e_step():
+        dbuf.copy_(pinned, non_blocking=True)
+        ubuf.copy_(u_pinned, non_blocking=True)
+        s.sample_batch_sharded(comm, dbuf, cfg, ubuf, out=out)
+        tok_host.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), dev)
+    e2e_value = B * e2e_steps / (e2e_ms / 1e3)
+    if rank == 0:
+        line = {
+            "metric": "sampled rows/s, vocabulary-sharded (B=1024, V=256000 f32, T0.9 k64 p0.92)",
+            "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": spec["name"], "B": B, "V": V, "V_per_gpu": Vs,
+                       "l2": f"rotating {nbuf} input buffers per rank ({nbuf * step_bytes / 2**20:.0f} MiB > 126 MiB L2)",
+                       "parallelism": f"vocab shards, {world} GPU(s), 3 NCCL all-gathers of per-row records"},
+            "roofline": {"bound": "hbm", "kernel": "slice_stats_kernel", "achieved": achieved, "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                         "bytes_per_launch": step_bytes},
+            "phase_us": {"slice_stats": scan_ms * 1e3, "to_last_exchange": mid_ms * 1e3, "finish": fin_ms * 1e3},
+            "step_hbm_gbs_per_gpu": step_bytes / (ms_per_step / 1e3) / 1e9,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": step_bytes + B * 4,
+                    "d2h_bytes_per_step": B * 4},
+            # shard_stats, shard_prologue, survivor, classify, row (record), table, finish
+            "gpu_launches": 7 * args.steps,
+            "clocks": clk,
+            "cpu_baseline": None,
+            "bench_rows_exact": exact, "bench_rows_checked": B * world,
+            "gathered_rows_first_step": gathered_first, "gathered_reasons": gathered_why,
+        }
+        print(json.dumps(line))
+    comm.close()
+    s.close()
+    dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -194,6 +350,8 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        if args.workload == 5:
+            return run_vocab_sharded(args, rank, world, local, dev)
 
     w = args.workload
     spec = synth.WORKLOADS[w]

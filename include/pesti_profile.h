@@ -15,7 +15,9 @@ extern "C" {
 /* enable != 0 starts recording (clears earlier records); 0 stops. */
 int pesti_profile_enable(pesti_sampler* s, int enable);
 /* Sums of the recorded slice-max, survivor and row-kernel times (ms) and the
- * number of calls recorded (at most 4096 are kept). */
+ * number of calls recorded (at most 4096 are kept).  For a sharded call the
+ * three intervals are instead: the HBM pass over the shard, everything from
+ * there to the end of the last exchange, and the finish. */
 int pesti_profile_read(pesti_sampler* s, double* max_ms, double* surv_ms, double* row_ms, int* calls);
 #ifdef __cplusplus
 }

@@ -65,10 +65,10 @@ typedef struct {
 
 typedef struct pesti_sampler pesti_sampler;
 
-/* Creates a sampler bound to CUDA device `device`: its own stream, events and
- * a workspace that grows on demand.  Replaces the context set-up of
- * CudaRuntime::new (llm-runner/src/cuda_runtime.rs:92-176) for this path.
- * A handle may be used from one thread at a time. */
+/* Creates a sampler bound to CUDA device `device`: events, a workspace that
+ * grows on demand, and a private stream for pesti_sample_row_host.  Replaces
+ * the context set-up of CudaRuntime::new (llm-runner/src/cuda_runtime.rs:92-176)
+ * for this path.  A handle may be used from one thread at a time. */
 int pesti_sampler_create(int device, pesti_sampler** out);
 void pesti_sampler_destroy(pesti_sampler* s);
 
@@ -89,7 +89,8 @@ void pesti_sampler_destroy(pesti_sampler* s);
  *                  with 0 / 0xffffffff.  Either may be NULL.
  *  d_kept_count    optional device [B] i64: length of each kept list (0 for
  *                  greedy rows).
- *  stream          cudaStream_t (NULL = the handle's own stream).
+ *  stream          cudaStream_t; NULL is the legacy default stream, as for
+ *                  CUDA's own calls (PyTorch's default stream is that stream).
  */
 int pesti_sample_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, int64_t B,
                        int64_t V, int64_t ld, const pesti_sampling_params* params,

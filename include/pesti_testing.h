@@ -22,6 +22,12 @@ int pesti_sample_batch_sharded_emulated(pesti_sampler* s, int shards, const void
                                         int64_t kept_width, int64_t* d_kept_count, void* stream);
 /* Rows of the handle's last sharded call that took the gathered path. */
 int64_t pesti_last_gathered_rows(pesti_sampler* s);
+/* The same rows by reason, counts[6]: [1] not a top-k row (top-p, no filter,
+ * top_k > 256, NaN, or every probability equal), [2] a shard's fold entries
+ * exceeded the row kernel's staging, [3] a shard's candidates exceeded its
+ * sort, [4] the chained fold state left a shard's table, [5] the merged
+ * candidates could not prove the top-k. */
+int pesti_last_gathered_reasons(pesti_sampler* s, int64_t* counts);
 #ifdef __cplusplus
 }
 #endif

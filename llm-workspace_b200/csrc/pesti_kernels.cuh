@@ -206,13 +206,16 @@ struct RowArgs {
 
 // Exchange record of one row of one vocabulary shard (second phase).
 enum : uint32_t { SH_OK = 0u, SH_SKIP = 1u, SH_FAIL = 2u };
+// Why a row took the gathered path (top 4 bits of its entry in the list).
+enum : uint32_t { GR_ROW = 1u, GR_ENTRIES = 2u, GR_CANDS = 3u, GR_CHAIN = 4u, GR_BOUND = 5u, GR_KINDS = 6u };
 struct ShardRec {
   double delta;     // exact fold of the shard's softmax terms from s_start, minus s_start
   float s_start;    // the approximate state the fold started from
   uint32_t status;  // SH_OK; SH_SKIP: not a sharded row; SH_FAIL: the row needs the gathered path
   float bound;      // every element of the shard not listed has an exp <= bound
   int32_t n;        // candidates listed (at most ksh), by (exp desc, column asc)
-  uint32_t pad[2];
+  uint32_t why;     // SH_FAIL: GR_ENTRIES (fold entries overflow) or GR_CANDS (candidates)
+  uint32_t pad;
 };
 struct ShardCand {
   uint32_t e_bits;  // exact exp (sampling.rs:127)
@@ -1478,15 +1481,16 @@ struct RowShared {
 };
 
 // Fast-path arrays, placed after RowShared in dynamic shared memory.
-constexpr int FAST_ENTS = 1024;  // fold entries of a row the fast path stages
+constexpr int FAST_ENTS = 4096;  // fold entries of a row the fast path stages
+constexpr int MERGE_EPT = FAST_ENTS / K2_NT;  // of them per thread in the merge
 constexpr int FAST_PAIRS = 2048; // (sub-slice, group) pairs of a row the fast path stages
 constexpr uint32_t ENT_REPLAY = 0xfffffffdu;  // staged entry: replay the whole sub-slice
 struct FastSmem {
   unsigned long long key[FAST_CAND];
-  float q[FAST_CAND];
+  float q[FAST_K];
   float stage[STAGE];
-  FoldEnt ent[FAST_ENTS];      // the row's entries in row order
-  FoldEnt ment[FAST_ENTS];     // the same with consecutive runs of one binade merged
+  FoldEnt ent[FAST_ENTS];      // the row's entries in row order; after the merge (in
+                               // place), the same with consecutive runs of one binade merged
   Seg wseg[K2_NT / 32];        // block-wide segmented scan: per-warp totals and prefixes
   Seg wpre[K2_NT / 32];
   int wfl[K2_NT / 32];
@@ -1746,7 +1750,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
     if (!ok) {
       if (tid == 0) {
         ShardRec* rc = reinterpret_cast<ShardRec*>(a.rec + b * a.rec_stride);
-        *rc = ShardRec{0.0, 0.0f, SH_SKIP, 0.0f, 0, {0u, 0u}};
+        *rc = ShardRec{0.0, 0.0f, SH_SKIP, 0.0f, 0, GR_ROW, 0u};
         a.nment_g[b] = -1;
       }
       return;
@@ -1908,22 +1912,34 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
     // Merge consecutive runs of one binade (their increments compose; the
     // merged run covers the row up to the last one's end), so that the walk
     // below takes one step per binade change or special.  A block-wide
-    // segmented scan: each thread holds two entries.
+    // segmented scan, MERGE_EPT consecutive entries per thread, written back
+    // in place (every thread has read its entries before the first barrier).
     if (fs.total <= FAST_ENTS) {
       const int total = fs.total;
       auto single = [](uint32_t key) { return key == fold::SPECIAL || key == ENT_REPLAY; };
-      const int e0 = 2 * tid, e1 = e0 + 1;
       const FoldEnt none{KEY_NONE, 0u, 0u, 0u};
-      const FoldEnt x0 = e0 < total ? fs.ent[e0] : none;
-      const FoldEnt x1 = e1 < total ? fs.ent[e1] : none;
+      const int e0 = tid * MERGE_EPT;
+      FoldEnt x[MERGE_EPT];
+#pragma unroll
+      for (int i = 0; i < MERGE_EPT; ++i) x[i] = e0 + i < total ? fs.ent[e0 + i] : none;
       const uint32_t kp = e0 > 0 && e0 < total ? fs.ent[e0 - 1].lo : KEY_NONE;
-      const uint32_t kn = e1 + 1 < total ? fs.ent[e1 + 1].lo : KEY_NONE;
-      const bool h0 = e0 < total && (e0 == 0 || single(x0.lo) || single(kp) || x0.lo != kp);
-      const bool h1 = e1 < total && (single(x1.lo) || single(x0.lo) || x1.lo != x0.lo);
-      const bool h2 = e1 + 1 < total && (single(kn) || single(x1.lo) || kn != x1.lo);
-      const Seg v0{x0.a0, x0.a1, 0u, x0.lo}, v1{x1.a0, x1.a1, 0u, x1.lo};
-      const Seg agg = e1 < total ? seg_join(v0, v1, h1) : v0;
-      const bool aflag = h0 || h1;
+      const uint32_t kn = e0 + MERGE_EPT < total ? fs.ent[e0 + MERGE_EPT].lo : KEY_NONE;
+      // h: entry i starts a run; the last one is followed by a start (or the end)
+      bool h[MERGE_EPT];
+      Seg agg{0u, 0u, 0u, KEY_NONE};
+      bool aflag = false;
+#pragma unroll
+      for (int i = 0; i < MERGE_EPT; ++i) {
+        const uint32_t pk = i == 0 ? kp : x[i - 1].lo;
+        h[i] = e0 + i < total && (e0 + i == 0 || single(x[i].lo) || single(pk) || x[i].lo != pk);
+        const Seg v{x[i].a0, x[i].a1, 0u, x[i].lo};
+        if (e0 + i < total) {
+          agg = i == 0 ? v : seg_join(agg, v, h[i]);
+          aflag = aflag || h[i];
+        }
+      }
+      const bool hn = e0 + MERGE_EPT < total &&
+                      (single(kn) || single(x[MERGE_EPT - 1].lo) || kn != x[MERGE_EPT - 1].lo);
       Seg inc = agg;
       bool fl = aflag;
 #pragma unroll
@@ -1962,15 +1978,24 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
       const Seg ex = seg_shfl_up(inc, 1);
       const bool exf = __shfl_up_sync(PESTI_FULL_MASK, fl, 1);
       if (lane > 0) pre = seg_join(pre, ex, exf);
-      const Seg i0v = seg_join(pre, v0, h0);
-      const Seg i1v = seg_join(i0v, v1, h1);
-      const bool end0 = e0 < total && (e1 >= total || h1);
-      const bool end1 = e1 < total && (e1 + 1 >= total || h2);
+      // an entry ends a merged run when the next one starts a run (or none follows)
+      int nend = 0;
+#pragma unroll
+      for (int i = 0; i < MERGE_EPT; ++i) {
+        const bool nxt = i + 1 < MERGE_EPT ? (e0 + i + 1 >= total || h[i + 1]) : (e0 + MERGE_EPT >= total || hn);
+        nend += (e0 + i < total && nxt) ? 1 : 0;
+      }
       int tot;
-      const int slot = block_excl_scan_add((end0 ? 1 : 0) + (end1 ? 1 : 0), sh.iscr, tot);
-      int o = slot;
-      if (end0) fs.ment[o++] = FoldEnt{single(x0.lo) ? x0.lo : i0v.key, i0v.a0, i0v.a1, x0.end};
-      if (end1) fs.ment[o] = FoldEnt{single(x1.lo) ? x1.lo : i1v.key, i1v.a0, i1v.a1, x1.end};
+      int o = block_excl_scan_add(nend, sh.iscr, tot);
+      Seg cur = pre;
+#pragma unroll
+      for (int i = 0; i < MERGE_EPT; ++i) {
+        if (e0 + i < total) {
+          cur = seg_join(cur, Seg{x[i].a0, x[i].a1, 0u, x[i].lo}, h[i]);
+          const bool nxt = i + 1 < MERGE_EPT ? (e0 + i + 1 >= total || h[i + 1]) : (e0 + MERGE_EPT >= total || hn);
+          if (nxt) fs.ent[o++] = FoldEnt{single(x[i].lo) ? x[i].lo : cur.key, cur.a0, cur.a1, x[i].end};
+        }
+      }
       if (tid == 0) fs.nment = tot;
       __syncthreads();
     }
@@ -2010,7 +2035,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
         for (; i < nm && fi < 0; i += 4) {
           FoldEnt en[4];  // four at a time: their loads do not depend on the state
 #pragma unroll
-          for (int u = 0; u < 4; ++u) en[u] = fs.ment[i + u < nm ? i + u : i];
+          for (int u = 0; u < 4; ++u) en[u] = fs.ent[i + u < nm ? i + u : i];
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             if (fi < 0 && i + u < nm) {
@@ -2025,8 +2050,8 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
           }
         }
         if (fi < 0) break;
-        const uint32_t from = fi > 0 ? fs.ment[fi - 1].end : 0u;
-        const uint32_t to = fs.ment[fi].end;
+        const uint32_t from = fi > 0 ? fs.ent[fi - 1].end : 0u;
+        const uint32_t to = fs.ent[fi].end;
         const void* src = a.dtype == PESTI_BF16 ? (const void*)((const uint16_t*)row + from)
                                                 : (const void*)((const float*)row + from);
         s = warp_fold(src, a.dtype, (long long)to - from, s, fs.stage, scale, T, m);
@@ -2049,7 +2074,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
           cd[j] = ShardCand{(uint32_t)(kv >> 32), ~(uint32_t)(kv & 0xffffffffull) + (uint32_t)a.col0};
         }
         if (ok)
-          for (int i = lane; i < fs.nment; i += 32) a.ment_g[b * FAST_ENTS + i] = fs.ment[i];
+          for (int i = lane; i < fs.nment; i += 32) a.ment_g[b * FAST_ENTS + i] = fs.ent[i];
         if (lane == 0) {
           ShardRec r;
           r.delta = ok ? (double)bitsf(s) - (double)ri.s_start : 0.0;
@@ -2057,7 +2082,8 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
           r.status = ok ? SH_OK : SH_FAIL;
           r.bound = ok && C > a.ksh ? bitsf((uint32_t)(fs.key[a.ksh] >> 32)) : ri.e_tau;
           r.n = nl;
-          r.pad[0] = r.pad[1] = 0u;
+          r.why = fs.total > FAST_ENTS ? GR_ENTRIES : (ok ? 0u : GR_CANDS);
+          r.pad = 0u;
           *rc = r;
           a.nment_g[b] = ok ? fs.nment : -1;
         }

@@ -70,8 +70,9 @@ struct pesti_sampler {
   bool prof = false;
   int prof_n = 0;
   cudaEvent_t prof_ev[kProfMax][4] = {};
-  // rows of the last sharded call that took the gathered path
+  // rows of the last sharded call that took the gathered path, by reason (GR_*)
   long long last_gathered_rows = 0;
+  long long last_gathered_why[pesti::GR_KINDS] = {};
 };
 
 namespace {
@@ -149,6 +150,9 @@ int ensure_row_smem_limit(int device) {
   PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)kRowSmemLimit),
                  "cudaFuncSetAttribute(row_kernel)");
+  PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::shard_table_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)pesti::TAB_SMEM),
+                 "cudaFuncSetAttribute(shard_table_kernel)");
   if (cached) g_row_limit_set[device].store(true, std::memory_order_release);
   return PESTI_OK;
 }
@@ -638,7 +642,7 @@ int shard_phase2(const ShardPlan& sp, char* ws, int li, int r, int device, const
 
 // Third phase of shard r (region li), once every record is in `recs`: its
 // table of exact folds around the chained estimate of its start, to `tab_out`.
-int shard_phase3(const ShardPlan& sp, char* ws, int li, int r, const ShardCall& c, const void* lg,
+int shard_phase3(const ShardPlan& sp, char* ws, int li, int r, int device, const ShardCall& c, const void* lg,
                  const unsigned char* recs, pesti::ShardTab* tab_out) {
   char* lws = ws + (size_t)li * sp.local_stride;
   pesti::TabArgs ta{};
@@ -655,7 +659,9 @@ int shard_phase3(const ShardPlan& sp, char* ws, int li, int r, const ShardCall& 
   ta.ment_g = (const pesti::FoldEnt*)(lws + sp.o_ment);
   ta.nment_g = (const int*)(lws + sp.o_nment);
   ta.tab_out = tab_out;
-  pesti::shard_table_kernel<<<(unsigned)c.B, 32, 0, c.st>>>(ta);
+  int rc = ensure_row_smem_limit(device);
+  if (rc) return rc;
+  pesti::shard_table_kernel<<<(unsigned)c.B, 32, pesti::TAB_SMEM, c.st>>>(ta);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "shard_table_kernel launch");
   return PESTI_OK;
@@ -691,15 +697,21 @@ int shard_finish(const ShardPlan& sp, char* ws, const ShardCall& c) {
 }
 
 // The rows listed by the finish (a host copy, sorted: every rank sees the
-// same list).  Synchronizes the stream.
-int read_flagged(const ShardPlan& sp, char* ws, cudaStream_t st, std::vector<int>& rows) {
+// same list), and how many for each reason.  Synchronizes the stream.
+int read_flagged(const ShardPlan& sp, char* ws, cudaStream_t st, std::vector<int>& rows, long long* why) {
   int n = 0;
   PESTI_CUDA_TRY(cudaMemcpyAsync(&n, ws + sp.o_nflag, sizeof(int), cudaMemcpyDeviceToHost, st), "flag count copy");
   PESTI_CUDA_TRY(cudaStreamSynchronize(st), "cudaStreamSynchronize");
   rows.assign((size_t)n, 0);
+  for (int q = 0; q < pesti::GR_KINDS; ++q) why[q] = 0;
   if (n > 0) {
     PESTI_CUDA_TRY(cudaMemcpy(rows.data(), ws + sp.o_flags, (size_t)n * sizeof(int), cudaMemcpyDeviceToHost),
                    "flag list copy");
+    for (int& r : rows) {
+      const uint32_t q = (uint32_t)r >> 28;
+      ++why[q < pesti::GR_KINDS ? q : 0];
+      r = (int)((uint32_t)r & 0x0fffffffu);
+    }
     std::sort(rows.begin(), rows.end());
   }
   return PESTI_OK;
@@ -803,7 +815,7 @@ int sample_sharded(pesti_sampler* s, pesti_comm* comm, int G, const void* d_logi
                    int params_on_device, const float* d_u, uint32_t* d_out, float* d_kept_p, uint32_t* d_kept_idx,
                    long long kept_width, int64_t* d_kept_count, void* stream) {
   PESTI_CUDA_TRY(cudaSetDevice(s->device), "cudaSetDevice");
-  cudaStream_t st = stream ? (cudaStream_t)stream : s->stream;
+  cudaStream_t st = (cudaStream_t)stream;  // NULL: the legacy default stream
   ShardCall c{};
   c.dtype = dtype;
   c.B = B;
@@ -833,6 +845,16 @@ int sample_sharded(pesti_sampler* s, pesti_comm* comm, int G, const void* d_logi
   unsigned char* rec_recv = (unsigned char*)(ws + sp.o_rec_recv);
   pesti::ShardTab* tab_recv = (pesti::ShardTab*)(ws + sp.o_tab_recv);
   s->ctr_zero_rows = 0;
+  // instrumentation (pesti_profile.h): the HBM pass, everything up to the
+  // last exchange, the finish
+  cudaEvent_t* pev = nullptr;
+  if (s->prof && s->prof_n < pesti_sampler::kProfMax) {
+    pev = s->prof_ev[s->prof_n++];
+    for (int q = 0; q < 4; ++q)
+      if (!pev[q]) PESTI_CUDA_TRY(cudaEventCreate(&pev[q]), "cudaEventCreate(profile)");
+  }
+  auto mark = [&](int q) { return pev ? cudaEventRecord(pev[q], st) : cudaSuccess; };
+  PESTI_CUDA_TRY(mark(0), "cudaEventRecord(profile)");
   if (comm) {
     const NcclApi& n = nccl_api();
     pesti::ShardSum* sum_send = (pesti::ShardSum*)(ws + sp.o_sum_send);
@@ -840,30 +862,34 @@ int sample_sharded(pesti_sampler* s, pesti_comm* comm, int G, const void* d_logi
     pesti::ShardTab* tab_send = (pesti::ShardTab*)(ws + sp.o_tab_send);
     rc = shard_phase1(sp, ws, 0, c, d_logits, sum_send);
     if (rc) return rc;
+    PESTI_CUDA_TRY(mark(1), "cudaEventRecord(profile)");
     ncclResult_t nr = n.all_gather(sum_send, sum_recv, (size_t)B * sizeof(pesti::ShardSum), ncclUint8, comm->comm, st);
     if (nr != ncclSuccess) return nccl_fail(nr, "ncclAllGather(summaries)");
     rc = shard_phase2(sp, ws, 0, comm->rank, s->device, c, d_logits, sum_recv, rec_send);
     if (rc) return rc;
     nr = n.all_gather(rec_send, rec_recv, (size_t)(B * sp.rec_stride), ncclUint8, comm->comm, st);
     if (nr != ncclSuccess) return nccl_fail(nr, "ncclAllGather(records)");
-    rc = shard_phase3(sp, ws, 0, comm->rank, c, d_logits, rec_recv, tab_send);
+    rc = shard_phase3(sp, ws, 0, comm->rank, s->device, c, d_logits, rec_recv, tab_send);
     if (rc) return rc;
     nr = n.all_gather(tab_send, tab_recv, (size_t)B * sizeof(pesti::ShardTab), ncclUint8, comm->comm, st);
     if (nr != ncclSuccess) return nccl_fail(nr, "ncclAllGather(tables)");
   } else {
     for (int g = 0; g < G; ++g)
       if ((rc = shard_phase1(sp, ws, g, c, lg(g), sum_recv + (size_t)g * B))) return rc;
+    PESTI_CUDA_TRY(mark(1), "cudaEventRecord(profile)");
     for (int g = 0; g < G; ++g)
       if ((rc = shard_phase2(sp, ws, g, g, s->device, c, lg(g), sum_recv, rec_recv + (size_t)g * B * sp.rec_stride)))
         return rc;
     for (int g = 0; g < G; ++g)
-      if ((rc = shard_phase3(sp, ws, g, g, c, lg(g), rec_recv, tab_recv + (size_t)g * B))) return rc;
+      if ((rc = shard_phase3(sp, ws, g, g, s->device, c, lg(g), rec_recv, tab_recv + (size_t)g * B))) return rc;
   }
+  PESTI_CUDA_TRY(mark(2), "cudaEventRecord(profile)");
   rc = shard_finish(sp, ws, c);
   if (rc) return rc;
+  PESTI_CUDA_TRY(mark(3), "cudaEventRecord(profile)");
   s->ctr_zero_rows = B;
   std::vector<int> rows;
-  rc = read_flagged(sp, ws, st, rows);
+  rc = read_flagged(sp, ws, st, rows, s->last_gathered_why);
   if (rc) return rc;
   s->last_gathered_rows = (long long)rows.size();
   return shard_gathered(s, comm, sp, c, d_logits, d_logits, rows);
@@ -944,7 +970,7 @@ int pesti_sample_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype
   if ((d_kept_p || d_kept_idx) && kept_width <= 0) return fail(PESTI_E_INVALID_ARG, "kept_width must be > 0");
   if (B == 0) return PESTI_OK;
   PESTI_CUDA_TRY(cudaSetDevice(s->device), "cudaSetDevice");
-  cudaStream_t st = stream ? (cudaStream_t)stream : s->stream;
+  cudaStream_t st = (cudaStream_t)stream;  // NULL: the legacy default stream
   pesti_sampling_params uni{};
   const pesti_sampling_params* d_per_row = nullptr;
   bool sorted_bufs = true;
@@ -961,7 +987,7 @@ int pesti_argmax_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype
   if (B > 0 && !d_out_tokens) return fail(PESTI_E_INVALID_ARG, "null output tokens");
   if (B == 0) return PESTI_OK;
   PESTI_CUDA_TRY(cudaSetDevice(s->device), "cudaSetDevice");
-  cudaStream_t st = stream ? (cudaStream_t)stream : s->stream;
+  cudaStream_t st = (cudaStream_t)stream;  // NULL: the legacy default stream
   pesti_sampling_params uni{};
   uni.temperature = 0.0f;
   uni.flags = PESTI_FLAG_GREEDY_IF_ZERO_T | (flags & PESTI_FLAG_ARGMAX_FIRST);
@@ -1141,6 +1167,12 @@ int pesti_sample_batch_sharded_emulated(pesti_sampler* s, int shards, const void
 }
 
 int64_t pesti_last_gathered_rows(pesti_sampler* s) { return s ? s->last_gathered_rows : -1; }
+
+int pesti_last_gathered_reasons(pesti_sampler* s, int64_t* counts) {
+  if (!s || !counts) return fail(PESTI_E_INVALID_ARG, "null argument");
+  for (int q = 0; q < pesti::GR_KINDS; ++q) counts[q] = s->last_gathered_why[q];
+  return PESTI_OK;
+}
 
 int pesti_profile_enable(pesti_sampler* s, int enable) {
   if (!s) return fail(PESTI_E_INVALID_ARG, "null sampler handle");

@@ -63,9 +63,12 @@ struct TabArgs {
 // One warp per row: lane j folds the shard's merged entries from the state
 // with bits base + j.  A run the state does not fit (or a replay marker) is
 // folded from the raw logits of its column range, one lane at a time.
+// Dynamic shared memory: TAB_SMEM bytes.
+constexpr size_t TAB_SMEM = FAST_ENTS * sizeof(FoldEnt) + STAGE * sizeof(float);
 __global__ void __launch_bounds__(32) shard_table_kernel(TabArgs a) {
-  __shared__ FoldEnt ent[FAST_ENTS];
-  __shared__ float stage[STAGE];
+  extern __shared__ __align__(16) unsigned char tab_smem[];
+  FoldEnt* ent = reinterpret_cast<FoldEnt*>(tab_smem);
+  float* stage = reinterpret_cast<float*>(ent + FAST_ENTS);
   const int lane = threadIdx.x;
   const long long b = blockIdx.x;
   ShardTab* out = a.tab_out + b;
@@ -146,7 +149,7 @@ struct FinishArgs {
   long long kept_width;
   int64_t* kept_count;
   int* nflag;                 // rows listed for the gathered path
-  int* flag_rows;
+  int* flag_rows;             // row | reason (GR_*) << 28
 };
 
 constexpr int FIN_KEYS = 4096;  // merged candidates a row may hold
@@ -177,16 +180,16 @@ __global__ void __launch_bounds__(K2_NT) shard_finish_kernel(FinishArgs a) {
       if (a.kept_idx) a.kept_idx[b * a.kept_width + j] = 0xffffffffu;
     }
   };
-  auto gather_row = [&]() {  // the row goes to the gathered path
+  auto gather_row = [&](uint32_t why) {  // the row goes to the gathered path
     if (tid == 0) {
       const int slot = atomicAdd(a.nflag, 1);
-      a.flag_rows[slot] = (int)b;
+      a.flag_rows[slot] = (int)((uint32_t)b | (why << 28));
       a.out[b] = 0xffffffffu;
     }
   };
   if (is_greedy(prm)) {  // generate(): temperature == 0 -> argmax (model.rs:517-521)
     if (ri.flags & MF_NAN) {  // Iterator::max_by over NaN: on whole rows
-      gather_row();
+      gather_row(GR_ROW);
       return;
     }
     const long long t = (prm.flags & PESTI_FLAG_ARGMAX_FIRST) ? ri.first_max : ri.last_max;
@@ -198,25 +201,25 @@ __global__ void __launch_bounds__(K2_NT) shard_finish_kernel(FinishArgs a) {
     return;
   }
   if (ri.uniform || !fast_topk(prm, VT)) {
-    gather_row();
+    gather_row(GR_ROW);
     return;
   }
   const long long k = (long long)prm.top_k;
   const long long keff = k < VT ? k : VT;
   if (tid == 0) {
     // s_{r+1} = F_r(s_r), each F_r read exactly from its table
-    uint32_t s = 0u;
-    int bad = 0, n = 0;
+    uint32_t s = 0u, bad = 0u;
+    int n = 0;
     for (int r = 0; r < a.G && !bad; ++r) {
       const ShardRec* rc = shard_rec(a.recs, a.rec_stride, a.B, r, b);
       const ShardTab* tb = a.tabs + (long long)r * a.B + b;
       if (rc->status != SH_OK || tb->status != SH_OK) {
-        bad = 1;
+        bad = rc->status != SH_OK ? rc->why : GR_CHAIN;
         break;
       }
       const uint32_t j = s - tb->base;
       if (j >= (uint32_t)TAB_W) {
-        bad = 1;
+        bad = GR_CHAIN;
         break;
       }
       s = tb->tab[j];
@@ -225,11 +228,13 @@ __global__ void __launch_bounds__(K2_NT) shard_finish_kernel(FinishArgs a) {
     }
     sh.off[a.G] = n;
     sh.s = s;
-    sh.bad = bad || n > FIN_KEYS || (long long)n < keff || !(bitsf(s) > 0.0f);
+    if (!bad && (n > FIN_KEYS || (long long)n < keff)) bad = GR_BOUND;
+    if (!bad && !(bitsf(s) > 0.0f)) bad = GR_CHAIN;
+    sh.bad = (int)bad;
   }
   __syncthreads();
   if (sh.bad) {
-    gather_row();
+    gather_row((uint32_t)sh.bad);
     return;
   }
   const float S = bitsf(sh.s);
@@ -255,7 +260,7 @@ __global__ void __launch_bounds__(K2_NT) shard_finish_kernel(FinishArgs a) {
     if (!(fdiv(shard_rec(a.recs, a.rec_stride, a.B, r, b)->bound, S) < pk)) sh.bad = 1;
   __syncthreads();
   if (sh.bad) {
-    gather_row();
+    gather_row(GR_BOUND);
     return;
   }
   if (tid == 0) {  // total over the kept list (sampling.rs:81)

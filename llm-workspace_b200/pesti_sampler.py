@@ -119,6 +119,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.pesti_sample_batch_sharded_emulated.restype = c_int
     lib.pesti_last_gathered_rows.argtypes = [vp]
     lib.pesti_last_gathered_rows.restype = i64
+    lib.pesti_last_gathered_reasons.argtypes = [vp, vp]
+    lib.pesti_last_gathered_reasons.restype = c_int
     _lib = lib
     return lib
 
@@ -248,6 +250,14 @@ class Sampler:
     def last_gathered_rows(self) -> int:
         """Rows of the last sharded call that took the gathered path."""
         return int(self._lib.pesti_last_gathered_rows(self._h))
+
+    GATHER_REASONS = ("", "row kind", "fold entries", "candidates", "chain", "top-k bound")
+
+    def last_gathered_reasons(self) -> dict:
+        """Those rows by reason (pesti_testing.h)."""
+        c = (ctypes.c_int64 * 6)()
+        _check(self._lib.pesti_last_gathered_reasons(self._h, c))
+        return {n: int(c[i]) for i, n in enumerate(self.GATHER_REASONS) if i and c[i]}
 
     def sample_batch_device_params(self, logits, d_params, u, out, stream=None):
         """Per-row parameters already on the device (a [B, 4] int32/f32 view of

@@ -132,14 +132,24 @@ def params_for(w: int, B: int, V: int):
     return out
 
 
-def make_logits(w: int, B: int = None, V: int = None, rows=None) -> np.ndarray:
-    """float32 logits of workload w ([B, V]); for workload 3 the values are
-    already bf16-representable (use f32_to_bf16_bits for the device copy)."""
+def make_logits(w: int, B: int = None, V: int = None, rows=None, cols=None) -> np.ndarray:
+    """float32 logits of workload w ([B, V], or the rows `rows` and columns
+    `cols` (a range) of it); for workload 3 the values are already
+    bf16-representable (use f32_to_bf16_bits for the device copy)."""
     spec = WORKLOADS[w]
     B = spec["B"] if B is None else B
     V = spec["V"] if V is None else V
     seed = 100 + w
     rows = range(B) if rows is None else rows
+    if cols is not None:
+        if w == 5:  # element-wise generator: only the columns asked for
+            out = np.empty((len(rows), len(cols)), dtype=np.float32)
+            for o, r in enumerate(rows):
+                z = normals(seed, r * V + cols.start, len(cols))
+                boost = row_hash(seed, r, V, 5)[cols.start:cols.stop] < np.uint64(int(0.001 * 2**64))
+                out[o] = (z * 2.5 + 6.0 * boost).astype(np.float32)
+            return out
+        return np.ascontiguousarray(make_logits(w, B, V, rows)[:, cols.start:cols.stop])
     out = np.empty((len(rows), V), dtype=np.float32)
     for o, r in enumerate(rows):
         z = normals(seed, r * V, V)

@@ -191,6 +191,7 @@ struct RowArgs {
   int64_t* kept_count;
   int* status;       // bit 0: a row needed sort buffers that were not provided
   int fast_enabled;  // the launch provides the fast path's shared memory
+  int fast_ents;     // and stages this many fold entries per row (<= FAST_ENTS)
   long long V_total;   // length of the whole row (V unless the call is one vocabulary shard)
   // vocabulary shard (shard = 1): instead of sampling, each row's fold from
   // the shard's approximate start state and its top candidates go to an
@@ -1481,7 +1482,8 @@ struct RowShared {
 };
 
 // Fast-path arrays, placed after RowShared in dynamic shared memory.
-constexpr int FAST_ENTS = 4096;  // fold entries of a row the fast path stages
+constexpr int FAST_ENTS = 4096;  // fold entries of a row the fast path can stage
+constexpr int FAST_ENTS_SHORT = 1024;  // the staging a launch over short rows provides
 constexpr int MERGE_EPT = FAST_ENTS / K2_NT;  // of them per thread in the merge
 constexpr int FAST_PAIRS = 2048; // (sub-slice, group) pairs of a row the fast path stages
 constexpr uint32_t ENT_REPLAY = 0xfffffffdu;  // staged entry: replay the whole sub-slice
@@ -1489,20 +1491,113 @@ struct FastSmem {
   unsigned long long key[FAST_CAND];
   float q[FAST_K];
   float stage[STAGE];
-  FoldEnt ent[FAST_ENTS];      // the row's entries in row order; after the merge (in
-                               // place), the same with consecutive runs of one binade merged
   Seg wseg[K2_NT / 32];        // block-wide segmented scan: per-warp totals and prefixes
   Seg wpre[K2_NT / 32];
   int wfl[K2_NT / 32];
-  uint16_t owner[FAST_ENTS];   // staging: the pair each entry comes from
   int pstart[FAST_PAIRS];      // staging: each pair's first entry in the row and in the pool
   int poff[FAST_PAIRS];
-  int total;                   // entries of the row (> FAST_ENTS: not staged)
+  int total;                   // entries of the row (> the launch's capacity: not staged)
   int nment;                   // merged entries
-  // followed by SubSurv[nsub] and int eoff[nsub] (scratch)
+  // followed by FoldEnt ent[cap] (the row's entries in row order; after the
+  // merge, in place, the same with consecutive runs of one binade merged),
+  // uint16_t owner[cap] (staging: the pair each entry comes from),
+  // SubSurv[nsub] and int eoff[nsub] (scratch); cap = RowArgs::fast_ents
 };
-__host__ __device__ inline size_t fast_smem_bytes(int nsub) {
-  return sizeof(FastSmem) + (size_t)nsub * (sizeof(SubSurv) + sizeof(int));
+__host__ __device__ inline size_t fast_smem_bytes(int nsub, int cap) {
+  return sizeof(FastSmem) + (size_t)cap * (sizeof(FoldEnt) + sizeof(uint16_t)) +
+         (size_t)nsub * (sizeof(SubSurv) + sizeof(int));
+}
+
+// Merge of a row's staged fold entries ent[0..total): consecutive runs of
+// one binade become one run (their increments compose; the merged run covers
+// the row up to the last one's end), so that the walk takes one step per
+// binade change or special.  A block-wide segmented scan with EPT consecutive
+// entries per thread (EPT * K2_NT >= total), written back in place (every
+// thread has read its entries before the first barrier); sets fs.nment.
+template <int EPT>
+__device__ __forceinline__ void merge_runs(FastSmem& fs, FoldEnt* ent, int total, RowShared& sh) {
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  auto single = [](uint32_t key) { return key == fold::SPECIAL || key == ENT_REPLAY; };
+  const FoldEnt none{KEY_NONE, 0u, 0u, 0u};
+  const int e0 = tid * EPT;
+  FoldEnt x[EPT];
+#pragma unroll
+  for (int i = 0; i < EPT; ++i) x[i] = e0 + i < total ? ent[e0 + i] : none;
+  const uint32_t kp = e0 > 0 && e0 < total ? ent[e0 - 1].lo : KEY_NONE;
+  const uint32_t kn = e0 + EPT < total ? ent[e0 + EPT].lo : KEY_NONE;
+  // h[i]: entry i starts a run; hn: the entry after the thread's last one does
+  bool h[EPT];
+  Seg agg{0u, 0u, 0u, KEY_NONE};
+  bool aflag = false;
+#pragma unroll
+  for (int i = 0; i < EPT; ++i) {
+    const uint32_t pk = i == 0 ? kp : x[i - 1].lo;
+    h[i] = e0 + i < total && (e0 + i == 0 || single(x[i].lo) || single(pk) || x[i].lo != pk);
+    const Seg v{x[i].a0, x[i].a1, 0u, x[i].lo};
+    if (e0 + i < total) {
+      agg = i == 0 ? v : seg_join(agg, v, h[i]);
+      aflag = aflag || h[i];
+    }
+  }
+  const bool hn = e0 + EPT < total && (single(kn) || single(x[EPT - 1].lo) || kn != x[EPT - 1].lo);
+  Seg inc = agg;
+  bool fl = aflag;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const Seg o = seg_shfl_up(inc, off);
+    const bool of = __shfl_up_sync(PESTI_FULL_MASK, fl, off);
+    if (lane >= off) {
+      inc = seg_join(o, inc, fl);
+      fl = fl || of;
+    }
+  }
+  if (lane == 31) {
+    fs.wseg[wid] = inc;
+    fs.wfl[wid] = fl ? 1 : 0;
+  }
+  __syncthreads();
+  if (wid == 0) {  // exclusive segmented scan over the warps' totals
+    constexpr int NW = K2_NT / 32;
+    const Seg idn{0u, 0u, 0u, KEY_NONE};
+    Seg wi = lane < NW ? fs.wseg[lane] : idn;
+    bool wf = lane < NW ? fs.wfl[lane] != 0 : false;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const Seg o = seg_shfl_up(wi, off);
+      const bool of = __shfl_up_sync(PESTI_FULL_MASK, wf, off);
+      if (lane >= off) {
+        wi = seg_join(o, wi, wf);
+        wf = wf || of;
+      }
+    }
+    const Seg we = seg_shfl_up(wi, 1);
+    if (lane < NW) fs.wpre[lane] = lane == 0 ? idn : we;
+  }
+  __syncthreads();
+  Seg pre = fs.wpre[wid];
+  const Seg ex = seg_shfl_up(inc, 1);
+  const bool exf = __shfl_up_sync(PESTI_FULL_MASK, fl, 1);
+  if (lane > 0) pre = seg_join(pre, ex, exf);
+  // an entry ends a merged run when the next one starts a run (or none follows)
+  bool end[EPT];
+  int nend = 0;
+#pragma unroll
+  for (int i = 0; i < EPT; ++i) {
+    end[i] = e0 + i < total && (i + 1 < EPT ? (e0 + i + 1 >= total || h[i + 1]) : (e0 + EPT >= total || hn));
+    nend += end[i] ? 1 : 0;
+  }
+  int tot;
+  int o = block_excl_scan_add(nend, sh.iscr, tot);
+  Seg cur = pre;
+#pragma unroll
+  for (int i = 0; i < EPT; ++i) {
+    if (e0 + i < total) {
+      cur = seg_join(cur, Seg{x[i].a0, x[i].a1, 0u, x[i].lo}, h[i]);
+      if (end[i]) ent[o++] = FoldEnt{single(x[i].lo) ? x[i].lo : cur.key, cur.a0, cur.a1, x[i].end};
+    }
+  }
+  if (tid == 0) fs.nment = tot;
+  __syncthreads();
 }
 
 // Rust's Iterator::max_by over the raw logits with partial_cmp (sampling.rs:115-122)
@@ -1830,7 +1925,10 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
   // ---------------- fast path: explicit top-k of at most FAST_K (one warp) ----------------
   if (a.fast_enabled && fast_topk(prm, VT)) {
     FastSmem& fs = *reinterpret_cast<FastSmem*>(row_smem + sizeof(RowShared));
-    SubSurv* ss = reinterpret_cast<SubSurv*>(row_smem + sizeof(RowShared) + sizeof(FastSmem));
+    const int cap = a.fast_ents;
+    FoldEnt* fent = reinterpret_cast<FoldEnt*>(row_smem + sizeof(RowShared) + sizeof(FastSmem));
+    uint16_t* fown = reinterpret_cast<uint16_t*>(fent + cap);
+    SubSurv* ss = reinterpret_cast<SubSurv*>(fown + cap);
     int* eoff = reinterpret_cast<int*>(ss + nsub);
     // stage the row's fold entries, compacted, with the whole block: one
     // thread per (sub-slice, group) pair in row order; a sub-slice with an
@@ -1881,129 +1979,42 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
           fs.pstart[t] = ex;
           fs.poff[t] = off;
         }
-        if (t < FAST_PAIRS && ex + ne <= FAST_ENTS) {
+        if (t < FAST_PAIRS && ex + ne <= cap) {
           if (inl) {  // a one-entry task keeps its entry in its record
-            fs.ent[ex] = ient;
-            fs.owner[ex] = 0xffffu;
+            fent[ex] = ient;
+            fown[ex] = 0xffffu;
           } else {
-            for (int i = 0; i < ne; ++i) fs.owner[ex + i] = (uint16_t)t;
+            for (int i = 0; i < ne; ++i) fown[ex + i] = (uint16_t)t;
           }
         }
         base += tot;
       }
-      if (npair > FAST_PAIRS) base = FAST_ENTS + 1;  // too many pairs to stage: the generic path
+      if (npair > FAST_PAIRS) base = cap + 1;  // too many pairs to stage: the generic path
       __syncthreads();
-      if (base <= FAST_ENTS) {
+      if (base <= cap) {
         for (int e = tid; e < base; e += K2_NT) {
-          const int t = fs.owner[e];
+          const int t = fown[e];
           if (t == 0xffff) continue;  // staged already
           const int off = fs.poff[t];
           if (off < 0) {
             const long long qend = ((long long)(-1 - off) + 1) * a.SL;
-            fs.ent[e] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)(qend < V ? qend : V)};
+            fent[e] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)(qend < V ? qend : V)};
           } else {
-            fs.ent[e] = pool[off + (e - fs.pstart[t])];
+            fent[e] = pool[off + (e - fs.pstart[t])];
           }
         }
       }
       if (tid == 0) fs.total = base;
       __syncthreads();
     }
-    // Merge consecutive runs of one binade (their increments compose; the
-    // merged run covers the row up to the last one's end), so that the walk
-    // below takes one step per binade change or special.  A block-wide
-    // segmented scan, MERGE_EPT consecutive entries per thread, written back
-    // in place (every thread has read its entries before the first barrier).
-    if (fs.total <= FAST_ENTS) {
-      const int total = fs.total;
-      auto single = [](uint32_t key) { return key == fold::SPECIAL || key == ENT_REPLAY; };
-      const FoldEnt none{KEY_NONE, 0u, 0u, 0u};
-      const int e0 = tid * MERGE_EPT;
-      FoldEnt x[MERGE_EPT];
-#pragma unroll
-      for (int i = 0; i < MERGE_EPT; ++i) x[i] = e0 + i < total ? fs.ent[e0 + i] : none;
-      const uint32_t kp = e0 > 0 && e0 < total ? fs.ent[e0 - 1].lo : KEY_NONE;
-      const uint32_t kn = e0 + MERGE_EPT < total ? fs.ent[e0 + MERGE_EPT].lo : KEY_NONE;
-      // h: entry i starts a run; the last one is followed by a start (or the end)
-      bool h[MERGE_EPT];
-      Seg agg{0u, 0u, 0u, KEY_NONE};
-      bool aflag = false;
-#pragma unroll
-      for (int i = 0; i < MERGE_EPT; ++i) {
-        const uint32_t pk = i == 0 ? kp : x[i - 1].lo;
-        h[i] = e0 + i < total && (e0 + i == 0 || single(x[i].lo) || single(pk) || x[i].lo != pk);
-        const Seg v{x[i].a0, x[i].a1, 0u, x[i].lo};
-        if (e0 + i < total) {
-          agg = i == 0 ? v : seg_join(agg, v, h[i]);
-          aflag = aflag || h[i];
-        }
-      }
-      const bool hn = e0 + MERGE_EPT < total &&
-                      (single(kn) || single(x[MERGE_EPT - 1].lo) || kn != x[MERGE_EPT - 1].lo);
-      Seg inc = agg;
-      bool fl = aflag;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const Seg o = seg_shfl_up(inc, off);
-        const bool of = __shfl_up_sync(PESTI_FULL_MASK, fl, off);
-        if (lane >= off) {
-          inc = seg_join(o, inc, fl);
-          fl = fl || of;
-        }
-      }
-      if (lane == 31) {
-        fs.wseg[wid] = inc;
-        fs.wfl[wid] = fl ? 1 : 0;
-      }
-      __syncthreads();
-      if (wid == 0) {  // exclusive segmented scan over the warps' totals
-        constexpr int NW = K2_NT / 32;
-        const Seg idn{0u, 0u, 0u, KEY_NONE};
-        Seg wi = lane < NW ? fs.wseg[lane] : idn;
-        bool wf = lane < NW ? fs.wfl[lane] != 0 : false;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          const Seg o = seg_shfl_up(wi, off);
-          const bool of = __shfl_up_sync(PESTI_FULL_MASK, wf, off);
-          if (lane >= off) {
-            wi = seg_join(o, wi, wf);
-            wf = wf || of;
-          }
-        }
-        const Seg we = seg_shfl_up(wi, 1);
-        if (lane < NW) fs.wpre[lane] = lane == 0 ? idn : we;
-      }
-      __syncthreads();
-      Seg pre = fs.wpre[wid];
-      const Seg ex = seg_shfl_up(inc, 1);
-      const bool exf = __shfl_up_sync(PESTI_FULL_MASK, fl, 1);
-      if (lane > 0) pre = seg_join(pre, ex, exf);
-      // an entry ends a merged run when the next one starts a run (or none follows)
-      int nend = 0;
-#pragma unroll
-      for (int i = 0; i < MERGE_EPT; ++i) {
-        const bool nxt = i + 1 < MERGE_EPT ? (e0 + i + 1 >= total || h[i + 1]) : (e0 + MERGE_EPT >= total || hn);
-        nend += (e0 + i < total && nxt) ? 1 : 0;
-      }
-      int tot;
-      int o = block_excl_scan_add(nend, sh.iscr, tot);
-      Seg cur = pre;
-#pragma unroll
-      for (int i = 0; i < MERGE_EPT; ++i) {
-        if (e0 + i < total) {
-          cur = seg_join(cur, Seg{x[i].a0, x[i].a1, 0u, x[i].lo}, h[i]);
-          const bool nxt = i + 1 < MERGE_EPT ? (e0 + i + 1 >= total || h[i + 1]) : (e0 + MERGE_EPT >= total || hn);
-          if (nxt) fs.ent[o++] = FoldEnt{single(x[i].lo) ? x[i].lo : cur.key, cur.a0, cur.a1, x[i].end};
-        }
-      }
-      if (tid == 0) fs.nment = tot;
-      __syncthreads();
-    }
+    // merge consecutive runs of one binade (fewer steps for the walk below)
+    if (fs.total <= 2 * K2_NT) merge_runs<2>(fs, fent, fs.total, sh);
+    else if (fs.total <= cap) merge_runs<MERGE_EPT>(fs, fent, fs.total, sh);
     const int C = a.cand_count[b];
     // a shard lists any number of candidates up to FAST_CAND (the row's k-th
     // largest may lie in another shard)
     const bool cand_ok = (a.shard || C >= keff) && C <= FAST_CAND;
-    if (wid == 1 && fs.total <= FAST_ENTS && cand_ok) {
+    if (wid == 1 && fs.total <= cap && cand_ok) {
       // candidates by (e desc, index asc) while warp 0 folds; the order by p
       // = e/S differs only inside groups of equal p (fixed up below)
       for (int j = lane; j < C; j += 32)
@@ -2023,7 +2034,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
 
     }
     uint32_t s = a.shard ? fbits(ri.s_start) : 0u;
-    if (wid == 0 && fs.total <= FAST_ENTS) {
+    if (wid == 0 && fs.total <= cap) {
       // softmax denominator (sampling.rs:128): walk the merged entries with the
       // exact state.  An entry the state does not fit (or a replay marker) is folded from
       // the raw logits of the row range it covers, from the state before it
@@ -2035,7 +2046,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
         for (; i < nm && fi < 0; i += 4) {
           FoldEnt en[4];  // four at a time: their loads do not depend on the state
 #pragma unroll
-          for (int u = 0; u < 4; ++u) en[u] = fs.ent[i + u < nm ? i + u : i];
+          for (int u = 0; u < 4; ++u) en[u] = fent[i + u < nm ? i + u : i];
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             if (fi < 0 && i + u < nm) {
@@ -2050,8 +2061,8 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
           }
         }
         if (fi < 0) break;
-        const uint32_t from = fi > 0 ? fs.ent[fi - 1].end : 0u;
-        const uint32_t to = fs.ent[fi].end;
+        const uint32_t from = fi > 0 ? fent[fi - 1].end : 0u;
+        const uint32_t to = fent[fi].end;
         const void* src = a.dtype == PESTI_BF16 ? (const void*)((const uint16_t*)row + from)
                                                 : (const void*)((const float*)row + from);
         s = warp_fold(src, a.dtype, (long long)to - from, s, fs.stage, scale, T, m);
@@ -2067,14 +2078,14 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
       if (wid == 0) {
         ShardRec* rc = reinterpret_cast<ShardRec*>(a.rec + b * a.rec_stride);
         ShardCand* cd = reinterpret_cast<ShardCand*>(rc + 1);
-        const bool ok = fs.total <= FAST_ENTS && cand_ok;
+        const bool ok = fs.total <= cap && cand_ok;
         const int nl = ok ? (C < a.ksh ? C : a.ksh) : 0;
         for (int j = lane; j < nl; j += 32) {
           const unsigned long long kv = fs.key[j];
           cd[j] = ShardCand{(uint32_t)(kv >> 32), ~(uint32_t)(kv & 0xffffffffull) + (uint32_t)a.col0};
         }
         if (ok)
-          for (int i = lane; i < fs.nment; i += 32) a.ment_g[b * FAST_ENTS + i] = fs.ent[i];
+          for (int i = lane; i < fs.nment; i += 32) a.ment_g[b * FAST_ENTS + i] = fent[i];
         if (lane == 0) {
           ShardRec r;
           r.delta = ok ? (double)bitsf(s) - (double)ri.s_start : 0.0;
@@ -2082,7 +2093,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
           r.status = ok ? SH_OK : SH_FAIL;
           r.bound = ok && C > a.ksh ? bitsf((uint32_t)(fs.key[a.ksh] >> 32)) : ri.e_tau;
           r.n = nl;
-          r.why = fs.total > FAST_ENTS ? GR_ENTRIES : (ok ? 0u : GR_CANDS);
+          r.why = fs.total > cap ? GR_ENTRIES : (ok ? 0u : GR_CANDS);
           r.pad = 0u;
           *rc = r;
           a.nment_g[b] = ok ? fs.nment : -1;
@@ -2090,7 +2101,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
       }
       return;
     }
-    if (wid == 0 && fs.total <= FAST_ENTS) {
+    if (wid == 0 && fs.total <= cap) {
       const float S = bitsf(s);
       bool ok = cand_ok;
       if (ok) {
@@ -2143,7 +2154,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
         }
       }
       if (lane == 0) sh.fast_ok = ok ? 1 : 0;
-    } else if (tid == 0 && fs.total > FAST_ENTS) {
+    } else if (tid == 0 && fs.total > cap) {
       sh.fast_ok = 0;
     }
     __syncthreads();

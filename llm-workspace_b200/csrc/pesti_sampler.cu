@@ -275,7 +275,7 @@ pesti::SliceArgs make_slice_args(const Plan& p, char* ws, const void* d_logits, 
   sa.band = 0x1p-12f;
   // the fast path stages the row's fold entries in shared memory; with very
   // many sub-slices it does not fit and all rows take the generic path
-  const size_t fast_bytes = pesti::fast_smem_bytes((int)p.nsub);
+  const size_t fast_bytes = pesti::fast_smem_bytes((int)p.nsub, pesti::FAST_ENTS);
   sa.fast_enabled = sizeof(pesti::RowShared) + fast_bytes <= kRowSmemLimit ? 1 : 0;
   return sa;
 }
@@ -372,11 +372,15 @@ pesti::RowArgs make_row_args(const Plan& p, char* ws, const pesti::SliceArgs& sa
   ra.status = (int*)(ws + p.o_status);
   ra.fast_enabled = sa.fast_enabled;
   ra.V_total = sa.V_total;
+  // fold entries the row kernel stages per row: rows up to 128k columns make
+  // a few hundred (about one per 256 survivors, plus the single elements)
+  ra.fast_ents = sa.V_total > 131072 ? pesti::FAST_ENTS : pesti::FAST_ENTS_SHORT;
   return ra;
 }
 
 int launch_row(const Plan& p, int device, const pesti::RowArgs& ra, cudaStream_t st) {
-  const size_t smem2 = sizeof(pesti::RowShared) + (ra.fast_enabled ? pesti::fast_smem_bytes((int)p.nsub) : 0);
+  const size_t smem2 =
+      sizeof(pesti::RowShared) + (ra.fast_enabled ? pesti::fast_smem_bytes((int)p.nsub, ra.fast_ents) : 0);
   if (smem2 > 48 * 1024) {
     int rc = ensure_row_smem_limit(device);
     if (rc) return rc;
@@ -631,6 +635,7 @@ int shard_phase2(const ShardPlan& sp, char* ws, int li, int r, int device, const
   if (rc) return rc;
   pesti::RowArgs ra = make_row_args(sp.local, lws, sa, c.d_u, c.d_out, nullptr, nullptr, 0, nullptr);
   ra.shard = 1;
+  ra.fast_ents = pesti::FAST_ENTS;
   ra.col0 = (long long)r * c.Vs;
   ra.rec = rec_out;
   ra.rec_stride = sp.rec_stride;

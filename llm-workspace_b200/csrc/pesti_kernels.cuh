@@ -42,6 +42,7 @@ constexpr int QCAP = 512;         // survivor queue per warp (power of two)
 constexpr int GR = 8;             // survivors per lane in one classification task
 constexpr int GROUP = 32 * GR;    // survivors per classification task
 constexpr int POOL_CAP = 4096;    // fold entries per row (all its classification tasks)
+constexpr int UNIT = 256;         // elements of one classification unit of the fused pass
 constexpr int STAGE = 256;        // values staged per round trip by warp_fold
 constexpr uint32_t TR_SAT = 0x40000000u;  // saturation of fold increments (>= any binade)
 
@@ -88,6 +89,16 @@ struct ShardSum {
 };
 static_assert(sizeof(ShardSum) == 40, "ShardSum is exchanged as raw bytes");
 
+// The pass over HBM's running state of a sub-slice at the start of each
+// UNIT-element unit, for the fused pass: the approximate mass of the
+// sub-slice's elements before the unit, relative to 2^mlog, and their max.
+struct UnitPre {
+  float mass;   // sum of 2^(x*c2 - mlog) over the sub-slice's elements before the unit
+  float mlog;   // log2-unit max those sums are relative to (-inf: none)
+  float pmax;   // max raw logit of the sub-slice before the unit (-inf: none)
+  float pad;
+};
+
 struct SubPre {       // per sub-slice, from the row prologue
   double A;           // approximate softmax mass of the earlier sub-slices
   float P;            // max raw logit of the earlier sub-slices
@@ -101,21 +112,22 @@ struct FoldEnt {      // one entry of a sub-slice's part of the softmax fold
                       // row from the previous entry's end (the elements between are no-ops)
 };
 
-struct SubSurv {      // survivor_kernel, one per sub-slice
-  int32_t count;      // survivors stored at the sub-slice's own start
-  int32_t ngroups;    // classification tasks of the sub-slice (fast-path rows)
+struct SubSurv {      // one per sub-slice: survivor_kernel, or the fused pass (fast-path rows)
+  int32_t count;      // survivors stored at the sub-slice's own start (survivor_kernel)
+  int32_t ngroups;    // classification groups of the sub-slice (tasks, or the fused pass's units)
   int32_t pad;        // survivor_kernel: the classification tasks list the candidates;
-                      // row_kernel: the sub-slice is replayed
+                      // row_kernel scratch: the sub-slice is replayed
   float pruned_max;   // largest raw logit dropped (-inf if none)
 };
 
-struct ClassTask {    // one group of GROUP survivors of a sub-slice
+
+struct ClassTask {    // one group of GROUP survivors of a sub-slice (task-queue classification)
   int32_t b;          // row
   int32_t qj;         // sub-slice * jmax + group
 };
 
-struct GroupEnt {     // classify_kernel, one per task: its fold entries
-  uint32_t ent[4];    // inl: the task's only entry (a FoldEnt), kept here instead of the pool
+struct GroupEnt {     // one per classification group (task or fused unit): its fold entries
+  uint32_t ent[4];    // inl: the unit's only entry (a FoldEnt), kept here instead of the pool
   int32_t off;        // first entry in the row's pool
   int32_t nent;       // entries (0 with replay)
   int32_t replay;     // the pool was full: the row kernel replays the sub-slice
@@ -137,10 +149,13 @@ struct SliceArgs {
   int* row_ctr;     // [B] blocks of the row finished (reset by the last one)
   SubSurv* surv;    // [B][P*K1_WARPS]
   float* seg_max;   // [B][nseg]
+  UnitPre* unit_pre;  // [B][nunit], nunit = ceil(V / UNIT)
   float* surv_raw;  // [B][V]: raw logits of the survivors of sub-slice s, compacted at its own start
   uint32_t* surv_idx;
-  int jmax;         // classification groups per sub-slice (ceil(SL / GROUP))
-  ClassTask* tasks; // [B*P*K1_WARPS*jmax]
+  int jmax;         // classification groups per sub-slice (ceil(SL / UNIT) = ceil(SL / GROUP))
+  int* item_next;   // items of the fused pass taken from the counter
+  int fused;        // the rows of the fast path take the fused pass (else: survivors + task queue)
+  ClassTask* tasks; // [B*P*K1_WARPS*jmax] task-queue classification
   int* task_count;  // tasks queued
   int* task_next;   // tasks taken
   GroupEnt* gsurv;  // [B][P*K1_WARPS][jmax]
@@ -730,6 +745,7 @@ __global__ void __launch_bounds__(K1_NT) slice_stats_kernel(SliceArgs a) {
     a.cand_count[b] = 0;
     a.pool_ctr[b] = 0;
     if (b == 0) {
+      *a.item_next = 0;
       *a.task_count = 0;
       *a.task_next = 0;
     }
@@ -741,7 +757,7 @@ __global__ void __launch_bounds__(K1_NT) slice_stats_kernel(SliceArgs a) {
   int last_nan = -1;
   uint32_t flags = 0;
   uint32_t sub_key = fkey(NEG_INF);     // max over the sub-slice, as an ordered key
-  float run_m = NEG_INF, run_s = 0.0f;  // online partial sum, log2 units
+  float run_m = NEG_INF, run_s = 0.0f;  // online partial sum, log2 units (per lane; fused: of the warp)
   float* segmax = a.seg_max + b * a.nseg;
   stream_subslice<TIn, VE, U, VEC>(row, start, end, [&](const float* x, long long pos0, int nv) {
     float lm = NEG_INF;
@@ -765,30 +781,54 @@ __global__ void __launch_bounds__(K1_NT) slice_stats_kernel(SliceArgs a) {
         }
       }
     }
-    // approximate partial softmax sum (steers the fold speculation only)
-    const float nm = fmaxf(run_m, lm * c2);
-    if (nm > NEG_INF) {
-      float acc = run_s * ex2_approx(run_m - nm);
-#pragma unroll
-      for (int e = 0; e < VE; ++e)
-        if (e < nv && !is_nan(x[e])) acc += ex2_approx(fmaf(x[e], c2, -nm));
-      run_s = acc;
-      run_m = nm;
-    }
+    const long long seg = (pos0 - (long long)lane * VE) / (32LL * VE);
     const uint32_t sk = __reduce_max_sync(PESTI_FULL_MASK, fkey(lm));
+    // approximate partial softmax sum (steers the fold speculation only)
+    if (a.fused) {
+      // warp-uniform running sum of the sub-slice, recorded at every unit start
+      constexpr int SPU = UNIT / (32 * VE);  // segments per unit
+      if (seg % SPU == 0 && lane == 0)
+        a.unit_pre[b * ((a.V + UNIT - 1) / UNIT) + seg / SPU] = UnitPre{run_s, run_m, fkey_inv(sub_key), 0.0f};
+      const float smax = fkey_inv(sk);
+      if (smax > NEG_INF) {
+        const float sc = smax * c2;
+        float ls = 0.0f;
+#pragma unroll
+        for (int e = 0; e < VE; ++e)
+          if (e < nv && !is_nan(x[e])) ls += ex2_approx(fmaf(x[e], c2, -sc));
+        ls = warp_reduce_add(ls);
+        const float nm = fmaxf(run_m, sc);
+        run_s = (run_m > NEG_INF ? run_s * ex2_approx(run_m - nm) : 0.0f) + ls * ex2_approx(sc - nm);
+        run_m = nm;
+      }
+    } else {
+      // per lane, combined at the end
+      const float nm = fmaxf(run_m, lm * c2);
+      if (nm > NEG_INF) {
+        float acc = run_s * ex2_approx(run_m - nm);
+#pragma unroll
+        for (int e = 0; e < VE; ++e)
+          if (e < nv && !is_nan(x[e])) acc += ex2_approx(fmaf(x[e], c2, -nm));
+        run_s = acc;
+        run_m = nm;
+      }
+    }
     sub_key = sk > sub_key ? sk : sub_key;
-    if (lane == 0) segmax[(pos0 - (long long)lane * VE) / (32LL * VE)] = fkey_inv(sk);
+    if (lane == 0) segmax[seg] = fkey_inv(sk);
   });
   const float mx = fkey_inv(sub_key);
   const int ln = (int)__reduce_max_sync(PESTI_FULL_MASK, (unsigned)(last_nan + 1)) - 1;
   const uint32_t fl = __reduce_or_sync(PESTI_FULL_MASK, flags);
-  const float wm = warp_reduce_fmax(run_m);
-  float ws = (run_m > NEG_INF && wm > NEG_INF) ? run_s * ex2_approx(run_m - wm) : 0.0f;
-  ws = warp_reduce_add(ws);
+  float ws = run_s;  // fused: already the warp's
+  if (!a.fused) {
+    const float wm = warp_reduce_fmax(run_m);
+    ws = (run_m > NEG_INF && wm > NEG_INF) ? run_s * ex2_approx(run_m - wm) : 0.0f;
+    ws = warp_reduce_add(ws);
+  }
   if (lane == 0) {
     SubStat m;
     m.max_raw = mx;
-    m.sum_rel = ws;  // relative to 2^(mx*c2) (wm == mx*c2: the same float product)
+    m.sum_rel = ws;  // relative to 2^(mx*c2) (the warp's max of run_m == mx*c2: the same float product)
     m.last_nan = ln;
     m.flags = fl;
     a.stats[b * (long long)a.P * K1_WARPS + sub] = m;
@@ -895,7 +935,8 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// One warp per sub-slice.  The sub-slice is read from L2 in 32*VE-element
+// One warp per sub-slice (with the fused pass: of a row NOT on the fast
+// path).  The sub-slice is read from L2 in 32*VE-element
 // chunks (one 16-byte load per lane) with K1_STAGES chunks in flight; every
 // element either provably leaves every fold unchanged (derivation above) or
 // survives, and survivors are stored (raw logit and index) in row order at the
@@ -921,6 +962,8 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
   const float t_eff = scale ? T : 1.0f;
   const float NEG_INF = -__int_as_float(0x7f800000);
   SubSurv* so = a.surv + b * nsub + sub;
+  // with the fused pass, the rows of the fast path are its alone
+  if (a.fused && a.fast_enabled && fast_topk(prm, a.V_total) && !is_greedy(prm) && !ri.uniform) return;
   if (is_greedy(prm) || ri.uniform) {
     if (lane == 0) *so = SubSurv{0, 0, 0, NEG_INF};
     return;
@@ -1103,22 +1146,19 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Classification of survivor groups into fold entries (rows of the fast path).
+// Classification of survivors into fold entries (rows of the fast path).
 //
-// Each task is GROUP consecutive survivors of one sub-slice.  Its approximate
-// starting state is the sub-slice's prefix mass A plus the masses of the
-// sub-slice's earlier groups, so the tasks are independent and a persistent
-// grid of warps takes them from a counter; the heavy start of every row (where
-// the running sum is still small and most elements survive) is spread over
-// many warps.  Lane l takes survivors [l*g, l*g + g), g = ceil(n/32): one warp
-// scan gives every element its approximate running state and a segmented scan
-// over the lanes joins the runs that cross lane boundaries.  The per-element
-// loops are kept rolled (the values wait in shared memory between the
-// passes): this code runs out of instruction cache long before it runs out of
-// issue slots.
+// A group is up to GROUP consecutive survivors of one sub-slice, classified
+// against an approximate fold state at its first survivor.  Lane l takes
+// survivors [l*g, l*g + g), g = ceil(n/32): one warp scan gives every element
+// its approximate running state and a segmented scan over the lanes joins the
+// runs that cross lane boundaries.  The per-element loops are kept rolled (the
+// values wait in shared memory between the passes): this code runs out of
+// instruction cache long before it runs out of issue slots.
 // ---------------------------------------------------------------------------
+
 struct ClassShared {
-  float raw[K1_WARPS][GROUP];     // the task's survivors (raw logit, row index)
+  float raw[K1_WARPS][GROUP];     // the group's survivors (raw logit, row index)
   uint32_t idx[K1_WARPS][GROUP];
   float ea[K1_WARPS][GROUP];
   uint32_t ck[K1_WARPS][GROUP];
@@ -1126,20 +1166,17 @@ struct ClassShared {
   uint32_t c1[K1_WARPS][GROUP];
 };
 
-__global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
-  __shared__ ClassShared sh;
-  grid_dep_launch_next();
-  grid_dep_wait();
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+// Group j of sub-slice `sub` of row b: n (1..GROUP) survivors in graw/gidx
+// (this warp's shared arrays), s_approx the approximate fold state before the
+// first of them.  Writes the group's GroupEnt and, unless it is one clean
+// run, its entries in the row's pool; returns the group's approximate mass
+// (the sum of the approximate exps).  All 32 lanes call it.
+__device__ __forceinline__ float classify_group(const SliceArgs& a, long long b, long long sub, int j, int n,
+                                            double s_approx, bool scale, float T, float m, float* graw,
+                                            uint32_t* gidx, float* eas, uint32_t* cks, uint32_t* c0s,
+                                            uint32_t* c1s) {
+  const int lane = threadIdx.x & 31;
   const int nsub = a.P * K1_WARPS;
-  const long long V = a.V;
-  const int ntasks = *a.task_count;
-  float* graw = sh.raw[w];
-  uint32_t* gidx = sh.idx[w];
-  float* eas = sh.ea[w];
-  uint32_t* cks = sh.ck[w];
-  uint32_t* c0s = sh.c0[w];
-  uint32_t* c1s = sh.c1[w];
   // e_exact lies within a relative 2*RELERR of the approximation (margin for
   // the float arithmetic of the bounds below)
   constexpr float DE = 2.0f * PESTI_EXPF_APPROX_RELERR;
@@ -1150,12 +1187,252 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
   // replayed there, so the band trades entries for replays and never decides
   // a result.
   const float BAND = a.band;
-  // Each warp's first task is its own index (a burst of thousands of atomics
-  // on one counter would serialise the start); later ones come from the
-  // counter, claimed while the current task runs.  The list is taken from its
-  // end: the survivor pass queues the tasks of its slowest warps (the dense
-  // start of each row, whose tasks cost the most) last.
-  // The next task's index and record are fetched while a task runs.
+  // element i of the group: its run key (binade or SPECIAL) and increments
+  auto classify = [&](int i, float ea, float av, float bv, uint32_t& key, uint32_t& k0, uint32_t& k1) {
+    uint32_t lo = 0u;
+    bool special;
+    const float eu = ea * (1.0f + DE);  // upper bound of the exact value
+    if (av < 0x1p-126f) {
+      special = eu >= 0x1p-127f || bv > 0x1p-126f * (1.0f - BAND);
+    } else {
+      lo = fbits(av) & 0x7f800000u;
+      const float lov = bitsf(lo);
+      special = eu >= bitsf(lo - 0x00800000u) || av < lov * (1.0f + BAND) || bv > 2.0f * lov * (1.0f - BAND);
+    }
+    bool need_exact = special;
+    k0 = k1 = 0u;
+    if (!special) {
+      const uint32_t E = lo >> 23;  // w = 2^(E-150) (E = 0: the subnormal grid 2^-149)
+      const int sh2 = 150 - (int)(E == 0u ? 1u : E);
+      if (ea == 0.0f) {
+        need_exact = E < 40u;  // exact e < 4.5e-38: rounds to 0 on any grid >= 2^-110
+      } else {
+        const float tt = __uint_as_float(fbits(ea) + ((uint32_t)sh2 << 23));  // ea/w, exact scaling
+        const float kr = rintf(tt);
+        const float slack = 0.5f - fabsf(tt - kr);
+        if (slack <= tt * DE + 0x1p-24f) need_exact = true;
+        else k0 = k1 = (uint32_t)kr;
+      }
+    }
+    if (need_exact) {
+      const float raw = graw[i];
+      const float ex = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127, exact
+      if (special) {
+        k0 = fbits(ex);
+      } else {
+        k0 = fbits(fadd(bitsf(lo), ex)) - lo;
+        k1 = fbits(fadd(bitsf(lo + 1u), ex)) - (lo + 1u);
+      }
+    }
+    key = special ? fold::SPECIAL : lo;
+  };
+
+  const int g = (n + 31) >> 5;  // elements per lane: the group's fill decides the loop length
+  const int i0 = lane * g;
+  const int nl = n - i0 < 0 ? 0 : (n - i0 > g ? g : n - i0);  // valid elements of the lane
+  __syncwarp();
+  // pass A: approximate exps (sampling.rs:46,127 within 2^-22)
+  float ltot = 0.0f;
+#pragma unroll 1
+  for (int jj = 0; jj < nl; ++jj) {
+    const float raw = graw[i0 + jj];
+    const float e = pesti_expf_approx(fsub(scale ? fdiv(raw, T) : raw, m));
+    eas[jj * 32 + lane] = e;
+    ltot += e;
+  }
+  const float lincl = warp_incl_scan_add(ltot);
+  const float gtot = __shfl_sync(PESTI_FULL_MASK, lincl, 31);
+  // approximate states as floats relative to the carried double (the guard
+  // band is 2^-12; float rounding is 2^-24)
+  const float sb = (float)s_approx;
+  const float lbase = lincl - ltot;
+
+  // A clean group: the whole range of its approximate states lies inside one
+  // binade (within the guard band), so every element is a plain increment
+  // k = rint(e/w) of one run (e < lo there, so k is in the binade's units).
+  // k comes from the approximation where it decides it and from the exact
+  // exp otherwise; unless some element is a tie (its k depends on the
+  // parity of the state), the group's fold is that run with the sum of the
+  // increments: one entry, no segmentation.
+  {
+    bool clean = false;
+    uint32_t clo = 0u;
+    if (sb >= 0x1p-126f) {
+      clo = fbits(sb) & 0x7f800000u;
+      const float lov = bitsf(clo);
+      clean = sb >= lov * (1.0f + BAND) && sb + gtot <= 2.0f * lov * (1.0f - BAND);
+    }
+    if (clean) {
+      const int sh2 = 150 - (int)(clo >> 23);  // w = 2^(E-150)
+      uint32_t ksum = 0u;
+      bool decided = true;
+#pragma unroll 1
+      for (int jj = 0; jj < nl; ++jj) {
+        const float ea = eas[jj * 32 + lane];
+        bool exact = false;
+        if (ea == 0.0f) {
+          exact = (clo >> 23) < 40u;  // else: exact e < 4.5e-38 rounds to 0 on this grid
+        } else {
+          const float tt = __uint_as_float(fbits(ea) + ((uint32_t)sh2 << 23));  // ea/w, exact scaling
+          const float kr = rintf(tt);
+          const float slack = 0.5f - fabsf(tt - kr);
+          if (slack > tt * DE + 0x1p-24f) ksum += (uint32_t)kr;
+          else exact = true;
+        }
+        if (exact) {
+          const float raw = graw[i0 + jj];
+          const float ex = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127, exact
+          const uint32_t k0 = fbits(fadd(bitsf(clo), ex)) - clo;
+          const uint32_t k1 = fbits(fadd(bitsf(clo + 1u), ex)) - (clo + 1u);
+          decided = decided && k0 == k1;
+          ksum += k0;
+        }
+      }
+      if (__all_sync(PESTI_FULL_MASK, decided)) {
+        const uint32_t inc = tr_sat(warp_reduce_add(ksum));  // each < 2^22, at most 256 of them
+        if (lane == 0)
+          a.gsurv[(b * nsub + sub) * a.jmax + j] = GroupEnt{{clo, inc, inc, gidx[n - 1] + 1u}, 0, 1, 0, 1};
+        return gtot;
+      }
+    }
+  }
+  // the key of the lane's last element decides whether the next lane's first
+  // element continues its run
+  uint32_t last_key = KEY_NONE;
+  if (nl > 0) {
+    const float el = eas[(nl - 1) * 32 + lane];
+    uint32_t k0, k1;
+    classify(i0 + nl - 1, el, sb + (lbase + (ltot - el)), sb + (lbase + ltot), last_key, k0, k1);
+  }
+  uint32_t prev_key = __shfl_up_sync(PESTI_FULL_MASK, last_key, 1);
+  if (lane == 0) prev_key = KEY_NONE;
+  // pass B: lane summary; `lead` continues the run open before the lane,
+  // `trail` is the run open after it (hh: the lane starts at least one run)
+  bool hh = false;
+  Seg lead{0u, 0u, 0u, KEY_NONE}, trail{0u, 0u, 0u, KEY_NONE};
+  int n_int = 0;  // entries closed inside the lane after its first run start
+  {
+    uint32_t cur = prev_key;
+    float runf = lbase;
+#pragma unroll 1
+    for (int jj = 0; jj < nl; ++jj) {
+      const float ea = eas[jj * 32 + lane];
+      const float av = sb + runf;
+      runf += ea;
+      uint32_t k, k0, k1;
+      classify(i0 + jj, ea, av, sb + runf, k, k0, k1);
+      cks[jj * 32 + lane] = k;
+      c0s[jj * 32 + lane] = k0;
+      c1s[jj * 32 + lane] = k1;
+      const bool head = k == fold::SPECIAL || cur == fold::SPECIAL || cur == KEY_NONE || k != cur;
+      if (head) {
+        if (hh && trail.cnt > 0u) ++n_int;
+        hh = true;
+        if (k == fold::SPECIAL) {
+          ++n_int;
+          trail = Seg{0u, 0u, 0u, KEY_NONE};
+        } else {
+          trail = Seg{k0, k1, 1u, k};
+        }
+      } else if (!hh) {
+        const Tr tt = tr_compose(Tr{lead.a0, lead.a1}, Tr{k0, k1});
+        lead = Seg{tt.a0, tt.a1, lead.cnt + 1u, KEY_NONE};
+      } else {
+        const Tr tt = tr_compose(Tr{trail.a0, trail.a1}, Tr{k0, k1});
+        trail = Seg{tt.a0, tt.a1, trail.cnt + 1u, trail.key};
+      }
+      cur = k;
+    }
+  }
+  // segmented inclusive scan over the lanes
+  Seg inc = hh ? trail : lead;
+  bool fl = hh;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const Seg o = seg_shfl_up(inc, off);
+    const bool of = __shfl_up_sync(PESTI_FULL_MASK, fl, off);
+    if (lane >= off) {
+      inc = seg_join(o, inc, fl);
+      fl = fl || of;
+    }
+  }
+  // the run open before the lane
+  const Seg none{0u, 0u, 0u, KEY_NONE};
+  Seg xin = seg_shfl_up(inc, 1);
+  const bool xfl = __shfl_up_sync(PESTI_FULL_MASK, fl, 1);
+  xin = lane == 0 ? none : seg_join(none, xin, xfl);
+  const Seg last = seg_shfl(inc, 31);
+  // entries, in row order: the run closed by the lane's first start, then
+  // the ones closed inside the lane; the run still open at the group's end
+  // closes it
+  const Seg first = seg_join(xin, lead, false);
+  const int ne = n_int + ((hh && first.cnt > 0u) ? 1 : 0);
+  const int neincl = warp_incl_scan_add(ne);
+  const int nclosed = __shfl_sync(PESTI_FULL_MASK, neincl, 31);
+  const int netot = nclosed + (last.cnt > 0u ? 1 : 0);
+  int off0 = 0;
+  if (lane == 0) off0 = atomicAdd(a.pool_ctr + b, netot);
+  off0 = __shfl_sync(PESTI_FULL_MASK, off0, 0);
+  const bool replay = off0 + netot > POOL_CAP;
+  if (!replay) {
+    FoldEnt* ent = a.pool + b * POOL_CAP + off0;
+    int slot = neincl - ne;
+    if (hh) {  // pass C: the same walk, writing the entries
+      uint32_t cur = prev_key;
+      bool started = false;
+      Seg tr{0u, 0u, 0u, KEY_NONE};
+      auto rend = [&](int i) { return gidx[i] + 1u; };  // past survivor i
+#pragma unroll 1
+      for (int jj = 0; jj < nl; ++jj) {
+        const uint32_t k = cks[jj * 32 + lane], k0 = c0s[jj * 32 + lane], k1 = c1s[jj * 32 + lane];
+        const bool head = k == fold::SPECIAL || cur == fold::SPECIAL || cur == KEY_NONE || k != cur;
+        if (head) {
+          if (!started) {
+            if (first.cnt > 0u) ent[slot++] = FoldEnt{first.key, first.a0, first.a1, rend(i0 + jj - 1)};
+            started = true;
+          } else if (tr.cnt > 0u) {
+            ent[slot++] = FoldEnt{tr.key, tr.a0, tr.a1, rend(i0 + jj - 1)};
+          }
+          if (k == fold::SPECIAL) {
+            ent[slot++] = FoldEnt{fold::SPECIAL, k0, 0u, rend(i0 + jj)};
+            tr = Seg{0u, 0u, 0u, KEY_NONE};
+          } else {
+            tr = Seg{k0, k1, 1u, k};
+          }
+        } else if (started) {
+          const Tr tt = tr_compose(Tr{tr.a0, tr.a1}, Tr{k0, k1});
+          tr = Seg{tt.a0, tt.a1, tr.cnt + 1u, tr.key};
+        }
+        cur = k;
+      }
+    }
+    if (lane == 0 && last.cnt > 0u) ent[nclosed] = FoldEnt{last.key, last.a0, last.a1, gidx[n - 1] + 1u};
+  }
+  if (lane == 0)
+    a.gsurv[(b * nsub + sub) * a.jmax + j] = GroupEnt{{0u, 0u, 0u, 0u}, off0, replay ? 0 : netot, replay ? 1 : 0, 0};
+  return gtot;
+}
+
+// The task-queue classification (rows of the fast path when the fused pass
+// is not used): each task is GROUP consecutive survivors of one sub-slice
+// stored by the survivor pass.  Its approximate starting state is the
+// sub-slice's prefix mass A plus the masses of the sub-slice's earlier
+// survivors, so the tasks are independent and a persistent grid of warps
+// takes them: each warp's first task is its own index (a burst of thousands
+// of atomics on one counter would serialise the start), later ones come from
+// the counter, claimed while the current task runs.  The list is taken from
+// its end: the survivor pass queues the tasks of its slowest warps (the
+// dense start of each row, whose tasks cost the most) last.
+__global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
+  __shared__ ClassShared sh;
+  grid_dep_launch_next();
+  grid_dep_wait();
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int nsub = a.P * K1_WARPS;
+  const long long V = a.V;
+  const int ntasks = *a.task_count;
+  float* graw = sh.raw[w];
+  uint32_t* gidx = sh.idx[w];
   const int nwarps = (int)gridDim.x * K1_WARPS;
   int t = (int)blockIdx.x * K1_WARPS + w;
   ClassTask tk_next = t < ntasks ? a.tasks[ntasks - 1 - t] : ClassTask{0, 0};
@@ -1196,7 +1473,6 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
       const float c2 = 1.4426950408889634f / (scale ? T : 1.0f);
       const float mc = m * 1.4426950408889634f;
       float acc = 0.0f;
-#pragma unroll 4
 #pragma unroll 8
       for (int i = lane; i < j * GROUP; i += 32) acc += ex2_approx(fmaf(sraw[i], c2, -mc));
       s_approx += (double)warp_reduce_add(acc);
@@ -1221,88 +1497,283 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
         }
       }
     }
-    // element i of the group: its run key (binade or SPECIAL) and increments
-    auto classify = [&](int i, float ea, float av, float bv, uint32_t& key, uint32_t& k0, uint32_t& k1) {
-      uint32_t lo = 0u;
-      bool special;
-      const float eu = ea * (1.0f + DE);  // upper bound of the exact value
-      if (av < 0x1p-126f) {
-        special = eu >= 0x1p-127f || bv > 0x1p-126f * (1.0f - BAND);
-      } else {
-        lo = fbits(av) & 0x7f800000u;
-        const float lov = bitsf(lo);
-        special = eu >= bitsf(lo - 0x00800000u) || av < lov * (1.0f + BAND) || bv > 2.0f * lov * (1.0f - BAND);
-      }
-      bool need_exact = special;
-      k0 = k1 = 0u;
-      if (!special) {
-        const uint32_t E = lo >> 23;  // w = 2^(E-150) (E = 0: the subnormal grid 2^-149)
-        const int sh2 = 150 - (int)(E == 0u ? 1u : E);
-        if (ea == 0.0f) {
-          need_exact = E < 40u;  // exact e < 4.5e-38: rounds to 0 on any grid >= 2^-110
-        } else {
-          const float tt = __uint_as_float(fbits(ea) + ((uint32_t)sh2 << 23));  // ea/w, exact scaling
-          const float kr = rintf(tt);
-          const float slack = 0.5f - fabsf(tt - kr);
-          if (slack <= tt * DE + 0x1p-24f) need_exact = true;
-          else k0 = k1 = (uint32_t)kr;
-        }
-      }
-      if (need_exact) {
-        const float raw = graw[i];
-        const float ex = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127, exact
-        if (special) {
-          k0 = fbits(ex);
-        } else {
-          k0 = fbits(fadd(bitsf(lo), ex)) - lo;
-          k1 = fbits(fadd(bitsf(lo + 1u), ex)) - (lo + 1u);
-        }
-      }
-      key = special ? fold::SPECIAL : lo;
-    };
+    (void)classify_group(a, b, sub, j, n, s_approx, scale, T, m, graw, gidx, sh.ea[w], sh.ck[w], sh.c0[w], sh.c1[w]);
+  }
+}
 
-    const int g = (n + 31) >> 5;  // elements per lane: the group's fill decides the loop length
-    const int i0 = lane * g;
-    const int nl = n - i0 < 0 ? 0 : (n - i0 > g ? g : n - i0);  // valid elements of the lane
-    __syncwarp();
-    // pass A: approximate exps (sampling.rs:46,127 within 2^-22)
-    float ltot = 0.0f;
-#pragma unroll 1
-    for (int jj = 0; jj < nl; ++jj) {
-      const float raw = graw[i0 + jj];
-      const float e = pesti_expf_approx(fsub(scale ? fdiv(raw, T) : raw, m));
-      eas[jj * 32 + lane] = e;
-      ltot += e;
+// The fused pass over the rows of the fast path: a persistent grid of warps
+// takes items (each warp its own index first, then from a counter, claimed
+// one item ahead): first every row's HEAD first units one at a time
+// (where the running sum is small, most elements survive and the general
+// classification is the rule, so they are spread over many warps), then
+// items of RUN consecutive UNIT-element units of one row.  Per item: the approximate fold state at its first
+// unit (the sub-slice's prefix mass plus the per-segment masses of the pass
+// over HBM) and the prefix max; per unit: the drop test of the survivor pass
+// (bound (a) with the prefix max up to each segment, bound (b)), the top-k
+// candidates (raw >= tau, exact exps), the survivors compacted in row order
+// into shared memory and classified as one group, whose approximate mass
+// advances the state.  The next unit's elements are fetched (cp.async) while
+// a unit is classified.
+constexpr int RUN = 4;    // units per item past the head: a sub-slice (a multiple of 1024 elements) holds whole items
+constexpr int HEAD = 16;  // units of each row taken one per item (a multiple of RUN)
+
+struct FusedShared {
+  ClassShared c;
+  float4 stage[K1_WARPS][2][2][32];  // per warp: two units' elements, at most 2 16-byte loads per lane
+};
+
+template <typename TIn, int VE, bool VEC>
+__global__ void __launch_bounds__(K1_NT, 3) fused_classify_kernel(SliceArgs a) {
+  extern __shared__ __align__(16) unsigned char fused_smem[];
+  FusedShared& fsh = *reinterpret_cast<FusedShared*>(fused_smem);
+  ClassShared& sh = fsh.c;
+  constexpr int LOADS = UNIT / (32 * VE);  // 16-byte loads per lane per unit
+  constexpr int SEGW = 32 * VE;            // elements of one segment
+  static_assert(LOADS <= 2, "stage holds two loads per lane");
+  grid_dep_launch_next();
+  grid_dep_wait();
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int nsub = a.P * K1_WARPS;
+  const long long V = a.V;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  float* graw = sh.raw[w];
+  uint32_t* gidx = sh.idx[w];
+  float4 (*stage)[2][32] = fsh.stage[w];
+  const int B = (int)a.B;
+  const int nchunk = (int)((V + UNIT - 1) / UNIT);
+  const int head = nchunk < HEAD ? nchunk : HEAD;
+  const int nhead = B * head;
+  const int nitem = nhead + B * ((nchunk - head + RUN - 1) / RUN);
+  const int nw = (int)gridDim.x * K1_WARPS;
+  const int ups = (int)(a.SL / UNIT);  // units per sub-slice
+  const int jmax_row = a.jmax;
+  // item it: row b, units [c0, cend)
+  auto coords = [&](int itm, int& bb, int& cc0, int& ccend) {
+    if (itm < nhead) {
+      bb = itm % B;
+      cc0 = itm / B;
+      ccend = cc0 + 1;
+    } else {
+      const int t = itm - nhead;
+      bb = t % B;
+      cc0 = head + (t / B) * RUN;
+      ccend = cc0 + RUN < nchunk ? cc0 + RUN : nchunk;
     }
-    const float lincl = warp_incl_scan_add(ltot);
-    // approximate states as floats relative to the carried double (the guard
-    // band is 2^-12; float rounding is 2^-24)
-    const float sb = (float)s_approx;
-    const float lbase = lincl - ltot;
-
-    // A clean group: the whole range of its approximate states lies inside one
-    // binade (within the guard band), so every element is a plain increment
-    // k = rint(e/w) of one run (e < lo there, so k is in the binade's units).
-    // k comes from the approximation where it decides it and from the exact
-    // exp otherwise; unless some element is a tie (its k depends on the
-    // parity of the state), the group's fold is that run with the sum of the
-    // increments: one entry, no segmentation.
-    {
-      const float gtot = __shfl_sync(PESTI_FULL_MASK, lincl, 31);
-      bool clean = false;
-      uint32_t clo = 0u;
-      if (sb >= 0x1p-126f) {
-        clo = fbits(sb) & 0x7f800000u;
-        const float lov = bitsf(clo);
-        clean = sb >= lov * (1.0f + BAND) && sb + gtot <= 2.0f * lov * (1.0f - BAND);
+  };
+  auto fetch = [&](int bb, int cc, int buf) {  // unit cc of row bb into stage[buf]
+    if (VEC && (long long)(cc + 1) * UNIT <= V) {
+      const TIn* row = (const TIn*)a.logits + (long long)bb * a.ld + (long long)cc * UNIT;
+#pragma unroll
+      for (int q = 0; q < LOADS; ++q) cp_async16(&stage[buf][q][lane], row + q * SEGW + lane * VE);
+    }
+  };
+  int it = (int)blockIdx.x * K1_WARPS + w;
+  int b = 0, c0 = 0, cend = 0;
+  if (it < nitem) coords(it, b, c0, cend);
+  int buf = 0;
+  if (it < nitem) fetch(b, c0, 0);
+  cp_async_commit();
+  int claim = 0;
+  if (lane == 0 && it < nitem) claim = atomicAdd(a.item_next, 1);
+  // an item's records: its row's parameters and prologue, its sub-slice's
+  // prefix, the state of the pass over HBM at its first unit; loaded one item
+  // ahead (their latency hides behind the current item)
+  struct ItemRec {
+    pesti_sampling_params prm;
+    RowInfo ri;
+    SubPre pr;
+    UnitPre up;
+  };
+  auto load_rec = [&](int bb, int cc0) {
+    ItemRec q;
+    q.prm = row_params(a.uni, a.per_row, bb);
+    q.ri = a.info[bb];
+    q.pr = a.pre[(long long)bb * nsub + cc0 / ups];
+    q.up = a.unit_pre[(long long)bb * nchunk + cc0];
+    return q;
+  };
+  ItemRec cur;
+  if (it < nitem) cur = load_rec(b, c0);
+  while (it < nitem) {
+    const int nit = nw + __shfl_sync(PESTI_FULL_MASK, claim, 0);  // the next item
+    int nb = 0, nc0 = 0, ncend = 0;
+    ItemRec nxt;
+    if (nit < nitem) {
+      coords(nit, nb, nc0, ncend);
+      if (lane == 0) claim = atomicAdd(a.item_next, 1);
+      nxt = load_rec(nb, nc0);
+    }
+    const pesti_sampling_params prm = cur.prm;
+    const RowInfo& ri = cur.ri;
+    const bool take = !is_greedy(prm) && !ri.uniform && a.fast_enabled && fast_topk(prm, a.V_total);
+    const float T = prm.temperature;
+    const bool scale = T > 0.0f;
+    const float t_eff = scale ? T : 1.0f;
+    const float m = ri.m;
+    const int sub = c0 / ups;
+    const long long sub0 = (long long)sub * a.SL;
+    const SubPre pr = cur.pr;
+    double s_est = 0.0;
+    float run_max = NEG_INF;
+    if (take) {
+      // the approximate state and the max before the item: the earlier
+      // sub-slices' (prologue) plus this sub-slice's up to the item (pass over HBM)
+      const float ym = ri.max_raw * (1.4426950408889634f / t_eff);
+      s_est = pr.A + (cur.up.mlog > NEG_INF ? (double)(cur.up.mass * ex2_approx(cur.up.mlog - ym)) : 0.0);
+      run_max = fmaxf(pr.P, cur.up.pmax);
+    }
+    const float c1 = ABSORB * t_eff * (1.0f + 0x1p-20f);
+    const float pf = (m - PRUNE_FLOOR) * t_eff;
+    const float p_floor = pf + 0x1p-20f * fabsf(pf);
+    auto bound_a = [&](float P) { return P >= p_floor ? fsub(P, fadd(c1, 0x1p-21f * fabsf(P))) : NEG_INF; };
+    for (int c = c0; c < cend; ++c, buf ^= 1) {
+      // the next unit's elements, while this one is classified
+      if (c + 1 < cend) fetch(b, c + 1, buf ^ 1);
+      else if (nit < nitem) fetch(nb, nc0, buf ^ 1);
+      cp_async_commit();
+      cp_async_wait<1>();
+      __syncwarp();
+      if (!take) continue;
+      const long long start = (long long)c * UNIT;
+      const int j = c - sub * ups;
+      const int len = (int)(V - start < UNIT ? V - start : UNIT);
+      // the unit's elements
+      float x[LOADS][VE];
+      int nv[LOADS];
+      if (VEC && len == UNIT) {
+#pragma unroll
+        for (int q = 0; q < LOADS; ++q) {
+          const float4 r4 = stage[buf][q][lane];
+          if (sizeof(TIn) == 4) {
+            x[q][0] = r4.x; x[q][1] = r4.y; x[q][2] = r4.z; x[q][3] = r4.w;
+          } else {
+            const uint32_t wds[4] = {__float_as_uint(r4.x), __float_as_uint(r4.y), __float_as_uint(r4.z),
+                                     __float_as_uint(r4.w)};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              x[q][2 * h] = __uint_as_float(wds[h] << 16);
+              x[q][2 * h + 1] = __uint_as_float(wds[h] & 0xffff0000u);
+            }
+          }
+          nv[q] = VE;
+        }
+      } else {
+        const TIn* row = (const TIn*)a.logits + (long long)b * a.ld + start;
+#pragma unroll
+        for (int q = 0; q < LOADS; ++q) {
+          const int p0 = q * SEGW + lane * VE;
+          nv[q] = 0;
+#pragma unroll
+          for (int e = 0; e < VE; ++e) {
+            x[q][e] = p0 + e < len ? load_logit<TIn>(row, p0 + e) : 0.0f;
+            nv[q] = p0 + e < len ? e + 1 : nv[q];
+          }
+        }
       }
-      if (clean) {
+      // drop test per segment (bound (a) with the max of the row before the
+      // segment, bound (b)); NaN fails it.  svm: the lane's survivors, bit q*VE + e
+      uint32_t svm = 0u;
+#pragma unroll
+      for (int q = 0; q < LOADS; ++q) {
+        const float thr = fmaxf(bound_a(run_max), pr.thrL);
+        float lm = NEG_INF;  // the segment's max (fmaxf skips NaN, as the pass over HBM)
+#pragma unroll
+        for (int e = 0; e < VE; ++e) {
+          if (e < nv[q]) lm = fmaxf(lm, x[q][e]);
+          if (e < nv[q] && x[q][e] >= thr) svm |= 1u << (q * VE + e);
+        }
+        run_max = fmaxf(run_max, fkey_inv(__reduce_max_sync(PESTI_FULL_MASK, fkey(lm))));
+      }
+      // top-k candidates (sampling.rs:46,127 exactly)
+      {
+        const float tau = ri.tau;
+#pragma unroll
+        for (int q = 0; q < LOADS; ++q) {
+          int cc = 0;
+#pragma unroll
+          for (int e = 0; e < VE; ++e) cc += (e < nv[q] && x[q][e] >= tau) ? 1 : 0;
+          if (__any_sync(PESTI_FULL_MASK, cc > 0)) {
+            const int ci = warp_incl_scan_add(cc);
+            const int ctot = __shfl_sync(PESTI_FULL_MASK, ci, 31);
+            int basec = 0;
+            if (lane == 0) basec = atomicAdd(a.cand_count + b, ctot);
+            basec = __shfl_sync(PESTI_FULL_MASK, basec, 0);
+            int slot = basec + ci - cc;
+            const uint32_t p0 = (uint32_t)(start + q * SEGW + lane * VE);
+#pragma unroll
+            for (int e = 0; e < VE; ++e) {
+              if (e < nv[q] && x[q][e] >= tau) {
+                if (slot < CAND_CAP) {
+                  a.cand_e[(long long)b * CAND_CAP + slot] = pesti_expf_call(fsub(scale ? fdiv(x[q][e], T) : x[q][e], m));
+                  a.cand_idx[(long long)b * CAND_CAP + slot] = p0 + (uint32_t)e;
+                }
+                ++slot;
+              }
+            }
+          }
+        }
+      }
+      if (j == 0) {
+        // the sub-slice's record; the last sub-slice holding columns also writes
+        // those of the sub-slices past the row's end (no units, no entries)
+        long long slen = V - sub0;
+        slen = slen > a.SL ? a.SL : slen;
+        if (lane == 0) a.surv[(long long)b * nsub + sub] = SubSurv{0, (int32_t)((slen + UNIT - 1) / UNIT), 0, NEG_INF};
+        if (sub0 + a.SL >= V)
+          for (int q = sub + 1 + lane; q < nsub; q += 32) a.surv[(long long)b * nsub + q] = SubSurv{0, 0, 0, NEG_INF};
+      }
+      // the survivors in row order (segment by segment, lane by lane)
+      int n = 0;
+#pragma unroll
+      for (int q = 0; q < LOADS; ++q) {
+        const uint32_t mq = (svm >> (q * VE)) & ((1u << VE) - 1u);
+        const int cq = __popc(mq);
+        const int iq = warp_incl_scan_add(cq);
+        int oq = n + iq - cq;
+        const uint32_t p0 = (uint32_t)(start + q * SEGW + lane * VE);
+#pragma unroll
+        for (int e = 0; e < VE; ++e) {
+          if ((mq >> e) & 1u) {
+            graw[oq] = x[q][e];
+            gidx[oq] = p0 + (uint32_t)e;
+            ++oq;
+          }
+        }
+        n += __shfl_sync(PESTI_FULL_MASK, iq, 31);
+      }
+      GroupEnt* ge = a.gsurv + ((long long)b * nsub + sub) * jmax_row + j;
+      if (n == 0) {
+        if (lane == 0) *ge = GroupEnt{{0u, 0u, 0u, 0u}, 0, 0, 0, 0};
+        continue;
+      }
+      __syncwarp();
+      // A clean unit (one pass per survivor): the range of its approximate
+      // states lies inside the binade of its start (within the guard band),
+      // so every survivor is a plain increment k = rint(e/w) of one run; k
+      // comes from the approximation (sampling.rs:46,127 within 2^-22) where
+      // it decides it and from the exact exp otherwise, and no survivor may be
+      // a tie.  Anything else goes to the general classification.
+      {
+        constexpr float DE = 2.0f * PESTI_EXPF_APPROX_RELERR;
+        const float BAND = a.band;
+        const float sb = (float)s_est;
+        const uint32_t clo = fbits(sb) & 0x7f800000u;
+        const float lov = bitsf(clo);
+        const bool possible = sb >= 0x1p-126f && sb >= lov * (1.0f + BAND);
         const int sh2 = 150 - (int)(clo >> 23);  // w = 2^(E-150)
+        const int g = (n + 31) >> 5;
+        const int i0 = lane * g;
+        const int nl = n - i0 < 0 ? 0 : (n - i0 > g ? g : n - i0);
+        float ltot = 0.0f;
         uint32_t ksum = 0u;
         bool decided = true;
-#pragma unroll 1
+#pragma unroll 2
         for (int jj = 0; jj < nl; ++jj) {
-          const float ea = eas[jj * 32 + lane];
+          const float raw = graw[i0 + jj];
+          const float xs = scale ? fdiv(raw, T) : raw;  // sampling.rs:46
+          const float ea = pesti_expf_approx(fsub(xs, m));
+          ltot += ea;
+          if (!possible) continue;
           bool exact = false;
           if (ea == 0.0f) {
             exact = (clo >> 23) < 40u;  // else: exact e < 4.5e-38 rounds to 0 on this grid
@@ -1314,137 +1785,33 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
             else exact = true;
           }
           if (exact) {
-            const float raw = graw[i0 + jj];
-            const float ex = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127, exact
-            const uint32_t k0 = fbits(fadd(bitsf(clo), ex)) - clo;
+            const float ex = pesti_expf_call(fsub(xs, m));  // sampling.rs:127, exact
+            const uint32_t k0 = fbits(fadd(lov, ex)) - clo;
             const uint32_t k1 = fbits(fadd(bitsf(clo + 1u), ex)) - (clo + 1u);
             decided = decided && k0 == k1;
             ksum += k0;
           }
         }
-        if (__all_sync(PESTI_FULL_MASK, decided)) {
-          const uint32_t inc = tr_sat(warp_reduce_add(ksum));  // each < 2^22, at most 256 of them
-          if (lane == 0)
-            a.gsurv[(b * nsub + sub) * a.jmax + j] = GroupEnt{{clo, inc, inc, gidx[n - 1] + 1u}, 0, 1, 0, 1};
+        const float usum = warp_reduce_add(ltot);
+        const bool clean = possible && sb + usum <= 2.0f * lov * (1.0f - BAND);
+        if (clean && __all_sync(PESTI_FULL_MASK, decided)) {
+          const uint32_t inc = tr_sat(__reduce_add_sync(PESTI_FULL_MASK, ksum));  // each < 2^22, at most 256
+          if (lane == 0) *ge = GroupEnt{{clo, inc, inc, gidx[n - 1] + 1u}, 0, 1, 0, 1};
+          s_est += (double)usum;
           continue;
         }
       }
+      s_est += (double)classify_group(a, b, sub, j, n, s_est, scale, T, m, graw, gidx, sh.ea[w], sh.ck[w], sh.c0[w],
+                                      sh.c1[w]);
+      __syncwarp();
     }
-    // the key of the lane's last element decides whether the next lane's first
-    // element continues its run
-    uint32_t last_key = KEY_NONE;
-    if (nl > 0) {
-      const float el = eas[(nl - 1) * 32 + lane];
-      uint32_t k0, k1;
-      classify(i0 + nl - 1, el, sb + (lbase + (ltot - el)), sb + (lbase + ltot), last_key, k0, k1);
-    }
-    uint32_t prev_key = __shfl_up_sync(PESTI_FULL_MASK, last_key, 1);
-    if (lane == 0) prev_key = KEY_NONE;
-    // pass B: lane summary; `lead` continues the run open before the lane,
-    // `trail` is the run open after it (hh: the lane starts at least one run)
-    bool hh = false;
-    Seg lead{0u, 0u, 0u, KEY_NONE}, trail{0u, 0u, 0u, KEY_NONE};
-    int n_int = 0;  // entries closed inside the lane after its first run start
-    {
-      uint32_t cur = prev_key;
-      float runf = lbase;
-#pragma unroll 1
-      for (int jj = 0; jj < nl; ++jj) {
-        const float ea = eas[jj * 32 + lane];
-        const float av = sb + runf;
-        runf += ea;
-        uint32_t k, k0, k1;
-        classify(i0 + jj, ea, av, sb + runf, k, k0, k1);
-        cks[jj * 32 + lane] = k;
-        c0s[jj * 32 + lane] = k0;
-        c1s[jj * 32 + lane] = k1;
-        const bool head = k == fold::SPECIAL || cur == fold::SPECIAL || cur == KEY_NONE || k != cur;
-        if (head) {
-          if (hh && trail.cnt > 0u) ++n_int;
-          hh = true;
-          if (k == fold::SPECIAL) {
-            ++n_int;
-            trail = Seg{0u, 0u, 0u, KEY_NONE};
-          } else {
-            trail = Seg{k0, k1, 1u, k};
-          }
-        } else if (!hh) {
-          const Tr tt = tr_compose(Tr{lead.a0, lead.a1}, Tr{k0, k1});
-          lead = Seg{tt.a0, tt.a1, lead.cnt + 1u, KEY_NONE};
-        } else {
-          const Tr tt = tr_compose(Tr{trail.a0, trail.a1}, Tr{k0, k1});
-          trail = Seg{tt.a0, tt.a1, trail.cnt + 1u, trail.key};
-        }
-        cur = k;
-      }
-    }
-    // segmented inclusive scan over the lanes
-    Seg inc = hh ? trail : lead;
-    bool fl = hh;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const Seg o = seg_shfl_up(inc, off);
-      const bool of = __shfl_up_sync(PESTI_FULL_MASK, fl, off);
-      if (lane >= off) {
-        inc = seg_join(o, inc, fl);
-        fl = fl || of;
-      }
-    }
-    // the run open before the lane
-    const Seg none{0u, 0u, 0u, KEY_NONE};
-    Seg xin = seg_shfl_up(inc, 1);
-    const bool xfl = __shfl_up_sync(PESTI_FULL_MASK, fl, 1);
-    xin = lane == 0 ? none : seg_join(none, xin, xfl);
-    const Seg last = seg_shfl(inc, 31);
-    // entries, in row order: the run closed by the lane's first start, then
-    // the ones closed inside the lane; the run still open at the group's end
-    // closes it
-    const Seg first = seg_join(xin, lead, false);
-    const int ne = n_int + ((hh && first.cnt > 0u) ? 1 : 0);
-    const int neincl = warp_incl_scan_add(ne);
-    const int nclosed = __shfl_sync(PESTI_FULL_MASK, neincl, 31);
-    const int netot = nclosed + (last.cnt > 0u ? 1 : 0);
-    int off0 = 0;
-    if (lane == 0) off0 = atomicAdd(a.pool_ctr + b, netot);
-    off0 = __shfl_sync(PESTI_FULL_MASK, off0, 0);
-    const bool replay = off0 + netot > POOL_CAP;
-    if (!replay) {
-      FoldEnt* ent = a.pool + b * POOL_CAP + off0;
-      int slot = neincl - ne;
-      if (hh) {  // pass C: the same walk, writing the entries
-        uint32_t cur = prev_key;
-        bool started = false;
-        Seg tr{0u, 0u, 0u, KEY_NONE};
-        auto rend = [&](int i) { return gidx[i] + 1u; };  // past survivor i
-#pragma unroll 1
-        for (int jj = 0; jj < nl; ++jj) {
-          const uint32_t k = cks[jj * 32 + lane], k0 = c0s[jj * 32 + lane], k1 = c1s[jj * 32 + lane];
-          const bool head = k == fold::SPECIAL || cur == fold::SPECIAL || cur == KEY_NONE || k != cur;
-          if (head) {
-            if (!started) {
-              if (first.cnt > 0u) ent[slot++] = FoldEnt{first.key, first.a0, first.a1, rend(i0 + jj - 1)};
-              started = true;
-            } else if (tr.cnt > 0u) {
-              ent[slot++] = FoldEnt{tr.key, tr.a0, tr.a1, rend(i0 + jj - 1)};
-            }
-            if (k == fold::SPECIAL) {
-              ent[slot++] = FoldEnt{fold::SPECIAL, k0, 0u, rend(i0 + jj)};
-              tr = Seg{0u, 0u, 0u, KEY_NONE};
-            } else {
-              tr = Seg{k0, k1, 1u, k};
-            }
-          } else if (started) {
-            const Tr tt = tr_compose(Tr{tr.a0, tr.a1}, Tr{k0, k1});
-            tr = Seg{tt.a0, tt.a1, tr.cnt + 1u, tr.key};
-          }
-          cur = k;
-        }
-      }
-      if (lane == 0 && last.cnt > 0u) ent[nclosed] = FoldEnt{last.key, last.a0, last.a1, gidx[n - 1] + 1u};
-    }
-    if (lane == 0)
-      a.gsurv[(b * nsub + sub) * a.jmax + j] = GroupEnt{{0u, 0u, 0u, 0u}, off0, replay ? 0 : netot, replay ? 1 : 0, 0};
+    it = nit;
+    b = nb;
+    c0 = nc0;
+    cend = ncend;
+    cur = nxt;
   }
+  cp_async_wait<0>();
 }
 
 // ---------------------------------------------------------------------------
@@ -1940,6 +2307,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
       int* rep = eoff;  // per sub-slice: a group overflowed
       for (int q = tid; q < nsub; q += K2_NT) {
         ss[q] = survs[q];
+        if ((long long)q * a.SL >= V) ss[q].ngroups = 0;  // past the row's end: no units
         rep[q] = 0;
       }
       __syncthreads();

@@ -127,6 +127,17 @@ int zero_counters(pesti_sampler* s, long long B, cudaStream_t st) {
 
 size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
 
+// Some row is neither greedy nor on the fast top-k path, so it needs the
+// survivor pass (for the row kernel's generic path).
+bool needs_survivor_pass(const pesti_sampling_params* p, long long n, long long V) {
+  for (long long i = 0; i < n; ++i) {
+    const bool greedy = (p[i].flags & PESTI_FLAG_GREEDY_IF_ZERO_T) && p[i].temperature == 0.0f;
+    const long long k = std::min<long long>(p[i].top_k, V);
+    if (!greedy && !(k >= 1 && k <= pesti::FAST_K)) return true;
+  }
+  return false;
+}
+
 bool needs_sorted_buffers(const pesti_sampling_params* p, long long n) {
   for (long long i = 0; i < n; ++i) {
     const bool greedy = (p[i].flags & PESTI_FLAG_GREEDY_IF_ZERO_T) && p[i].temperature == 0.0f;
@@ -153,6 +164,15 @@ int ensure_row_smem_limit(int device) {
   PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::shard_table_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)pesti::TAB_SMEM),
                  "cudaFuncSetAttribute(shard_table_kernel)");
+  const int fused = (int)sizeof(pesti::FusedShared);
+  PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::fused_classify_kernel<float, 4, true>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, fused), "cudaFuncSetAttribute(fused)");
+  PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::fused_classify_kernel<float, 4, false>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, fused), "cudaFuncSetAttribute(fused)");
+  PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::fused_classify_kernel<uint16_t, 8, true>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, fused), "cudaFuncSetAttribute(fused)");
+  PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::fused_classify_kernel<uint16_t, 8, false>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, fused), "cudaFuncSetAttribute(fused)");
   if (cached) g_row_limit_set[device].store(true, std::memory_order_release);
   return PESTI_OK;
 }
@@ -183,8 +203,9 @@ struct Plan {
   int num_sms;
   long long nsub, nseg, jmax;
   bool sorted_bufs;
-  size_t o_ctr, o_stats, o_pre, o_info, o_surv, o_segmax, o_se, o_si, o_cc, o_ce, o_ci;
-  size_t o_gsurv, o_tasks, o_tctr, o_pctr, o_pool;
+  bool survivors = true;  // some row may need the survivor pass (not on the fast path)
+  size_t o_ctr, o_stats, o_pre, o_info, o_surv, o_segmax, o_upre, o_se, o_si, o_cc, o_ce, o_ci;
+  size_t o_gsurv, o_inext, o_tasks, o_tctr, o_pctr, o_pool;
   size_t o_E, o_I, o_status;
   size_t o_sk0 = 0, o_sv0 = 0, o_sk1 = 0, o_sv1 = 0, o_q = 0;
   size_t bytes;  // workspace the call needs
@@ -198,7 +219,7 @@ Plan make_plan(int num_sms, pesti_dtype dtype, long long B, long long V, bool so
   p.num_sms = num_sms;
   p.nsub = (long long)p.g.P * pesti::K1_WARPS;
   p.nseg = (std::max(1LL, V) + 32LL * ve - 1) / (32LL * ve);
-  p.jmax = (p.g.SL + pesti::GROUP - 1) / pesti::GROUP;
+  p.jmax = (p.g.SL + pesti::UNIT - 1) / pesti::UNIT;
   const size_t ngrp = (size_t)B * p.nsub * p.jmax;
   p.sorted_bufs = sorted_bufs;
   const size_t bv = (size_t)B * (size_t)std::max(1LL, V);
@@ -214,6 +235,7 @@ Plan make_plan(int num_sms, pesti_dtype dtype, long long B, long long V, bool so
   p.o_info = take((size_t)B * sizeof(pesti::RowInfo));
   p.o_surv = take((size_t)B * p.nsub * sizeof(pesti::SubSurv));
   p.o_segmax = take((size_t)B * p.nseg * 4);
+  p.o_upre = take((size_t)B * ((std::max(1LL, V) + pesti::UNIT - 1) / pesti::UNIT) * sizeof(pesti::UnitPre));
   p.o_se = take(bv * 4);
   p.o_si = take(bv * 4);
   p.o_cc = take((size_t)B * 4);
@@ -223,6 +245,7 @@ Plan make_plan(int num_sms, pesti_dtype dtype, long long B, long long V, bool so
   p.o_I = take(bv * 4);
   p.o_status = take(16);
   p.o_gsurv = take(ngrp * sizeof(pesti::GroupEnt));
+  p.o_inext = take(sizeof(int));
   p.o_tasks = take(ngrp * sizeof(pesti::ClassTask));
   p.o_tctr = take(2 * sizeof(int));
   p.o_pctr = take((size_t)B * sizeof(int));
@@ -259,12 +282,17 @@ pesti::SliceArgs make_slice_args(const Plan& p, char* ws, const void* d_logits, 
   sa.row_ctr = (int*)(ws + p.o_ctr);
   sa.surv = (pesti::SubSurv*)(ws + p.o_surv);
   sa.seg_max = (float*)(ws + p.o_segmax);
+  sa.unit_pre = (pesti::UnitPre*)(ws + p.o_upre);
   sa.surv_raw = (float*)(ws + p.o_se);
   sa.surv_idx = (uint32_t*)(ws + p.o_si);
   sa.jmax = (int)p.jmax;
+  sa.item_next = (int*)(ws + p.o_inext);
   sa.tasks = (pesti::ClassTask*)(ws + p.o_tasks);
   sa.task_count = (int*)(ws + p.o_tctr);
   sa.task_next = sa.task_count + 1;
+  // rows past 128k columns (and vocabulary shards, set by their caller) take
+  // the fused pass; shorter ones the survivor pass and the task queue
+  sa.fused = V > 131072 ? 1 : 0;
   sa.gsurv = (pesti::GroupEnt*)(ws + p.o_gsurv);
   sa.pool = (pesti::FoldEnt*)(ws + p.o_pool);
   sa.pool_ctr = (int*)(ws + p.o_pctr);
@@ -302,28 +330,56 @@ int launch_slice_stats(const Plan& p, const pesti::SliceArgs& sa, cudaStream_t s
   return PESTI_OK;
 }
 
-// The survivor and classification passes.
-int launch_survivors(const Plan& p, const pesti::SliceArgs& sa, cudaStream_t st) {
+// The survivor pass and the classification of the fast path's rows: either
+// the task queue over the survivors, or (sa.fused) the fused pass, with the
+// survivor pass only for the rows off the fast path (skipped when the call
+// has none).
+int launch_survivors(const Plan& p, const pesti::SliceArgs& sa, int device, cudaStream_t st) {
   const bool aligned = rows_aligned(sa.logits, (pesti_dtype)sa.dtype, sa.ld);
-  const dim3 g1((unsigned)(p.g.P * sa.B));
-  // the survivor pass reads from L2: fewer loads in flight, smaller code
   const dim3 b1(pesti::K1_NT);
   cudaError_t e;
-  if (sa.dtype == PESTI_BF16) {
-    if (aligned) e = launch_dependent(pesti::survivor_kernel<uint16_t, 8, true>, g1, b1, 0, st, sa);
-    else e = launch_dependent(pesti::survivor_kernel<uint16_t, 8, false>, g1, b1, 0, st, sa);
-  } else {
-    if (aligned) e = launch_dependent(pesti::survivor_kernel<float, 4, true>, g1, b1, 0, st, sa);
-    else e = launch_dependent(pesti::survivor_kernel<float, 4, false>, g1, b1, 0, st, sa);
+  if (!sa.fused || p.survivors || !sa.fast_enabled) {
+    // the survivor pass reads from L2: fewer loads in flight, smaller code
+    const dim3 g1((unsigned)(p.g.P * sa.B));
+    if (sa.dtype == PESTI_BF16) {
+      if (aligned) e = launch_dependent(pesti::survivor_kernel<uint16_t, 8, true>, g1, b1, 0, st, sa);
+      else e = launch_dependent(pesti::survivor_kernel<uint16_t, 8, false>, g1, b1, 0, st, sa);
+    } else {
+      if (aligned) e = launch_dependent(pesti::survivor_kernel<float, 4, true>, g1, b1, 0, st, sa);
+      else e = launch_dependent(pesti::survivor_kernel<float, 4, false>, g1, b1, 0, st, sa);
+    }
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "survivor_kernel launch");
   }
+  if (!sa.fused) {
+    // classification tasks: a persistent grid takes them from a counter
+    const long long most = (long long)sa.B * p.nsub * p.jmax;
+    const long long blocks = std::min<long long>(4LL * p.num_sms, (most + pesti::K1_WARPS - 1) / pesti::K1_WARPS);
+    e = launch_dependent(pesti::classify_kernel, dim3((unsigned)std::max(1LL, blocks)), b1, 0, st, sa);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "classify_kernel launch");
+    return PESTI_OK;
+  }
+  if (!sa.fast_enabled) return PESTI_OK;
+  int rc = ensure_row_smem_limit(device);
+  if (rc) return rc;
+  // a persistent grid over the rows' UNIT-element units: as many blocks as
+  // fit on the device at once
+  const size_t smem = sizeof(pesti::FusedShared);
+  void (*kern)(pesti::SliceArgs) =
+      sa.dtype == PESTI_BF16 ? (aligned ? pesti::fused_classify_kernel<uint16_t, 8, true>
+                                        : pesti::fused_classify_kernel<uint16_t, 8, false>)
+                             : (aligned ? pesti::fused_classify_kernel<float, 4, true>
+                                        : pesti::fused_classify_kernel<float, 4, false>);
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, pesti::K1_NT, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  const long long units = sa.B * ((sa.V + pesti::UNIT - 1) / pesti::UNIT);
+  const long long blocks =
+      std::min<long long>((long long)std::max(1, per_sm) * p.num_sms, (units + pesti::K1_WARPS - 1) / pesti::K1_WARPS);
+  e = launch_dependent(kern, dim3((unsigned)std::max(1LL, blocks)), b1, smem, st, sa);
   if (e == cudaSuccess) e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "survivor_kernel launch");
-  // classification tasks: a persistent grid takes them from a counter
-  const long long most = (long long)sa.B * p.nsub * p.jmax;
-  const long long blocks = std::min<long long>(4LL * p.num_sms, (most + pesti::K1_WARPS - 1) / pesti::K1_WARPS);
-  e = launch_dependent(pesti::classify_kernel, dim3((unsigned)std::max(1LL, blocks)), b1, 0, st, sa);
-  if (e == cudaSuccess) e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "classify_kernel launch");
+  if (e != cudaSuccess) return cuda_fail(e, "fused_classify_kernel launch");
   return PESTI_OK;
 }
 
@@ -403,7 +459,7 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
   int rc = launch_slice_stats(p, sa, st);
   if (rc) return rc;
   if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[1], st), "cudaEventRecord(profile)");
-  rc = launch_survivors(p, sa, st);
+  rc = launch_survivors(p, sa, device, st);
   if (rc) return rc;
   if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[2], st), "cudaEventRecord(profile)");
   const pesti::RowArgs ra = make_row_args(p, ws, sa, d_u, d_out, d_kept_p, d_kept_idx, kept_width, d_kept_count);
@@ -415,9 +471,10 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
 
 int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long B, long long V,
            long long ld, const pesti_sampling_params& uni, const pesti_sampling_params* d_per_row,
-           bool sorted_bufs, const float* d_u, uint32_t* d_out, float* d_kept_p,
+           bool sorted_bufs, bool survivors, const float* d_u, uint32_t* d_out, float* d_kept_p,
            uint32_t* d_kept_idx, long long kept_width, int64_t* d_kept_count, cudaStream_t st) {
-  const Plan p = make_plan(s->num_sms, dtype, B, V, sorted_bufs);
+  Plan p = make_plan(s->num_sms, dtype, B, V, sorted_bufs);
+  p.survivors = survivors;
   int rc = ensure_ws(s, p.bytes);
   if (rc) return rc;
   rc = zero_counters(s, B, st);
@@ -437,11 +494,12 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
 // Per-row parameters as the kernels read them: one uniform entry, or a
 // device array (the caller's, or the host entries copied to the handle's).
 int stage_params(pesti_sampler* s, const pesti_sampling_params* params, int params_per_row, int params_on_device,
-                 long long B, cudaStream_t st, pesti_sampling_params& uni,
-                 const pesti_sampling_params*& d_per_row, bool& sorted_bufs) {
+                 long long B, long long V, cudaStream_t st, pesti_sampling_params& uni,
+                 const pesti_sampling_params*& d_per_row, bool& sorted_bufs, bool& survivors) {
   uni = pesti_sampling_params{};
   d_per_row = nullptr;
   sorted_bufs = true;
+  survivors = true;
   if (params_on_device) {
     if (params_per_row) d_per_row = params;
     else {
@@ -449,9 +507,11 @@ int stage_params(pesti_sampler* s, const pesti_sampling_params* params, int para
       PESTI_CUDA_TRY(cudaMemcpyAsync(&uni, params, sizeof(uni), cudaMemcpyDeviceToHost, st), "params copy");
       PESTI_CUDA_TRY(cudaStreamSynchronize(st), "params sync");
       sorted_bufs = needs_sorted_buffers(&uni, 1);
+      survivors = needs_survivor_pass(&uni, 1, V);
     }
   } else if (params_per_row) {
     sorted_bufs = needs_sorted_buffers(params, B);
+    survivors = needs_survivor_pass(params, B, V);
     if ((size_t)B > s->h_params_cap) {
       if (s->params_ev_used) cudaEventSynchronize(s->params_ev);
       if (s->h_params) cudaFreeHost(s->h_params);
@@ -473,6 +533,7 @@ int stage_params(pesti_sampler* s, const pesti_sampling_params* params, int para
   } else {
     uni = params[0];
     sorted_bufs = needs_sorted_buffers(&uni, 1);
+    survivors = needs_survivor_pass(&uni, 1, V);
   }
   return PESTI_OK;
 }
@@ -557,6 +618,7 @@ struct ShardPlan {
 ShardPlan make_shard_plan(int num_sms, pesti_dtype dtype, long long B, long long Vs, int G, int nlocal, int ksh) {
   ShardPlan sp;
   sp.local = make_plan(num_sms, dtype, B, Vs, false);
+  sp.local.survivors = false;  // rows off the fast path take the gathered path
   sp.G = G;
   sp.nlocal = nlocal;
   sp.B = B;
@@ -612,6 +674,7 @@ int shard_phase1(const ShardPlan& sp, char* ws, int li, const ShardCall& c, cons
   sa.V_total = sp.VT;
   sa.band = kShardBand;
   sa.shard_out = sum_out;
+  sa.fused = 1;  // the second phase's fused pass reads this pass's per-unit states
   return launch_slice_stats(sp.local, sa, c.st);
 }
 
@@ -627,11 +690,12 @@ int shard_phase2(const ShardPlan& sp, char* ws, int li, int r, int device, const
   sa.shard_all = sums;
   sa.shard_G = sp.G;
   sa.shard_rank = r;
+  sa.fused = 1;
   if (c.dtype == PESTI_BF16) pesti::shard_prologue_kernel<uint16_t, 8><<<(unsigned)c.B, pesti::K1_NT, 0, c.st>>>(sa);
   else pesti::shard_prologue_kernel<float, 4><<<(unsigned)c.B, pesti::K1_NT, 0, c.st>>>(sa);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "shard_prologue_kernel launch");
-  int rc = launch_survivors(sp.local, sa, c.st);
+  int rc = launch_survivors(sp.local, sa, device, c.st);
   if (rc) return rc;
   pesti::RowArgs ra = make_row_args(sp.local, lws, sa, c.d_u, c.d_out, nullptr, nullptr, 0, nullptr);
   ra.shard = 1;
@@ -833,8 +897,9 @@ int sample_sharded(pesti_sampler* s, pesti_comm* comm, int G, const void* d_logi
   c.kept_width = kept_width;
   c.d_kept_count = d_kept_count;
   c.st = st;
-  bool sorted_bufs = false;
-  int rc = stage_params(s, params, params_per_row, params_on_device, B, st, c.uni, c.d_per_row, sorted_bufs);
+  bool sorted_bufs = false, survivors = false;
+  int rc = stage_params(s, params, params_per_row, params_on_device, B, Vs * G, st, c.uni, c.d_per_row, sorted_bufs,
+                        survivors);
   if (rc) return rc;
   const int esize = dtype == PESTI_BF16 ? 2 : 4;
   const int nlocal = comm ? 1 : G;
@@ -978,10 +1043,10 @@ int pesti_sample_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype
   cudaStream_t st = (cudaStream_t)stream;  // NULL: the legacy default stream
   pesti_sampling_params uni{};
   const pesti_sampling_params* d_per_row = nullptr;
-  bool sorted_bufs = true;
-  rc = stage_params(s, params, params_per_row, params_on_device, B, st, uni, d_per_row, sorted_bufs);
+  bool sorted_bufs = true, survivors = true;
+  rc = stage_params(s, params, params_per_row, params_on_device, B, V, st, uni, d_per_row, sorted_bufs, survivors);
   if (rc) return rc;
-  return launch(s, d_logits, dtype, B, V, ld, uni, d_per_row, sorted_bufs, d_u, d_out_tokens,
+  return launch(s, d_logits, dtype, B, V, ld, uni, d_per_row, sorted_bufs, survivors, d_u, d_out_tokens,
                 d_kept_p, d_kept_idx, kept_width, d_kept_count, st);
 }
 
@@ -996,7 +1061,7 @@ int pesti_argmax_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype
   pesti_sampling_params uni{};
   uni.temperature = 0.0f;
   uni.flags = PESTI_FLAG_GREEDY_IF_ZERO_T | (flags & PESTI_FLAG_ARGMAX_FIRST);
-  return launch(s, d_logits, dtype, B, V, ld, uni, nullptr, false, nullptr, d_out_tokens, nullptr,
+  return launch(s, d_logits, dtype, B, V, ld, uni, nullptr, false, false, nullptr, d_out_tokens, nullptr,
                 nullptr, 0, nullptr, st);
 }
 
@@ -1020,7 +1085,7 @@ int pesti_sample_row_host(pesti_sampler* s, const float* h_logits, int64_t V,
     PESTI_CUDA_TRY(cudaMemcpyAsync(s->d_row, h_logits, (size_t)V * sizeof(float), cudaMemcpyHostToDevice, st), "logits copy");
   PESTI_CUDA_TRY(cudaMemcpyAsync(s->d_u1, &u, sizeof(float), cudaMemcpyHostToDevice, st), "u copy");
   int rc = launch(s, s->d_row, PESTI_F32, 1, V, std::max<int64_t>(V, 1), *params, nullptr,
-                  needs_sorted_buffers(params, 1), s->d_u1, s->d_tok1, nullptr, nullptr, 0, nullptr, st);
+                  needs_sorted_buffers(params, 1), needs_survivor_pass(params, 1, V), s->d_u1, s->d_tok1, nullptr, nullptr, 0, nullptr, st);
   if (rc) return rc;
   uint32_t tok = 0;
   PESTI_CUDA_TRY(cudaMemcpyAsync(&tok, s->d_tok1, sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "token copy");
@@ -1052,7 +1117,7 @@ int pesti_sample_batch_noalloc(const void* d_logits, pesti_dtype dtype, int64_t 
 
   pesti_sampling_params uni{};
   const pesti_sampling_params* d_per_row = nullptr;
-  bool sorted_bufs = true;
+  bool sorted_bufs = true, survivors = true;
   size_t params_bytes = 0;  // host per-row params go to the front of the scratch
   if (params_on_device) {
     if (params_per_row) d_per_row = params;
@@ -1060,15 +1125,19 @@ int pesti_sample_batch_noalloc(const void* d_logits, pesti_dtype dtype, int64_t 
       PESTI_CUDA_TRY(cudaMemcpyAsync(&uni, params, sizeof(uni), cudaMemcpyDeviceToHost, st), "params copy");
       PESTI_CUDA_TRY(cudaStreamSynchronize(st), "params sync");
       sorted_bufs = needs_sorted_buffers(&uni, 1);
+      survivors = needs_survivor_pass(&uni, 1, V);
     }
   } else if (params_per_row) {
     sorted_bufs = needs_sorted_buffers(params, B);
+    survivors = needs_survivor_pass(params, B, V);
     params_bytes = align_up((size_t)B * sizeof(pesti_sampling_params));
   } else {
     uni = params[0];
     sorted_bufs = needs_sorted_buffers(&uni, 1);
+    survivors = needs_survivor_pass(&uni, 1, V);
   }
-  const Plan p = make_plan(dev.num_sms, dtype, B, V, sorted_bufs);
+  Plan p = make_plan(dev.num_sms, dtype, B, V, sorted_bufs);
+  p.survivors = survivors;
   const size_t need = params_bytes + p.bytes;
   if (need > (size_t)PESTI_NOALLOC_SCRATCH_BYTES)
     return fail(PESTI_E_INVALID_ARG,

@@ -42,6 +42,26 @@ for _p in (os.path.join(ROOT, "llm-workspace_b200"), os.path.join(ROOT, "oracle"
 import numpy as np  # noqa: E402
 
 METRIC = "sampled rows/s (B=64, V=128256 f32, T0.7 k50 p0.9)"
+
+
+def metric_for(w: int) -> str:
+    """The metric line of workload w (workload 2 is the headline)."""
+    import synth
+    if w == 2:
+        return METRIC
+    spec = synth.WORKLOADS[w]
+    return f"sampled rows/s ({spec['name']})"
+
+
+def params_text(w: int) -> str:
+    import synth
+    spec = synth.WORKLOADS[w]
+    ps_ = synth.params_for(w, spec["B"], spec["V"])
+    if len(set(ps_)) == 1:
+        t, p, k = ps_[0]
+        note = " (top-p unused since top_k > 0, sampling.rs:66)" if k > 0 and p > 0 else ""
+        return f"T{t} top_k{k} top_p{p}{note}"
+    return "per-row mix (synth.ROW_CLASSES_4)"
 UNIT = "rows/s"
 L2_BYTES = 126 * 1024 * 1024
 
@@ -155,7 +175,7 @@ def run_reference(args):
     dt = time.perf_counter() - t0
     value = rows_per_step * args.steps / dt
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
+        "metric": metric_for(w), "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
@@ -516,11 +536,11 @@ def main():
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": metric_for(w), "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic",
             "config": {"workload": spec["name"], "B_per_gpu": B, "V": V, "input_dtype": spec["dtype"],
-                       "params": "T0.7 top_k50 top_p0.9 (top-p unused since top_k > 0, sampling.rs:66)",
+                       "params": params_text(w),
                        "l2": f"rotating {nbuf} input buffers ({nbuf * step_bytes / 2**20:.0f} MiB > 126 MiB L2)",
                        "parallelism": f"rows split, {world} GPU(s), no collective"},
             "roofline": {"bound": "hbm", "kernel": "slice_stats_kernel", "achieved": achieved, "peak": peak,

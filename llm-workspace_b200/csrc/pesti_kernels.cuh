@@ -422,13 +422,16 @@ struct StatsShared {
   int match[MAX_MATCH];
   int nmatch;
   float tau;
+  uint32_t tbin, tabove;  // the candidate threshold's 12-bit bin and the count above it
   int last;
 };
 
 // Candidate threshold: a lower bound of the k-th largest raw logit among the
 // call's columns, from the segment maxima (maxima of disjoint segments are
-// distinct elements), rounded down to the start of its 12-bit key bin; -inf
-// when there are fewer than k segments.  Every thread of the block calls it.
+// distinct elements): the k-th largest segment max rounded down to the start
+// of its 20-bit key bin (a 12-bit histogram, then 8 more bits inside the bin
+// that holds it); -inf when there are fewer than k segments.  Every thread of
+// the block calls it.
 template <int SEG_REG>
 __device__ float kth_lower_bound(const SliceArgs& a, const float* segm, const float (&segr)[SEG_REG],
                                  bool seg_in_regs, long long keff, StatsShared& sh) {
@@ -458,17 +461,57 @@ __device__ float kth_lower_bound(const SliceArgs& a, const float* segm, const fl
   for (int q = 0; q < BPT; ++q) loc += sh.hist[TAU_BINS - 1 - BPT * tid - q];
   uint32_t tot;
   const uint32_t ex = block_excl_scan_add(loc, sh.uscr, tot);
-  if (tid == 0) sh.tau = NEG_INF;
+  if (tid == 0) {
+    sh.tau = NEG_INF;
+    sh.tbin = 0xffffffffu;
+  }
   __syncthreads();
   if ((long long)ex < keff && (long long)(ex + loc) >= keff) {
     uint32_t cum = ex;
     for (int q = 0; q < BPT; ++q) {
       const int bin = TAU_BINS - 1 - BPT * tid - q;
-      cum += sh.hist[bin];
-      if ((long long)cum >= keff) {
-        sh.tau = fkey_inv((uint32_t)bin << 20);
+      if ((long long)(cum + sh.hist[bin]) >= keff) {
+        sh.tbin = (uint32_t)bin;
+        sh.tabove = cum;
         break;
       }
+      cum += sh.hist[bin];
+    }
+  }
+  __syncthreads();
+  const uint32_t tb = sh.tbin;
+  if (tb == 0xffffffffu) return NEG_INF;  // fewer than k segments
+  // the second level: 8 more key bits of the segment maxima inside bin tb
+  for (int i = tid; i < 256; i += K1_NT) sh.hist[i] = 0u;
+  __syncthreads();
+  auto add2 = [&](float v) {
+    const bool ok = !is_nan(v) && v > NEG_INF && (fkey(v) >> 20) == tb;
+    if (ok) atomicAdd(&sh.hist[(fkey(v) >> 12) & 255u], 1u);
+  };
+  if (seg_in_regs) {
+#pragma unroll
+    for (int r = 0; r < SEG_REG; ++r) add2(segr[r]);
+  } else {
+    for (long long j = tid; j < a.nseg; j += K1_NT) add2(segm[j]);
+  }
+  __syncthreads();
+  if (tid < 32) {  // top-down over the 256 sub-bins, 8 per lane
+    uint32_t c8[8], lsum = 0u;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      c8[q] = sh.hist[255 - (lane * 8 + q)];
+      lsum += c8[q];
+    }
+    const uint32_t incl = warp_incl_scan_add(lsum) + sh.tabove;
+    const uint32_t excl = incl - lsum;
+    if ((long long)excl < keff && (long long)incl >= keff) {
+      uint32_t cum = excl;
+      int q = 0;
+      for (; q < 7; ++q) {
+        if ((long long)(cum + c8[q]) >= keff) break;
+        cum += c8[q];
+      }
+      sh.tau = fkey_inv((tb << 20) | ((uint32_t)(255 - (lane * 8 + q)) << 12));
     }
   }
   __syncthreads();

@@ -300,7 +300,10 @@ pesti::SliceArgs make_slice_args(const Plan& p, char* ws, const void* d_logits, 
   sa.cand_e = (float*)(ws + p.o_ce);
   sa.cand_idx = (uint32_t*)(ws + p.o_ci);
   sa.V_total = V;
-  sa.band = 0x1p-12f;
+  // guard band of the fold classification: the speculation runs ahead of the
+  // fold by the mass the fold absorbs, which grows along the row (up to about
+  // 6e-4 of it on rows of 256k)
+  sa.band = V > 131072 ? 0x1p-10f : 0x1p-12f;
   // the fast path stages the row's fold entries in shared memory; with very
   // many sub-slices it does not fit and all rows take the generic path
   const size_t fast_bytes = pesti::fast_smem_bytes((int)p.nsub, pesti::FAST_ENTS);

@@ -347,6 +347,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", type=int, default=2)
+    ap.add_argument("--rows", type=int, default=0,
+                    help="rows per GPU instead of the workload's batch (small cases for profiler captures)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernels-only", action="store_true",
                     help="only the warm-up and timed steps (for profiler captures); prints ms_per_step")
@@ -375,7 +377,7 @@ def main():
 
     w = args.workload
     spec = synth.WORKLOADS[w]
-    B, V = spec["B"], spec["V"]
+    B, V = (args.rows or spec["B"]), spec["V"]
     rows = rank_rows(rank, world, B)
     x = synth.make_logits(w, rows=rows)
     params = synth.params_for(w, B, V)

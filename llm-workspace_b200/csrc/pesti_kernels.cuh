@@ -2175,6 +2175,36 @@ __device__ void warp_sort_keys(unsigned long long* key, int n) {
   __syncwarp();
 }
 
+// The sequential f32 fold s = s0; s = s + v[j] over n values in shared
+// memory by one thread, with the query of fold::thread_fold (first j with
+// bits(s) >= tau_bits); the loads go out eight at a time ahead of the
+// dependent adds.
+__device__ __forceinline__ fold::Result serial_fold8(const float* v, long long n, uint32_t s0_bits,
+                                                     uint32_t tau_bits, bool stop_at_hit) {
+  fold::Result r;
+  uint32_t s = s0_bits & 0x7fffffffu;
+  r.hit = -1;
+  r.hit_s_bits = 0;
+  for (long long j0 = 0; j0 < n; j0 += 8) {
+    float x[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) x[u] = j0 + u < n ? v[j0 + u] : 0.0f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (j0 + u < n) {
+        s = fbits(fadd(bitsf(s), x[u]));
+        if (r.hit < 0 && s >= tau_bits) {
+          r.hit = j0 + u;
+          r.hit_s_bits = s;
+        }
+      }
+    }
+    if (stop_at_hit && r.hit >= 0) break;
+  }
+  r.s_bits = s;
+  return r;
+}
+
 // Fold of the exps of n raw logits (f32 or bf16, in global memory) by one
 // warp, starting from state s (bits).  The exact exps are staged STAGE at a
 // time in shared memory; each step takes 32 of them with a transducer scan
@@ -2340,6 +2370,19 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
     uint16_t* fown = reinterpret_cast<uint16_t*>(fent + cap);
     SubSurv* ss = reinterpret_cast<SubSurv*>(fown + cap);
     int* eoff = reinterpret_cast<int*>(ss + nsub);
+    // warp 1 fetches the candidates now (they are sorted after the staging)
+    int C = 0;
+    unsigned long long ck[2] = {0ull, 0ull};
+    if (wid == 1) {
+      C = a.cand_count[b];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int j = r * 32 + lane;
+        if (j < C && j < CAND_CAP)
+          ck[r] = ((unsigned long long)fbits(a.cand_e[b * CAND_CAP + j]) << 32) |
+                  (unsigned long long)(~a.cand_idx[b * CAND_CAP + j]);
+      }
+    }
     // stage the row's fold entries, compacted, with the whole block: one
     // thread per (sub-slice, group) pair in row order; a sub-slice with an
     // overflowed group stages a single replay marker
@@ -2348,16 +2391,20 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
       const GroupEnt* gs = a.gsurv + b * nsub * a.jmax;
       const FoldEnt* pool = a.pool + b * POOL_CAP;
       int* rep = eoff;  // per sub-slice: a group overflowed
+      const int npair = nsub * a.jmax;
+      // with at most one pair per thread, its record is read once (here)
+      const bool one = npair <= K2_NT;
+      GroupEnt ge1{{0u, 0u, 0u, 0u}, 0, 0, 0, 0};
+      if (one && tid < npair) ge1 = gs[tid];
       for (int q = tid; q < nsub; q += K2_NT) {
         ss[q] = survs[q];
         if ((long long)q * a.SL >= V) ss[q].ngroups = 0;  // past the row's end: no units
         rep[q] = 0;
       }
       __syncthreads();
-      const int npair = nsub * a.jmax;
       for (int t = tid; t < npair; t += K2_NT) {
         const int q = t / a.jmax, j = t - q * a.jmax;
-        if (j < ss[q].ngroups && gs[t].replay) rep[q] = 1;
+        if (j < ss[q].ngroups && (one ? ge1.replay : gs[t].replay)) rep[q] = 1;
       }
       __syncthreads();
       // each pair's place in the row (a block scan), then every entry copied
@@ -2376,7 +2423,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
               ne = j == 0 ? 1 : 0;
               off = -1 - q;  // replay marker of sub-slice q
             } else {
-              const GroupEnt ge = gs[t];
+              const GroupEnt ge = one ? ge1 : gs[t];
               ne = ge.nent;
               off = ge.off;
               inl = ge.inl != 0;
@@ -2421,14 +2468,17 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
     // merge consecutive runs of one binade (fewer steps for the walk below)
     if (fs.total <= 2 * K2_NT) merge_runs<2>(fs, fent, fs.total, sh);
     else if (fs.total <= cap) merge_runs<MERGE_EPT>(fs, fent, fs.total, sh);
-    const int C = a.cand_count[b];
+    if (wid != 1) C = a.cand_count[b];
     // a shard lists any number of candidates up to FAST_CAND (the row's k-th
     // largest may lie in another shard)
     const bool cand_ok = (a.shard || C >= keff) && C <= FAST_CAND;
     if (wid == 1 && fs.total <= cap && cand_ok) {
       // candidates by (e desc, index asc) while warp 0 folds; the order by p
       // = e/S differs only inside groups of equal p (fixed up below)
-      for (int j = lane; j < C; j += 32)
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+        if (r * 32 + lane < C) fs.key[r * 32 + lane] = ck[r];
+      for (int j = 64 + lane; j < C; j += 32)
         fs.key[j] = ((unsigned long long)fbits(a.cand_e[b * CAND_CAP + j]) << 32) |
                     (unsigned long long)(~a.cand_idx[b * CAND_CAP + j]);
       __syncwarp();
@@ -2545,14 +2595,15 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
       }
       if (ok) {
         // total over the kept list (sampling.rs:81), normalisation (:94), draw (:99-111)
+        for (long long j = lane; j < keff; j += 32) fs.q[j] = bitsf((uint32_t)(fs.key[j] >> 32));
+        __syncwarp();
         uint32_t tb = 0u;
-        if (lane == 0)
-          for (long long j = 0; j < keff; ++j) tb = fbits(fadd(bitsf(tb), bitsf((uint32_t)(fs.key[j] >> 32))));
+        if (lane == 0) tb = serial_fold8(fs.q, keff, 0u, fold::NO_QUERY, false).s_bits;
         const float total = bitsf(__shfl_sync(PESTI_FULL_MASK, tb, 0));
-        for (long long j = lane; j < keff; j += 32) fs.q[j] = fdiv(bitsf((uint32_t)(fs.key[j] >> 32)), total);
+        for (long long j = lane; j < keff; j += 32) fs.q[j] = fdiv(fs.q[j], total);
         __syncwarp();
         if (lane == 0) {
-          const fold::Result dr = fold::thread_fold(fs.q, keff, 0u, r_tau, true);
+          const fold::Result dr = serial_fold8(fs.q, keff, 0u, r_tau, true);
           const long long at = dr.hit >= 0 ? dr.hit : keff - 1;
           a.out[b] = ~(uint32_t)(fs.key[at] & 0xffffffffull);
           if (a.kept_count) a.kept_count[b] = keff;

@@ -158,6 +158,7 @@ struct SliceArgs {
   ClassTask* tasks; // [B*P*K1_WARPS*jmax] task-queue classification
   int* task_count;  // tasks queued
   int* task_next;   // tasks taken
+  int* task_count_h;  // tasks of the rows' first sub-slices (the slowest), queued from the top of the list
   GroupEnt* gsurv;  // [B][P*K1_WARPS][jmax]
   FoldEnt* pool;    // [B][POOL_CAP] fold entries
   int* pool_ctr;    // [B]
@@ -791,6 +792,7 @@ __global__ void __launch_bounds__(K1_NT) slice_stats_kernel(SliceArgs a) {
       *a.item_next = 0;
       *a.task_count = 0;
       *a.task_next = 0;
+      *a.task_count_h = 0;
     }
   }
   const TIn* row = (const TIn*)a.logits + b * a.ld;
@@ -1182,8 +1184,14 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
   const float pm = warp_reduce_fmax(pruned_max);
   const int ngroups = fast ? (int)((sins + GROUP - 1) / GROUP) : 0;
   if (ngroups > 0 && lane == 0) {
-    const int t0 = atomicAdd(a.task_count, ngroups);
-    for (int j = 0; j < ngroups; ++j) a.tasks[t0 + j] = ClassTask{(int)b, (int)(sub * a.jmax + j)};
+    // a row's first sub-slice, where the running sum is small and most
+    // elements need the general classification, has the slowest tasks: they
+    // go to the top of the list, which the classification takes first
+    const bool heavy = sub == 0;
+    const long long cap = a.B * (long long)nsub * a.jmax;
+    const int t0 = atomicAdd(heavy ? a.task_count_h : a.task_count, ngroups);
+    for (int j = 0; j < ngroups; ++j)
+      a.tasks[heavy ? cap - 1 - (t0 + j) : t0 + j] = ClassTask{(int)b, (int)(sub * a.jmax + j)};
   }
   if (lane == 0) *so = SubSurv{(int32_t)sins, ngroups, cand_here ? 0 : 1, pm};
 }
@@ -1463,9 +1471,11 @@ __device__ __forceinline__ float classify_group(const SliceArgs& a, long long b,
 // survivors, so the tasks are independent and a persistent grid of warps
 // takes them: each warp's first task is its own index (a burst of thousands
 // of atomics on one counter would serialise the start), later ones come from
-// the counter, claimed while the current task runs.  The list is taken from
-// its end: the survivor pass queues the tasks of its slowest warps (the
-// dense start of each row, whose tasks cost the most) last.
+// the counter, claimed when a task is done (a claim made earlier would tie
+// the next task to a warp whose current one runs long, while other warps
+// idle).  The tasks of every row's first sub-slice, which cost the most, are
+// taken first; then the others from the end of their list (the survivor pass
+// queues the tasks of its slowest warps last).
 __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
   __shared__ ClassShared sh;
   grid_dep_launch_next();
@@ -1473,23 +1483,18 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int nsub = a.P * K1_WARPS;
   const long long V = a.V;
-  const int ntasks = *a.task_count;
+  const int nlow = *a.task_count, nhigh = *a.task_count_h;
+  const int ntasks = nlow + nhigh;
+  const long long cap = a.B * (long long)nsub * a.jmax;  // the list's slots
+  auto task_at = [&](int i) { return i < nhigh ? a.tasks[cap - 1 - i] : a.tasks[nlow - 1 - (i - nhigh)]; };
   float* graw = sh.raw[w];
   uint32_t* gidx = sh.idx[w];
   const int nwarps = (int)gridDim.x * K1_WARPS;
   int t = (int)blockIdx.x * K1_WARPS + w;
-  ClassTask tk_next = t < ntasks ? a.tasks[ntasks - 1 - t] : ClassTask{0, 0};
-  int claim = 0;
-  if (lane == 0 && t < ntasks) claim = atomicAdd(a.task_next, 1);
+  ClassTask tk_next = t < ntasks ? task_at(t) : ClassTask{0, 0};
   for (;;) {
     if (t >= ntasks) break;
     const ClassTask tk = tk_next;
-    const int tn = nwarps + __shfl_sync(PESTI_FULL_MASK, claim, 0);
-    if (tn < ntasks) {
-      tk_next = a.tasks[ntasks - 1 - tn];
-      if (lane == 0) claim = atomicAdd(a.task_next, 1);
-    }
-    t = tn;
     const long long b = tk.b;
     const long long sub = tk.qj / a.jmax;
     const int j = tk.qj - (int)sub * a.jmax;
@@ -1521,26 +1526,39 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
       s_approx += (double)warp_reduce_add(acc);
     }
     __syncwarp();
-    if (ssv.pad) {  // the group's top-k candidates (all of them survived)
-      const float tau = ri.tau;
+    // the group's top-k candidates (all of them survived): counted first and
+    // their slots reserved with one atomic, whose latency the classification
+    // overlaps; written after it (the row kernel sorts the candidates, so
+    // their order in the list is free)
+    const float tau = ri.tau;
+    int ccount = 0, cbase = 0;
+    if (ssv.pad) {
+      for (int i0 = 0; i0 < n; i0 += 32) {
+        const int i = i0 + lane;
+        ccount += __popc(__ballot_sync(PESTI_FULL_MASK, i < n && graw[i] >= tau));
+      }
+      if (ccount > 0 && lane == 0) cbase = atomicAdd(a.cand_count + b, ccount);
+    }
+    (void)classify_group(a, b, sub, j, n, s_approx, scale, T, m, graw, gidx, sh.ea[w], sh.ck[w], sh.c0[w], sh.c1[w]);
+    int claim = 0;
+    if (lane == 0) claim = atomicAdd(a.task_next, 1);  // its latency overlaps the candidate writes
+    if (ccount > 0) {
+      int slot0 = __shfl_sync(PESTI_FULL_MASK, cbase, 0);
       for (int i0 = 0; i0 < n; i0 += 32) {
         const int i = i0 + lane;
         const float raw = i < n ? graw[i] : 0.0f;
         const bool cand = i < n && raw >= tau;
         const uint32_t bal = __ballot_sync(PESTI_FULL_MASK, cand);
-        if (bal) {
-          int basec = 0;
-          if (lane == 0) basec = atomicAdd(a.cand_count + b, __popc(bal));
-          basec = __shfl_sync(PESTI_FULL_MASK, basec, 0);
-          const int slot = basec + __popc(bal & ((1u << lane) - 1u));
-          if (cand && slot < CAND_CAP) {
-            a.cand_e[b * CAND_CAP + slot] = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127
-            a.cand_idx[b * CAND_CAP + slot] = gidx[i];
-          }
+        const int slot = slot0 + __popc(bal & ((1u << lane) - 1u));
+        if (cand && slot < CAND_CAP) {
+          a.cand_e[b * CAND_CAP + slot] = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127
+          a.cand_idx[b * CAND_CAP + slot] = gidx[i];
         }
+        slot0 += __popc(bal);
       }
     }
-    (void)classify_group(a, b, sub, j, n, s_approx, scale, T, m, graw, gidx, sh.ea[w], sh.ck[w], sh.c0[w], sh.c1[w]);
+    t = nwarps + __shfl_sync(PESTI_FULL_MASK, claim, 0);
+    if (t < ntasks) tk_next = task_at(t);
   }
 }
 

@@ -247,7 +247,7 @@ Plan make_plan(int num_sms, pesti_dtype dtype, long long B, long long V, bool so
   p.o_gsurv = take(ngrp * sizeof(pesti::GroupEnt));
   p.o_inext = take(sizeof(int));
   p.o_tasks = take(ngrp * sizeof(pesti::ClassTask));
-  p.o_tctr = take(2 * sizeof(int));
+  p.o_tctr = take(3 * sizeof(int));
   p.o_pctr = take((size_t)B * sizeof(int));
   p.o_pool = take((size_t)B * pesti::POOL_CAP * sizeof(pesti::FoldEnt));
   if (sorted_bufs) {
@@ -290,6 +290,7 @@ pesti::SliceArgs make_slice_args(const Plan& p, char* ws, const void* d_logits, 
   sa.tasks = (pesti::ClassTask*)(ws + p.o_tasks);
   sa.task_count = (int*)(ws + p.o_tctr);
   sa.task_next = sa.task_count + 1;
+  sa.task_count_h = sa.task_count + 2;
   // rows past 128k columns (and vocabulary shards, set by their caller) take
   // the fused pass; shorter ones the survivor pass and the task queue
   sa.fused = V > 131072 ? 1 : 0;

@@ -393,7 +393,10 @@ def main():
     bufs = [host.to(dev) for _ in range(nbuf)]
     ud = torch.from_numpy(u).to(dev)
     out = torch.empty(B, dtype=torch.int32, device=dev)
-    cfgs = [ps.SamplingConfig(t, p, k) for (t, p, k) in params]
+    # one SamplingConfig when every row shares it (as the reference's API
+    # takes it), else the per-row list converted once
+    cfgs = (ps.SamplingConfig(*params[0]) if len(set(params)) == 1
+            else ps.PreparedParams([ps.SamplingConfig(t, p, k) for (t, p, k) in params]))
     s = ps.Sampler(local)
     stream = torch.cuda.current_stream(dev)
 

@@ -1221,8 +1221,10 @@ struct ClassShared {
 // (this warp's shared arrays), s_approx the approximate fold state before the
 // first of them.  Writes the group's GroupEnt and, unless it is one clean
 // run, its entries in the row's pool; returns the group's approximate mass
-// (the sum of the approximate exps).  All 32 lanes call it.
+// (the sum of the approximate exps).  try_clean = false skips the clean case
+// (a caller that has tried it already).  All 32 lanes call it.
 __device__ __forceinline__ float classify_group(const SliceArgs& a, long long b, long long sub, int j, int n,
+                                            bool try_clean,
                                             double s_approx, bool scale, float T, float m, float* graw,
                                             uint32_t* gidx, float* eas, uint32_t* cks, uint32_t* c0s,
                                             uint32_t* c1s) {
@@ -1282,6 +1284,27 @@ __device__ __forceinline__ float classify_group(const SliceArgs& a, long long b,
   const int i0 = lane * g;
   const int nl = n - i0 < 0 ? 0 : (n - i0 > g ? g : n - i0);  // valid elements of the lane
   __syncwarp();
+  // approximate states as floats relative to the carried double (the guard
+  // band is 2^-12; float rounding is 2^-24)
+  const float sb = (float)s_approx;
+  // A clean group: the whole range of its approximate states lies inside one
+  // binade (within the guard band), so every element is a plain increment
+  // k = rint(e/w) of one run (e < lo there, so k is in the binade's units).
+  // k comes from the approximation where it decides it and from the exact
+  // exp otherwise; unless some element is a tie (its k depends on the
+  // parity of the state), the group's fold is that run with the sum of the
+  // increments: one entry, no segmentation.  The binade is that of the
+  // start, so the increments are formed in pass A itself, speculatively; the
+  // group's end state decides, and only then are the exact exps of the
+  // elements the approximation leaves undecided taken.
+  uint32_t clo = 0u;
+  bool possible = false;
+  if (try_clean && sb >= 0x1p-126f) {
+    clo = fbits(sb) & 0x7f800000u;
+    possible = sb >= bitsf(clo) * (1.0f + BAND);
+  }
+  const int sh2 = 150 - (int)(clo >> 23);  // w = 2^(E-150) (E = 0: the subnormal grid 2^-149)
+  uint32_t ksum = 0u, undecided = 0u;  // undecided: bit jj, element jj of the lane
   // pass A: approximate exps (sampling.rs:46,127 within 2^-22)
   float ltot = 0.0f;
 #pragma unroll 1
@@ -1290,61 +1313,39 @@ __device__ __forceinline__ float classify_group(const SliceArgs& a, long long b,
     const float e = pesti_expf_approx(fsub(scale ? fdiv(raw, T) : raw, m));
     eas[jj * 32 + lane] = e;
     ltot += e;
+    if (possible) {
+      bool exact;
+      if (e == 0.0f) {
+        exact = (clo >> 23) < 40u;  // else: exact e < 4.5e-38 rounds to 0 on this grid
+      } else {
+        const float tt = __uint_as_float(fbits(e) + ((uint32_t)sh2 << 23));  // e/w, exact scaling
+        const float kr = rintf(tt);
+        const float slack = 0.5f - fabsf(tt - kr);
+        exact = !(slack > tt * DE + 0x1p-24f);
+        if (!exact) ksum += (uint32_t)kr;
+      }
+      if (exact) undecided |= 1u << jj;
+    }
   }
   const float lincl = warp_incl_scan_add(ltot);
   const float gtot = __shfl_sync(PESTI_FULL_MASK, lincl, 31);
-  // approximate states as floats relative to the carried double (the guard
-  // band is 2^-12; float rounding is 2^-24)
-  const float sb = (float)s_approx;
   const float lbase = lincl - ltot;
-
-  // A clean group: the whole range of its approximate states lies inside one
-  // binade (within the guard band), so every element is a plain increment
-  // k = rint(e/w) of one run (e < lo there, so k is in the binade's units).
-  // k comes from the approximation where it decides it and from the exact
-  // exp otherwise; unless some element is a tie (its k depends on the
-  // parity of the state), the group's fold is that run with the sum of the
-  // increments: one entry, no segmentation.
-  {
-    bool clean = false;
-    uint32_t clo = 0u;
-    if (sb >= 0x1p-126f) {
-      clo = fbits(sb) & 0x7f800000u;
-      const float lov = bitsf(clo);
-      clean = sb >= lov * (1.0f + BAND) && sb + gtot <= 2.0f * lov * (1.0f - BAND);
+  if (possible && sb + gtot <= 2.0f * bitsf(clo) * (1.0f - BAND)) {
+    bool decided = true;
+    for (uint32_t um = undecided; um != 0u; um &= um - 1u) {
+      const int jj = __ffs(um) - 1;
+      const float raw = graw[i0 + jj];
+      const float ex = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127, exact
+      const uint32_t k0 = fbits(fadd(bitsf(clo), ex)) - clo;
+      const uint32_t k1 = fbits(fadd(bitsf(clo + 1u), ex)) - (clo + 1u);
+      decided = decided && k0 == k1;
+      ksum += k0;
     }
-    if (clean) {
-      const int sh2 = 150 - (int)(clo >> 23);  // w = 2^(E-150)
-      uint32_t ksum = 0u;
-      bool decided = true;
-#pragma unroll 1
-      for (int jj = 0; jj < nl; ++jj) {
-        const float ea = eas[jj * 32 + lane];
-        bool exact = false;
-        if (ea == 0.0f) {
-          exact = (clo >> 23) < 40u;  // else: exact e < 4.5e-38 rounds to 0 on this grid
-        } else {
-          const float tt = __uint_as_float(fbits(ea) + ((uint32_t)sh2 << 23));  // ea/w, exact scaling
-          const float kr = rintf(tt);
-          const float slack = 0.5f - fabsf(tt - kr);
-          if (slack > tt * DE + 0x1p-24f) ksum += (uint32_t)kr;
-          else exact = true;
-        }
-        if (exact) {
-          const float raw = graw[i0 + jj];
-          const float ex = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:46,127, exact
-          const uint32_t k0 = fbits(fadd(bitsf(clo), ex)) - clo;
-          const uint32_t k1 = fbits(fadd(bitsf(clo + 1u), ex)) - (clo + 1u);
-          decided = decided && k0 == k1;
-          ksum += k0;
-        }
-      }
-      if (__all_sync(PESTI_FULL_MASK, decided)) {
-        const uint32_t inc = tr_sat(warp_reduce_add(ksum));  // each < 2^22, at most 256 of them
-        if (lane == 0)
-          a.gsurv[(b * nsub + sub) * a.jmax + j] = GroupEnt{{clo, inc, inc, gidx[n - 1] + 1u}, 0, 1, 0, 1};
-        return gtot;
-      }
+    if (__all_sync(PESTI_FULL_MASK, decided)) {
+      const uint32_t inc = tr_sat(warp_reduce_add(ksum));  // each < 2^22, at most 256 of them
+      if (lane == 0)
+        a.gsurv[(b * nsub + sub) * a.jmax + j] = GroupEnt{{clo, inc, inc, gidx[n - 1] + 1u}, 0, 1, 0, 1};
+      return gtot;
     }
   }
   // the key of the lane's last element decides whether the next lane's first
@@ -1421,12 +1422,19 @@ __device__ __forceinline__ float classify_group(const SliceArgs& a, long long b,
   const int neincl = warp_incl_scan_add(ne);
   const int nclosed = __shfl_sync(PESTI_FULL_MASK, neincl, 31);
   const int netot = nclosed + (last.cnt > 0u ? 1 : 0);
+  // the entries' place in the row's pool: one atomic, whose latency pass C
+  // overlaps when the entries fit in the warp's approximate-exp array (no
+  // longer read): pass C writes them there and they are copied once the
+  // place is known
+  constexpr int STAGED = GROUP * (int)sizeof(float) / (int)sizeof(FoldEnt);
+  const bool staged = netot <= STAGED;
   int off0 = 0;
   if (lane == 0) off0 = atomicAdd(a.pool_ctr + b, netot);
-  off0 = __shfl_sync(PESTI_FULL_MASK, off0, 0);
-  const bool replay = off0 + netot > POOL_CAP;
-  if (!replay) {
-    FoldEnt* ent = a.pool + b * POOL_CAP + off0;
+  if (!staged) off0 = __shfl_sync(PESTI_FULL_MASK, off0, 0);
+  const bool replay_known = !staged && off0 + netot > POOL_CAP;
+  if (!replay_known) {
+    FoldEnt* ent = staged ? reinterpret_cast<FoldEnt*>(eas) : a.pool + b * POOL_CAP + off0;
+    __syncwarp();  // every lane is done reading eas
     int slot = neincl - ne;
     if (hh) {  // pass C: the same walk, writing the entries
       uint32_t cur = prev_key;
@@ -1459,6 +1467,16 @@ __device__ __forceinline__ float classify_group(const SliceArgs& a, long long b,
     }
     if (lane == 0 && last.cnt > 0u) ent[nclosed] = FoldEnt{last.key, last.a0, last.a1, gidx[n - 1] + 1u};
   }
+  if (staged) {
+    off0 = __shfl_sync(PESTI_FULL_MASK, off0, 0);
+    __syncwarp();  // the staged entries of every lane are visible
+    if (off0 + netot <= POOL_CAP) {
+      const FoldEnt* sent = reinterpret_cast<const FoldEnt*>(eas);
+      FoldEnt* ent = a.pool + b * POOL_CAP + off0;
+      for (int e = lane; e < netot; e += 32) ent[e] = sent[e];
+    }
+  }
+  const bool replay = off0 + netot > POOL_CAP;
   if (lane == 0)
     a.gsurv[(b * nsub + sub) * a.jmax + j] = GroupEnt{{0u, 0u, 0u, 0u}, off0, replay ? 0 : netot, replay ? 1 : 0, 0};
   return gtot;
@@ -1539,7 +1557,8 @@ __global__ void __launch_bounds__(K1_NT) classify_kernel(SliceArgs a) {
       }
       if (ccount > 0 && lane == 0) cbase = atomicAdd(a.cand_count + b, ccount);
     }
-    (void)classify_group(a, b, sub, j, n, s_approx, scale, T, m, graw, gidx, sh.ea[w], sh.ck[w], sh.c0[w], sh.c1[w]);
+    (void)classify_group(a, b, sub, j, n, true, s_approx, scale, T, m, graw, gidx, sh.ea[w], sh.ck[w], sh.c0[w],
+                         sh.c1[w]);
     int claim = 0;
     if (lane == 0) claim = atomicAdd(a.task_next, 1);  // its latency overlaps the candidate writes
     if (ccount > 0) {
@@ -1862,8 +1881,9 @@ __global__ void __launch_bounds__(K1_NT, 3) fused_classify_kernel(SliceArgs a) {
           continue;
         }
       }
-      s_est += (double)classify_group(a, b, sub, j, n, s_est, scale, T, m, graw, gidx, sh.ea[w], sh.ck[w], sh.c0[w],
-                                      sh.c1[w]);
+      // (its clean case was tried above)
+      s_est += (double)classify_group(a, b, sub, j, n, false, s_est, scale, T, m, graw, gidx, sh.ea[w], sh.ck[w],
+                                      sh.c0[w], sh.c1[w]);
       __syncwarp();
     }
     it = nit;

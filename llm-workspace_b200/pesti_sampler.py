@@ -143,6 +143,20 @@ class SamplingConfig:
         return _Params(float(self.temperature), float(self.top_p), int(self.top_k), flags)
 
 
+class PreparedParams:
+    """Per-row sampling parameters converted once into the C layout, for
+    callers that sample many batches with the same rows' configs: pass it to
+    the batch calls in place of the list (converting a long list on every
+    call costs host time comparable to the GPU step)."""
+
+    def __init__(self, configs: Sequence[SamplingConfig], greedy_if_zero_t: bool = True,
+                 argmax_first: bool = False):
+        self.rows = len(configs)
+        self.greedy_if_zero_t = greedy_if_zero_t
+        self.argmax_first = argmax_first
+        self.arr = (_Params * self.rows)(*[c.to_params(greedy_if_zero_t, argmax_first) for c in configs])
+
+
 class Pcg32:
     """PCG32 (O'Neill 2014, XSH-RR 64->32) with the reference's f32 draw.
 
@@ -337,6 +351,13 @@ def _batch_args(logits, configs, out, greedy_if_zero_t, argmax_first, kept_width
     if isinstance(configs, SamplingConfig):
         arr = (_Params * 1)(configs.to_params(greedy_if_zero_t, argmax_first))
         per_row = 0
+    elif isinstance(configs, PreparedParams):
+        if configs.rows != B:
+            raise ValueError("need one config per row")
+        if (configs.greedy_if_zero_t, configs.argmax_first) != (greedy_if_zero_t, argmax_first):
+            raise ValueError("PreparedParams were made with other flags")
+        arr = configs.arr
+        per_row = 1
     else:
         if len(configs) != B:
             raise ValueError("need one config per row")

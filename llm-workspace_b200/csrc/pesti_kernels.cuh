@@ -413,6 +413,7 @@ __device__ __forceinline__ void stream_subslice(const TIn* row, long long start,
 // ---------------------------------------------------------------------------
 struct StatsShared {
   uint32_t hist[TAU_BINS];
+  uint32_t hist2[256];  // the candidate threshold's second level
   float mraw[MAX_SUBS];
   float srel[MAX_SUBS];
   double dscr[34];
@@ -439,6 +440,11 @@ __device__ float kth_lower_bound(const SliceArgs& a, const float* segm, const fl
   const int tid = threadIdx.x, lane = tid & 31;
   const float NEG_INF = -__int_as_float(0x7f800000);
   for (int i = tid; i < TAU_BINS; i += K1_NT) sh.hist[i] = 0u;
+  for (int i = tid; i < 256; i += K1_NT) sh.hist2[i] = 0u;
+  if (tid == 0) {
+    sh.tau = NEG_INF;
+    sh.tbin = 0xffffffffu;
+  }
   __syncthreads();
   auto add = [&](float v) {  // -inf (also padding) and NaN are not counted
     const bool ok = !is_nan(v) && v > NEG_INF;
@@ -459,14 +465,10 @@ __device__ float kth_lower_bound(const SliceArgs& a, const float* segm, const fl
   constexpr int BPT = TAU_BINS / K1_NT;  // top-down: thread t owns bins [4096-16(t+1), 4096-16t)
   uint32_t loc = 0;
 #pragma unroll
-  for (int q = 0; q < BPT; ++q) loc += sh.hist[TAU_BINS - 1 - BPT * tid - q];
+  for (int q = 0; q < BPT; ++q)  // in an order rotated by the thread: 2-way bank conflicts, not 16
+    loc += sh.hist[TAU_BINS - 1 - BPT * tid - ((q + tid) & (BPT - 1))];
   uint32_t tot;
-  const uint32_t ex = block_excl_scan_add(loc, sh.uscr, tot);
-  if (tid == 0) {
-    sh.tau = NEG_INF;
-    sh.tbin = 0xffffffffu;
-  }
-  __syncthreads();
+  const uint32_t ex = block_excl_scan_add(loc, sh.uscr, tot);  // ends with a barrier
   if ((long long)ex < keff && (long long)(ex + loc) >= keff) {
     uint32_t cum = ex;
     for (int q = 0; q < BPT; ++q) {
@@ -483,11 +485,9 @@ __device__ float kth_lower_bound(const SliceArgs& a, const float* segm, const fl
   const uint32_t tb = sh.tbin;
   if (tb == 0xffffffffu) return NEG_INF;  // fewer than k segments
   // the second level: 8 more key bits of the segment maxima inside bin tb
-  for (int i = tid; i < 256; i += K1_NT) sh.hist[i] = 0u;
-  __syncthreads();
   auto add2 = [&](float v) {
     const bool ok = !is_nan(v) && v > NEG_INF && (fkey(v) >> 20) == tb;
-    if (ok) atomicAdd(&sh.hist[(fkey(v) >> 12) & 255u], 1u);
+    if (ok) atomicAdd(&sh.hist2[(fkey(v) >> 12) & 255u], 1u);
   };
   if (seg_in_regs) {
 #pragma unroll
@@ -500,7 +500,7 @@ __device__ float kth_lower_bound(const SliceArgs& a, const float* segm, const fl
     uint32_t c8[8], lsum = 0u;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      c8[q] = sh.hist[255 - (lane * 8 + q)];
+      c8[q] = sh.hist2[255 - (lane * 8 + q)];
       lsum += c8[q];
     }
     const uint32_t incl = warp_incl_scan_add(lsum) + sh.tabove;
@@ -543,6 +543,12 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
   const bool scale = T > 0.0f;
   const float t_eff = scale ? T : 1.0f;
   const SubStat* st = a.stats + b * nsub;
+  // the table of the exact exp that one thread takes at the end (the
+  // candidate threshold's) is brought into this SM's L1 now
+  if (tid < 4) {
+    const char* tab = reinterpret_cast<const char*>(tid < 2 ? pesti_exp_t_hi_d : pesti_exp_t_lo_d);
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(tab + (tid & 1) * 128));
+  }
   // the segment maxima (for the candidate threshold) are fetched now, while
   // the sub-slice statistics are combined
   constexpr int SEG_REG = 4;
@@ -693,7 +699,11 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
   const bool uniform = (fl & MF_NAN) || (scale && T == INF && (fl & (MF_POSINF | MF_NEGINF))) ||
                        !(fabsf(m) < INF) || VT <= 0;
   const bool need_pre = !is_greedy(prm) && !uniform;
-  if (need_pre) {
+  // with at most 32*PER sub-slices only warp 0 holds any: it computes the
+  // prefix alone (the same values, without block barriers), and the other
+  // warps go on to the candidate threshold
+  const bool warp0_only = nsub <= 32 * (MAX_SUBS / K1_NT);
+  if (need_pre && (!warp0_only || w == 0)) {
     // exclusive prefix of the approximate softmax mass and of the max, per sub-slice
     const float c2 = 1.4426950408889634f / t_eff;
     const float ym = mx * c2;
@@ -712,17 +722,19 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
       run = fmaxf(run, mm);
     }
     double dt;
-    double ex = ex0 + block_excl_scan_add(lsum, sh.dscr, dt);
+    double ex = ex0 + (warp0_only ? warp_incl_scan_add(lsum) - lsum : block_excl_scan_add(lsum, sh.dscr, dt));
     float inc = run;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const float y = __shfl_up_sync(PESTI_FULL_MASK, inc, o);
       if (lane >= o) inc = fmaxf(inc, y);
     }
-    if (lane == 31) sh.fscr[w] = inc;
-    __syncthreads();
     float wpre = pmax0;
-    for (int q = 0; q < w; ++q) wpre = fmaxf(wpre, sh.fscr[q]);
+    if (!warp0_only) {
+      if (lane == 31) sh.fscr[w] = inc;
+      __syncthreads();
+      for (int q = 0; q < w; ++q) wpre = fmaxf(wpre, sh.fscr[q]);
+    }
     float exc = __shfl_up_sync(PESTI_FULL_MASK, inc, 1);
     if (lane == 0) exc = NEG_INF;
     float pmax = fmaxf(wpre, exc);
@@ -2539,25 +2551,34 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
       // the raw logits of the row range it covers, from the state before it
       // (the dropped elements in the range are exact no-ops).
       const int nm = fs.nment;
+      constexpr int WB = 8;  // entries per batch; the next batch is loaded while one is walked
       int i = 0;
       while (i < nm) {
         int fi = -1;  // first entry the state does not fit
-        for (; i < nm && fi < 0; i += 4) {
-          FoldEnt en[4];  // four at a time: their loads do not depend on the state
+        FoldEnt nx[WB];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) en[u] = fent[i + u < nm ? i + u : i];
+        for (int u = 0; u < WB; ++u) nx[u] = fent[i + u < nm ? i + u : nm - 1];
+        for (; i < nm; i += WB) {
+          FoldEnt en[WB];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if (fi < 0 && i + u < nm) {
-              const bool sp = en[u].lo == fold::SPECIAL;
-              const uint32_t s_sp = fbits(fadd(bitsf(s), bitsf(en[u].a0)));
-              const uint32_t ns = s + ((s & 1u) ? en[u].a1 : en[u].a0);  // < 2^31 + 2^30: no wrap
-              // also false for every replay marker (no binade has its bits)
-              const bool fits = fold::binade_lo_bits(s) == en[u].lo && ns < fold::binade_hi_bits(en[u].lo);
-              if (!sp && !fits) fi = i + u;
-              else s = sp ? s_sp : ns;
-            }
+          for (int u = 0; u < WB; ++u) {
+            en[u] = nx[u];
+            const int k = i + WB + u;
+            nx[u] = fent[k < nm ? k : nm - 1];
           }
+          // branch-free: the state stops at the first entry it does not fit
+#pragma unroll
+          for (int u = 0; u < WB; ++u) {
+            const bool live = fi < 0 && i + u < nm;
+            const bool sp = en[u].lo == fold::SPECIAL;
+            const uint32_t s_sp = fbits(fadd(bitsf(s), bitsf(en[u].a0)));
+            const uint32_t ns = s + ((s & 1u) ? en[u].a1 : en[u].a0);  // < 2^31 + 2^30: no wrap
+            // also false for every replay marker (no binade has its bits)
+            const bool fits = fold::binade_lo_bits(s) == en[u].lo && ns < fold::binade_hi_bits(en[u].lo);
+            fi = live && !sp && !fits ? i + u : fi;
+            s = live && (sp || fits) ? (sp ? s_sp : ns) : s;
+          }
+          if (fi >= 0) break;
         }
         if (fi < 0) break;
         const uint32_t from = fi > 0 ? fent[fi - 1].end : 0u;

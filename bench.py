@@ -66,8 +66,15 @@ UNIT = "rows/s"
 L2_BYTES = 126 * 1024 * 1024
 
 
-# slice_stats_kernel, survivor_kernel, classify_kernel, row_kernel
-KERNELS_PER_STEP = 4
+def kernels_per_step(V, params):
+    """This library's launches in one step: the HBM pass; for rows of at most
+    128k columns the survivor pass and the task-queue classification, else
+    the fused pass (plus the survivor pass when some row is off the top-k fast
+    path); the row kernel."""
+    if V <= 131072:
+        return 4
+    off_fast = any(not (1 <= k <= 256) or t <= 0 for (t, _, k) in params)
+    return 4 if off_fast else 3
 
 
 def measured_peaks():
@@ -555,7 +562,7 @@ def main():
             "step_hbm_gbs": step_bytes / (ms_per_step / 1e3) / 1e9,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": step_bytes + B * 4,
                     "d2h_bytes_per_step": B * 4},
-            "gpu_launches": KERNELS_PER_STEP * args.steps,
+            "gpu_launches": kernels_per_step(V, params) * args.steps,
             "clocks": clk,
             "b1_latency_us": lat,
             "cpu_baseline": cpu,

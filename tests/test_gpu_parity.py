@@ -174,3 +174,25 @@ def test_host_row_api_matches_oracle(sampler):
     for b in range(20):
         t = sampler.sample_with_u(x[b], ps.SamplingConfig(0.8, 0.95, 40), float(u[b]))
         assert t == O.sample(x[b], 0.8, 0.95, 40, float(u[b]), O.EXP_CR)
+
+
+def test_prepared_params_and_single_config_match_the_list(sampler):
+    """The three ways of passing the rows' configs (one SamplingConfig, a list,
+    PreparedParams made once and reused) give the same tokens and kept lists,
+    and PreparedParams refuses a batch of another size."""
+    import torch
+    import pesti_sampler as ps
+    B = 16
+    x = synth.make_logits(2, B=B)
+    u = synth.make_u(2, B)
+    d = torch.from_numpy(x).cuda()
+    ud = torch.from_numpy(u).cuda()
+    cfg = ps.SamplingConfig(0.7, 0.9, 50)
+    prep = ps.PreparedParams([cfg] * B)
+    want = [t.cpu().numpy() for t in sampler.sample_batch(d, [cfg] * B, ud, kept_width=KW)]
+    for how in (cfg, prep, prep):  # the prepared params are reused
+        got = [t.cpu().numpy() for t in sampler.sample_batch(d, how, ud, kept_width=KW)]
+        for g, w_ in zip(got, want):
+            assert np.array_equal(g.view(np.uint8), w_.view(np.uint8))
+    with pytest.raises(ValueError):
+        sampler.sample_batch(d[:8], prep, ud[:8])

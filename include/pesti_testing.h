@@ -28,6 +28,13 @@ int64_t pesti_last_gathered_rows(pesti_sampler* s);
  * sort, [4] the chained fold state left a shard's table, [5] the merged
  * candidates could not prove the top-k. */
 int pesti_last_gathered_reasons(pesti_sampler* s, int64_t* counts);
+
+/* The largest relative error of the hardware 2^y approximation
+ * (ex2.approx.ftz.f32) over every float y in [-200, 0] and -inf, against
+ * exp2 in double, on the current device (below y = -126 a flushed 0 counts
+ * as exact): the classification's cheap exp assumes it is below
+ * PESTI_EX2_APPROX_RELERR. */
+int pesti_test_ex2_approx_max_relerr(double* out);
 #ifdef __cplusplus
 }
 #endif

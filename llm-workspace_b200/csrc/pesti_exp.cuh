@@ -123,6 +123,12 @@ PESTI_HD float pesti_expf(float x) {
 // caller treats those elements exactly.
 #define PESTI_EXPF_APPROX_RELERR 0x1p-22f
 
+// Relative error bound of the hardware 2^y approximation (ex2.approx.ftz.f32)
+// for every float y in [-200, 0] (0, flushed, allowed below -126) and -inf (0);
+// tests/test_ex2_bound.py measures it exhaustively against exp2 in double and
+// checks it against this value.
+#define PESTI_EX2_APPROX_RELERR 0x1p-22f
+
 #if defined(__CUDA_ARCH__)
 #define PXF_FMA(a, b, c) __fmaf_rn((a), (b), (c))
 #define PXF_MUL(a, b) __fmul_rn((a), (b))

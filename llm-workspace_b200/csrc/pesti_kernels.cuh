@@ -294,6 +294,20 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// exp(z) for z <= 0 by the hardware 2^y, y = z log2 e with log2 e split in two
+// floats (LH + LL, their sum within 3e-16 of it) and one rounding, so that
+// |y - z log2 e| <= |z| log2 e 2^-24 (1 + 2^-23) and 2^y is within
+// |z| 2^-24 * 1.0001 of exp(z).  Against the correctly rounded f32 exp (within
+// 2^-24 of exp(z)) the relative error is below
+// PESTI_EX2_APPROX_RELERR + (|z| + 1) 2^-24 * 1.001 whenever it is not 0; it is
+// 0 only when exp(z) < 2^-126 (y below -126, where subnormal results flush).
+__device__ __forceinline__ float exp_hw(float z) {
+  return ex2_approx(__fmaf_rn(z, 0x1.715476p+0f, __fmul_rn(z, 0x1.4ae0c0p-26f)));
+}
+// Twice that bound (the margin the decisions below keep), as DE_0 + |z| DE_Z.
+constexpr float DE_Z = 0x1.01p-23f;  // >= 2 * 1.001 * 2^-24
+constexpr float DE_0 = 2.0f * PESTI_EX2_APPROX_RELERR + DE_Z;
+
 // Programmatic dependent launch: a kernel lets the next one in the stream be
 // scheduled early (launch_dependents) and the next one waits for the
 // previous grid's completion and memory (wait) before it touches its inputs.
@@ -1242,9 +1256,10 @@ __device__ __forceinline__ float classify_group(const SliceArgs& a, long long b,
                                             uint32_t* c1s) {
   const int lane = threadIdx.x & 31;
   const int nsub = a.P * K1_WARPS;
-  // e_exact lies within a relative 2*RELERR of the approximation (margin for
-  // the float arithmetic of the bounds below)
-  constexpr float DE = 2.0f * PESTI_EXPF_APPROX_RELERR;
+  // e_exact lies within a relative DE of the approximation (twice its error
+  // bound: margin for the float arithmetic of the bounds below); DE grows with
+  // |z| (see exp_hw) and is set after pass A from the group's largest |z|
+  float DE = 0.0f;
   // Guard band around binade edges (2^-12 for whole rows).  The approximate
   // state tracks the fold within about 1.2e-4 on a row of 128k (its bias is
   // the mass that the fold absorbs, and it grows along the row); a run
@@ -1317,28 +1332,34 @@ __device__ __forceinline__ float classify_group(const SliceArgs& a, long long b,
   }
   const int sh2 = 150 - (int)(clo >> 23);  // w = 2^(E-150) (E = 0: the subnormal grid 2^-149)
   uint32_t ksum = 0u, undecided = 0u;  // undecided: bit jj, element jj of the lane
-  // pass A: approximate exps (sampling.rs:46,127 within 2^-22)
+  // pass A: approximate exps of the reference's arguments z = x/T - m
+  // (sampling.rs:46,127; z exact, exp within DE_0/2 + |z| DE_Z/2)
   float ltot = 0.0f;
+  float zmax = 0.0f;  // the largest |z| of the lane's elements with e > 0
 #pragma unroll 1
   for (int jj = 0; jj < nl; ++jj) {
     const float raw = graw[i0 + jj];
-    const float e = pesti_expf_approx(fsub(scale ? fdiv(raw, T) : raw, m));
+    const float z = fsub(scale ? fdiv(raw, T) : raw, m);
+    const float e = exp_hw(z);
     eas[jj * 32 + lane] = e;
     ltot += e;
+    if (e > 0.0f) zmax = fmaxf(zmax, -z);
     if (possible) {
       bool exact;
       if (e == 0.0f) {
-        exact = (clo >> 23) < 40u;  // else: exact e < 4.5e-38 rounds to 0 on this grid
+        exact = (clo >> 23) < 40u;  // else: exact e < 1.2e-38 rounds to 0 on this grid
       } else {
         const float tt = __uint_as_float(fbits(e) + ((uint32_t)sh2 << 23));  // e/w, exact scaling
         const float kr = rintf(tt);
         const float slack = 0.5f - fabsf(tt - kr);
-        exact = !(slack > tt * DE + 0x1p-24f);
+        exact = !(slack > tt * fmaf(-z, DE_Z, DE_0) + 0x1p-24f);
         if (!exact) ksum += (uint32_t)kr;
       }
       if (exact) undecided |= 1u << jj;
     }
   }
+  // the group's margin (zmax >= 0: its bits order as unsigned integers)
+  DE = fmaf(__uint_as_float(__reduce_max_sync(PESTI_FULL_MASK, __float_as_uint(zmax))), DE_Z, DE_0);
   const float lincl = warp_incl_scan_add(ltot);
   const float gtot = __shfl_sync(PESTI_FULL_MASK, lincl, 31);
   const float lbase = lincl - ltot;

@@ -1246,6 +1246,25 @@ int pesti_sample_batch_sharded_emulated(pesti_sampler* s, int shards, const void
 
 int64_t pesti_last_gathered_rows(pesti_sampler* s) { return s ? s->last_gathered_rows : -1; }
 
+int pesti_test_ex2_approx_max_relerr(double* out) {
+  if (!out) return fail(PESTI_E_INVALID_ARG, "null output");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(PESTI_E_NO_DEVICE, "no CUDA device available");
+  unsigned long long* d = nullptr;
+  PESTI_CUDA_TRY(cudaMalloc(&d, sizeof(unsigned long long)), "cudaMalloc");
+  cudaError_t e = cudaMemset(d, 0, sizeof(unsigned long long));
+  if (e == cudaSuccess) {
+    pesti::ex2_approx_error_kernel<<<1184, 256>>>(d);
+    e = cudaGetLastError();
+  }
+  unsigned long long bits = 0ull;
+  if (e == cudaSuccess) e = cudaMemcpy(&bits, d, sizeof(bits), cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  if (e != cudaSuccess) return cuda_fail(e, "ex2_approx_error_kernel");
+  std::memcpy(out, &bits, sizeof(double));
+  return PESTI_OK;
+}
+
 int pesti_last_gathered_reasons(pesti_sampler* s, int64_t* counts) {
   if (!s || !counts) return fail(PESTI_E_INVALID_ARG, "null argument");
   for (int q = 0; q < pesti::GR_KINDS; ++q) counts[q] = s->last_gathered_why[q];

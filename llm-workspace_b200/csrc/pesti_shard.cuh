@@ -333,3 +333,36 @@ __global__ void gather_row_values_kernel(const int* rows, int n, const float* u,
 }
 
 }  // namespace pesti
+
+namespace pesti {
+
+// Test support: the largest relative error of the hardware 2^y approximation
+// (ex2.approx.ftz.f32) against exp2 in double, over every float y in
+// [-200, 0] and y = -inf, as the bits of a non-negative double (which order
+// as unsigned integers).  Below y = -126 (results under 2^-126) a result of 0
+// is allowed (flushed); any other result counts with its error, and a
+// non-zero result for -inf counts as error 1.  The bound the classification's
+// cheap exp relies on is checked against it.
+__global__ void ex2_approx_error_kernel(unsigned long long* max_bits) {
+  const uint32_t n = 0x43480000u + 1u;  // bit patterns 0x80000000 (-0) .. 0xC3480000 (-200)
+  unsigned long long best = 0ull;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float y = __uint_as_float(0x80000000u + i);
+    const float r = ex2_approx(y);
+    const double ref = exp2((double)y);
+    double rel = fabs((double)r - ref) / ref;
+    if (y < -126.0f && r == 0.0f) rel = 0.0;
+    const unsigned long long b = (unsigned long long)__double_as_longlong(rel);
+    best = b > best ? b : best;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0 && ex2_approx(-__int_as_float(0x7f800000)) != 0.0f)
+    best = (unsigned long long)__double_as_longlong(1.0);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(PESTI_FULL_MASK, best, o);
+    best = t > best ? t : best;
+  }
+  if ((threadIdx.x & 31) == 0) atomicMax(max_bits, best);
+}
+
+}  // namespace pesti

@@ -109,50 +109,8 @@ PESTI_HD float pesti_expf(float x) {
   return f;
 }
 
-// Fast approximate exp in single precision, for the survivor pass: it needs
-// exp only to within a relative error bound, to round e/w to an integer
-// whenever e/w is not close to a rounding boundary (the exact value is
-// computed otherwise).  Cody-Waite reduction k = rint(x/ln2), r = x - k*ln2
-// (ln2 split in a 9-bit head and a tail, so k*head is exact for |k| < 2^15),
-// then the degree-7 Taylor polynomial of exp(r) on |r| <= ln2/2 in Horner form
-// with fma, scaled by 2^k.  Every step is a single IEEE float operation, so the
-// host build computes the same bits; tests/test_exp_exhaustive.py measures the
-// relative error against the correctly rounded f32 exp (the value the folds
-// add) over every float in [-86, 0] and checks it against
-// PESTI_EXPF_APPROX_RELERR.  Returns 0 for x <= -86 (exp(x) < 4.5e-38); the
-// caller treats those elements exactly.
-#define PESTI_EXPF_APPROX_RELERR 0x1p-22f
-
 // Relative error bound of the hardware 2^y approximation (ex2.approx.ftz.f32)
 // for every float y in [-200, 0] (0, flushed, allowed below -126) and -inf (0);
 // tests/test_ex2_bound.py measures it exhaustively against exp2 in double and
 // checks it against this value.
 #define PESTI_EX2_APPROX_RELERR 0x1p-22f
-
-#if defined(__CUDA_ARCH__)
-#define PXF_FMA(a, b, c) __fmaf_rn((a), (b), (c))
-#define PXF_MUL(a, b) __fmul_rn((a), (b))
-#define PXF_RINT(a) rintf(a)
-#else
-#define PXF_FMA(a, b, c) std::fma((float)(a), (float)(b), (float)(c))
-#define PXF_MUL(a, b) ((float)(a) * (float)(b))
-#define PXF_RINT(a) std::nearbyint((float)(a))
-#endif
-
-PESTI_HD float pesti_expf_approx(float x) {
-  if (!(x > -86.0f)) return 0.0f;  // also NaN
-  if (x > 0.0f) x = 0.0f;
-  const float kf = PXF_RINT(PXF_MUL(x, 0x1.715476p+0f));
-  float r = PXF_FMA(-kf, 0x1.63p-1f, x);
-  r = PXF_FMA(-kf, -0x1.bd0106p-13f, r);
-  float p = 0x1.a01a02p-13f;
-  p = PXF_FMA(p, r, 0x1.6c16c2p-10f);
-  p = PXF_FMA(p, r, 0x1.111112p-7f);
-  p = PXF_FMA(p, r, 0x1.555556p-5f);
-  p = PXF_FMA(p, r, 0x1.555556p-3f);
-  p = PXF_FMA(p, r, 0x1p-1f);
-  p = PXF_FMA(p, r, 1.0f);
-  p = PXF_FMA(p, r, 1.0f);
-  const int k = (int)kf;  // -124 <= k <= 0 here
-  return PXF_MUL(p, PX_BITS2F((uint32_t)(k + 127) << 23));
-}

@@ -957,8 +957,8 @@ __global__ void __launch_bounds__(K1_NT) shard_prologue_kernel(SliceArgs a) {
 // relative 2^-10 of it) is SPECIAL: the row kernel adds it with a real f32
 // add.  Maximal runs of the others in one binade become one entry holding the
 // run's integer increments for an even and an odd entry state.  An increment
-// is e/w rounded to an integer; it is taken from an approximation of e with
-// relative error < 2^-20 (pesti_expf_approx) whenever e/w is farther than that
+// is e/w rounded to an integer; it is taken from an approximation of e
+// (exp_hw, with its error bound) whenever e/w is farther than that bound
 // from a rounding boundary, and from the exact exp otherwise.  The row kernel
 // checks every run against the exact state (right binade at entry, still
 // inside it at exit) and replays the run element by element when the check
@@ -1863,11 +1863,12 @@ __global__ void __launch_bounds__(K1_NT, 3) fused_classify_kernel(SliceArgs a) {
       // A clean unit (one pass per survivor): the range of its approximate
       // states lies inside the binade of its start (within the guard band),
       // so every survivor is a plain increment k = rint(e/w) of one run; k
-      // comes from the approximation (sampling.rs:46,127 within 2^-22) where
-      // it decides it and from the exact exp otherwise, and no survivor may be
-      // a tie.  Anything else goes to the general classification.
+      // comes from the approximation (exp_hw of the exact argument,
+      // sampling.rs:46,127, with its error bound as margin) where it decides
+      // it and from the exact exp otherwise (taken once the unit is known to
+      // be clean), and no survivor may be a tie.  Anything else goes to the
+      // general classification.
       {
-        constexpr float DE = 2.0f * PESTI_EXPF_APPROX_RELERR;
         const float BAND = a.band;
         const float sb = (float)s_est;
         const uint32_t clo = fbits(sb) & 0x7f800000u;
@@ -1878,40 +1879,44 @@ __global__ void __launch_bounds__(K1_NT, 3) fused_classify_kernel(SliceArgs a) {
         const int i0 = lane * g;
         const int nl = n - i0 < 0 ? 0 : (n - i0 > g ? g : n - i0);
         float ltot = 0.0f;
-        uint32_t ksum = 0u;
-        bool decided = true;
+        uint32_t ksum = 0u, undecided = 0u;  // undecided: bit jj, element jj of the lane
 #pragma unroll 2
         for (int jj = 0; jj < nl; ++jj) {
           const float raw = graw[i0 + jj];
-          const float xs = scale ? fdiv(raw, T) : raw;  // sampling.rs:46
-          const float ea = pesti_expf_approx(fsub(xs, m));
+          const float z = fsub(scale ? fdiv(raw, T) : raw, m);  // sampling.rs:46,127
+          const float ea = exp_hw(z);
           ltot += ea;
           if (!possible) continue;
-          bool exact = false;
+          bool exact;
           if (ea == 0.0f) {
-            exact = (clo >> 23) < 40u;  // else: exact e < 4.5e-38 rounds to 0 on this grid
+            exact = (clo >> 23) < 40u;  // else: exact e < 1.2e-38 rounds to 0 on this grid
           } else {
             const float tt = __uint_as_float(fbits(ea) + ((uint32_t)sh2 << 23));  // ea/w, exact scaling
             const float kr = rintf(tt);
             const float slack = 0.5f - fabsf(tt - kr);
-            if (slack > tt * DE + 0x1p-24f) ksum += (uint32_t)kr;
-            else exact = true;
+            exact = !(slack > tt * fmaf(-z, DE_Z, DE_0) + 0x1p-24f);
+            if (!exact) ksum += (uint32_t)kr;
           }
-          if (exact) {
-            const float ex = pesti_expf_call(fsub(xs, m));  // sampling.rs:127, exact
+          if (exact) undecided |= 1u << jj;
+        }
+        const float usum = warp_reduce_add(ltot);
+        if (possible && sb + usum <= 2.0f * lov * (1.0f - BAND)) {
+          bool decided = true;
+          for (uint32_t um = undecided; um != 0u; um &= um - 1u) {
+            const int jj = __ffs(um) - 1;
+            const float raw = graw[i0 + jj];
+            const float ex = pesti_expf_call(fsub(scale ? fdiv(raw, T) : raw, m));  // sampling.rs:127, exact
             const uint32_t k0 = fbits(fadd(lov, ex)) - clo;
             const uint32_t k1 = fbits(fadd(bitsf(clo + 1u), ex)) - (clo + 1u);
             decided = decided && k0 == k1;
             ksum += k0;
           }
-        }
-        const float usum = warp_reduce_add(ltot);
-        const bool clean = possible && sb + usum <= 2.0f * lov * (1.0f - BAND);
-        if (clean && __all_sync(PESTI_FULL_MASK, decided)) {
-          const uint32_t inc = tr_sat(__reduce_add_sync(PESTI_FULL_MASK, ksum));  // each < 2^22, at most 256
-          if (lane == 0) *ge = GroupEnt{{clo, inc, inc, gidx[n - 1] + 1u}, 0, 1, 0, 1};
-          s_est += (double)usum;
-          continue;
+          if (__all_sync(PESTI_FULL_MASK, decided)) {
+            const uint32_t inc = tr_sat(__reduce_add_sync(PESTI_FULL_MASK, ksum));  // each < 2^22, at most 256
+            if (lane == 0) *ge = GroupEnt{{clo, inc, inc, gidx[n - 1] + 1u}, 0, 1, 0, 1};
+            s_est += (double)usum;
+            continue;
+          }
         }
       }
       // (its clean case was tried above)

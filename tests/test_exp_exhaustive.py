@@ -29,19 +29,3 @@ def test_exp_correctly_rounded_everywhere():
     assert bad_cr == 0, out
     # glibc 2.39 expf misrounds ~9.7e4 of these inputs (by one ulp)
     assert bad_platform < 200000
-
-
-@pytest.mark.slow
-def test_approximate_exp_error_bound():
-    """The survivor pass rounds exp/ulp from an approximation with a stated
-    relative error bound; the bound must hold on every input it is used for."""
-    src = os.path.join(ROOT, "tests", "expapprox_exhaustive.cpp")
-    inc = os.path.join(ROOT, "llm-workspace_b200", "csrc")
-    with tempfile.TemporaryDirectory() as d:
-        exe = os.path.join(d, "expapprox_exhaustive")
-        subprocess.run(["g++", "-O2", "-std=c++17", "-fno-fast-math", "-ffp-contract=off", "-I", inc,
-                        "-o", exe, src, "-lpthread"], check=True)
-        out = subprocess.run([exe, "-104"], check=True, capture_output=True, text=True).stdout
-    n, worst, over = out.split()
-    assert int(n) == 1120927745
-    assert int(over) == 0, out  # within PESTI_EXPF_APPROX_RELERR (2^-22) of the f32 exp everywhere

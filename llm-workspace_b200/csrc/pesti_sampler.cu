@@ -85,7 +85,9 @@ struct Geometry {
 Geometry pick_geometry(int num_sms, long long B, long long V, int ve) {
   const long long target = 4LL * num_sms;
   long long P = (target + B - 1) / std::max(1LL, B);
-  const long long pmax_v = std::max(1LL, V / (pesti::K1_WARPS * 1024LL));
+  // at most one 1024-element chunk per warp and sub-slice: a short batch of
+  // short rows gets as many warps as its rows have chunks
+  const long long pmax_v = std::max(1LL, (V + pesti::K1_WARPS * 1024LL - 1) / (pesti::K1_WARPS * 1024LL));
   P = std::max(1LL, std::min({P, pmax_v, (long long)(pesti::MAX_SUBS / pesti::K1_WARPS)}));
   // whole 16-byte-vector chunks per sub-slice (32 lanes x 16 bytes x 8 or 4
   // loads in flight = 1024 elements): only the row's last sub-slice has a tail

@@ -183,6 +183,25 @@ int pesti_sample_batch_sharded(pesti_sampler* s, pesti_comm* c, const void* d_lo
                                uint32_t* d_out_tokens, float* d_kept_p, uint32_t* d_kept_idx,
                                int64_t kept_width, int64_t* d_kept_count, void* stream);
 
+/*
+ * No counterpart in the reference, whose draw comes from StdRng on the host
+ * (sampling.rs:98) once per sample() call.
+ *
+ * Per-row draws on the device, for a decode loop that keeps its generators
+ * on the GPU: no draw crosses from the host each step, and the draws feed
+ * d_u of the batch calls directly.  Each row has its own PCG32 generator
+ * (O'Neill 2014, XSH-RR 64->32) in d_state: [B][2] u64, state then
+ * increment, owned by the caller.
+ *  - pesti_pcg32_seed: row b's generator is the one seeded with `seed` on
+ *    stream first_stream + b;
+ *  - pesti_pcg32_draw: d_u[b] = (next_u32 >> 8) * 2^-24 (the [0, 1) 24-bit
+ *    grid of the reference's f32 draw), and row b's generator advances.
+ * Both are stream-ordered (NULL: the legacy default stream) and allocate
+ * nothing.
+ */
+int pesti_pcg32_seed(uint64_t* d_state, int64_t B, uint64_t seed, uint64_t first_stream, void* stream);
+int pesti_pcg32_draw(uint64_t* d_state, int64_t B, float* d_u, void* stream);
+
 /* Message of the last failure on the calling thread ("" if none). */
 const char* pesti_last_error(void);
 

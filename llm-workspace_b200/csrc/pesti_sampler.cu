@@ -20,6 +20,7 @@
 #include "pesti_kernels.cuh"
 #include "pesti_noalloc.h"
 #include "pesti_shard.cuh"
+#include "pesti_rng.cuh"
 
 namespace {
 
@@ -1247,6 +1248,30 @@ int pesti_sample_batch_sharded_emulated(pesti_sampler* s, int shards, const void
 }
 
 int64_t pesti_last_gathered_rows(pesti_sampler* s) { return s ? s->last_gathered_rows : -1; }
+
+int pesti_pcg32_seed(uint64_t* d_state, int64_t B, uint64_t seed, uint64_t first_stream, void* stream) {
+  if (B < 0) return fail(PESTI_E_INVALID_ARG, "B < 0");
+  if (B == 0) return PESTI_OK;
+  if (!d_state) return fail(PESTI_E_INVALID_ARG, "null state");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(PESTI_E_NO_DEVICE, "no CUDA device available");
+  const long long blocks = (B + 255) / 256;
+  pesti::pcg32_seed_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(d_state, B, seed, first_stream);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PESTI_OK : cuda_fail(e, "pcg32_seed_kernel launch");
+}
+
+int pesti_pcg32_draw(uint64_t* d_state, int64_t B, float* d_u, void* stream) {
+  if (B < 0) return fail(PESTI_E_INVALID_ARG, "B < 0");
+  if (B == 0) return PESTI_OK;
+  if (!d_state || !d_u) return fail(PESTI_E_INVALID_ARG, "null state or draws");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(PESTI_E_NO_DEVICE, "no CUDA device available");
+  const long long blocks = (B + 255) / 256;
+  pesti::pcg32_draw_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(d_state, B, d_u);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PESTI_OK : cuda_fail(e, "pcg32_draw_kernel launch");
+}
 
 int pesti_test_ex2_approx_max_relerr(double* out) {
   if (!out) return fail(PESTI_E_INVALID_ARG, "null output");

@@ -117,6 +117,10 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.pesti_sample_batch_sharded_emulated.argtypes = [vp, c_int, vp, c_int, i64, i64, i64, ctypes.POINTER(_Params),
                                                         c_int, c_int, vp, vp, vp, vp, i64, vp, vp]
     lib.pesti_sample_batch_sharded_emulated.restype = c_int
+    lib.pesti_pcg32_seed.argtypes = [vp, i64, ctypes.c_uint64, ctypes.c_uint64, vp]
+    lib.pesti_pcg32_seed.restype = c_int
+    lib.pesti_pcg32_draw.argtypes = [vp, i64, vp, vp]
+    lib.pesti_pcg32_draw.restype = c_int
     lib.pesti_last_gathered_rows.argtypes = [vp]
     lib.pesti_last_gathered_rows.restype = i64
     lib.pesti_last_gathered_reasons.argtypes = [vp, vp]
@@ -187,6 +191,30 @@ class Pcg32:
     def draws(self, n: int):
         import numpy as np
         return np.array([self.next_f32() for _ in range(n)], dtype=np.float32)
+
+
+class DeviceRng:
+    """Per-row PCG32 generators on the device (pesti_pcg32_seed /
+    pesti_pcg32_draw): row b's draws are those of Pcg32(seed, first_stream + b)
+    in sequence, produced where the batch calls read them, with no host copy."""
+
+    def __init__(self, B: int, seed: int, first_stream: int = 0, device: int = 0, stream=None):
+        import torch
+        self._lib = load_library()
+        self.B = int(B)
+        self.state = torch.empty((self.B, 2), dtype=torch.int64, device=f"cuda:{device}")
+        st = stream if stream is not None else torch.cuda.current_stream(self.state.device).cuda_stream
+        _check(self._lib.pesti_pcg32_seed(self.state.data_ptr(), self.B, int(seed) & ((1 << 64) - 1),
+                                          int(first_stream) & ((1 << 64) - 1), st))
+
+    def draw(self, out=None, stream=None):
+        """The next draw of every row: a [B] float32 CUDA tensor."""
+        import torch
+        if out is None:
+            out = torch.empty(self.B, dtype=torch.float32, device=self.state.device)
+        st = stream if stream is not None else torch.cuda.current_stream(self.state.device).cuda_stream
+        _check(self._lib.pesti_pcg32_draw(self.state.data_ptr(), self.B, out.data_ptr(), st))
+        return out
 
 
 class Sampler:

@@ -55,3 +55,6 @@ def test_invalid_arguments_are_rejected_without_a_device():
     assert lib.pesti_sample_batch(None, None, 0, 1, 1, 1, None, 0, 0, None, None, None, None, 0, None, None) \
         == pesti_sampler.PESTI_E_INVALID_ARG
     assert lib.pesti_argmax_batch(None, None, 0, 1, 1, 1, 0, None, None) == pesti_sampler.PESTI_E_INVALID_ARG
+    # the device draws: a negative row count and a null state are refused before any device work
+    assert lib.pesti_pcg32_seed(None, -1, 1, 0, None) == pesti_sampler.PESTI_E_INVALID_ARG
+    assert lib.pesti_pcg32_draw(None, 4, None, None) == pesti_sampler.PESTI_E_INVALID_ARG

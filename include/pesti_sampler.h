@@ -44,7 +44,10 @@ extern "C" {
 #define PESTI_E_UNSUPPORTED (-5)
 #define PESTI_E_NO_DEVICE (-6)
 
-typedef enum { PESTI_F32 = 0, PESTI_BF16 = 1 } pesti_dtype;
+/* Logit element types.  BF16 and F16 logits are widened to f32 exactly, so
+ * results are those of the reference on the widened values (a caller of the
+ * reference's &[f32] API would widen them the same way). */
+typedef enum { PESTI_F32 = 0, PESTI_BF16 = 1, PESTI_F16 = 2 } pesti_dtype;
 
 /* Per-row sampling parameters: SamplingConfig (sampling.rs:12-21) without the
  * seed, which sample() never reads. */
@@ -74,7 +77,7 @@ void pesti_sampler_destroy(pesti_sampler* s);
 
 /*
  * Batched sample over row-major logits [B, ld] (first V columns of each row),
- * dtype F32 or BF16, on device memory.  Replaces, per row, the call
+ * dtype F32, BF16 or F16, on device memory.  Replaces, per row, the call
  *   generate():  if T == 0 { argmax(row) } else { sample(row, cfg, rng) }
  * (model.rs:517-521) when params carry PESTI_FLAG_GREEDY_IF_ZERO_T, and
  * sample(row, cfg, rng) (sampling.rs:39) otherwise.

@@ -20,6 +20,7 @@
 #pragma once
 #include <stdint.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include "pesti_common.cuh"
 #include "pesti_exp.cuh"
 #include "pesti_fold.cuh"
@@ -262,7 +263,11 @@ __device__ __forceinline__ bool sum_pruning_ok(const pesti_sampling_params& p) {
   return p.top_k >= 1u || !(p.top_p > 0.0f);
 }
 
+// Logit element types of the kernels: float (PESTI_F32), uint16_t (the bits
+// of a bf16, PESTI_BF16) and __half (PESTI_F16).  Every one widens to f32
+// exactly, which is what the reference's &[f32] would hold.
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t h) { return __uint_as_float(((uint32_t)h) << 16); }
+__device__ __forceinline__ float f16_bits_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
 template <typename TIn>
 __device__ __forceinline__ float load_logit(const TIn* row, long long j);
@@ -272,9 +277,31 @@ template <>
 __device__ __forceinline__ float load_logit<uint16_t>(const uint16_t* row, long long j) {
   return bf16_bits_to_f32(__ldg(row + j));
 }
+template <>
+__device__ __forceinline__ float load_logit<__half>(const __half* row, long long j) {
+  return f16_bits_to_f32(__ldg(reinterpret_cast<const unsigned short*>(row) + j));
+}
 __device__ __forceinline__ float load_logit_dyn(const void* row, int dtype, long long j) {
-  return dtype == PESTI_BF16 ? load_logit<uint16_t>((const uint16_t*)row, j)
-                             : load_logit<float>((const float*)row, j);
+  return dtype == PESTI_BF16  ? load_logit<uint16_t>((const uint16_t*)row, j)
+         : dtype == PESTI_F16 ? load_logit<__half>((const __half*)row, j)
+                              : load_logit<float>((const float*)row, j);
+}
+// The two 16-bit logits of a 32-bit word (the lower address first), widened.
+template <typename TIn>
+__device__ __forceinline__ void unpack2(uint32_t w, float& lo, float& hi);
+template <>
+__device__ __forceinline__ void unpack2<uint16_t>(uint32_t w, float& lo, float& hi) {
+  lo = __uint_as_float(w << 16);
+  hi = __uint_as_float(w & 0xffff0000u);
+}
+template <>
+__device__ __forceinline__ void unpack2<__half>(uint32_t w, float& lo, float& hi) {
+  lo = f16_bits_to_f32((uint16_t)(w & 0xffffu));
+  hi = f16_bits_to_f32((uint16_t)(w >> 16));
+}
+template <>
+__device__ __forceinline__ void unpack2<float>(uint32_t, float& lo, float& hi) {  // never called
+  lo = hi = 0.0f;
 }
 
 // Order-preserving u32 key of a float (for selection over signed values).
@@ -395,10 +422,7 @@ __device__ __forceinline__ void stream_subslice(const TIn* row, long long start,
           const uint32_t wds[4] = {__float_as_uint(raw[uu].x), __float_as_uint(raw[uu].y),
                                    __float_as_uint(raw[uu].z), __float_as_uint(raw[uu].w)};
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            x[2 * q] = __uint_as_float(wds[q] << 16);
-            x[2 * q + 1] = __uint_as_float(wds[q] & 0xffff0000u);
-          }
+          for (int q = 0; q < 4; ++q) unpack2<TIn>(wds[q], x[2 * q], x[2 * q + 1]);
         }
         f(x, pos + (long long)uu * 32 * VE + (long long)lane * VE, VE);
       }
@@ -1105,10 +1129,7 @@ __global__ void __launch_bounds__(K1_NT, 4) survivor_kernel(SliceArgs a) {
           const uint32_t wds[4] = {__float_as_uint(r4.x), __float_as_uint(r4.y), __float_as_uint(r4.z),
                                    __float_as_uint(r4.w)};
 #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            x[q][2 * h] = __uint_as_float(wds[h] << 16);
-            x[q][2 * h + 1] = __uint_as_float(wds[h] & 0xffff0000u);
-          }
+          for (int h = 0; h < 4; ++h) unpack2<TIn>(wds[h], x[q][2 * h], x[q][2 * h + 1]);
         }
         nv[q] = VE;
       }
@@ -1763,10 +1784,7 @@ __global__ void __launch_bounds__(K1_NT, 3) fused_classify_kernel(SliceArgs a) {
             const uint32_t wds[4] = {__float_as_uint(r4.x), __float_as_uint(r4.y), __float_as_uint(r4.z),
                                      __float_as_uint(r4.w)};
 #pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              x[q][2 * h] = __uint_as_float(wds[h] << 16);
-              x[q][2 * h + 1] = __uint_as_float(wds[h] & 0xffff0000u);
-            }
+            for (int h = 0; h < 4; ++h) unpack2<TIn>(wds[h], x[q][2 * h], x[q][2 * h + 1]);
           }
           nv[q] = VE;
         }
@@ -2344,7 +2362,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
   const RowInfo ri = a.info[b];
   const float T = prm.temperature;
   const int nsub = a.P * K1_WARPS;
-  const void* row = a.dtype == PESTI_BF16 ? (const void*)((const uint16_t*)a.logits + b * a.ld)
+  const void* row = a.dtype != PESTI_F32 ? (const void*)((const uint16_t*)a.logits + b * a.ld)
                                           : (const void*)((const float*)a.logits + b * a.ld);
   float* E = a.E + b * V;
   uint32_t* I = a.I + b * V;
@@ -2609,7 +2627,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
         if (fi < 0) break;
         const uint32_t from = fi > 0 ? fent[fi - 1].end : 0u;
         const uint32_t to = fent[fi].end;
-        const void* src = a.dtype == PESTI_BF16 ? (const void*)((const uint16_t*)row + from)
+        const void* src = a.dtype != PESTI_F32 ? (const void*)((const uint16_t*)row + from)
                                                 : (const void*)((const float*)row + from);
         s = warp_fold(src, a.dtype, (long long)to - from, s, fs.stage, scale, T, m);
         i = fi + 1;

@@ -176,6 +176,10 @@ int ensure_row_smem_limit(int device) {
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, fused), "cudaFuncSetAttribute(fused)");
   PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::fused_classify_kernel<uint16_t, 8, false>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, fused), "cudaFuncSetAttribute(fused)");
+  PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::fused_classify_kernel<__half, 8, true>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, fused), "cudaFuncSetAttribute(fused)");
+  PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::fused_classify_kernel<__half, 8, false>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, fused), "cudaFuncSetAttribute(fused)");
   if (cached) g_row_limit_set[device].store(true, std::memory_order_release);
   return PESTI_OK;
 }
@@ -215,7 +219,7 @@ struct Plan {
 };
 
 Plan make_plan(int num_sms, pesti_dtype dtype, long long B, long long V, bool sorted_bufs) {
-  const int esize = dtype == PESTI_BF16 ? 2 : 4;
+  const int esize = dtype == PESTI_F32 ? 4 : 2;
   const int ve = 16 / esize;
   Plan p;
   p.g = pick_geometry(num_sms, B, V > 0 ? V : 1, ve);
@@ -316,7 +320,7 @@ pesti::SliceArgs make_slice_args(const Plan& p, char* ws, const void* d_logits, 
 }
 
 bool rows_aligned(const void* d_logits, pesti_dtype dtype, long long ld) {
-  const int esize = dtype == PESTI_BF16 ? 2 : 4;
+  const int esize = dtype == PESTI_F32 ? 4 : 2;
   return ((uintptr_t)d_logits % 16 == 0) && ((ld * esize) % 16 == 0);
 }
 
@@ -325,7 +329,10 @@ bool rows_aligned(const void* d_logits, pesti_dtype dtype, long long ld) {
 int launch_slice_stats(const Plan& p, const pesti::SliceArgs& sa, cudaStream_t st) {
   const bool aligned = rows_aligned(sa.logits, (pesti_dtype)sa.dtype, sa.ld);
   const dim3 g1((unsigned)(p.g.P * sa.B));
-  if (sa.dtype == PESTI_BF16) {
+  if (sa.dtype == PESTI_F16) {
+    if (aligned) pesti::slice_stats_kernel<__half, 8, 4, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
+    else pesti::slice_stats_kernel<__half, 8, 4, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
+  } else if (sa.dtype == PESTI_BF16) {
     if (aligned) pesti::slice_stats_kernel<uint16_t, 8, 4, true><<<g1, pesti::K1_NT, 0, st>>>(sa);
     else pesti::slice_stats_kernel<uint16_t, 8, 4, false><<<g1, pesti::K1_NT, 0, st>>>(sa);
   } else {
@@ -348,7 +355,10 @@ int launch_survivors(const Plan& p, const pesti::SliceArgs& sa, int device, cuda
   if (!sa.fused || p.survivors || !sa.fast_enabled) {
     // the survivor pass reads from L2: fewer loads in flight, smaller code
     const dim3 g1((unsigned)(p.g.P * sa.B));
-    if (sa.dtype == PESTI_BF16) {
+    if (sa.dtype == PESTI_F16) {
+      if (aligned) e = launch_dependent(pesti::survivor_kernel<__half, 8, true>, g1, b1, 0, st, sa);
+      else e = launch_dependent(pesti::survivor_kernel<__half, 8, false>, g1, b1, 0, st, sa);
+    } else if (sa.dtype == PESTI_BF16) {
       if (aligned) e = launch_dependent(pesti::survivor_kernel<uint16_t, 8, true>, g1, b1, 0, st, sa);
       else e = launch_dependent(pesti::survivor_kernel<uint16_t, 8, false>, g1, b1, 0, st, sa);
     } else {
@@ -374,8 +384,10 @@ int launch_survivors(const Plan& p, const pesti::SliceArgs& sa, int device, cuda
   // fit on the device at once
   const size_t smem = sizeof(pesti::FusedShared);
   void (*kern)(pesti::SliceArgs) =
-      sa.dtype == PESTI_BF16 ? (aligned ? pesti::fused_classify_kernel<uint16_t, 8, true>
-                                        : pesti::fused_classify_kernel<uint16_t, 8, false>)
+      sa.dtype == PESTI_F16    ? (aligned ? pesti::fused_classify_kernel<__half, 8, true>
+                                          : pesti::fused_classify_kernel<__half, 8, false>)
+      : sa.dtype == PESTI_BF16 ? (aligned ? pesti::fused_classify_kernel<uint16_t, 8, true>
+                                          : pesti::fused_classify_kernel<uint16_t, 8, false>)
                              : (aligned ? pesti::fused_classify_kernel<float, 4, true>
                                         : pesti::fused_classify_kernel<float, 4, false>);
   int per_sm = 0;
@@ -698,7 +710,8 @@ int shard_phase2(const ShardPlan& sp, char* ws, int li, int r, int device, const
   sa.shard_G = sp.G;
   sa.shard_rank = r;
   sa.fused = 1;
-  if (c.dtype == PESTI_BF16) pesti::shard_prologue_kernel<uint16_t, 8><<<(unsigned)c.B, pesti::K1_NT, 0, c.st>>>(sa);
+  if (c.dtype == PESTI_F16) pesti::shard_prologue_kernel<__half, 8><<<(unsigned)c.B, pesti::K1_NT, 0, c.st>>>(sa);
+  else if (c.dtype == PESTI_BF16) pesti::shard_prologue_kernel<uint16_t, 8><<<(unsigned)c.B, pesti::K1_NT, 0, c.st>>>(sa);
   else pesti::shard_prologue_kernel<float, 4><<<(unsigned)c.B, pesti::K1_NT, 0, c.st>>>(sa);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "shard_prologue_kernel launch");
@@ -800,7 +813,7 @@ int shard_gathered(pesti_sampler* s, pesti_comm* comm, const ShardPlan& sp, cons
                    const void* local_logits, const void* whole_logits, const std::vector<int>& rows) {
   const long long nf = (long long)rows.size();
   if (nf == 0) return PESTI_OK;
-  const int esize = c.dtype == PESTI_BF16 ? 2 : 4;
+  const int esize = c.dtype == PESTI_F32 ? 4 : 2;
   const long long VT = sp.VT;
   const long long W = (c.d_kept_p || c.d_kept_idx) ? c.kept_width : 0;
   const Plan pf = make_plan(s->num_sms, c.dtype, nf, VT, true);
@@ -908,7 +921,7 @@ int sample_sharded(pesti_sampler* s, pesti_comm* comm, int G, const void* d_logi
   int rc = stage_params(s, params, params_per_row, params_on_device, B, Vs * G, st, c.uni, c.d_per_row, sorted_bufs,
                         survivors);
   if (rc) return rc;
-  const int esize = dtype == PESTI_BF16 ? 2 : 4;
+  const int esize = dtype == PESTI_F32 ? 4 : 2;
   const int nlocal = comm ? 1 : G;
   const int ksh = shard_list_size(params, params_per_row, params_on_device, B, Vs * G, G);
   const ShardPlan sp = make_shard_plan(s->num_sms, dtype, B, Vs, G, nlocal, ksh);
@@ -973,7 +986,7 @@ int sample_sharded(pesti_sampler* s, pesti_comm* comm, int G, const void* d_logi
 }
 
 int check_shapes(const void* d_logits, pesti_dtype dtype, int64_t B, int64_t V, int64_t ld) {
-  if (dtype != PESTI_F32 && dtype != PESTI_BF16) return fail(PESTI_E_INVALID_ARG, "unsupported dtype");
+  if (dtype != PESTI_F32 && dtype != PESTI_BF16 && dtype != PESTI_F16) return fail(PESTI_E_INVALID_ARG, "unsupported dtype");
   if (B < 0 || V < 0) return fail(PESTI_E_INVALID_ARG, "negative B or V");
   if (V > 0x7fffffffLL) return fail(PESTI_E_INVALID_ARG, "V exceeds 2^31-1");
   if (B > 0x7fffffffLL) return fail(PESTI_E_INVALID_ARG, "B exceeds 2^31-1");

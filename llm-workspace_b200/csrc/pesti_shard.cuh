@@ -95,7 +95,7 @@ __global__ void __launch_bounds__(32) shard_table_kernel(TabArgs a) {
   const float T = prm.temperature;
   const bool scale = T > 0.0f;
   const float m = a.info[b].m;
-  const void* row = a.dtype == PESTI_BF16 ? (const void*)((const uint16_t*)a.logits + b * a.ld)
+  const void* row = a.dtype != PESTI_F32 ? (const void*)((const uint16_t*)a.logits + b * a.ld)
                                           : (const void*)((const float*)a.logits + b * a.ld);
   const uint32_t eb = fbits(__double2float_rn(est));
   const uint32_t base = eb >= (uint32_t)TAB_BELOW ? eb - (uint32_t)TAB_BELOW : 0u;
@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(32) shard_table_kernel(TabArgs a) {
     uint32_t bad = __ballot_sync(PESTI_FULL_MASK, !fits);
     if (bad) {
       const uint32_t from = i > 0 ? ent[i - 1].end : 0u;
-      const void* src = a.dtype == PESTI_BF16 ? (const void*)((const uint16_t*)row + from)
+      const void* src = a.dtype != PESTI_F32 ? (const void*)((const uint16_t*)row + from)
                                               : (const void*)((const float*)row + from);
       while (bad) {
         const int l = __ffs(bad) - 1;

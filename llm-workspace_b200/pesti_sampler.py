@@ -40,6 +40,7 @@ PESTI_E_NO_DEVICE = -6
 
 PESTI_F32 = 0
 PESTI_BF16 = 1
+PESTI_F16 = 2
 
 FLAG_GREEDY_IF_ZERO_T = 1
 FLAG_ARGMAX_FIRST = 2
@@ -306,7 +307,7 @@ class Sampler:
         pesti_sampling_params records)."""
         import torch
         B, V = logits.shape
-        dtype = PESTI_BF16 if logits.dtype == torch.bfloat16 else PESTI_F32
+        dtype = _dtype_of(logits)
         st = stream if stream is not None else torch.cuda.current_stream(logits.device).cuda_stream
         _check(self._lib.pesti_sample_batch(
             self._h, logits.data_ptr(), dtype, B, V, logits.stride(0),
@@ -318,7 +319,7 @@ class Sampler:
         """sampling.rs:115-122 over each row (last of equal maxima unless first)."""
         import torch
         B, V = logits.shape
-        dtype = PESTI_BF16 if logits.dtype == torch.bfloat16 else PESTI_F32
+        dtype = _dtype_of(logits)
         if out is None:
             out = torch.empty(B, dtype=torch.int32, device=logits.device)
         st = stream if stream is not None else torch.cuda.current_stream(logits.device).cuda_stream
@@ -365,15 +366,22 @@ def _ptr(t):
     return t.data_ptr() if t is not None else None
 
 
+def _dtype_of(logits) -> int:
+    """pesti_dtype of a logits tensor (float32, bfloat16 or float16)."""
+    import torch
+    dtype = {torch.float32: PESTI_F32, torch.bfloat16: PESTI_BF16, torch.float16: PESTI_F16}.get(logits.dtype)
+    if dtype is None:
+        raise ValueError("logits must be float32, bfloat16 or float16")
+    return dtype
+
+
 def _batch_args(logits, configs, out, greedy_if_zero_t, argmax_first, kept_width, stream):
     """Shape, dtype, parameter array and output tensors of a batch call."""
     import torch
     if logits.dim() != 2:
         raise ValueError("logits must be [B, V]")
     B, V = logits.shape
-    dtype = {torch.float32: PESTI_F32, torch.bfloat16: PESTI_BF16}.get(logits.dtype)
-    if dtype is None:
-        raise ValueError("logits must be float32 or bfloat16")
+    dtype = _dtype_of(logits)
     if logits.stride(1) != 1:
         raise ValueError("logits rows must be contiguous")
     if isinstance(configs, SamplingConfig):
@@ -461,9 +469,7 @@ def sample_batch_noalloc(logits, configs: Union[SamplingConfig, Sequence[Samplin
     import torch
     lib = load_library()
     B, V = logits.shape
-    dtype = {torch.float32: PESTI_F32, torch.bfloat16: PESTI_BF16}.get(logits.dtype)
-    if dtype is None:
-        raise ValueError("logits must be float32 or bfloat16")
+    dtype = _dtype_of(logits)
     if logits.stride(1) != 1:
         raise ValueError("logits rows must be contiguous")
     if isinstance(configs, SamplingConfig):

@@ -220,3 +220,54 @@ def test_device_draws_equal_the_host_generator(sampler):
     a = sampler.sample_batch(d, cfg, ud).cpu().numpy()
     b_ = sampler.sample_batch(d, cfg, torch.from_numpy(hu).cuda()).cpu().numpy()
     assert np.array_equal(a, b_)
+
+
+def _run_f16(sampler, x16, params, u, ld=None, kept_width=KW):
+    import torch
+    import pesti_sampler as ps
+    B, V = x16.shape
+    host = torch.from_numpy(np.ascontiguousarray(x16))
+    if ld is not None and ld != V:
+        big = torch.zeros((B, ld), dtype=torch.float16)
+        big[:, :V] = host
+        dev = big.cuda()[:, :V]
+    else:
+        dev = host.cuda()
+    cfgs = [ps.SamplingConfig(temperature=t, top_p=p, top_k=k) for (t, p, k) in params]
+    ud = torch.from_numpy(np.ascontiguousarray(u, dtype=np.float32)).cuda()
+    tok, kp, ki, kc = sampler.sample_batch(dev, cfgs, ud, kept_width=kept_width)
+    torch.cuda.synchronize()
+    return (tok.cpu().numpy().view(np.uint32), kp.cpu().numpy(), ki.cpu().numpy().view(np.uint32),
+            kc.cpu().numpy())
+
+
+@pytest.mark.parametrize("w,B,ld_extra", [(2, 16, 0), (2, 8, 1), (3, 4, 0), (4, 60, 0), (5, 8, 0)])
+def test_f16_logits(sampler, w, B, ld_extra):
+    """f16 logits: the results of the oracle on the same values widened to f32
+    (what a caller of the reference's &[f32] API would pass), bit for bit;
+    the rounding to f16 also makes many ties.  ld_extra 1 takes the unaligned
+    (scalar-load) paths."""
+    spec = synth.WORKLOADS[w]
+    V = spec["V"]
+    x16 = synth.make_logits(w, B=B).astype(np.float16)
+    x = x16.astype(np.float32)
+    params = synth.params_for(w, B, V)
+    u = synth.make_u(w, B)
+    got = _run_f16(sampler, x16, params, u, ld=V + ld_extra if ld_extra else None)
+    check_exact(x, params, u, got, f"f16 workload{w}")
+
+
+def test_f16_emulated_shards_match_whole_rows(sampler):
+    """Vocabulary shards of f16 logits (one GPU emulating 4 shards) give the
+    whole-row results bit for bit."""
+    import torch
+    import pesti_sampler as ps
+    B = 16
+    x16 = synth.make_logits(5, B=B).astype(np.float16)
+    d = torch.from_numpy(x16).cuda()
+    u = torch.from_numpy(synth.make_u(5, B)).cuda()
+    cfg = ps.SamplingConfig(0.9, 0.92, 64)
+    whole = [t.cpu().numpy() for t in sampler.sample_batch(d, cfg, u, kept_width=KW)]
+    got = [t.cpu().numpy() for t in sampler.sample_batch_sharded_emulated(d, cfg, u, 4, kept_width=KW)]
+    for g, w_ in zip(got, whole):
+        assert np.array_equal(g.view(np.uint8), w_.view(np.uint8))

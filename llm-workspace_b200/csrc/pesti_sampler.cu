@@ -298,9 +298,13 @@ pesti::SliceArgs make_slice_args(const Plan& p, char* ws, const void* d_logits, 
   sa.task_count = (int*)(ws + p.o_tctr);
   sa.task_next = sa.task_count + 1;
   sa.task_count_h = sa.task_count + 2;
-  // rows past 128k columns (and vocabulary shards, set by their caller) take
-  // the fused pass; shorter ones the survivor pass and the task queue
-  sa.fused = V > 131072 ? 1 : 0;
+  // the fused pass (vocabulary shards: set by their caller) or the survivor
+  // pass and the task queue, as measured on B200: the fused pass is faster on
+  // rows beyond 128k columns and on short rows (at most 64k) when every row is
+  // on the top-k fast path (it needs no survivor pass then): 3.07 M against
+  // 2.20 M rows/s on 1000 rows of 32000; the task queue on rows of 128k
+  // (913 k against 798 k rows/s, 64 rows) and on mixed batches
+  sa.fused = (V > 131072 || (V <= 65536 && !p.survivors)) ? 1 : 0;
   sa.gsurv = (pesti::GroupEnt*)(ws + p.o_gsurv);
   sa.pool = (pesti::FoldEnt*)(ws + p.o_pool);
   sa.pool_ctr = (int*)(ws + p.o_pctr);
@@ -449,7 +453,7 @@ pesti::RowArgs make_row_args(const Plan& p, char* ws, const pesti::SliceArgs& sa
   ra.V_total = sa.V_total;
   // fold entries the row kernel stages per row: rows up to 128k columns make
   // a few hundred (about one per 256 survivors, plus the single elements)
-  ra.fast_ents = sa.V_total > 131072 ? pesti::FAST_ENTS : pesti::FAST_ENTS_SHORT;
+  ra.fast_ents = sa.V_total > 131072 || sa.fused ? pesti::FAST_ENTS : pesti::FAST_ENTS_SHORT;
   return ra;
 }
 

@@ -68,11 +68,12 @@ L2_BYTES = 126 * 1024 * 1024
 
 def kernels_per_step(V, params):
     """This library's launches in one step: the HBM pass; the fused pass (rows
-    beyond 128k columns, or of at most 64k when every row is on the top-k fast
-    path), plus the survivor pass when some row is off that path, else the
-    survivor pass and the task-queue classification; the row kernel."""
+    beyond 128k columns, or of at most 64k in batches of 32 rows or more when
+    every row is on the top-k fast path), plus the survivor pass when some row
+    is off that path, else the survivor pass and the task-queue
+    classification; the row kernel."""
     off_fast = any(not (1 <= k <= 256) or t <= 0 for (t, _, k) in params)
-    fused = V > 131072 or (V <= 65536 and not off_fast)
+    fused = V > 131072 or (V <= 65536 and not off_fast and len(params) >= 32)
     if not fused:
         return 4
     return 4 if off_fast else 3

@@ -301,10 +301,11 @@ pesti::SliceArgs make_slice_args(const Plan& p, char* ws, const void* d_logits, 
   // the fused pass (vocabulary shards: set by their caller) or the survivor
   // pass and the task queue, as measured on B200: the fused pass is faster on
   // rows beyond 128k columns and on short rows (at most 64k) when every row is
-  // on the top-k fast path (it needs no survivor pass then): 3.07 M against
-  // 2.20 M rows/s on 1000 rows of 32000; the task queue on rows of 128k
-  // (913 k against 798 k rows/s, 64 rows) and on mixed batches
-  sa.fused = (V > 131072 || (V <= 65536 && !p.survivors)) ? 1 : 0;
+  // on the top-k fast path (it needs no survivor pass then) in batches of 32
+  // rows or more: 3.07 M against 2.20 M rows/s on 1000 rows of 32000; the
+  // task queue on rows of 128k (913 k against 798 k rows/s, 64 rows), on
+  // mixed batches and on single rows (B=1 p50 62.2 against 64.7 us)
+  sa.fused = (V > 131072 || (V <= 65536 && !p.survivors && B >= 32)) ? 1 : 0;
   sa.gsurv = (pesti::GroupEnt*)(ws + p.o_gsurv);
   sa.pool = (pesti::FoldEnt*)(ws + p.o_pool);
   sa.pool_ctr = (int*)(ws + p.o_pctr);

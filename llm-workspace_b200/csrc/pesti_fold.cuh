@@ -392,11 +392,24 @@ __device__ __noinline__ int block_radix_sort(uint32_t* k0, uint32_t* v0, uint32_
     for (int i = tid; i < NW * 256; i += NT) (&sm.hist[0][0])[i] = 0u;
     if (tid == 0) sm.skip = 0;
     __syncthreads();
-    for (long long j0 = beg; j0 < end; j0 += 32) {
-      const long long j = j0 + lane;
-      const uint32_t d = j < end ? ((kin[j] >> shift) & 255u) : 256u + (uint32_t)lane;
-      const uint32_t peers = __match_any_sync(PESTI_FULL_MASK, d);  // one add per digit per warp
-      if (d < 256u && (peers & ((1u << lane) - 1u)) == 0u) sm.hist[w][d] += (uint32_t)__popc(peers);
+    // RB steps of 32 keys at a time: their loads are issued together, then
+    // counted in order (the counters chain through shared memory)
+    constexpr int RB = 8;
+    for (long long j0 = beg; j0 < end; j0 += 32 * RB) {
+      uint32_t kb[RB];
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        const long long j = j0 + r * 32 + lane;
+        kb[r] = j < end ? kin[j] : 0u;
+      }
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        const long long j = j0 + r * 32 + lane;
+        const uint32_t d = j < end ? ((kb[r] >> shift) & 255u) : 256u + (uint32_t)lane;
+        const uint32_t peers = __match_any_sync(PESTI_FULL_MASK, d);  // one add per digit per warp
+        if (d < 256u && (peers & ((1u << lane) - 1u)) == 0u) sm.hist[w][d] += (uint32_t)__popc(peers);
+        __syncwarp();
+      }
     }
     __syncthreads();
     if (tid < 256) {
@@ -426,23 +439,33 @@ __device__ __noinline__ int block_radix_sort(uint32_t* k0, uint32_t* v0, uint32_
       ex += loc[r];
     }
     __syncthreads();
-    for (long long j0 = beg; j0 < end; j0 += 32) {
-      const long long j = j0 + lane;
-      const bool valid = j < end;
-      const uint32_t key = valid ? kin[j] : 0u;
-      const uint32_t val = valid ? vin[j] : 0u;
-      const uint32_t d = valid ? ((key >> shift) & 255u) : 256u + (uint32_t)lane;
-      const uint32_t peers = __match_any_sync(PESTI_FULL_MASK, d);
-      const uint32_t lower = peers & ((1u << lane) - 1u);
-      uint32_t dst = 0;
-      if (valid) dst = sm.hist[w][d] + (uint32_t)__popc(lower);
-      __syncwarp();
-      if (valid) {
-        kout[dst] = key;
-        vout[dst] = val;
-        if (lower == 0u) sm.hist[w][d] += (uint32_t)__popc(peers);
+    for (long long j00 = beg; j00 < end; j00 += 32 * RB) {
+      uint32_t kb[RB], vb[RB];
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        const long long j = j00 + r * 32 + lane;
+        kb[r] = j < end ? kin[j] : 0u;
+        vb[r] = j < end ? vin[j] : 0u;
       }
-      __syncwarp();
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        const long long j = j00 + r * 32 + lane;
+        const bool valid = j < end;
+        const uint32_t key = kb[r];
+        const uint32_t val = vb[r];
+        const uint32_t d = valid ? ((key >> shift) & 255u) : 256u + (uint32_t)lane;
+        const uint32_t peers = __match_any_sync(PESTI_FULL_MASK, d);
+        const uint32_t lower = peers & ((1u << lane) - 1u);
+        uint32_t dst = 0;
+        if (valid) dst = sm.hist[w][d] + (uint32_t)__popc(lower);
+        __syncwarp();
+        if (valid) {
+          kout[dst] = key;
+          vout[dst] = val;
+          if (lower == 0u) sm.hist[w][d] += (uint32_t)__popc(peers);
+        }
+        __syncwarp();
+      }
     }
     __syncthreads();
     cur ^= 1;

@@ -394,7 +394,7 @@ __device__ __noinline__ int block_radix_sort(uint32_t* k0, uint32_t* v0, uint32_
     __syncthreads();
     // RB steps of 32 keys at a time: their loads are issued together, then
     // counted in order (the counters chain through shared memory)
-    constexpr int RB = 8;
+    constexpr int RB = 16;
     for (long long j0 = beg; j0 < end; j0 += 32 * RB) {
       uint32_t kb[RB];
 #pragma unroll

@@ -2757,6 +2757,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
     __syncthreads();
     const long long n = sh.n;
     long long above = 0;  // elements whose exp exceeds that of every dropped one
+    constexpr int REB = 8;  // loads issued per thread before their stores (key and cut loops)
     for (int s = 0; s < nsub; ++s) {
       const SubInfo si = sh.sub[s];
       for (long long jj = tid; jj < si.cnt; jj += K2_NT) {
@@ -2887,15 +2888,39 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
     }
 
     // ---- sorted path: top-p (sampling.rs:65-78) or a large top-k ----
-    for (long long j = tid; j < n; j += K2_NT) {
-      SK0[j] = ~fbits(fdiv(E[j], S));
-      SV0[j] = (uint32_t)j;
+    for (long long j0 = tid; j0 < n; j0 += (long long)K2_NT * REB) {
+      float ev[REB];
+#pragma unroll
+      for (int r = 0; r < REB; ++r) {
+        const long long j = j0 + (long long)r * K2_NT;
+        ev[r] = j < n ? E[j] : 0.0f;
+      }
+#pragma unroll
+      for (int r = 0; r < REB; ++r) {
+        const long long j = j0 + (long long)r * K2_NT;
+        if (j < n) {
+          SK0[j] = ~fbits(fdiv(ev[r], S));
+          SV0[j] = (uint32_t)j;
+        }
+      }
     }
     __syncthreads();
     const int which = sort::block_radix_sort(SK0, SV0, SK1, SV1, n, sh.u.s);
     const uint32_t* SK = which ? SK1 : SK0;
     const uint32_t* SV = which ? SV1 : SV0;
-    for (long long j = tid; j < n; j += K2_NT) Q[j] = bitsf(~SK[j]);
+    for (long long j0 = tid; j0 < n; j0 += (long long)K2_NT * REB) {
+      uint32_t kv[REB];
+#pragma unroll
+      for (int r = 0; r < REB; ++r) {
+        const long long j = j0 + (long long)r * K2_NT;
+        kv[r] = j < n ? SK[j] : 0u;
+      }
+#pragma unroll
+      for (int r = 0; r < REB; ++r) {
+        const long long j = j0 + (long long)r * K2_NT;
+        if (j < n) Q[j] = bitsf(~kv[r]);
+      }
+    }
     __syncthreads();
     long long c;
     long long kept_total;
@@ -2927,7 +2952,19 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
       if (a.kept_idx) a.kept_idx[b * a.kept_width + j] = in ? I[SV[j]] : 0xffffffffu;
     }
     __syncthreads();
-    for (long long j = tid; j < c; j += K2_NT) Q[j] = fdiv(Q[j], total);
+    for (long long j0 = tid; j0 < c; j0 += (long long)K2_NT * REB) {
+      float qv[REB];
+#pragma unroll
+      for (int r = 0; r < REB; ++r) {
+        const long long j = j0 + (long long)r * K2_NT;
+        qv[r] = j < c ? Q[j] : 0.0f;
+      }
+#pragma unroll
+      for (int r = 0; r < REB; ++r) {
+        const long long j = j0 + (long long)r * K2_NT;
+        if (j < c) Q[j] = fdiv(qv[r], total);
+      }
+    }
     __syncthreads();
     const fold::Result dr = fold::block_fold(Q, c, 0u, r_tau, true, sh.u.f);
     if (tid == 0) {

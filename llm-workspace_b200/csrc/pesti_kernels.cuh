@@ -2760,15 +2760,30 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
     constexpr int REB = 8;  // loads issued per thread before their stores (key and cut loops)
     for (int s = 0; s < nsub; ++s) {
       const SubInfo si = sh.sub[s];
-      for (long long jj = tid; jj < si.cnt; jj += K2_NT) {
-        float raw;
-        uint32_t idx;
+      // the next step's load is issued before this step's exp
+      float raw_n = 0.0f;
+      uint32_t idx_n = 0u;
+      if (tid < si.cnt) {
         if (si.dense) {
-          idx = (uint32_t)(si.start + jj);
-          raw = load_logit_dyn(row, a.dtype, si.start + jj);
+          idx_n = (uint32_t)(si.start + tid);
+          raw_n = load_logit_dyn(row, a.dtype, si.start + tid);
         } else {
-          raw = a.surv_raw[b * V + si.start + jj];
-          idx = a.surv_idx[b * V + si.start + jj];
+          raw_n = a.surv_raw[b * V + si.start + tid];
+          idx_n = a.surv_idx[b * V + si.start + tid];
+        }
+      }
+      for (long long jj = tid; jj < si.cnt; jj += K2_NT) {
+        const float raw = raw_n;
+        const uint32_t idx = idx_n;
+        const long long jn = jj + K2_NT;
+        if (jn < si.cnt) {
+          if (si.dense) {
+            idx_n = (uint32_t)(si.start + jn);
+            raw_n = load_logit_dyn(row, a.dtype, si.start + jn);
+          } else {
+            raw_n = a.surv_raw[b * V + si.start + jn];
+            idx_n = a.surv_idx[b * V + si.start + jn];
+          }
         }
         const float x = scale ? fdiv(raw, T) : raw;  // sampling.rs:46
         const float e = pesti_expf(fsub(x, m));      // sampling.rs:127

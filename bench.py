@@ -3,22 +3,29 @@
 Workload (default): the batched Llama-3-vocab case -- logits [64, 128256] f32,
 N(0,1)*3 plus a Zipf(1.1) rank bias, temperature 0.7, top-k 50, top-p 0.9,
 per-row draws from PCG32 seed 1.  A step samples one token for every row of
-one batch already resident in HBM; per GPU the batch is fixed (weak scaling:
-each rank samples its own 64 rows, no collective on the data path).
+one batch already resident in HBM.  Under torchrun (N > 1) the configured
+batch is split into N contiguous row blocks, one per rank, with no collective
+on the data path (strong scaling: the total work is fixed).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload 1..5]
 
 --workload 5 under torchrun (N > 1) runs the vocabulary-sharded path instead:
 the [1024, 256000] f32 batch is split into N contiguous column ranges, one
-per rank (strong scaling: the total work is fixed), and every rank receives
-all 1024 tokens (pesti_sample_batch_sharded; three NCCL all-gathers of
-per-row records, no logits moved).
+per rank (strong scaling), and every rank receives all 1024 tokens
+(pesti_sample_batch_sharded; three NCCL all-gathers of per-row records, no
+logits moved).
 
 Keys beyond the base contract:
-  roofline      the slice-max pass (the HBM pass over the logits; the dominant
-                kernel), achieved = logit bytes per launch / its mean CUDA-event
-                duration, against the measured HBM copy bandwidth
-  step_hbm_gbs  logit bytes / whole step time (both kernels)
+  roofline      the whole step: logit bytes per step / step time against the
+                measured HBM copy bandwidth; `kernels` gives each timed
+                interval's own figure (profiled pass, CUDA events on the
+                launching stream); `traffic` is the step's DRAM bytes from an
+                ncu capture of the same loop (warm L2, see TRAFFIC_PER_STEP)
+  parity        the batch's results against the oracle: rows bit-exact with
+                exp correctly rounded, and against the platform-expf oracle
+                the token mismatch rate outside the 1e-6 boundary band, the
+                largest relative probability error and the share of top-k
+                rows whose index sets are identical
   b1_latency_us p50/p99 wall time of one B=1 row (workload 1 shape, [1,32000]
                 f32, device-resident), launch and sync included
   cpu_baseline  the reference algorithm (C++ restatement of sampling.rs) on the
@@ -65,6 +72,11 @@ def params_text(w: int) -> str:
 UNIT = "rows/s"
 L2_BYTES = 126 * 1024 * 1024
 
+# DRAM bytes (read + write) of one step, summed over its kernels, from ncu
+# captures of this loop with the caches left warm (--cache-control none):
+# the command and per-kernel figures are in profiles/traffic_step_<workload>.md.
+TRAFFIC_PER_STEP = {}
+
 
 def kernels_per_step(V, params):
     """This library's launches in one step: the HBM pass; the fused pass (rows
@@ -77,6 +89,28 @@ def kernels_per_step(V, params):
     if not fused:
         return 4
     return 4 if off_fast else 3
+
+
+def merge_parity(reps):
+    """The parity figures of every rank's rows, as one batch."""
+    reps = [r for r in reps if r]
+    if not reps:
+        return None
+    rows = sum(r["rows"] for r in reps)
+    topk_rows = sum(r["topk_rows"] for r in reps)
+    topk_ok = sum((r["topk_sets_exact"] or 0.0) * r["topk_rows"] for r in reps)
+    outside = sum(r["token_mismatches_outside_band"] for r in reps)
+    return {
+        "rows": rows,
+        "rows_exact_cr_exp": sum(r["rows_exact"] for r in reps),
+        "token_mismatch_rate": outside / max(rows, 1),
+        "token_mismatches": sum(r["token_mismatches"] for r in reps),
+        "rows_near_boundary": sum(r["rows_near_boundary"] for r in reps),
+        "max_prob_rel_err": max(r["max_prob_rel_err"] for r in reps),
+        "topk_sets_exact": (topk_ok / topk_rows) if topk_rows else None,
+        "against": "oracle (C++ restatement of sampling.rs:39-134): bit-exact rows with exp correctly "
+                   "rounded; the other figures against glibc expf, 1e-6 boundary band",
+    }
 
 
 def measured_peaks():
@@ -186,9 +220,12 @@ def run_reference(args):
     line = {
         "metric": metric_for(w), "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": spec["dtype"],
         "data": "synthetic",
-        "config": {"workload": spec["name"], "B": B, "V": V, "rows_per_step": rows_per_step},
+        "config": {"workload": spec["name"], "B": B, "B_per_gpu": B, "V": V, "input_dtype": spec["dtype"],
+                   "params": params_text(w), "l2": "not applicable (host memory)",
+                   "parallelism": f"{nthreads} host threads, rows in parallel; {rows_per_step} of the {B} rows "
+                                  "per step"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "port",
                          "sample": f"{rows_per_step} of the {B} rows per step, {args.steps} steps; "
                                    "C++ restatement of sampling.rs:39-134 with glibc expf (the Rust "
@@ -233,20 +270,29 @@ def run_vocab_sharded(args, rank, world, local, dev):
     def step(i):
         s.sample_batch_sharded(comm, bufs[i % nbuf], cfg, ud, out=out)
 
-    # correctness guard: every rank's tokens against the whole rows sampled on rank 0's GPU
-    step(0)
+    # correctness guard: every rank's tokens against the whole rows sampled on
+    # rank 0's GPU, and rank 0's results (tokens and kept lists of all rows)
+    # against the oracle
+    KW = 64
+    tok, kp, ki, kc = s.sample_batch_sharded(comm, bufs[0], cfg, ud, kept_width=KW)
     torch.cuda.synchronize()
     gathered_first = s.last_gathered_rows()
     gathered_why = s.last_gathered_reasons()
-    mine = out.cpu().numpy().view(np.uint32).copy()
+    mine = tok.cpu().numpy().view(np.uint32).copy()
     check = None
+    parity = None
     if rank == 0:
-        whole = torch.from_numpy(synth.make_logits(w)).to(dev)
+        import oracle as O
+        full = synth.make_logits(w)
+        whole = torch.from_numpy(full).to(dev)
         ref = s.sample_batch(whole, cfg, ud)
         torch.cuda.synchronize()
         check = ref.cpu().numpy().view(np.uint32)
         del whole
         torch.cuda.empty_cache()
+        parity = merge_parity([O.parity_report(full, (T, P, K), u, mine, kp.cpu().numpy(), ki.cpu().numpy(),
+                                               kc.cpu().numpy(), KW)])
+        del full
     all_tok = [None] * world
     dist.all_gather_object(all_tok, mine)
     exact = int(sum(int((t == check).sum()) for t in all_tok)) if rank == 0 else None
@@ -339,7 +385,7 @@ def run_vocab_sharded(args, rank, world, local, dev):
             "gpu_launches": 7 * args.steps,
             "clocks": clk,
             "cpu_baseline": None,
-            "bench_rows_exact": exact, "bench_rows_checked": B * world,
+            "rows_equal_whole_row_sampler": exact, "rows_checked": B * world, "parity": parity,
             "gathered_rows_first_step": gathered_first, "gathered_reasons": gathered_why,
         }
         print(json.dumps(line))
@@ -386,11 +432,14 @@ def main():
 
     w = args.workload
     spec = synth.WORKLOADS[w]
-    B, V = (args.rows or spec["B"]), spec["V"]
+    B_total, V = (args.rows or spec["B"]), spec["V"]
+    if B_total % world:
+        raise SystemExit(f"the batch of {B_total} rows does not split over {world} ranks")
+    B = B_total // world  # this rank's contiguous row block of the configured batch
     rows = rank_rows(rank, world, B)
     x = synth.make_logits(w, rows=rows)
-    params = synth.params_for(w, B, V)
-    u = synth.make_u(w, B)
+    params = synth.params_for(w, B_total, V)[rows.start:rows.stop]
+    u = synth.make_u(w, B_total)[rows.start:rows.stop]
     bf16 = spec["dtype"] == "bf16"
     if bf16:
         host = torch.from_numpy(synth.f32_to_bf16_bits(x).view(np.int16)).view(torch.bfloat16)
@@ -416,14 +465,21 @@ def main():
         if world > 1:
             dist.barrier()
 
-    # correctness guard on the benchmark's own input (exact vs the oracle)
-    check_rows = None
-    if rank == 0 and not args.kernels_only:
+    # correctness guard on the benchmark's own input: every rank's rows
+    # against the oracle (the parity figures of the drop-in contract)
+    parity = None
+    if not args.kernels_only:
         import oracle as O
-        step(0)
+        KW = 64
+        tok, kp, ki, kc = s.sample_batch(bufs[0], cfgs, ud, kept_width=KW)
         torch.cuda.synchronize()
-        want = O.sample_batch(x, params, u, O.EXP_CR)["tokens"]
-        check_rows = int((out.cpu().numpy().view(np.uint32) == want).sum())
+        rep = O.parity_report(x, params, u, tok.cpu().numpy(), kp.cpu().numpy(), ki.cpu().numpy(),
+                              kc.cpu().numpy(), KW)
+        reps = [rep]
+        if world > 1:
+            reps = [None] * world
+            dist.all_gather_object(reps, rep)
+        parity = merge_parity(reps)
 
     for i in range(args.warmup):
         step(i)
@@ -466,7 +522,7 @@ def main():
     barrier()
     elapsed_ms = max_over_ranks(elapsed_ms, dev)
     ms_per_step = elapsed_ms / args.steps
-    value = world * B * args.steps / (elapsed_ms / 1e3)
+    value = B_total * args.steps / (elapsed_ms / 1e3)
 
     # per-kernel device times (profiled pass, separate from the timed loop)
     lib = ps.load_library()
@@ -482,18 +538,15 @@ def main():
     t_max, t_surv, t_row, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_double(), ctypes.c_int()
     lib.pesti_profile_read(s._h, ctypes.byref(t_max), ctypes.byref(t_surv), ctypes.byref(t_row), ctypes.byref(n))
     lib.pesti_profile_enable(s._h, 0)
-    scan_ms = t_max.value / max(1, n.value)
-    surv_ms = t_surv.value / max(1, n.value)
-    row_ms = t_row.value / max(1, n.value)
+    scan_ms = max_over_ranks(t_max.value / max(1, n.value), dev)
+    surv_ms = max_over_ranks(t_surv.value / max(1, n.value), dev)
+    row_ms = max_over_ranks(t_row.value / max(1, n.value), dev)
     peak, peak_kind = measured_peaks()
-    achieved = step_bytes / (scan_ms / 1e3) / 1e9
-    traffic = None
-    tpath = os.path.join(ROOT, "profiles", "slice_stats_traffic.json")
-    if os.path.exists(tpath):
-        try:
-            traffic = json.load(open(tpath)).get(f"workload{w}")
-        except Exception:
-            traffic = None
+    achieved = step_bytes / (ms_per_step / 1e3) / 1e9
+
+    def kern(ms):
+        gbs = step_bytes / (ms / 1e3) / 1e9 if ms > 0 else None
+        return {"us": ms * 1e3, "logit_gbs": gbs, "frac": gbs / peak if gbs else None}
 
     # end to end through the public API with host buffers
     pinned = host.pin_memory()
@@ -522,7 +575,7 @@ def main():
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
     e2e_ms = max_over_ranks(e2e_ms, dev)
-    e2e_value = world * B * e2e_steps / (e2e_ms / 1e3)
+    e2e_value = B_total * e2e_steps / (e2e_ms / 1e3)
 
     # B = 1 latency (workload 1 shape), device-resident logits, host wall clock
     lat = None
@@ -549,26 +602,28 @@ def main():
                          "threads; C++ restatement of sampling.rs:39-134 with glibc expf"}
 
     if rank == 0:
+        nk = kernels_per_step(V, params)
         line = {
             "metric": metric_for(w), "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic",
-            "config": {"workload": spec["name"], "B_per_gpu": B, "V": V, "input_dtype": spec["dtype"],
+            "scaling": "strong", "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic",
+            "config": {"workload": spec["name"], "B": B_total, "B_per_gpu": B, "V": V, "input_dtype": spec["dtype"],
                        "params": params_text(w),
                        "l2": f"rotating {nbuf} input buffers ({nbuf * step_bytes / 2**20:.0f} MiB > 126 MiB L2)",
-                       "parallelism": f"rows split, {world} GPU(s), no collective"},
-            "roofline": {"bound": "hbm", "kernel": "slice_stats_kernel", "achieved": achieved, "peak": peak,
-                         "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": traffic, "bytes_per_launch": step_bytes},
-            "kernel_us": {"slice_stats": scan_ms * 1e3, "survivor+classify": surv_ms * 1e3, "row": row_ms * 1e3},
-            "step_hbm_gbs": step_bytes / (ms_per_step / 1e3) / 1e9,
+                       "parallelism": f"row blocks of {B} rows on each of {world} GPU(s), no collective"},
+            "roofline": {"bound": "hbm", "kernel": f"whole step ({nk} launches)", "achieved": achieved,
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": TRAFFIC_PER_STEP.get(w) if world == 1 else None,
+                         "bytes_per_launch": step_bytes,
+                         "kernels": {"slice_stats": kern(scan_ms), "survivor+classify": kern(surv_ms),
+                                     "row": kern(row_ms)}},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": step_bytes + B * 4,
                     "d2h_bytes_per_step": B * 4},
-            "gpu_launches": kernels_per_step(V, params) * args.steps,
+            "gpu_launches": nk * args.steps,
             "clocks": clk,
             "b1_latency_us": lat,
             "cpu_baseline": cpu,
-            "bench_rows_exact": check_rows,
+            "parity": parity,
         }
         print(json.dumps(line))
     s.close()

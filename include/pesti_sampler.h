@@ -135,9 +135,15 @@ int pesti_sample_row_host(pesti_sampler* s, const float* h_logits, int64_t V,
  *    8 rows of V = 128256 with top-p need about 37 MB;
  *  - calls whose GPU work overlaps (on streams with no order between them)
  *    race on the array: order them on one stream;
- *  - host per-row params are copied into the array, so the caller may reuse
- *    them once the call returns; a single params entry on the device is read
- *    back with a stream synchronization, as in pesti_sample_batch.
+ *  - host per-row params are copied into the array on the stream.  From
+ *    ordinary (pageable) host memory the copy has taken the values when the
+ *    call returns, so the caller may reuse them at once.  From page-locked
+ *    host memory (cudaMallocHost, cudaHostRegister, torch's pin_memory) the
+ *    copy runs later, when the stream reaches it: the caller must leave those
+ *    params unchanged until then (synchronize the stream, or wait on an event
+ *    recorded after the call, before rewriting them);
+ *  - a single params entry on the device is read back with a stream
+ *    synchronization, as in pesti_sample_batch.
  * The first call on a device does the set-up: it looks the array up with
  * cudaGetSymbolAddress, which loads it onto that device.  Make that first call
  * before any stream capture.  No call allocates: none calls cudaMalloc,

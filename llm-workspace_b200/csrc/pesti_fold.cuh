@@ -370,7 +370,6 @@ constexpr int NW = NT / 32;
 struct Smem {
   uint32_t hist[NW][256];
   uint32_t iscr[34];
-  int skip;
 };
 
 // Stable ascending LSD radix sort (8-bit digits) of n (key, value) pairs held
@@ -390,7 +389,6 @@ __device__ __noinline__ int block_radix_sort(uint32_t* k0, uint32_t* v0, uint32_
     uint32_t* kout = cur ? k0 : k1;
     uint32_t* vout = cur ? v0 : v1;
     for (int i = tid; i < NW * 256; i += NT) (&sm.hist[0][0])[i] = 0u;
-    if (tid == 0) sm.skip = 0;
     __syncthreads();
     // RB steps of 32 keys at a time: their loads are issued together, then
     // counted in order (the counters chain through shared memory)
@@ -412,13 +410,16 @@ __device__ __noinline__ int block_radix_sort(uint32_t* k0, uint32_t* v0, uint32_
       }
     }
     __syncthreads();
+    // a pass whose digit is the same for every key moves nothing; the
+    // decision is taken by the barrier itself, so every warp sees the same
+    // value and no shared flag outlives the pass
+    bool one_digit = false;
     if (tid < 256) {
       uint32_t t = 0;
       for (int ww = 0; ww < NW; ++ww) t += sm.hist[ww][tid];
-      if ((long long)t == n) sm.skip = 1;
+      one_digit = (long long)t == n;
     }
-    __syncthreads();
-    if (sm.skip) continue;  // uniform across the block
+    if (__syncthreads_or(one_digit)) continue;
     // exclusive scan in (digit, warp) order: CPT counters per thread
     constexpr int CPT = NW * 256 / NT;
     static_assert(CPT * NT == NW * 256, "counter split");

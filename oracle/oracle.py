@@ -211,3 +211,65 @@ def py_sample(logits, temperature, top_p, top_k, r):
         if rr <= c:
             return i, ip
     return (norm[-1][1] if norm else 0), ip
+
+
+# ---------------------------------------------------------------------------
+# Parity figures of a batch against both oracle modes (tests and the bench's
+# correctness guard).
+# ---------------------------------------------------------------------------
+BOUNDARY_BAND = 1e-6
+
+
+def parity_report(logits: np.ndarray, params, u: np.ndarray, tokens, kept_p, kept_idx, kept_count,
+                  kept_width: int, nthreads: int = 0) -> dict:
+    """The figures the drop-in contract is stated in, for one batch:
+
+    rows_exact        rows whose token, kept-list length, kept indices and kept
+                      probabilities (bits, first kept_width entries) equal the
+                      oracle's with exp correctly rounded;
+    token_mismatch_rate  against the oracle with the platform expf (what the
+                      Rust reference calls): tokens that differ, outside the
+                      rows whose draw lies within 1e-6 of a cumulative-
+                      probability boundary, over all rows;
+    rows_near_boundary   rows inside that band;
+    max_prob_rel_err  largest relative difference of a kept probability from
+                      the platform-expf oracle's, over entries with the same
+                      index at the same position;
+    topk_sets_exact   fraction of the top-k rows (T != 0, 0 < top_k <=
+                      kept_width) whose top-k index set equals the
+                      platform-expf oracle's."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    B = x.shape[0]
+    tok = np.asarray(tokens).view(np.uint32).reshape(B)
+    kp = np.asarray(kept_p, dtype=np.float32).reshape(B, kept_width)
+    ki = np.asarray(kept_idx).view(np.uint32).reshape(B, kept_width)
+    kc = np.asarray(kept_count).reshape(B)
+    cr = sample_batch(x, params, u, EXP_CR, kept_width=kept_width, nthreads=nthreads)
+    exact = ((tok == cr["tokens"]) & (kc == cr["kept_count"]) & (ki == cr["kept_idx"]).all(axis=1)
+             & (kp.view(np.uint32) == cr["kept_p"].view(np.uint32)).all(axis=1))
+    ref = sample_batch(x, params, u, EXP_PLATFORM, kept_width=kept_width, nthreads=nthreads)
+    mism = tok != ref["tokens"]
+    near = ref["boundary_dist"] <= BOUNDARY_BAND
+    valid = ref["kept_idx"] != 0xFFFFFFFF
+    same = valid & (ki == ref["kept_idx"])
+    rp = ref["kept_p"][same].astype(np.float64)
+    gp = kp[same].astype(np.float64)
+    rel = np.abs(gp - rp) / np.maximum(np.abs(rp), 1e-38)
+    plist = [params] * B if isinstance(params, tuple) else list(params)
+    topk_rows, topk_ok = 0, 0
+    for b in range(B):
+        t, _, k = plist[b]
+        if t != 0.0 and 0 < k <= kept_width:
+            topk_rows += 1
+            topk_ok += int(set(ki[b, :k].tolist()) == set(ref["kept_idx"][b, :k].tolist()))
+    return {
+        "rows": B,
+        "rows_exact": int(exact.sum()),
+        "token_mismatches": int(mism.sum()),
+        "token_mismatches_outside_band": int((mism & ~near).sum()),
+        "token_mismatch_rate": float((mism & ~near).sum()) / max(B, 1),
+        "rows_near_boundary": int(near.sum()),
+        "max_prob_rel_err": float(rel.max()) if rel.size else 0.0,
+        "topk_rows": topk_rows,
+        "topk_sets_exact": (topk_ok / topk_rows) if topk_rows else None,
+    }

@@ -94,3 +94,35 @@ def test_noalloc_refuses_a_batch_larger_than_its_scratch():
     assert "PESTI_NOALLOC_SCRATCH_BYTES" in msg and str(ps.NOALLOC_SCRATCH_BYTES) in msg, msg
     torch.cuda.synchronize()
     assert bool((out == -7).all())
+
+
+def test_noalloc_page_locked_params(sampler):
+    """Per-row params in page-locked host memory: the copy into the scratch
+    array runs when the stream reaches it, so the caller rewrites the params
+    for the next call only after synchronizing.  Two calls from the same
+    page-locked array, each with its own configs, give the allocating entry
+    point's results bit for bit."""
+    import torch
+    import pesti_sampler as ps
+    lib = ps.load_library()
+    B = 8
+    x = torch.from_numpy(synth.make_logits(2, B=B)).cuda()
+    u = torch.from_numpy(synth.make_u(2, B)).cuda()
+    sets = [[ps.SamplingConfig(0.7, 0.9, 50)] * 4 + [ps.SamplingConfig(1.0, 0.0, 5)] * 4,
+            [ps.SamplingConfig(0.0, 0.0, 0), ps.SamplingConfig(0.9, 0.0, 64)] * 4]
+    page_locked = torch.empty(B * ctypes.sizeof(ps._Params), dtype=torch.uint8).pin_memory()
+    arr = (ps._Params * B).from_address(page_locked.data_ptr())
+    st = torch.cuda.current_stream().cuda_stream
+    for cfgs in sets:
+        for i, c in enumerate(cfgs):
+            arr[i] = c.to_params(True)
+        out, kp, ki, kc = _outputs(B)
+        rc = lib.pesti_sample_batch_noalloc(x.data_ptr(), ps.PESTI_F32, B, x.shape[1], x.shape[1], arr, 1, 0,
+                                            u.data_ptr(), out.data_ptr(), kp.data_ptr(), ki.data_ptr(), KW,
+                                            kc.data_ptr(), st)
+        assert rc == ps.PESTI_OK, lib.pesti_last_error().decode()
+        torch.cuda.synchronize()  # the stream has passed the call: the params may change now
+        want = [t.cpu().numpy() for t in sampler.sample_batch(x, cfgs, u, kept_width=KW)]
+        got = [t.cpu().numpy() for t in (out, kp, ki, kc)]
+        for g, w_ in zip(got, want):
+            assert np.array_equal(g.view(np.uint8), w_.view(np.uint8))

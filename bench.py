@@ -78,17 +78,76 @@ L2_BYTES = 126 * 1024 * 1024
 TRAFFIC_PER_STEP = {}
 
 
+def cluster_pass(V, params):
+    """The batch takes the cluster pass: every row greedy (T == 0) or top-k
+    <= 256, rows of at most 131072 columns."""
+    return 1 <= V <= 131072 and all(t == 0.0 or 1 <= k <= 256 for (t, _, k) in params)
+
+
 def kernels_per_step(V, params):
-    """This library's launches in one step: the HBM pass; the fused pass (rows
-    beyond 128k columns, or of at most 64k in batches of 32 rows or more when
-    every row is on the top-k fast path), plus the survivor pass when some row
-    is off that path, else the survivor pass and the task-queue
-    classification; the row kernel."""
+    """This library's launches in one step.  The cluster pass: the cluster
+    kernel and the row kernel (whose blocks return at once unless the cluster
+    left their row).  Otherwise: the HBM pass; the fused pass (rows beyond 128k
+    columns, or of at most 64k in batches of 32 rows or more when every row is
+    on the top-k fast path), plus the survivor pass when some row is off that
+    path, else the survivor pass and the task-queue classification; the row
+    kernel."""
+    if cluster_pass(V, params):
+        return 2
     off_fast = any(not (1 <= k <= 256) or t <= 0 for (t, _, k) in params)
     fused = V > 131072 or (V <= 65536 and not off_fast and len(params) >= 32)
     if not fused:
         return 4
     return 4 if off_fast else 3
+
+
+def b1_latency(s, ps, synth, dev, rows=1000, warm=64):
+    """p50/p99 host wall time (us) of one B=1 pesti_sample_batch call on a
+    device-resident [1, 32000] f32 row (T 0.8, top-k 40) followed by
+    cudaStreamSynchronize, with the call's arguments prepared beforehand as a
+    decode loop would hold them."""
+    import ctypes
+    import glob
+
+    import torch
+    x1 = torch.from_numpy(synth.make_logits(1, B=64)).to(dev)
+    u1 = torch.from_numpy(synth.make_u(1, 64)).to(dev)
+    o1 = torch.empty(1, dtype=torch.int32, device=dev)
+    lib = ps.load_library()
+    prm = (ps._Params * 1)(ps.SamplingConfig(0.8, 0.95, 40).to_params(True))
+    st = torch.cuda.current_stream(dev).cuda_stream
+    V = x1.shape[1]
+    rowp = [x1[r:r + 1].data_ptr() for r in range(64)]
+    up = [u1[r:r + 1].data_ptr() for r in range(64)]
+    outp = o1.data_ptr()
+    sync = None
+    for path in glob.glob(os.path.join(os.path.dirname(torch.__file__), "..", "nvidia", "cuda_runtime", "lib",
+                                       "libcudart.so*")):
+        try:
+            cudart = ctypes.CDLL(path)
+            cudart.cudaStreamSynchronize.argtypes = [ctypes.c_void_p]
+            sync = lambda: cudart.cudaStreamSynchronize(st)  # noqa: E731
+            break
+        except OSError:
+            continue
+    if sync is None:
+        sync = torch.cuda.synchronize
+    call = lib.pesti_sample_batch
+    h = s._h
+    ts = []
+    for i in range(rows + warm):
+        r = i % 64
+        t0 = time.perf_counter()
+        rc = call(h, rowp[r], ps.PESTI_F32, 1, V, V, prm, 0, 0, up[r], outp, None, None, 0, None, st)
+        sync()
+        t1 = time.perf_counter()
+        if rc != 0:
+            raise RuntimeError(lib.pesti_last_error().decode())
+        if i >= warm:
+            ts.append((t1 - t0) * 1e6)
+    return {"p50": float(np.percentile(ts, 50)), "p99": float(np.percentile(ts, 99)), "rows": len(ts),
+            "how": "pesti_sample_batch through ctypes on a device-resident [1, 32000] f32 row, then "
+                   "cudaStreamSynchronize; host wall clock"}
 
 
 def merge_parity(reps):
@@ -577,22 +636,12 @@ def main():
     e2e_ms = max_over_ranks(e2e_ms, dev)
     e2e_value = B_total * e2e_steps / (e2e_ms / 1e3)
 
-    # B = 1 latency (workload 1 shape), device-resident logits, host wall clock
+    # B = 1 latency (workload 1 shape, [1, 32000] f32 rows already on the
+    # device): host wall clock of one pesti_sample_batch call through the C ABI
+    # plus the stream synchronisation that waits for its token
     lat = None
     if rank == 0:
-        x1 = torch.from_numpy(synth.make_logits(1, B=64)).to(dev)
-        u1 = torch.from_numpy(synth.make_u(1, 64)).to(dev)
-        o1 = torch.empty(1, dtype=torch.int32, device=dev)
-        c1 = ps.SamplingConfig(0.8, 0.95, 40)
-        ts = []
-        for i in range(1064):
-            r = i % 64
-            t0 = time.perf_counter()
-            s.sample_batch(x1[r:r + 1], c1, u1[r:r + 1], out=o1)
-            torch.cuda.synchronize()
-            if i >= 64:
-                ts.append((time.perf_counter() - t0) * 1e6)
-        lat = {"p50": float(np.percentile(ts, 50)), "p99": float(np.percentile(ts, 99)), "rows": len(ts)}
+        lat = b1_latency(s, ps, synth, dev)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -615,8 +664,10 @@ def main():
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": TRAFFIC_PER_STEP.get(w) if world == 1 else None,
                          "bytes_per_launch": step_bytes,
-                         "kernels": {"slice_stats": kern(scan_ms), "survivor+classify": kern(surv_ms),
-                                     "row": kern(row_ms)}},
+                         "kernels": ({"row_cluster": kern(scan_ms), "row (rows the cluster pass left)": kern(row_ms)}
+                                     if cluster_pass(V, params) else
+                                     {"slice_stats": kern(scan_ms), "survivor+classify": kern(surv_ms),
+                                      "row": kern(row_ms)})},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": step_bytes + B * 4,
                     "d2h_bytes_per_step": B * 4},
             "gpu_launches": nk * args.steps,

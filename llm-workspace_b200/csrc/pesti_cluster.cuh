@@ -1,0 +1,1012 @@
+// One thread-block cluster per row: the whole sampling step of a row in one
+// launch (sampling.rs:39-111 for top-k rows, and the argmax branch of
+// generate, transformer/model.rs:517-521).
+//
+// The row is split over the cluster's CTAs and their warps; warp g (in row
+// order, over the CTAs by rank) owns the contiguous range [g*SLW, (g+1)*SLW).
+// The CTAs exchange their partial results through distributed shared memory
+// and cluster barriers, so nothing crosses a kernel boundary:
+//
+//   pass 1   each warp streams its range from HBM: maximum (NaN ignored, as
+//            the f32::max fold of sampling.rs:126 does), NaN/inf flags, an
+//            approximate softmax mass relative to its own maximum, and the
+//            maximum of every 32*VE-element segment;
+//   combine  every CTA reads every warp's summary from the cluster: the row
+//            maximum m, each warp's approximate fold state at its start (the
+//            mass of the earlier warps) and prefix maximum, the pruning
+//            thresholds, and the candidate threshold tau (a lower bound of
+//            the k-th largest logit, from the segment maxima);
+//   pass 2   each warp re-reads its range (from L2): elements that provably
+//            leave the softmax fold unchanged are dropped; every survivor
+//            gets its exact exp and its approximate fold state, and becomes
+//            either part of a run (a plain integer increment of the state's
+//            bits inside one binade, as a transducer for an even and an odd
+//            entry state) or an explicit element (added with a real f32 add);
+//            elements at or above tau are the top-k candidates;
+//   walk     the leader CTA gathers every CTA's entries and candidates, walks
+//            the entries with the exact state (the softmax sum S bit for bit,
+//            sampling.rs:128), sorts the candidates by (p desc, index asc),
+//            and folds total, normalises and draws (sampling.rs:81-111).
+//
+// A run whose binade the approximate state predicted wrongly fails its check
+// in the walk and is folded again from the raw logits of its range, so the
+// approximation never decides a result.  Rows the cluster cannot finish
+// exactly (NaN or infinite rows, rows that are not top-k <= 256, too many
+// candidates, a probability tie at the candidate threshold) get their row
+// prologue written and a flag set; the row kernel's generic path samples them
+// in the launch that follows.
+#pragma once
+#include <cooperative_groups.h>
+#include "pesti_kernels.cuh"
+
+namespace pesti {
+namespace cg = cooperative_groups;
+
+constexpr int CL_WARPS = 8;             // warps per CTA
+constexpr int CL_NT = CL_WARPS * 32;
+constexpr int CL_MAXC = 16;             // CTAs per cluster (row)
+constexpr int CL_SEGS = 16;             // 32*VE-element segments per warp at most
+constexpr int CL_U = 4;                 // segments loaded at once per warp (pass 1)
+constexpr int CL_STAGES = 4;            // segments in flight per warp through shared memory (pass 2)
+constexpr int CL_R = 4;                 // survivors per lane in one classification batch
+constexpr int CL_BATCH = 32 * CL_R;     // survivors classified together
+constexpr int CL_RING = 256;            // survivor ring per warp (power of two)
+constexpr int CL_EW = 48;               // fold entries per warp (beyond: its range is replayed)
+constexpr int CL_LIST = 128;            // merged fold entries per CTA (beyond: its range is replayed)
+constexpr int CL_CCAP = 256;            // top-k candidates per CTA
+constexpr int CL_LOCAL = 512;           // fold entries of a row the leader gathers
+constexpr long long CL_MAX_V = 131072;  // longest row of the cluster path
+
+struct ClusterArgs {
+  const void* logits;
+  int dtype;
+  long long B, V, ld;
+  pesti_sampling_params uni;
+  const pesti_sampling_params* per_row;
+  int SLW;            // elements per warp: a multiple of 32*VE, at most CL_SEGS*32*VE
+  const float* u;
+  uint32_t* out;
+  float* kept_p;
+  uint32_t* kept_idx;
+  long long kept_width;
+  int64_t* kept_count;
+  int* fb;            // [B]: 1 when the row is left to the row kernel's generic path
+  RowInfo* info;      // [B]: those rows' prologue
+  float band;         // relative guard band around binade edges
+  int early_dependents;  // let the row kernel launch at once (its blocks then wait for this grid)
+};
+
+struct ClWarp {       // one warp's pass-1 summary, read by every CTA of the cluster
+  float max_raw;      // max of its raw logits, NaN ignored (-inf: none)
+  float sum_rel;      // sum of 2^(raw*c2 - max_raw*c2), c2 = log2(e)/T_eff (approximate)
+  int32_t last_nan;   // last NaN index, -1
+  uint32_t flags;     // MF_*
+  int32_t first_max, last_max;  // first / last index holding max_raw (greedy rows), -1
+  int32_t pad0, pad1;
+};
+
+struct ClShared {
+  ClWarp wst[CL_WARPS];
+  float segmax[CL_WARPS][CL_SEGS];
+  double A[CL_WARPS];         // approximate fold state at each warp's start
+  float P[CL_WARPS];          // max raw logit before each warp
+  float thrL[CL_WARPS];       // raw logits below it are absorbed by the running sum (or -inf)
+  int wn[CL_WARPS];           // fold entries of each warp (-1: overflow, replay its range)
+  float cand_e[CL_CCAP];      // the CTA's top-k candidates: exact exp, row index
+  uint32_t cand_i[CL_CCAP];
+  int ncand;                  // candidates found (may exceed CL_CCAP)
+  int nlist;                  // merged fold entries of the CTA
+  FoldEnt list[CL_LIST];
+  // row state, computed by every CTA
+  float max_raw, m, tau, e_tau;
+  uint32_t flags;
+  int last_nan, first_max, last_max;
+  int status;                 // leader: 0 sampled, 1 fallback
+  double dscr[34];
+  float fscr[34];
+  int iscr[34];
+  uint32_t uscr[34];
+  union {
+    struct {                  // the candidate threshold (combine)
+      uint32_t hist[256];
+      float tau;
+    } t;
+    struct {                  // pass 2: staged segments, survivor rings and fold entries per warp
+      float4 stg[CL_WARPS][CL_STAGES * 32];
+      float qraw[CL_WARPS][CL_RING];
+      uint32_t qidx[CL_WARPS][CL_RING];
+      FoldEnt went[CL_WARPS][CL_EW];
+    } c;
+    struct {                  // leader: the row's entries and candidates
+      FoldEnt ent[CL_LOCAL];
+      unsigned long long key[FAST_CAND];
+      float q[FAST_K];
+      float stage[STAGE];
+      int coff[CL_MAXC + 1];
+      int ccnt[CL_MAXC + 1];
+      int nent, ncand;
+    } f;
+  } u;
+};
+
+// Candidate threshold: a lower bound of the keff-th largest raw logit, from
+// the row's segment maxima (vals, NV per thread, -inf where none; maxima of
+// disjoint segments are distinct elements).  A 256-bin histogram of their
+// distance below the row max mx in units of t_eff/8 places the keff-th
+// largest; the threshold lies two bins further down (one bin for the
+// rounding of the distances), rounded toward -inf.  -inf when the first 255
+// bins hold fewer than keff maxima.  Every thread calls it.
+template <int NV>
+__device__ float cl_tau(const float (&vals)[NV], float mx, float t_eff, long long keff, ClShared& sh) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  uint32_t* hist = sh.u.t.hist;
+  for (int i = tid; i < 256; i += CL_NT) hist[i] = 0u;
+  __syncthreads();
+  const float inv = 8.0f / t_eff;
+#pragma unroll
+  for (int r = 0; r < NV; ++r) {
+    const float v = vals[r];
+    if (v > NEG_INF) {  // also false for NaN
+      const float d = (mx - v) * inv;
+      const uint32_t bin = d < 255.0f ? (uint32_t)d : 255u;
+      atomicAdd(&hist[bin], 1u);
+    }
+  }
+  __syncthreads();
+  if (tid < 32) {
+    uint32_t c8[8], lsum = 0u;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      c8[q] = lane * 8 + q < 255 ? hist[lane * 8 + q] : 0u;
+      lsum += c8[q];
+    }
+    const uint32_t incl = warp_incl_scan_add(lsum);
+    const uint32_t excl = incl - lsum;
+    int bin = 1 << 30;
+    if ((long long)excl < keff && (long long)incl >= keff) {
+      uint32_t cum = excl;
+      int q = 0;
+      for (; q < 7; ++q) {
+        if ((long long)(cum + c8[q]) >= keff) break;
+        cum += c8[q];
+      }
+      bin = lane * 8 + q;
+    }
+    bin = __reduce_min_sync(PESTI_FULL_MASK, (uint32_t)bin);
+    if (lane == 0)
+      sh.u.t.tau = bin < 255 ? __fsub_rd(mx, __fmul_ru(t_eff, (float)(bin + 2) * 0.125f)) : NEG_INF;
+  }
+  __syncthreads();
+  return sh.u.t.tau;
+}
+
+// Loads segment q of a warp's range (32*VE elements, VE per lane, in row
+// order): one 16-byte load per lane when the segment is whole and the rows are
+// 16-byte aligned, scalar loads otherwise (0 beyond the range, nv valid).
+template <typename TIn, int VE, bool VEC>
+__device__ __forceinline__ void cl_load(const TIn* row, long long pos0, long long end, float (&x)[VE], int& nv) {
+  if (VEC && pos0 + VE <= end) {
+    const float4 r4 = __ldg(reinterpret_cast<const float4*>(row + pos0));
+    if (sizeof(TIn) == 4) {
+      x[0] = r4.x; x[1] = r4.y; x[2] = r4.z; x[3] = r4.w;
+    } else {
+      const uint32_t wds[4] = {__float_as_uint(r4.x), __float_as_uint(r4.y), __float_as_uint(r4.z),
+                               __float_as_uint(r4.w)};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) unpack2<TIn>(wds[h], x[2 * h], x[2 * h + 1]);
+    }
+    nv = VE;
+    return;
+  }
+  nv = 0;
+#pragma unroll
+  for (int e = 0; e < VE; ++e) {
+    const bool in = pos0 + e < end;
+    x[e] = in ? load_logit<TIn>(row, pos0 + e) : 0.0f;
+    nv = in ? e + 1 : nv;
+  }
+}
+
+__device__ __forceinline__ void cl_write_pad(const ClusterArgs& a, long long b, long long from) {
+  for (long long j = from + (threadIdx.x & 31); j < a.kept_width; j += 32) {
+    if (a.kept_p) a.kept_p[b * a.kept_width + j] = 0.0f;
+    if (a.kept_idx) a.kept_idx[b * a.kept_width + j] = 0xffffffffu;
+  }
+}
+
+template <typename TIn, int VE, bool VEC>
+__global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
+  __shared__ __align__(16) ClShared sh;
+  cg::cluster_group cl = cg::this_cluster();
+  const int C = (int)cl.num_blocks();
+  const int cr = (int)cl.block_rank();
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const long long b = blockIdx.x / C;
+  if (a.early_dependents) grid_dep_launch_next();
+  const long long V = a.V;
+  const pesti_sampling_params prm = row_params(a.uni, a.per_row, b);
+  const float T = prm.temperature;
+  const bool scale = T > 0.0f;
+  const float t_eff = scale ? T : 1.0f;
+  const float NEG_INF = -__int_as_float(0x7f800000), INF = __int_as_float(0x7f800000);
+  const bool greedy = is_greedy(prm);
+  const TIn* row = (const TIn*)a.logits + b * a.ld;
+  constexpr int SEG = 32 * VE;
+  const int g = cr * CL_WARPS + w;  // the warp's place in the row
+  const long long s0 = (long long)g * a.SLW;
+  const long long s1 = s0 + a.SLW < V ? s0 + a.SLW : V;
+  const int nseg = s0 < V ? (int)((s1 - s0 + SEG - 1) / SEG) : 0;
+  const float c2 = 1.4426950408889634f / t_eff;
+
+  // ---------------- pass 1: the HBM stream ----------------
+  {
+    float lmax = NEG_INF, lsum = 0.0f;  // lane: max and sum of 2^(x*c2 - lmax*c2)
+    float gmax = NEG_INF;               // greedy rows: the lane's max, with its indices
+    uint32_t lflags = 0u;
+    int lnan = -1, lfirst = -1, llast = -1;
+    for (int q0 = 0; q0 < nseg; q0 += CL_U) {
+      float x[CL_U][VE];
+      int nv[CL_U];
+#pragma unroll
+      for (int uu = 0; uu < CL_U; ++uu) {
+        nv[uu] = 0;
+        if (q0 + uu < nseg) cl_load<TIn, VE, VEC>(row, s0 + (long long)(q0 + uu) * SEG + lane * VE, s1, x[uu], nv[uu]);
+      }
+#pragma unroll
+      for (int uu = 0; uu < CL_U; ++uu) {
+        if (q0 + uu >= nseg) break;
+        const long long p0 = s0 + (long long)(q0 + uu) * SEG + lane * VE;
+        float smax = NEG_INF;
+#pragma unroll
+        for (int e = 0; e < VE; ++e) {
+          const float v = x[uu][e];
+          const bool in = e < nv[uu];
+          if (in) {
+            if (is_nan(v)) {
+              lflags |= MF_NAN;
+              lnan = (int)(p0 + e);
+            } else {
+              if (v == INF) lflags |= MF_POSINF;
+              if (v == NEG_INF) lflags |= MF_NEGINF;
+              smax = fmaxf(smax, v);
+              if (greedy) {  // first and last index of the lane's max so far
+                if (lfirst < 0 || v > gmax) {
+                  gmax = v;
+                  lfirst = (int)(p0 + e);
+                  llast = lfirst;
+                } else if (v == gmax) {
+                  llast = (int)(p0 + e);
+                }
+              }
+            }
+          }
+        }
+        // the segment's max (every lane's keys; NaN never reaches smax)
+        const uint32_t sk = __reduce_max_sync(PESTI_FULL_MASK, fkey(smax));
+        if (lane == 0) sh.segmax[w][q0 + uu] = fkey_inv(sk);
+        if (smax > lmax) {
+          lsum = lmax > NEG_INF ? lsum * ex2_approx(fmaf(lmax, c2, -smax * c2)) : 0.0f;
+          lmax = smax;
+        }
+        if (lmax > NEG_INF) {
+          const float ym = lmax * c2;
+#pragma unroll
+          for (int e = 0; e < VE; ++e)
+            if (e < nv[uu] && !is_nan(x[uu][e])) lsum += ex2_approx(fmaf(x[uu][e], c2, -ym));
+        }
+      }
+    }
+    for (int q = nseg + lane; q < CL_SEGS; q += 32) sh.segmax[w][q] = NEG_INF;
+    // the warp's summary
+    const float wmax = fkey_inv(__reduce_max_sync(PESTI_FULL_MASK, fkey(lmax)));
+    float part = 0.0f;
+    if (lmax > NEG_INF && wmax > NEG_INF) part = lsum * ex2_approx(fmaf(lmax, c2, -wmax * c2));
+    if (!(wmax < INF)) part = 0.0f;  // an infinite row is uniform; its mass is never used
+    const float wsum = warp_reduce_add(part);
+    const uint32_t wfl = __reduce_or_sync(PESTI_FULL_MASK, lflags);
+    const int wnan = (int)__reduce_max_sync(PESTI_FULL_MASK, (uint32_t)(lnan + 1)) - 1;
+    int wfirst = -1, wlast = -1;
+    if (greedy) {
+      // first / last index of the warp's max (the lanes' own maxima may be lower)
+      const bool mine = gmax == wmax && lfirst >= 0;
+      wfirst = (int)__reduce_min_sync(PESTI_FULL_MASK, mine ? (uint32_t)lfirst : 0xffffffffu);
+      wlast = (int)__reduce_max_sync(PESTI_FULL_MASK, mine ? (uint32_t)(llast + 1) : 0u) - 1;
+      if (wfirst == (int)0xffffffff) wfirst = -1;
+    }
+    if (lane == 0) sh.wst[w] = ClWarp{wmax, wsum, wnan, wfl, wfirst, wlast, 0, 0};
+  }
+  cl.sync();
+
+  // ---------------- combine: the row prologue, in every CTA ----------------
+  const int NWR = C * CL_WARPS;
+  ClWarp rw{NEG_INF, 0.0f, -1, 0u, -1, -1, 0, 0};
+  if (tid < NWR) rw = *cl.map_shared_rank(&sh.wst[tid % CL_WARPS], tid / CL_WARPS);
+  // every segment max of the row (for the candidate threshold), fetched now
+  constexpr int NV = CL_MAXC * CL_WARPS * CL_SEGS / CL_NT;
+  float vals[NV];
+#pragma unroll
+  for (int r = 0; r < NV; ++r) {
+    const int i = r * CL_NT + tid;
+    const int wi = i / CL_SEGS;
+    vals[r] = wi < NWR ? *cl.map_shared_rank(&sh.segmax[wi % CL_WARPS][i % CL_SEGS], wi / CL_WARPS) : NEG_INF;
+  }
+  // row max, flags, last NaN
+  uint32_t mk = __reduce_max_sync(PESTI_FULL_MASK, fkey(rw.max_raw));
+  uint32_t fo = __reduce_or_sync(PESTI_FULL_MASK, rw.flags);
+  uint32_t ln = __reduce_max_sync(PESTI_FULL_MASK, (uint32_t)(rw.last_nan + 1));
+  if (lane == 0) {
+    sh.uscr[w] = mk;
+    sh.iscr[w] = (int)fo;
+    sh.iscr[8 + w] = (int)ln;
+  }
+  __syncthreads();
+  mk = 0u;
+  fo = 0u;
+  ln = 0u;
+  for (int q = 0; q < CL_WARPS; ++q) {
+    mk = mk > sh.uscr[q] ? mk : sh.uscr[q];
+    fo |= (uint32_t)sh.iscr[q];
+    ln = ln > (uint32_t)sh.iscr[8 + q] ? ln : (uint32_t)sh.iscr[8 + q];
+  }
+  const float mx = fkey_inv(mk);
+  const uint32_t fl = fo;
+  const int last_nan = (int)ln - 1;
+  int first_max = -1, last_max = -1;
+  if (greedy) {
+    const bool hold = tid < NWR && rw.max_raw == mx && rw.first_max >= 0;
+    uint32_t fm = __reduce_min_sync(PESTI_FULL_MASK, hold ? (uint32_t)rw.first_max : 0xffffffffu);
+    uint32_t lm = __reduce_max_sync(PESTI_FULL_MASK, hold ? (uint32_t)(rw.last_max + 1) : 0u);
+    __syncthreads();
+    if (lane == 0) {
+      sh.uscr[w] = fm;
+      sh.uscr[8 + w] = lm;
+    }
+    __syncthreads();
+    fm = 0xffffffffu;
+    lm = 0u;
+    for (int q = 0; q < CL_WARPS; ++q) {
+      fm = fm < sh.uscr[q] ? fm : sh.uscr[q];
+      lm = lm > sh.uscr[8 + q] ? lm : sh.uscr[8 + q];
+    }
+    first_max = fm == 0xffffffffu ? -1 : (int)fm;
+    last_max = (int)lm - 1;
+  }
+  const float m = scale ? fdiv(mx, T) : mx;  // sampling.rs:46 on the max element
+  const bool uniform = (fl & MF_NAN) || (scale && T == INF && (fl & (MF_POSINF | MF_NEGINF))) ||
+                       !(fabsf(m) < INF);
+  const long long k = (long long)prm.top_k;
+  const long long keff = k < V ? k : V;
+  const bool fast = !greedy && !uniform && fast_topk(prm, V);
+  // greedy rows are finished here (NaN rows with the last-index rule go to
+  // the row kernel, which re-scans after the last NaN as max_by does)
+  int decided = -1;  // 0: sampled here, 1: fallback
+  if (greedy) decided = ((fl & MF_NAN) && !(prm.flags & PESTI_FLAG_ARGMAX_FIRST)) ? 1 : 0;
+  else if (!fast) decided = 1;
+
+  float tau = INF;
+  if (decided < 0) {
+    // prefix mass and prefix max of the warps (exclusive, in row order)
+    const float ym = mx * c2;
+    // (float exp2 within 2 ulp: the pruning's lower bound keeps a 2^-10 slack)
+    const double mass = (tid < NWR && rw.max_raw > NEG_INF) ? (double)(exp2f(rw.max_raw * c2 - ym) * rw.sum_rel) : 0.0;
+    double tot;
+    const double A = block_excl_scan_add(mass, sh.dscr, tot);
+    float inc = tid < NWR ? rw.max_raw : NEG_INF;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(PESTI_FULL_MASK, inc, o);
+      if (lane >= o) inc = fmaxf(inc, y);
+    }
+    if (lane == 31) sh.fscr[w] = inc;
+    __syncthreads();
+    float pm = NEG_INF;
+    for (int q = 0; q < w; ++q) pm = fmaxf(pm, sh.fscr[q]);
+    float exc = __shfl_up_sync(PESTI_FULL_MASK, inc, 1);
+    if (lane == 0) exc = NEG_INF;
+    pm = fmaxf(pm, exc);
+    if (tid < NWR && tid / CL_WARPS == cr) {
+      const int wl = tid % CL_WARPS;
+      sh.A[wl] = A;
+      sh.P[wl] = pm;
+      // bound (b) of the pruning, in raw units (derivation at row_prologue):
+      // L <= the running sum, t = m + ln(L) - 17.36, rounded toward -inf
+      const double lfac = (1.0 - (double)V * 0x1p-24) * (1.0 - 0x1p-10) * exp2(-0x1p-20 * ((double)fabsf(ym) + 64.0));
+      const double L = A * lfac;
+      float thr = NEG_INF;
+      if (L >= 0x1p-60) {
+        const double tL = (double)m + log(L) - 17.36;
+        const double eta = 0x1p-20 * (fabs(tL) + fabs((double)m) + 1.0);
+        thr = __double2float_rd((tL - eta) * (double)t_eff);
+      }
+      sh.thrL[wl] = thr;
+    }
+    // candidate threshold from every segment max of the row
+    tau = cl_tau<NV>(vals, mx, t_eff, keff, sh);
+    if (tid == 0) {
+      sh.tau = tau;
+      sh.e_tau = tau > NEG_INF && tau < INF ? pesti_expf_call(fsub(scale ? fdiv(tau, T) : tau, m)) : 0.0f;
+      sh.ncand = 0;
+    }
+    __syncthreads();  // the histogram's space becomes the survivor rings
+  }
+  if (cr == 0 && tid == 0) {
+    sh.max_raw = mx;
+    sh.m = m;
+    sh.flags = fl;
+    sh.last_nan = last_nan;
+    sh.first_max = first_max;
+    sh.last_max = last_max;
+  }
+
+  // ---------------- pass 2: survivors, fold entries, candidates ----------------
+  if (decided < 0) {
+    const float c1 = ABSORB * t_eff * (1.0f + 0x1p-20f);
+    const float pf = (m - PRUNE_FLOOR) * t_eff;
+    const float p_floor = pf + 0x1p-20f * fabsf(pf);
+    auto bound_a = [&](float Pv) { return Pv >= p_floor ? fsub(Pv, fadd(c1, 0x1p-21f * fabsf(Pv))) : NEG_INF; };
+    const double lfac = (1.0 - (double)V * 0x1p-24) * (1.0 - 0x1p-10) * exp2(-0x1p-20 * ((double)fabsf(mx * c2) + 64.0));
+    // bound (b) from a lower bound L of the running sum (derivation at
+    // row_prologue): raw logits below it leave every later state unchanged
+    auto bound_b = [&](double L) {
+      float thr = NEG_INF;
+      if (L >= 0x1p-60) {
+        const double tL = (double)m + log(L) - 17.36;
+        const double eta = 0x1p-20 * (fabs(tL) + fabs((double)m) + 1.0);
+        thr = __double2float_rd((tL - eta) * (double)t_eff);
+      }
+      return thr;
+    };
+    float thr_b = sh.thrL[w];
+    float run_max = sh.P[w];
+    const float BAND = a.band;
+    float* qraw = sh.u.c.qraw[w];
+    uint32_t* qidx = sh.u.c.qidx[w];
+    FoldEnt* went = sh.u.c.went[w];
+    float4* stg = sh.u.c.stg[w];
+    // approximate fold state before the next survivor: the earlier warps'
+    // mass plus the exact exps of this warp's survivors so far
+    double s_run = sh.A[w];
+    double s_thr = s_run;         // the state bound (b) was last taken at
+    uint32_t head = 0u, tail = 0u;  // ring positions (consumed / appended)
+    int wn = 0;                   // entries written
+    bool over = false;            // entries overflowed: the walk replays the range
+    uint32_t lkey = KEY_NONE;     // key of the last entry written
+
+    const int nfull = VEC ? (int)((s1 - s0) / SEG) : 0;  // whole segments, staged through shared memory
+    if (VEC) {
+#pragma unroll
+      for (int st = 0; st < CL_STAGES; ++st) {
+        if (st < nfull) cp_async16(&stg[st * 32 + lane], row + s0 + (long long)st * SEG + lane * VE);
+        cp_async_commit();
+      }
+    }
+#pragma unroll 1
+    for (int q = 0; q < nseg; ++q) {
+      float x[VE];
+      int nv;
+      const long long p0 = s0 + (long long)q * SEG + lane * VE;
+      const bool piped = VEC && q < nfull;
+      if (piped) {
+        cp_async_wait<CL_STAGES - 1>();  // segment q has arrived (each lane reads its own bytes)
+        const float4 r4 = stg[(q % CL_STAGES) * 32 + lane];
+        if (sizeof(TIn) == 4) {
+          x[0] = r4.x; x[1] = r4.y; x[2] = r4.z; x[3] = r4.w;
+        } else {
+          const uint32_t wds[4] = {__float_as_uint(r4.x), __float_as_uint(r4.y), __float_as_uint(r4.z),
+                                   __float_as_uint(r4.w)};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) unpack2<TIn>(wds[h], x[2 * h], x[2 * h + 1]);
+        }
+        nv = VE;
+      } else {
+        cl_load<TIn, VE, false>(row, p0, s1, x, nv);
+      }
+      if (piped) {  // the stage just read takes segment q + CL_STAGES
+        const int qn = q + CL_STAGES;
+        if (qn < nfull) cp_async16(&stg[(q % CL_STAGES) * 32 + lane], row + s0 + (long long)qn * SEG + lane * VE);
+        cp_async_commit();
+      }
+      // bound (b) again once the running state has doubled (it only rises)
+      if (s_run >= 2.0 * s_thr && s_run > 0.0) {
+        float tb = 0.0f;
+        if (lane == 0) tb = bound_b(s_run * lfac);
+        thr_b = fmaxf(thr_b, __shfl_sync(PESTI_FULL_MASK, tb, 0));
+        s_thr = s_run;
+      }
+      const float thr = fmaxf(bound_a(run_max), thr_b);
+      run_max = fmaxf(run_max, sh.segmax[w][q]);
+      // top-k candidates (raw >= tau; their exact exps, sampling.rs:127)
+      int nc = 0;
+#pragma unroll
+      for (int e = 0; e < VE; ++e) nc += (e < nv && x[e] >= tau) ? 1 : 0;
+      if (__any_sync(PESTI_FULL_MASK, nc > 0)) {
+        const int cin = warp_incl_scan_add(nc);
+        int cb = 0;
+        if (lane == 31) cb = atomicAdd(&sh.ncand, cin);
+        cb = __shfl_sync(PESTI_FULL_MASK, cb, 31) + cin - nc;
+#pragma unroll
+        for (int e = 0; e < VE; ++e) {
+          if (e < nv && x[e] >= tau) {
+            if (cb < CL_CCAP) {
+              sh.cand_e[cb] = pesti_expf_call(fsub(scale ? fdiv(x[e], T) : x[e], m));
+              sh.cand_i[cb] = (uint32_t)(p0 + e);
+            }
+            ++cb;
+          }
+        }
+      }
+      if (over) continue;
+      // survivors into the ring in row order: the segment in parts of 128
+      // elements (all of the lanes [ph*LPP, (ph+1)*LPP)), so that the ring
+      // never holds more than 31 + 128 of them
+      constexpr int NPART = VE / 4;
+      constexpr int LPP = 32 / NPART;
+      uint32_t sv = 0u;
+#pragma unroll
+      for (int e = 0; e < VE; ++e) sv |= (e < nv && x[e] >= thr) ? (1u << e) : 0u;
+#pragma unroll 1
+      for (int ph = 0; ph < NPART; ++ph) {
+        const bool mine = lane / LPP == ph;
+        const int cnt = mine ? __popc(sv) : 0;
+        const int sin = warp_incl_scan_add(cnt);
+        const int tot = __shfl_sync(PESTI_FULL_MASK, sin, 31);
+        uint32_t o = tail + (uint32_t)(sin - cnt);
+        if (mine) {
+#pragma unroll
+          for (int e = 0; e < VE; ++e) {
+            if (sv & (1u << e)) {
+              qraw[o & (CL_RING - 1)] = x[e];
+              qidx[o & (CL_RING - 1)] = (uint32_t)(p0 + e);
+              ++o;
+            }
+          }
+        }
+        tail += (uint32_t)tot;
+        __syncwarp();
+        // classification of the survivors, CL_BATCH at a time (fewer at the end)
+#pragma unroll 1
+        while (!over && (tail - head >= (uint32_t)CL_BATCH || (q == nseg - 1 && ph == NPART - 1 && tail > head))) {
+          const int n = tail - head >= (uint32_t)CL_BATCH ? CL_BATCH : (int)(tail - head);
+          // fast path: element j*32 + lane of the batch for j < CL_R.  The
+          // approximate exps (exp_hw, within DE_0 + |z| DE_Z of the exact
+          // value with twice its margin) decide rint(e/w) unless e/w lies
+          // near a half-integer; those lanes take the exact exp.  The batch
+          // is one plain increment when its whole state range lies inside
+          // one binade away from its edges, no element is large next to the
+          // state and none is a tie.
+          float z[CL_R], ea[CL_R];
+          float lsum = 0.0f, lmaxe = 0.0f;
+#pragma unroll
+          for (int j = 0; j < CL_R; ++j) {
+            const int i = j * 32 + lane;
+            z[j] = 0.0f;
+            ea[j] = 0.0f;
+            if (i < n) {
+              const float raw = qraw[(head + i) & (CL_RING - 1)];
+              z[j] = fsub(scale ? fdiv(raw, T) : raw, m);  // sampling.rs:46,127: the exact argument
+              ea[j] = exp_hw(z[j]);
+              lsum += ea[j];
+              lmaxe = fmaxf(lmaxe, ea[j] * fmaf(-z[j], DE_Z, 1.0f + DE_0));
+            }
+          }
+          const float btot = warp_reduce_add(lsum);
+          const float sb = (float)s_run;
+          bool done = false;
+          if (sb >= 0x1p-126f) {
+            const uint32_t lo = fbits(sb) & 0x7f800000u;
+            const float lov = bitsf(lo);
+            if (sb >= lov * (1.0f + BAND) && sb + btot * (1.0f + 0x1p-20f) <= 2.0f * lov * (1.0f - BAND) &&
+                __all_sync(PESTI_FULL_MASK, lmaxe < 0.5f * lov)) {
+              const uint32_t E = lo >> 23;
+              const int sh2 = 150 - (int)E;  // w = 2^(E-150)
+              uint32_t ksum = 0u;
+              bool tie = false;
+#pragma unroll
+              for (int j = 0; j < CL_R; ++j) {
+                const int i = j * 32 + lane;
+                if (i < n) {
+                  bool exact;
+                  uint32_t kd = 0u;
+                  if (ea[j] == 0.0f) {
+                    exact = E < 40u;  // else the exact value (< 2^-126) rounds to 0 on this grid
+                  } else {
+                    const float tt = __uint_as_float(fbits(ea[j]) + ((uint32_t)sh2 << 23));  // ea/w, exact scaling
+                    const float kr = rintf(tt);
+                    const float slack = 0.5f - fabsf(tt - kr);
+                    exact = !(slack > tt * fmaf(-z[j], DE_Z, DE_0) + 0x1p-24f);
+                    kd = (uint32_t)kr;
+                  }
+                  if (exact) {
+                    const float ex = pesti_expf_call(z[j]);
+                    const uint32_t k0 = fbits(fadd(lov, ex)) - lo;
+                    const uint32_t k1 = fbits(fadd(bitsf(lo + 1u), ex)) - (lo + 1u);
+                    tie = tie || k0 != k1;
+                    kd = k0;
+                  }
+                  ksum += kd;
+                }
+              }
+              if (!__any_sync(PESTI_FULL_MASK, tie)) {
+                const uint32_t ks = tr_sat(warp_reduce_add(ksum));  // each < 2^22, at most CL_BATCH of them
+                const uint32_t last_end = qidx[(head + n - 1) & (CL_RING - 1)] + 1u;
+                if (lkey == lo) {
+                  if (lane == 0) {
+                    const FoldEnt pe = went[wn - 1];
+                    went[wn - 1] = FoldEnt{lo, tr_sat(pe.a0 + ks), tr_sat(pe.a1 + ks), last_end};
+                  }
+                } else {
+                  if (lane == 0 && wn < CL_EW) went[wn] = FoldEnt{lo, ks, ks, last_end};
+                  ++wn;
+                  if (wn > CL_EW) over = true;
+                }
+                lkey = lo;
+                done = true;
+              }
+            }
+          }
+          if (!done) {
+            // per element, 32 at a time in row order: its approximate state
+            // decides a run of its binade or an explicit element (near a
+            // binade edge, or large next to the state); the approximate exp
+            // decides each increment where it can, the exact exp is taken
+            // for explicit elements and undecided increments.  Runs are
+            // summed over the lanes (composed, when some element is a tie).
+            float sbj = sb;
+#pragma unroll 1
+            for (int j = 0; j * 32 < n && !over; ++j) {
+              const int i = j * 32 + lane;
+              const int nj = n - j * 32 < 32 ? n - j * 32 : 32;
+              const bool valid = i < n;
+              float zj = 0.0f, eaj = 0.0f;
+#pragma unroll
+              for (int r = 0; r < CL_R; ++r) {
+                zj = r == j ? z[r] : zj;
+                eaj = r == j ? ea[r] : eaj;
+              }
+              const uint32_t idx = valid ? qidx[(head + i) & (CL_RING - 1)] : 0u;
+              const float incl = warp_incl_scan_add(eaj);
+              float excl = __shfl_up_sync(PESTI_FULL_MASK, incl, 1);
+              if (lane == 0) excl = 0.0f;
+              const float av = sbj + excl;  // approximate state before the element
+              const float bv = av + eaj;    // and after it
+              const float dej = fmaf(-zj, DE_Z, DE_0);
+              uint32_t key = KEY_NONE, k0 = 0u, k1 = 0u;
+              if (valid) {
+                bool special = !(av >= 0x1p-126f);
+                uint32_t lo = 0u;
+                float lov = 0.0f;
+                if (!special) {
+                  lo = fbits(av) & 0x7f800000u;
+                  lov = bitsf(lo);
+                  special = eaj * (1.0f + dej) >= 0.5f * lov || av < lov * (1.0f + BAND) ||
+                            bv > 2.0f * lov * (1.0f - BAND);
+                }
+                bool need = special;
+                if (!special) {
+                  const uint32_t E = lo >> 23;
+                  if (eaj == 0.0f) {
+                    need = E < 40u;  // else the exact value (< 2^-126) rounds to 0 on this grid
+                  } else {
+                    const float tt = __uint_as_float(fbits(eaj) + ((uint32_t)(150 - (int)E) << 23));  // ea/w
+                    const float kr = rintf(tt);
+                    need = !(0.5f - fabsf(tt - kr) > tt * dej + 0x1p-24f);
+                    k0 = k1 = (uint32_t)kr;
+                  }
+                }
+                if (need) {
+                  const float ex = pesti_expf_call(zj);  // sampling.rs:127, exact
+                  if (special) {
+                    k0 = fbits(ex);
+                  } else {
+                    k0 = fbits(fadd(lov, ex)) - lo;
+                    k1 = fbits(fadd(bitsf(lo + 1u), ex)) - (lo + 1u);
+                  }
+                }
+                key = special ? fold::SPECIAL : lo;
+              }
+              uint32_t pkey = __shfl_up_sync(PESTI_FULL_MASK, key, 1);
+              if (lane == 0) pkey = lkey;
+              const bool hd = valid && (key == fold::SPECIAL || pkey == fold::SPECIAL || pkey == KEY_NONE || key != pkey);
+              // lane 0 may continue the warp's last entry (a run of the same binade)
+              const bool cont = __shfl_sync(PESTI_FULL_MASK, valid && !hd, 0);
+              const bool nhd = __shfl_down_sync(PESTI_FULL_MASK, hd, 1);
+              const bool is_end = valid && (lane == nj - 1 || nhd);
+              const uint32_t ends = __ballot_sync(PESTI_FULL_MASK, is_end);
+              const int base = cont ? wn - 1 : wn;
+              const int slot = base + __popc(ends & ((1u << lane) - 1u));
+              const bool tie = valid && key != fold::SPECIAL && k0 != k1;
+              if (!__any_sync(PESTI_FULL_MASK, tie)) {
+                // plain integer increments: a run is a difference of prefix sums
+                const uint32_t H = __ballot_sync(PESTI_FULL_MASK, hd || lane == 0);
+                const uint32_t kk = valid && key != fold::SPECIAL ? k0 : 0u;
+                const uint32_t sc = warp_incl_scan_add(kk);
+                const int st = 31 - __clz(H & (0xffffffffu >> (31 - lane)));  // the run's first lane
+                const uint32_t pre = __shfl_sync(PESTI_FULL_MASK, sc, st > 0 ? st - 1 : 0);
+                uint32_t run = tr_sat(sc - (st > 0 ? pre : 0u));
+                if (is_end && slot < CL_EW) {
+                  if (key == fold::SPECIAL) {
+                    went[slot] = FoldEnt{key, k0, 0u, idx + 1u};
+                  } else if (st == 0 && cont) {
+                    const FoldEnt pe = went[slot];
+                    went[slot] = FoldEnt{key, tr_sat(pe.a0 + run), tr_sat(pe.a1 + run), idx + 1u};
+                  } else {
+                    went[slot] = FoldEnt{key, run, run, idx + 1u};
+                  }
+                }
+              } else {
+                // some element is a tie: compose the (even, odd) increments
+                Seg v{k0, k1, 1u, key};
+                if (cont && lane == 0) {
+                  const FoldEnt pe = went[wn - 1];
+                  const Tr t = tr_compose(Tr{pe.a0, pe.a1}, Tr{k0, k1});
+                  v = Seg{t.a0, t.a1, 1u, key};
+                }
+                Seg inc = v;
+                bool flg = hd || lane == 0;
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                  const Seg o2 = seg_shfl_up(inc, off);
+                  const bool of = __shfl_up_sync(PESTI_FULL_MASK, flg, off);
+                  if (lane >= off) {
+                    inc = seg_join(o2, inc, flg);
+                    flg = flg || of;
+                  }
+                }
+                if (is_end && slot < CL_EW) went[slot] = FoldEnt{key, inc.a0, inc.a1, idx + 1u};
+              }
+              wn = base + __popc(ends);
+              if (wn > CL_EW) over = true;
+              lkey = __shfl_sync(PESTI_FULL_MASK, key, nj - 1);
+              sbj += __shfl_sync(PESTI_FULL_MASK, incl, 31);
+              __syncwarp();
+            }
+          }
+          s_run += (double)btot;
+          head += (uint32_t)n;
+          __syncwarp();
+        }
+      }
+    }
+    if (VEC) cp_async_wait<0>();
+    if (lane == 0) sh.wn[w] = over ? -1 : wn;
+  }
+  __syncthreads();
+
+  // ---------------- the CTA's entries, merged, in row order ----------------
+  if (decided < 0 && tid == 0) {
+    int nl = 0;
+    uint32_t last = KEY_NONE;
+    bool full = false;
+    const long long cta_end = ((long long)(cr + 1) * CL_WARPS * a.SLW) < V ? (long long)(cr + 1) * CL_WARPS * a.SLW : V;
+    for (int q = 0; q < CL_WARPS && !full; ++q) {
+      const long long ws0 = (long long)(cr * CL_WARPS + q) * a.SLW;
+      if (ws0 >= V) break;
+      const int n = sh.wn[q];
+      if (n < 0) {
+        const long long we = ws0 + a.SLW < V ? ws0 + a.SLW : V;
+        if (nl < CL_LIST) sh.list[nl++] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)we};
+        else full = true;
+        last = ENT_REPLAY;
+        continue;
+      }
+      for (int i = 0; i < n; ++i) {
+        const FoldEnt e = sh.u.c.went[q][i];
+        if (e.lo != fold::SPECIAL && e.lo == last) {
+          const Tr t = tr_compose(Tr{sh.list[nl - 1].a0, sh.list[nl - 1].a1}, Tr{e.a0, e.a1});
+          sh.list[nl - 1] = FoldEnt{e.lo, t.a0, t.a1, e.end};
+        } else if (nl < CL_LIST) {
+          sh.list[nl++] = e;
+        } else {
+          full = true;
+          break;
+        }
+        last = e.lo;
+      }
+    }
+    if (full) {  // too many entries: the walk folds the CTA's whole range
+      sh.list[0] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)cta_end};
+      nl = 1;
+    }
+    sh.nlist = nl;
+  }
+  cl.sync();
+
+  // ---------------- the leader gathers the row's entries and candidates ----------------
+  if (cr == 0 && decided < 0) {
+    // the CTAs' counts, their offsets in the row (warp 0, one lane per CTA)
+    if (w == 0) {
+      int ne_c = 0, nc_c = 0;
+      if (lane < C) {
+        ne_c = *cl.map_shared_rank(&sh.nlist, lane);
+        nc_c = *cl.map_shared_rank(&sh.ncand, lane);
+      }
+      const bool bad = __any_sync(PESTI_FULL_MASK, nc_c > CL_CCAP);
+      const int ein = warp_incl_scan_add(ne_c);
+      const int cin = warp_incl_scan_add(nc_c);
+      if (lane < C) {
+        sh.u.f.ccnt[lane] = ein - ne_c;
+        sh.u.f.coff[lane] = cin - nc_c;
+      }
+      const int ne = __shfl_sync(PESTI_FULL_MASK, ein, 31);
+      const int ncd = __shfl_sync(PESTI_FULL_MASK, cin, 31);
+      if (lane == 0) {
+        sh.u.f.ccnt[C] = ne;
+        sh.u.f.coff[C] = ncd;
+        sh.u.f.nent = ne;
+        sh.u.f.ncand = ncd;
+        sh.status = (bad || ne > CL_LOCAL || ncd > FAST_CAND || ncd < keff) ? 1 : 0;
+      }
+    }
+    __syncthreads();
+    if (sh.status == 0) {
+      const int ne = sh.u.f.nent, ncd = sh.u.f.ncand;
+      for (int i = tid; i < ne; i += CL_NT) {
+        int c = 0;
+        while (i >= sh.u.f.ccnt[c + 1]) ++c;
+        sh.u.f.ent[i] = *cl.map_shared_rank(&sh.list[i - sh.u.f.ccnt[c]], c);
+      }
+      for (int i = tid; i < ncd; i += CL_NT) {
+        int c = 0;
+        while (i >= sh.u.f.coff[c + 1]) ++c;
+        const int j = i - sh.u.f.coff[c];
+        const float e = *cl.map_shared_rank(&sh.cand_e[j], c);
+        const uint32_t ix = *cl.map_shared_rank(&sh.cand_i[j], c);
+        sh.u.f.key[i] = ((unsigned long long)fbits(e) << 32) | (unsigned long long)(~ix);
+      }
+    }
+  }
+  cl.sync();  // after this the other CTAs' shared memory is no longer read
+  if (cr != 0) return;
+
+  // ---------------- leader: walk, top-k, draw ----------------
+  int status = decided < 0 ? sh.status : decided;
+  if (decided == 0 && greedy) {  // generate(): temperature == 0 -> argmax (model.rs:517-521)
+    if (w == 0) {
+      const uint32_t tok = (prm.flags & PESTI_FLAG_ARGMAX_FIRST) ? (first_max >= 0 ? (uint32_t)first_max : 0u)
+                                                                 : (last_max >= 0 ? (uint32_t)last_max : 0u);
+      if (lane == 0) {
+        a.out[b] = tok;
+        if (a.kept_count) a.kept_count[b] = 0;
+        a.fb[b] = 0;
+      }
+      cl_write_pad(a, b, 0);
+    }
+    return;
+  }
+  const int ncd = decided < 0 ? sh.u.f.ncand : 0;
+  if (status == 0) {
+    if (w == 1) {  // candidates by (e desc, index asc) while warp 0 walks
+      unsigned long long* key = sh.u.f.key;
+      if (ncd <= 32) warp_sort_keys<1>(key, ncd);
+      else if (ncd <= 64) warp_sort_keys<2>(key, ncd);
+      else if (ncd <= 128) warp_sort_keys<4>(key, ncd);
+      else {
+        int mm2 = 1;
+        while (mm2 < ncd) mm2 <<= 1;
+        for (int j = ncd + lane; j < mm2; j += 32) key[j] = 0ull;
+        __syncwarp();
+        warp_bitonic_desc(key, mm2);
+      }
+    }
+    if (w == 0) {
+      // softmax denominator (sampling.rs:128): the entries with the exact state;
+      // an entry the state does not fit (or a replay marker) is folded from the
+      // raw logits of its range, from the state before it
+      const FoldEnt* fent = sh.u.f.ent;
+      const int nm = sh.u.f.nent;
+      uint32_t s = 0u;
+      constexpr int WB = 8;
+      int i = 0;
+      while (i < nm) {
+        int fi = -1;
+        FoldEnt nx[WB];
+#pragma unroll
+        for (int uu = 0; uu < WB; ++uu) nx[uu] = fent[i + uu < nm ? i + uu : nm - 1];
+        for (; i < nm; i += WB) {
+          FoldEnt en[WB];
+#pragma unroll
+          for (int uu = 0; uu < WB; ++uu) {
+            en[uu] = nx[uu];
+            const int kk = i + WB + uu;
+            nx[uu] = fent[kk < nm ? kk : nm - 1];
+          }
+#pragma unroll
+          for (int uu = 0; uu < WB; ++uu) {
+            const bool live = fi < 0 && i + uu < nm;
+            const bool sp = en[uu].lo == fold::SPECIAL;
+            const uint32_t s_sp = fbits(fadd(bitsf(s), bitsf(en[uu].a0)));
+            const uint32_t ns = s + ((s & 1u) ? en[uu].a1 : en[uu].a0);
+            const bool fits = fold::binade_lo_bits(s) == en[uu].lo && ns < fold::binade_hi_bits(en[uu].lo);
+            fi = live && !sp && !fits ? i + uu : fi;
+            s = live && (sp || fits) ? (sp ? s_sp : ns) : s;
+          }
+          if (fi >= 0) break;
+        }
+        if (fi < 0) break;
+        const uint32_t from = fi > 0 ? fent[fi - 1].end : 0u;
+        const uint32_t to = fent[fi].end;
+        s = warp_fold(row + from, a.dtype, (long long)to - from, s, sh.u.f.stage, scale, T, m);
+        i = fi + 1;
+      }
+      sh.uscr[0] = s;
+    }
+    __syncthreads();
+    if (w == 0) {
+      const float S = bitsf(sh.uscr[0]);
+      unsigned long long* key = sh.u.f.key;
+      // p = e/S (sampling.rs:130); the list stays sorted by p except inside
+      // groups of equal p, which the stable sort (sampling.rs:60) orders by index
+      for (int j = lane; j < ncd; j += 32) {
+        const unsigned long long kv = key[j];
+        key[j] = ((unsigned long long)fbits(fdiv(bitsf((uint32_t)(kv >> 32)), S)) << 32) | (kv & 0xffffffffull);
+      }
+      __syncwarp();
+      bool viol = false;
+      for (int j = lane; j + 1 < ncd; j += 32) viol |= key[j] < key[j + 1];
+      if (__any_sync(PESTI_FULL_MASK, viol)) {
+        if (lane == 0) {  // insertion sort: only equal-p groups are out of order
+          for (int j = 1; j < ncd; ++j) {
+            const unsigned long long kv = key[j];
+            int t = j - 1;
+            while (t >= 0 && key[t] < kv) {
+              key[t + 1] = key[t];
+              --t;
+            }
+            key[t + 1] = kv;
+          }
+        }
+        __syncwarp();
+      }
+      // every element below the candidates (raw < tau) must rank below the keff-th
+      const float pk = bitsf((uint32_t)(key[keff - 1] >> 32));
+      const bool ok = !(S > 0.0f) ? false : fdiv(sh.e_tau, S) < pk;
+      if (ok) {
+        const uint32_t r_tau = fold::tau_bits_of(a.u ? a.u[b] : 0.0f);
+        float* q = sh.u.f.q;
+        for (long long j = lane; j < keff; j += 32) q[j] = bitsf((uint32_t)(key[j] >> 32));
+        __syncwarp();
+        uint32_t tb = 0u;
+        if (lane == 0) tb = serial_fold8(q, keff, 0u, fold::NO_QUERY, false).s_bits;  // sampling.rs:81
+        const float total = bitsf(__shfl_sync(PESTI_FULL_MASK, tb, 0));
+        for (long long j = lane; j < keff; j += 32) q[j] = fdiv(q[j], total);  // sampling.rs:94
+        __syncwarp();
+        if (lane == 0) {
+          const fold::Result dr = serial_fold8(q, keff, 0u, r_tau, true);  // sampling.rs:99-105
+          const long long at = dr.hit >= 0 ? dr.hit : keff - 1;           // sampling.rs:108-111
+          a.out[b] = ~(uint32_t)(key[at] & 0xffffffffull);
+          if (a.kept_count) a.kept_count[b] = keff;
+        }
+        for (long long j = lane; j < a.kept_width; j += 32) {
+          const bool in = j < keff;
+          const unsigned long long kv = in ? key[j] : 0ull;
+          if (a.kept_p) a.kept_p[b * a.kept_width + j] = in ? bitsf((uint32_t)(kv >> 32)) : 0.0f;
+          if (a.kept_idx) a.kept_idx[b * a.kept_width + j] = in ? ~(uint32_t)(kv & 0xffffffffull) : 0xffffffffu;
+        }
+      }
+      if (lane == 0) sh.status = ok ? 0 : 1;
+    }
+    __syncthreads();
+    status = sh.status;
+  }
+  if (tid == 0) {
+    a.fb[b] = status;
+    if (status) {  // the row kernel's generic path takes the row: its prologue
+      RowInfo ri;
+      ri.max_raw = sh.max_raw;
+      ri.m = sh.m;
+      ri.tau = INF;
+      ri.flags = sh.flags;
+      ri.last_max = sh.last_max;
+      ri.first_max = sh.first_max;
+      ri.last_nan = sh.last_nan;
+      ri.uniform = ((sh.flags & MF_NAN) || (scale && T == INF && (sh.flags & (MF_POSINF | MF_NEGINF))) ||
+                    !(fabsf(sh.m) < INF)) ? 1 : 0;
+      ri.e_tau = 0.0f;
+      ri.s_start = 0.0f;
+      a.info[b] = ri;
+    }
+  }
+}
+
+}  // namespace pesti

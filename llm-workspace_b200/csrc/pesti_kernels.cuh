@@ -220,6 +220,9 @@ struct RowArgs {
   int ksh;
   FoldEnt* ment_g;         // [B][FAST_ENTS] merged fold entries
   int* nment_g;            // [B] their count (-1: the row is not sampled from shards)
+  // rows left by the cluster pass (only != null): a block samples its row only
+  // when only[b] != 0, from the whole row (no survivor lists) on the generic path
+  const int* only;
 };
 
 // Exchange record of one row of one vocabulary shard (second phase).
@@ -2357,6 +2360,7 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
   RowShared& sh = *reinterpret_cast<RowShared*>(row_smem);
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const long long b = blockIdx.x;
+  if (a.only && a.only[b] == 0) return;  // the cluster pass sampled the row
   const long long V = a.V;
   const pesti_sampling_params prm = row_params(a.uni, a.per_row, b);
   const RowInfo ri = a.info[b];
@@ -2729,14 +2733,15 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
 
   // largest dropped logit -> an upper bound of the exp of every dropped element
   float pm = -INF;
-  for (int s = tid; s < nsub; s += K2_NT)
-    if ((long long)s * a.SL < V) pm = fmaxf(pm, survs[s].pruned_max);
+  if (!a.only)
+    for (int s = tid; s < nsub; s += K2_NT)
+      if ((long long)s * a.SL < V) pm = fmaxf(pm, survs[s].pruned_max);
   pm = -block_reduce_min(-pm, sh.fscr);
   const float e_pruned = pm > -INF ? pesti_expf(fsub(scale ? fdiv(pm, T) : pm, m)) : 0.0f;
 
   // ---------------- generic path ----------------
   // rows of the fast path have no survivor list: all their elements
-  bool dense_all = a.fast_enabled && fast_topk(prm, V);
+  bool dense_all = a.only != nullptr || (a.fast_enabled && fast_topk(prm, V));
   for (int attempt = 0; attempt < 2; ++attempt) {
     for (int s = tid; s < nsub; s += K2_NT) {
       const long long st = (long long)s * a.SL;

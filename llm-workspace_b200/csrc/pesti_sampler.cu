@@ -18,6 +18,7 @@
 #include "../../include/pesti_profile.h"
 #include "../../include/pesti_testing.h"
 #include "pesti_kernels.cuh"
+#include "pesti_cluster.cuh"
 #include "pesti_noalloc.h"
 #include "pesti_shard.cuh"
 #include "pesti_rng.cuh"
@@ -213,7 +214,7 @@ struct Plan {
   bool survivors = true;  // some row may need the survivor pass (not on the fast path)
   size_t o_ctr, o_stats, o_pre, o_info, o_surv, o_segmax, o_upre, o_se, o_si, o_cc, o_ce, o_ci;
   size_t o_gsurv, o_inext, o_tasks, o_tctr, o_pctr, o_pool;
-  size_t o_E, o_I, o_status;
+  size_t o_E, o_I, o_status, o_fb;
   size_t o_sk0 = 0, o_sv0 = 0, o_sk1 = 0, o_sv1 = 0, o_q = 0;
   size_t bytes;  // workspace the call needs
 };
@@ -251,6 +252,7 @@ Plan make_plan(int num_sms, pesti_dtype dtype, long long B, long long V, bool so
   p.o_E = take(bv * 4);
   p.o_I = take(bv * 4);
   p.o_status = take(16);
+  p.o_fb = take((size_t)B * sizeof(int));
   p.o_gsurv = take(ngrp * sizeof(pesti::GroupEnt));
   p.o_inext = take(sizeof(int));
   p.o_tasks = take(ngrp * sizeof(pesti::ClassTask));
@@ -493,10 +495,168 @@ int run_plan(const Plan& p, char* ws, int device, cudaEvent_t* pev, const void* 
   return PESTI_OK;
 }
 
+// ---------------------------------------------------------------------------
+// The cluster pass: one thread-block cluster per row (pesti_cluster.cuh), then
+// the row kernel for the rows it leaves (usually none: its blocks return at
+// once).  Used when every row is greedy or on the top-k fast path and rows are
+// at most CL_MAX_V long.
+// ---------------------------------------------------------------------------
+std::atomic<int> g_cluster_override{0};  // pesti_testing_set_cluster
+
+using ClusterKernel = void (*)(pesti::ClusterArgs);
+
+ClusterKernel cluster_kernel_for(pesti_dtype dtype, bool aligned) {
+  if (dtype == PESTI_F16) return aligned ? pesti::row_cluster_kernel<__half, 8, true> : pesti::row_cluster_kernel<__half, 8, false>;
+  if (dtype == PESTI_BF16)
+    return aligned ? pesti::row_cluster_kernel<uint16_t, 8, true> : pesti::row_cluster_kernel<uint16_t, 8, false>;
+  return aligned ? pesti::row_cluster_kernel<float, 4, true> : pesti::row_cluster_kernel<float, 4, false>;
+}
+
+// Largest cluster (16 or 8 CTAs) the device runs this kernel with; 16 needs
+// the non-portable size, allowed once per device and kernel.
+constexpr int kClusterKinds = 6;
+std::atomic<int> g_cluster_max[kMaxDevices][kClusterKinds];
+
+int cluster_max_for(int device, ClusterKernel kern, int kind) {
+  const bool cached = device >= 0 && device < kMaxDevices;
+  if (cached) {
+    const int v = g_cluster_max[device][kind].load(std::memory_order_acquire);
+    if (v) return v;
+  }
+  int best = 8;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(16);
+    cfg.blockDim = dim3(pesti::CL_NT);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 16;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) best = 16;
+  }
+  cudaGetLastError();  // a refused query leaves no error behind
+  if (cached) g_cluster_max[device][kind].store(best, std::memory_order_release);
+  return best;
+}
+
+struct ClusterGeom {
+  int C;    // CTAs per row
+  int SLW;  // elements per warp
+};
+
+// Cluster size and warp range for rows of V elements: 16 CTAs for short
+// batches (latency), 8 otherwise, each warp at most CL_SEGS segments.
+bool cluster_geometry(long long B, long long V, int esize, int cmax, ClusterGeom& g) {
+  const long long seg = 32LL * (16 / esize);
+  const int forced = g_cluster_override.load(std::memory_order_relaxed);
+  int C = forced > 0 ? forced : (B <= 16 ? 16 : 8);
+  if (C > cmax) C = cmax;
+  auto slw = [&](int c) {
+    const long long per = (V + (long long)c * pesti::CL_WARPS - 1) / ((long long)c * pesti::CL_WARPS);
+    return (per + seg - 1) / seg * seg;
+  };
+  if (forced <= 0 && slw(C) > pesti::CL_SEGS * seg && cmax >= 16) C = 16;
+  // no more CTAs than the row has warp ranges for
+  const long long need = (V + pesti::CL_WARPS * seg - 1) / (pesti::CL_WARPS * seg);
+  if ((long long)C > need && forced <= 0) C = (int)std::max(1LL, need);
+  const long long L = slw(C);
+  if (L > pesti::CL_SEGS * seg) return false;
+  g.C = C;
+  g.SLW = (int)L;
+  return true;
+}
+
+bool use_cluster_path(long long V, bool survivors) {
+  return !survivors && V >= 1 && V <= pesti::CL_MAX_V && g_cluster_override.load(std::memory_order_relaxed) >= 0;
+}
+
+int run_cluster(const Plan& p, const ClusterGeom& cgm, char* ws, int device, cudaEvent_t* pev,
+                const void* d_logits, pesti_dtype dtype, long long B, long long V, long long ld,
+                const pesti_sampling_params& uni, const pesti_sampling_params* d_per_row, const float* d_u,
+                uint32_t* d_out, float* d_kept_p, uint32_t* d_kept_idx, long long kept_width,
+                int64_t* d_kept_count, cudaStream_t st) {
+  const bool aligned = rows_aligned(d_logits, dtype, ld);
+  pesti::ClusterArgs ca{};
+  ca.logits = d_logits;
+  ca.dtype = (int)dtype;
+  ca.B = B;
+  ca.V = V;
+  ca.ld = ld;
+  ca.uni = uni;
+  ca.per_row = d_per_row;
+  ca.SLW = cgm.SLW;
+  ca.u = d_u;
+  ca.out = d_out;
+  ca.kept_p = d_kept_p;
+  ca.kept_idx = d_kept_idx;
+  ca.kept_width = (d_kept_p || d_kept_idx) ? kept_width : 0;
+  ca.kept_count = d_kept_count;
+  ca.fb = (int*)(ws + p.o_fb);
+  ca.info = (pesti::RowInfo*)(ws + p.o_info);
+  ca.band = 0x1p-12f;
+  // a short batch lets the row kernel's few blocks be scheduled while the
+  // cluster pass runs (they wait for it on the device), hiding that launch
+  ca.early_dependents = B <= 16 ? 1 : 0;
+  if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[0], st), "cudaEventRecord(profile)");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(B * cgm.C));
+  cfg.blockDim = dim3(pesti::CL_NT);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cgm.C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, cluster_kernel_for(dtype, aligned), ca);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "row_cluster_kernel launch");
+  if (pev) {
+    PESTI_CUDA_TRY(cudaEventRecord(pev[1], st), "cudaEventRecord(profile)");
+    PESTI_CUDA_TRY(cudaEventRecord(pev[2], st), "cudaEventRecord(profile)");
+  }
+  // the rows the cluster pass left: the row kernel's generic path over whole rows
+  pesti::SliceArgs sa = make_slice_args(p, ws, d_logits, dtype, B, V, ld, uni, d_per_row);
+  sa.fast_enabled = 0;
+  pesti::RowArgs ra = make_row_args(p, ws, sa, d_u, d_out, d_kept_p, d_kept_idx, kept_width, d_kept_count);
+  ra.only = ca.fb;
+  ra.fast_enabled = 0;
+  int rc = launch_row(p, device, ra, st);
+  if (rc) return rc;
+  if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[3], st), "cudaEventRecord(profile)");
+  return PESTI_OK;
+}
+
 int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long B, long long V,
            long long ld, const pesti_sampling_params& uni, const pesti_sampling_params* d_per_row,
            bool sorted_bufs, bool survivors, const float* d_u, uint32_t* d_out, float* d_kept_p,
            uint32_t* d_kept_idx, long long kept_width, int64_t* d_kept_count, cudaStream_t st) {
+  const int esize = dtype == PESTI_F32 ? 4 : 2;
+  ClusterGeom cgm{};
+  if (use_cluster_path(V, survivors)) {
+    const int kind = (int)dtype * 2 + (rows_aligned(d_logits, dtype, ld) ? 1 : 0);
+    const int cmax = cluster_max_for(s->device, cluster_kernel_for(dtype, kind & 1), kind);
+    if (cluster_geometry(B, V, esize, cmax, cgm)) {
+      // the row kernel's generic path may take any row: whole-row buffers
+      Plan p = make_plan(s->num_sms, dtype, B, V, true);
+      int rc = ensure_ws(s, p.bytes);
+      if (rc) return rc;
+      cudaEvent_t* pev = nullptr;
+      if (s->prof && s->prof_n < pesti_sampler::kProfMax) {
+        pev = s->prof_ev[s->prof_n++];
+        for (int q = 0; q < 4; ++q)
+          if (!pev[q]) PESTI_CUDA_TRY(cudaEventCreate(&pev[q]), "cudaEventCreate(profile)");
+      }
+      return run_cluster(p, cgm, (char*)s->ws, s->device, pev, d_logits, dtype, B, V, ld, uni, d_per_row, d_u,
+                         d_out, d_kept_p, d_kept_idx, kept_width, d_kept_count, st);
+    }
+  }
   Plan p = make_plan(s->num_sms, dtype, B, V, sorted_bufs);
   p.survivors = survivors;
   int rc = ensure_ws(s, p.bytes);
@@ -1266,6 +1426,13 @@ int pesti_sample_batch_sharded_emulated(pesti_sampler* s, int shards, const void
 }
 
 int64_t pesti_last_gathered_rows(pesti_sampler* s) { return s ? s->last_gathered_rows : -1; }
+
+int pesti_testing_set_cluster(int mode) {
+  if (mode != -1 && mode != 0 && !(mode >= 1 && mode <= pesti::CL_MAXC))
+    return fail(PESTI_E_INVALID_ARG, "cluster mode must be -1, 0 or 1..16");
+  g_cluster_override.store(mode, std::memory_order_relaxed);
+  return PESTI_OK;
+}
 
 int pesti_pcg32_seed(uint64_t* d_state, int64_t B, uint64_t seed, uint64_t first_stream, void* stream) {
   if (B < 0) return fail(PESTI_E_INVALID_ARG, "B < 0");

@@ -126,6 +126,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.pesti_last_gathered_rows.restype = i64
     lib.pesti_last_gathered_reasons.argtypes = [vp, vp]
     lib.pesti_last_gathered_reasons.restype = c_int
+    lib.pesti_testing_set_cluster.argtypes = [c_int]
+    lib.pesti_testing_set_cluster.restype = c_int
     _lib = lib
     return lib
 
@@ -448,6 +450,13 @@ class Comm:
             self.close()
         except Exception:
             pass
+
+
+def set_cluster_mode(mode: int) -> None:
+    """pesti_testing_set_cluster: -1 sends greedy/top-k batches through the
+    four-kernel pipeline instead of the cluster pass, 1..16 forces that many
+    CTAs per row's cluster, 0 restores the default (process-wide)."""
+    _check(load_library().pesti_testing_set_cluster(int(mode)))
 
 
 NOALLOC_SCRATCH_BYTES = 64 << 20  # PESTI_NOALLOC_SCRATCH_BYTES

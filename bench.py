@@ -78,13 +78,19 @@ L2_BYTES = 126 * 1024 * 1024
 TRAFFIC_PER_STEP = {}
 
 
-def cluster_pass(V, params):
-    """The batch takes the cluster pass: every row greedy (T == 0) or top-k
-    <= 256, rows of at most 131072 columns."""
-    return 1 <= V <= 131072 and all(t == 0.0 or 1 <= k <= 256 for (t, _, k) in params)
+def cluster_pass(V, params, bf16=False):
+    """The batch takes the cluster pass: every row greedy (T == 0), top-k
+    <= 256 or (bf16) top-p, rows of at most 131072 columns (262144 for bf16),
+    and either some bf16 top-p row or at most 32 rows."""
+    if not 1 <= V <= (262144 if bf16 else 131072):
+        return False
+    nuc = [bf16 and k == 0 and p > 0 for (t, p, k) in params]
+    if not all(t == 0.0 or 1 <= k <= 256 or n for (t, p, k), n in zip(params, nuc)):
+        return False
+    return any(nuc) or len(params) <= 32
 
 
-def kernels_per_step(V, params):
+def kernels_per_step(V, params, bf16=False):
     """This library's launches in one step.  The cluster pass: the cluster
     kernel and the row kernel (whose blocks return at once unless the cluster
     left their row).  Otherwise: the HBM pass; the fused pass (rows beyond 128k
@@ -92,7 +98,7 @@ def kernels_per_step(V, params):
     on the top-k fast path), plus the survivor pass when some row is off that
     path, else the survivor pass and the task-queue classification; the row
     kernel."""
-    if cluster_pass(V, params):
+    if cluster_pass(V, params, bf16):
         return 2
     off_fast = any(not (1 <= k <= 256) or t <= 0 for (t, _, k) in params)
     fused = V > 131072 or (V <= 65536 and not off_fast and len(params) >= 32)
@@ -651,7 +657,7 @@ def main():
                          "threads; C++ restatement of sampling.rs:39-134 with glibc expf"}
 
     if rank == 0:
-        nk = kernels_per_step(V, params)
+        nk = kernels_per_step(V, params, bf16)
         line = {
             "metric": metric_for(w), "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -665,7 +671,7 @@ def main():
                          "traffic": TRAFFIC_PER_STEP.get(w) if world == 1 else None,
                          "bytes_per_launch": step_bytes,
                          "kernels": ({"row_cluster": kern(scan_ms), "row (rows the cluster pass left)": kern(row_ms)}
-                                     if cluster_pass(V, params) else
+                                     if cluster_pass(V, params, bf16) else
                                      {"slice_stats": kern(scan_ms), "survivor+classify": kern(surv_ms),
                                       "row": kern(row_ms)})},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": step_bytes + B * 4,

@@ -185,6 +185,24 @@ typedef struct pesti_comm pesti_comm;
 #define PESTI_COMM_ID_BYTES 128
 int pesti_comm_id(void* id);
 int pesti_comm_create(int world_size, int rank, const void* id, int device, pesti_comm** out);
+/*
+ * No counterpart in the reference, whose only failure detection is the HTTP
+ * health check of a remote runner with a 3 s limit
+ * (llm-runner/src/remote_discovery.rs:36-70).
+ *
+ * pesti_comm_create with a deadline (pesti_comm_create uses 120000 ms).  The
+ * communicator is made non-blocking (ncclCommInitRankConfig with blocking = 0)
+ * and its set-up is polled with ncclCommGetAsyncError: if every rank has not
+ * joined after timeout_ms, the set-up is aborted (ncclCommAbort) and the call
+ * returns PESTI_E_TIMEOUT, so a rank that exits or never starts does not hang
+ * the others.  The same deadline bounds, on the host, each
+ * pesti_sample_batch_sharded call's exchanges: a call whose all-gathers do not
+ * complete within timeout_ms of its start, or that reports an NCCL error,
+ * aborts the communicator and returns PESTI_E_TIMEOUT (or PESTI_E_NCCL);
+ * every later call on that communicator fails with PESTI_E_NCCL, and
+ * pesti_comm_destroy releases it.
+ */
+int pesti_comm_create_timed(int world_size, int rank, const void* id, int device, int timeout_ms, pesti_comm** out);
 void pesti_comm_destroy(pesti_comm* c);
 int pesti_sample_batch_sharded(pesti_sampler* s, pesti_comm* c, const void* d_logits, pesti_dtype dtype,
                                int64_t B, int64_t V_shard, int64_t ld, const pesti_sampling_params* params,

@@ -29,11 +29,13 @@ int64_t pesti_last_gathered_rows(pesti_sampler* s);
  * candidates could not prove the top-k. */
 int pesti_last_gathered_reasons(pesti_sampler* s, int64_t* counts);
 
-/* Batches of greedy and top-k (<= 256) rows of at most 131072 columns take
- * the cluster pass (one thread-block cluster per row) by default.  mode -1
- * sends them through the four-kernel pipeline instead, 1..16 forces that
- * many CTAs per row's cluster (when the rows allow it), 0 restores the
- * default.  Process-wide; for tests and measurements. */
+/* The cluster pass (one thread-block cluster per row) takes batches of at
+ * most 32 greedy and top-k (<= 256) rows, and every batch with bf16 top-p
+ * rows (rows of at most 131072 f32 or 262144 16-bit columns).  mode -1 sends
+ * every batch through the four-kernel pipeline instead, 1..16 sends every
+ * batch the cluster pass can take through it with that many CTAs per row's
+ * cluster, 0 restores the default.  Process-wide; for tests and
+ * measurements. */
 int pesti_testing_set_cluster(int mode);
 
 /* The largest relative error of the hardware 2^y approximation

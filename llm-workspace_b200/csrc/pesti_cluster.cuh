@@ -3,7 +3,9 @@
 // generate, transformer/model.rs:517-521).
 //
 // The row is split over the cluster's CTAs and their warps; warp g (in row
-// order, over the CTAs by rank) owns the contiguous range [g*SLW, (g+1)*SLW).
+// order, over the CTAs by rank) owns the contiguous range [wstart[g], wstart[g+1]).
+// The first warps of a row get shorter ranges: there the running sum is small,
+// most elements survive the pruning and the state crosses binades often.
 // The CTAs exchange their partial results through distributed shared memory
 // and cluster barriers, so nothing crosses a kernel boundary:
 //
@@ -45,7 +47,7 @@ namespace cg = cooperative_groups;
 constexpr int CL_WARPS = 8;             // warps per CTA
 constexpr int CL_NT = CL_WARPS * 32;
 constexpr int CL_MAXC = 16;             // CTAs per cluster (row)
-constexpr int CL_SEGS = 16;             // 32*VE-element segments per warp at most
+constexpr int CL_SEGS = 20;             // 32*VE-element segments per warp at most
 constexpr int CL_U = 4;                 // segments loaded at once per warp (pass 1)
 constexpr int CL_STAGES = 4;            // segments in flight per warp through shared memory (pass 2)
 constexpr int CL_R = 4;                 // survivors per lane in one classification batch
@@ -55,7 +57,9 @@ constexpr int CL_EW = 48;               // fold entries per warp (beyond: its ra
 constexpr int CL_LIST = 128;            // merged fold entries per CTA (beyond: its range is replayed)
 constexpr int CL_CCAP = 256;            // top-k candidates per CTA
 constexpr int CL_LOCAL = 512;           // fold entries of a row the leader gathers
-constexpr long long CL_MAX_V = 131072;  // longest row of the cluster path
+constexpr long long CL_MAX_V = 131072;  // longest row of the cluster path (f32)
+constexpr long long CL_MAX_V16 = 262144;  // the same for 16-bit logits
+static_assert(CL_SEGS <= 32, "one lane per segment in the warp summary");
 
 struct ClusterArgs {
   const void* logits;
@@ -63,7 +67,9 @@ struct ClusterArgs {
   long long B, V, ld;
   pesti_sampling_params uni;
   const pesti_sampling_params* per_row;
-  int SLW;            // elements per warp: a multiple of 32*VE, at most CL_SEGS*32*VE
+  // warp g of the row owns [wstart[g], wstart[g+1]): multiples of 32*VE (the
+  // last end is V), at most CL_SEGS*32*VE long, C*CL_WARPS + 1 entries
+  int wstart[CL_MAXC * CL_WARPS + 1];
   const float* u;
   uint32_t* out;
   float* kept_p;
@@ -74,6 +80,7 @@ struct ClusterArgs {
   RowInfo* info;      // [B]: those rows' prologue
   float band;         // relative guard band around binade edges
   int early_dependents;  // let the row kernel launch at once (its blocks then wait for this grid)
+  int nucleus;          // bf16 top-p rows are folded here and finished by the row kernel
 };
 
 struct ClWarp {       // one warp's pass-1 summary, read by every CTA of the cluster
@@ -82,12 +89,14 @@ struct ClWarp {       // one warp's pass-1 summary, read by every CTA of the clu
   int32_t last_nan;   // last NaN index, -1
   uint32_t flags;     // MF_*
   int32_t first_max, last_max;  // first / last index holding max_raw (greedy rows), -1
-  int32_t pad0, pad1;
+  float min_raw;      // min of its raw logits, NaN ignored (+inf: none)
+  int32_t pad1;
 };
 
 struct ClShared {
   ClWarp wst[CL_WARPS];
   float segmax[CL_WARPS][CL_SEGS];
+  float segmass[CL_WARPS][CL_SEGS];  // approximate mass of each segment relative to its max
   double A[CL_WARPS];         // approximate fold state at each warp's start
   float P[CL_WARPS];          // max raw logit before each warp
   float thrL[CL_WARPS];       // raw logits below it are absorbed by the running sum (or -inf)
@@ -98,7 +107,7 @@ struct ClShared {
   int nlist;                  // merged fold entries of the CTA
   FoldEnt list[CL_LIST];
   // row state, computed by every CTA
-  float max_raw, m, tau, e_tau;
+  float max_raw, m, tau, e_tau, min_raw;
   uint32_t flags;
   int last_nan, first_max, last_max;
   int status;                 // leader: 0 sampled, 1 fallback
@@ -216,7 +225,7 @@ __device__ __forceinline__ void cl_write_pad(const ClusterArgs& a, long long b, 
 }
 
 template <typename TIn, int VE, bool VEC>
-__global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
+__global__ void __launch_bounds__(CL_NT, 4) row_cluster_kernel(ClusterArgs a) {
   __shared__ __align__(16) ClShared sh;
   cg::cluster_group cl = cg::this_cluster();
   const int C = (int)cl.num_blocks();
@@ -234,15 +243,16 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
   const TIn* row = (const TIn*)a.logits + b * a.ld;
   constexpr int SEG = 32 * VE;
   const int g = cr * CL_WARPS + w;  // the warp's place in the row
-  const long long s0 = (long long)g * a.SLW;
-  const long long s1 = s0 + a.SLW < V ? s0 + a.SLW : V;
+  const long long s0 = a.wstart[g];
+  const long long s1 = a.wstart[g + 1];
   const int nseg = s0 < V ? (int)((s1 - s0 + SEG - 1) / SEG) : 0;
   const float c2 = 1.4426950408889634f / t_eff;
 
   // ---------------- pass 1: the HBM stream ----------------
   {
-    float lmax = NEG_INF, lsum = 0.0f;  // lane: max and sum of 2^(x*c2 - lmax*c2)
-    float gmax = NEG_INF;               // greedy rows: the lane's max, with its indices
+    float lmax = NEG_INF;   // lane: max of its elements
+    float lmin = INF;       // and min
+    float gmax = NEG_INF;   // greedy rows: the lane's max, with its indices
     uint32_t lflags = 0u;
     int lnan = -1, lfirst = -1, llast = -1;
     for (int q0 = 0; q0 < nseg; q0 += CL_U) {
@@ -270,6 +280,7 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
               if (v == INF) lflags |= MF_POSINF;
               if (v == NEG_INF) lflags |= MF_NEGINF;
               smax = fmaxf(smax, v);
+              lmin = fminf(lmin, v);
               if (greedy) {  // first and last index of the lane's max so far
                 if (lfirst < 0 || v > gmax) {
                   gmax = v;
@@ -282,27 +293,37 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
             }
           }
         }
-        // the segment's max (every lane's keys; NaN never reaches smax)
-        const uint32_t sk = __reduce_max_sync(PESTI_FULL_MASK, fkey(smax));
-        if (lane == 0) sh.segmax[w][q0 + uu] = fkey_inv(sk);
-        if (smax > lmax) {
-          lsum = lmax > NEG_INF ? lsum * ex2_approx(fmaf(lmax, c2, -smax * c2)) : 0.0f;
-          lmax = smax;
-        }
-        if (lmax > NEG_INF) {
-          const float ym = lmax * c2;
+        // the segment's max (every lane's keys; NaN never reaches smax) and
+        // its approximate mass relative to that max: sum of 2^(x*c2 - max*c2)
+        const float segm = fkey_inv(__reduce_max_sync(PESTI_FULL_MASK, fkey(smax)));
+        lmax = fmaxf(lmax, smax);
+        float ls = 0.0f;
+        if (segm > NEG_INF && segm < INF) {
+          const float ym = segm * c2;
 #pragma unroll
           for (int e = 0; e < VE; ++e)
-            if (e < nv[uu] && !is_nan(x[uu][e])) lsum += ex2_approx(fmaf(x[uu][e], c2, -ym));
+            if (e < nv[uu] && !is_nan(x[uu][e])) ls += ex2_approx(fmaf(x[uu][e], c2, -ym));
+        }
+        const float smass = warp_reduce_add(ls);
+        if (lane == 0) {
+          sh.segmax[w][q0 + uu] = segm;
+          sh.segmass[w][q0 + uu] = smass;
         }
       }
     }
-    for (int q = nseg + lane; q < CL_SEGS; q += 32) sh.segmax[w][q] = NEG_INF;
-    // the warp's summary
+    for (int q = nseg + lane; q < CL_SEGS; q += 32) {
+      sh.segmax[w][q] = NEG_INF;
+      sh.segmass[w][q] = 0.0f;
+    }
+    __syncwarp();
+    // the warp's summary: its max, and its mass relative to it (an infinite
+    // row is uniform, its mass is never used)
     const float wmax = fkey_inv(__reduce_max_sync(PESTI_FULL_MASK, fkey(lmax)));
     float part = 0.0f;
-    if (lmax > NEG_INF && wmax > NEG_INF) part = lsum * ex2_approx(fmaf(lmax, c2, -wmax * c2));
-    if (!(wmax < INF)) part = 0.0f;  // an infinite row is uniform; its mass is never used
+    if (lane < nseg && wmax < INF) {
+      const float sq = sh.segmax[w][lane];
+      if (sq > NEG_INF) part = sh.segmass[w][lane] * ex2_approx(fmaf(sq, c2, -wmax * c2));
+    }
     const float wsum = warp_reduce_add(part);
     const uint32_t wfl = __reduce_or_sync(PESTI_FULL_MASK, lflags);
     const int wnan = (int)__reduce_max_sync(PESTI_FULL_MASK, (uint32_t)(lnan + 1)) - 1;
@@ -314,13 +335,14 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
       wlast = (int)__reduce_max_sync(PESTI_FULL_MASK, mine ? (uint32_t)(llast + 1) : 0u) - 1;
       if (wfirst == (int)0xffffffff) wfirst = -1;
     }
-    if (lane == 0) sh.wst[w] = ClWarp{wmax, wsum, wnan, wfl, wfirst, wlast, 0, 0};
+    const float wmin = -fkey_inv(__reduce_max_sync(PESTI_FULL_MASK, fkey(-lmin)));
+    if (lane == 0) sh.wst[w] = ClWarp{wmax, wsum, wnan, wfl, wfirst, wlast, wmin, 0};
   }
   cl.sync();
 
   // ---------------- combine: the row prologue, in every CTA ----------------
   const int NWR = C * CL_WARPS;
-  ClWarp rw{NEG_INF, 0.0f, -1, 0u, -1, -1, 0, 0};
+  ClWarp rw{NEG_INF, 0.0f, -1, 0u, -1, -1, INF, 0};
   if (tid < NWR) rw = *cl.map_shared_rank(&sh.wst[tid % CL_WARPS], tid / CL_WARPS);
   // every segment max of the row (for the candidate threshold), fetched now
   constexpr int NV = CL_MAXC * CL_WARPS * CL_SEGS / CL_NT;
@@ -335,8 +357,10 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
   uint32_t mk = __reduce_max_sync(PESTI_FULL_MASK, fkey(rw.max_raw));
   uint32_t fo = __reduce_or_sync(PESTI_FULL_MASK, rw.flags);
   uint32_t ln = __reduce_max_sync(PESTI_FULL_MASK, (uint32_t)(rw.last_nan + 1));
+  uint32_t mn = __reduce_max_sync(PESTI_FULL_MASK, fkey(-rw.min_raw));
   if (lane == 0) {
     sh.uscr[w] = mk;
+    sh.uscr[16 + w] = mn;
     sh.iscr[w] = (int)fo;
     sh.iscr[8 + w] = (int)ln;
   }
@@ -344,11 +368,14 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
   mk = 0u;
   fo = 0u;
   ln = 0u;
+  mn = 0u;
   for (int q = 0; q < CL_WARPS; ++q) {
     mk = mk > sh.uscr[q] ? mk : sh.uscr[q];
+    mn = mn > sh.uscr[16 + q] ? mn : sh.uscr[16 + q];
     fo |= (uint32_t)sh.iscr[q];
     ln = ln > (uint32_t)sh.iscr[8 + q] ? ln : (uint32_t)sh.iscr[8 + q];
   }
+  const float mnv = -fkey_inv(mn);  // row min (NaN ignored)
   const float mx = fkey_inv(mk);
   const uint32_t fl = fo;
   const int last_nan = (int)ln - 1;
@@ -378,11 +405,14 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
   const long long k = (long long)prm.top_k;
   const long long keff = k < V ? k : V;
   const bool fast = !greedy && !uniform && fast_topk(prm, V);
+  // top-p rows of bf16 logits: the cluster folds S exactly, the row kernel
+  // takes their sorted folds by distinct values (pesti_nucleus.cuh)
+  const bool nuc = a.nucleus && !greedy && !uniform && a.dtype == PESTI_BF16 && prm.top_k == 0u && prm.top_p > 0.0f;
   // greedy rows are finished here (NaN rows with the last-index rule go to
   // the row kernel, which re-scans after the last NaN as max_by does)
   int decided = -1;  // 0: sampled here, 1: fallback
   if (greedy) decided = ((fl & MF_NAN) && !(prm.flags & PESTI_FLAG_ARGMAX_FIRST)) ? 1 : 0;
-  else if (!fast) decided = 1;
+  else if (!fast && !nuc) decided = 1;
 
   float tau = INF;
   if (decided < 0) {
@@ -421,8 +451,8 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
       }
       sh.thrL[wl] = thr;
     }
-    // candidate threshold from every segment max of the row
-    tau = cl_tau<NV>(vals, mx, t_eff, keff, sh);
+    // candidate threshold from every segment max of the row (none for top-p rows)
+    tau = nuc ? INF : cl_tau<NV>(vals, mx, t_eff, keff, sh);
     if (tid == 0) {
       sh.tau = tau;
       sh.e_tau = tau > NEG_INF && tau < INF ? pesti_expf_call(fsub(scale ? fdiv(tau, T) : tau, m)) : 0.0f;
@@ -437,15 +467,25 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
     sh.last_nan = last_nan;
     sh.first_max = first_max;
     sh.last_max = last_max;
+    sh.min_raw = mnv;
   }
 
-  // ---------------- pass 2: survivors, fold entries, candidates ----------------
+  // ---------------- pass 2: fold entries and candidates ----------------
+  // Segment by segment in row order, with the approximate fold state s_run
+  // (the mass of the row before the segment, from pass 1).  A segment whose
+  // whole state range lies inside one binade, away from its edges, with no
+  // element large next to the state, adds rint(e/w) per element (w the
+  // binade's ulp): the approximate exps decide those increments with a proven
+  // margin, the exact exp is taken where they do not, and consecutive such
+  // segments of one binade form one run.  Any other segment goes element by
+  // element (its survivors of the pruning, with their own approximate states).
   if (decided < 0) {
     const float c1 = ABSORB * t_eff * (1.0f + 0x1p-20f);
     const float pf = (m - PRUNE_FLOOR) * t_eff;
     const float p_floor = pf + 0x1p-20f * fabsf(pf);
     auto bound_a = [&](float Pv) { return Pv >= p_floor ? fsub(Pv, fadd(c1, 0x1p-21f * fabsf(Pv))) : NEG_INF; };
-    const double lfac = (1.0 - (double)V * 0x1p-24) * (1.0 - 0x1p-10) * exp2(-0x1p-20 * ((double)fabsf(mx * c2) + 64.0));
+    const float ym = mx * c2;
+    const double lfac = (1.0 - (double)V * 0x1p-24) * (1.0 - 0x1p-10) * exp2(-0x1p-20 * ((double)fabsf(ym) + 64.0));
     // bound (b) from a lower bound L of the running sum (derivation at
     // row_prologue): raw logits below it leave every later state unchanged
     auto bound_b = [&](double L) {
@@ -457,6 +497,7 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
       }
       return thr;
     };
+    const float rT = scale ? 1.0f / T : 1.0f;  // the approximate argument x*rT - m (margins below)
     float thr_b = sh.thrL[w];
     float run_max = sh.P[w];
     const float BAND = a.band;
@@ -464,14 +505,33 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
     uint32_t* qidx = sh.u.c.qidx[w];
     FoldEnt* went = sh.u.c.went[w];
     float4* stg = sh.u.c.stg[w];
-    // approximate fold state before the next survivor: the earlier warps'
-    // mass plus the exact exps of this warp's survivors so far
-    double s_run = sh.A[w];
+    double s_run = sh.A[w];       // approximate fold state before the next segment
     double s_thr = s_run;         // the state bound (b) was last taken at
-    uint32_t head = 0u, tail = 0u;  // ring positions (consumed / appended)
     int wn = 0;                   // entries written
     bool over = false;            // entries overflowed: the walk replays the range
     uint32_t lkey = KEY_NONE;     // key of the last entry written
+    uint32_t pkey = KEY_NONE;     // the open run of whole segments (its binade), not yet written
+    uint32_t pk = 0u;             // its increment, this lane's part
+    uint32_t pend = 0u;           // the row index past its last element
+
+    // the open run becomes an entry (or extends the last one, of the same binade)
+    auto flush = [&]() {
+      if (pkey == KEY_NONE) return;
+      const uint32_t ks = tr_sat(warp_reduce_add(pk));
+      if (lkey == pkey) {
+        if (lane == 0) {
+          const FoldEnt pe = went[wn - 1];
+          went[wn - 1] = FoldEnt{pkey, tr_sat(pe.a0 + ks), tr_sat(pe.a1 + ks), pend};
+        }
+      } else {
+        if (lane == 0 && wn < CL_EW) went[wn] = FoldEnt{pkey, ks, ks, pend};
+        ++wn;
+        if (wn > CL_EW) over = true;
+      }
+      lkey = pkey;
+      pkey = KEY_NONE;
+      pk = 0u;
+    };
 
     const int nfull = VEC ? (int)((s1 - s0) / SEG) : 0;  // whole segments, staged through shared memory
     if (VEC) {
@@ -507,15 +567,7 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
         if (qn < nfull) cp_async16(&stg[(q % CL_STAGES) * 32 + lane], row + s0 + (long long)qn * SEG + lane * VE);
         cp_async_commit();
       }
-      // bound (b) again once the running state has doubled (it only rises)
-      if (s_run >= 2.0 * s_thr && s_run > 0.0) {
-        float tb = 0.0f;
-        if (lane == 0) tb = bound_b(s_run * lfac);
-        thr_b = fmaxf(thr_b, __shfl_sync(PESTI_FULL_MASK, tb, 0));
-        s_thr = s_run;
-      }
-      const float thr = fmaxf(bound_a(run_max), thr_b);
-      run_max = fmaxf(run_max, sh.segmax[w][q]);
+      const float segm = sh.segmax[w][q];
       // top-k candidates (raw >= tau; their exact exps, sampling.rs:127)
       int nc = 0;
 #pragma unroll
@@ -525,249 +577,262 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
         int cb = 0;
         if (lane == 31) cb = atomicAdd(&sh.ncand, cin);
         cb = __shfl_sync(PESTI_FULL_MASK, cb, 31) + cin - nc;
+        uint32_t cm = 0u;
 #pragma unroll
-        for (int e = 0; e < VE; ++e) {
-          if (e < nv && x[e] >= tau) {
-            if (cb < CL_CCAP) {
-              sh.cand_e[cb] = pesti_expf_call(fsub(scale ? fdiv(x[e], T) : x[e], m));
-              sh.cand_i[cb] = (uint32_t)(p0 + e);
-            }
-            ++cb;
+        for (int e = 0; e < VE; ++e) cm |= (e < nv && x[e] >= tau) ? (1u << e) : 0u;
+#pragma unroll 1
+        for (; cm != 0u; cm &= cm - 1u, ++cb) {
+          const int e = __ffs(cm) - 1;
+          float xv = x[0];
+#pragma unroll
+          for (int r2 = 1; r2 < VE; ++r2) xv = e == r2 ? x[r2] : xv;
+          if (cb < CL_CCAP) {
+            sh.cand_e[cb] = pesti_expf_call(fsub(scale ? fdiv(xv, T) : xv, m));
+            sh.cand_i[cb] = (uint32_t)(p0 + e);
           }
         }
       }
-      if (over) continue;
-      // survivors into the ring in row order: the segment in parts of 128
-      // elements (all of the lanes [ph*LPP, (ph+1)*LPP)), so that the ring
-      // never holds more than 31 + 128 of them
-      constexpr int NPART = VE / 4;
-      constexpr int LPP = 32 / NPART;
-      uint32_t sv = 0u;
-#pragma unroll
-      for (int e = 0; e < VE; ++e) sv |= (e < nv && x[e] >= thr) ? (1u << e) : 0u;
-#pragma unroll 1
-      for (int ph = 0; ph < NPART; ++ph) {
-        const bool mine = lane / LPP == ph;
-        const int cnt = mine ? __popc(sv) : 0;
-        const int sin = warp_incl_scan_add(cnt);
-        const int tot = __shfl_sync(PESTI_FULL_MASK, sin, 31);
-        uint32_t o = tail + (uint32_t)(sin - cnt);
-        if (mine) {
+      // the segment's largest exp and its mass, relative to the row max
+      const float emx = segm > NEG_INF ? ex2_approx(fmaf(segm, c2, -ym)) : 0.0f;
+      const float smass = emx * sh.segmass[w][q];
+      if (over) {
+        s_run += (double)smass;
+        continue;
+      }
+      const float sb = (float)s_run;
+      bool done = false;
+      if (sb >= 0x1p-126f) {
+        const uint32_t lo = fbits(sb) & 0x7f800000u;
+        const float lov = bitsf(lo);
+        if (sb >= lov * (1.0f + BAND) && sb + smass * (1.0f + 0x1p-14f) <= 2.0f * lov * (1.0f - BAND) &&
+            emx * (1.0f + 0x1p-14f) < 0.5f * lov) {
+          // plain increments: rint(e/w) from the approximate exp where its
+          // margin decides it.  Against the exact exp of the reference's
+          // argument z = fl(fl(x/T) - m), exp_hw(fl(x*rT - m)) is within
+          // DE_0/2 + DE_Z*(|x*rT| + 1.5|z'|) relative; the test keeps twice that.
+          const uint32_t E = lo >> 23;
+          const uint32_t sc = (uint32_t)(150 - (int)E) << 23;  // e/w = e * 2^(150-E)
+          uint32_t kseg = 0u, und = 0u;  // und: elements the approximation leaves undecided
 #pragma unroll
           for (int e = 0; e < VE; ++e) {
-            if (sv & (1u << e)) {
-              qraw[o & (CL_RING - 1)] = x[e];
-              qidx[o & (CL_RING - 1)] = (uint32_t)(p0 + e);
-              ++o;
-            }
-          }
-        }
-        tail += (uint32_t)tot;
-        __syncwarp();
-        // classification of the survivors, CL_BATCH at a time (fewer at the end)
-#pragma unroll 1
-        while (!over && (tail - head >= (uint32_t)CL_BATCH || (q == nseg - 1 && ph == NPART - 1 && tail > head))) {
-          const int n = tail - head >= (uint32_t)CL_BATCH ? CL_BATCH : (int)(tail - head);
-          // fast path: element j*32 + lane of the batch for j < CL_R.  The
-          // approximate exps (exp_hw, within DE_0 + |z| DE_Z of the exact
-          // value with twice its margin) decide rint(e/w) unless e/w lies
-          // near a half-integer; those lanes take the exact exp.  The batch
-          // is one plain increment when its whole state range lies inside
-          // one binade away from its edges, no element is large next to the
-          // state and none is a tie.
-          float z[CL_R], ea[CL_R];
-          float lsum = 0.0f, lmaxe = 0.0f;
-#pragma unroll
-          for (int j = 0; j < CL_R; ++j) {
-            const int i = j * 32 + lane;
-            z[j] = 0.0f;
-            ea[j] = 0.0f;
-            if (i < n) {
-              const float raw = qraw[(head + i) & (CL_RING - 1)];
-              z[j] = fsub(scale ? fdiv(raw, T) : raw, m);  // sampling.rs:46,127: the exact argument
-              ea[j] = exp_hw(z[j]);
-              lsum += ea[j];
-              lmaxe = fmaxf(lmaxe, ea[j] * fmaf(-z[j], DE_Z, 1.0f + DE_0));
-            }
-          }
-          const float btot = warp_reduce_add(lsum);
-          const float sb = (float)s_run;
-          bool done = false;
-          if (sb >= 0x1p-126f) {
-            const uint32_t lo = fbits(sb) & 0x7f800000u;
-            const float lov = bitsf(lo);
-            if (sb >= lov * (1.0f + BAND) && sb + btot * (1.0f + 0x1p-20f) <= 2.0f * lov * (1.0f - BAND) &&
-                __all_sync(PESTI_FULL_MASK, lmaxe < 0.5f * lov)) {
-              const uint32_t E = lo >> 23;
-              const int sh2 = 150 - (int)E;  // w = 2^(E-150)
-              uint32_t ksum = 0u;
-              bool tie = false;
-#pragma unroll
-              for (int j = 0; j < CL_R; ++j) {
-                const int i = j * 32 + lane;
-                if (i < n) {
-                  bool exact;
-                  uint32_t kd = 0u;
-                  if (ea[j] == 0.0f) {
-                    exact = E < 40u;  // else the exact value (< 2^-126) rounds to 0 on this grid
-                  } else {
-                    const float tt = __uint_as_float(fbits(ea[j]) + ((uint32_t)sh2 << 23));  // ea/w, exact scaling
-                    const float kr = rintf(tt);
-                    const float slack = 0.5f - fabsf(tt - kr);
-                    exact = !(slack > tt * fmaf(-z[j], DE_Z, DE_0) + 0x1p-24f);
-                    kd = (uint32_t)kr;
-                  }
-                  if (exact) {
-                    const float ex = pesti_expf_call(z[j]);
-                    const uint32_t k0 = fbits(fadd(lov, ex)) - lo;
-                    const uint32_t k1 = fbits(fadd(bitsf(lo + 1u), ex)) - (lo + 1u);
-                    tie = tie || k0 != k1;
-                    kd = k0;
-                  }
-                  ksum += kd;
-                }
-              }
-              if (!__any_sync(PESTI_FULL_MASK, tie)) {
-                const uint32_t ks = tr_sat(warp_reduce_add(ksum));  // each < 2^22, at most CL_BATCH of them
-                const uint32_t last_end = qidx[(head + n - 1) & (CL_RING - 1)] + 1u;
-                if (lkey == lo) {
-                  if (lane == 0) {
-                    const FoldEnt pe = went[wn - 1];
-                    went[wn - 1] = FoldEnt{lo, tr_sat(pe.a0 + ks), tr_sat(pe.a1 + ks), last_end};
-                  }
-                } else {
-                  if (lane == 0 && wn < CL_EW) went[wn] = FoldEnt{lo, ks, ks, last_end};
-                  ++wn;
-                  if (wn > CL_EW) over = true;
-                }
-                lkey = lo;
-                done = true;
-              }
-            }
-          }
-          if (!done) {
-            // per element, 32 at a time in row order: its approximate state
-            // decides a run of its binade or an explicit element (near a
-            // binade edge, or large next to the state); the approximate exp
-            // decides each increment where it can, the exact exp is taken
-            // for explicit elements and undecided increments.  Runs are
-            // summed over the lanes (composed, when some element is a tie).
-            float sbj = sb;
-#pragma unroll 1
-            for (int j = 0; j * 32 < n && !over; ++j) {
-              const int i = j * 32 + lane;
-              const int nj = n - j * 32 < 32 ? n - j * 32 : 32;
-              const bool valid = i < n;
-              float zj = 0.0f, eaj = 0.0f;
-#pragma unroll
-              for (int r = 0; r < CL_R; ++r) {
-                zj = r == j ? z[r] : zj;
-                eaj = r == j ? ea[r] : eaj;
-              }
-              const uint32_t idx = valid ? qidx[(head + i) & (CL_RING - 1)] : 0u;
-              const float incl = warp_incl_scan_add(eaj);
-              float excl = __shfl_up_sync(PESTI_FULL_MASK, incl, 1);
-              if (lane == 0) excl = 0.0f;
-              const float av = sbj + excl;  // approximate state before the element
-              const float bv = av + eaj;    // and after it
-              const float dej = fmaf(-zj, DE_Z, DE_0);
-              uint32_t key = KEY_NONE, k0 = 0u, k1 = 0u;
-              if (valid) {
-                bool special = !(av >= 0x1p-126f);
-                uint32_t lo = 0u;
-                float lov = 0.0f;
-                if (!special) {
-                  lo = fbits(av) & 0x7f800000u;
-                  lov = bitsf(lo);
-                  special = eaj * (1.0f + dej) >= 0.5f * lov || av < lov * (1.0f + BAND) ||
-                            bv > 2.0f * lov * (1.0f - BAND);
-                }
-                bool need = special;
-                if (!special) {
-                  const uint32_t E = lo >> 23;
-                  if (eaj == 0.0f) {
-                    need = E < 40u;  // else the exact value (< 2^-126) rounds to 0 on this grid
-                  } else {
-                    const float tt = __uint_as_float(fbits(eaj) + ((uint32_t)(150 - (int)E) << 23));  // ea/w
-                    const float kr = rintf(tt);
-                    need = !(0.5f - fabsf(tt - kr) > tt * dej + 0x1p-24f);
-                    k0 = k1 = (uint32_t)kr;
-                  }
-                }
-                if (need) {
-                  const float ex = pesti_expf_call(zj);  // sampling.rs:127, exact
-                  if (special) {
-                    k0 = fbits(ex);
-                  } else {
-                    k0 = fbits(fadd(lov, ex)) - lo;
-                    k1 = fbits(fadd(bitsf(lo + 1u), ex)) - (lo + 1u);
-                  }
-                }
-                key = special ? fold::SPECIAL : lo;
-              }
-              uint32_t pkey = __shfl_up_sync(PESTI_FULL_MASK, key, 1);
-              if (lane == 0) pkey = lkey;
-              const bool hd = valid && (key == fold::SPECIAL || pkey == fold::SPECIAL || pkey == KEY_NONE || key != pkey);
-              // lane 0 may continue the warp's last entry (a run of the same binade)
-              const bool cont = __shfl_sync(PESTI_FULL_MASK, valid && !hd, 0);
-              const bool nhd = __shfl_down_sync(PESTI_FULL_MASK, hd, 1);
-              const bool is_end = valid && (lane == nj - 1 || nhd);
-              const uint32_t ends = __ballot_sync(PESTI_FULL_MASK, is_end);
-              const int base = cont ? wn - 1 : wn;
-              const int slot = base + __popc(ends & ((1u << lane) - 1u));
-              const bool tie = valid && key != fold::SPECIAL && k0 != k1;
-              if (!__any_sync(PESTI_FULL_MASK, tie)) {
-                // plain integer increments: a run is a difference of prefix sums
-                const uint32_t H = __ballot_sync(PESTI_FULL_MASK, hd || lane == 0);
-                const uint32_t kk = valid && key != fold::SPECIAL ? k0 : 0u;
-                const uint32_t sc = warp_incl_scan_add(kk);
-                const int st = 31 - __clz(H & (0xffffffffu >> (31 - lane)));  // the run's first lane
-                const uint32_t pre = __shfl_sync(PESTI_FULL_MASK, sc, st > 0 ? st - 1 : 0);
-                uint32_t run = tr_sat(sc - (st > 0 ? pre : 0u));
-                if (is_end && slot < CL_EW) {
-                  if (key == fold::SPECIAL) {
-                    went[slot] = FoldEnt{key, k0, 0u, idx + 1u};
-                  } else if (st == 0 && cont) {
-                    const FoldEnt pe = went[slot];
-                    went[slot] = FoldEnt{key, tr_sat(pe.a0 + run), tr_sat(pe.a1 + run), idx + 1u};
-                  } else {
-                    went[slot] = FoldEnt{key, run, run, idx + 1u};
-                  }
-                }
+            if (e < nv) {
+              const float xv = x[e];
+              const float zq = scale ? fmaf(xv, rT, -m) : fsub(xv, m);
+              const float ea = exp_hw(zq);
+              bool exact;
+              uint32_t kd = 0u;
+              if (ea == 0.0f) {
+                exact = E < 40u;  // else the exact value (< 2^-126) rounds to 0 on this grid
               } else {
-                // some element is a tie: compose the (even, odd) increments
-                Seg v{k0, k1, 1u, key};
-                if (cont && lane == 0) {
-                  const FoldEnt pe = went[wn - 1];
-                  const Tr t = tr_compose(Tr{pe.a0, pe.a1}, Tr{k0, k1});
-                  v = Seg{t.a0, t.a1, 1u, key};
-                }
-                Seg inc = v;
-                bool flg = hd || lane == 0;
-#pragma unroll
-                for (int off = 1; off < 32; off <<= 1) {
-                  const Seg o2 = seg_shfl_up(inc, off);
-                  const bool of = __shfl_up_sync(PESTI_FULL_MASK, flg, off);
-                  if (lane >= off) {
-                    inc = seg_join(o2, inc, flg);
-                    flg = flg || of;
-                  }
-                }
-                if (is_end && slot < CL_EW) went[slot] = FoldEnt{key, inc.a0, inc.a1, idx + 1u};
+                const float tt = __uint_as_float(fbits(ea) + sc);
+                const float kr = rintf(tt);
+                const float de = scale ? fmaf(2.0f * fabsf(xv * rT) + 3.0f * fabsf(zq), DE_Z, DE_0)
+                                       : fmaf(-zq, DE_Z, DE_0);
+                exact = !(0.5f - fabsf(tt - kr) > tt * de + 0x1p-24f);
+                kd = (uint32_t)kr;
               }
-              wn = base + __popc(ends);
-              if (wn > CL_EW) over = true;
-              lkey = __shfl_sync(PESTI_FULL_MASK, key, nj - 1);
-              sbj += __shfl_sync(PESTI_FULL_MASK, incl, 31);
-              __syncwarp();
+              kseg += exact ? 0u : kd;
+              und |= exact ? (1u << e) : 0u;
             }
           }
-          s_run += (double)btot;
-          head += (uint32_t)n;
-          __syncwarp();
+          bool tie = false;
+#pragma unroll 1
+          for (uint32_t mm = und; mm != 0u; mm &= mm - 1u) {
+            const int e = __ffs(mm) - 1;
+            float xv = x[0];
+#pragma unroll
+            for (int r2 = 1; r2 < VE; ++r2) xv = e == r2 ? x[r2] : xv;
+            const float ex = pesti_expf_call(fsub(scale ? fdiv(xv, T) : xv, m));  // sampling.rs:46,127
+            const uint32_t k0 = fbits(fadd(lov, ex)) - lo;
+            const uint32_t k1 = fbits(fadd(bitsf(lo + 1u), ex)) - (lo + 1u);
+            tie = tie || k0 != k1;
+            kseg += k0;
+          }
+          if (!__any_sync(PESTI_FULL_MASK, tie)) {
+            if (pkey != lo) {
+              flush();
+              pkey = lo;
+            }
+            pk += kseg;
+            pend = (uint32_t)(s0 + (long long)q * SEG + SEG < s1 ? s0 + (long long)q * SEG + SEG : s1);
+            done = true;
+          }
         }
       }
+      if (!done) {
+        flush();
+        // a segment whose entries would overflow the warp's list (explicit
+        // elements near a binade edge) is rolled back and refolded by the walk
+        // from its raw logits instead: its entries, and the last entry before
+        // it (which its first run may extend), are kept aside
+        const int wn0 = wn;
+        const uint32_t lkey0 = lkey;
+        FoldEnt prev0{0u, 0u, 0u, 0u};
+        if (wn0 > 0 && wn0 <= CL_EW) prev0 = went[wn0 - 1];
+        // element by element: the survivors of the pruning, in row order
+        if (s_run >= 2.0 * s_thr && s_run > 0.0) {  // bound (b) again once the state has doubled
+          float tb = 0.0f;
+          if (lane == 0) tb = bound_b(s_run * lfac);
+          thr_b = fmaxf(thr_b, __shfl_sync(PESTI_FULL_MASK, tb, 0));
+          s_thr = s_run;
+        }
+        const float thr = fmaxf(bound_a(run_max), thr_b);
+        // survivors into the ring in row order: parts of 128 elements (all
+        // of the lanes [ph*LPP, (ph+1)*LPP))
+        constexpr int NPART = VE / 4;
+        constexpr int LPP = 32 / NPART;
+        uint32_t sv = 0u;
+#pragma unroll
+        for (int e = 0; e < VE; ++e) sv |= (e < nv && x[e] >= thr) ? (1u << e) : 0u;
+        uint32_t tail = 0u;
+#pragma unroll
+        for (int ph = 0; ph < NPART; ++ph) {
+          const bool mine = lane / LPP == ph;
+          const int cnt = mine ? __popc(sv) : 0;
+          const int sin = warp_incl_scan_add(cnt);
+          const int tot = __shfl_sync(PESTI_FULL_MASK, sin, 31);
+          uint32_t o = tail + (uint32_t)(sin - cnt);
+          if (mine) {
+#pragma unroll
+            for (int e = 0; e < VE; ++e) {
+              if (sv & (1u << e)) {
+                qraw[o] = x[e];
+                qidx[o] = (uint32_t)(p0 + e);
+                ++o;
+              }
+            }
+          }
+          tail += (uint32_t)tot;
+        }
+        __syncwarp();
+        // 32 survivors at a time: each element's approximate state decides a
+        // run of its binade or an explicit element (near a binade edge, or
+        // large next to the state); runs are summed over the lanes (composed
+        // when some element is a tie)
+        float sbj = sb;
+        const int n = (int)tail;
+#pragma unroll 1
+        for (int j = 0; j * 32 < n && !over; ++j) {
+          const int i = j * 32 + lane;
+          const int nj = n - j * 32 < 32 ? n - j * 32 : 32;
+          const bool valid = i < n;
+          const float raw = valid ? qraw[i] : 0.0f;
+          const uint32_t idx = valid ? qidx[i] : 0u;
+          const float zj = valid ? fsub(scale ? fdiv(raw, T) : raw, m) : 0.0f;  // sampling.rs:46,127
+          const float eaj = valid ? exp_hw(zj) : 0.0f;
+          const float incl = warp_incl_scan_add(eaj);
+          float excl = __shfl_up_sync(PESTI_FULL_MASK, incl, 1);
+          if (lane == 0) excl = 0.0f;
+          const float av = sbj + excl;  // approximate state before the element
+          const float bv = av + eaj;    // and after it
+          const float dej = fmaf(-zj, DE_Z, DE_0);
+          uint32_t key = KEY_NONE, k0 = 0u, k1 = 0u;
+          if (valid) {
+            bool special = !(av >= 0x1p-126f);
+            uint32_t lo = 0u;
+            float lov = 0.0f;
+            if (!special) {
+              lo = fbits(av) & 0x7f800000u;
+              lov = bitsf(lo);
+              special = eaj * (1.0f + dej) >= 0.5f * lov || av < lov * (1.0f + BAND) ||
+                        bv > 2.0f * lov * (1.0f - BAND);
+            }
+            bool need = special;
+            if (!special) {
+              const uint32_t E = lo >> 23;
+              if (eaj == 0.0f) {
+                need = E < 40u;  // else the exact value (< 2^-126) rounds to 0 on this grid
+              } else {
+                const float tt = __uint_as_float(fbits(eaj) + ((uint32_t)(150 - (int)E) << 23));  // ea/w
+                const float kr = rintf(tt);
+                need = !(0.5f - fabsf(tt - kr) > tt * dej + 0x1p-24f);
+                k0 = k1 = (uint32_t)kr;
+              }
+            }
+            if (need) {
+              const float ex = pesti_expf_call(zj);  // sampling.rs:127, exact
+              if (special) {
+                k0 = fbits(ex);
+              } else {
+                k0 = fbits(fadd(lov, ex)) - lo;
+                k1 = fbits(fadd(bitsf(lo + 1u), ex)) - (lo + 1u);
+              }
+            }
+            key = special ? fold::SPECIAL : lo;
+          }
+          uint32_t pky = __shfl_up_sync(PESTI_FULL_MASK, key, 1);
+          if (lane == 0) pky = lkey;
+          const bool hd = valid && (key == fold::SPECIAL || pky == fold::SPECIAL || pky == KEY_NONE || key != pky);
+          // lane 0 may continue the warp's last entry (a run of the same binade)
+          const bool cont = __shfl_sync(PESTI_FULL_MASK, valid && !hd, 0);
+          const bool nhd = __shfl_down_sync(PESTI_FULL_MASK, hd, 1);
+          const bool is_end = valid && (lane == nj - 1 || nhd);
+          const uint32_t ends = __ballot_sync(PESTI_FULL_MASK, is_end);
+          const int base = cont ? wn - 1 : wn;
+          const int slot = base + __popc(ends & ((1u << lane) - 1u));
+          const bool tie = valid && key != fold::SPECIAL && k0 != k1;
+          if (!__any_sync(PESTI_FULL_MASK, tie)) {
+            // plain integer increments: a run is a difference of prefix sums
+            const uint32_t H = __ballot_sync(PESTI_FULL_MASK, hd || lane == 0);
+            const uint32_t kk = valid && key != fold::SPECIAL ? k0 : 0u;
+            const uint32_t scn = warp_incl_scan_add(kk);
+            const int st = 31 - __clz(H & (0xffffffffu >> (31 - lane)));  // the run's first lane
+            const uint32_t pre = __shfl_sync(PESTI_FULL_MASK, scn, st > 0 ? st - 1 : 0);
+            const uint32_t run = tr_sat(scn - (st > 0 ? pre : 0u));
+            if (is_end && slot < CL_EW) {
+              if (key == fold::SPECIAL) {
+                went[slot] = FoldEnt{key, k0, 0u, idx + 1u};
+              } else if (st == 0 && cont) {
+                const FoldEnt pe = went[slot];
+                went[slot] = FoldEnt{key, tr_sat(pe.a0 + run), tr_sat(pe.a1 + run), idx + 1u};
+              } else {
+                went[slot] = FoldEnt{key, run, run, idx + 1u};
+              }
+            }
+          } else {
+            // some element is a tie: compose the (even, odd) increments
+            Seg v{k0, k1, 1u, key};
+            if (cont && lane == 0) {
+              const FoldEnt pe = went[wn - 1];
+              const Tr t = tr_compose(Tr{pe.a0, pe.a1}, Tr{k0, k1});
+              v = Seg{t.a0, t.a1, 1u, key};
+            }
+            Seg inc = v;
+            bool flg = hd || lane == 0;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+              const Seg o2 = seg_shfl_up(inc, off);
+              const bool of = __shfl_up_sync(PESTI_FULL_MASK, flg, off);
+              if (lane >= off) {
+                inc = seg_join(o2, inc, flg);
+                flg = flg || of;
+              }
+            }
+            if (is_end && slot < CL_EW) went[slot] = FoldEnt{key, inc.a0, inc.a1, idx + 1u};
+          }
+          wn = base + __popc(ends);
+          if (wn > CL_EW) over = true;
+          lkey = __shfl_sync(PESTI_FULL_MASK, key, nj - 1);
+          sbj += __shfl_sync(PESTI_FULL_MASK, incl, 31);
+          __syncwarp();
+        }
+        if (over && wn0 < CL_EW) {
+          const uint32_t seg_end = (uint32_t)(s0 + (long long)q * SEG + SEG < s1 ? s0 + (long long)q * SEG + SEG : s1);
+          if (lane == 0) {
+            if (wn0 > 0) went[wn0 - 1] = prev0;
+            went[wn0] = FoldEnt{ENT_REPLAY, 0u, 0u, seg_end};
+          }
+          __syncwarp();
+          wn = wn0 + 1;
+          lkey = ENT_REPLAY;
+          over = false;
+        }
+        (void)lkey0;
+      }
+      run_max = fmaxf(run_max, segm);
+      s_run += (double)smass;
     }
+    if (!over) flush();
     if (VEC) cp_async_wait<0>();
     if (lane == 0) sh.wn[w] = over ? -1 : wn;
   }
@@ -778,13 +843,13 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
     int nl = 0;
     uint32_t last = KEY_NONE;
     bool full = false;
-    const long long cta_end = ((long long)(cr + 1) * CL_WARPS * a.SLW) < V ? (long long)(cr + 1) * CL_WARPS * a.SLW : V;
+    const long long cta_end = a.wstart[(cr + 1) * CL_WARPS];
     for (int q = 0; q < CL_WARPS && !full; ++q) {
-      const long long ws0 = (long long)(cr * CL_WARPS + q) * a.SLW;
+      const long long ws0 = a.wstart[cr * CL_WARPS + q];
       if (ws0 >= V) break;
       const int n = sh.wn[q];
       if (n < 0) {
-        const long long we = ws0 + a.SLW < V ? ws0 + a.SLW : V;
+        const long long we = a.wstart[cr * CL_WARPS + q + 1];
         if (nl < CL_LIST) sh.list[nl++] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)we};
         else full = true;
         last = ENT_REPLAY;
@@ -835,7 +900,7 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
         sh.u.f.coff[C] = ncd;
         sh.u.f.nent = ne;
         sh.u.f.ncand = ncd;
-        sh.status = (bad || ne > CL_LOCAL || ncd > FAST_CAND || ncd < keff) ? 1 : 0;
+        sh.status = (bad || ne > CL_LOCAL || (!nuc && (ncd > FAST_CAND || ncd < keff))) ? 1 : 0;
       }
     }
     __syncthreads();
@@ -932,7 +997,9 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
       sh.uscr[0] = s;
     }
     __syncthreads();
-    if (w == 0) {
+    if (nuc) {  // S for the row kernel's sorted folds by distinct values
+      if (tid == 0) sh.status = 2;
+    } else if (w == 0) {
       const float S = bitsf(sh.uscr[0]);
       unsigned long long* key = sh.u.f.key;
       // p = e/S (sampling.rs:130); the list stays sorted by p except inside
@@ -1004,6 +1071,8 @@ __global__ void __launch_bounds__(CL_NT) row_cluster_kernel(ClusterArgs a) {
                     !(fabsf(sh.m) < INF)) ? 1 : 0;
       ri.e_tau = 0.0f;
       ri.s_start = 0.0f;
+      ri.S = status == 2 ? bitsf(sh.uscr[0]) : 0.0f;
+      ri.min_raw = sh.min_raw;
       a.info[b] = ri;
     }
   }

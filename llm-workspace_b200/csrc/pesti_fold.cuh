@@ -360,6 +360,240 @@ __device__ inline Result repeat_fold(float v, long long count, uint32_t s0_bits,
   return r;
 }
 
+// ---------------------------------------------------------------------------
+// The same fold over a sequence given as runs of equal values: entry j stands
+// for cnt[j] >= 1 consecutive copies of val[j] (the sorted probabilities of a
+// row whose logits take few distinct values: every copy of a value has the
+// same probability).  Inside a binade each copy of a value adds the same
+// integer to bits(s) (after at most one tie step), so a run of cnt copies is
+// cnt times that increment; entries that may leave the binade, are large next
+// to the state, are ties or may reach the query are folded exactly copy by
+// copy (repeat_fold, O(binades) per entry).  Result::hit is the first entry
+// whose running sum reaches tau, hit_copy the copy (0-based) inside it.
+// ---------------------------------------------------------------------------
+struct RunResult {
+  uint32_t s_bits;
+  long long hit;        // entry of the first copy with fold >= tau, -1 if none
+  long long hit_copy;   // that copy's place inside its entry
+  uint32_t hit_s_bits;  // fold value at the hit
+};
+
+struct RunSmem {
+  float v[TS];
+  uint32_t c[TS];
+  long long pinc[TS];
+  uint32_t cls[TS];
+  uint32_t seg_lo[TS];
+  unsigned short seg_start[TS];
+  double dscr[34];
+  long long lscr[34];
+  int iscr[34];
+  uint32_t s_bits;
+  uint32_t hit_s_bits;
+  long long pos;
+  long long hit;
+  long long hit_copy;
+  int done;
+  int seq_left;
+};
+
+__device__ __noinline__ RunResult block_fold_runs(const float* __restrict__ val, const uint32_t* __restrict__ cnt,
+                                                  long long n, uint32_t s0_bits, uint32_t tau_bits, bool stop_at_hit,
+                                                  RunSmem& sm) {
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    sm.s_bits = s0_bits & 0x7fffffffu;
+    sm.pos = 0;
+    sm.hit = -1;
+    sm.hit_copy = -1;
+    sm.hit_s_bits = 0;
+    sm.done = 0;
+    sm.seq_left = 0;
+  }
+  __syncthreads();
+  const float tauf = bitsf(tau_bits == NO_QUERY ? 0x7f800000u : tau_bits);
+  // one entry folded exactly by the calling thread (with the query)
+  auto exact_entry = [&](long long at, float v, uint32_t c, uint32_t s) -> uint32_t {
+    const Result r = repeat_fold(v, (long long)c, s, sm.hit < 0 ? tau_bits : NO_QUERY, stop_at_hit);
+    if (sm.hit < 0 && r.hit >= 0) {
+      sm.hit = at;
+      sm.hit_copy = r.hit;
+      sm.hit_s_bits = r.hit_s_bits;
+      if (stop_at_hit) sm.done = 1;
+    }
+    return r.s_bits;
+  };
+  while (true) {
+    const long long pos = sm.pos;
+    const uint32_t s_bits = sm.s_bits;
+    const int done = sm.done;
+    const int seq_left = sm.seq_left;
+    __syncthreads();
+    if (done || pos >= n) break;
+    if (seq_left > 0) {
+      // progress guarantee: a few entries folded one by one
+      if (tid == 0) {
+        uint32_t s = s_bits;
+        long long p = pos;
+        const long long lim = pos + seq_left < n ? pos + seq_left : n;
+        for (; p < lim && !sm.done; ++p) s = exact_entry(p, val[p], cnt[p], s);
+        sm.s_bits = s;
+        sm.pos = p;
+        sm.seq_left = 0;
+      }
+      __syncthreads();
+      continue;
+    }
+    const int len = (int)((n - pos) < (long long)TS ? (n - pos) : (long long)TS);
+    // ---- load the tile and form the approximate running sum ----
+    float v[EPT];
+    uint32_t c[EPT];
+    double lsum = 0.0;
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) {
+      const int j = tid * EPT + e;
+      v[e] = j < len ? val[pos + j] : 0.0f;
+      c[e] = j < len ? cnt[pos + j] : 0u;
+      if (j < len) {
+        sm.v[j] = v[e];
+        sm.c[j] = c[e];
+      }
+      lsum += (double)v[e] * (double)c[e];
+    }
+    double dtot;
+    double a = (double)bitsf(s_bits) + block_excl_scan_add(lsum, sm.dscr, dtot);
+    // ---- classify ----
+    long long kk[EPT];
+    long long lk = 0;
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) {
+      const int j = tid * EPT + e;
+      kk[e] = 0;
+      if (j >= len) continue;
+      const double b = a + (double)v[e] * (double)c[e];
+      uint32_t lo_bits;
+      bool big, near;
+      if (a < 0x1p-126) {
+        lo_bits = 0u;
+        big = v[e] >= 0x1p-127f;
+        near = b > 0x1p-126 * (1.0 - MU);
+      } else {
+        const uint32_t ab = fbits(__double2float_rz(a));
+        lo_bits = ab & 0x7f800000u;
+        big = fbits(v[e]) >= lo_bits - 0x00800000u;
+        const double lo = (double)bitsf(lo_bits);
+        near = a < lo * (1.0 + MU) || b > 2.0 * lo * (1.0 - MU);
+      }
+      const bool q = tau_bits != NO_QUERY && (double)tauf <= b * (1.0 + MU) + 0x1p-149 &&
+                     (double)tauf >= a * (1.0 - MU);
+      bool sp = big || near || q;
+      if (!sp) {
+        const uint32_t k0 = fbits(fadd(bitsf(lo_bits), v[e])) - lo_bits;
+        const uint32_t k1 = fbits(fadd(bitsf(lo_bits + 1u), v[e])) - (lo_bits + 1u);
+        if (k0 != k1) sp = true;
+        else kk[e] = (long long)k0 * (long long)c[e];
+      }
+      sm.cls[j] = sp ? SPECIAL : lo_bits;
+      lk += kk[e];
+      a = b;
+    }
+    long long ktot;
+    long long kex = block_excl_scan_add(lk, sm.lscr, ktot);  // also orders cls[] writes
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) {
+      const int j = tid * EPT + e;
+      kex += kk[e];
+      if (j < len) sm.pinc[j] = kex;
+    }
+    // ---- segment heads ----
+    int hc = 0;
+    bool head[EPT];
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) {
+      const int j = tid * EPT + e;
+      head[e] = false;
+      if (j >= len) continue;
+      const uint32_t cur = sm.cls[j];
+      const uint32_t prev = j > 0 ? sm.cls[j - 1] : SPECIAL;
+      head[e] = j == 0 || cur == SPECIAL || prev == SPECIAL || cur != prev;
+      hc += head[e] ? 1 : 0;
+    }
+    int htot;
+    int hex = block_excl_scan_add(hc, sm.iscr, htot);
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) {
+      const int j = tid * EPT + e;
+      if (head[e]) {
+        sm.seg_start[hex] = (unsigned short)j;
+        sm.seg_lo[hex] = sm.cls[j];
+        ++hex;
+      }
+    }
+    __syncthreads();
+    // ---- walk the segments with the exact state ----
+    if (tid == 0) {
+      uint32_t s = s_bits;
+      long long newpos = pos + len;
+      for (int g = 0; g < htot; ++g) {
+        const int st = sm.seg_start[g];
+        const int en = (g + 1 < htot ? (int)sm.seg_start[g + 1] : len) - 1;
+        const uint32_t cl = sm.seg_lo[g];
+        if (cl == SPECIAL) {
+          s = exact_entry(pos + st, sm.v[st], sm.c[st], s);
+          if (sm.done) {
+            newpos = pos + st + 1;
+            break;
+          }
+          continue;
+        }
+        if (binade_lo_bits(s) != cl) {  // predicted binade wrong: restart here
+          newpos = pos + st;
+          break;
+        }
+        const long long base = st > 0 ? sm.pinc[st - 1] : 0ll;
+        const long long nb = (long long)s + (sm.pinc[en] - base);
+        if (nb >= (long long)binade_hi_bits(cl)) {  // left the binade inside the run
+          newpos = pos + st;
+          break;
+        }
+        if (sm.hit < 0 && nb >= (long long)tau_bits) {
+          int l = st, h = en;  // first entry jj whose last copy reaches tau
+          while (l < h) {
+            const int mid = (l + h) >> 1;
+            if ((long long)s + (sm.pinc[mid] - base) >= (long long)tau_bits) h = mid;
+            else l = mid + 1;
+          }
+          const long long before = (long long)s + ((l > st ? sm.pinc[l - 1] : base) - base);
+          const long long k = (sm.pinc[l] - (l > st ? sm.pinc[l - 1] : base)) / (long long)sm.c[l];
+          long long need = 1;  // copies of entry l until the fold reaches tau
+          if ((long long)tau_bits > before && k > 0) need = ((long long)tau_bits - before + k - 1) / k;
+          sm.hit = pos + l;
+          sm.hit_copy = need - 1;
+          sm.hit_s_bits = (uint32_t)(before + need * k);
+          if (stop_at_hit) {
+            sm.done = 1;
+            s = sm.hit_s_bits;
+            newpos = pos + l + 1;
+            break;
+          }
+        }
+        s = (uint32_t)nb;
+      }
+      if (newpos == pos) sm.seq_left = SEQ_STEP;  // no progress: entry by entry
+      sm.s_bits = s;
+      sm.pos = newpos;
+    }
+    __syncthreads();
+  }
+  RunResult r;
+  r.s_bits = sm.s_bits;
+  r.hit = sm.hit;
+  r.hit_copy = sm.hit_copy;
+  r.hit_s_bits = sm.hit_s_bits;
+  __syncthreads();
+  return r;
+}
+
 }  // namespace fold
 
 namespace sort {

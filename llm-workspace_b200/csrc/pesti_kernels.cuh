@@ -74,6 +74,8 @@ struct RowInfo {      // row prologue, written by the last slice_stats block of 
   float e_tau;        // exact exp(RN(tau/T) - m) when tau is finite, else 0
   float s_start;      // vocabulary shard: approximate softmax fold state at the shard's first
                       // column (the mass of the earlier shards); 0 for whole rows
+  float S;            // the cluster pass's exact softmax sum (rows it leaves with only[b] == 2)
+  float min_raw;      // the smallest raw logit (NaN ignored; the cluster pass only)
 };
 
 // One vocabulary shard of a row, summarised before the shards are combined
@@ -221,8 +223,10 @@ struct RowArgs {
   FoldEnt* ment_g;         // [B][FAST_ENTS] merged fold entries
   int* nment_g;            // [B] their count (-1: the row is not sampled from shards)
   // rows left by the cluster pass (only != null): a block samples its row only
-  // when only[b] != 0, from the whole row (no survivor lists) on the generic path
+  // when only[b] != 0, from the whole row (no survivor lists) on the generic
+  // path, or (only[b] == 2, nucleus != 0) a bf16 top-p row by distinct values
   const int* only;
+  int nucleus;  // the launch provides the nucleus rows' shared memory
 };
 
 // Exchange record of one row of one vocabulary shard (second phase).
@@ -823,6 +827,8 @@ __device__ void row_prologue(const SliceArgs& a, long long b, StatsShared& sh) {
     ri.uniform = uniform ? 1 : 0;
     ri.e_tau = tau > NEG_INF && tau < INF ? pesti_expf_call(fsub(scale ? fdiv(tau, T) : tau, m)) : 0.0f;
     ri.s_start = (float)ex0;
+    ri.S = 0.0f;
+    ri.min_raw = 0.0f;
     a.info[b] = ri;
   }
 }
@@ -2354,6 +2360,10 @@ __device__ uint32_t warp_fold(const void* raw, int dtype, long long n, uint32_t 
   return s;
 }
 
+}  // namespace pesti
+#include "pesti_nucleus.cuh"
+namespace pesti {
+
 __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
   grid_dep_wait();
   extern __shared__ __align__(16) unsigned char row_smem[];
@@ -2417,6 +2427,14 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
   const long long k = (long long)prm.top_k;
   const bool topp = prm.top_p > 0.0f && k == 0;
   const uint32_t r_tau = fold::tau_bits_of(r);
+
+  // top-p rows of bf16 logits whose softmax sum the cluster pass has folded:
+  // by distinct values (pesti_nucleus.cuh); the generic path if that fails
+  if (a.only && a.nucleus && a.only[b] == 2 && a.dtype == PESTI_BF16 && !ri.uniform) {
+    NucSmem& ns = *reinterpret_cast<NucSmem*>(row_smem + sizeof(RowShared));
+    if (nucleus_rows(a, b, ri, prm, (const uint16_t*)row, sh, ns)) return;
+    __syncthreads();
+  }
 
   if (ri.uniform) {
     // softmax sum is NaN or not > 0: every probability is 1/V (sampling.rs:129-133).

@@ -8,6 +8,9 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
+#include <cmath>
+#include <thread>
 #include <climits>
 #include <cstdio>
 #include <cstring>
@@ -45,6 +48,7 @@ int cuda_fail(cudaError_t e, const char* what) {
 }  // namespace
 
 constexpr size_t kRowSmemLimit = 220 * 1024;
+static_assert(sizeof(pesti::RowShared) + sizeof(pesti::NucSmem) <= kRowSmemLimit, "nucleus rows' shared memory");
 
 struct pesti_sampler {
   int device = 0;
@@ -140,6 +144,25 @@ bool needs_survivor_pass(const pesti_sampling_params* p, long long n, long long 
     if (!greedy && !(k >= 1 && k <= pesti::FAST_K)) return true;
   }
   return false;
+}
+
+// What the cluster pass can take of a batch whose host params are p[0..n):
+// 0 not every row (some row is neither greedy nor top-k <= 256, nor a bf16
+// top-p row), 1 every row greedy or top-k <= 256, 2 also bf16 top-p rows
+// (finished by the row kernel from the cluster's exact softmax sum).
+int cluster_kind(const pesti_sampling_params* p, long long n, long long V, pesti_dtype dtype) {
+  int kind = 1;
+  for (long long i = 0; i < n; ++i) {
+    const bool greedy = (p[i].flags & PESTI_FLAG_GREEDY_IF_ZERO_T) && p[i].temperature == 0.0f;
+    const long long k = std::min<long long>(p[i].top_k, V);
+    if (greedy || (k >= 1 && k <= pesti::FAST_K)) continue;
+    if (dtype == PESTI_BF16 && p[i].top_k == 0 && p[i].top_p > 0.0f) {
+      kind = 2;
+      continue;
+    }
+    return 0;
+  }
+  return kind;
 }
 
 bool needs_sorted_buffers(const pesti_sampling_params* p, long long n) {
@@ -461,8 +484,9 @@ pesti::RowArgs make_row_args(const Plan& p, char* ws, const pesti::SliceArgs& sa
 }
 
 int launch_row(const Plan& p, int device, const pesti::RowArgs& ra, cudaStream_t st) {
-  const size_t smem2 =
+  size_t smem2 =
       sizeof(pesti::RowShared) + (ra.fast_enabled ? pesti::fast_smem_bytes((int)p.nsub, ra.fast_ents) : 0);
+  if (ra.nucleus) smem2 = std::max(smem2, sizeof(pesti::RowShared) + sizeof(pesti::NucSmem));
   if (smem2 > 48 * 1024) {
     int rc = ensure_row_smem_limit(device);
     if (rc) return rc;
@@ -544,41 +568,70 @@ int cluster_max_for(int device, ClusterKernel kern, int kind) {
 }
 
 struct ClusterGeom {
-  int C;    // CTAs per row
-  int SLW;  // elements per warp
+  int C;  // CTAs per row
+  int wstart[pesti::CL_MAXC * pesti::CL_WARPS + 1];  // warp ranges (ClusterArgs::wstart)
 };
 
-// Cluster size and warp range for rows of V elements: 16 CTAs for short
-// batches (latency), 8 otherwise, each warp at most CL_SEGS segments.
+// Relative lengths of the first warp ranges of a row: there the running sum
+// is small, most elements survive the pruning and the state crosses binades
+// often, so those warps have more to do per element.
+constexpr double kHeadWeight[4] = {0.25, 0.25, 0.5, 0.5};
+
+// Cluster size and warp ranges for rows of V elements: 16 CTAs for short
+// batches (latency), 8 otherwise; every range a multiple of 32*VE elements and
+// at most CL_SEGS of them.
 bool cluster_geometry(long long B, long long V, int esize, int cmax, ClusterGeom& g) {
   const long long seg = 32LL * (16 / esize);
   const int forced = g_cluster_override.load(std::memory_order_relaxed);
+  auto standard = [&](int c) {  // the length of an ordinary warp range
+    const int n = c * pesti::CL_WARPS;
+    double w = 0.0;
+    for (int q = 0; q < n; ++q) w += q < 4 ? kHeadWeight[q] : 1.0;
+    const long long per = (long long)std::ceil((double)V / w);
+    return std::max(seg, (per + seg - 1) / seg * seg);
+  };
   int C = forced > 0 ? forced : (B <= 16 ? 16 : 8);
   if (C > cmax) C = cmax;
-  auto slw = [&](int c) {
-    const long long per = (V + (long long)c * pesti::CL_WARPS - 1) / ((long long)c * pesti::CL_WARPS);
-    return (per + seg - 1) / seg * seg;
-  };
-  if (forced <= 0 && slw(C) > pesti::CL_SEGS * seg && cmax >= 16) C = 16;
+  if (forced <= 0 && standard(C) > pesti::CL_SEGS * seg && cmax >= 16) C = 16;
   // no more CTAs than the row has warp ranges for
   const long long need = (V + pesti::CL_WARPS * seg - 1) / (pesti::CL_WARPS * seg);
   if ((long long)C > need && forced <= 0) C = (int)std::max(1LL, need);
-  const long long L = slw(C);
+  const long long L = standard(C);
   if (L > pesti::CL_SEGS * seg) return false;
+  const int n = C * pesti::CL_WARPS;
+  long long pos = 0;
+  for (int q = 0; q < n; ++q) {
+    const double wq = q < 4 ? kHeadWeight[q] : 1.0;
+    long long len = (long long)std::ceil(wq * (double)L / (double)seg) * seg;
+    g.wstart[q] = (int)std::min(pos, V);
+    pos += len;
+  }
+  g.wstart[n] = (int)V;
+  if (pos < V) return false;  // (cannot happen: the lengths sum to at least V)
   g.C = C;
-  g.SLW = (int)L;
   return true;
 }
 
-bool use_cluster_path(long long V, bool survivors) {
-  return !survivors && V >= 1 && V <= pesti::CL_MAX_V && g_cluster_override.load(std::memory_order_relaxed) >= 0;
+// Batches of at most this many rows take the cluster pass when they can (its
+// one launch per call is what a short batch's latency needs); longer batches
+// of top-k rows keep the four-kernel pipeline, which was faster on B200 at 64
+// rows of 128k (72.6 against 110 us per step) and at 1000 rows of 32k.
+constexpr long long kClusterMaxRows = 32;
+
+bool use_cluster_path(long long B, long long V, int esize, int ckind) {
+  const long long vmax = esize == 4 ? pesti::CL_MAX_V : pesti::CL_MAX_V16;
+  const int ov = g_cluster_override.load(std::memory_order_relaxed);
+  if (ov < 0 || ckind <= 0 || V < 1 || V > vmax) return false;
+  // bf16 top-p rows always (their sorted folds by distinct values need the
+  // cluster's exact softmax sum); others for short batches, or when a test forces it
+  return ckind == 2 || B <= kClusterMaxRows || ov > 0;
 }
 
 int run_cluster(const Plan& p, const ClusterGeom& cgm, char* ws, int device, cudaEvent_t* pev,
                 const void* d_logits, pesti_dtype dtype, long long B, long long V, long long ld,
                 const pesti_sampling_params& uni, const pesti_sampling_params* d_per_row, const float* d_u,
                 uint32_t* d_out, float* d_kept_p, uint32_t* d_kept_idx, long long kept_width,
-                int64_t* d_kept_count, cudaStream_t st) {
+                int64_t* d_kept_count, bool nucleus, cudaStream_t st) {
   const bool aligned = rows_aligned(d_logits, dtype, ld);
   pesti::ClusterArgs ca{};
   ca.logits = d_logits;
@@ -588,7 +641,7 @@ int run_cluster(const Plan& p, const ClusterGeom& cgm, char* ws, int device, cud
   ca.ld = ld;
   ca.uni = uni;
   ca.per_row = d_per_row;
-  ca.SLW = cgm.SLW;
+  std::memcpy(ca.wstart, cgm.wstart, sizeof(int) * (cgm.C * pesti::CL_WARPS + 1));
   ca.u = d_u;
   ca.out = d_out;
   ca.kept_p = d_kept_p;
@@ -597,7 +650,11 @@ int run_cluster(const Plan& p, const ClusterGeom& cgm, char* ws, int device, cud
   ca.kept_count = d_kept_count;
   ca.fb = (int*)(ws + p.o_fb);
   ca.info = (pesti::RowInfo*)(ws + p.o_info);
-  ca.band = 0x1p-12f;
+  // guard band: the speculation runs ahead of the fold by the mass the fold
+  // absorbs, which grows along the row (about 1.2e-4 of it at 128k columns,
+  // up to 6e-4 at 256k)
+  ca.band = V > 131072 ? 0x1p-10f : 0x1p-12f;
+  ca.nucleus = nucleus ? 1 : 0;
   // a short batch lets the row kernel's few blocks be scheduled while the
   // cluster pass runs (they wait for it on the device), hiding that launch
   ca.early_dependents = B <= 16 ? 1 : 0;
@@ -627,6 +684,7 @@ int run_cluster(const Plan& p, const ClusterGeom& cgm, char* ws, int device, cud
   pesti::RowArgs ra = make_row_args(p, ws, sa, d_u, d_out, d_kept_p, d_kept_idx, kept_width, d_kept_count);
   ra.only = ca.fb;
   ra.fast_enabled = 0;
+  ra.nucleus = nucleus ? 1 : 0;
   int rc = launch_row(p, device, ra, st);
   if (rc) return rc;
   if (pev) PESTI_CUDA_TRY(cudaEventRecord(pev[3], st), "cudaEventRecord(profile)");
@@ -635,11 +693,11 @@ int run_cluster(const Plan& p, const ClusterGeom& cgm, char* ws, int device, cud
 
 int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long B, long long V,
            long long ld, const pesti_sampling_params& uni, const pesti_sampling_params* d_per_row,
-           bool sorted_bufs, bool survivors, const float* d_u, uint32_t* d_out, float* d_kept_p,
+           bool sorted_bufs, bool survivors, int ckind, const float* d_u, uint32_t* d_out, float* d_kept_p,
            uint32_t* d_kept_idx, long long kept_width, int64_t* d_kept_count, cudaStream_t st) {
   const int esize = dtype == PESTI_F32 ? 4 : 2;
   ClusterGeom cgm{};
-  if (use_cluster_path(V, survivors)) {
+  if (use_cluster_path(B, V, esize, ckind)) {
     const int kind = (int)dtype * 2 + (rows_aligned(d_logits, dtype, ld) ? 1 : 0);
     const int cmax = cluster_max_for(s->device, cluster_kernel_for(dtype, kind & 1), kind);
     if (cluster_geometry(B, V, esize, cmax, cgm)) {
@@ -654,7 +712,7 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
           if (!pev[q]) PESTI_CUDA_TRY(cudaEventCreate(&pev[q]), "cudaEventCreate(profile)");
       }
       return run_cluster(p, cgm, (char*)s->ws, s->device, pev, d_logits, dtype, B, V, ld, uni, d_per_row, d_u,
-                         d_out, d_kept_p, d_kept_idx, kept_width, d_kept_count, st);
+                         d_out, d_kept_p, d_kept_idx, kept_width, d_kept_count, ckind == 2, st);
     }
   }
   Plan p = make_plan(s->num_sms, dtype, B, V, sorted_bufs);
@@ -679,11 +737,13 @@ int launch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long 
 // device array (the caller's, or the host entries copied to the handle's).
 int stage_params(pesti_sampler* s, const pesti_sampling_params* params, int params_per_row, int params_on_device,
                  long long B, long long V, cudaStream_t st, pesti_sampling_params& uni,
-                 const pesti_sampling_params*& d_per_row, bool& sorted_bufs, bool& survivors) {
+                 const pesti_sampling_params*& d_per_row, bool& sorted_bufs, bool& survivors,
+                 pesti_dtype dtype = PESTI_F32, int* ckind = nullptr) {
   uni = pesti_sampling_params{};
   d_per_row = nullptr;
   sorted_bufs = true;
   survivors = true;
+  if (ckind) *ckind = 0;  // params on the device: not known here
   if (params_on_device) {
     if (params_per_row) d_per_row = params;
     else {
@@ -692,10 +752,12 @@ int stage_params(pesti_sampler* s, const pesti_sampling_params* params, int para
       PESTI_CUDA_TRY(cudaStreamSynchronize(st), "params sync");
       sorted_bufs = needs_sorted_buffers(&uni, 1);
       survivors = needs_survivor_pass(&uni, 1, V);
+      if (ckind) *ckind = cluster_kind(&uni, 1, V, dtype);
     }
   } else if (params_per_row) {
     sorted_bufs = needs_sorted_buffers(params, B);
     survivors = needs_survivor_pass(params, B, V);
+    if (ckind) *ckind = cluster_kind(params, B, V, dtype);
     if ((size_t)B > s->h_params_cap) {
       if (s->params_ev_used) cudaEventSynchronize(s->params_ev);
       if (s->h_params) cudaFreeHost(s->h_params);
@@ -718,6 +780,7 @@ int stage_params(pesti_sampler* s, const pesti_sampling_params* params, int para
     uni = params[0];
     sorted_bufs = needs_sorted_buffers(&uni, 1);
     survivors = needs_survivor_pass(&uni, 1, V);
+    if (ckind) *ckind = cluster_kind(&uni, 1, V, dtype);
   }
   return PESTI_OK;
 }
@@ -738,6 +801,9 @@ struct NcclApi {
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
   ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
+  ncclResult_t (*comm_init_rank_config)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
 };
 
 const NcclApi& nccl_api() {
@@ -754,7 +820,11 @@ const NcclApi& nccl_api() {
     a.comm_destroy = (decltype(a.comm_destroy))dlsym(h, "ncclCommDestroy");
     a.all_gather = (decltype(a.all_gather))dlsym(h, "ncclAllGather");
     a.error_string = (decltype(a.error_string))dlsym(h, "ncclGetErrorString");
-    a.loaded = a.get_unique_id && a.comm_init_rank && a.comm_destroy && a.all_gather && a.error_string;
+    a.comm_init_rank_config = (decltype(a.comm_init_rank_config))dlsym(h, "ncclCommInitRankConfig");
+    a.get_async_error = (decltype(a.get_async_error))dlsym(h, "ncclCommGetAsyncError");
+    a.comm_abort = (decltype(a.comm_abort))dlsym(h, "ncclCommAbort");
+    a.loaded = a.get_unique_id && a.comm_init_rank && a.comm_destroy && a.all_gather && a.error_string &&
+               a.comm_init_rank_config && a.get_async_error && a.comm_abort;
     if (!a.loaded) a.err = "libnccl.so.2 lacks an entry point";
     return a;
   }();
@@ -773,7 +843,75 @@ struct pesti_comm {
   int rank = 0;
   int device = 0;
   ncclComm_t comm = nullptr;
+  int timeout_ms = 120000;  // deadline of the set-up and of each sharded call's exchanges
+  bool aborted = false;     // a deadline passed or an exchange failed: the communicator is gone
 };
+
+namespace {
+
+using Clock = std::chrono::steady_clock;
+
+Clock::time_point deadline_of(const pesti_comm* c) { return Clock::now() + std::chrono::milliseconds(c->timeout_ms); }
+
+void comm_abort(pesti_comm* c) {
+  if (c->comm && !c->aborted) nccl_api().comm_abort(c->comm);
+  c->aborted = true;
+}
+
+// Waits, on the host, until the communicator's pending operation (its
+// set-up, or the enqueueing of a collective) has completed: polls
+// ncclCommGetAsyncError until it no longer reports ncclInProgress.  An error,
+// or the deadline passing first, aborts the communicator.
+int comm_settle(pesti_comm* c, ncclResult_t issued, Clock::time_point deadline, const char* what) {
+  const NcclApi& n = nccl_api();
+  if (issued != ncclSuccess && issued != ncclInProgress) {
+    comm_abort(c);
+    return nccl_fail(issued, what);
+  }
+  for (;;) {
+    ncclResult_t st = ncclSuccess;
+    const ncclResult_t r = n.get_async_error(c->comm, &st);
+    if (r != ncclSuccess) {
+      comm_abort(c);
+      return nccl_fail(r, "ncclCommGetAsyncError");
+    }
+    if (st == ncclSuccess) return PESTI_OK;
+    if (st != ncclInProgress) {
+      comm_abort(c);
+      return nccl_fail(st, what);
+    }
+    if (Clock::now() >= deadline) {
+      comm_abort(c);
+      return fail(PESTI_E_TIMEOUT, std::string(what) + ": not complete after " + std::to_string(c->timeout_ms) +
+                                       " ms (a rank did not join or stopped); the communicator was aborted");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+// Waits for stream st with the communicator's deadline: the stream's work
+// includes the communicator's collectives, which wait for every rank.
+int stream_settle(pesti_comm* c, cudaStream_t st, Clock::time_point deadline, const char* what) {
+  const NcclApi& n = nccl_api();
+  for (;;) {
+    const cudaError_t e = cudaStreamQuery(st);
+    if (e == cudaSuccess) return PESTI_OK;
+    if (e != cudaErrorNotReady) return cuda_fail(e, what);
+    ncclResult_t as = ncclSuccess;
+    if (n.get_async_error(c->comm, &as) == ncclSuccess && as != ncclSuccess && as != ncclInProgress) {
+      comm_abort(c);
+      return nccl_fail(as, what);
+    }
+    if (Clock::now() >= deadline) {
+      comm_abort(c);
+      return fail(PESTI_E_TIMEOUT, std::string(what) + ": the exchanges did not finish within " +
+                                       std::to_string(c->timeout_ms) + " ms; the communicator was aborted");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+}  // namespace
 
 namespace {
 
@@ -952,10 +1090,16 @@ int shard_finish(const ShardPlan& sp, char* ws, const ShardCall& c) {
 
 // The rows listed by the finish (a host copy, sorted: every rank sees the
 // same list), and how many for each reason.  Synchronizes the stream.
-int read_flagged(const ShardPlan& sp, char* ws, cudaStream_t st, std::vector<int>& rows, long long* why) {
+int read_flagged(const ShardPlan& sp, char* ws, cudaStream_t st, std::vector<int>& rows, long long* why,
+                 pesti_comm* comm, Clock::time_point deadline) {
   int n = 0;
   PESTI_CUDA_TRY(cudaMemcpyAsync(&n, ws + sp.o_nflag, sizeof(int), cudaMemcpyDeviceToHost, st), "flag count copy");
-  PESTI_CUDA_TRY(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+  if (comm) {
+    const int rc = stream_settle(comm, st, deadline, "sharded exchanges");
+    if (rc) return rc;
+  } else {
+    PESTI_CUDA_TRY(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+  }
   rows.assign((size_t)n, 0);
   for (int q = 0; q < pesti::GR_KINDS; ++q) why[q] = 0;
   if (n > 0) {
@@ -1017,7 +1161,8 @@ int shard_gathered(pesti_sampler* s, pesti_comm* comm, const ShardPlan& sp, cons
         (const unsigned char*)local_logits, c.ld * esize, d_rows, (int)nf, sh_bytes, send, sh_bytes);
     PESTI_CUDA_TRY(cudaGetLastError(), "gather_rows_kernel launch");
     const ncclResult_t nr = nccl_api().all_gather(send, recv, (size_t)(nf * sh_bytes), ncclUint8, comm->comm, c.st);
-    if (nr != ncclSuccess) return nccl_fail(nr, "ncclAllGather(rows)");
+    const int src = comm_settle(comm, nr, deadline_of(comm), "ncclAllGather(rows)");
+    if (src) return src;
     for (int g = 0; g < sp.G; ++g)
       PESTI_CUDA_TRY(cudaMemcpy2DAsync(full + (size_t)g * sh_bytes, (size_t)row_bytes, recv + (size_t)g * nf * sh_bytes,
                                        (size_t)sh_bytes, (size_t)sh_bytes, (size_t)nf, cudaMemcpyDeviceToDevice, c.st),
@@ -1070,6 +1215,8 @@ int sample_sharded(pesti_sampler* s, pesti_comm* comm, int G, const void* d_logi
                    long long kept_width, int64_t* d_kept_count, void* stream) {
   PESTI_CUDA_TRY(cudaSetDevice(s->device), "cudaSetDevice");
   cudaStream_t st = (cudaStream_t)stream;  // NULL: the legacy default stream
+  if (comm && comm->aborted) return fail(PESTI_E_NCCL, "the communicator was aborted by an earlier failure");
+  const Clock::time_point deadline = comm ? deadline_of(comm) : Clock::time_point{};
   ShardCall c{};
   c.dtype = dtype;
   c.B = B;
@@ -1119,15 +1266,15 @@ int sample_sharded(pesti_sampler* s, pesti_comm* comm, int G, const void* d_logi
     if (rc) return rc;
     PESTI_CUDA_TRY(mark(1), "cudaEventRecord(profile)");
     ncclResult_t nr = n.all_gather(sum_send, sum_recv, (size_t)B * sizeof(pesti::ShardSum), ncclUint8, comm->comm, st);
-    if (nr != ncclSuccess) return nccl_fail(nr, "ncclAllGather(summaries)");
+    if ((rc = comm_settle(comm, nr, deadline, "ncclAllGather(summaries)"))) return rc;
     rc = shard_phase2(sp, ws, 0, comm->rank, s->device, c, d_logits, sum_recv, rec_send);
     if (rc) return rc;
     nr = n.all_gather(rec_send, rec_recv, (size_t)(B * sp.rec_stride), ncclUint8, comm->comm, st);
-    if (nr != ncclSuccess) return nccl_fail(nr, "ncclAllGather(records)");
+    if ((rc = comm_settle(comm, nr, deadline, "ncclAllGather(records)"))) return rc;
     rc = shard_phase3(sp, ws, 0, comm->rank, s->device, c, d_logits, rec_recv, tab_send);
     if (rc) return rc;
     nr = n.all_gather(tab_send, tab_recv, (size_t)B * sizeof(pesti::ShardTab), ncclUint8, comm->comm, st);
-    if (nr != ncclSuccess) return nccl_fail(nr, "ncclAllGather(tables)");
+    if ((rc = comm_settle(comm, nr, deadline, "ncclAllGather(tables)"))) return rc;
   } else {
     for (int g = 0; g < G; ++g)
       if ((rc = shard_phase1(sp, ws, g, c, lg(g), sum_recv + (size_t)g * B))) return rc;
@@ -1144,7 +1291,7 @@ int sample_sharded(pesti_sampler* s, pesti_comm* comm, int G, const void* d_logi
   PESTI_CUDA_TRY(mark(3), "cudaEventRecord(profile)");
   s->ctr_zero_rows = B;
   std::vector<int> rows;
-  rc = read_flagged(sp, ws, st, rows, s->last_gathered_why);
+  rc = read_flagged(sp, ws, st, rows, s->last_gathered_why, comm, deadline);
   if (rc) return rc;
   s->last_gathered_rows = (long long)rows.size();
   return shard_gathered(s, comm, sp, c, d_logits, d_logits, rows);
@@ -1229,9 +1376,11 @@ int pesti_sample_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype
   pesti_sampling_params uni{};
   const pesti_sampling_params* d_per_row = nullptr;
   bool sorted_bufs = true, survivors = true;
-  rc = stage_params(s, params, params_per_row, params_on_device, B, V, st, uni, d_per_row, sorted_bufs, survivors);
+  int ckind = 0;
+  rc = stage_params(s, params, params_per_row, params_on_device, B, V, st, uni, d_per_row, sorted_bufs, survivors,
+                    dtype, &ckind);
   if (rc) return rc;
-  return launch(s, d_logits, dtype, B, V, ld, uni, d_per_row, sorted_bufs, survivors, d_u, d_out_tokens,
+  return launch(s, d_logits, dtype, B, V, ld, uni, d_per_row, sorted_bufs, survivors, ckind, d_u, d_out_tokens,
                 d_kept_p, d_kept_idx, kept_width, d_kept_count, st);
 }
 
@@ -1246,7 +1395,7 @@ int pesti_argmax_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype
   pesti_sampling_params uni{};
   uni.temperature = 0.0f;
   uni.flags = PESTI_FLAG_GREEDY_IF_ZERO_T | (flags & PESTI_FLAG_ARGMAX_FIRST);
-  return launch(s, d_logits, dtype, B, V, ld, uni, nullptr, false, false, nullptr, d_out_tokens, nullptr,
+  return launch(s, d_logits, dtype, B, V, ld, uni, nullptr, false, false, 1, nullptr, d_out_tokens, nullptr,
                 nullptr, 0, nullptr, st);
 }
 
@@ -1270,7 +1419,8 @@ int pesti_sample_row_host(pesti_sampler* s, const float* h_logits, int64_t V,
     PESTI_CUDA_TRY(cudaMemcpyAsync(s->d_row, h_logits, (size_t)V * sizeof(float), cudaMemcpyHostToDevice, st), "logits copy");
   PESTI_CUDA_TRY(cudaMemcpyAsync(s->d_u1, &u, sizeof(float), cudaMemcpyHostToDevice, st), "u copy");
   int rc = launch(s, s->d_row, PESTI_F32, 1, V, std::max<int64_t>(V, 1), *params, nullptr,
-                  needs_sorted_buffers(params, 1), needs_survivor_pass(params, 1, V), s->d_u1, s->d_tok1, nullptr, nullptr, 0, nullptr, st);
+                  needs_sorted_buffers(params, 1), needs_survivor_pass(params, 1, V),
+                  cluster_kind(params, 1, V, PESTI_F32), s->d_u1, s->d_tok1, nullptr, nullptr, 0, nullptr, st);
   if (rc) return rc;
   uint32_t tok = 0;
   PESTI_CUDA_TRY(cudaMemcpyAsync(&tok, s->d_tok1, sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "token copy");
@@ -1356,10 +1506,15 @@ int pesti_comm_id(void* id) {
 }
 
 int pesti_comm_create(int world_size, int rank, const void* id, int device, pesti_comm** out) {
+  return pesti_comm_create_timed(world_size, rank, id, device, 120000, out);
+}
+
+int pesti_comm_create_timed(int world_size, int rank, const void* id, int device, int timeout_ms, pesti_comm** out) {
   if (!out || !id) return fail(PESTI_E_INVALID_ARG, "null argument");
   *out = nullptr;
   if (world_size < 1 || world_size > pesti::FIN_MAXG || rank < 0 || rank >= world_size)
     return fail(PESTI_E_INVALID_ARG, "bad world size or rank (1..64 ranks)");
+  if (timeout_ms < 1) return fail(PESTI_E_INVALID_ARG, "timeout_ms must be >= 1");
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(PESTI_E_NO_DEVICE, "no CUDA device available");
   if (device < 0 || device >= ndev) return fail(PESTI_E_INVALID_ARG, "device index out of range");
@@ -1368,21 +1523,33 @@ int pesti_comm_create(int world_size, int rank, const void* id, int device, pest
   PESTI_CUDA_TRY(cudaSetDevice(device), "cudaSetDevice");
   ncclUniqueId u;
   std::memcpy(&u, id, sizeof(u));
-  ncclComm_t comm = nullptr;
-  const ncclResult_t r = n.comm_init_rank(&comm, world_size, u, rank);
-  if (r != ncclSuccess) return nccl_fail(r, "ncclCommInitRank");
   pesti_comm* c = new pesti_comm();
   c->world = world_size;
   c->rank = rank;
   c->device = device;
-  c->comm = comm;
+  c->timeout_ms = timeout_ms;
+  // non-blocking: the set-up runs in the background and is polled with a
+  // deadline, so a rank that never joins cannot hang the others
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  const Clock::time_point deadline = deadline_of(c);
+  const ncclResult_t r = n.comm_init_rank_config(&c->comm, world_size, u, rank, &cfg);
+  if (!c->comm) {
+    delete c;
+    return nccl_fail(r == ncclSuccess ? ncclInternalError : r, "ncclCommInitRankConfig");
+  }
+  const int rc = comm_settle(c, r, deadline, "ncclCommInitRankConfig");
+  if (rc) {  // the communicator was aborted (ncclCommAbort frees it)
+    delete c;
+    return rc;
+  }
   *out = c;
   return PESTI_OK;
 }
 
 void pesti_comm_destroy(pesti_comm* c) {
   if (!c) return;
-  if (c->comm) {
+  if (c->comm && !c->aborted) {
     cudaSetDevice(c->device);
     nccl_api().comm_destroy(c->comm);
   }

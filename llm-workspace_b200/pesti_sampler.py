@@ -110,6 +110,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.pesti_comm_id.restype = c_int
     lib.pesti_comm_create.argtypes = [c_int, c_int, vp, c_int, ctypes.POINTER(vp)]
     lib.pesti_comm_create.restype = c_int
+    lib.pesti_comm_create_timed.argtypes = [c_int, c_int, vp, c_int, c_int, ctypes.POINTER(vp)]
+    lib.pesti_comm_create_timed.restype = c_int
     lib.pesti_comm_destroy.argtypes = [vp]
     lib.pesti_comm_destroy.restype = None
     lib.pesti_sample_batch_sharded.argtypes = [vp, vp, vp, c_int, i64, i64, i64, ctypes.POINTER(_Params), c_int,
@@ -419,9 +421,12 @@ class Comm:
     """A pesti_comm (an NCCL communicator over this process group's ranks) for
     Sampler.sample_batch_sharded.  Rank 0 makes the id (pesti_comm_id); it is
     broadcast over the default torch.distributed group, then every rank
-    calls pesti_comm_create.  Collective: every rank constructs it."""
+    calls pesti_comm_create_timed.  Collective: every rank constructs it.
+    timeout_ms bounds the set-up and each sharded call's exchanges (a rank
+    that does not join or stops makes the others fail with PESTI_E_TIMEOUT
+    instead of hanging)."""
 
-    def __init__(self, device: int):
+    def __init__(self, device: int, timeout_ms: int = 120000):
         import torch
         import torch.distributed as dist
         lib = load_library()
@@ -435,7 +440,7 @@ class Comm:
         dist.broadcast(t, 0)
         buf = (ctypes.c_uint8 * COMM_ID_BYTES).from_buffer_copy(bytes(t.cpu().tolist()))
         h = ctypes.c_void_p()
-        _check(lib.pesti_comm_create(world, rank, buf, int(device), ctypes.byref(h)))
+        _check(lib.pesti_comm_create_timed(world, rank, buf, int(device), int(timeout_ms), ctypes.byref(h)))
         self._h = h
         self._lib = lib
         self.rank, self.world, self.device = rank, world, device

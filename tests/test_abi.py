@@ -58,3 +58,9 @@ def test_invalid_arguments_are_rejected_without_a_device():
     # the device draws: a negative row count and a null state are refused before any device work
     assert lib.pesti_pcg32_seed(None, -1, 1, 0, None) == pesti_sampler.PESTI_E_INVALID_ARG
     assert lib.pesti_pcg32_draw(None, 4, None, None) == pesti_sampler.PESTI_E_INVALID_ARG
+    # a communicator needs a positive deadline; refused before any device or NCCL work
+    import ctypes
+    h = ctypes.c_void_p()
+    buf = (ctypes.c_uint8 * pesti_sampler.COMM_ID_BYTES)()
+    assert lib.pesti_comm_create_timed(2, 0, buf, 0, 0, ctypes.byref(h)) == pesti_sampler.PESTI_E_INVALID_ARG
+    assert lib.pesti_comm_create_timed(2, 2, buf, 0, 1000, ctypes.byref(h)) == pesti_sampler.PESTI_E_INVALID_ARG

@@ -1,10 +1,11 @@
 """The cluster pass (one thread-block cluster per row) against the oracle and
 against the four-kernel pipeline, through the C ABI.
 
-Batches whose rows are all greedy or top-k <= 256, at most 131072 columns
-long, take the cluster pass by default; pesti_testing_set_cluster(-1) sends
-them through the four-kernel pipeline instead, and 1..16 forces the cluster
-size.  Every result must be bit-identical to the oracle with exp correctly
+Batches of at most 32 rows that are all greedy or top-k <= 256, and batches
+with bf16 top-p rows, take the cluster pass by default;
+pesti_testing_set_cluster(-1) sends every batch through the four-kernel
+pipeline instead, and 1..16 sends every batch the cluster pass can take
+through it with that cluster size.  Every result must be bit-identical to the oracle with exp correctly
 rounded (tokens, kept lists, kept probabilities), whatever the cluster size,
 including the rows the cluster pass hands to the row kernel (NaN and infinite
 rows, too many tied candidates).
@@ -50,7 +51,7 @@ def test_cluster_pass_equals_the_pipeline(sampler, cluster_mode):
         u = synth.make_u(w, B)
         cluster_mode(-1)
         want = run_gpu(sampler, x, params, u)
-        cluster_mode(0)
+        cluster_mode(8)  # the cluster pass whatever the batch size
         got = run_gpu(sampler, x, params, u)
         for g, w_ in zip(got, want):
             assert np.array_equal(np.asarray(g).view(np.uint8), np.asarray(w_).view(np.uint8))
@@ -155,3 +156,53 @@ def test_cluster_single_rows_from_the_host(sampler, cluster_mode):
     for b in range(32):
         t = sampler.sample_with_u(x[b], ps.SamplingConfig(0.8, 0.95, 40), float(u[b]))
         assert t == O.sample(x[b], 0.8, 0.95, 40, float(u[b]), O.EXP_CR)
+
+
+def _nucleus_cases():
+    """bf16 rows with top-p (the cluster pass folds S, the row kernel takes the
+    sorted folds by distinct values), including what that path hands on to
+    the generic sorted path."""
+    rng = np.random.default_rng(33)
+    bf = lambda a: synth.bf16_bits_to_f32(synth.f32_to_bf16_bits(np.asarray(a, np.float32)))
+    cases = []
+    x = synth.make_logits(3, B=6)
+    cases.append(("workload3", x, [(1.0, 0.95, 0)] * 6))
+    x = bf(rng.standard_normal((4, 20000)) * 2)
+    cases.append(("top-p 1.0 and 1e-6", x, [(0.9, 1.0, 0), (1.1, 1e-6, 0), (0.7, 0.5, 0), (1.0, 0.999, 0)]))
+    x = bf(np.zeros((2, 5000)))
+    x[1, ::7] = 1.0
+    cases.append(("constant and two-valued", x, [(1.0, 0.9, 0), (1.0, 0.3, 0)]))
+    x = bf(rng.standard_normal((3, 9000)) * 1e-6)  # magnitudes far below the top binade
+    x[0, 5] = 3.0
+    cases.append(("tiny magnitudes", x, [(1.0, 0.9, 0), (0.5, 0.99, 0), (2.0, 0.2, 0)]))
+    x = bf(-np.abs(rng.standard_normal((2, 7000))) * 3 - 1)  # only negative logits
+    cases.append(("negative", x, [(1.0, 0.9, 0), (0.8, 0.7, 0)]))
+    x = bf(np.round(rng.standard_normal((3, 30000)) * 4) / 4)  # few distinct values, big groups
+    cases.append(("few values", x, [(1.0, 0.95, 0), (0.6, 0.8, 0), (1.3, 0.1, 0)]))
+    x = bf(rng.standard_normal((4, 40000)) * 2)
+    cases.append(("mixed kinds", x, [(1.0, 0.9, 0), (0.7, 0.0, 50), (0.0, 0.0, 0), (1.0, 0.95, 0)]))
+    return cases
+
+
+@pytest.mark.parametrize("case", _nucleus_cases(), ids=lambda c: c[0])
+@pytest.mark.parametrize("kw", [KW, 2000])
+def test_cluster_nucleus_rows(sampler, cluster_mode, case, kw):
+    """bf16 top-p rows: tokens, kept lists (their first kw entries) and kept
+    counts bit for bit against the oracle, and equal to the four-kernel
+    pipeline's."""
+    name, x, params = case
+    B = x.shape[0]
+    cluster_mode(0)
+    for u in (np.zeros(B, np.float32), np.full(B, 0.5, np.float32), np.full(B, np.float32(0.99999994)),
+              synth.make_u(3, B)):
+        got = run_gpu(sampler, x, params, u, bf16=True, kept_width=kw)
+        want = O.sample_batch(x, params, u, O.EXP_CR, kept_width=kw)
+        tok, kp, ki, kc = got
+        assert np.array_equal(tok, want["tokens"]), (name, tok, want["tokens"])
+        assert np.array_equal(kc, want["kept_count"]), name
+        assert np.array_equal(ki, want["kept_idx"]), name
+        assert np.array_equal(kp.view(np.uint32), want["kept_p"].view(np.uint32)), name
+    cluster_mode(-1)
+    pipe = run_gpu(sampler, x, params, u, bf16=True, kept_width=kw)
+    for g, w_ in zip(got, pipe):
+        assert np.array_equal(np.asarray(g).view(np.uint8), np.asarray(w_).view(np.uint8))

@@ -75,6 +75,76 @@ struct NucOrder {
   __device__ __forceinline__ int length() const { return NUC_HALF + ntp + 1 + ntn + NUC_HALF; }
 };
 
+// Eight consecutive bf16 logits from j (one 16-byte load when the row is
+// aligned and whole there), widened; u16[e] = 0 past V with nv the valid count.
+__device__ __forceinline__ void nuc_load8(const uint16_t* row, long long j, long long V, bool vec, uint16_t (&h)[8],
+                                          int& nv) {
+  if (vec && j + 8 <= V) {
+    const uint4 w4 = __ldg(reinterpret_cast<const uint4*>(row + j));
+    const uint32_t wd[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      h[2 * q] = (uint16_t)(wd[q] & 0xffffu);
+      h[2 * q + 1] = (uint16_t)(wd[q] >> 16);
+    }
+    nv = 8;
+    return;
+  }
+  nv = 0;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const bool in = j + e < V;
+    h[e] = in ? row[j + e] : (uint16_t)0;
+    nv = in ? e + 1 : nv;
+  }
+}
+
+// The elements of the row that satisfy pred, in index order: those whose
+// ranks among them lie in [first, first + count) are passed to emit(rank, j).
+// Each warp owns a contiguous chunk of the row and reads it 32 elements at a
+// time (coalesced); the chunks' counts give each warp its first rank.  The
+// whole block calls it.
+template <typename Pred, typename Emit>
+__device__ void nuc_ordered(const uint16_t* row, long long V, bool vec, Pred pred, long long first, long long count,
+                            Emit emit, RowShared& sh) {
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  constexpr int NW = K2_NT / 32;
+  const long long chunk = ((V + NW - 1) / NW + 255) / 256 * 256;  // whole 256-element steps of the warp
+  const long long c0 = (long long)wid * chunk, c1 = c0 + chunk < V ? c0 + chunk : V;
+  int n = 0;
+  for (long long j = c0 + lane * 8; j < c1; j += 256) {
+    uint16_t h[8];
+    int nv;
+    nuc_load8(row, j, c1, vec, h, nv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) n += (e < nv && pred(bf16_bits_to_f32(h[e]))) ? 1 : 0;
+  }
+  n = warp_reduce_add(n);
+  __syncthreads();
+  if (lane == 0) sh.iscr[wid] = n;
+  __syncthreads();
+  long long k = 0;
+  for (int q = 0; q < wid; ++q) k += sh.iscr[q];
+  if (k + n > first && k < first + count) {
+    for (long long j0 = c0; j0 < c1 && k < first + count; j0 += 256) {
+      const long long j = j0 + lane * 8;
+      uint16_t h[8];
+      int nv = 0;
+      if (j < c1) nuc_load8(row, j, c1, vec, h, nv);
+      uint32_t hm = 0u;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) hm |= (e < nv && pred(bf16_bits_to_f32(h[e]))) ? (1u << e) : 0u;
+      const int c = __popc(hm);
+      const int inc = warp_incl_scan_add(c);
+      long long r = k + inc - c;
+      for (uint32_t mm = hm; mm != 0u; mm &= mm - 1u, ++r)
+        if (r >= first && r < first + count) emit(r, j + __ffs(mm) - 1);
+      k += __shfl_sync(PESTI_FULL_MASK, inc, 31);
+    }
+  }
+  __syncthreads();
+}
+
 __device__ bool nucleus_rows(const RowArgs& a, long long b, const RowInfo& ri, const pesti_sampling_params& prm,
                              const uint16_t* row, RowShared& sh, NucSmem& ns) {
   const int tid = threadIdx.x;
@@ -93,21 +163,29 @@ __device__ bool nucleus_rows(const RowArgs& a, long long b, const RowInfo& ri, c
     ns.ntiny = 0;
   }
   __syncthreads();
-  // ---- histogram of the row ----
-  for (long long j = tid; j < V; j += K2_NT) {
-    const uint32_t u = ((uint32_t)row[j]) << 16;
-    if ((u & 0x7fffffffu) == 0u) {
-      atomicAdd(&ns.zero, 1u);
-      continue;
-    }
-    const int s = nuc_slot(u, E_lo);
-    if (s >= 0) {
-      atomicAdd(&ns.u.h.tab[s], 1u);
-    } else {
-      const int t = atomicAdd(&ns.ntiny, 1);
-      if (t < NUC_TINY) {
-        ns.u.h.tiny_v[t] = u;
-        ns.u.h.tiny_i[t] = (uint32_t)j;
+  // ---- histogram of the row: eight elements per thread and step ----
+  const bool vec = ((uintptr_t)row % 16) == 0;
+  for (long long j = (long long)tid * 8; j < V; j += (long long)K2_NT * 8) {
+    uint16_t h[8];
+    int nv;
+    nuc_load8(row, j, V, vec, h, nv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (e >= nv) continue;
+      const uint32_t u = ((uint32_t)h[e]) << 16;
+      if ((u & 0x7fffffffu) == 0u) {
+        atomicAdd(&ns.zero, 1u);
+        continue;
+      }
+      const int s = nuc_slot(u, E_lo);
+      if (s >= 0) {
+        atomicAdd(&ns.u.h.tab[s], 1u);
+      } else {
+        const int t = atomicAdd(&ns.ntiny, 1);
+        if (t < NUC_TINY) {
+          ns.u.h.tiny_v[t] = u;
+          ns.u.h.tiny_i[t] = (uint32_t)(j + e);
+        }
       }
     }
   }
@@ -265,35 +343,12 @@ __device__ bool nucleus_rows(const RowArgs& a, long long b, const RowInfo& ri, c
   __syncthreads();
   // group g holds the values in [gmin[g], gmin[g-1]) (descending, contiguous)
   auto in_group = [&](float x, long long g) { return x >= ns.gmin[g] && (g == 0 || x < ns.gmin[g - 1]); };
-  // the t-th element (index order) of group g: contiguous chunks of the row per
-  // thread, counted, then found inside the chunk that holds it
-  auto nth_of_group = [&](long long g, long long t) -> long long {
-    const long long chunk = (V + K2_NT - 1) / K2_NT;
-    const long long c0 = tid * chunk, c1 = c0 + chunk < V ? c0 + chunk : V;
-    long long n = 0;
-    for (long long j = c0; j < c1; ++j) n += in_group(bf16_bits_to_f32(row[j]), g) ? 1 : 0;
-    long long tot;
-    const long long ex = block_excl_scan_add(n, sh.lscr, tot);
-    if (tid == 0) sh.n = -1;
-    __syncthreads();
-    if (t >= ex && t < ex + n) {
-      long long k = ex;
-      for (long long j = c0; j < c1; ++j) {
-        if (in_group(bf16_bits_to_f32(row[j]), g)) {
-          if (k == t) {
-            sh.n = j;
-            break;
-          }
-          ++k;
-        }
-      }
-    }
-    __syncthreads();
-    const long long res = sh.n;
-    __syncthreads();
-    return res;
-  };
-  const long long tok = nth_of_group(dg, dc);
+  // the dc-th element (index order) of group dg
+  if (tid == 0) sh.n = -1;
+  nuc_ordered(row, V, vec, [&](float x) { return in_group(x, dg); }, dc, 1,
+              [&](long long, long long j) { sh.n = j; }, sh);
+  const long long tok = sh.n;
+  __syncthreads();
   if (tok < 0) return false;
   // ---- the kept list's first kept_width entries ----
   const long long kw = a.kept_width < K ? a.kept_width : K;
@@ -318,17 +373,24 @@ __device__ bool nucleus_rows(const RowArgs& a, long long b, const RowInfo& ri, c
     if (tid == 0) ns.nkey = 0;
     __syncthreads();
     const float lim = gl > 0 ? ns.gmin[gl - 1] : __int_as_float(0x7f800000);
-    for (long long j = tid; j < V && pl > 0; j += K2_NT) {
-      const float x = bf16_bits_to_f32(row[j]);
-      if (x >= lim) {
-        int lo2 = 0, hi2 = (int)gl - 1;  // its group: the first g with x >= gmin[g]
-        while (lo2 < hi2) {
-          const int mid = (lo2 + hi2) >> 1;
-          if (x >= ns.gmin[mid]) hi2 = mid;
-          else lo2 = mid + 1;
+    for (long long j0 = (long long)tid * 8; j0 < V && pl > 0; j0 += (long long)K2_NT * 8) {
+      uint16_t h[8];
+      int nv;
+      nuc_load8(row, j0, V, vec, h, nv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float x = bf16_bits_to_f32(h[e]);
+        if (e < nv && x >= lim) {
+          int lo2 = 0, hi2 = (int)gl - 1;  // its group: the first g with x >= gmin[g]
+          while (lo2 < hi2) {
+            const int mid = (lo2 + hi2) >> 1;
+            if (x >= ns.gmin[mid]) hi2 = mid;
+            else lo2 = mid + 1;
+          }
+          const int slot = atomicAdd(&ns.nkey, 1);
+          if (slot < NUC_KEPT)
+            ns.u.kkey[slot] = ((unsigned long long)(0xffffffffu - (uint32_t)lo2) << 32) | (uint32_t)~(uint32_t)(j0 + e);
         }
-        const int slot = atomicAdd(&ns.nkey, 1);
-        if (slot < NUC_KEPT) ns.u.kkey[slot] = ((unsigned long long)(0xffffffffu - (uint32_t)lo2) << 32) | (uint32_t)~(uint32_t)j;
       }
     }
     __syncthreads();
@@ -348,22 +410,12 @@ __device__ bool nucleus_rows(const RowArgs& a, long long b, const RowInfo& ri, c
       if (a.kept_idx) a.kept_idx[b * a.kept_width + j] = ~(uint32_t)(kv & 0xffffffffull);
     }
     // then the first kw - pl elements of group gl, in index order
-    const long long need = kw - pl;
-    {
-      const long long chunk = (V + K2_NT - 1) / K2_NT;
-      const long long c0 = tid * chunk, c1 = c0 + chunk < V ? c0 + chunk : V;
-      long long n = 0;
-      for (long long j = c0; j < c1; ++j) n += in_group(bf16_bits_to_f32(row[j]), gl) ? 1 : 0;
-      long long tot;
-      long long k = block_excl_scan_add(n, sh.lscr, tot);
-      for (long long j = c0; j < c1 && k < need; ++j) {
-        if (in_group(bf16_bits_to_f32(row[j]), gl)) {
-          if (a.kept_p) a.kept_p[b * a.kept_width + pl + k] = ns.gp[gl];
-          if (a.kept_idx) a.kept_idx[b * a.kept_width + pl + k] = (uint32_t)j;
-          ++k;
-        }
-      }
-    }
+    const float pgl = ns.gp[gl];
+    nuc_ordered(row, V, vec, [&](float x) { return in_group(x, gl); }, 0, kw - pl,
+                [&](long long r, long long j) {
+                  if (a.kept_p) a.kept_p[b * a.kept_width + pl + r] = pgl;
+                  if (a.kept_idx) a.kept_idx[b * a.kept_width + pl + r] = (uint32_t)j;
+                }, sh);
   }
   for (long long j = kw + tid; j < a.kept_width; j += K2_NT) {
     if (a.kept_p) a.kept_p[b * a.kept_width + j] = 0.0f;

@@ -78,19 +78,20 @@ L2_BYTES = 126 * 1024 * 1024
 TRAFFIC_PER_STEP = {}
 
 
-def cluster_pass(V, params, bf16=False):
+def cluster_pass(V, params, bf16=False, mode=0):
     """The batch takes the cluster pass: every row greedy (T == 0), top-k
     <= 256 or (bf16) top-p, rows of at most 131072 columns (262144 for bf16),
-    and either some bf16 top-p row or at most 32 rows."""
-    if not 1 <= V <= (262144 if bf16 else 131072):
+    and either some bf16 top-p row, at most 32 rows, or the pass forced
+    (mode > 0); mode -1 sends every batch through the pipeline."""
+    if mode < 0 or not 1 <= V <= (262144 if bf16 else 131072):
         return False
     nuc = [bf16 and k == 0 and p > 0 for (t, p, k) in params]
     if not all(t == 0.0 or 1 <= k <= 256 or n for (t, p, k), n in zip(params, nuc)):
         return False
-    return any(nuc) or len(params) <= 32
+    return any(nuc) or len(params) <= 32 or mode > 0
 
 
-def kernels_per_step(V, params, bf16=False):
+def kernels_per_step(V, params, bf16=False, mode=0):
     """This library's launches in one step.  The cluster pass: the cluster
     kernel and the row kernel (whose blocks return at once unless the cluster
     left their row).  Otherwise: the HBM pass; the fused pass (rows beyond 128k
@@ -98,7 +99,7 @@ def kernels_per_step(V, params, bf16=False):
     on the top-k fast path), plus the survivor pass when some row is off that
     path, else the survivor pass and the task-queue classification; the row
     kernel."""
-    if cluster_pass(V, params, bf16):
+    if cluster_pass(V, params, bf16, mode):
         return 2
     off_fast = any(not (1 <= k <= 256) or t <= 0 for (t, _, k) in params)
     fused = V > 131072 or (V <= 65536 and not off_fast and len(params) >= 32)
@@ -472,6 +473,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernels-only", action="store_true",
                     help="only the warm-up and timed steps (for profiler captures); prints ms_per_step")
+    ap.add_argument("--cluster", type=int, default=0,
+                    help="path of the batch: 0 the library's routing, -1 the four-kernel pipeline, "
+                         "1..16 the cluster pass with that many CTAs per row (profiles of either path)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -521,6 +525,7 @@ def main():
     cfgs = (ps.SamplingConfig(*params[0]) if len(set(params)) == 1
             else ps.PreparedParams([ps.SamplingConfig(t, p, k) for (t, p, k) in params]))
     s = ps.Sampler(local)
+    ps.set_cluster_mode(args.cluster)
     stream = torch.cuda.current_stream(dev)
 
     def step(i):
@@ -657,7 +662,7 @@ def main():
                          "threads; C++ restatement of sampling.rs:39-134 with glibc expf"}
 
     if rank == 0:
-        nk = kernels_per_step(V, params, bf16)
+        nk = kernels_per_step(V, params, bf16, args.cluster)
         line = {
             "metric": metric_for(w), "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -665,13 +670,15 @@ def main():
             "config": {"workload": spec["name"], "B": B_total, "B_per_gpu": B, "V": V, "input_dtype": spec["dtype"],
                        "params": params_text(w),
                        "l2": f"rotating {nbuf} input buffers ({nbuf * step_bytes / 2**20:.0f} MiB > 126 MiB L2)",
-                       "parallelism": f"row blocks of {B} rows on each of {world} GPU(s), no collective"},
+                       "parallelism": f"row blocks of {B} rows on each of {world} GPU(s), no collective",
+                       "path": ("cluster pass" if cluster_pass(V, params, bf16, args.cluster) else "four-kernel pipeline")
+                       + (f" (forced, --cluster {args.cluster})" if args.cluster else "")},
             "roofline": {"bound": "hbm", "kernel": f"whole step ({nk} launches)", "achieved": achieved,
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": TRAFFIC_PER_STEP.get(w) if world == 1 else None,
                          "bytes_per_launch": step_bytes,
                          "kernels": ({"row_cluster": kern(scan_ms), "row (rows the cluster pass left)": kern(row_ms)}
-                                     if cluster_pass(V, params, bf16) else
+                                     if cluster_pass(V, params, bf16, args.cluster) else
                                      {"slice_stats": kern(scan_ms), "survivor+classify": kern(surv_ms),
                                       "row": kern(row_ms)})},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": step_bytes + B * 4,

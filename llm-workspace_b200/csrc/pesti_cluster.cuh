@@ -57,6 +57,9 @@ constexpr int CL_EW = 48;               // fold entries per warp (beyond: its ra
 constexpr int CL_LIST = 128;            // merged fold entries per CTA (beyond: its range is replayed)
 constexpr int CL_CCAP = 256;            // top-k candidates per CTA
 constexpr int CL_LOCAL = 512;           // fold entries of a row the leader gathers
+constexpr int CL_RGRP = CL_NT - 32;     // the leader's replay group: every warp but warp 1
+constexpr int CL_RPT = 4;               // replayed elements per thread and chunk
+constexpr int CL_RCH = CL_RGRP * CL_RPT;  // replayed elements per chunk
 constexpr long long CL_MAX_V = 131072;  // longest row of the cluster path (f32)
 constexpr long long CL_MAX_V16 = 262144;  // the same for 16-bit logits
 static_assert(CL_SEGS <= 32, "one lane per segment in the warp summary");
@@ -134,9 +137,67 @@ struct ClShared {
       int coff[CL_MAXC + 1];
       int ccnt[CL_MAXC + 1];
       int nent, ncand;
+      int rep_fi[2];            // walk -> replay group: the entry to replay (-1: done), by parity
+      uint32_t rep_s;           // the exact state at the start of a replay chunk
+      int rcnt[CL_RPT * (CL_WARPS - 1)];  // kept elements per (element slot, group warp)
+      float rstage[CL_RCH];     // a replay chunk's kept exps, in row order
     } f;
   } u;
 };
+
+// Named barrier of the leader's replay group (warps 0 and 2..7).
+__device__ __forceinline__ void cl_rbar() { asm volatile("bar.sync 1, %0;" ::"n"(CL_RGRP) : "memory"); }
+
+// Fold of the exps of the row's elements [from, to) from the exact state s
+// (held by warp 0) by the replay group; the result is warp 0's.  Per chunk of
+// CL_RCH elements every thread takes the exact exps of its elements.  An
+// element whose addition leaves both an even and an odd state of the chunk's
+// starting binade unchanged (its exp is below half that binade's ulp) is
+// dropped: the state never decreases, so the exp stays below half the ulp
+// of every binade the state can reach.  Warp 0 folds the rest in row order.
+__device__ uint32_t cl_replay(const void* row, int dtype, uint32_t from, uint32_t to, uint32_t s, bool scale,
+                              float T, float m, ClShared& sh) {
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int gt = w == 0 ? lane : tid - 32;  // 0 .. CL_RGRP-1 in row order
+  const int gw = gt >> 5;
+  const uint32_t lt = (1u << lane) - 1u;
+  for (uint32_t base = from; base < to; base += CL_RCH) {
+    if (tid == 0) sh.u.f.rep_s = s;
+    cl_rbar();
+    const uint32_t lo = fold::binade_lo_bits(sh.u.f.rep_s);
+    float e[CL_RPT];
+    uint32_t bm[CL_RPT];
+#pragma unroll
+    for (int k = 0; k < CL_RPT; ++k) {
+      const uint32_t idx = base + (uint32_t)(k * CL_RGRP + gt);
+      const bool valid = idx < to;
+      e[k] = 0.0f;
+      if (valid) {
+        const float xr = load_logit_dyn(row, dtype, (long long)idx);
+        e[k] = pesti_expf_call(fsub(scale ? fdiv(xr, T) : xr, m));  // sampling.rs:46,127
+      }
+      const bool kept = valid && (fbits(fadd(bitsf(lo), e[k])) != lo || fbits(fadd(bitsf(lo + 1u), e[k])) != lo + 1u);
+      bm[k] = __ballot_sync(PESTI_FULL_MASK, kept);
+      if (lane == 0) sh.u.f.rcnt[k * (CL_WARPS - 1) + gw] = __popc(bm[k]);
+    }
+    cl_rbar();
+    int off[CL_RPT], tot = 0;
+#pragma unroll
+    for (int k = 0; k < CL_RPT; ++k) off[k] = 0;
+    for (int j = 0; j < CL_RPT * (CL_WARPS - 1); ++j) {
+      const int c = sh.u.f.rcnt[j];
+#pragma unroll
+      for (int k = 0; k < CL_RPT; ++k) off[k] += j < k * (CL_WARPS - 1) + gw ? c : 0;
+      tot += c;
+    }
+#pragma unroll
+    for (int k = 0; k < CL_RPT; ++k)
+      if ((bm[k] >> lane) & 1u) sh.u.f.rstage[off[k] + __popc(bm[k] & lt)] = e[k];
+    cl_rbar();
+    if (w == 0) s = warp_fold_staged(sh.u.f.rstage, tot, s);
+  }
+  return s;
+}
 
 // Candidate threshold: a lower bound of the keff-th largest raw logit, from
 // the row's segment maxima (vals, NV per thread, -inf where none; maxima of
@@ -625,11 +686,10 @@ __global__ void __launch_bounds__(CL_NT, 4) row_cluster_kernel(ClusterArgs a) {
                 exact = E < 40u;  // else the exact value (< 2^-126) rounds to 0 on this grid
               } else {
                 const float tt = __uint_as_float(fbits(ea) + sc);
-                const float kr = rintf(tt);
+                const float kr = rint_small(tt, kd);
                 const float de = scale ? fmaf(2.0f * fabsf(xv * rT) + 3.0f * fabsf(zq), DE_Z, DE_0)
                                        : fmaf(-zq, DE_Z, DE_0);
-                exact = !(0.5f - fabsf(tt - kr) > tt * de + 0x1p-24f);
-                kd = (uint32_t)kr;
+                exact = !(tt < 0x1p22f && 0.5f - fabsf(tt - kr) > tt * de + 0x1p-24f);
               }
               kseg += exact ? 0u : kd;
               und |= exact ? (1u << e) : 0u;
@@ -744,9 +804,10 @@ __global__ void __launch_bounds__(CL_NT, 4) row_cluster_kernel(ClusterArgs a) {
                 need = E < 40u;  // else the exact value (< 2^-126) rounds to 0 on this grid
               } else {
                 const float tt = __uint_as_float(fbits(eaj) + ((uint32_t)(150 - (int)E) << 23));  // ea/w
-                const float kr = rintf(tt);
-                need = !(0.5f - fabsf(tt - kr) > tt * dej + 0x1p-24f);
-                k0 = k1 = (uint32_t)kr;
+                uint32_t kq;
+                const float kr = rint_small(tt, kq);
+                need = !(tt < 0x1p22f && 0.5f - fabsf(tt - kr) > tt * dej + 0x1p-24f);
+                k0 = k1 = kq;
               }
             }
             if (need) {
@@ -840,38 +901,57 @@ __global__ void __launch_bounds__(CL_NT, 4) row_cluster_kernel(ClusterArgs a) {
 
   // ---------------- the CTA's entries, merged, in row order ----------------
   if (decided < 0 && tid == 0) {
+    // the warps of repl (a bit mask) and the warps that overflowed become one
+    // replay marker each; false when the merged list does not fit
     int nl = 0;
-    uint32_t last = KEY_NONE;
-    bool full = false;
-    const long long cta_end = a.wstart[(cr + 1) * CL_WARPS];
-    for (int q = 0; q < CL_WARPS && !full; ++q) {
-      const long long ws0 = a.wstart[cr * CL_WARPS + q];
-      if (ws0 >= V) break;
-      const int n = sh.wn[q];
-      if (n < 0) {
-        const long long we = a.wstart[cr * CL_WARPS + q + 1];
-        if (nl < CL_LIST) sh.list[nl++] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)we};
-        else full = true;
-        last = ENT_REPLAY;
-        continue;
-      }
-      for (int i = 0; i < n; ++i) {
-        const FoldEnt e = sh.u.c.went[q][i];
-        if (e.lo != fold::SPECIAL && e.lo == last) {
-          const Tr t = tr_compose(Tr{sh.list[nl - 1].a0, sh.list[nl - 1].a1}, Tr{e.a0, e.a1});
-          sh.list[nl - 1] = FoldEnt{e.lo, t.a0, t.a1, e.end};
-        } else if (nl < CL_LIST) {
-          sh.list[nl++] = e;
-        } else {
-          full = true;
-          break;
+    auto merge = [&](uint32_t repl) -> bool {
+      nl = 0;
+      uint32_t last = KEY_NONE;
+      for (int q = 0; q < CL_WARPS; ++q) {
+        const long long ws0 = a.wstart[cr * CL_WARPS + q];
+        if (ws0 >= V) break;
+        const int n = sh.wn[q];
+        if (n < 0 || ((repl >> q) & 1u)) {
+          const long long we = a.wstart[cr * CL_WARPS + q + 1];
+          if (last == ENT_REPLAY) {
+            sh.list[nl - 1].end = (uint32_t)we;
+          } else {
+            if (nl >= CL_LIST) return false;
+            sh.list[nl++] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)we};
+          }
+          last = ENT_REPLAY;
+          continue;
         }
-        last = e.lo;
+        for (int i = 0; i < n; ++i) {
+          const FoldEnt e = sh.u.c.went[q][i];
+          if (e.lo != fold::SPECIAL && e.lo == last) {
+            const Tr t = tr_compose(Tr{sh.list[nl - 1].a0, sh.list[nl - 1].a1}, Tr{e.a0, e.a1});
+            sh.list[nl - 1] = FoldEnt{e.lo, t.a0, t.a1, e.end};
+          } else {
+            if (nl >= CL_LIST) return false;
+            sh.list[nl++] = e;
+          }
+          last = e.lo;
+        }
       }
-    }
-    if (full) {  // too many entries: the walk folds the CTA's whole range
-      sh.list[0] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)cta_end};
-      nl = 1;
+      return true;
+    };
+    // too many entries: the warps with the most entries are replayed in the
+    // walk instead, one at a time, until the list fits
+    uint32_t repl = 0u;
+    while (!merge(repl)) {
+      int best = -1, bn = 0;
+      for (int q = 0; q < CL_WARPS; ++q)
+        if (!((repl >> q) & 1u) && sh.wn[q] > bn) {
+          bn = sh.wn[q];
+          best = q;
+        }
+      if (best < 0) {  // cannot happen (CL_WARPS markers fit): the whole range
+        sh.list[0] = FoldEnt{ENT_REPLAY, 0u, 0u, (uint32_t)a.wstart[(cr + 1) * CL_WARPS]};
+        nl = 1;
+        break;
+      }
+      repl |= 1u << best;
     }
     sh.nlist = nl;
   }
@@ -954,47 +1034,55 @@ __global__ void __launch_bounds__(CL_NT, 4) row_cluster_kernel(ClusterArgs a) {
         warp_bitonic_desc(key, mm2);
       }
     }
-    if (w == 0) {
-      // softmax denominator (sampling.rs:128): the entries with the exact state;
-      // an entry the state does not fit (or a replay marker) is folded from the
-      // raw logits of its range, from the state before it
+    if (w != 1) {
+      // softmax denominator (sampling.rs:128): warp 0 walks the entries with the
+      // exact state; an entry the state does not fit (or a replay marker) is
+      // folded from the raw logits of its range, from the state before it, by
+      // the replay group (warps 0, 2..7)
       const FoldEnt* fent = sh.u.f.ent;
       const int nm = sh.u.f.nent;
       uint32_t s = 0u;
       constexpr int WB = 8;
       int i = 0;
-      while (i < nm) {
+      for (int it = 0;; ++it) {
         int fi = -1;
-        FoldEnt nx[WB];
+        if (w == 0 && i < nm) {
+          FoldEnt nx[WB];
 #pragma unroll
-        for (int uu = 0; uu < WB; ++uu) nx[uu] = fent[i + uu < nm ? i + uu : nm - 1];
-        for (; i < nm; i += WB) {
-          FoldEnt en[WB];
+          for (int uu = 0; uu < WB; ++uu) nx[uu] = fent[i + uu < nm ? i + uu : nm - 1];
+          for (; i < nm; i += WB) {
+            FoldEnt en[WB];
 #pragma unroll
-          for (int uu = 0; uu < WB; ++uu) {
-            en[uu] = nx[uu];
-            const int kk = i + WB + uu;
-            nx[uu] = fent[kk < nm ? kk : nm - 1];
+            for (int uu = 0; uu < WB; ++uu) {
+              en[uu] = nx[uu];
+              const int kk = i + WB + uu;
+              nx[uu] = fent[kk < nm ? kk : nm - 1];
+            }
+#pragma unroll
+            for (int uu = 0; uu < WB; ++uu) {
+              const bool live = fi < 0 && i + uu < nm;
+              const bool sp = en[uu].lo == fold::SPECIAL;
+              const uint32_t s_sp = fbits(fadd(bitsf(s), bitsf(en[uu].a0)));
+              const uint32_t ns = s + ((s & 1u) ? en[uu].a1 : en[uu].a0);
+              const bool fits = fold::binade_lo_bits(s) == en[uu].lo && ns < fold::binade_hi_bits(en[uu].lo);
+              fi = live && !sp && !fits ? i + uu : fi;
+              s = live && (sp || fits) ? (sp ? s_sp : ns) : s;
+            }
+            if (fi >= 0) break;
           }
-#pragma unroll
-          for (int uu = 0; uu < WB; ++uu) {
-            const bool live = fi < 0 && i + uu < nm;
-            const bool sp = en[uu].lo == fold::SPECIAL;
-            const uint32_t s_sp = fbits(fadd(bitsf(s), bitsf(en[uu].a0)));
-            const uint32_t ns = s + ((s & 1u) ? en[uu].a1 : en[uu].a0);
-            const bool fits = fold::binade_lo_bits(s) == en[uu].lo && ns < fold::binade_hi_bits(en[uu].lo);
-            fi = live && !sp && !fits ? i + uu : fi;
-            s = live && (sp || fits) ? (sp ? s_sp : ns) : s;
-          }
-          if (fi >= 0) break;
         }
+        // the entry to replay, double-buffered by parity: a group warp reads
+        // slot it&1 before the barrier that lets warp 0 write it again
+        if (tid == 0) sh.u.f.rep_fi[it & 1] = fi;
+        cl_rbar();
+        fi = sh.u.f.rep_fi[it & 1];
         if (fi < 0) break;
         const uint32_t from = fi > 0 ? fent[fi - 1].end : 0u;
         const uint32_t to = fent[fi].end;
-        s = warp_fold(row + from, a.dtype, (long long)to - from, s, sh.u.f.stage, scale, T, m);
+        s = cl_replay(row, a.dtype, from, to, s, scale, T, m, sh);
         i = fi + 1;
       }
-      sh.uscr[0] = s;
+      if (tid == 0) sh.uscr[0] = s;
     }
     __syncthreads();
     if (nuc) {  // S for the row kernel's sorted folds by distinct values

@@ -335,6 +335,16 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // 2^-24 of exp(z)) the relative error is below
 // PESTI_EX2_APPROX_RELERR + (|z| + 1) 2^-24 * 1.001 whenever it is not 0; it is
 // 0 only when exp(z) < 2^-126 (y below -126, where subnormal results flush).
+// rint(t) for 0 <= t < 2^23 (round to nearest even, as rintf) and its
+// integer k, by one float addition of 2^23: in [2^23, 2^24) the floats are
+// the integers, and k is the distance of the sum's bits from 2^23's.  This
+// keeps the rounding and the conversion off the special-function pipe.
+__device__ __forceinline__ float rint_small(float t, uint32_t& k) {
+  const float r = __fadd_rn(t, 0x1p23f);
+  k = __float_as_uint(r) - 0x4b000000u;
+  return __fsub_rn(r, 0x1p23f);
+}
+
 __device__ __forceinline__ float exp_hw(float z) {
   return ex2_approx(__fmaf_rn(z, 0x1.715476p+0f, __fmul_rn(z, 0x1.4ae0c0p-26f)));
 }
@@ -1318,10 +1328,11 @@ __device__ __forceinline__ float classify_group(const SliceArgs& a, long long b,
         need_exact = E < 40u;  // exact e < 4.5e-38: rounds to 0 on any grid >= 2^-110
       } else {
         const float tt = __uint_as_float(fbits(ea) + ((uint32_t)sh2 << 23));  // ea/w, exact scaling
-        const float kr = rintf(tt);
+        uint32_t kq;
+        const float kr = rint_small(tt, kq);
         const float slack = 0.5f - fabsf(tt - kr);
-        if (slack <= tt * DE + 0x1p-24f) need_exact = true;
-        else k0 = k1 = (uint32_t)kr;
+        if (!(tt < 0x1p22f) || slack <= tt * DE + 0x1p-24f) need_exact = true;
+        else k0 = k1 = kq;
       }
     }
     if (need_exact) {
@@ -1380,10 +1391,11 @@ __device__ __forceinline__ float classify_group(const SliceArgs& a, long long b,
         exact = (clo >> 23) < 40u;  // else: exact e < 1.2e-38 rounds to 0 on this grid
       } else {
         const float tt = __uint_as_float(fbits(e) + ((uint32_t)sh2 << 23));  // e/w, exact scaling
-        const float kr = rintf(tt);
+        uint32_t kq;
+        const float kr = rint_small(tt, kq);
         const float slack = 0.5f - fabsf(tt - kr);
-        exact = !(slack > tt * fmaf(-z, DE_Z, DE_0) + 0x1p-24f);
-        if (!exact) ksum += (uint32_t)kr;
+        exact = !(tt < 0x1p22f && slack > tt * fmaf(-z, DE_Z, DE_0) + 0x1p-24f);
+        if (!exact) ksum += kq;
       }
       if (exact) undecided |= 1u << jj;
     }
@@ -1919,10 +1931,11 @@ __global__ void __launch_bounds__(K1_NT, 3) fused_classify_kernel(SliceArgs a) {
             exact = (clo >> 23) < 40u;  // else: exact e < 1.2e-38 rounds to 0 on this grid
           } else {
             const float tt = __uint_as_float(fbits(ea) + ((uint32_t)sh2 << 23));  // ea/w, exact scaling
-            const float kr = rintf(tt);
+            uint32_t kq;
+            const float kr = rint_small(tt, kq);
             const float slack = 0.5f - fabsf(tt - kr);
-            exact = !(slack > tt * fmaf(-z, DE_Z, DE_0) + 0x1p-24f);
-            if (!exact) ksum += (uint32_t)kr;
+            exact = !(tt < 0x1p22f && slack > tt * fmaf(-z, DE_Z, DE_0) + 0x1p-24f);
+            if (!exact) ksum += kq;
           }
           if (exact) undecided |= 1u << jj;
         }
@@ -2308,11 +2321,51 @@ __device__ __forceinline__ fold::Result serial_fold8(const float* v, long long n
   return r;
 }
 
+// Fold of len values in shared memory, in order, by one warp from state s
+// (bits): each step takes 32 of them with a transducer scan over the lanes,
+// adds the first one that would leave the binade (or is large next to s)
+// directly, and resumes after it.  All 32 lanes must call it; the result is
+// warp-uniform.
+__device__ __forceinline__ uint32_t warp_fold_staged(const float* stage, int len, uint32_t s) {
+  const int lane = threadIdx.x & 31;
+  int j = 0;
+  while (j < len) {
+    const int idx = j + lane;
+    const bool valid = idx < len;
+    const float x = valid ? stage[idx] : 0.0f;
+    const uint32_t lo = fold::binade_lo_bits(s);
+    const uint32_t hi = fold::binade_hi_bits(lo);
+    const bool big = valid && (lo == 0u ? x >= 0x1p-127f : fbits(x) >= lo - 0x00800000u);
+    Tr t{0u, 0u};
+    if (valid && !big) {
+      t.a0 = fbits(fadd(bitsf(lo), x)) - lo;
+      t.a1 = fbits(fadd(bitsf(lo + 1u), x)) - (lo + 1u);
+    }
+    const Tr incl = tr_warp_incl_scan(t);
+    const unsigned long long sum = (unsigned long long)s + ((s & 1u) ? incl.a1 : incl.a0);
+    const uint32_t after = sum > 0xffffffffull ? 0xffffffffu : (uint32_t)sum;
+    const bool bad = valid && (big || after >= hi);
+    const uint32_t badm = __ballot_sync(PESTI_FULL_MASK, bad);
+    const int nvalid = len - j < 32 ? len - j : 32;
+    if (badm == 0u) {
+      s = __shfl_sync(PESTI_FULL_MASK, after, nvalid - 1);
+      j += nvalid;
+    } else {
+      const int f0 = __ffs(badm) - 1;
+      const uint32_t prev = __shfl_sync(PESTI_FULL_MASK, after, f0 > 0 ? f0 - 1 : 0);
+      const uint32_t before = f0 > 0 ? prev : s;  // lanes < f0 are exact
+      const float xf = __shfl_sync(PESTI_FULL_MASK, x, f0);
+      s = fbits(fadd(bitsf(before), xf));
+      j += f0 + 1;
+    }
+  }
+  return s;
+}
+
 // Fold of the exps of n raw logits (f32 or bf16, in global memory) by one
 // warp, starting from state s (bits).  The exact exps are staged STAGE at a
-// time in shared memory; each step takes 32 of them with a transducer scan
-// over the lanes, adds the first one that would leave the binade (or is large
-// next to s) directly, and resumes after it.  All 32 lanes must call it.
+// time in shared memory and folded by warp_fold_staged.  All 32 lanes must
+// call it.
 __device__ uint32_t warp_fold(const void* raw, int dtype, long long n, uint32_t s, float* stage, bool scale,
                               float T, float m) {
   const int lane = threadIdx.x & 31;
@@ -2324,37 +2377,7 @@ __device__ uint32_t warp_fold(const void* raw, int dtype, long long n, uint32_t 
       stage[i] = pesti_expf_call(fsub(scale ? fdiv(xr, T) : xr, m));  // sampling.rs:46,127
     }
     __syncwarp();
-    int j = 0;
-    while (j < len) {
-      const int idx = j + lane;
-      const bool valid = idx < len;
-      const float x = valid ? stage[idx] : 0.0f;
-      const uint32_t lo = fold::binade_lo_bits(s);
-      const uint32_t hi = fold::binade_hi_bits(lo);
-      const bool big = valid && (lo == 0u ? x >= 0x1p-127f : fbits(x) >= lo - 0x00800000u);
-      Tr t{0u, 0u};
-      if (valid && !big) {
-        t.a0 = fbits(fadd(bitsf(lo), x)) - lo;
-        t.a1 = fbits(fadd(bitsf(lo + 1u), x)) - (lo + 1u);
-      }
-      const Tr incl = tr_warp_incl_scan(t);
-      const unsigned long long sum = (unsigned long long)s + ((s & 1u) ? incl.a1 : incl.a0);
-      const uint32_t after = sum > 0xffffffffull ? 0xffffffffu : (uint32_t)sum;
-      const bool bad = valid && (big || after >= hi);
-      const uint32_t badm = __ballot_sync(PESTI_FULL_MASK, bad);
-      const int nvalid = len - j < 32 ? len - j : 32;
-      if (badm == 0u) {
-        s = __shfl_sync(PESTI_FULL_MASK, after, nvalid - 1);
-        j += nvalid;
-      } else {
-        const int f0 = __ffs(badm) - 1;
-        const uint32_t prev = __shfl_sync(PESTI_FULL_MASK, after, f0 > 0 ? f0 - 1 : 0);
-        const uint32_t before = f0 > 0 ? prev : s;  // lanes < f0 are exact
-        const float xf = __shfl_sync(PESTI_FULL_MASK, x, f0);
-        s = fbits(fadd(bitsf(before), xf));
-        j += f0 + 1;
-      }
-    }
+    s = warp_fold_staged(stage, len, s);
   }
   __syncwarp();
   return s;

@@ -50,6 +50,7 @@ constexpr int CL_MAXC = 16;             // CTAs per cluster (row)
 constexpr int CL_SEGS = 20;             // 32*VE-element segments per warp at most
 constexpr int CL_U = 4;                 // segments loaded at once per warp (pass 1)
 constexpr int CL_STAGES = 4;            // segments in flight per warp through shared memory (pass 2)
+constexpr int CL_P1S = 8;               // segments in flight per warp through shared memory (pass 1)
 constexpr int CL_R = 4;                 // survivors per lane in one classification batch
 constexpr int CL_BATCH = 32 * CL_R;     // survivors classified together
 constexpr int CL_RING = 256;            // survivor ring per warp (power of two)
@@ -119,6 +120,9 @@ struct ClShared {
   int iscr[34];
   uint32_t uscr[34];
   union {
+    struct {                  // pass 1: the HBM stream's ring of segments per warp
+      float4 ring[CL_WARPS][CL_P1S * 32];
+    } r;
     struct {                  // the candidate threshold (combine)
       uint32_t hist[256];
       float tau;
@@ -316,40 +320,94 @@ __global__ void __launch_bounds__(CL_NT, 4) row_cluster_kernel(ClusterArgs a) {
     float gmax = NEG_INF;   // greedy rows: the lane's max, with its indices
     uint32_t lflags = 0u;
     int lnan = -1, lfirst = -1, llast = -1;
+    // whole segments of aligned rows stream through a ring of CL_P1S
+    // segments per warp (cp.async, each lane its own 16 bytes), so that the
+    // next segments' loads are in flight while one is processed
+    const int nfull1 = VEC ? (int)((s1 - s0) / SEG) : 0;
+    float4* ring = sh.u.r.ring[w];
+    if (VEC) {
+#pragma unroll
+      for (int st = 0; st < CL_P1S; ++st) {
+        if (st < nfull1) cp_async16(&ring[st * 32 + lane], row + s0 + (long long)st * SEG + lane * VE);
+        cp_async_commit();
+      }
+    }
     for (int q0 = 0; q0 < nseg; q0 += CL_U) {
       float x[CL_U][VE];
       int nv[CL_U];
 #pragma unroll
       for (int uu = 0; uu < CL_U; ++uu) {
+        const int q = q0 + uu;
         nv[uu] = 0;
-        if (q0 + uu < nseg) cl_load<TIn, VE, VEC>(row, s0 + (long long)(q0 + uu) * SEG + lane * VE, s1, x[uu], nv[uu]);
+        if (VEC && q < nfull1) {
+          cp_async_wait<CL_P1S - 1>();  // segment q has arrived
+          const float4 r4 = ring[(q % CL_P1S) * 32 + lane];
+          if (sizeof(TIn) == 4) {
+            x[uu][0] = r4.x; x[uu][1] = r4.y; x[uu][2] = r4.z; x[uu][3] = r4.w;
+          } else {
+            const uint32_t wds[4] = {__float_as_uint(r4.x), __float_as_uint(r4.y), __float_as_uint(r4.z),
+                                     __float_as_uint(r4.w)};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) unpack2<TIn>(wds[h], x[uu][2 * h], x[uu][2 * h + 1]);
+          }
+          nv[uu] = VE;
+          const int qn = q + CL_P1S;  // the slot just read takes segment q + CL_P1S
+          if (qn < nfull1) cp_async16(&ring[(q % CL_P1S) * 32 + lane], row + s0 + (long long)qn * SEG + lane * VE);
+          cp_async_commit();
+        } else if (q < nseg) {
+          cl_load<TIn, VE, VEC>(row, s0 + (long long)q * SEG + lane * VE, s1, x[uu], nv[uu]);
+        }
       }
+      float lsu[CL_U];  // the lane's part of each segment's mass
 #pragma unroll
       for (int uu = 0; uu < CL_U; ++uu) {
-        if (q0 + uu >= nseg) break;
+        lsu[uu] = 0.0f;
+        if (q0 + uu >= nseg) continue;
         const long long p0 = s0 + (long long)(q0 + uu) * SEG + lane * VE;
         float smax = NEG_INF;
+        if (nv[uu] == VE) {
+          // a whole lane: fmaxf/fminf skip NaN (as f32::max does), the
+          // infinities show in the lane's max and min, NaN in one flag
+          float smin = INF;
+          bool nan = false;
 #pragma unroll
-        for (int e = 0; e < VE; ++e) {
-          const float v = x[uu][e];
-          const bool in = e < nv[uu];
-          if (in) {
-            if (is_nan(v)) {
-              lflags |= MF_NAN;
-              lnan = (int)(p0 + e);
-            } else {
-              if (v == INF) lflags |= MF_POSINF;
-              if (v == NEG_INF) lflags |= MF_NEGINF;
-              smax = fmaxf(smax, v);
-              lmin = fminf(lmin, v);
-              if (greedy) {  // first and last index of the lane's max so far
-                if (lfirst < 0 || v > gmax) {
-                  gmax = v;
-                  lfirst = (int)(p0 + e);
-                  llast = lfirst;
-                } else if (v == gmax) {
-                  llast = (int)(p0 + e);
-                }
+          for (int e = 0; e < VE; ++e) {
+            const float v = x[uu][e];
+            smax = fmaxf(smax, v);
+            smin = fminf(smin, v);
+            nan = nan || is_nan(v);
+          }
+          lmin = fminf(lmin, smin);
+          lflags |= (smax == INF ? MF_POSINF : 0u) | (smin == NEG_INF ? MF_NEGINF : 0u);
+          if (nan) {  // rare: the flag and the last NaN's index
+            lflags |= MF_NAN;
+#pragma unroll
+            for (int e = 0; e < VE; ++e) lnan = is_nan(x[uu][e]) ? (int)(p0 + e) : lnan;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < VE; ++e) {
+            const float v = x[uu][e];
+            const bool in = e < nv[uu];
+            const bool nan = in && is_nan(v);
+            const bool ok = in && !nan;
+            lflags |= (nan ? MF_NAN : 0u) | (ok && v == INF ? MF_POSINF : 0u) | (ok && v == NEG_INF ? MF_NEGINF : 0u);
+            lnan = nan ? (int)(p0 + e) : lnan;
+            smax = fmaxf(smax, ok ? v : NEG_INF);
+            lmin = fminf(lmin, ok ? v : INF);
+          }
+        }
+        if (greedy) {  // first and last index of the lane's max so far (greedy is row-uniform)
+#pragma unroll
+          for (int e = 0; e < VE; ++e) {
+            const float v = x[uu][e];
+            if (e < nv[uu] && !is_nan(v)) {
+              if (lfirst < 0 || v > gmax) {
+                gmax = v;
+                lfirst = (int)(p0 + e);
+                llast = lfirst;
+              } else if (v == gmax) {
+                llast = (int)(p0 + e);
               }
             }
           }
@@ -365,13 +423,28 @@ __global__ void __launch_bounds__(CL_NT, 4) row_cluster_kernel(ClusterArgs a) {
           for (int e = 0; e < VE; ++e)
             if (e < nv[uu] && !is_nan(x[uu][e])) ls += ex2_approx(fmaf(x[uu][e], c2, -ym));
         }
-        const float smass = warp_reduce_add(ls);
-        if (lane == 0) {
-          sh.segmax[w][q0 + uu] = segm;
-          sh.segmass[w][q0 + uu] = smass;
-        }
+        lsu[uu] = ls;
+        if (lane == 0) sh.segmax[w][q0 + uu] = segm;
+      }
+      // the CL_U masses summed over the lanes together: halves of the values
+      // are exchanged (lane bit 4, then bit 3), then each lane's one value is
+      // reduced over the 8 lanes that share it; lane 8*uu ends with mass uu
+      static_assert(CL_U == 4, "the transposed reduction takes four values");
+      {
+        const bool h16 = (lane & 16) != 0, h8 = (lane & 8) != 0;
+        const float k0 = h16 ? lsu[2] : lsu[0], k1 = h16 ? lsu[3] : lsu[1];
+        const float s0v = h16 ? lsu[0] : lsu[2], s1v = h16 ? lsu[1] : lsu[3];
+        const float b0 = k0 + __shfl_xor_sync(PESTI_FULL_MASK, s0v, 16);
+        const float b1 = k1 + __shfl_xor_sync(PESTI_FULL_MASK, s1v, 16);
+        float c = (h8 ? b1 : b0) + __shfl_xor_sync(PESTI_FULL_MASK, h8 ? b0 : b1, 8);
+        c += __shfl_xor_sync(PESTI_FULL_MASK, c, 4);
+        c += __shfl_xor_sync(PESTI_FULL_MASK, c, 2);
+        c += __shfl_xor_sync(PESTI_FULL_MASK, c, 1);
+        const int uu = lane >> 3;  // (bit 4, bit 3) = the value's index
+        if ((lane & 7) == 0 && q0 + uu < nseg) sh.segmass[w][q0 + uu] = c;
       }
     }
+    if (VEC) cp_async_wait<0>();  // the ring's last (empty) groups; its space is reused after pass 1
     for (int q = nseg + lane; q < CL_SEGS; q += 32) {
       sh.segmax[w][q] = NEG_INF;
       sh.segmass[w][q] = 0.0f;
@@ -674,26 +747,22 @@ __global__ void __launch_bounds__(CL_NT, 4) row_cluster_kernel(ClusterArgs a) {
           const uint32_t E = lo >> 23;
           const uint32_t sc = (uint32_t)(150 - (int)E) << 23;  // e/w = e * 2^(150-E)
           uint32_t kseg = 0u, und = 0u;  // und: elements the approximation leaves undecided
+          // branch-free per element: an exp that flushed to 0 is an exact
+          // value below 2^-126, which rounds to 0 on a grid of E >= 40
 #pragma unroll
           for (int e = 0; e < VE; ++e) {
-            if (e < nv) {
-              const float xv = x[e];
-              const float zq = scale ? fmaf(xv, rT, -m) : fsub(xv, m);
-              const float ea = exp_hw(zq);
-              bool exact;
-              uint32_t kd = 0u;
-              if (ea == 0.0f) {
-                exact = E < 40u;  // else the exact value (< 2^-126) rounds to 0 on this grid
-              } else {
-                const float tt = __uint_as_float(fbits(ea) + sc);
-                const float kr = rint_small(tt, kd);
-                const float de = scale ? fmaf(2.0f * fabsf(xv * rT) + 3.0f * fabsf(zq), DE_Z, DE_0)
-                                       : fmaf(-zq, DE_Z, DE_0);
-                exact = !(tt < 0x1p22f && 0.5f - fabsf(tt - kr) > tt * de + 0x1p-24f);
-              }
-              kseg += exact ? 0u : kd;
-              und |= exact ? (1u << e) : 0u;
-            }
+            const float xv = x[e];
+            const float zq = fmaf(xv, rT, -m);  // rT = 1 for unscaled rows: exactly fl(x - m)
+            const float ea = exp_hw(zq);
+            const float tt = __uint_as_float(fbits(ea) + sc);
+            uint32_t kd;
+            const float kr = rint_small(tt, kd);
+            const float de = fmaf(arg_margin(xv, rT, zq), DE_Z, DE_0);
+            const bool in = e < nv;
+            const bool dec = ea != 0.0f && tt < 0x1p22f && 0.5f - fabsf(tt - kr) > tt * de + 0x1p-24f;
+            const bool zero = ea == 0.0f && E >= 40u;
+            kseg += in && dec ? kd : 0u;
+            und |= in && !dec && !zero ? (1u << e) : 0u;
           }
           bool tie = false;
 #pragma unroll 1
@@ -778,14 +847,16 @@ __global__ void __launch_bounds__(CL_NT, 4) row_cluster_kernel(ClusterArgs a) {
           const bool valid = i < n;
           const float raw = valid ? qraw[i] : 0.0f;
           const uint32_t idx = valid ? qidx[i] : 0u;
-          const float zj = valid ? fsub(scale ? fdiv(raw, T) : raw, m) : 0.0f;  // sampling.rs:46,127
-          const float eaj = valid ? exp_hw(zj) : 0.0f;
+          // the approximate argument x*rT - m (its margin in dej); the exact
+          // z = fl(fl(x/T) - m) (sampling.rs:46,127) only where an exact exp is taken
+          const float zq = valid ? fmaf(raw, rT, -m) : 0.0f;  // rT = 1 for unscaled rows: exactly fl(x - m)
+          const float eaj = valid ? exp_hw(zq) : 0.0f;
           const float incl = warp_incl_scan_add(eaj);
           float excl = __shfl_up_sync(PESTI_FULL_MASK, incl, 1);
           if (lane == 0) excl = 0.0f;
           const float av = sbj + excl;  // approximate state before the element
           const float bv = av + eaj;    // and after it
-          const float dej = fmaf(-zj, DE_Z, DE_0);
+          const float dej = fmaf(arg_margin(raw, rT, zq), DE_Z, DE_0);
           uint32_t key = KEY_NONE, k0 = 0u, k1 = 0u;
           if (valid) {
             bool special = !(av >= 0x1p-126f);
@@ -811,7 +882,8 @@ __global__ void __launch_bounds__(CL_NT, 4) row_cluster_kernel(ClusterArgs a) {
               }
             }
             if (need) {
-              const float ex = pesti_expf_call(zj);  // sampling.rs:127, exact
+              const float zj = fsub(scale ? fdiv(raw, T) : raw, m);  // sampling.rs:46,127
+              const float ex = pesti_expf_call(zj);                   // exact
               if (special) {
                 k0 = fbits(ex);
               } else {

@@ -349,8 +349,17 @@ __device__ __forceinline__ float exp_hw(float z) {
   return ex2_approx(__fmaf_rn(z, 0x1.715476p+0f, __fmul_rn(z, 0x1.4ae0c0p-26f)));
 }
 // Twice that bound (the margin the decisions below keep), as DE_0 + |z| DE_Z.
+// From the approximate argument z' = fl(x*rT - m) (rT = fl(1/T)) instead of
+// the reference's z = fl(fl(x/T) - m), z' - z is within (|x*rT| + |z'|) 2^-23
+// (1 + 2^-20), so exp_hw(z') is within DE_0/2 + DE_Z (|x*rT| + 1.5 |z'|) of
+// exp(z) relative, and the decisions keep DE_0 + DE_Z * arg_margin.
 constexpr float DE_Z = 0x1.01p-23f;  // >= 2 * 1.001 * 2^-24
 constexpr float DE_0 = 2.0f * PESTI_EX2_APPROX_RELERR + DE_Z;
+// (rT = 1 for unscaled rows, where fmaf(x, 1, -m) is exactly fl(x - m); the
+// scaled rows' margin is valid, and larger, there too.)
+__device__ __forceinline__ float arg_margin(float x, float rT, float zq) {
+  return fmaf(2.0f, fabsf(x * rT), 3.0f * fabsf(zq));
+}
 
 // Programmatic dependent launch: a kernel lets the next one in the stream be
 // scheduled early (launch_dependents) and the next one waits for the
@@ -1374,17 +1383,20 @@ __device__ __forceinline__ float classify_group(const SliceArgs& a, long long b,
   const int sh2 = 150 - (int)(clo >> 23);  // w = 2^(E-150) (E = 0: the subnormal grid 2^-149)
   uint32_t ksum = 0u, undecided = 0u;  // undecided: bit jj, element jj of the lane
   // pass A: approximate exps of the reference's arguments z = x/T - m
-  // (sampling.rs:46,127; z exact, exp within DE_0/2 + |z| DE_Z/2)
+  // (sampling.rs:46,127), from the approximate argument x*rT - m: within
+  // (DE_0 + arg_margin * DE_Z) / 2 of the exact exp
+  const float rT = scale ? 1.0f / T : 1.0f;
   float ltot = 0.0f;
-  float zmax = 0.0f;  // the largest |z| of the lane's elements with e > 0
+  float zmax = 0.0f;  // the largest arg_margin of the lane's elements with e > 0
 #pragma unroll 1
   for (int jj = 0; jj < nl; ++jj) {
     const float raw = graw[i0 + jj];
-    const float z = fsub(scale ? fdiv(raw, T) : raw, m);
-    const float e = exp_hw(z);
+    const float zq = fmaf(raw, rT, -m);
+    const float e = exp_hw(zq);
+    const float q = arg_margin(raw, rT, zq);
     eas[jj * 32 + lane] = e;
     ltot += e;
-    if (e > 0.0f) zmax = fmaxf(zmax, -z);
+    if (e > 0.0f) zmax = fmaxf(zmax, q);
     if (possible) {
       bool exact;
       if (e == 0.0f) {
@@ -1394,7 +1406,7 @@ __device__ __forceinline__ float classify_group(const SliceArgs& a, long long b,
         uint32_t kq;
         const float kr = rint_small(tt, kq);
         const float slack = 0.5f - fabsf(tt - kr);
-        exact = !(tt < 0x1p22f && slack > tt * fmaf(-z, DE_Z, DE_0) + 0x1p-24f);
+        exact = !(tt < 0x1p22f && slack > tt * fmaf(q, DE_Z, DE_0) + 0x1p-24f);
         if (!exact) ksum += kq;
       }
       if (exact) undecided |= 1u << jj;
@@ -1764,6 +1776,7 @@ __global__ void __launch_bounds__(K1_NT, 3) fused_classify_kernel(SliceArgs a) {
     const float T = prm.temperature;
     const bool scale = T > 0.0f;
     const float t_eff = scale ? T : 1.0f;
+    const float rT = scale ? 1.0f / T : 1.0f;  // the approximate argument x*rT - m of the clean units
     const float m = ri.m;
     const int sub = c0 / ups;
     const long long sub0 = (long long)sub * a.SL;
@@ -1922,8 +1935,8 @@ __global__ void __launch_bounds__(K1_NT, 3) fused_classify_kernel(SliceArgs a) {
 #pragma unroll 2
         for (int jj = 0; jj < nl; ++jj) {
           const float raw = graw[i0 + jj];
-          const float z = fsub(scale ? fdiv(raw, T) : raw, m);  // sampling.rs:46,127
-          const float ea = exp_hw(z);
+          const float zq = fmaf(raw, rT, -m);  // approximate x/T - m (rT = 1: exactly x - m)
+          const float ea = exp_hw(zq);
           ltot += ea;
           if (!possible) continue;
           bool exact;
@@ -1934,7 +1947,7 @@ __global__ void __launch_bounds__(K1_NT, 3) fused_classify_kernel(SliceArgs a) {
             uint32_t kq;
             const float kr = rint_small(tt, kq);
             const float slack = 0.5f - fabsf(tt - kr);
-            exact = !(tt < 0x1p22f && slack > tt * fmaf(-z, DE_Z, DE_0) + 0x1p-24f);
+            exact = !(tt < 0x1p22f && slack > tt * fmaf(arg_margin(raw, rT, zq), DE_Z, DE_0) + 0x1p-24f);
             if (!exact) ksum += kq;
           }
           if (exact) undecided |= 1u << jj;

@@ -75,7 +75,11 @@ L2_BYTES = 126 * 1024 * 1024
 # DRAM bytes (read + write) of one step, summed over its kernels, from ncu
 # captures of this loop with the caches left warm (--cache-control none):
 # the command and per-kernel figures are in profiles/traffic_step_<workload>.md.
-TRAFFIC_PER_STEP = {}
+TRAFFIC_PER_STEP = {
+    1: 246_770_000,  # profiles/traffic_step_single_1000x32000_f32.md
+    2: 40_580_000,   # profiles/traffic_step_batched_64x128256_f32.md
+    3: 98_740_000,   # profiles/traffic_step_nucleus_256x152064_bf16.md
+}
 
 
 def cluster_pass(V, params, bf16=False, mode=0):
@@ -675,7 +679,8 @@ def main():
                        + (f" (forced, --cluster {args.cluster})" if args.cluster else "")},
             "roofline": {"bound": "hbm", "kernel": f"whole step ({nk} launches)", "achieved": achieved,
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": TRAFFIC_PER_STEP.get(w) if world == 1 else None,
+                         "traffic": (TRAFFIC_PER_STEP.get(w) if world == 1 and not args.rows and not args.cluster
+                                     else None),
                          "bytes_per_launch": step_bytes,
                          "kernels": ({"row_cluster": kern(scan_ms), "row (rows the cluster pass left)": kern(row_ms)}
                                      if cluster_pass(V, params, bf16, args.cluster) else

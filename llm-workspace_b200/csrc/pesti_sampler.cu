@@ -654,8 +654,9 @@ int run_cluster(const Plan& p, const ClusterGeom& cgm, char* ws, int device, cud
   // absorbs, which grows along the row (about 1.2e-4 of it at 128k columns,
   // up to 6e-4 at 256k).  A run predicted in the wrong binade is replayed, so
   // the band trades replays against general segments: on rows of 128k columns
-  // 2^-13 gave the fewest of both (against 2^-11, 2^-12 and 2^-14)
-  ca.band = V > 131072 ? 0x1p-10f : 0x1p-13f;
+  // 2^-13 gave the fewest of both (against 2^-11, 2^-12 and 2^-14); on bf16
+  // rows of 152064 columns 2^-12 was 6 % faster than 2^-10 and 2^-11
+  ca.band = V > 196608 ? 0x1p-10f : (V > 131072 ? 0x1p-12f : 0x1p-13f);
   ca.nucleus = nucleus ? 1 : 0;
   // a short batch lets the row kernel's few blocks be scheduled while the
   // cluster pass runs (they wait for it on the device), hiding that launch

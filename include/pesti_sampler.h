@@ -46,8 +46,16 @@ extern "C" {
 
 /* Logit element types.  BF16 and F16 logits are widened to f32 exactly, so
  * results are those of the reference on the widened values (a caller of the
- * reference's &[f32] API would widen them the same way). */
-typedef enum { PESTI_F32 = 0, PESTI_BF16 = 1, PESTI_F16 = 2 } pesti_dtype;
+ * reference's &[f32] API would widen them the same way).
+ *
+ * FP8_E4M3 (OCP E4M3FN: no infinities, S.1111.111 is NaN) and FP8_E5M2 (IEEE
+ * layout with infinities and NaNs), the float8 crate's F8E4M3 and F8E5M2,
+ * are taken by pesti_sample_batch and pesti_argmax_batch only.  Every value
+ * of both formats is an f16 value: the call first widens the [B, V] logits
+ * exactly into f16 in the handle's workspace (2 bytes per logit, on the
+ * call's stream), then samples those.  The other entry points refuse them
+ * with PESTI_E_INVALID_ARG. */
+typedef enum { PESTI_F32 = 0, PESTI_BF16 = 1, PESTI_F16 = 2, PESTI_FP8_E4M3 = 3, PESTI_FP8_E5M2 = 4 } pesti_dtype;
 
 /* Per-row sampling parameters: SamplingConfig (sampling.rs:12-21) without the
  * seed, which sample() never reads. */
@@ -228,6 +236,30 @@ int pesti_sample_batch_sharded(pesti_sampler* s, pesti_comm* c, const void* d_lo
  */
 int pesti_pcg32_seed(uint64_t* d_state, int64_t B, uint64_t seed, uint64_t first_stream, void* stream);
 int pesti_pcg32_draw(uint64_t* d_state, int64_t B, float* d_u, void* stream);
+
+/*
+ * The loop control of generate() (transformer/model.rs:508-531: stop tokens,
+ * the max_tokens bound, pos >= max_seq_len) on the device, for B sequences
+ * decoded together.  Called after each step's sample, it keeps each
+ * sequence's tokens on the GPU and feeds the next step's input, so a decode
+ * loop reads nothing back per step.  For every row b with d_done[b] == 0,
+ * t = d_next[b] (the step's sampled token):
+ *  - t in d_stop[0..n_stop): the row finishes (d_done[b] = 1) and t is not
+ *    kept (the reference breaks before pushing it);
+ *  - otherwise d_generated[b*cap + d_count[b]] = t, d_count[b] += 1 and
+ *    d_last[b] = t (the next forward's input token); the row finishes when
+ *    d_count[b] reaches max_seq_len (d_done[b] = 3) or max_tokens (2).
+ * A row whose d_count[b] is already max_tokens finishes without taking t.
+ * Finished rows are left as they are, whatever d_next holds for them.
+ * d_active (optional; mapped host memory works) receives the number of rows
+ * still running, for a host that checks it now and then instead of
+ * synchronising every step.  The caller zeroes d_count and d_done before the
+ * first step; cap >= min(max_tokens, max_seq_len).  Stream-ordered (NULL: the
+ * legacy default stream); allocates nothing.
+ */
+int pesti_generate_advance(const uint32_t* d_next, int64_t B, const uint32_t* d_stop, int64_t n_stop,
+                           int64_t max_tokens, int64_t max_seq_len, uint32_t* d_generated, int64_t cap,
+                           int32_t* d_count, uint8_t* d_done, uint32_t* d_last, int32_t* d_active, void* stream);
 
 /* Message of the last failure on the calling thread ("" if none). */
 const char* pesti_last_error(void);

@@ -2,6 +2,8 @@
 // Launch geometry, workspace and error reporting live here; the arithmetic is
 // in pesti_kernels.cuh.
 #include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 #include <dlfcn.h>
 #include <nccl.h>
@@ -25,6 +27,7 @@
 #include "pesti_noalloc.h"
 #include "pesti_shard.cuh"
 #include "pesti_rng.cuh"
+#include "pesti_generate.cuh"
 
 namespace {
 
@@ -66,6 +69,9 @@ struct pesti_sampler {
   size_t h_params_cap = 0;
   cudaEvent_t params_ev = nullptr;
   bool params_ev_used = false;
+  // fp8 logits widened to f16 (grown on demand)
+  void* d_wide = nullptr;
+  size_t d_wide_cap = 0;
   // single-row host API buffers
   float* d_row = nullptr;
   size_t d_row_cap = 0;
@@ -1300,6 +1306,67 @@ int sample_sharded(pesti_sampler* s, pesti_comm* comm, int G, const void* d_logi
   return shard_gathered(s, comm, sp, c, d_logits, d_logits, rows);
 }
 
+// fp8 logits -> f16, exactly (every E4M3 and E5M2 value, NaN and the E5M2
+// infinities included, is an f16 value).  Row b's V bytes at src + b*ld go to
+// dst + b*V; each thread widens 8 consecutive bytes, with an 8-byte load and a
+// 16-byte store where both are aligned.
+template <bool E4M3>
+__global__ void __launch_bounds__(256) widen_fp8_kernel(const uint8_t* __restrict__ src, long long ld,
+                                                        __half* __restrict__ dst, long long V) {
+  constexpr __nv_fp8_interpretation_t kind = E4M3 ? __NV_E4M3 : __NV_E5M2;
+  const long long b = blockIdx.y;
+  const long long c0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c0 >= V) return;
+  const uint8_t* s = src + b * ld + c0;
+  __half* d = dst + b * V + c0;
+  if (c0 + 8 <= V && ((uintptr_t)s % 8 == 0) && ((uintptr_t)d % 16 == 0)) {
+    const uint2 w = *reinterpret_cast<const uint2*>(s);
+    uint4 o;
+    const uint32_t in[2] = {w.x, w.y};
+    uint32_t out[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const __nv_fp8x2_storage_t pair = (__nv_fp8x2_storage_t)((in[h >> 1] >> (16 * (h & 1))) & 0xffffu);
+      const __half2_raw r = __nv_cvt_fp8x2_to_halfraw2(pair, kind);
+      out[h] = (uint32_t)r.x | ((uint32_t)r.y << 16);
+    }
+    o.x = out[0]; o.y = out[1]; o.z = out[2]; o.w = out[3];
+    *reinterpret_cast<uint4*>(d) = o;
+    return;
+  }
+  for (int e = 0; e < 8 && c0 + e < V; ++e) {
+    const __half_raw r = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)s[e], kind);
+    d[e] = __half(r);
+  }
+}
+
+bool is_fp8(pesti_dtype dtype) { return dtype == PESTI_FP8_E4M3 || dtype == PESTI_FP8_E5M2; }
+
+// Widens fp8 logits into the handle's f16 buffer on stream st; the call then
+// samples (*out, PESTI_F16, ld = V).
+int widen_fp8(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long long B, long long V, long long ld,
+              cudaStream_t st, const void** out) {
+  const size_t need = (size_t)B * (size_t)V * 2;
+  if (need > s->d_wide_cap) {
+    if (s->d_wide) {
+      PESTI_CUDA_TRY(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+      cudaFree(s->d_wide);
+      s->d_wide = nullptr;
+      s->d_wide_cap = 0;
+    }
+    PESTI_CUDA_TRY(cudaMalloc(&s->d_wide, need), "cudaMalloc(fp8 widening buffer)");
+    s->d_wide_cap = need;
+  }
+  const dim3 grid((unsigned)((V + 256 * 8 - 1) / (256 * 8)), (unsigned)B);
+  if (dtype == PESTI_FP8_E4M3)
+    widen_fp8_kernel<true><<<grid, 256, 0, st>>>((const uint8_t*)d_logits, ld, (__half*)s->d_wide, V);
+  else
+    widen_fp8_kernel<false><<<grid, 256, 0, st>>>((const uint8_t*)d_logits, ld, (__half*)s->d_wide, V);
+  PESTI_CUDA_TRY(cudaGetLastError(), "widen_fp8_kernel launch");
+  *out = s->d_wide;
+  return PESTI_OK;
+}
+
 int check_shapes(const void* d_logits, pesti_dtype dtype, int64_t B, int64_t V, int64_t ld) {
   if (dtype != PESTI_F32 && dtype != PESTI_BF16 && dtype != PESTI_F16) return fail(PESTI_E_INVALID_ARG, "unsupported dtype");
   if (B < 0 || V < 0) return fail(PESTI_E_INVALID_ARG, "negative B or V");
@@ -1353,6 +1420,7 @@ void pesti_sampler_destroy(pesti_sampler* s) {
   if (s->d_params) cudaFree(s->d_params);
   if (s->h_params) cudaFreeHost(s->h_params);
   if (s->d_row) cudaFree(s->d_row);
+  if (s->d_wide) cudaFree(s->d_wide);
   if (s->d_u1) cudaFree(s->d_u1);
   if (s->d_tok1) cudaFree(s->d_tok1);
   if (s->params_ev) cudaEventDestroy(s->params_ev);
@@ -1368,7 +1436,8 @@ int pesti_sample_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype
                        int params_per_row, int params_on_device, const float* d_u,
                        uint32_t* d_out_tokens, float* d_kept_p, uint32_t* d_kept_idx,
                        int64_t kept_width, int64_t* d_kept_count, void* stream) {
-  int rc = check_common(s, d_logits, dtype, B, V, ld);
+  const bool fp8 = is_fp8(dtype);
+  int rc = check_common(s, d_logits, fp8 ? PESTI_F16 : dtype, B, V, ld);
   if (rc) return rc;
   if (!params) return fail(PESTI_E_INVALID_ARG, "null params");
   if (B > 0 && (!d_u || !d_out_tokens)) return fail(PESTI_E_INVALID_ARG, "null u or output tokens");
@@ -1376,6 +1445,14 @@ int pesti_sample_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype
   if (B == 0) return PESTI_OK;
   PESTI_CUDA_TRY(cudaSetDevice(s->device), "cudaSetDevice");
   cudaStream_t st = (cudaStream_t)stream;  // NULL: the legacy default stream
+  if (fp8 && V > 0) {  // widened exactly to f16 first
+    rc = widen_fp8(s, d_logits, dtype, B, V, ld, st, &d_logits);
+    if (rc) return rc;
+    dtype = PESTI_F16;
+    ld = V;
+  } else if (fp8) {
+    dtype = PESTI_F16;
+  }
   pesti_sampling_params uni{};
   const pesti_sampling_params* d_per_row = nullptr;
   bool sorted_bufs = true, survivors = true;
@@ -1389,12 +1466,21 @@ int pesti_sample_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype
 
 int pesti_argmax_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, int64_t B,
                        int64_t V, int64_t ld, uint32_t flags, uint32_t* d_out_tokens, void* stream) {
-  int rc = check_common(s, d_logits, dtype, B, V, ld);
+  const bool fp8 = is_fp8(dtype);
+  int rc = check_common(s, d_logits, fp8 ? PESTI_F16 : dtype, B, V, ld);
   if (rc) return rc;
   if (B > 0 && !d_out_tokens) return fail(PESTI_E_INVALID_ARG, "null output tokens");
   if (B == 0) return PESTI_OK;
   PESTI_CUDA_TRY(cudaSetDevice(s->device), "cudaSetDevice");
   cudaStream_t st = (cudaStream_t)stream;  // NULL: the legacy default stream
+  if (fp8 && V > 0) {  // widened exactly to f16 first
+    rc = widen_fp8(s, d_logits, dtype, B, V, ld, st, &d_logits);
+    if (rc) return rc;
+    dtype = PESTI_F16;
+    ld = V;
+  } else if (fp8) {
+    dtype = PESTI_F16;
+  }
   pesti_sampling_params uni{};
   uni.temperature = 0.0f;
   uni.flags = PESTI_FLAG_GREEDY_IF_ZERO_T | (flags & PESTI_FLAG_ARGMAX_FIRST);
@@ -1626,6 +1712,25 @@ int pesti_pcg32_draw(uint64_t* d_state, int64_t B, float* d_u, void* stream) {
   pesti::pcg32_draw_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(d_state, B, d_u);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? PESTI_OK : cuda_fail(e, "pcg32_draw_kernel launch");
+}
+
+int pesti_generate_advance(const uint32_t* d_next, int64_t B, const uint32_t* d_stop, int64_t n_stop,
+                           int64_t max_tokens, int64_t max_seq_len, uint32_t* d_generated, int64_t cap,
+                           int32_t* d_count, uint8_t* d_done, uint32_t* d_last, int32_t* d_active, void* stream) {
+  if (B < 0 || n_stop < 0) return fail(PESTI_E_INVALID_ARG, "B or n_stop < 0");
+  if (max_tokens < 0 || max_seq_len < 0) return fail(PESTI_E_INVALID_ARG, "max_tokens or max_seq_len < 0");
+  if (max_tokens > 0x7fffffffLL || max_seq_len > 0x7fffffffLL) return fail(PESTI_E_INVALID_ARG, "limits exceed 2^31-1");
+  if (cap < std::min(max_tokens, max_seq_len)) return fail(PESTI_E_INVALID_ARG, "cap is below min(max_tokens, max_seq_len)");
+  if (B == 0) return PESTI_OK;
+  if (!d_next || !d_generated || !d_count || !d_done || !d_last) return fail(PESTI_E_INVALID_ARG, "null argument");
+  if (n_stop > 0 && !d_stop) return fail(PESTI_E_INVALID_ARG, "null stop list");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(PESTI_E_NO_DEVICE, "no CUDA device available");
+  pesti::generate_advance_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(d_next, B, d_stop, n_stop, max_tokens,
+                                                                      max_seq_len, d_generated, cap, d_count,
+                                                                      d_done, d_last, d_active);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PESTI_OK : cuda_fail(e, "generate_advance_kernel launch");
 }
 
 int pesti_test_ex2_approx_max_relerr(double* out) {

@@ -41,6 +41,8 @@ PESTI_E_NO_DEVICE = -6
 PESTI_F32 = 0
 PESTI_BF16 = 1
 PESTI_F16 = 2
+PESTI_FP8_E4M3 = 3  # sample_batch and argmax_batch only (widened exactly to f16 first)
+PESTI_FP8_E5M2 = 4
 
 FLAG_GREEDY_IF_ZERO_T = 1
 FLAG_ARGMAX_FIRST = 2
@@ -124,6 +126,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.pesti_pcg32_seed.restype = c_int
     lib.pesti_pcg32_draw.argtypes = [vp, i64, vp, vp]
     lib.pesti_pcg32_draw.restype = c_int
+    lib.pesti_generate_advance.argtypes = [vp, i64, vp, i64, i64, i64, vp, i64, vp, vp, vp, vp, vp]
+    lib.pesti_generate_advance.restype = c_int
     lib.pesti_last_gathered_rows.argtypes = [vp]
     lib.pesti_last_gathered_rows.restype = i64
     lib.pesti_last_gathered_reasons.argtypes = [vp, vp]
@@ -220,6 +224,47 @@ class DeviceRng:
         st = stream if stream is not None else torch.cuda.current_stream(self.state.device).cuda_stream
         _check(self._lib.pesti_pcg32_draw(self.state.data_ptr(), self.B, out.data_ptr(), st))
         return out
+
+
+class DecodeState:
+    """The loop control of generate() (transformer/model.rs:508-531) for B
+    sequences on the device (pesti_generate_advance): after each step's
+    sample, advance(tokens) keeps the tokens on the GPU and finishes rows on
+    a stop token, after max_tokens tokens, or at max_seq_len.  `last` is the
+    next step's input token per row; `active()` reads the number of rows
+    still running (a host read: call it now and then, not every step)."""
+
+    def __init__(self, B: int, max_tokens: int, max_seq_len: int, stop_tokens=(), device=0):
+        import torch
+        self._lib = load_library()
+        self.B, self.max_tokens, self.max_seq_len = int(B), int(max_tokens), int(max_seq_len)
+        self.cap = max(1, min(self.max_tokens, self.max_seq_len))
+        dev = torch.device("cuda", device)
+        self.generated = torch.zeros(self.B, self.cap, dtype=torch.int32, device=dev)
+        self.count = torch.zeros(self.B, dtype=torch.int32, device=dev)
+        self.done = torch.zeros(self.B, dtype=torch.uint8, device=dev)
+        self.last = torch.zeros(self.B, dtype=torch.int32, device=dev)
+        self._active = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.stop = torch.tensor(list(stop_tokens) or [0], dtype=torch.int64).to(torch.int32).to(dev)
+        self.n_stop = len(stop_tokens)
+
+    def advance(self, tokens, stream=None):
+        """Takes the step's [B] sampled tokens (int32 u32 bits, on the device)."""
+        import torch
+        st = stream if stream is not None else torch.cuda.current_stream(tokens.device).cuda_stream
+        _check(self._lib.pesti_generate_advance(
+            tokens.data_ptr(), self.B, self.stop.data_ptr(), self.n_stop, self.max_tokens, self.max_seq_len,
+            self.generated.data_ptr(), self.cap, self.count.data_ptr(), self.done.data_ptr(), self.last.data_ptr(),
+            self._active.data_ptr(), st))
+
+    def active(self) -> int:
+        return int(self._active.item())
+
+    def sequences(self):
+        """The generated tokens of every row (lists of ints, u32)."""
+        g = self.generated.cpu().numpy().view("uint32")
+        c = self.count.cpu().numpy()
+        return [list(map(int, g[b, :c[b]])) for b in range(self.B)]
 
 
 class Sampler:
@@ -371,11 +416,14 @@ def _ptr(t):
 
 
 def _dtype_of(logits) -> int:
-    """pesti_dtype of a logits tensor (float32, bfloat16 or float16)."""
+    """pesti_dtype of a logits tensor (float32, bfloat16, float16, or the fp8
+    formats float8_e4m3fn and float8_e5m2)."""
     import torch
-    dtype = {torch.float32: PESTI_F32, torch.bfloat16: PESTI_BF16, torch.float16: PESTI_F16}.get(logits.dtype)
+    dtype = {torch.float32: PESTI_F32, torch.bfloat16: PESTI_BF16, torch.float16: PESTI_F16,
+             getattr(torch, "float8_e4m3fn", None): PESTI_FP8_E4M3,
+             getattr(torch, "float8_e5m2", None): PESTI_FP8_E5M2}.get(logits.dtype)
     if dtype is None:
-        raise ValueError("logits must be float32, bfloat16 or float16")
+        raise ValueError("logits must be float32, bfloat16, float16, float8_e4m3fn or float8_e5m2")
     return dtype
 
 

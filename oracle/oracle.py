@@ -273,3 +273,26 @@ def parity_report(logits: np.ndarray, params, u: np.ndarray, tokens, kept_p, kep
         "topk_rows": topk_rows,
         "topk_sets_exact": (topk_ok / topk_rows) if topk_rows else None,
     }
+
+
+def generate_control(steps, stop_tokens, max_tokens, max_seq_len):
+    """The loop control of generate() (transformer/model.rs:508-531) for one
+    sequence, given the token each step would sample (`steps`, in order):
+    the generated tokens and why the loop ended ("stop", "max_tokens",
+    "max_seq_len", or None while it would still run).  Test infrastructure:
+    restates the loop with the sampler replaced by the given tokens."""
+    generated = []
+    pos = 0
+    it = iter(steps)
+    for _ in range(max_tokens):  # for _ in 0..max_tokens
+        try:
+            next_token = next(it)
+        except StopIteration:
+            return generated, None
+        if next_token in stop_tokens:  # stop_tokens.contains(&next_token) -> break
+            return generated, "stop"
+        generated.append(next_token)  # generated.push; context.push
+        pos += 1
+        if pos >= max_seq_len:
+            return generated, "max_seq_len"
+    return generated, "max_tokens"

@@ -64,3 +64,13 @@ def test_invalid_arguments_are_rejected_without_a_device():
     buf = (ctypes.c_uint8 * pesti_sampler.COMM_ID_BYTES)()
     assert lib.pesti_comm_create_timed(2, 0, buf, 0, 0, ctypes.byref(h)) == pesti_sampler.PESTI_E_INVALID_ARG
     assert lib.pesti_comm_create_timed(2, 2, buf, 0, 1000, ctypes.byref(h)) == pesti_sampler.PESTI_E_INVALID_ARG
+    # the device loop control: bad limits and a too-small output are refused before any device work
+    assert lib.pesti_generate_advance(None, 4, None, 0, -1, 8, None, 8, None, None, None, None, None) \
+        == pesti_sampler.PESTI_E_INVALID_ARG
+    assert lib.pesti_generate_advance(None, 4, None, 0, 10, 8, None, 4, None, None, None, None, None) \
+        == pesti_sampler.PESTI_E_INVALID_ARG
+    assert lib.pesti_generate_advance(None, 4, None, 0, 10, 8, None, 8, None, None, None, None, None) \
+        == pesti_sampler.PESTI_E_INVALID_ARG
+    # fp8 logits are taken by the batch calls only; the others refuse them
+    assert lib.pesti_sample_batch_noalloc(None, pesti_sampler.PESTI_FP8_E4M3, 1, 1, 1, None, 0, 0, None, None,
+                                          None, None, 0, None, None) == pesti_sampler.PESTI_E_INVALID_ARG

@@ -313,3 +313,51 @@ def test_f16_emulated_shards_match_whole_rows(sampler):
     got = [t.cpu().numpy() for t in sampler.sample_batch_sharded_emulated(d, cfg, u, 4, kept_width=KW)]
     for g, w_ in zip(got, whole):
         assert np.array_equal(g.view(np.uint8), w_.view(np.uint8))
+
+
+def _fp8_case(fmt, B, V, seed):
+    """fp8 logits of one format ([B, V] uint8 bits) and their exact f32
+    values, with the format's specials planted: NaN (both formats), the
+    infinities (E5M2), signed zeros and subnormals."""
+    import torch
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((B, V)) * 3).astype(np.float32)
+    tdt = torch.float8_e4m3fn if fmt == "e4m3" else torch.float8_e5m2
+    bits = torch.from_numpy(x).to(tdt).view(torch.uint8).numpy().copy()
+    bits[0, 3] = 0x01            # the smallest subnormal
+    bits[0, 4] = 0x80            # -0
+    bits[1, 5] = 0x7f            # NaN (E4M3) / NaN (E5M2)
+    if fmt == "e5m2":
+        bits[2, 6] = 0x7c        # +inf
+        bits[3, 7] = 0xfc        # -inf
+    widened = torch.from_numpy(bits).view(tdt).to(torch.float32).numpy()
+    return bits, widened, tdt
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+@pytest.mark.parametrize("V,ld_extra", [(32000, 0), (5001, 3)])
+def test_fp8_logits(sampler, fmt, V, ld_extra):
+    """fp8 logits (E4M3FN and E5M2): the oracle's results on the same values
+    widened to f32, bit for bit, for sampled rows of every kind and for
+    argmax; rows with NaN or infinities included.  ld_extra takes the
+    unaligned (byte-wise) widening."""
+    import torch
+    import pesti_sampler as ps
+    B = 12
+    bits, x, tdt = _fp8_case(fmt, B, V, 7 if fmt == "e4m3" else 8)
+    kinds = [(0.8, 0.0, 40), (1.0, 0.9, 0), (0.7, 0.0, 0), (0.0, 0.0, 0), (1.2, 0.0, 256), (0.9, 0.95, 1000)]
+    params = [kinds[r % len(kinds)] for r in range(B)]
+    u = synth.make_u(1, B)
+    ld = V + ld_extra
+    host = np.zeros((B, ld), np.uint8)
+    host[:, :V] = bits
+    dev = torch.from_numpy(host).cuda().view(tdt)[:, :V]
+    cfgs = [ps.SamplingConfig(temperature=t, top_p=p, top_k=k) for (t, p, k) in params]
+    ud = torch.from_numpy(u).cuda()
+    tok, kp, ki, kc = sampler.sample_batch(dev, cfgs, ud, kept_width=KW)
+    got = (tok.cpu().numpy().view(np.uint32), kp.cpu().numpy(), ki.cpu().numpy().view(np.uint32), kc.cpu().numpy())
+    check_exact(x, params, u, got, f"fp8 {fmt}")
+    last = sampler.argmax_batch(dev).cpu().numpy()
+    first = sampler.argmax_batch(dev, first=True).cpu().numpy()
+    assert list(last) == [O.argmax(r) for r in x]
+    assert list(first) == [O.argmax_first(r) for r in x]

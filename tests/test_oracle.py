@@ -135,3 +135,13 @@ def test_platform_exp_rarely_differs():
     a = O.sample_batch(x, (0.8, 0.95, 40), u, O.EXP_PLATFORM)["tokens"]
     b = O.sample_batch(x, (0.8, 0.95, 40), u, O.EXP_CR)["tokens"]
     assert (a != b).sum() <= 1
+
+
+def test_generate_control_exits():
+    """The restated loop control of generate() (transformer/model.rs:508-531)
+    on its three exits and on a loop still running."""
+    assert O.generate_control([1, 2, 3, 4], stop_tokens=[3], max_tokens=10, max_seq_len=10) == ([1, 2], "stop")
+    assert O.generate_control([1, 2, 3, 4], stop_tokens=[], max_tokens=2, max_seq_len=10) == ([1, 2], "max_tokens")
+    assert O.generate_control([1, 2, 3, 4], stop_tokens=[], max_tokens=10, max_seq_len=3) == ([1, 2, 3], "max_seq_len")
+    assert O.generate_control([1, 2], stop_tokens=[], max_tokens=10, max_seq_len=10) == ([1, 2], None)
+    assert O.generate_control([5], stop_tokens=[5], max_tokens=0, max_seq_len=10) == ([], "max_tokens")

@@ -2857,6 +2857,35 @@ __global__ void __launch_bounds__(K2_NT) row_kernel(RowArgs a) {
     const fold::Result sr = fold::block_fold(E, n, 0u, fold::NO_QUERY, false, sh.u.f);
     const float S = bitsf(sr.s_bits);
 
+    // top-p rows whose largest probability already reaches top_p: the
+    // sorted cumulative sum stops after its first element (sampling.rs:66-78),
+    // total is that probability, normalised it is 1 and the draw takes it
+    // (sampling.rs:81-105).  The row's largest exp is exp(0) = 1, and the
+    // first element of the stable sort is the lowest index among the
+    // elements of that probability.  No sort needed.
+    if (k == 0 && prm.top_p > 0.0f) {
+      const float p0 = fdiv(1.0f, S);  // sampling.rs:130 on the row's maximum
+      if (p0 >= prm.top_p) {
+        if (tid == 0) sh.e_star = 0xffffffffu;
+        __syncthreads();
+        uint32_t best = 0xffffffffu;
+        for (long long j = tid; j < n; j += K2_NT)
+          if (fdiv(E[j], S) == p0) best = I[j] < best ? I[j] : best;
+        if (best != 0xffffffffu) atomicMin(&sh.e_star, best);
+        __syncthreads();
+        const uint32_t idx0 = sh.e_star;
+        if (tid == 0) {
+          a.out[b] = idx0;
+          if (a.kept_count) a.kept_count[b] = 1;
+        }
+        for (long long j = tid; j < a.kept_width; j += K2_NT) {
+          if (a.kept_p) a.kept_p[b * a.kept_width + j] = j == 0 ? p0 : 0.0f;
+          if (a.kept_idx) a.kept_idx[b * a.kept_width + j] = j == 0 ? idx0 : 0xffffffffu;
+        }
+        return;
+      }
+    }
+
     int need_dense = 0;
     if (k > 0) {
       const long long keff = k < V ? k : V;

@@ -72,13 +72,14 @@ def params_text(w: int) -> str:
 UNIT = "rows/s"
 L2_BYTES = 126 * 1024 * 1024
 
-# DRAM bytes (read + write) of one step, summed over its kernels, from ncu
-# captures of this loop with the caches left warm (--cache-control none):
-# the command and per-kernel figures are in profiles/traffic_step_<workload>.md.
+# DRAM bytes (read + write) of one step, summed over its kernels, from one
+# ncu capture per workload of this loop with the caches left warm: one-pass
+# metrics (dram__bytes_read.sum, dram__bytes_write.sum, gpu__time_duration.sum,
+# --cache-control none) over `bench.py --workload N --kernels-only --steps 3 --warmup 3`.
 TRAFFIC_PER_STEP = {
-    1: 246_770_000,  # profiles/traffic_step_single_1000x32000_f32.md
-    2: 40_580_000,   # profiles/traffic_step_batched_64x128256_f32.md
-    3: 98_740_000,   # profiles/traffic_step_nucleus_256x152064_bf16.md
+    1: 246_770_000,  # [1000 x 32000] f32: K0 142.4 MB, K1f 102.1 MB, K2 2.2 MB
+    2: 40_580_000,   # [64 x 128256] f32: K0 37.6 MB, K1a 2.0 MB, K1b 0.7 MB, K2 0.3 MB
+    3: 98_740_000,   # [256 x 152064] bf16: cluster pass 88.0 MB, nucleus rows 10.8 MB
 }
 
 

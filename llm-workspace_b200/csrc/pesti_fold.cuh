@@ -610,6 +610,19 @@ struct Smem {
 // in global memory, by one block.  Ping-pongs between (k0, v0) and (k1, v1);
 // returns 0 if the result is in (k0, v0), 1 if in (k1, v1).  Passes whose
 // digit is the same for every key are skipped.
+// The lanes of the warp holding the same 9-bit value d as this lane (d <
+// 512), as a mask: one ballot per bit, the lanes agreeing on every bit
+// (the warp-level multisplit of the radix sort; all 32 lanes call it).
+__device__ __forceinline__ uint32_t match_digit9(uint32_t d) {
+  uint32_t m = 0xffffffffu;
+#pragma unroll
+  for (int bit = 0; bit < 9; ++bit) {
+    const uint32_t bb = __ballot_sync(0xffffffffu, (d >> bit) & 1u);
+    m &= ((d >> bit) & 1u) ? bb : ~bb;
+  }
+  return m;
+}
+
 __device__ __noinline__ int block_radix_sort(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1,
                                              long long n, Smem& sm) {
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
@@ -638,7 +651,7 @@ __device__ __noinline__ int block_radix_sort(uint32_t* k0, uint32_t* v0, uint32_
       for (int r = 0; r < RB; ++r) {
         const long long j = j0 + r * 32 + lane;
         const uint32_t d = j < end ? ((kb[r] >> shift) & 255u) : 256u + (uint32_t)lane;
-        const uint32_t peers = __match_any_sync(PESTI_FULL_MASK, d);  // one add per digit per warp
+        const uint32_t peers = match_digit9(d);  // one add per digit per warp
         if (d < 256u && (peers & ((1u << lane) - 1u)) == 0u) sm.hist[w][d] += (uint32_t)__popc(peers);
         __syncwarp();
       }
@@ -689,7 +702,7 @@ __device__ __noinline__ int block_radix_sort(uint32_t* k0, uint32_t* v0, uint32_
         const uint32_t key = kb[r];
         const uint32_t val = vb[r];
         const uint32_t d = valid ? ((key >> shift) & 255u) : 256u + (uint32_t)lane;
-        const uint32_t peers = __match_any_sync(PESTI_FULL_MASK, d);
+        const uint32_t peers = match_digit9(d);
         const uint32_t lower = peers & ((1u << lane) - 1u);
         uint32_t dst = 0;
         if (valid) dst = sm.hist[w][d] + (uint32_t)__popc(lower);

@@ -650,10 +650,7 @@ __device__ __noinline__ int block_radix_sort(uint32_t* k0, uint32_t* v0, uint32_
 #pragma unroll
       for (int r = 0; r < RB; ++r) {
         const long long j = j0 + r * 32 + lane;
-        const uint32_t d = j < end ? ((kb[r] >> shift) & 255u) : 256u + (uint32_t)lane;
-        const uint32_t peers = match_digit9(d);  // one add per digit per warp
-        if (d < 256u && (peers & ((1u << lane) - 1u)) == 0u) sm.hist[w][d] += (uint32_t)__popc(peers);
-        __syncwarp();
+        if (j < end) atomicAdd(&sm.hist[w][(kb[r] >> shift) & 255u], 1u);  // the counts only: no order
       }
     }
     __syncthreads();

@@ -1312,31 +1312,32 @@ int sample_sharded(pesti_sampler* s, pesti_comm* comm, int G, const void* d_logi
 // 16-byte store where both are aligned.
 template <bool E4M3>
 __global__ void __launch_bounds__(256) widen_fp8_kernel(const uint8_t* __restrict__ src, long long ld,
-                                                        __half* __restrict__ dst, long long V) {
+                                                        __half* __restrict__ dst, long long B, long long V) {
   constexpr __nv_fp8_interpretation_t kind = E4M3 ? __NV_E4M3 : __NV_E5M2;
-  const long long b = blockIdx.y;
   const long long c0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (c0 >= V) return;
-  const uint8_t* s = src + b * ld + c0;
-  __half* d = dst + b * V + c0;
-  if (c0 + 8 <= V && ((uintptr_t)s % 8 == 0) && ((uintptr_t)d % 16 == 0)) {
-    const uint2 w = *reinterpret_cast<const uint2*>(s);
-    uint4 o;
-    const uint32_t in[2] = {w.x, w.y};
-    uint32_t out[4];
+  for (long long b = blockIdx.y; b < B; b += gridDim.y) {  // gridDim.y is at most 65535
+    const uint8_t* s = src + b * ld + c0;
+    __half* d = dst + b * V + c0;
+    if (c0 + 8 <= V && ((uintptr_t)s % 8 == 0) && ((uintptr_t)d % 16 == 0)) {
+      const uint2 w = *reinterpret_cast<const uint2*>(s);
+      uint4 o;
+      const uint32_t in[2] = {w.x, w.y};
+      uint32_t out[4];
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const __nv_fp8x2_storage_t pair = (__nv_fp8x2_storage_t)((in[h >> 1] >> (16 * (h & 1))) & 0xffffu);
-      const __half2_raw r = __nv_cvt_fp8x2_to_halfraw2(pair, kind);
-      out[h] = (uint32_t)r.x | ((uint32_t)r.y << 16);
+      for (int h = 0; h < 4; ++h) {
+        const __nv_fp8x2_storage_t pair = (__nv_fp8x2_storage_t)((in[h >> 1] >> (16 * (h & 1))) & 0xffffu);
+        const __half2_raw r = __nv_cvt_fp8x2_to_halfraw2(pair, kind);
+        out[h] = (uint32_t)r.x | ((uint32_t)r.y << 16);
+      }
+      o.x = out[0]; o.y = out[1]; o.z = out[2]; o.w = out[3];
+      *reinterpret_cast<uint4*>(d) = o;
+      continue;
     }
-    o.x = out[0]; o.y = out[1]; o.z = out[2]; o.w = out[3];
-    *reinterpret_cast<uint4*>(d) = o;
-    return;
-  }
-  for (int e = 0; e < 8 && c0 + e < V; ++e) {
-    const __half_raw r = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)s[e], kind);
-    d[e] = __half(r);
+    for (int e = 0; e < 8 && c0 + e < V; ++e) {
+      const __half_raw r = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)s[e], kind);
+      d[e] = __half(r);
+    }
   }
 }
 
@@ -1357,11 +1358,11 @@ int widen_fp8(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, long lo
     PESTI_CUDA_TRY(cudaMalloc(&s->d_wide, need), "cudaMalloc(fp8 widening buffer)");
     s->d_wide_cap = need;
   }
-  const dim3 grid((unsigned)((V + 256 * 8 - 1) / (256 * 8)), (unsigned)B);
+  const dim3 grid((unsigned)((V + 256 * 8 - 1) / (256 * 8)), (unsigned)(B < 65535 ? B : 65535));
   if (dtype == PESTI_FP8_E4M3)
-    widen_fp8_kernel<true><<<grid, 256, 0, st>>>((const uint8_t*)d_logits, ld, (__half*)s->d_wide, V);
+    widen_fp8_kernel<true><<<grid, 256, 0, st>>>((const uint8_t*)d_logits, ld, (__half*)s->d_wide, B, V);
   else
-    widen_fp8_kernel<false><<<grid, 256, 0, st>>>((const uint8_t*)d_logits, ld, (__half*)s->d_wide, V);
+    widen_fp8_kernel<false><<<grid, 256, 0, st>>>((const uint8_t*)d_logits, ld, (__half*)s->d_wide, B, V);
   PESTI_CUDA_TRY(cudaGetLastError(), "widen_fp8_kernel launch");
   *out = s->d_wide;
   return PESTI_OK;

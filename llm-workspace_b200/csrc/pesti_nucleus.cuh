@@ -111,22 +111,55 @@ __device__ void nuc_ordered(const uint16_t* row, long long V, bool vec, Pred pre
   constexpr int NW = K2_NT / 32;
   const long long chunk = ((V + NW - 1) / NW + 255) / 256 * 256;  // whole 256-element steps of the warp
   const long long c0 = (long long)wid * chunk, c1 = c0 + chunk < V ? c0 + chunk : V;
+  // the warp's count of each 256-element step, kept in the row kernel's
+  // shared scratch (free while this path runs), so that the scan for the
+  // wanted positions starts at the step that holds the first of them
+  uint32_t* scnt = &sh.u.s.hist[wid][0];
+  const int nstep = (int)((c1 - c0 + 255) / 256);
   int n = 0;
-  for (long long j = c0 + lane * 8; j < c1; j += 256) {
-    uint16_t h[8];
-    int nv;
-    nuc_load8(row, j, c1, vec, h, nv);
+  {
+    int st = 0;
+    for (long long j = c0 + lane * 8; st < nstep; j += 256, ++st) {
+      uint16_t h[8];
+      int nv = 0;
+      if (j < c1) nuc_load8(row, j, c1, vec, h, nv);
+      int c = 0;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) n += (e < nv && pred(bf16_bits_to_f32(h[e]))) ? 1 : 0;
+      for (int e = 0; e < 8; ++e) c += (e < nv && pred(bf16_bits_to_f32(h[e]))) ? 1 : 0;
+      c = (int)__reduce_add_sync(PESTI_FULL_MASK, (unsigned)c);
+      if (lane == 0 && st < 256) scnt[st] = (uint32_t)c;
+      n += c;
+    }
   }
-  n = warp_reduce_add(n);
   __syncthreads();
   if (lane == 0) sh.iscr[wid] = n;
   __syncthreads();
   long long k = 0;
   for (int q = 0; q < wid; ++q) k += sh.iscr[q];
   if (k + n > first && k < first + count) {
-    for (long long j0 = c0; j0 < c1 && k < first + count; j0 += 256) {
+    // skip the whole steps that end before position `first`
+    long long j0 = c0;
+    if (nstep <= 256) {  // (rows of at most 16 * 256 * 256 elements; longer ones scan from the start)
+      long long base = k;
+      for (int t0 = 0; t0 < nstep; t0 += 32) {
+        const int t = t0 + lane;
+        const int c = t < nstep ? (int)scnt[t] : 0;
+        const int inc = warp_incl_scan_add(c);
+        // the first step of this batch whose running count passes `first`
+        const uint32_t past = __ballot_sync(PESTI_FULL_MASK, t < nstep && base + inc > first);
+        if (past) {
+          const int f = __ffs(past) - 1;
+          const int before = __shfl_sync(PESTI_FULL_MASK, inc - c, f);
+          j0 = c0 + (long long)(t0 + f) * 256;
+          k = base + before;
+          break;
+        }
+        base += __shfl_sync(PESTI_FULL_MASK, inc, 31);
+        j0 = c0 + (long long)(t0 + 32) * 256;
+        k = base;
+      }
+    }
+    for (; j0 < c1 && k < first + count; j0 += 256) {
       const long long j = j0 + lane * 8;
       uint16_t h[8];
       int nv = 0;

@@ -261,6 +261,55 @@ int pesti_generate_advance(const uint32_t* d_next, int64_t B, const uint32_t* d_
                            int64_t max_tokens, int64_t max_seq_len, uint32_t* d_generated, int64_t cap,
                            int32_t* d_count, uint8_t* d_done, uint32_t* d_last, int32_t* d_active, void* stream);
 
+/*
+ * The sampler chain of PESTI's llama.cpp backend: `build_sampler`
+ * (llm-runner/src/llama.rs:465-508) over the fields of its SamplingConfig
+ * (llm-runner/src/llama/sampler.rs:19-79), for B rows with one parameter set.
+ * The stages run in build_sampler's order and under its gates:
+ *   temperature         temperature > 0
+ *   top-k               top_k > 0
+ *   top-p (min_keep 0)  top_p > 0 (1 or more keeps every candidate)
+ *   min-p (min_keep 256) min_p > 0: p >= min_p * p_max, at least 256 kept
+ *   top-n-sigma         0 < tfs < 1, n = tfs: logit >= max - n * sigma
+ *   typical (min_keep 0) 0 < typical_p < 1
+ *   penalties           repetition_penalty != 1, over the last repeat_last_n
+ *                       tokens of the row's history (all of it when
+ *                       repeat_last_n < 0, none when 0), with
+ *                       frequency_penalty and presence_penalty (0.0 in the
+ *                       reference)
+ * and end with an inverse-CDF draw on d_u[b] over the candidates sorted by
+ * logit (the chain as built has no selecting stage; the draw is the Rust
+ * sampler's, sampling.rs:97-111).  The stages restate the published filters
+ * of llama.cpp, whose sources are not in the reference tree; probabilities
+ * are computed in f64.  NaN logits count as -inf.
+ *
+ * d_history: [B, history_ld] int32 token ids (the row's recent tokens, oldest
+ * first), d_history_len (optional): [B] counts of valid leading entries
+ * (history_ld for every row when NULL); ids outside [0, V) are ignored.  The
+ * window (min(repeat_last_n, history_ld), or history_ld) is at most 8192.
+ * d_out_kept (optional): [B] candidates left before the draw.
+ * Logits: PESTI_F32, PESTI_BF16, PESTI_F16, and the fp8 types (widened to f16
+ * in the handle's workspace first).  Scratch: 16 bytes per logit in the
+ * handle's workspace.  Stream-ordered; one 1024-thread block per row.
+ */
+typedef struct {
+  float temperature;        /* llama/sampler.rs:33 */
+  int32_t top_k;            /* :36 */
+  float top_p;              /* :40 */
+  float min_p;              /* :44 */
+  float tfs;                /* :47, passed to top-n-sigma (llama.rs:488-491) */
+  float typical_p;          /* :50 */
+  float repetition_penalty; /* :62 */
+  int32_t repeat_last_n;    /* :65 */
+  float frequency_penalty;  /* 0.0 in build_sampler (llama.rs:502-503) */
+  float presence_penalty;   /* 0.0 in build_sampler */
+} pesti_llama_chain_params;
+
+int pesti_llama_chain_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, int64_t B, int64_t V,
+                            int64_t ld, const pesti_llama_chain_params* params, const int32_t* d_history,
+                            const int32_t* d_history_len, int64_t history_ld, const float* d_u,
+                            int32_t* d_out_tokens, int32_t* d_out_kept, void* stream);
+
 /* Message of the last failure on the calling thread ("" if none). */
 const char* pesti_last_error(void);
 

@@ -1,0 +1,604 @@
+// The llama.cpp sampler chain of PESTI's llama.cpp backend
+// (llm-runner/src/llama.rs:465-508, `build_sampler`) on the GPU, one thread
+// block of 1024 per row:
+//
+//   temperature (T > 0) -> top-k (k > 0) -> top-p (p > 0) -> min-p (> 0,
+//   at least 256 kept) -> top-n-sigma (n = tfs, 0 < tfs < 1) -> typical
+//   (0 < p < 1) -> repetition / frequency / presence penalties (penalty != 1)
+//   -> inverse-CDF draw with the caller's u.
+//
+// The stages are the published filters (llama.cpp, wrapped by the
+// llama-cpp-2 crate, is not part of the reference tree).  The row's candidate
+// list is kept in index order in a per-row scratch array (logit, index, f64
+// probability weight).  Every cut is a radix select over 8-bit digits of a
+// sort key (the ordered bits of the f32 logit, or of the f64 typical
+// deviation), by count (top-k, min-p's min_keep) or by probability mass
+// (top-p, typical, the draw), followed by an ordered compaction in place.
+// Masses are summed in f64 in a fixed order (per-warp histograms, warp
+// butterflies, warps in order), so a row gives the same result on every run.
+//
+// Conventions shared with the CPU restatement of the chain: NaN logits count
+// as -inf; the weight of a candidate is exp(l - max) in f64 (1 when l == max);
+// ties in a sort key keep index order; a mass cut keeps the shortest prefix
+// whose running mass reaches target * S, or the whole list when rounding
+// leaves the target unreached.
+#pragma once
+#include <math.h>
+#include <stdint.h>
+
+#include "pesti_common.cuh"
+
+namespace pesti {
+
+constexpr int CH_THREADS = 1024;
+constexpr int CH_WARPS = CH_THREADS / 32;
+constexpr int CH_WINDOW = 8192;  // repetition window tokens held in shared memory
+constexpr int CH_MIN_P_KEEP = 256;
+
+// Mirrors pesti_llama_chain_params (the fields of llm-runner/src/llama/sampler.rs
+// that build_sampler reads).
+struct ChainArgs {
+  float temperature;
+  int32_t top_k;
+  float top_p;
+  float min_p;
+  float tfs;
+  float typical_p;
+  float repetition_penalty;
+  int32_t repeat_last_n;
+  float frequency_penalty;
+  float presence_penalty;
+};
+
+// Dynamic shared memory of the chain kernel.
+struct ChainShared {
+  double whist[CH_WARPS][256];  // per-warp mass histograms
+  double mass[256];
+  uint32_t cnt[256];
+  double wd[CH_WARPS];
+  uint32_t wu[CH_WARPS];
+  uint32_t wu2[CH_WARPS];
+  float wf[CH_WARPS];
+  unsigned long long prefix;
+  long long rem_cnt;
+  double rem_mass;
+  int all;  // the target was not reached: take every element of the bucket
+  int pos;
+  int take_eq;
+  int window[CH_WINDOW];
+};
+
+__device__ __forceinline__ uint32_t ch_desc_key(float l) {
+  const uint32_t u = __float_as_uint(l);
+  const uint32_t asc = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ~asc;
+}
+
+// Candidate sources: the raw row (widened, NaN -> -inf, divided by T) or the
+// scratch list.
+struct ChRaw {
+  const void* row;
+  int dtype;
+  float T;
+  __device__ __forceinline__ float logit(int j) const {
+    float x = load_logit_dyn(row, dtype, j);
+    if (x != x) x = -INFINITY;
+    return T > 0.0f ? fdiv(x, T) : x;
+  }
+  __device__ __forceinline__ int index(int j) const { return j; }
+};
+struct ChList {
+  float* l;
+  int* i;
+  __device__ __forceinline__ float logit(int j) const { return l[j]; }
+  __device__ __forceinline__ int index(int j) const { return i[j]; }
+};
+
+// ---- block helpers (every thread calls them; each starts with a barrier) ----
+
+__device__ __forceinline__ double ch_sum_d(ChainShared& sh, double v) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  v = warp_reduce_add(v);
+  __syncthreads();
+  if (lane == 0) sh.wd[w] = v;
+  __syncthreads();
+  return warp_reduce_add(sh.wd[lane]);
+}
+
+__device__ __forceinline__ float ch_max_f(ChainShared& sh, float v) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  v = warp_reduce_fmax(v);
+  __syncthreads();
+  if (lane == 0) sh.wf[w] = v;
+  __syncthreads();
+  return warp_reduce_fmax(sh.wf[lane]);
+}
+
+__device__ __forceinline__ uint32_t ch_sum_u(ChainShared& sh, uint32_t v) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  v = warp_reduce_add(v);
+  __syncthreads();
+  if (lane == 0) sh.wu[w] = v;
+  __syncthreads();
+  return warp_reduce_add(sh.wu[lane]);
+}
+
+__device__ __forceinline__ int ch_max_i(ChainShared& sh, int v) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  v = warp_reduce_max(v);
+  __syncthreads();
+  if (lane == 0) sh.wu[w] = (uint32_t)v;
+  __syncthreads();
+  return warp_reduce_max((int)sh.wu[lane]);
+}
+
+// Exclusive block prefix of two 0/1 flags over one 1024-element tile, and
+// their tile totals.
+__device__ __forceinline__ void ch_scan2(ChainShared& sh, bool a, bool b, uint32_t& ea, uint32_t& eb, uint32_t& ta,
+                                         uint32_t& tb) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const uint32_t lt = (1u << lane) - 1u;
+  const uint32_t ba = __ballot_sync(PESTI_FULL_MASK, a), bb = __ballot_sync(PESTI_FULL_MASK, b);
+  __syncthreads();
+  if (lane == 0) {
+    sh.wu[w] = __popc(ba);
+    sh.wu2[w] = __popc(bb);
+  }
+  __syncthreads();
+  const uint32_t va = sh.wu[lane], vb = sh.wu2[lane];
+  const uint32_t ia = warp_incl_scan_add(va), ib = warp_incl_scan_add(vb);
+  ea = __shfl_sync(PESTI_FULL_MASK, ia - va, w) + __popc(ba & lt);
+  eb = __shfl_sync(PESTI_FULL_MASK, ib - vb, w) + __popc(bb & lt);
+  ta = __shfl_sync(PESTI_FULL_MASK, ia, 31);
+  tb = __shfl_sync(PESTI_FULL_MASK, ib, 31);
+}
+
+// Inclusive block prefix of an f64 over one tile (fixed order) and its total.
+__device__ __forceinline__ double ch_scan_d(ChainShared& sh, double v, double& total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const double iv = warp_incl_scan_add(v);
+  __syncthreads();
+  if (lane == 31) sh.wd[w] = iv;
+  __syncthreads();
+  const double t = sh.wd[lane];
+  const double it = warp_incl_scan_add(t);
+  total = __shfl_sync(PESTI_FULL_MASK, it, 31);
+  return __shfl_sync(PESTI_FULL_MASK, it - t, w) + iv;
+}
+
+// One warp's contribution to the digit histograms: counts by shared atomics,
+// masses into the warp's own histogram, one group of equal digits at a time
+// (a fixed order, so the f64 sums do not depend on timing).
+__device__ __forceinline__ void ch_hist_add(ChainShared& sh, bool act, uint32_t d, double w, bool by_mass) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  uint32_t rem = __ballot_sync(PESTI_FULL_MASK, act);
+  int rounds = 0;
+  while (rem) {
+    if (!by_mass && rounds == 4) {  // counts are exact in any order
+      if (rem & (1u << lane)) atomicAdd(&sh.cnt[d], 1u);
+      break;
+    }
+    const int L = __ffs(rem) - 1;
+    const uint32_t d0 = __shfl_sync(PESTI_FULL_MASK, d, L);
+    const bool in = act && d == d0;
+    const uint32_t g = __ballot_sync(PESTI_FULL_MASK, in);
+    if (by_mass) {
+      const double s = warp_reduce_add(in ? w : 0.0);
+      if (lane == L) sh.whist[wid][d0] += s;
+    }
+    if (lane == L) atomicAdd(&sh.cnt[d0], (uint32_t)__popc(g));
+    rem &= ~g;
+    ++rounds;
+  }
+}
+
+// Radix select over the n elements of a list.  By count: the want_cnt
+// smallest keys (ties in list order).  By mass: the shortest prefix in key
+// order whose running mass reaches want_mass.  Leaves in shared memory the
+// boundary key (sh.prefix), and how many elements equal to it are kept
+// (sh.rem_cnt by count; the walk below by mass).
+template <typename K, class KeyF, class WF>
+__device__ void ch_radix(ChainShared& sh, int n, KeyF key, WF wt, bool by_mass, long long want_cnt, double want_mass) {
+  constexpr int NB = (int)sizeof(K) * 8;
+  const int tid = threadIdx.x, lane = tid & 31;
+  __syncthreads();
+  if (tid == 0) {
+    sh.prefix = 0ull;
+    sh.rem_cnt = want_cnt;
+    sh.rem_mass = want_mass;
+    sh.all = 0;
+  }
+  for (int shift = NB - 8; shift >= 0; shift -= 8) {
+    __syncthreads();
+    for (int t = tid; t < 256; t += CH_THREADS) sh.cnt[t] = 0u;
+    if (by_mass)
+      for (int t = tid; t < CH_WARPS * 256; t += CH_THREADS) (&sh.whist[0][0])[t] = 0.0;
+    __syncthreads();
+    const K pre = (K)sh.prefix;
+    const int hs = shift + 8;
+    for (int j0 = 0; j0 < n; j0 += CH_THREADS) {
+      const int j = j0 + tid;
+      bool act = false;
+      uint32_t d = 0u;
+      double w = 0.0;
+      if (j < n) {
+        const K k = key(j);
+        act = hs >= NB || (k >> hs) == (pre >> hs);
+        d = (uint32_t)(k >> shift) & 255u;
+        if (act && by_mass) w = wt(j);
+      }
+      ch_hist_add(sh, act, d, w, by_mass);
+    }
+    __syncthreads();
+    if (by_mass && tid < 256) {
+      double m = 0.0;
+      for (int q = 0; q < CH_WARPS; ++q) m += sh.whist[q][tid];
+      sh.mass[tid] = m;
+    }
+    __syncthreads();
+    if (tid < 32) {
+      // lane: bins 8*lane .. 8*lane+7
+      uint32_t c8 = 0u;
+      double m8 = 0.0;
+      for (int q = 0; q < 8; ++q) {
+        c8 += sh.cnt[lane * 8 + q];
+        if (by_mass) m8 += sh.mass[lane * 8 + q];
+      }
+      const uint32_t ic = warp_incl_scan_add(c8);
+      const double im = warp_incl_scan_add(m8);
+      long long cc = (long long)(ic - c8);
+      double cm = im - m8;
+      const long long rc = sh.rem_cnt;
+      const double rm = sh.rem_mass;
+      const bool all = sh.all != 0;
+      int hit = -1, last = -1;
+      long long hc = 0;
+      double hm = 0.0;
+      for (int q = 0; q < 8; ++q) {
+        const int b = lane * 8 + q;
+        const uint32_t c = sh.cnt[b];
+        if (c == 0u) continue;
+        last = b;
+        const double m = by_mass ? sh.mass[b] : 0.0;
+        if (hit < 0 && !all && (by_mass ? cm + m >= rm : cc + (long long)c >= rc)) {
+          hit = b;
+          hc = cc;
+          hm = cm;
+        }
+        cc += c;
+        cm += m;
+      }
+      const uint32_t hb = __ballot_sync(PESTI_FULL_MASK, hit >= 0);
+      if (hb) {
+        const int L = __ffs(hb) - 1;
+        if (lane == L) {
+          sh.prefix |= (unsigned long long)hit << shift;
+          sh.rem_cnt = rc - hc;
+          sh.rem_mass = rm - hm;
+        }
+      } else {
+        // unreached (or already taking everything): the highest bucket, whole
+        const uint32_t lb = __ballot_sync(PESTI_FULL_MASK, last >= 0);
+        if (lb) {
+          const int L = 31 - __clz(lb);
+          if (lane == L) {
+            sh.prefix |= (unsigned long long)last << shift;
+            sh.rem_cnt = (long long)sh.cnt[last];
+            sh.rem_mass = INFINITY;
+            sh.all = 1;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// After ch_radix: the elements equal to the boundary key, in list order,
+// until the kept count (by count) or the running mass (by mass) is reached.
+// Sets sh.take_eq (kept elements equal to the boundary key) and sh.pos (the
+// list position of the last kept one); when the target stays unreached,
+// every equal element is kept and sh.pos is the last of them.
+template <typename K, class KeyF, class WF>
+__device__ void ch_walk(ChainShared& sh, int n, KeyF key, WF wt, bool by_mass) {
+  const int tid = threadIdx.x;
+  __syncthreads();
+  const K bk = (K)sh.prefix;
+  const long long rc = sh.rem_cnt;
+  const double rm = sh.rem_mass;
+  __syncthreads();
+  if (tid == 0) sh.pos = 0x7fffffff;
+  uint32_t base_c = 0u;
+  double base_m = 0.0;
+  int last_eq = -1;
+  for (int j0 = 0; j0 < n; j0 += CH_THREADS) {
+    const int j = j0 + tid;
+    const bool eq = j < n && key(j) == bk;
+    const double w = (eq && by_mass) ? wt(j) : 0.0;
+    uint32_t ec, e2, tc, t2;
+    ch_scan2(sh, eq, false, ec, e2, tc, t2);
+    double tm = 0.0;
+    const double im = by_mass ? ch_scan_d(sh, w, tm) : 0.0;
+    const bool hit = eq && (by_mass ? base_m + im >= rm : (long long)(base_c + ec + 1u) >= rc);
+    if (hit) atomicMin(&sh.pos, j);
+    if (eq) last_eq = j;
+    __syncthreads();
+    const int p = sh.pos;
+    if (hit && p == j) sh.take_eq = (int)(base_c + ec + 1u);
+    base_c += tc;
+    base_m += tm;
+    if (p != 0x7fffffff) break;
+  }
+  const int lastj = ch_max_i(sh, last_eq);
+  if (tid == 0 && sh.pos == 0x7fffffff) {
+    sh.pos = lastj;
+    sh.take_eq = (int)base_c;
+  }
+  __syncthreads();
+}
+
+// Ordered compaction of a source into the list: keeps key < boundary, and
+// the first take_eq elements equal to it.  Returns the new length.
+template <typename K, class Src, class KeyF>
+__device__ int ch_compact_select(ChainShared& sh, const Src& src, int n, KeyF key, K bk, long long take_eq,
+                                 float* ol, int* oi) {
+  const int tid = threadIdx.x;
+  uint32_t base_eq = 0u, base_out = 0u;
+  for (int j0 = 0; j0 < n; j0 += CH_THREADS) {
+    const int j = j0 + tid;
+    const bool have = j < n;
+    float l = 0.0f;
+    int ix = 0;
+    K k = 0;
+    if (have) {
+      l = src.logit(j);
+      ix = src.index(j);
+      k = key(j);
+    }
+    const bool eq = have && k == bk;
+    uint32_t eeq, e2, teq, t2;
+    ch_scan2(sh, eq, false, eeq, e2, teq, t2);
+    const bool keep = have && (k < bk || (eq && (long long)(base_eq + eeq) < take_eq));
+    uint32_t eo, e3, to, t3;
+    ch_scan2(sh, keep, false, eo, e3, to, t3);
+    if (keep) {
+      ol[base_out + eo] = l;
+      oi[base_out + eo] = ix;
+    }
+    base_eq += teq;
+    base_out += to;
+  }
+  __syncthreads();
+  return (int)base_out;
+}
+
+// Ordered compaction by a predicate on the logit.
+template <class Src, class Pred>
+__device__ int ch_compact_pred(ChainShared& sh, const Src& src, int n, Pred keepf, float* ol, int* oi) {
+  const int tid = threadIdx.x;
+  uint32_t base_out = 0u;
+  for (int j0 = 0; j0 < n; j0 += CH_THREADS) {
+    const int j = j0 + tid;
+    const bool have = j < n;
+    float l = 0.0f;
+    int ix = 0;
+    if (have) {
+      l = src.logit(j);
+      ix = src.index(j);
+    }
+    const bool keep = have && keepf(l);
+    uint32_t eo, e2, to, t2;
+    ch_scan2(sh, keep, false, eo, e2, to, t2);
+    if (keep) {
+      ol[base_out + eo] = l;
+      oi[base_out + eo] = ix;
+    }
+    base_out += to;
+  }
+  __syncthreads();
+  return (int)base_out;
+}
+
+// f64 weights exp(l - max) of the list into cw; returns their sum (fixed
+// order).  mx: the list's largest logit.
+__device__ __forceinline__ double ch_weights(ChainShared& sh, const float* l, double* cw, int n, float mx) {
+  double s = 0.0;
+  for (int j = threadIdx.x; j < n; j += CH_THREADS) {
+    const float x = l[j];
+    const double w = x == mx ? 1.0 : exp((double)x - (double)mx);
+    cw[j] = w;
+    s += w;
+  }
+  return ch_sum_d(sh, s);
+}
+
+__device__ __forceinline__ float ch_list_max(ChainShared& sh, const float* l, int n) {
+  float m = -INFINITY;
+  for (int j = threadIdx.x; j < n; j += CH_THREADS) m = fmaxf(m, l[j]);
+  return ch_max_f(sh, m);
+}
+
+__global__ void __launch_bounds__(CH_THREADS, 1)
+    llama_chain_kernel(const void* __restrict__ logits, int dtype, int V, long long ld, ChainArgs a,
+                       const int32_t* __restrict__ hist, const int32_t* __restrict__ hist_len, long long hist_ld,
+                       const float* __restrict__ u, int32_t* __restrict__ out_tok, int32_t* __restrict__ out_kept,
+                       float* __restrict__ sl, int* __restrict__ si, double* __restrict__ sw) {
+  extern __shared__ __align__(16) unsigned char ch_smem[];
+  ChainShared& sh = *reinterpret_cast<ChainShared*>(ch_smem);
+  const int tid = threadIdx.x;
+  const long long b = blockIdx.x;
+  const int esz = dtype == 0 ? 4 : 2;
+  const ChRaw raw{(const unsigned char*)logits + b * ld * esz, dtype, a.temperature};
+  float* l = sl + b * (long long)V;
+  int* ix = si + b * (long long)V;
+  double* cw = sw + b * (long long)V;
+  const ChList list{l, ix};
+  auto lkey = [&](int j) -> uint32_t { return ch_desc_key(list.logit(j)); };
+  auto wlist = [&](int j) -> double { return cw[j]; };
+  auto wnone = [&](int) -> double { return 0.0; };
+  int n = V;
+
+  // temperature + top-k, from the raw row into the list
+  if (a.top_k > 0 && a.top_k < n) {
+    auto rkey = [&](int j) -> uint32_t { return ch_desc_key(raw.logit(j)); };
+    ch_radix<uint32_t>(sh, n, rkey, wnone, false, a.top_k, 0.0);
+    const uint32_t bk = (uint32_t)sh.prefix;
+    const long long te = sh.rem_cnt;
+    n = ch_compact_select<uint32_t>(sh, raw, n, rkey, bk, te, l, ix);
+  } else {
+    n = ch_compact_pred(sh, raw, n, [](float) { return true; }, l, ix);
+  }
+
+  // top-p
+  if (a.top_p > 0.0f && a.top_p < 1.0f) {
+    const float mx = ch_list_max(sh, l, n);
+    const double S = ch_weights(sh, l, cw, n, mx);
+    ch_radix<uint32_t>(sh, n, lkey, wlist, true, 0, (double)a.top_p * S);
+    ch_walk<uint32_t>(sh, n, lkey, wlist, true);
+    const uint32_t bk = (uint32_t)sh.prefix;
+    const long long te = sh.take_eq;
+    n = ch_compact_select<uint32_t>(sh, list, n, lkey, bk, te, l, ix);
+  }
+
+  // min-p, at least 256 kept
+  if (a.min_p > 0.0f) {
+    const float mx = ch_list_max(sh, l, n);
+    const double thr = log((double)a.min_p);
+    uint32_t c = 0u;
+    for (int j = tid; j < n; j += CH_THREADS) {
+      const float x = l[j];
+      const double d = x == mx ? 0.0 : (double)x - (double)mx;
+      c += d >= thr ? 1u : 0u;
+    }
+    c = ch_sum_u(sh, c);
+    const int keep = max((int)c, min(CH_MIN_P_KEEP, n));
+    if (keep < n) {
+      ch_radix<uint32_t>(sh, n, lkey, wnone, false, keep, 0.0);
+      const uint32_t bk = (uint32_t)sh.prefix;
+      const long long te = sh.rem_cnt;
+      n = ch_compact_select<uint32_t>(sh, list, n, lkey, bk, te, l, ix);
+    }
+  }
+
+  // top-n-sigma (the config's tfs)
+  if (a.tfs > 0.0f && a.tfs < 1.0f) {
+    const float mx = ch_list_max(sh, l, n);
+    double s = 0.0;
+    uint32_t c = 0u;
+    for (int j = tid; j < n; j += CH_THREADS) {
+      const float x = l[j];
+      if (isfinite(x)) {
+        s += (double)x;
+        ++c;
+      }
+    }
+    s = ch_sum_d(sh, s);
+    c = ch_sum_u(sh, c);
+    if (c > 0u) {
+      const double mu = s / (double)c;
+      double q = 0.0;
+      for (int j = tid; j < n; j += CH_THREADS) {
+        const float x = l[j];
+        if (isfinite(x)) {
+          const double e = (double)x - mu;
+          q += e * e;
+        }
+      }
+      q = ch_sum_d(sh, q);
+      const double sigma = sqrt(q / (double)c);
+      const double thr = (double)mx - (double)a.tfs * sigma;
+      n = ch_compact_pred(sh, list, n, [thr](float x) { return (double)x >= thr; }, l, ix);
+    }
+  }
+
+  // typical
+  if (a.typical_p > 0.0f && a.typical_p < 1.0f) {
+    const float mx = ch_list_max(sh, l, n);
+    const double S = ch_weights(sh, l, cw, n, mx);
+    double e = 0.0;
+    for (int j = tid; j < n; j += CH_THREADS) {
+      const float x = l[j];
+      const double w = cw[j];
+      if (w > 0.0) e += w * (x == mx ? 0.0 : (double)x - (double)mx);
+    }
+    e = ch_sum_d(sh, e);
+    const double lnS = log(S);
+    const double H = lnS - e / S;
+    auto tkey = [&](int j) -> unsigned long long {
+      const float x = l[j];
+      const double d = x == mx ? 0.0 : (double)x - (double)mx;
+      return (unsigned long long)__double_as_longlong(fabs(lnS - d - H));
+    };
+    ch_radix<unsigned long long>(sh, n, tkey, wlist, true, 0, (double)a.typical_p * S);
+    ch_walk<unsigned long long>(sh, n, tkey, wlist, true);
+    const unsigned long long bk = sh.prefix;
+    const long long te = sh.take_eq;
+    n = ch_compact_select<unsigned long long>(sh, list, n, tkey, bk, te, l, ix);
+  }
+
+  // penalties over the last repeat_last_n tokens of the row's history
+  if (a.repetition_penalty != 1.0f && a.repeat_last_n != 0 && hist != nullptr) {
+    const long long hl = hist_len ? min(max((long long)hist_len[b], 0ll), hist_ld) : hist_ld;
+    const long long w = a.repeat_last_n < 0 ? hl : min(hl, (long long)a.repeat_last_n);
+    const int32_t* h = hist + b * hist_ld + (hl - w);
+    __syncthreads();
+    for (int t = tid; t < CH_WINDOW; t += CH_THREADS) {
+      const int32_t v = t < w ? h[t] : -1;
+      sh.window[t] = (v >= 0 && v < V) ? v : 0x7fffffff;
+    }
+    __syncthreads();
+    // bitonic sort of the window (ascending)
+    for (int k = 2; k <= CH_WINDOW; k <<= 1) {
+      for (int jj = k >> 1; jj > 0; jj >>= 1) {
+        for (int t = tid; t < CH_WINDOW; t += CH_THREADS) {
+          const int p = t ^ jj;
+          if (p > t) {
+            const int x = sh.window[t], y = sh.window[p];
+            const bool up = (t & k) == 0;
+            if ((x > y) == up) {
+              sh.window[t] = y;
+              sh.window[p] = x;
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    const float rp = a.repetition_penalty;
+    for (int t = tid; t < CH_WINDOW; t += CH_THREADS) {
+      const int tok = sh.window[t];
+      if (tok == 0x7fffffff || (t > 0 && sh.window[t - 1] == tok)) continue;
+      int e2 = t + 1;
+      while (e2 < CH_WINDOW && sh.window[e2] == tok) ++e2;
+      const int c = e2 - t;
+      // the candidate list is in index order
+      int lo = 0, hi = n;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (ix[mid] < tok) lo = mid + 1; else hi = mid;
+      }
+      if (lo < n && ix[lo] == tok) {
+        float v = l[lo];
+        v = v <= 0.0f ? __fmul_rn(v, rp) : fdiv(v, rp);
+        const float sub = fadd(__fmul_rn((float)c, a.frequency_penalty), c > 0 ? a.presence_penalty : 0.0f);
+        l[lo] = fsub(v, sub);
+      }
+    }
+    __syncthreads();
+  }
+
+  // the draw
+  {
+    const float mx = ch_list_max(sh, l, n);
+    const double S = ch_weights(sh, l, cw, n, mx);
+    ch_radix<uint32_t>(sh, n, lkey, wlist, true, 0, (double)u[b] * S);
+    ch_walk<uint32_t>(sh, n, lkey, wlist, true);
+    if (tid == 0) {
+      // every stage keeps at least one candidate; -1 would mark an empty list
+      out_tok[b] = (n > 0 && sh.pos >= 0 && sh.pos < n) ? ix[sh.pos] : -1;
+      if (out_kept) out_kept[b] = n;
+    }
+  }
+}
+
+}  // namespace pesti

@@ -28,6 +28,7 @@
 #include "pesti_shard.cuh"
 #include "pesti_rng.cuh"
 #include "pesti_generate.cuh"
+#include "pesti_chain.cuh"
 
 namespace {
 
@@ -72,6 +73,10 @@ struct pesti_sampler {
   // fp8 logits widened to f16 (grown on demand)
   void* d_wide = nullptr;
   size_t d_wide_cap = 0;
+  // llama.cpp chain scratch: per logit an f32 logit, an int32 index and an
+  // f64 weight (grown on demand)
+  void* d_chain = nullptr;
+  size_t d_chain_cap = 0;
   // single-row host API buffers
   float* d_row = nullptr;
   size_t d_row_cap = 0;
@@ -1422,6 +1427,7 @@ void pesti_sampler_destroy(pesti_sampler* s) {
   if (s->h_params) cudaFreeHost(s->h_params);
   if (s->d_row) cudaFree(s->d_row);
   if (s->d_wide) cudaFree(s->d_wide);
+  if (s->d_chain) cudaFree(s->d_chain);
   if (s->d_u1) cudaFree(s->d_u1);
   if (s->d_tok1) cudaFree(s->d_tok1);
   if (s->params_ev) cudaEventDestroy(s->params_ev);
@@ -1732,6 +1738,63 @@ int pesti_generate_advance(const uint32_t* d_next, int64_t B, const uint32_t* d_
                                                                       d_done, d_last, d_active);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? PESTI_OK : cuda_fail(e, "generate_advance_kernel launch");
+}
+
+int pesti_llama_chain_batch(pesti_sampler* s, const void* d_logits, pesti_dtype dtype, int64_t B, int64_t V,
+                            int64_t ld, const pesti_llama_chain_params* params, const int32_t* d_history,
+                            const int32_t* d_history_len, int64_t history_ld, const float* d_u,
+                            int32_t* d_out_tokens, int32_t* d_out_kept, void* stream) {
+  const bool fp8 = is_fp8(dtype);
+  int rc = check_common(s, d_logits, fp8 ? PESTI_F16 : dtype, B, V, ld);
+  if (rc) return rc;
+  if (!params) return fail(PESTI_E_INVALID_ARG, "null params");
+  if (B == 0) return PESTI_OK;
+  if (V < 1) return fail(PESTI_E_INVALID_ARG, "V must be at least 1");
+  if (!d_u || !d_out_tokens) return fail(PESTI_E_INVALID_ARG, "null u or output tokens");
+  if (history_ld < 0) return fail(PESTI_E_INVALID_ARG, "history_ld < 0");
+  const pesti_llama_chain_params& p = *params;
+  const bool penalties = p.repetition_penalty != 1.0f && p.repeat_last_n != 0 && history_ld > 0;
+  if (penalties) {
+    if (!d_history) return fail(PESTI_E_INVALID_ARG, "null history");
+    const int64_t win = p.repeat_last_n < 0 ? history_ld : std::min<int64_t>(p.repeat_last_n, history_ld);
+    if (win > pesti::CH_WINDOW) return fail(PESTI_E_INVALID_ARG, "repetition window above 8192 tokens");
+  }
+  PESTI_CUDA_TRY(cudaSetDevice(s->device), "cudaSetDevice");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (fp8) {
+    rc = widen_fp8(s, d_logits, dtype, B, V, ld, st, &d_logits);
+    if (rc) return rc;
+    dtype = PESTI_F16;
+    ld = V;
+  }
+  const size_t per = (size_t)B * (size_t)V;
+  const size_t need = per * (sizeof(float) + sizeof(int) + sizeof(double));
+  if (need > s->d_chain_cap) {
+    if (s->d_chain) {
+      PESTI_CUDA_TRY(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+      cudaFree(s->d_chain);
+      s->d_chain = nullptr;
+      s->d_chain_cap = 0;
+    }
+    PESTI_CUDA_TRY(cudaMalloc(&s->d_chain, need), "cudaMalloc(chain scratch)");
+    s->d_chain_cap = need;
+  }
+  double* sw = (double*)s->d_chain;
+  float* sl = (float*)(sw + per);
+  int* si = (int*)(sl + per);
+  pesti::ChainArgs a{p.temperature,        p.top_k,         p.top_p,
+                     p.min_p,              p.tfs,           p.typical_p,
+                     p.repetition_penalty, p.repeat_last_n, p.frequency_penalty,
+                     p.presence_penalty};
+  if (!penalties) a.repetition_penalty = 1.0f;
+  const size_t smem = sizeof(pesti::ChainShared);
+  PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::llama_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                 "cudaFuncSetAttribute(chain)");
+  pesti::llama_chain_kernel<<<(unsigned)B, pesti::CH_THREADS, smem, st>>>(
+      d_logits, (int)dtype, (int)V, ld, a, penalties ? d_history : nullptr, d_history_len, history_ld, d_u,
+      d_out_tokens, d_out_kept, sl, si, sw);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PESTI_OK : cuda_fail(e, "llama_chain_kernel launch");
 }
 
 int pesti_test_ex2_approx_max_relerr(double* out) {

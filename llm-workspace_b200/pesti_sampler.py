@@ -128,6 +128,9 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.pesti_pcg32_draw.restype = c_int
     lib.pesti_generate_advance.argtypes = [vp, i64, vp, i64, i64, i64, vp, i64, vp, vp, vp, vp, vp]
     lib.pesti_generate_advance.restype = c_int
+    lib.pesti_llama_chain_batch.argtypes = [vp, vp, c_int, i64, i64, i64, ctypes.POINTER(LlamaChainParams), vp, vp,
+                                            i64, vp, vp, vp, vp]
+    lib.pesti_llama_chain_batch.restype = c_int
     lib.pesti_last_gathered_rows.argtypes = [vp]
     lib.pesti_last_gathered_rows.restype = i64
     lib.pesti_last_gathered_reasons.argtypes = [vp, vp]
@@ -154,6 +157,24 @@ class SamplingConfig:
     def to_params(self, greedy_if_zero_t: bool = False, argmax_first: bool = False) -> _Params:
         flags = (FLAG_GREEDY_IF_ZERO_T if greedy_if_zero_t else 0) | (FLAG_ARGMAX_FIRST if argmax_first else 0)
         return _Params(float(self.temperature), float(self.top_p), int(self.top_k), flags)
+
+
+class LlamaChainParams(ctypes.Structure):
+    """pesti_llama_chain_params: the fields of the llama.cpp backend's
+    SamplingConfig (llm-runner/src/llama/sampler.rs:19-79) that build_sampler
+    (llm-runner/src/llama.rs:465-508) reads.  Defaults are that config's."""
+    _fields_ = [("temperature", ctypes.c_float), ("top_k", ctypes.c_int32), ("top_p", ctypes.c_float),
+                ("min_p", ctypes.c_float), ("tfs", ctypes.c_float), ("typical_p", ctypes.c_float),
+                ("repetition_penalty", ctypes.c_float), ("repeat_last_n", ctypes.c_int32),
+                ("frequency_penalty", ctypes.c_float), ("presence_penalty", ctypes.c_float)]
+
+    def __init__(self, temperature=0.7, top_k=40, top_p=0.95, min_p=0.0, tfs=1.0, typical_p=1.0,
+                 repetition_penalty=1.0, repeat_last_n=64, frequency_penalty=0.0, presence_penalty=0.0):
+        super().__init__(temperature, top_k, top_p, min_p, tfs, typical_p, repetition_penalty, repeat_last_n,
+                         frequency_penalty, presence_penalty)
+
+    def as_dict(self) -> dict:
+        return {f: getattr(self, f) for f, _ in self._fields_}
 
 
 class PreparedParams:
@@ -374,6 +395,30 @@ class Sampler:
         st = stream if stream is not None else torch.cuda.current_stream(logits.device).cuda_stream
         _check(self._lib.pesti_argmax_batch(self._h, logits.data_ptr(), dtype, B, V, logits.stride(0),
                                             FLAG_ARGMAX_FIRST if first else 0, out.data_ptr(), st))
+        return out
+
+    def llama_chain_batch(self, logits, params: LlamaChainParams, u, history=None, history_len=None,
+                          out=None, kept=None, stream=None):
+        """pesti_llama_chain_batch: the llama.cpp backend's sampler chain
+        (llama.rs:465-508) over each row of `logits` ([B, V] CUDA tensor, f32,
+        bf16, f16 or fp8).  history: [B, H] int32 CUDA tensor of recent tokens
+        (oldest first) for the penalties, history_len: optional [B] int32.
+        Returns the [B] int32 tokens, and `kept` ([B] int32, candidates left
+        before the draw) filled when given."""
+        import torch
+        B, V = logits.shape
+        dtype = _dtype_of(logits)
+        if out is None:
+            out = torch.empty(B, dtype=torch.int32, device=logits.device)
+        st = stream if stream is not None else torch.cuda.current_stream(logits.device).cuda_stream
+        hld = 0
+        if history is not None:
+            if history.dim() != 2 or history.shape[0] != B or not history.is_contiguous():
+                raise ValueError("history must be a contiguous [B, H] tensor")
+            hld = history.shape[1]
+        _check(self._lib.pesti_llama_chain_batch(
+            self._h, logits.data_ptr(), dtype, B, V, logits.stride(0), ctypes.byref(params),
+            _ptr(history), _ptr(history_len), hld, u.data_ptr(), out.data_ptr(), _ptr(kept), st))
         return out
 
     # -- single row from host memory (the reference's own signature) -------

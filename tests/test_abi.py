@@ -71,6 +71,9 @@ def test_invalid_arguments_are_rejected_without_a_device():
         == pesti_sampler.PESTI_E_INVALID_ARG
     assert lib.pesti_generate_advance(None, 4, None, 0, 10, 8, None, 8, None, None, None, None, None) \
         == pesti_sampler.PESTI_E_INVALID_ARG
+    # the llama.cpp chain: a null handle is refused before any device work
+    assert lib.pesti_llama_chain_batch(None, None, 0, 1, 1, 1, None, None, None, 0, None, None, None, None) \
+        == pesti_sampler.PESTI_E_INVALID_ARG
     # fp8 logits are taken by the batch calls only; the others refuse them
     assert lib.pesti_sample_batch_noalloc(None, pesti_sampler.PESTI_FP8_E4M3, 1, 1, 1, None, 0, 0, None, None,
                                           None, None, 0, None, None) == pesti_sampler.PESTI_E_INVALID_ARG

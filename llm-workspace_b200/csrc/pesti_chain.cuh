@@ -34,6 +34,7 @@ constexpr int CH_THREADS = 1024;
 constexpr int CH_WARPS = CH_THREADS / 32;
 constexpr int CH_WINDOW = 8192;  // repetition window tokens held in shared memory
 constexpr int CH_MIN_P_KEEP = 256;
+constexpr int CH_Q = 4;  // 1024-element sub-tiles per chunk, loaded together
 
 // Mirrors pesti_llama_chain_params (the fields of llm-runner/src/llama/sampler.rs
 // that build_sampler reads).
@@ -65,6 +66,10 @@ struct ChainShared {
   int all;  // the target was not reached: take every element of the bucket
   int pos;
   int take_eq;
+  uint32_t h12[4096];  // top-k prefilter: counts of the top 12 key bits
+  uint32_t cq[CH_Q][CH_WARPS];
+  uint32_t cq2[CH_Q][CH_WARPS];
+  double dq[CH_Q][CH_WARPS];
   int window[CH_WINDOW];
 };
 
@@ -132,40 +137,6 @@ __device__ __forceinline__ int ch_max_i(ChainShared& sh, int v) {
   return warp_reduce_max((int)sh.wu[lane]);
 }
 
-// Exclusive block prefix of two 0/1 flags over one 1024-element tile, and
-// their tile totals.
-__device__ __forceinline__ void ch_scan2(ChainShared& sh, bool a, bool b, uint32_t& ea, uint32_t& eb, uint32_t& ta,
-                                         uint32_t& tb) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const uint32_t lt = (1u << lane) - 1u;
-  const uint32_t ba = __ballot_sync(PESTI_FULL_MASK, a), bb = __ballot_sync(PESTI_FULL_MASK, b);
-  __syncthreads();
-  if (lane == 0) {
-    sh.wu[w] = __popc(ba);
-    sh.wu2[w] = __popc(bb);
-  }
-  __syncthreads();
-  const uint32_t va = sh.wu[lane], vb = sh.wu2[lane];
-  const uint32_t ia = warp_incl_scan_add(va), ib = warp_incl_scan_add(vb);
-  ea = __shfl_sync(PESTI_FULL_MASK, ia - va, w) + __popc(ba & lt);
-  eb = __shfl_sync(PESTI_FULL_MASK, ib - vb, w) + __popc(bb & lt);
-  ta = __shfl_sync(PESTI_FULL_MASK, ia, 31);
-  tb = __shfl_sync(PESTI_FULL_MASK, ib, 31);
-}
-
-// Inclusive block prefix of an f64 over one tile (fixed order) and its total.
-__device__ __forceinline__ double ch_scan_d(ChainShared& sh, double v, double& total) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const double iv = warp_incl_scan_add(v);
-  __syncthreads();
-  if (lane == 31) sh.wd[w] = iv;
-  __syncthreads();
-  const double t = sh.wd[lane];
-  const double it = warp_incl_scan_add(t);
-  total = __shfl_sync(PESTI_FULL_MASK, it, 31);
-  return __shfl_sync(PESTI_FULL_MASK, it - t, w) + iv;
-}
-
 // One warp's contribution to the digit histograms: counts by shared atomics,
 // masses into the warp's own histogram, one group of equal digits at a time
 // (a fixed order, so the f64 sums do not depend on timing).
@@ -192,13 +163,71 @@ __device__ __forceinline__ void ch_hist_add(ChainShared& sh, bool act, uint32_t 
   }
 }
 
-// Radix select over the n elements of a list.  By count: the want_cnt
-// smallest keys (ties in list order).  By mass: the shortest prefix in key
-// order whose running mass reaches want_mass.  Leaves in shared memory the
-// boundary key (sh.prefix), and how many elements equal to it are kept
-// (sh.rem_cnt by count; the walk below by mass).
-template <typename K, class KeyF, class WF>
-__device__ void ch_radix(ChainShared& sh, int n, KeyF key, WF wt, bool by_mass, long long want_cnt, double want_mass) {
+// Top-k prefilter over a source: counts the top 12 bits of every key, and
+// returns the largest 12-bit bucket b such that the buckets up to b hold at
+// least k elements (the k-th smallest key lies in bucket b).
+template <class Src, class KeyF>
+__device__ uint32_t ch_bucket12(ChainShared& sh, const Src& src, int n, KeyF key, long long k) {
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  __syncthreads();
+  for (int t = tid; t < 4096; t += CH_THREADS) sh.h12[t] = 0u;
+  __syncthreads();
+  for (int j0 = 0; j0 < n; j0 += CH_THREADS * CH_Q) {
+    uint32_t dq[CH_Q];
+#pragma unroll
+    for (int q = 0; q < CH_Q; ++q) {
+      const int j = j0 + q * CH_THREADS + tid;
+      dq[q] = j < n ? key(src.logit(j)) >> 20 : 0xffffffffu;
+    }
+#pragma unroll
+    for (int q = 0; q < CH_Q; ++q) {
+      const bool act = dq[q] != 0xffffffffu;
+      uint32_t rem = __ballot_sync(PESTI_FULL_MASK, act);
+      for (int r = 0; rem && r < 4; ++r) {
+        const int L = __ffs(rem) - 1;
+        const uint32_t d0 = __shfl_sync(PESTI_FULL_MASK, dq[q], L);
+        const uint32_t g = __ballot_sync(PESTI_FULL_MASK, act && dq[q] == d0);
+        if (lane == L) atomicAdd(&sh.h12[d0], (uint32_t)__popc(g));
+        rem &= ~g;
+      }
+      if (rem & (1u << lane)) atomicAdd(&sh.h12[dq[q]], 1u);
+    }
+  }
+  __syncthreads();
+  // thread t: bins 4t .. 4t+3; block prefix of their counts
+  uint32_t c[4], c4 = 0u;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    c[q] = sh.h12[tid * 4 + q];
+    c4 += c[q];
+  }
+  const uint32_t ic = warp_incl_scan_add(c4);
+  if (lane == 31) sh.wu[w] = ic;
+  __syncthreads();
+  const uint32_t vw = sh.wu[lane];
+  const uint32_t iw = warp_incl_scan_add(vw);
+  long long cum = (long long)__shfl_sync(PESTI_FULL_MASK, iw - vw, w) + (ic - c4);
+  if (tid == 0) sh.prefix = 4095ull;
+  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if (cum < k && cum + c[q] >= k) sh.prefix = (unsigned long long)(tid * 4 + q);
+    cum += c[q];
+  }
+  __syncthreads();
+  return (uint32_t)sh.prefix;
+}
+
+// Radix select over the n elements of a source; key(l) maps a logit to its
+// sort key.  By count: the want_cnt smallest keys (ties in list order).  By
+// mass: the shortest prefix in key order whose running mass reaches
+// want_mass.  Leaves in shared memory the boundary key (sh.prefix) and, by
+// count, how many elements equal to it are kept (sh.rem_cnt); by mass the
+// walk below finds that.  Each chunk loads CH_Q sub-tiles of 1024 elements
+// before it adds them up, so their loads are in flight together.
+template <typename K, class Src, class KeyF, class WF>
+__device__ void ch_radix(ChainShared& sh, const Src& src, int n, KeyF key, WF wt, bool by_mass, long long want_cnt,
+                         double want_mass) {
   constexpr int NB = (int)sizeof(K) * 8;
   const int tid = threadIdx.x, lane = tid & 31;
   __syncthreads();
@@ -216,18 +245,25 @@ __device__ void ch_radix(ChainShared& sh, int n, KeyF key, WF wt, bool by_mass, 
     __syncthreads();
     const K pre = (K)sh.prefix;
     const int hs = shift + 8;
-    for (int j0 = 0; j0 < n; j0 += CH_THREADS) {
-      const int j = j0 + tid;
-      bool act = false;
-      uint32_t d = 0u;
-      double w = 0.0;
-      if (j < n) {
-        const K k = key(j);
-        act = hs >= NB || (k >> hs) == (pre >> hs);
-        d = (uint32_t)(k >> shift) & 255u;
-        if (act && by_mass) w = wt(j);
+    for (int j0 = 0; j0 < n; j0 += CH_THREADS * CH_Q) {
+      K kq[CH_Q];
+      double wq[CH_Q];
+#pragma unroll
+      for (int q = 0; q < CH_Q; ++q) {
+        const int j = j0 + q * CH_THREADS + tid;
+        kq[q] = 0;
+        wq[q] = 0.0;
+        if (j < n) {
+          kq[q] = key(src.logit(j));
+          if (by_mass) wq[q] = wt(j);
+        }
       }
-      ch_hist_add(sh, act, d, w, by_mass);
+#pragma unroll
+      for (int q = 0; q < CH_Q; ++q) {
+        const int j = j0 + q * CH_THREADS + tid;
+        const bool act = j < n && (hs >= NB || (kq[q] >> hs) == (pre >> hs));
+        ch_hist_add(sh, act, (uint32_t)(kq[q] >> shift) & 255u, wq[q], by_mass);
+      }
     }
     __syncthreads();
     if (by_mass && tid < 256) {
@@ -298,35 +334,80 @@ __device__ void ch_radix(ChainShared& sh, int n, KeyF key, WF wt, bool by_mass, 
 // until the kept count (by count) or the running mass (by mass) is reached.
 // Sets sh.take_eq (kept elements equal to the boundary key) and sh.pos (the
 // list position of the last kept one); when the target stays unreached,
-// every equal element is kept and sh.pos is the last of them.
-template <typename K, class KeyF, class WF>
-__device__ void ch_walk(ChainShared& sh, int n, KeyF key, WF wt, bool by_mass) {
-  const int tid = threadIdx.x;
+// every equal element is kept and sh.pos is the last of them.  The running
+// mass is summed in list order: sub-tile, then warp, then lane.
+template <typename K, class Src, class KeyF, class WF>
+__device__ void ch_walk(ChainShared& sh, const Src& src, int n, KeyF key, WF wt, bool by_mass) {
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const uint32_t lt = (1u << lane) - 1u;
   __syncthreads();
   const K bk = (K)sh.prefix;
   const long long rc = sh.rem_cnt;
   const double rm = sh.rem_mass;
   __syncthreads();
   if (tid == 0) sh.pos = 0x7fffffff;
-  uint32_t base_c = 0u;
+  long long base_c = 0;
   double base_m = 0.0;
   int last_eq = -1;
-  for (int j0 = 0; j0 < n; j0 += CH_THREADS) {
-    const int j = j0 + tid;
-    const bool eq = j < n && key(j) == bk;
-    const double w = (eq && by_mass) ? wt(j) : 0.0;
-    uint32_t ec, e2, tc, t2;
-    ch_scan2(sh, eq, false, ec, e2, tc, t2);
-    double tm = 0.0;
-    const double im = by_mass ? ch_scan_d(sh, w, tm) : 0.0;
-    const bool hit = eq && (by_mass ? base_m + im >= rm : (long long)(base_c + ec + 1u) >= rc);
-    if (hit) atomicMin(&sh.pos, j);
-    if (eq) last_eq = j;
+  for (int j0 = 0; j0 < n; j0 += CH_THREADS * CH_Q) {
+    bool eq[CH_Q];
+    double wv[CH_Q];
+#pragma unroll
+    for (int q = 0; q < CH_Q; ++q) {
+      const int j = j0 + q * CH_THREADS + tid;
+      eq[q] = false;
+      wv[q] = 0.0;
+      if (j < n) {
+        eq[q] = key(src.logit(j)) == bk;
+        if (by_mass) wv[q] = wt(j);
+      }
+      if (!eq[q]) wv[q] = 0.0;
+    }
+    uint32_t be[CH_Q];
+    double iw[CH_Q];
+#pragma unroll
+    for (int q = 0; q < CH_Q; ++q) {
+      be[q] = __ballot_sync(PESTI_FULL_MASK, eq[q]);
+      iw[q] = by_mass ? warp_incl_scan_add(wv[q]) : 0.0;
+      if (lane == 31) {
+        sh.cq[q][w] = __popc(be[q]);
+        sh.dq[q][w] = iw[q];
+      }
+    }
+    __syncthreads();
+    long long run_c = base_c;
+    double run_m = base_m;
+    bool hit = false;
+    int hitj = 0;
+    long long hit_rank = 0;
+#pragma unroll
+    for (int q = 0; q < CH_Q; ++q) {
+      const uint32_t vc = sh.cq[q][lane];
+      const uint32_t ic = warp_incl_scan_add(vc);
+      const long long ex_c = run_c + __shfl_sync(PESTI_FULL_MASK, ic - vc, w) + __popc(be[q] & lt);
+      double ex_m = run_m, tot_m = 0.0;
+      if (by_mass) {
+        const double vm = sh.dq[q][lane];
+        const double im = warp_incl_scan_add(vm);
+        ex_m += __shfl_sync(PESTI_FULL_MASK, im - vm, w);
+        tot_m = __shfl_sync(PESTI_FULL_MASK, im, 31);
+      }
+      const bool h = eq[q] && (by_mass ? ex_m + iw[q] >= rm : ex_c + 1 >= rc);
+      if (h && !hit) {
+        hit = true;
+        hitj = j0 + q * CH_THREADS + tid;
+        hit_rank = ex_c + 1;
+      }
+      if (eq[q]) last_eq = j0 + q * CH_THREADS + tid;
+      run_c += __shfl_sync(PESTI_FULL_MASK, ic, 31);
+      run_m += tot_m;
+    }
+    if (hit) atomicMin(&sh.pos, hitj);
     __syncthreads();
     const int p = sh.pos;
-    if (hit && p == j) sh.take_eq = (int)(base_c + ec + 1u);
-    base_c += tc;
-    base_m += tm;
+    if (hit && p == hitj) sh.take_eq = (int)hit_rank;
+    base_c = run_c;
+    base_m = run_m;
     if (p != 0x7fffffff) break;
   }
   const int lastj = ch_max_i(sh, last_eq);
@@ -337,72 +418,87 @@ __device__ void ch_walk(ChainShared& sh, int n, KeyF key, WF wt, bool by_mass) {
   __syncthreads();
 }
 
-// Ordered compaction of a source into the list: keeps key < boundary, and
-// the first take_eq elements equal to it.  Returns the new length.
-template <typename K, class Src, class KeyF>
-__device__ int ch_compact_select(ChainShared& sh, const Src& src, int n, KeyF key, K bk, long long take_eq,
-                                 float* ol, int* oi) {
-  const int tid = threadIdx.x;
-  uint32_t base_eq = 0u, base_out = 0u;
-  for (int j0 = 0; j0 < n; j0 += CH_THREADS) {
-    const int j = j0 + tid;
-    const bool have = j < n;
-    float l = 0.0f;
-    int ix = 0;
-    K k = 0;
-    if (have) {
-      l = src.logit(j);
-      ix = src.index(j);
-      k = key(j);
-    }
-    const bool eq = have && k == bk;
-    uint32_t eeq, e2, teq, t2;
-    ch_scan2(sh, eq, false, eeq, e2, teq, t2);
-    const bool keep = have && (k < bk || (eq && (long long)(base_eq + eeq) < take_eq));
-    uint32_t eo, e3, to, t3;
-    ch_scan2(sh, keep, false, eo, e3, to, t3);
-    if (keep) {
-      ol[base_out + eo] = l;
-      oi[base_out + eo] = ix;
-    }
-    base_eq += teq;
-    base_out += to;
-  }
+// Ordered compaction of a source into the list (in place when the source is
+// the list).  SEL: keeps key < bk and the first take_eq elements equal to bk;
+// otherwise keeps the elements whose logit satisfies pred.  Returns the new
+// length.  Each chunk's elements are read before its first barrier and
+// written after it, to positions below the chunk's end.
+template <bool SEL, typename K, class Src, class KeyF, class Pred>
+__device__ int ch_compact(ChainShared& sh, const Src& src, int n, KeyF key, K bk, long long take_eq, Pred pred,
+                          float* ol, int* oi) {
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const uint32_t lt = (1u << lane) - 1u;
+  long long base_eq = 0;
+  int base_out = 0;
   __syncthreads();
-  return (int)base_out;
-}
-
-// Ordered compaction by a predicate on the logit.
-template <class Src, class Pred>
-__device__ int ch_compact_pred(ChainShared& sh, const Src& src, int n, Pred keepf, float* ol, int* oi) {
-  const int tid = threadIdx.x;
-  uint32_t base_out = 0u;
-  for (int j0 = 0; j0 < n; j0 += CH_THREADS) {
-    const int j = j0 + tid;
-    const bool have = j < n;
-    float l = 0.0f;
-    int ix = 0;
-    if (have) {
-      l = src.logit(j);
-      ix = src.index(j);
+  for (int j0 = 0; j0 < n; j0 += CH_THREADS * CH_Q) {
+    float lv[CH_Q];
+    int iv[CH_Q];
+    bool kp[CH_Q], eq[CH_Q];
+#pragma unroll
+    for (int q = 0; q < CH_Q; ++q) {
+      const int j = j0 + q * CH_THREADS + tid;
+      const bool have = j < n;
+      lv[q] = have ? src.logit(j) : 0.0f;
+      iv[q] = have ? src.index(j) : 0;
+      if (SEL) {
+        const K k = key(lv[q]);
+        kp[q] = have && k < bk;
+        eq[q] = have && k == bk;
+      } else {
+        kp[q] = have && pred(lv[q]);
+        eq[q] = false;
+      }
     }
-    const bool keep = have && keepf(l);
-    uint32_t eo, e2, to, t2;
-    ch_scan2(sh, keep, false, eo, e2, to, t2);
-    if (keep) {
-      ol[base_out + eo] = l;
-      oi[base_out + eo] = ix;
+    if (SEL) {
+      uint32_t be[CH_Q];
+#pragma unroll
+      for (int q = 0; q < CH_Q; ++q) {
+        be[q] = __ballot_sync(PESTI_FULL_MASK, eq[q]);
+        if (lane == 0) sh.cq[q][w] = __popc(be[q]);
+      }
+      __syncthreads();
+      long long run = base_eq;
+#pragma unroll
+      for (int q = 0; q < CH_Q; ++q) {
+        const uint32_t v = sh.cq[q][lane];
+        const uint32_t ic = warp_incl_scan_add(v);
+        const long long r = run + __shfl_sync(PESTI_FULL_MASK, ic - v, w) + __popc(be[q] & lt);
+        kp[q] = kp[q] || (eq[q] && r < take_eq);
+        run += __shfl_sync(PESTI_FULL_MASK, ic, 31);
+      }
+      base_eq = run;
     }
-    base_out += to;
+    uint32_t bo[CH_Q];
+#pragma unroll
+    for (int q = 0; q < CH_Q; ++q) {
+      bo[q] = __ballot_sync(PESTI_FULL_MASK, kp[q]);
+      if (lane == 0) sh.cq2[q][w] = __popc(bo[q]);
+    }
+    __syncthreads();
+    int run = base_out;
+#pragma unroll
+    for (int q = 0; q < CH_Q; ++q) {
+      const uint32_t v = sh.cq2[q][lane];
+      const uint32_t ic = warp_incl_scan_add(v);
+      const int pos = run + (int)__shfl_sync(PESTI_FULL_MASK, ic - v, w) + __popc(bo[q] & lt);
+      if (kp[q]) {
+        ol[pos] = lv[q];
+        oi[pos] = iv[q];
+      }
+      run += (int)__shfl_sync(PESTI_FULL_MASK, ic, 31);
+    }
+    base_out = run;
+    __syncthreads();
   }
-  __syncthreads();
-  return (int)base_out;
+  return base_out;
 }
 
 // f64 weights exp(l - max) of the list into cw; returns their sum (fixed
 // order).  mx: the list's largest logit.
 __device__ __forceinline__ double ch_weights(ChainShared& sh, const float* l, double* cw, int n, float mx) {
   double s = 0.0;
+#pragma unroll 4
   for (int j = threadIdx.x; j < n; j += CH_THREADS) {
     const float x = l[j];
     const double w = x == mx ? 1.0 : exp((double)x - (double)mx);
@@ -414,6 +510,7 @@ __device__ __forceinline__ double ch_weights(ChainShared& sh, const float* l, do
 
 __device__ __forceinline__ float ch_list_max(ChainShared& sh, const float* l, int n) {
   float m = -INFINITY;
+#pragma unroll 4
   for (int j = threadIdx.x; j < n; j += CH_THREADS) m = fmaxf(m, l[j]);
   return ch_max_f(sh, m);
 }
@@ -433,31 +530,39 @@ __global__ void __launch_bounds__(CH_THREADS, 1)
   int* ix = si + b * (long long)V;
   double* cw = sw + b * (long long)V;
   const ChList list{l, ix};
-  auto lkey = [&](int j) -> uint32_t { return ch_desc_key(list.logit(j)); };
+  auto dkey = [](float x) -> uint32_t { return ch_desc_key(x); };
   auto wlist = [&](int j) -> double { return cw[j]; };
-  auto wnone = [&](int) -> double { return 0.0; };
+  auto wnone = [](int) -> double { return 0.0; };
+  auto every = [](float) { return true; };
   int n = V;
 
   // temperature + top-k, from the raw row into the list
   if (a.top_k > 0 && a.top_k < n) {
-    auto rkey = [&](int j) -> uint32_t { return ch_desc_key(raw.logit(j)); };
-    ch_radix<uint32_t>(sh, n, rkey, wnone, false, a.top_k, 0.0);
-    const uint32_t bk = (uint32_t)sh.prefix;
-    const long long te = sh.rem_cnt;
-    n = ch_compact_select<uint32_t>(sh, raw, n, rkey, bk, te, l, ix);
+    // two passes over the row: the 12-bit bucket of the k-th largest logit,
+    // then every element up to that bucket into the list; the exact select
+    // runs on the list
+    const uint32_t b12 = ch_bucket12(sh, raw, n, dkey, a.top_k);
+    n = ch_compact<false, uint32_t>(sh, raw, n, dkey, 0u, 0, [b12](float x) { return (ch_desc_key(x) >> 20) <= b12; },
+                                    l, ix);
+    if (a.top_k < n) {
+      ch_radix<uint32_t>(sh, list, n, dkey, wnone, false, a.top_k, 0.0);
+      const uint32_t bk = (uint32_t)sh.prefix;
+      const long long te = sh.rem_cnt;
+      n = ch_compact<true, uint32_t>(sh, list, n, dkey, bk, te, every, l, ix);
+    }
   } else {
-    n = ch_compact_pred(sh, raw, n, [](float) { return true; }, l, ix);
+    n = ch_compact<false, uint32_t>(sh, raw, n, dkey, 0u, 0, every, l, ix);
   }
 
   // top-p
   if (a.top_p > 0.0f && a.top_p < 1.0f) {
     const float mx = ch_list_max(sh, l, n);
     const double S = ch_weights(sh, l, cw, n, mx);
-    ch_radix<uint32_t>(sh, n, lkey, wlist, true, 0, (double)a.top_p * S);
-    ch_walk<uint32_t>(sh, n, lkey, wlist, true);
+    ch_radix<uint32_t>(sh, list, n, dkey, wlist, true, 0, (double)a.top_p * S);
+    ch_walk<uint32_t>(sh, list, n, dkey, wlist, true);
     const uint32_t bk = (uint32_t)sh.prefix;
     const long long te = sh.take_eq;
-    n = ch_compact_select<uint32_t>(sh, list, n, lkey, bk, te, l, ix);
+    n = ch_compact<true, uint32_t>(sh, list, n, dkey, bk, te, every, l, ix);
   }
 
   // min-p, at least 256 kept
@@ -465,6 +570,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1)
     const float mx = ch_list_max(sh, l, n);
     const double thr = log((double)a.min_p);
     uint32_t c = 0u;
+#pragma unroll 4
     for (int j = tid; j < n; j += CH_THREADS) {
       const float x = l[j];
       const double d = x == mx ? 0.0 : (double)x - (double)mx;
@@ -473,10 +579,10 @@ __global__ void __launch_bounds__(CH_THREADS, 1)
     c = ch_sum_u(sh, c);
     const int keep = max((int)c, min(CH_MIN_P_KEEP, n));
     if (keep < n) {
-      ch_radix<uint32_t>(sh, n, lkey, wnone, false, keep, 0.0);
+      ch_radix<uint32_t>(sh, list, n, dkey, wnone, false, keep, 0.0);
       const uint32_t bk = (uint32_t)sh.prefix;
       const long long te = sh.rem_cnt;
-      n = ch_compact_select<uint32_t>(sh, list, n, lkey, bk, te, l, ix);
+      n = ch_compact<true, uint32_t>(sh, list, n, dkey, bk, te, every, l, ix);
     }
   }
 
@@ -507,7 +613,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1)
       q = ch_sum_d(sh, q);
       const double sigma = sqrt(q / (double)c);
       const double thr = (double)mx - (double)a.tfs * sigma;
-      n = ch_compact_pred(sh, list, n, [thr](float x) { return (double)x >= thr; }, l, ix);
+      n = ch_compact<false, uint32_t>(sh, list, n, dkey, 0u, 0, [thr](float x) { return (double)x >= thr; }, l, ix);
     }
   }
 
@@ -524,16 +630,15 @@ __global__ void __launch_bounds__(CH_THREADS, 1)
     e = ch_sum_d(sh, e);
     const double lnS = log(S);
     const double H = lnS - e / S;
-    auto tkey = [&](int j) -> unsigned long long {
-      const float x = l[j];
+    auto tkey = [&](float x) -> unsigned long long {
       const double d = x == mx ? 0.0 : (double)x - (double)mx;
       return (unsigned long long)__double_as_longlong(fabs(lnS - d - H));
     };
-    ch_radix<unsigned long long>(sh, n, tkey, wlist, true, 0, (double)a.typical_p * S);
-    ch_walk<unsigned long long>(sh, n, tkey, wlist, true);
+    ch_radix<unsigned long long>(sh, list, n, tkey, wlist, true, 0, (double)a.typical_p * S);
+    ch_walk<unsigned long long>(sh, list, n, tkey, wlist, true);
     const unsigned long long bk = sh.prefix;
     const long long te = sh.take_eq;
-    n = ch_compact_select<unsigned long long>(sh, list, n, tkey, bk, te, l, ix);
+    n = ch_compact<true, unsigned long long>(sh, list, n, tkey, bk, te, every, l, ix);
   }
 
   // penalties over the last repeat_last_n tokens of the row's history
@@ -591,8 +696,8 @@ __global__ void __launch_bounds__(CH_THREADS, 1)
   {
     const float mx = ch_list_max(sh, l, n);
     const double S = ch_weights(sh, l, cw, n, mx);
-    ch_radix<uint32_t>(sh, n, lkey, wlist, true, 0, (double)u[b] * S);
-    ch_walk<uint32_t>(sh, n, lkey, wlist, true);
+    ch_radix<uint32_t>(sh, list, n, dkey, wlist, true, 0, (double)u[b] * S);
+    ch_walk<uint32_t>(sh, list, n, dkey, wlist, true);
     if (tid == 0) {
       // every stage keeps at least one candidate; -1 would mark an empty list
       out_tok[b] = (n > 0 && sh.pos >= 0 && sh.pos < n) ? ix[sh.pos] : -1;

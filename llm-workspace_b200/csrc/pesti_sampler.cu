@@ -77,6 +77,7 @@ struct pesti_sampler {
   // f64 weight (grown on demand)
   void* d_chain = nullptr;
   size_t d_chain_cap = 0;
+  bool chain_smem_set = false;
   // single-row host API buffers
   float* d_row = nullptr;
   size_t d_row_cap = 0;
@@ -1788,8 +1789,12 @@ int pesti_llama_chain_batch(pesti_sampler* s, const void* d_logits, pesti_dtype 
                      p.presence_penalty};
   if (!penalties) a.repetition_penalty = 1.0f;
   const size_t smem = sizeof(pesti::ChainShared);
-  PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::llama_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                 "cudaFuncSetAttribute(chain)");
+  if (!s->chain_smem_set) {
+    PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::llama_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)smem),
+                   "cudaFuncSetAttribute(chain)");
+    s->chain_smem_set = true;
+  }
   pesti::llama_chain_kernel<<<(unsigned)B, pesti::CH_THREADS, smem, st>>>(
       d_logits, (int)dtype, (int)V, ld, a, penalties ? d_history : nullptr, d_history_len, history_ld, d_u,
       d_out_tokens, d_out_kept, sl, si, sw);

@@ -466,6 +466,78 @@ def run_vocab_sharded(args, rank, world, local, dev):
     return 0
 
 
+def run_chain(args, dev):
+    """The llama.cpp backend's sampler chain (llm-runner/src/llama.rs:465-508)
+    with one SamplingConfig preset over the workload's [B, V] logits and a
+    256-token history per row; every row checked against the chain's CPU
+    restatement before timing."""
+    import torch
+
+    import llama_chain as LC
+    import pesti_sampler as ps
+    import synth
+
+    w = args.workload
+    spec = synth.WORKLOADS[w]
+    B, V = (args.rows or spec["B"]), spec["V"]
+    bf16 = spec["dtype"] == "bf16"
+    x = synth.make_logits(w, rows=range(B))
+    u = synth.make_u(w, B)
+    rng = np.random.default_rng(20240)
+    hist = rng.integers(0, V, size=(B, 256)).astype(np.int32)
+    p = ps.LlamaChainParams() if args.chain == "default" else getattr(ps.LlamaChainParams, args.chain)()
+    if bf16:
+        host = torch.from_numpy(synth.f32_to_bf16_bits(x).view(np.int16)).view(torch.bfloat16)
+    else:
+        host = torch.from_numpy(x)
+    step_bytes = B * V * (2 if bf16 else 4)
+    nbuf = max(2, math.ceil(2 * L2_BYTES / step_bytes))
+    bufs = [host.to(dev) for _ in range(nbuf)]
+    ud = torch.from_numpy(u).to(dev)
+    hd = torch.from_numpy(hist).to(dev)
+    out = torch.empty(B, dtype=torch.int32, device=dev)
+    kept = torch.empty(B, dtype=torch.int32, device=dev)
+    s = ps.Sampler(dev.index or 0)
+    stream = torch.cuda.current_stream(dev)
+
+    parity = None
+    if not args.kernels_only:
+        s.llama_chain_batch(bufs[0], p, ud, history=hd, out=out, kept=kept)
+        torch.cuda.synchronize()
+        xw = bufs[0].float().cpu().numpy()
+        ot, ok, om = LC.chain_batch(xw, p.as_dict(), hist, u)
+        near = om < 1e-9
+        tok, kp = out.cpu().numpy(), kept.cpu().numpy()
+        agree = (ot == tok) & (ok == kp)
+        parity = {"rows": B, "rows_agree": int(agree.sum()), "rows_near_boundary": int(near.sum()),
+                  "rows_disagree_off_boundary": int((~agree & ~near).sum())}
+
+    for i in range(args.warmup):
+        s.llama_chain_batch(bufs[i % nbuf], p, ud, history=hd, out=out, kept=kept)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev.index or 0)
+    clocks.start()
+    time.sleep(0.3)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        s.llama_chain_batch(bufs[i % nbuf], p, ud, history=hd, out=out, kept=kept)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    line = {
+        "metric": f"rows/s, llama.cpp sampler chain ({args.chain} preset)", "value": round(B / (ms / 1e3), 1),
+        "unit": "rows/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "higher_is_better": True, "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic",
+        "config": {"workload": f"[{B} x {V}] {spec['dtype']}", "chain": p.as_dict(), "history": 256,
+                   "l2": f"{nbuf} rotating input buffers, {nbuf * step_bytes / 1e6:.0f} MB > L2"},
+        "gpu_launches": args.steps, "parity": parity, "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -478,6 +550,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernels-only", action="store_true",
                     help="only the warm-up and timed steps (for profiler captures); prints ms_per_step")
+    ap.add_argument("--chain", default="",
+                    choices=["", "default", "greedy", "creative", "balanced", "precise"],
+                    help="time the llama.cpp backend's sampler chain (pesti_llama_chain_batch) with that "
+                         "SamplingConfig preset on the workload's shape, on one GPU")
     ap.add_argument("--cluster", type=int, default=0,
                     help="path of the batch: 0 the library's routing, -1 the four-kernel pipeline, "
                          "1..16 the cluster pass with that many CTAs per row (profiles of either path)")
@@ -498,6 +574,10 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.chain:
+        if world > 1:
+            raise SystemExit("--chain runs on one GPU")
+        return run_chain(args, dev)
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)

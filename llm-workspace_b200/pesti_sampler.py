@@ -176,6 +176,24 @@ class LlamaChainParams(ctypes.Structure):
     def as_dict(self) -> dict:
         return {f: getattr(self, f) for f, _ in self._fields_}
 
+    # the presets of llm-runner/src/llama/sampler.rs:116-173
+    @classmethod
+    def greedy(cls) -> "LlamaChainParams":
+        return cls(temperature=0.0, top_k=1, top_p=0.0, min_p=0.0, tfs=1.0, typical_p=1.0, repetition_penalty=1.0)
+
+    @classmethod
+    def creative(cls) -> "LlamaChainParams":
+        return cls(temperature=1.0, top_k=50, top_p=0.99, min_p=0.05, tfs=0.5, typical_p=0.5)
+
+    @classmethod
+    def balanced(cls) -> "LlamaChainParams":
+        return cls(temperature=0.7, top_k=40, top_p=0.95, min_p=0.0, tfs=1.0, typical_p=1.0)
+
+    @classmethod
+    def precise(cls) -> "LlamaChainParams":
+        return cls(temperature=0.3, top_k=20, top_p=0.9, min_p=0.1, tfs=1.0, typical_p=1.0,
+                   repetition_penalty=1.1, repeat_last_n=128)
+
 
 class PreparedParams:
     """Per-row sampling parameters converted once into the C layout, for

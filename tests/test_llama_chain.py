@@ -121,6 +121,15 @@ def test_typical_keeps_mass_at_least_p():
     assert 1 <= kept < kept_all
 
 
+def test_library_presets_are_the_configs_presets():
+    import pesti_sampler as ps
+    for name in ("greedy", "creative", "balanced", "precise"):
+        got = getattr(ps.LlamaChainParams, name)().as_dict()
+        want = ps.LlamaChainParams(**PRESETS[name]).as_dict()
+        assert got == want, name
+    assert ps.LlamaChainParams().as_dict() == ps.LlamaChainParams(**PRESETS["default"]).as_dict()
+
+
 # ---- GPU parity ----
 
 def _gpu_chain(x, params, u, hist=None, dtype="f32"):

@@ -137,29 +137,28 @@ __device__ __forceinline__ int ch_max_i(ChainShared& sh, int v) {
   return warp_reduce_max((int)sh.wu[lane]);
 }
 
-// One warp's contribution to the digit histograms: counts by shared atomics,
-// masses into the warp's own histogram, one group of equal digits at a time
-// (a fixed order, so the f64 sums do not depend on timing).
+// One warp's contribution to the digit histograms.  By count: a shared
+// atomic per element.  By mass: one group of equal digits at a time, its
+// f64 sum by a warp butterfly into the warp's own histogram (a fixed order,
+// so the sums do not depend on timing).
 __device__ __forceinline__ void ch_hist_add(ChainShared& sh, bool act, uint32_t d, double w, bool by_mass) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (!by_mass) {  // counts are exact in any order: one atomic per element
+    if (act) atomicAdd(&sh.cnt[d], 1u);
+    return;
+  }
   uint32_t rem = __ballot_sync(PESTI_FULL_MASK, act);
-  int rounds = 0;
   while (rem) {
-    if (!by_mass && rounds == 4) {  // counts are exact in any order
-      if (rem & (1u << lane)) atomicAdd(&sh.cnt[d], 1u);
-      break;
-    }
     const int L = __ffs(rem) - 1;
     const uint32_t d0 = __shfl_sync(PESTI_FULL_MASK, d, L);
     const bool in = act && d == d0;
     const uint32_t g = __ballot_sync(PESTI_FULL_MASK, in);
-    if (by_mass) {
-      const double s = warp_reduce_add(in ? w : 0.0);
-      if (lane == L) sh.whist[wid][d0] += s;
+    const double s = warp_reduce_add(in ? w : 0.0);
+    if (lane == L) {
+      sh.whist[wid][d0] += s;
+      atomicAdd(&sh.cnt[d0], (uint32_t)__popc(g));
     }
-    if (lane == L) atomicAdd(&sh.cnt[d0], (uint32_t)__popc(g));
     rem &= ~g;
-    ++rounds;
   }
 }
 
@@ -180,18 +179,8 @@ __device__ uint32_t ch_bucket12(ChainShared& sh, const Src& src, int n, KeyF key
       dq[q] = j < n ? key(src.logit(j)) >> 20 : 0xffffffffu;
     }
 #pragma unroll
-    for (int q = 0; q < CH_Q; ++q) {
-      const bool act = dq[q] != 0xffffffffu;
-      uint32_t rem = __ballot_sync(PESTI_FULL_MASK, act);
-      for (int r = 0; rem && r < 4; ++r) {
-        const int L = __ffs(rem) - 1;
-        const uint32_t d0 = __shfl_sync(PESTI_FULL_MASK, dq[q], L);
-        const uint32_t g = __ballot_sync(PESTI_FULL_MASK, act && dq[q] == d0);
-        if (lane == L) atomicAdd(&sh.h12[d0], (uint32_t)__popc(g));
-        rem &= ~g;
-      }
-      if (rem & (1u << lane)) atomicAdd(&sh.h12[dq[q]], 1u);
-    }
+    for (int q = 0; q < CH_Q; ++q)
+      if (dq[q] != 0xffffffffu) atomicAdd(&sh.h12[dq[q]], 1u);
   }
   __syncthreads();
   // thread t: bins 4t .. 4t+3; block prefix of their counts

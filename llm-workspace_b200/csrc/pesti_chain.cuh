@@ -67,6 +67,8 @@ struct ChainShared {
   int pos;
   int take_eq;
   uint32_t h12[4096];  // top-k prefilter: counts of the top 12 key bits
+  uint8_t wkeep[128];  // one-warp path: kept flags by list position
+  int wn;              // one-warp path: the new list length
   uint32_t cq[CH_Q][CH_WARPS];
   uint32_t cq2[CH_Q][CH_WARPS];
   double dq[CH_Q][CH_WARPS];
@@ -483,6 +485,178 @@ __device__ int ch_compact(ChainShared& sh, const Src& src, int n, KeyF key, K bk
   return base_out;
 }
 
+// ---- one-warp path for short lists (at most 128 candidates) ----
+// A stage on a short list runs in warp 0 alone: a bitonic sort in registers
+// by (key, list position), an f64 prefix in sorted order, and an ordered
+// compaction, with no block-wide barrier inside.
+
+constexpr int CH_WE = 4;             // list elements per lane
+constexpr int CH_WN = 32 * CH_WE;    // 128
+
+template <typename K>
+__device__ __forceinline__ bool ch_pair_less(K ka, int ja, K kb, int jb) {
+  return ka < kb || (ka == kb && ja < jb);
+}
+
+// Orders two registers of one lane: ascending when up.
+template <typename K>
+__device__ __forceinline__ void ch_cex(K& ka, int& ja, K& kb, int& jb, bool up) {
+  const bool sw = up ? ch_pair_less(kb, jb, ka, ja) : ch_pair_less(ka, ja, kb, jb);
+  if (sw) {
+    const K tk = ka;
+    ka = kb;
+    kb = tk;
+    const int tj = ja;
+    ja = jb;
+    jb = tj;
+  }
+}
+
+// Warp 0 sorts the first n (<= 128) list elements by (key, position): lane
+// l ends with sorted positions h*32 + l in kk[h], jj[h] (padding: the
+// largest key, position 0x7fffffff).
+template <typename K, class KeyF>
+__device__ __forceinline__ void ch_warp_sort(const float* l, int n, KeyF key, K (&kk)[CH_WE], int (&jj)[CH_WE]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int h = 0; h < CH_WE; ++h) {
+    const int j = h * 32 + lane;
+    if (j < n) {
+      kk[h] = key(l[j]);
+      jj[h] = j;
+    } else {
+      kk[h] = ~(K)0;
+      jj[h] = 0x7fffffff;
+    }
+  }
+#pragma unroll
+  for (int k = 2; k <= CH_WN; k <<= 1) {
+#pragma unroll
+    for (int js = k >> 1; js > 0; js >>= 1) {
+      if (js == 64) {
+        ch_cex(kk[0], jj[0], kk[2], jj[2], (lane & k) == 0);
+        ch_cex(kk[1], jj[1], kk[3], jj[3], ((32 + lane) & k) == 0);
+      } else if (js == 32) {
+        ch_cex(kk[0], jj[0], kk[1], jj[1], (lane & k) == 0);
+        ch_cex(kk[2], jj[2], kk[3], jj[3], ((64 + lane) & k) == 0);
+      } else {
+        const bool lower = (lane & js) == 0;
+#pragma unroll
+        for (int h = 0; h < CH_WE; ++h) {
+          const K ok = __shfl_xor_sync(PESTI_FULL_MASK, kk[h], js);
+          const int oj = __shfl_xor_sync(PESTI_FULL_MASK, jj[h], js);
+          const bool up = ((h * 32 + lane) & k) == 0;
+          const bool oless = ch_pair_less(ok, oj, kk[h], jj[h]);
+          const bool same = ok == kk[h] && oj == jj[h];
+          // ascending pairs: the lower position keeps the smaller
+          const bool take = (lower == up) ? oless : (!oless && !same);
+          if (take) {
+            kk[h] = ok;
+            jj[h] = oj;
+          }
+        }
+      }
+    }
+  }
+}
+
+// Warp 0: max, weights into cw and their sum (lane order, then a butterfly).
+__device__ __forceinline__ double ch_warp_weights(const float* l, double* cw, int n, float& mx_out) {
+  const int lane = threadIdx.x & 31;
+  float mx = -INFINITY;
+#pragma unroll
+  for (int h = 0; h < CH_WE; ++h) {
+    const int j = h * 32 + lane;
+    if (j < n) mx = fmaxf(mx, l[j]);
+  }
+  mx = warp_reduce_fmax(mx);
+  double s = 0.0;
+#pragma unroll
+  for (int h = 0; h < CH_WE; ++h) {
+    const int j = h * 32 + lane;
+    if (j < n) {
+      const float x = l[j];
+      const double w = x == mx ? 1.0 : exp((double)x - (double)mx);
+      cw[j] = w;
+      s += w;
+    }
+  }
+  __syncwarp();
+  mx_out = mx;
+  return warp_reduce_add(s);
+}
+
+// Warp 0: the cut on a short list, by count (the want_cnt first in key
+// order) or by mass (the shortest prefix in key order whose running mass
+// reaches target, or all).  Marks the kept list positions in sh.wkeep and
+// returns the list position of the last kept element.
+template <typename K, class KeyF>
+__device__ __forceinline__ int ch_warp_select(ChainShared& sh, const float* l, const double* cw, int n, KeyF key,
+                                              bool by_mass, int want_cnt, double target) {
+  const int lane = threadIdx.x & 31;
+  K kk[CH_WE];
+  int jj[CH_WE];
+  ch_warp_sort<K>(l, n, key, kk, jj);
+  int pstar = -1;
+  if (by_mass) {
+    double run = 0.0;
+#pragma unroll
+    for (int h = 0; h < CH_WE; ++h) {
+      const bool v = jj[h] < n;
+      const double w = v ? cw[jj[h]] : 0.0;
+      const double c = run + warp_incl_scan_add(w);
+      const uint32_t hb = __ballot_sync(PESTI_FULL_MASK, v && c >= target);
+      if (pstar < 0 && hb) pstar = h * 32 + __ffs(hb) - 1;
+      run = __shfl_sync(PESTI_FULL_MASK, c, 31);
+    }
+    if (pstar < 0) pstar = n - 1;
+  } else {
+    pstar = min(want_cnt, n) - 1;
+  }
+#pragma unroll
+  for (int h = 0; h < CH_WE; ++h)
+    if (jj[h] < n) sh.wkeep[jj[h]] = (h * 32 + lane) <= pstar ? 1 : 0;
+  const int hq = pstar >> 5;
+  int mine = jj[0];
+#pragma unroll
+  for (int h = 1; h < CH_WE; ++h)
+    if (hq == h) mine = jj[h];
+  const int bj = __shfl_sync(PESTI_FULL_MASK, mine, pstar & 31);
+  __syncwarp();
+  return bj;
+}
+
+// Warp 0: ordered compaction of a short list in place by sh.wkeep.
+__device__ __forceinline__ int ch_warp_compact(ChainShared& sh, float* l, int* ix, int n) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t lt = (1u << lane) - 1u;
+  float lv[CH_WE];
+  int iv[CH_WE];
+  bool kp[CH_WE];
+  __syncwarp();
+#pragma unroll
+  for (int h = 0; h < CH_WE; ++h) {
+    const int j = h * 32 + lane;
+    kp[h] = j < n && sh.wkeep[j] != 0;
+    lv[h] = j < n ? l[j] : 0.0f;
+    iv[h] = j < n ? ix[j] : 0;
+  }
+  __syncwarp();
+  int run = 0;
+#pragma unroll
+  for (int h = 0; h < CH_WE; ++h) {
+    const uint32_t b = __ballot_sync(PESTI_FULL_MASK, kp[h]);
+    if (kp[h]) {
+      const int pos = run + __popc(b & lt);
+      l[pos] = lv[h];
+      ix[pos] = iv[h];
+    }
+    run += __popc(b);
+  }
+  __syncwarp();
+  return run;
+}
+
 // f64 weights exp(l - max) of the list into cw; returns their sum (fixed
 // order).  mx: the list's largest logit.
 __device__ __forceinline__ double ch_weights(ChainShared& sh, const float* l, double* cw, int n, float mx) {
@@ -533,7 +707,15 @@ __global__ void __launch_bounds__(CH_THREADS, 1)
     const uint32_t b12 = ch_bucket12(sh, raw, n, dkey, a.top_k);
     n = ch_compact<false, uint32_t>(sh, raw, n, dkey, 0u, 0, [b12](float x) { return (ch_desc_key(x) >> 20) <= b12; },
                                     l, ix);
-    if (a.top_k < n) {
+    if (a.top_k < n && n <= CH_WN) {
+      if (tid < 32) {
+        ch_warp_select<uint32_t>(sh, l, cw, n, dkey, false, a.top_k, 0.0);
+        const int m = ch_warp_compact(sh, l, ix, n);
+        if (tid == 0) sh.wn = m;
+      }
+      __syncthreads();
+      n = sh.wn;
+    } else if (a.top_k < n) {
       ch_radix<uint32_t>(sh, list, n, dkey, wnone, false, a.top_k, 0.0);
       const uint32_t bk = (uint32_t)sh.prefix;
       const long long te = sh.rem_cnt;
@@ -544,7 +726,17 @@ __global__ void __launch_bounds__(CH_THREADS, 1)
   }
 
   // top-p
-  if (a.top_p > 0.0f && a.top_p < 1.0f) {
+  if (a.top_p > 0.0f && a.top_p < 1.0f && n <= CH_WN) {
+    if (tid < 32) {
+      float mx;
+      const double S = ch_warp_weights(l, cw, n, mx);
+      ch_warp_select<uint32_t>(sh, l, cw, n, dkey, true, 0, (double)a.top_p * S);
+      const int m = ch_warp_compact(sh, l, ix, n);
+      if (tid == 0) sh.wn = m;
+    }
+    __syncthreads();
+    n = sh.wn;
+  } else if (a.top_p > 0.0f && a.top_p < 1.0f) {
     const float mx = ch_list_max(sh, l, n);
     const double S = ch_weights(sh, l, cw, n, mx);
     ch_radix<uint32_t>(sh, list, n, dkey, wlist, true, 0, (double)a.top_p * S);
@@ -607,7 +799,34 @@ __global__ void __launch_bounds__(CH_THREADS, 1)
   }
 
   // typical
-  if (a.typical_p > 0.0f && a.typical_p < 1.0f) {
+  if (a.typical_p > 0.0f && a.typical_p < 1.0f && n <= CH_WN) {
+    if (tid < 32) {
+      float mx;
+      const double S = ch_warp_weights(l, cw, n, mx);
+      double e = 0.0;
+#pragma unroll
+      for (int h = 0; h < CH_WE; ++h) {
+        const int j = h * 32 + tid;
+        if (j < n) {
+          const float x = l[j];
+          const double w = cw[j];
+          if (w > 0.0) e += w * (x == mx ? 0.0 : (double)x - (double)mx);
+        }
+      }
+      e = warp_reduce_add(e);
+      const double lnS = log(S);
+      const double H = lnS - e / S;
+      auto tkey = [&](float x) -> unsigned long long {
+        const double d = x == mx ? 0.0 : (double)x - (double)mx;
+        return (unsigned long long)__double_as_longlong(fabs(lnS - d - H));
+      };
+      ch_warp_select<unsigned long long>(sh, l, cw, n, tkey, true, 0, (double)a.typical_p * S);
+      const int m = ch_warp_compact(sh, l, ix, n);
+      if (tid == 0) sh.wn = m;
+    }
+    __syncthreads();
+    n = sh.wn;
+  } else if (a.typical_p > 0.0f && a.typical_p < 1.0f) {
     const float mx = ch_list_max(sh, l, n);
     const double S = ch_weights(sh, l, cw, n, mx);
     double e = 0.0;
@@ -682,7 +901,17 @@ __global__ void __launch_bounds__(CH_THREADS, 1)
   }
 
   // the draw
-  {
+  if (n <= CH_WN) {
+    if (tid < 32) {
+      float mx;
+      const double S = ch_warp_weights(l, cw, n, mx);
+      const int bj = ch_warp_select<uint32_t>(sh, l, cw, n, dkey, true, 0, (double)u[b] * S);
+      if (tid == 0) {
+        out_tok[b] = (n > 0 && bj >= 0 && bj < n) ? ix[bj] : -1;
+        if (out_kept) out_kept[b] = n;
+      }
+    }
+  } else {
     const float mx = ch_list_max(sh, l, n);
     const double S = ch_weights(sh, l, cw, n, mx);
     ch_radix<uint32_t>(sh, list, n, dkey, wlist, true, 0, (double)u[b] * S);

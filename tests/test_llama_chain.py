@@ -139,6 +139,8 @@ def _gpu_chain(x, params, u, hist=None, dtype="f32"):
     t = torch.from_numpy(x).cuda()
     if dtype == "bf16":
         t = t.to(torch.bfloat16)
+    elif dtype == "f16":
+        t = t.half()
     elif dtype == "e4m3":
         t = t.to(torch.float8_e4m3fn)
     ud = torch.from_numpy(u).cuda()
@@ -223,6 +225,43 @@ def test_chain_fp8_logits():
     u = _u(rng, 8)
     tok, kept, xw = _gpu_chain(x, PRESETS["creative"], u, dtype="e4m3")
     _check(xw, PRESETS["creative"], u, None, tok, kept)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("last_n", [0, 1, 37, 500, -1])
+def test_chain_penalty_windows_and_history_lengths(last_n):
+    """Per-row history lengths (d_history_len) and every window rule:
+    repeat_last_n 0 (no penalty), shorter and longer than the history, -1
+    (all of it)."""
+    import torch
+    import pesti_sampler as ps
+    rng = np.random.default_rng(100 + last_n)
+    B, V, H = 12, 20000, 300
+    x = _logits(rng, B, V)
+    u = _u(rng, B)
+    hist = _history(rng, x, H)
+    hl = rng.integers(0, H + 1, size=B).astype(np.int32)
+    hl[0], hl[1] = 0, H
+    params = dict(temperature=0.9, top_k=0, top_p=0.0, repetition_penalty=1.4, repeat_last_n=last_n,
+                  frequency_penalty=0.05, presence_penalty=0.3)
+    s = _sampler()
+    kept = torch.empty(B, dtype=torch.int32, device="cuda")
+    tok = s.llama_chain_batch(torch.from_numpy(x).cuda(), ps.LlamaChainParams(**params), torch.from_numpy(u).cuda(),
+                              history=torch.from_numpy(hist).cuda(), history_len=torch.from_numpy(hl).cuda(),
+                              kept=kept)
+    torch.cuda.synchronize()
+    rows_hist = [hist[b, :hl[b]] for b in range(B)]
+    _check(x, params, u, rows_hist, tok.cpu().numpy(), kept.cpu().numpy())
+
+
+@pytest.mark.gpu
+def test_chain_f16_logits():
+    rng = np.random.default_rng(13)
+    x = _logits(rng, 8, 32000, scale=2.0)
+    u = _u(rng, 8)
+    hist = _history(rng, x, 128)
+    tok, kept, xw = _gpu_chain(x, PRESETS["precise"], u, hist, dtype="f16")
+    _check(xw, PRESETS["precise"], u, hist, tok, kept)
 
 
 @pytest.mark.gpu

@@ -34,7 +34,8 @@ constexpr int CH_THREADS = 1024;
 constexpr int CH_WARPS = CH_THREADS / 32;
 constexpr int CH_WINDOW = 8192;  // repetition window tokens held in shared memory
 constexpr int CH_MIN_P_KEEP = 256;
-constexpr int CH_Q = 4;  // 1024-element sub-tiles per chunk, loaded together
+constexpr int CH_Q = 4;     // 1024-element sub-tiles per chunk, loaded together
+constexpr int CH_QRAW = 8;  // the same for the two passes over the raw row
 
 // Mirrors pesti_llama_chain_params (the fields of llm-runner/src/llama/sampler.rs
 // that build_sampler reads).
@@ -69,8 +70,8 @@ struct ChainShared {
   uint32_t h12[4096];  // top-k prefilter: counts of the top 12 key bits
   uint8_t wkeep[128];  // one-warp path: kept flags by list position
   int wn;              // one-warp path: the new list length
-  uint32_t cq[CH_Q][CH_WARPS];
-  uint32_t cq2[CH_Q][CH_WARPS];
+  uint32_t cq[CH_QRAW][CH_WARPS];
+  uint32_t cq2[CH_QRAW][CH_WARPS];
   double dq[CH_Q][CH_WARPS];
   int window[CH_WINDOW];
 };
@@ -83,12 +84,12 @@ __device__ __forceinline__ uint32_t ch_desc_key(float l) {
 
 // Candidate sources: the raw row (widened, NaN -> -inf, divided by T) or the
 // scratch list.
+template <typename TIn>
 struct ChRaw {
-  const void* row;
-  int dtype;
+  const TIn* row;
   float T;
   __device__ __forceinline__ float logit(int j) const {
-    float x = load_logit_dyn(row, dtype, j);
+    float x = load_logit<TIn>(row, j);
     if (x != x) x = -INFINITY;
     return T > 0.0f ? fdiv(x, T) : x;
   }
@@ -167,21 +168,21 @@ __device__ __forceinline__ void ch_hist_add(ChainShared& sh, bool act, uint32_t 
 // Top-k prefilter over a source: counts the top 12 bits of every key, and
 // returns the largest 12-bit bucket b such that the buckets up to b hold at
 // least k elements (the k-th smallest key lies in bucket b).
-template <class Src, class KeyF>
+template <int Q, class Src, class KeyF>
 __device__ uint32_t ch_bucket12(ChainShared& sh, const Src& src, int n, KeyF key, long long k) {
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   __syncthreads();
   for (int t = tid; t < 4096; t += CH_THREADS) sh.h12[t] = 0u;
   __syncthreads();
-  for (int j0 = 0; j0 < n; j0 += CH_THREADS * CH_Q) {
-    uint32_t dq[CH_Q];
+  for (int j0 = 0; j0 < n; j0 += CH_THREADS * Q) {
+    uint32_t dq[Q];
 #pragma unroll
-    for (int q = 0; q < CH_Q; ++q) {
+    for (int q = 0; q < Q; ++q) {
       const int j = j0 + q * CH_THREADS + tid;
       dq[q] = j < n ? key(src.logit(j)) >> 20 : 0xffffffffu;
     }
 #pragma unroll
-    for (int q = 0; q < CH_Q; ++q)
+    for (int q = 0; q < Q; ++q)
       if (dq[q] != 0xffffffffu) atomicAdd(&sh.h12[dq[q]], 1u);
   }
   __syncthreads();
@@ -414,7 +415,7 @@ __device__ void ch_walk(ChainShared& sh, const Src& src, int n, KeyF key, WF wt,
 // otherwise keeps the elements whose logit satisfies pred.  Returns the new
 // length.  Each chunk's elements are read before its first barrier and
 // written after it, to positions below the chunk's end.
-template <bool SEL, typename K, class Src, class KeyF, class Pred>
+template <bool SEL, typename K, int Q = CH_Q, class Src, class KeyF, class Pred>
 __device__ int ch_compact(ChainShared& sh, const Src& src, int n, KeyF key, K bk, long long take_eq, Pred pred,
                           float* ol, int* oi) {
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
@@ -422,12 +423,12 @@ __device__ int ch_compact(ChainShared& sh, const Src& src, int n, KeyF key, K bk
   long long base_eq = 0;
   int base_out = 0;
   __syncthreads();
-  for (int j0 = 0; j0 < n; j0 += CH_THREADS * CH_Q) {
-    float lv[CH_Q];
-    int iv[CH_Q];
-    bool kp[CH_Q], eq[CH_Q];
+  for (int j0 = 0; j0 < n; j0 += CH_THREADS * Q) {
+    float lv[Q];
+    int iv[Q];
+    bool kp[Q], eq[Q];
 #pragma unroll
-    for (int q = 0; q < CH_Q; ++q) {
+    for (int q = 0; q < Q; ++q) {
       const int j = j0 + q * CH_THREADS + tid;
       const bool have = j < n;
       lv[q] = have ? src.logit(j) : 0.0f;
@@ -442,16 +443,16 @@ __device__ int ch_compact(ChainShared& sh, const Src& src, int n, KeyF key, K bk
       }
     }
     if (SEL) {
-      uint32_t be[CH_Q];
+      uint32_t be[Q];
 #pragma unroll
-      for (int q = 0; q < CH_Q; ++q) {
+      for (int q = 0; q < Q; ++q) {
         be[q] = __ballot_sync(PESTI_FULL_MASK, eq[q]);
         if (lane == 0) sh.cq[q][w] = __popc(be[q]);
       }
       __syncthreads();
       long long run = base_eq;
 #pragma unroll
-      for (int q = 0; q < CH_Q; ++q) {
+      for (int q = 0; q < Q; ++q) {
         const uint32_t v = sh.cq[q][lane];
         const uint32_t ic = warp_incl_scan_add(v);
         const long long r = run + __shfl_sync(PESTI_FULL_MASK, ic - v, w) + __popc(be[q] & lt);
@@ -460,16 +461,16 @@ __device__ int ch_compact(ChainShared& sh, const Src& src, int n, KeyF key, K bk
       }
       base_eq = run;
     }
-    uint32_t bo[CH_Q];
+    uint32_t bo[Q];
 #pragma unroll
-    for (int q = 0; q < CH_Q; ++q) {
+    for (int q = 0; q < Q; ++q) {
       bo[q] = __ballot_sync(PESTI_FULL_MASK, kp[q]);
       if (lane == 0) sh.cq2[q][w] = __popc(bo[q]);
     }
     __syncthreads();
     int run = base_out;
 #pragma unroll
-    for (int q = 0; q < CH_Q; ++q) {
+    for (int q = 0; q < Q; ++q) {
       const uint32_t v = sh.cq2[q][lane];
       const uint32_t ic = warp_incl_scan_add(v);
       const int pos = run + (int)__shfl_sync(PESTI_FULL_MASK, ic - v, w) + __popc(bo[q] & lt);
@@ -678,8 +679,10 @@ __device__ __forceinline__ float ch_list_max(ChainShared& sh, const float* l, in
   return ch_max_f(sh, m);
 }
 
+// TIn: float (f32 logits), uint16_t (bf16 bits) or __half.
+template <typename TIn>
 __global__ void __launch_bounds__(CH_THREADS, 1)
-    llama_chain_kernel(const void* __restrict__ logits, int dtype, int V, long long ld, ChainArgs a,
+    llama_chain_kernel(const TIn* __restrict__ logits, int V, long long ld, ChainArgs a,
                        const int32_t* __restrict__ hist, const int32_t* __restrict__ hist_len, long long hist_ld,
                        const float* __restrict__ u, int32_t* __restrict__ out_tok, int32_t* __restrict__ out_kept,
                        float* __restrict__ sl, int* __restrict__ si, double* __restrict__ sw) {
@@ -687,8 +690,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1)
   ChainShared& sh = *reinterpret_cast<ChainShared*>(ch_smem);
   const int tid = threadIdx.x;
   const long long b = blockIdx.x;
-  const int esz = dtype == 0 ? 4 : 2;
-  const ChRaw raw{(const unsigned char*)logits + b * ld * esz, dtype, a.temperature};
+  const ChRaw<TIn> raw{logits + b * ld, a.temperature};
   float* l = sl + b * (long long)V;
   int* ix = si + b * (long long)V;
   double* cw = sw + b * (long long)V;
@@ -704,9 +706,9 @@ __global__ void __launch_bounds__(CH_THREADS, 1)
     // two passes over the row: the 12-bit bucket of the k-th largest logit,
     // then every element up to that bucket into the list; the exact select
     // runs on the list
-    const uint32_t b12 = ch_bucket12(sh, raw, n, dkey, a.top_k);
-    n = ch_compact<false, uint32_t>(sh, raw, n, dkey, 0u, 0, [b12](float x) { return (ch_desc_key(x) >> 20) <= b12; },
-                                    l, ix);
+    const uint32_t b12 = ch_bucket12<CH_QRAW>(sh, raw, n, dkey, a.top_k);
+    n = ch_compact<false, uint32_t, CH_QRAW>(sh, raw, n, dkey, 0u, 0,
+                                             [b12](float x) { return (ch_desc_key(x) >> 20) <= b12; }, l, ix);
     if (a.top_k < n && n <= CH_WN) {
       if (tid < 32) {
         ch_warp_select<uint32_t>(sh, l, cw, n, dkey, false, a.top_k, 0.0);
@@ -722,7 +724,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1)
       n = ch_compact<true, uint32_t>(sh, list, n, dkey, bk, te, every, l, ix);
     }
   } else {
-    n = ch_compact<false, uint32_t>(sh, raw, n, dkey, 0u, 0, every, l, ix);
+    n = ch_compact<false, uint32_t, CH_QRAW>(sh, raw, n, dkey, 0u, 0, every, l, ix);
   }
 
   // top-p
@@ -854,16 +856,19 @@ __global__ void __launch_bounds__(CH_THREADS, 1)
     const long long hl = hist_len ? min(max((long long)hist_len[b], 0ll), hist_ld) : hist_ld;
     const long long w = a.repeat_last_n < 0 ? hl : min(hl, (long long)a.repeat_last_n);
     const int32_t* h = hist + b * hist_ld + (hl - w);
+    // the window padded to a power of two (at least 2, at most CH_WINDOW)
+    int wp = 2;
+    while (wp < w) wp <<= 1;
     __syncthreads();
-    for (int t = tid; t < CH_WINDOW; t += CH_THREADS) {
+    for (int t = tid; t < wp; t += CH_THREADS) {
       const int32_t v = t < w ? h[t] : -1;
       sh.window[t] = (v >= 0 && v < V) ? v : 0x7fffffff;
     }
     __syncthreads();
     // bitonic sort of the window (ascending)
-    for (int k = 2; k <= CH_WINDOW; k <<= 1) {
+    for (int k = 2; k <= wp; k <<= 1) {
       for (int jj = k >> 1; jj > 0; jj >>= 1) {
-        for (int t = tid; t < CH_WINDOW; t += CH_THREADS) {
+        for (int t = tid; t < wp; t += CH_THREADS) {
           const int p = t ^ jj;
           if (p > t) {
             const int x = sh.window[t], y = sh.window[p];
@@ -878,11 +883,11 @@ __global__ void __launch_bounds__(CH_THREADS, 1)
       }
     }
     const float rp = a.repetition_penalty;
-    for (int t = tid; t < CH_WINDOW; t += CH_THREADS) {
+    for (int t = tid; t < wp; t += CH_THREADS) {
       const int tok = sh.window[t];
       if (tok == 0x7fffffff || (t > 0 && sh.window[t - 1] == tok)) continue;
       int e2 = t + 1;
-      while (e2 < CH_WINDOW && sh.window[e2] == tok) ++e2;
+      while (e2 < wp && sh.window[e2] == tok) ++e2;
       const int c = e2 - t;
       // the candidate list is in index order
       int lo = 0, hi = n;

@@ -1790,14 +1790,31 @@ int pesti_llama_chain_batch(pesti_sampler* s, const void* d_logits, pesti_dtype 
   if (!penalties) a.repetition_penalty = 1.0f;
   const size_t smem = sizeof(pesti::ChainShared);
   if (!s->chain_smem_set) {
-    PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::llama_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::llama_chain_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)smem),
+                   "cudaFuncSetAttribute(chain)");
+    PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::llama_chain_kernel<uint16_t>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                   "cudaFuncSetAttribute(chain)");
+    PESTI_CUDA_TRY(cudaFuncSetAttribute(pesti::llama_chain_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)smem),
                    "cudaFuncSetAttribute(chain)");
     s->chain_smem_set = true;
   }
-  pesti::llama_chain_kernel<<<(unsigned)B, pesti::CH_THREADS, smem, st>>>(
-      d_logits, (int)dtype, (int)V, ld, a, penalties ? d_history : nullptr, d_history_len, history_ld, d_u,
-      d_out_tokens, d_out_kept, sl, si, sw);
+  const int32_t* hp = penalties ? d_history : nullptr;
+  const dim3 grid((unsigned)B), block(pesti::CH_THREADS);
+  if (dtype == PESTI_BF16)
+    pesti::llama_chain_kernel<uint16_t><<<grid, block, smem, st>>>((const uint16_t*)d_logits, (int)V, ld, a, hp,
+                                                                   d_history_len, history_ld, d_u, d_out_tokens,
+                                                                   d_out_kept, sl, si, sw);
+  else if (dtype == PESTI_F16)
+    pesti::llama_chain_kernel<__half><<<grid, block, smem, st>>>((const __half*)d_logits, (int)V, ld, a, hp,
+                                                                 d_history_len, history_ld, d_u, d_out_tokens,
+                                                                 d_out_kept, sl, si, sw);
+  else
+    pesti::llama_chain_kernel<float><<<grid, block, smem, st>>>((const float*)d_logits, (int)V, ld, a, hp,
+                                                                d_history_len, history_ld, d_u, d_out_tokens,
+                                                                d_out_kept, sl, si, sw);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? PESTI_OK : cuda_fail(e, "llama_chain_kernel launch");
 }

@@ -1768,6 +1768,8 @@ int pesti_llama_chain_batch(pesti_sampler* s, const void* d_logits, pesti_dtype 
     dtype = PESTI_F16;
     ld = V;
   }
+  // scratch of 16 bytes per logit; refuse sizes whose byte count overflows
+  if ((size_t)B > (SIZE_MAX / 16) / (size_t)V) return fail(PESTI_E_INVALID_ARG, "B * V too large");
   const size_t per = (size_t)B * (size_t)V;
   const size_t need = per * (sizeof(float) + sizeof(int) + sizeof(double));
   if (need > s->d_chain_cap) {

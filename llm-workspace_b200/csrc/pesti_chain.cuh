@@ -240,22 +240,18 @@ __device__ void ch_radix(ChainShared& sh, const Src& src, int n, KeyF key, WF wt
     for (int j0 = 0; j0 < n; j0 += CH_THREADS * CH_Q) {
       K kq[CH_Q];
       double wq[CH_Q];
+      bool aq[CH_Q];
 #pragma unroll
       for (int q = 0; q < CH_Q; ++q) {
         const int j = j0 + q * CH_THREADS + tid;
-        kq[q] = 0;
-        wq[q] = 0.0;
-        if (j < n) {
-          kq[q] = key(src.logit(j));
-          if (by_mass) wq[q] = wt(j);
-        }
+        kq[q] = j < n ? key(src.logit(j)) : (K)0;
+        aq[q] = j < n && (hs >= NB || (kq[q] >> hs) == (pre >> hs));
       }
+      // weights only of the elements inside the prefix found so far
 #pragma unroll
-      for (int q = 0; q < CH_Q; ++q) {
-        const int j = j0 + q * CH_THREADS + tid;
-        const bool act = j < n && (hs >= NB || (kq[q] >> hs) == (pre >> hs));
-        ch_hist_add(sh, act, (uint32_t)(kq[q] >> shift) & 255u, wq[q], by_mass);
-      }
+      for (int q = 0; q < CH_Q; ++q) wq[q] = (by_mass && aq[q]) ? wt(j0 + q * CH_THREADS + tid) : 0.0;
+#pragma unroll
+      for (int q = 0; q < CH_Q; ++q) ch_hist_add(sh, aq[q], (uint32_t)(kq[q] >> shift) & 255u, wq[q], by_mass);
     }
     __syncthreads();
     if (by_mass && tid < 256) {
@@ -347,14 +343,10 @@ __device__ void ch_walk(ChainShared& sh, const Src& src, int n, KeyF key, WF wt,
 #pragma unroll
     for (int q = 0; q < CH_Q; ++q) {
       const int j = j0 + q * CH_THREADS + tid;
-      eq[q] = false;
-      wv[q] = 0.0;
-      if (j < n) {
-        eq[q] = key(src.logit(j)) == bk;
-        if (by_mass) wv[q] = wt(j);
-      }
-      if (!eq[q]) wv[q] = 0.0;
+      eq[q] = j < n && key(src.logit(j)) == bk;
     }
+#pragma unroll
+    for (int q = 0; q < CH_Q; ++q) wv[q] = (by_mass && eq[q]) ? wt(j0 + q * CH_THREADS + tid) : 0.0;
     uint32_t be[CH_Q];
     double iw[CH_Q];
 #pragma unroll

@@ -527,6 +527,10 @@ def run_chain(args, dev):
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = t0.elapsed_time(t1) / args.steps
+    # the logits are the algorithmic bytes of a step (read once); the
+    # history and draws are a few KB
+    peak, peak_kind = measured_peaks()
+    gbs = step_bytes / (ms / 1e3) / 1e9
     line = {
         "metric": f"rows/s, llama.cpp sampler chain ({args.chain} preset)", "value": round(B / (ms / 1e3), 1),
         "unit": "rows/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
@@ -534,6 +538,8 @@ def run_chain(args, dev):
         "config": {"workload": f"[{B} x {V}] {spec['dtype']}", "chain": p.as_dict(), "history": 256,
                    "l2": f"{nbuf} rotating input buffers, {nbuf * step_bytes / 1e6:.0f} MB > L2"},
         "gpu_launches": args.steps, "parity": parity, "clocks": clk,
+        "roofline": {"bound": "hbm", "kernel": "llama_chain_kernel", "achieved": round(gbs, 1), "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": round(gbs / peak, 4), "traffic": None},
     }
     print(json.dumps(line), flush=True)
 
